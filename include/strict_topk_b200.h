@@ -1,0 +1,209 @@
+/*
+ * strict_topk_b200.h — C ABI of libstk_sm100.so, the sm_100a (B200) kernels
+ * behind the `strict_topk` speculative block-sparse decode API.
+ *
+ * Every entry point:
+ *   - takes raw device pointers, explicit sizes, dtype enums and a CUDA stream
+ *     (passed as `void*`, i.e. a cudaStream_t), never a framework type;
+ *   - is asynchronous and stream-ordered: it only enqueues kernels, never
+ *     synchronises the device, never allocates (scratch is caller-provided),
+ *     and is capturable into a CUDA graph;
+ *   - returns 0 on success, a negative STK_E* code for an invalid argument
+ *     found on the host (message in stk_last_error()), or a positive
+ *     cudaError_t from a launch.
+ * Device-detected data faults (an out-of-range block ID, a bounded wait that
+ * ran out) are written to the optional `status` word (first code wins) and
+ * never trap.
+ *
+ * The reference (6Mikao9/strict-topk-overlap) is Python + Triton with no FFI
+ * of its own; each entry point names the reference function(s) whose device
+ * work it replaces (file:line within that project).
+ */
+#ifndef STRICT_TOPK_B200_H_
+#define STRICT_TOPK_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define STK_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define STK_API __attribute__((visibility("default")))
+#else
+#define STK_API
+#endif
+
+/* dtypes */
+#define STK_F32 0
+#define STK_F16 1
+#define STK_BF16 2
+
+/* host-side error codes */
+#define STK_EINVAL (-1)   /* bad shape / argument */
+#define STK_ESMEM (-2)    /* per-row sizes exceed the kernel's shared-memory plan */
+#define STK_EDIM (-3)     /* head dimension unsupported (> 1024) */
+#define STK_EWS (-4)      /* workspace too small */
+
+/* device status codes (written to *status) */
+#define STK_STATUS_OK 0
+#define STK_STATUS_WAIT_TIMEOUT 1
+#define STK_STATUS_BAD_BLOCK_ID 2
+#define STK_STATUS_SHAPE_OVERFLOW 3
+
+/* block-state job modes */
+#define STK_MODE_FULL 0   /* (m, l, u) per block */
+#define STK_MODE_MASS 1   /* (m, l) only, K read only */
+#define STK_MODE_FIXED 2  /* l, u (and |w v| envelope) at a caller-given logit frame */
+
+/* prediction modes */
+#define STK_PRED_SAVED 0
+#define STK_PRED_HYBRID 1
+#define STK_PRED_COMPACT 2
+#define STK_PRED_NONE 3
+
+/* repair variants */
+#define STK_VAR_SPLIT 0         /* kernels.py:554-600  repair()              */
+#define STK_VAR_FUSED 1         /* fused.py:176-220    repair_fused()        */
+#define STK_VAR_SIGNED 2        /* signed_repair.py:175-232 repair_signed()  */
+#define STK_VAR_SIGNED_FUSED 3  /* signed_fused.py:148-193 repair_signed_fused() */
+#define STK_VAR_SAVED 4         /* gqa.py:186-188, gqa_light.py:63-77, gqa_hierarchical.py:137-144 */
+#define STK_VAR_UNION 5         /* gqa.py:191-193      repair_union()        */
+
+/* KV cache description. Dense: k/v are [hkv, n, b, d] (per request, requests
+ * `kv_request_stride` elements apart). Paged: k/v are page pools
+ * [pages, hkv, page_size, d] and block `j` of request `r` is made of pages
+ * page_table[(block_offsets[r] + j) * (b / page_size) + i]. */
+typedef struct stk_kv {
+  const void* k;
+  const void* v;
+  int kv_dtype;
+  int hkv, n, b, d;
+  const int32_t* page_table;    /* NULL = dense */
+  const int32_t* block_offsets; /* [R + 1] per-request block offsets, or NULL (one request) */
+  int page_size;
+  long long kv_request_stride;  /* dense batched layouts; 0 for one request */
+} stk_kv;
+
+/* Speculative prediction state (strict_topk.kernels.Prediction, kernels.py:13-39). */
+typedef struct stk_prediction {
+  int mode;                 /* STK_PRED_* */
+  int sc;                   /* state slots: sp (saved/hybrid) or capacity (compact) */
+  const float* m;           /* [rows, sc] */
+  const float* l;           /* [rows, sc] */
+  const float* u;           /* [rows, sc, d] */
+  const uint8_t* high;      /* [rows, sp] (hybrid, compact) */
+  const void* retained_ids; /* [rows, sc] (compact) */
+  int retained_ids64;
+  const float* low_m;       /* [rows] */
+  const float* low_l;       /* [rows] */
+  const float* low_u;       /* [rows, d] */
+  const float* low_abs;     /* [rows, d] */
+  const float* mass_m;      /* [rows, sp] (keep_mass) */
+  const float* mass_l;      /* [rows, sp] */
+} stk_prediction;
+
+/* Repair outputs (RepairResult / SignedRepairResult, kernels.py:33-39,
+ * signed_repair.py:12-15). Optional pointers may be NULL. */
+typedef struct stk_repair_out {
+  float* out;            /* [rows, d] FP32 */
+  uint8_t* fallback;     /* [rows] */
+  float* remaining;      /* [rows] */
+  uint8_t* approx;       /* [rows] or NULL */
+  float* extra;          /* [rows] or NULL */
+  int32_t* positive_jobs;/* [rows] or NULL */
+  int32_t* total_jobs;   /* [rows] or NULL */
+} stk_repair_out;
+
+STK_API int stk_abi_version(void);
+STK_API const char* stk_last_error(void);
+STK_API int stk_device_sm_count(int device);
+
+/* Fused min/max query-sign bound scores, FP64 fixed-order sum rounded to FP32.
+ * Replaces selector.py:30-45 block_scores() (_score, selector.py:8-20) and the
+ * scoring half of gqa.py:145-161 (_bound_score, gqa.py:15-26).
+ * q [hq, d] (q_dtype); lo/hi [hmeta, n, d] FP32 with hq % hmeta == 0;
+ * scores [hq, n] FP32. */
+STK_API int stk_bound_scores(const void* q, int q_dtype, const float* lo, const float* hi, int hq, int hmeta, int n, int d,
+                     float* scores, void* stream);
+
+/* Workspace (bytes) for stk_select_topk: FP64 scores of every selection row. */
+STK_API size_t stk_select_workspace_bytes(int sel_heads, int total_blocks);
+
+/* Score + strict Top-K, ties to the lower block ID, IDs ascending per row.
+ * Replaces selector.py:48-50 select_blocks() and gqa.py:145-161
+ * select_blocks() (torch.topk at selector.py:43 / gqa.py:161).
+ * q [R, hq, d]; lo/hi [hmeta, total_blocks, d]; requests own block ranges
+ * block_offsets[r]..block_offsets[r+1] (or [0, n) when NULL, R == 1).
+ * group_select = 0: one row per query head; 1: one row per KV head, scored by
+ * the sum of its query heads' scores (shared per-group selection).
+ * ids_out [R, rows_per_request, topk] int32 (+ id_base); keys_out optional
+ * [.., topk] order keys (for cross-shard merges). */
+STK_API int stk_select_topk(const void* q, int q_dtype, const float* lo, const float* hi, int R, int hq, int hmeta, int n,
+                    const int32_t* block_offsets, int total_blocks, int max_blocks, int d, int topk, int group_select,
+                    int id_base, int32_t* ids_out, unsigned long long* keys_out, void* workspace,
+                    size_t workspace_bytes, int32_t* status, void* stream);
+
+/* Merge shard-local Top-K candidates (ascending IDs per row) into the global
+ * strict Top-K. New: the context-parallel exchange of the decode path. */
+STK_API int stk_merge_candidates(const unsigned long long* keys, const int32_t* ids, int rows, int ncand, int topk,
+                         int32_t* ids_out, int32_t* status, void* stream);
+
+/* Per-block softmax states for ids [rows, s] (row = r * hq + h, kv = h / (hq / hkv)).
+ * Replaces kernels.py:425-434 block_partials() (_partial, kernels.py:42-71),
+ * gqa.py:128-137 partials() and its REPAIR slot search (gqa.py:29-59),
+ * gqa_hierarchical.py:55-61 partials(), kernels.py:263-278 (_mass_only),
+ * kernels.py:312-356 (_compact_values, fixed-frame low aggregation) and
+ * kernels.py:384-407 (_wrong_aggregate).
+ * active: NULL, per-row [rows] (active_mode 1) or per-slot [rows, s] (2).
+ * pred != NULL: search each id in pred[row, :sp], write slot_out, skip hits. */
+STK_API int stk_block_states(const stk_kv* kv, const void* q, int q_dtype, int rows, int hq, const void* ids, int ids64,
+                     int s, const uint8_t* active, int active_mode, int active_invert, const void* pred, int pred64,
+                     int sp, int32_t* slot_out, int mode, const float* frame, float* m, float* l, float* u,
+                     float* uabs, int32_t* status, void* stream);
+
+/* LSE merge of per-slot states with an optional include mask.
+ * Replaces kernels.py:487-492 merge_partials() (_merge, kernels.py:74-91). */
+STK_API int stk_merge_states(const float* m, const float* l, const float* u, const uint8_t* include, int rows, int s, int d,
+                     float* out, void* stream);
+
+/* Full speculation for one prediction mode.
+ * Replaces kernels.py:500-551 speculate() incl. _group (kernels.py:94-117) and
+ * the compact pipeline (_mass_only, _compact_group, _compact_values).
+ * Outputs follow stk_prediction: state m/l/u [rows, sc]; high [rows, sp];
+ * retained_ids [rows, sc]; low m/l [rows], low u/abs [rows, d];
+ * overflow [rows]; mass_m/mass_l [rows, sp] (compact: pass-1 statistics).
+ * workspace: stk_speculate_workspace_bytes(). */
+STK_API size_t stk_speculate_workspace_bytes(int rows, int sp, int d, int mode);
+STK_API int stk_speculate(const stk_kv* kv, const void* q, int q_dtype, int rows, int hq, const void* pred, int pred64, int sp,
+                  int mode, float mass_threshold, int sc, float* state_m, float* state_l, float* state_u,
+                  uint8_t* high, void* retained_ids, float* low_m, float* low_l, float* low_u, float* low_abs,
+                  uint8_t* overflow, float* mass_m, float* mass_l, void* workspace, size_t workspace_bytes,
+                  int32_t* status, void* stream);
+
+/* One-launch repair: set difference, signed recompute of misses and
+ * wrong-low blocks, guarded LSE merge, in-launch strict fallback.
+ * Replaces kernels.py:554-600 repair(), fused.py:176-220 repair_fused(),
+ * signed_repair.py:175-232 repair_signed(), signed_fused.py:148-193
+ * repair_signed_fused(), gqa.py:164-193 repair_saved()/repair_union(),
+ * gqa_light.py:63-92 repair_saved_light()/auto, gqa_hierarchical.py:207-236
+ * repair_saved()/repair_saved_shared(); with pred_state->mode ==
+ * STK_PRED_NONE it is kernels.py:495-497 exact_attention() / gqa.py:140-142. */
+STK_API int stk_repair(const stk_kv* kv, const void* q, int q_dtype, int rows, int hq, const void* sel, int sel64, int sa,
+               const void* pred, int pred64, int sp, const stk_prediction* pred_state, int variant,
+               float min_remaining, float cancellation_tol, float max_extra_mass, int max_blocks,
+               const stk_repair_out* out, int32_t* status, void* stream);
+
+/* Prefetch baseline: read predicted K/V, write per-tile checksums.
+ * Replaces kernels.py:553-560 touch_kv() (_touch, kernels.py:250-260).
+ * out [rows, s, ceil(b * d / 1024)] FP32. */
+STK_API int stk_touch_kv(const stk_kv* kv, int rows, int hq, const void* ids, int ids64, int s, float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* STRICT_TOPK_B200_H_ */

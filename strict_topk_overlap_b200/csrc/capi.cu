@@ -1,0 +1,299 @@
+// extern "C" entry points of libstk_sm100.so (declared in include/strict_topk_b200.h).
+// Host-side validation, argument packing and launch orchestration only; all
+// arithmetic lives in select.cu, states.cu and repair.cu.
+#include <math.h>
+#include <stdarg.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "internal.cuh"
+#include "../../include/strict_topk_b200.h"
+
+
+using namespace stk;
+
+namespace {
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_status(int rc, const char* what) {
+  if (rc > 0) {
+    g_err = std::string(what) + ": " + cudaGetErrorString(static_cast<cudaError_t>(rc));
+  } else if (rc < 0) {
+    g_err = std::string(what) + ": per-row sizes exceed the kernel plan";
+  }
+  return rc;
+}
+
+constexpr int kMaxDevices = 64;
+std::atomic<int> g_sm_count[kMaxDevices];
+
+int sm_count_current() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  int v = g_sm_count[dev].load(std::memory_order_relaxed);
+  if (v <= 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    g_sm_count[dev].store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
+bool valid_dtype(int t) { return t == STK_F32 || t == STK_F16 || t == STK_BF16; }
+
+KVLayout make_layout(const stk_kv* kv) {
+  KVLayout L;
+  L.k = kv->k;
+  L.v = kv->v;
+  L.hkv = kv->hkv;
+  L.n = kv->n;
+  L.b = kv->b;
+  L.d = kv->d;
+  L.page_table = kv->page_table;
+  L.block_offsets = kv->block_offsets;
+  L.page_size = kv->page_size > 0 ? kv->page_size : kv->b;
+  L.kv_request_stride = kv->kv_request_stride;
+  return L;
+}
+
+int check_kv(const stk_kv* kv, int hq) {
+  if (kv == nullptr || kv->k == nullptr || kv->v == nullptr) return fail(STK_EINVAL, "kv description is null");
+  if (!valid_dtype(kv->kv_dtype)) return fail(STK_EINVAL, "unsupported KV dtype %d", kv->kv_dtype);
+  if (kv->hkv <= 0 || kv->b <= 0 || kv->d <= 0 || (kv->n <= 0 && kv->block_offsets == nullptr))
+    return fail(STK_EINVAL, "KV shape must be nonempty (hkv=%d n=%d b=%d d=%d)", kv->hkv, kv->n, kv->b, kv->d);
+  if (hq <= 0 || hq % kv->hkv != 0) return fail(STK_EINVAL, "query heads %d not divisible by KV heads %d", hq, kv->hkv);
+  if (kv->d > 1024) return fail(STK_EDIM, "head dim %d > 1024 unsupported", kv->d);
+  if (kv->page_table != nullptr) {
+    if (kv->page_size <= 0 || kv->b % kv->page_size != 0)
+      return fail(STK_EINVAL, "page size %d must divide the block size %d", kv->page_size, kv->b);
+    if (kv->block_offsets == nullptr) return fail(STK_EINVAL, "paged KV needs block_offsets");
+  }
+  return 0;
+}
+
+float attn_scale(int d) { return static_cast<float>(1.0 / sqrt(static_cast<double>(d))); }
+}  // namespace
+
+extern "C" {
+
+int stk_abi_version(void) { return STK_ABI_VERSION; }
+
+const char* stk_last_error(void) { return g_err.c_str(); }
+
+int stk_device_sm_count(int device) {
+  int v = 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return -1;
+  return v;
+}
+
+int stk_bound_scores(const void* q, int q_dtype, const float* lo, const float* hi, int hq, int hmeta, int n, int d,
+                     float* scores, void* stream) {
+  if (!q || !lo || !hi || !scores) return fail(STK_EINVAL, "null pointer");
+  if (!valid_dtype(q_dtype)) return fail(STK_EINVAL, "unsupported q dtype");
+  if (hq <= 0 || hmeta <= 0 || n <= 0 || d <= 0 || hq % hmeta) return fail(STK_EINVAL, "bad score shape");
+  ScoreArgs a{};
+  a.q = q; a.q_dtype = q_dtype; a.lo = lo; a.hi = hi;
+  a.R = 1; a.hq = hq; a.hmeta = hmeta; a.d = d; a.n = n;
+  a.block_offsets = nullptr; a.total_blocks = n; a.group_select = 0;
+  a.scores_f32 = scores; a.scores_f64 = nullptr;
+  if ((reinterpret_cast<uintptr_t>(lo) | reinterpret_cast<uintptr_t>(hi)) & 15) {
+    // The vectorised path needs 16-byte rows; misaligned metadata uses scalar loads.
+  }
+  return cuda_status(launch_score(a, static_cast<cudaStream_t>(stream)), "bound_scores");
+}
+
+size_t stk_select_workspace_bytes(int sel_heads, int total_blocks) {
+  return static_cast<size_t>(sel_heads) * static_cast<size_t>(total_blocks) * sizeof(double);
+}
+
+int stk_select_topk(const void* q, int q_dtype, const float* lo, const float* hi, int R, int hq, int hmeta, int n,
+                    const int32_t* block_offsets, int total_blocks, int max_blocks, int d, int topk, int group_select,
+                    int id_base, int32_t* ids_out, unsigned long long* keys_out, void* workspace,
+                    size_t workspace_bytes, int32_t* status, void* stream) {
+  if (!q || !lo || !hi || !ids_out || !workspace) return fail(STK_EINVAL, "null pointer");
+  if (!valid_dtype(q_dtype)) return fail(STK_EINVAL, "unsupported q dtype");
+  if (R <= 0 || hq <= 0 || hmeta <= 0 || d <= 0 || hq % hmeta) return fail(STK_EINVAL, "bad select shape");
+  if (block_offsets == nullptr) {
+    if (R != 1 || n <= 0) return fail(STK_EINVAL, "one request with n > 0 expected without block_offsets");
+    total_blocks = n;
+    max_blocks = n;
+  }
+  if (topk <= 0 || topk > max_blocks) return fail(STK_EINVAL, "topk %d outside [1, %d]", topk, max_blocks);
+  const int hsel = group_select ? hmeta : hq;
+  if (workspace_bytes < stk_select_workspace_bytes(hsel, total_blocks)) return fail(STK_EWS, "select workspace too small");
+  if (static_cast<size_t>(max_blocks) * 8 > 200 * 1024)
+    return fail(STK_ESMEM, "%d blocks per row exceed the single-pass selection plan (max 25600); "
+                "split the row into segments and merge candidates", max_blocks);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ScoreArgs a{};
+  a.q = q; a.q_dtype = q_dtype; a.lo = lo; a.hi = hi;
+  a.R = R; a.hq = hq; a.hmeta = hmeta; a.d = d; a.n = n;
+  a.block_offsets = block_offsets; a.total_blocks = total_blocks;
+  a.group_select = group_select; a.scores_f32 = nullptr;
+  a.scores_f64 = static_cast<double*>(workspace);
+  int rc = launch_score(a, s);
+  if (rc) return cuda_status(rc, "score");
+  SelectArgs b{};
+  b.scores = static_cast<const double*>(workspace);
+  b.R = R; b.hsel = hsel; b.topk = topk; b.n = n;
+  b.block_offsets = block_offsets; b.total_blocks = total_blocks;
+  b.id_base = id_base; b.ids_out = ids_out; b.keys_out = keys_out; b.status = status;
+  return cuda_status(launch_select(b, max_blocks, s), "select");
+}
+
+int stk_merge_candidates(const unsigned long long* keys, const int32_t* ids, int rows, int ncand, int topk,
+                         int32_t* ids_out, int32_t* status, void* stream) {
+  if (!keys || !ids || !ids_out) return fail(STK_EINVAL, "null pointer");
+  if (rows <= 0 || ncand <= 0 || topk <= 0 || topk > ncand) return fail(STK_EINVAL, "bad candidate shape");
+  MergeArgs a{keys, ids, rows, ncand, topk, ids_out, status};
+  return cuda_status(launch_merge_candidates(a, static_cast<cudaStream_t>(stream)), "merge_candidates");
+}
+
+int stk_block_states(const stk_kv* kv, const void* q, int q_dtype, int rows, int hq, const void* ids, int ids64,
+                     int s, const uint8_t* active, int active_mode, int active_invert, const void* pred, int pred64,
+                     int sp, int32_t* slot_out, int mode, const float* frame, float* m, float* l, float* u,
+                     float* uabs, int32_t* status, void* stream) {
+  int rc = check_kv(kv, hq);
+  if (rc) return rc;
+  if (!q || !ids || !valid_dtype(q_dtype)) return fail(STK_EINVAL, "bad q / ids");
+  if (rows <= 0 || rows % hq != 0 || s <= 0) return fail(STK_EINVAL, "bad job shape rows=%d s=%d", rows, s);
+  if (mode < 0 || mode > 2) return fail(STK_EINVAL, "bad mode");
+  if (mode != STK_MODE_FIXED && (!m || !l)) return fail(STK_EINVAL, "m/l outputs required");
+  if (mode != STK_MODE_MASS && !u) return fail(STK_EINVAL, "u output required");
+  if (mode == STK_MODE_FIXED && !frame) return fail(STK_EINVAL, "frame required");
+  if (pred && sp <= 0) return fail(STK_EINVAL, "pred needs sp > 0");
+  JobArgs a{};
+  a.L = make_layout(kv);
+  a.q = q; a.q_dtype = q_dtype;
+  a.rows = rows; a.hq = hq; a.g = hq / kv->hkv; a.d = kv->d; a.scale = attn_scale(kv->d);
+  a.ids = ids; a.ids64 = ids64; a.s = s;
+  a.active = active; a.active_mode = active ? active_mode : 0; a.active_invert = active_invert;
+  a.pred = pred; a.pred64 = pred64; a.sp = sp; a.slot_out = slot_out;
+  a.mode = mode; a.frame = frame; a.m = m; a.l = l; a.u = u; a.uabs = uabs; a.status = status;
+  return cuda_status(launch_jobs(a, kv->kv_dtype, sm_count_current(), static_cast<cudaStream_t>(stream)), "block_states");
+}
+
+int stk_merge_states(const float* m, const float* l, const float* u, const uint8_t* include, int rows, int s, int d,
+                     float* out, void* stream) {
+  if (!m || !l || !u || !out || rows <= 0 || s <= 0 || d <= 0) return fail(STK_EINVAL, "bad merge arguments");
+  return cuda_status(launch_merge(m, l, u, include, rows, s, d, out, static_cast<cudaStream_t>(stream)), "merge");
+}
+
+size_t stk_speculate_workspace_bytes(int rows, int sp, int d, int mode) {
+  if (mode != STK_PRED_COMPACT) return 0;
+  // Fixed-frame low aggregation: per-slot u and |w v| rows.
+  return static_cast<size_t>(rows) * sp * d * sizeof(float) * 2;
+}
+
+int stk_speculate(const stk_kv* kv, const void* q, int q_dtype, int rows, int hq, const void* pred, int pred64, int sp,
+                  int mode, float mass_threshold, int sc, float* state_m, float* state_l, float* state_u,
+                  uint8_t* high, void* retained_ids, float* low_m, float* low_l, float* low_u, float* low_abs,
+                  uint8_t* overflow, float* mass_m, float* mass_l, void* workspace, size_t workspace_bytes,
+                  int32_t* status, void* stream) {
+  int rc = check_kv(kv, hq);
+  if (rc) return rc;
+  if (!(mass_threshold >= 0.f && mass_threshold <= 1.f)) return fail(STK_EINVAL, "mass_threshold must be in [0,1]");
+  if (rows <= 0 || rows % hq || sp <= 0) return fail(STK_EINVAL, "bad speculate shape");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int d = kv->d;
+  if (mode == STK_PRED_SAVED || mode == STK_PRED_HYBRID) {
+    rc = stk_block_states(kv, q, q_dtype, rows, hq, pred, pred64, sp, nullptr, 0, 0, nullptr, 0, 0, nullptr,
+                          STK_MODE_FULL, nullptr, state_m, state_l, state_u, nullptr, status, stream);
+    if (rc || mode == STK_PRED_SAVED) return rc;
+    if (!high || !low_m || !low_l || !low_u || !low_abs) return fail(STK_EINVAL, "hybrid outputs required");
+    return cuda_status(launch_hybrid_group(state_m, state_l, state_u, rows, sp, d, mass_threshold, high, low_m, low_l,
+                                           low_u, low_abs, st),
+                       "hybrid_group");
+  }
+  if (mode != STK_PRED_COMPACT) return fail(STK_EINVAL, "bad prediction mode %d", mode);
+  if (!mass_m || !mass_l || !high || !retained_ids || !overflow || !low_m || !low_l || !low_u || !low_abs)
+    return fail(STK_EINVAL, "compact outputs required");
+  if (sc <= 0 || sc > sp) return fail(STK_EINVAL, "compact capacity %d outside [1, %d]", sc, sp);
+  if (workspace_bytes < stk_speculate_workspace_bytes(rows, sp, d, mode)) return fail(STK_EWS, "compact workspace too small");
+  // Pass 1: per-block (m, l) from K only (kernels.py:263-278).
+  rc = stk_block_states(kv, q, q_dtype, rows, hq, pred, pred64, sp, nullptr, 0, 0, nullptr, 0, 0, nullptr,
+                        STK_MODE_MASS, nullptr, mass_m, mass_l, nullptr, nullptr, status, stream);
+  if (rc) return rc;
+  // Grouping with capacity-C packing (kernels.py:281-309).
+  rc = launch_compact_group(mass_m, mass_l, pred, pred64, rows, sp, sc, mass_threshold, high, retained_ids, low_m,
+                            low_l, overflow, st);
+  if (rc) return cuda_status(rc, "compact_group");
+  // Pass 2a: retained high blocks, full states (kernels.py:387-406).
+  rc = stk_block_states(kv, q, q_dtype, rows, hq, retained_ids, pred64, sc, nullptr, 0, 0, nullptr, 0, 0, nullptr,
+                        STK_MODE_FULL, nullptr, state_m, state_l, state_u, nullptr, status, stream);
+  if (rc) return rc;
+  // Pass 2b: low blocks per token at low_m, then per-row sums (kernels.py:370-386).
+  float* su = static_cast<float*>(workspace);
+  float* sa = su + static_cast<size_t>(rows) * sp * d;
+  rc = stk_block_states(kv, q, q_dtype, rows, hq, pred, pred64, sp, high, 2, 1, nullptr, 0, 0, nullptr,
+                        STK_MODE_FIXED, low_m, nullptr, nullptr, su, sa, status, stream);
+  if (rc) return rc;
+  return cuda_status(launch_slot_sum(su, sa, rows, sp, d, low_u, low_abs, st), "slot_sum");
+}
+
+int stk_repair(const stk_kv* kv, const void* q, int q_dtype, int rows, int hq, const void* sel, int sel64, int sa,
+               const void* pred, int pred64, int sp, const stk_prediction* ps, int variant, float min_remaining,
+               float cancellation_tol, float max_extra_mass, int max_blocks, const stk_repair_out* out,
+               int32_t* status, void* stream) {
+  int rc = check_kv(kv, hq);
+  if (rc) return rc;
+  if (!q || !sel || !out || !out->out || !valid_dtype(q_dtype)) return fail(STK_EINVAL, "bad repair pointers");
+  if (rows <= 0 || rows % hq || sa <= 0) return fail(STK_EINVAL, "bad repair shape");
+  if (variant < 0 || variant > 5) return fail(STK_EINVAL, "bad variant");
+  if (!(max_extra_mass >= 0.f && max_extra_mass <= 1.f)) return fail(STK_EINVAL, "max_extra_mass must be in [0, 1]");
+  const int pmode = ps ? ps->mode : STK_PRED_NONE;
+  if (pmode != STK_PRED_NONE) {
+    if (!pred || sp <= 0 || !ps->m || !ps->l || !ps->u) return fail(STK_EINVAL, "prediction state required");
+    if ((pmode == STK_PRED_HYBRID || pmode == STK_PRED_COMPACT) &&
+        (!ps->high || !ps->low_m || !ps->low_l || !ps->low_u || !ps->low_abs))
+      return fail(STK_EINVAL, "hybrid/compact prediction needs high mask and low aggregate");
+    if (pmode == STK_PRED_COMPACT && !ps->retained_ids) return fail(STK_EINVAL, "compact prediction needs retained ids");
+    if (max_extra_mass > 0.f && (pmode == STK_PRED_HYBRID || pmode == STK_PRED_COMPACT) && (!ps->mass_m || !ps->mass_l))
+      return fail(STK_EINVAL, "positive max_extra_mass requires speculate(..., keep_mass=True)");
+  }
+  const int max_n = kv->block_offsets ? max_blocks : kv->n;
+  if (max_n <= 0) return fail(STK_EINVAL, "max_blocks required for batched layouts");
+  RepairArgs a{};
+  a.L = make_layout(kv);
+  a.q = q; a.q_dtype = q_dtype;
+  a.rows = rows; a.hq = hq; a.g = hq / kv->hkv; a.d = kv->d; a.scale = attn_scale(kv->d);
+  a.sel = sel; a.sel64 = sel64; a.sa = sa;
+  a.pred = pmode == STK_PRED_NONE ? nullptr : pred; a.pred64 = pred64; a.sp = pmode == STK_PRED_NONE ? 0 : sp;
+  a.pmode = pmode; a.sc = pmode == STK_PRED_NONE ? 0 : ps->sc;
+  if (ps) {
+    a.pm = ps->m; a.pl = ps->l; a.pu = ps->u; a.high = ps->high;
+    a.rids = ps->retained_ids; a.rids64 = ps->retained_ids64;
+    a.low_m = ps->low_m; a.low_l = ps->low_l; a.low_u = ps->low_u; a.low_abs = ps->low_abs;
+    a.mass_m = ps->mass_m; a.mass_l = ps->mass_l;
+  }
+  a.variant = variant;
+  a.min_remaining = min_remaining; a.cancel_tol = cancellation_tol; a.eps = max_extra_mass;
+  a.max_n = max_n;
+  a.out = out->out; a.fallback = out->fallback; a.remaining = out->remaining; a.approx = out->approx;
+  a.extra = out->extra; a.pos_out = out->positive_jobs; a.total_out = out->total_jobs;
+  a.status = status;
+  return cuda_status(launch_repair(a, kv->kv_dtype, static_cast<cudaStream_t>(stream)), "repair");
+}
+
+int stk_touch_kv(const stk_kv* kv, int rows, int hq, const void* ids, int ids64, int s, float* out, void* stream) {
+  int rc = check_kv(kv, hq);
+  if (rc) return rc;
+  if (!ids || !out || rows <= 0 || s <= 0) return fail(STK_EINVAL, "bad touch arguments");
+  return cuda_status(launch_touch(make_layout(kv), rows, hq, hq / kv->hkv, ids, ids64, s, out, kv->kv_dtype,
+                                  static_cast<cudaStream_t>(stream)),
+                     "touch_kv");
+}
+
+}  // extern "C"

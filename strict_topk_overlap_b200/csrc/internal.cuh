@@ -1,0 +1,131 @@
+// Internal argument structs and launchers shared by the library's translation units.
+#pragma once
+#include "common.cuh"
+
+namespace stk {
+
+enum JobMode : int { kModeFull = 0, kModeMass = 1, kModeFixed = 2 };
+
+enum PredMode : int { kPredSaved = 0, kPredHybrid = 1, kPredCompact = 2, kPredNone = 3 };
+
+enum Variant : int {
+  kVarSplit = 0,        // kernels.repair: guards in the common frame
+  kVarFused = 1,        // fused.repair_fused: negatives per token at low_m
+  kVarSigned = 2,       // signed_repair.repair_signed: negatives block-local, rescaled to low_m
+  kVarSignedFused = 3,  // signed_fused: hybrid block-local rescaled, compact per token
+  kVarSaved = 4,        // gqa.repair_saved / gqa_light / hierarchical: output only
+  kVarUnion = 5,        // gqa.repair_union: all predicted states + misses
+};
+
+struct ScoreArgs {
+  const void* q;  // [R * hq, d]
+  int q_dtype;
+  const float* lo;  // [hmeta, total_blocks, d]
+  const float* hi;
+  int R, hq, hmeta, d;
+  int n;                     // blocks per request when block_offsets is null
+  const int* block_offsets;  // [R + 1] or null
+  int total_blocks;
+  int group_select;   // 1: write per-KV-group sums instead of per-head scores
+  float* scores_f32;  // optional [hq, total_blocks]
+  double* scores_f64; // optional [hq or hmeta (group), total_blocks]
+};
+
+struct SelectArgs {
+  const double* scores;  // [hsel, total_blocks]
+  int R, hsel, topk;
+  int n;                     // blocks per request when block_offsets is null
+  const int* block_offsets;  // [R + 1] or null
+  int total_blocks;
+  int id_base;               // added to every written ID (shard offset)
+  int* ids_out;              // [R * hsel, topk], ascending
+  unsigned long long* keys_out;  // optional: [R * hsel, topk] ordered keys of the chosen IDs
+  int* status;
+};
+
+struct MergeArgs {
+  const unsigned long long* keys;  // [rows, ncand]
+  const int* ids;                  // [rows, ncand], ascending per row
+  int rows, ncand, topk;
+  int* ids_out;                    // [rows, topk] ascending
+  int* status;
+};
+
+struct JobArgs {
+  KVLayout L;
+  const void* q;  // [rows, d]
+  int q_dtype;
+  int rows, hq, g, d;
+  float scale;  // D^-0.5 as FP32
+  const void* ids;  // [rows, s] block ids (per request)
+  int ids64, s;
+  const unsigned char* active;  // optional mask
+  int active_mode;              // 0 none, 1 per row [rows], 2 per slot [rows, s]
+  int active_invert;            // 1: a set mask entry means "skip"
+  const void* pred;             // optional: search ids in pred[row, :sp]; hits are skipped
+  int pred64, sp;
+  int* slot_out;                // optional [rows, s]: matching pred slot or -1
+  int mode;                     // JobMode
+  const float* frame;           // kModeFixed: [rows] fixed logit frame
+  float* m;                     // [rows, s]   (full, mass)
+  float* l;                     // [rows, s]
+  float* u;                     // [rows, s, d] (full, fixed)
+  float* uabs;                  // [rows, s, d] (fixed, optional)
+  int* status;
+};
+
+struct RepairArgs {
+  KVLayout L;
+  const void* q;
+  int q_dtype;
+  int rows, hq, g, d;
+  float scale;
+  const void* sel;  // A [rows, sa]
+  int sel64, sa;
+  const void* pred;  // P [rows, sp] (null for kPredNone)
+  int pred64, sp;
+  int pmode, sc;
+  const float* pm;  // [rows, sc]
+  const float* pl;
+  const float* pu;  // [rows, sc, d]
+  const unsigned char* high;  // [rows, sp]
+  const void* rids;           // [rows, sc] compact retained ids
+  int rids64;
+  const float* low_m;  // [rows]
+  const float* low_l;
+  const float* low_u;    // [rows, d]
+  const float* low_abs;  // [rows, d]
+  const float* mass_m;   // [rows, sp]
+  const float* mass_l;
+  int variant;
+  float min_remaining, cancel_tol, eps;
+  int max_n;  // upper bound of blocks per request (bitmap size)
+  float* out;                // [rows, d]
+  unsigned char* fallback;   // [rows]
+  float* remaining;          // [rows]
+  unsigned char* approx;     // [rows] or null
+  float* extra;              // [rows] or null
+  int* pos_out;              // [rows] or null
+  int* total_out;            // [rows] or null
+  int* status;
+};
+
+int launch_score(const ScoreArgs& a, cudaStream_t stream);
+int launch_select(const SelectArgs& a, int max_n, cudaStream_t stream);
+int launch_merge_candidates(const MergeArgs& a, cudaStream_t stream);
+int launch_jobs(const JobArgs& a, int kv_dtype, int num_sms, cudaStream_t stream);
+int launch_merge(const float* m, const float* l, const float* u, const unsigned char* include, int rows, int s, int d,
+                 float* out, cudaStream_t stream);
+int launch_hybrid_group(const float* m, const float* l, const float* u, int rows, int s, int d, float tau,
+                        unsigned char* high, float* low_m, float* low_l, float* low_u, float* low_abs,
+                        cudaStream_t stream);
+int launch_compact_group(const float* pm, const float* pl, const void* pred, int pred64, int rows, int s, int c,
+                         float tau, unsigned char* high, void* rids, float* low_m, float* low_l,
+                         unsigned char* overflow, cudaStream_t stream);
+int launch_slot_sum(const float* x, const float* y, int rows, int s, int d, float* out_x, float* out_y,
+                    cudaStream_t stream);
+int launch_touch(const KVLayout& L, int rows, int hq, int g, const void* ids, int ids64, int s, float* out,
+                 int kv_dtype, cudaStream_t stream);
+int launch_repair(const RepairArgs& a, int kv_dtype, cudaStream_t stream);
+
+}  // namespace stk

@@ -1,0 +1,714 @@
+// K3: one repair kernel for every strict / relaxed repair entry point.
+//
+// Replaces, with one launch per call:
+//   kernels.py:120-247,359-407 + repair()       (split repair, 3-5 launches)
+//   fused.py:10-173          (_accumulate, _repair)
+//   signed_repair.py:18-172  (_schedule, _signed_partials, _merge) + _fallback
+//   signed_fused.py:14-145   (_kv_tile, _corrections, _finalize)
+//   gqa.py:29-104            (REPAIR _partial + _merge_repair, saved and union)
+//   gqa_light.py:10-60       (_repair_light)
+//   gqa_hierarchical.py:99-130 (_match_ids, REPAIR packed partials, _groups)
+//   kernels.py:437-447       (exact_attention = repair with no prediction)
+//
+// One CTA per (request, query head) row. Phases:
+//   1. set difference A vs P through shared-memory bitmaps over block IDs;
+//      hit / miss / high / wrong-low flags; optional extra-mass budget (EPS);
+//      job queue = misses in A order, then wrong-low blocks in P order.
+//   2. warps stream queued blocks through a private TMA (cp.async.bulk) ring:
+//      misses are added (+) to a per-warp LSE state, wrong-low blocks are
+//      subtracted (-) from the low group in its own exponent frame, retained
+//      prediction states are merged in.
+//   3. warp states are merged in warp order; the variant's guards (remaining
+//      low mass, cancellation envelope, non-finite output) are evaluated.
+//   4. a flagged row recomputes the strict selected set in the same launch.
+#include "internal.cuh"
+
+namespace stk {
+
+
+
+constexpr int kNW = 4;  // warps per CTA
+
+// Negative-job frame rules.
+enum NegRule : int { kNegPerToken = 0, kNegBlockRescale = 1 };
+
+struct RepairShared {
+  unsigned* bitA;
+  unsigned* bitP;
+  long long* a_ids;
+  long long* p_ids;
+  unsigned char* a_miss;
+  unsigned char* p_flag;  // bit0 hit, bit1 high, bit2 wrong
+  unsigned char* keep;
+  int* queue;
+  float* aggU;   // [kNW][d] positive numerators
+  float* aggN;   // [kNW][d] negative numerators (low frame)
+  float* aggS;   // [kNW][4]: posM, posZ, negZ, -
+  float* vecA;   // [d]
+  float* vecB;   // [d]
+};
+
+struct RowScalars {
+  int miss_count, wrong_count, queue_len;
+  int low_hit;
+  int skip;
+  float extra;
+  float lm;
+};
+
+__device__ __forceinline__ bool bit_test(const unsigned* bits, long long i) {
+  return (bits[i >> 5] >> (i & 31)) & 1u;
+}
+
+// ------------------------------------------------------------------ per-warp block engine
+
+// Accumulates a block (all chunks) into either the warp's positive LSE state
+// or its negative low-frame sums. `neg_rule` / `frame` only matter for negatives.
+template <typename T, int DPL>
+struct BlockAcc {
+  float m, l;
+  float u[DPL > 0 ? DPL : 1];
+};
+
+template <typename T, int DPL, int NST>
+struct WarpRing {
+  T* stages;
+  uint64_t* bar;
+  unsigned phase;
+  static constexpr int D = 32 * DPL;
+  static constexpr int kChunkElems = 32 * D;
+  static constexpr int kStageElems = 2 * kChunkElems;
+};
+
+// Merge a block state into the warp's positive aggregate (smem, lane-owned dims).
+__device__ __forceinline__ void agg_pos_merge(float* S, float* U, int d, float mb, float lb, const float* ub_lane,
+                                              int dpl, int lane, bool lane_contig) {
+  if (mb == neg_inf()) return;
+  const float M = S[0];
+  const float Mn = fmaxf(M, mb);
+  const float a1 = expf(M - Mn), a2 = expf(mb - Mn);
+  __syncwarp();
+  if (lane_contig) {
+    for (int j = 0; j < dpl; ++j) {
+      const int dd = lane * dpl + j;
+      if (dd < d) U[dd] = U[dd] * a1 + ub_lane[j] * a2;
+    }
+  } else {
+    for (int j = 0, dd = lane; dd < d; ++j, dd += 32) U[dd] = U[dd] * a1 + ub_lane[j] * a2;
+  }
+  __syncwarp();
+  if (lane == 0) {
+    S[1] = S[1] * a1 + lb * a2;
+    S[0] = Mn;
+  }
+  __syncwarp();
+}
+
+// ------------------------------------------------------------------ kernel
+
+template <typename T, int DPL, int NST>
+__global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ uint64_t bars[kNW * NST];
+  __shared__ RowScalars rs;
+  __shared__ int sh_count[4];
+  __shared__ float sh_f[8];
+
+  constexpr bool kFast = DPL > 0;
+  const int D = kFast ? 32 * DPL : a.d;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row = blockIdx.x;
+  const int r = row / a.hq;
+  const int kv = (row - r * a.hq) / a.g;
+  const int nblocks = request_blocks(a.L, r);
+  const bool hybrid = a.pmode == kPredHybrid || a.pmode == kPredCompact;
+  const bool has_pred = a.pmode != kPredNone;
+
+  // ---- shared memory carve-up
+  size_t off = 0;
+  T* stages = nullptr;
+  const size_t stage_elems = kFast ? static_cast<size_t>(2) * 32 * D : 0;
+  if (kFast) {
+    stages = reinterpret_cast<T*>(smem);
+    off += kNW * NST * stage_elems * sizeof(T);
+  }
+  RepairShared S;
+  const int nwords = (a.max_n + 31) / 32;
+  S.bitA = reinterpret_cast<unsigned*>(smem + off); off += nwords * 4;
+  S.bitP = reinterpret_cast<unsigned*>(smem + off); off += nwords * 4;
+  off = (off + 7) & ~size_t(7);
+  S.a_ids = reinterpret_cast<long long*>(smem + off); off += a.sa * 8;
+  S.p_ids = reinterpret_cast<long long*>(smem + off); off += a.sp * 8;
+  S.queue = reinterpret_cast<int*>(smem + off); off += (a.sa + a.sp) * 4;
+  S.aggU = reinterpret_cast<float*>(smem + off); off += kNW * D * 4;
+  S.aggN = reinterpret_cast<float*>(smem + off); off += kNW * D * 4;
+  S.aggS = reinterpret_cast<float*>(smem + off); off += kNW * 4 * 4;
+  S.vecA = reinterpret_cast<float*>(smem + off); off += D * 4;
+  S.vecB = reinterpret_cast<float*>(smem + off); off += D * 4;
+  S.a_miss = smem + off; off += a.sa;
+  S.p_flag = smem + off; off += a.sp;
+  S.keep = smem + off; off += a.sc;
+
+  // ---- phase 1: ids, bitmaps, flags
+  for (int i = tid; i < nwords; i += blockDim.x) { S.bitA[i] = 0; S.bitP[i] = 0; }
+  if (kFast && lane == 0) {
+    for (int st = 0; st < NST; ++st) mbar_init(&bars[warp * NST + st], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  for (int i = tid; i < a.sa; i += blockDim.x) {
+    long long id = load_id(a.sel, a.sel64, static_cast<long long>(row) * a.sa + i);
+    if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); id = -1; }
+    S.a_ids[i] = id;
+    if (id >= 0) atomicOr(&S.bitA[id >> 5], 1u << (id & 31));
+  }
+  if (has_pred) {
+    for (int i = tid; i < a.sp; i += blockDim.x) {
+      long long id = load_id(a.pred, a.pred64, static_cast<long long>(row) * a.sp + i);
+      if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); id = -1; }
+      S.p_ids[i] = id;
+      if (id >= 0) atomicOr(&S.bitP[id >> 5], 1u << (id & 31));
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < a.sa; i += blockDim.x) {
+    const long long id = S.a_ids[i];
+    S.a_miss[i] = id >= 0 && !(has_pred && bit_test(S.bitP, id));
+  }
+  for (int i = tid; i < a.sp && has_pred; i += blockDim.x) {
+    const long long id = S.p_ids[i];
+    const bool hit = id >= 0 && bit_test(S.bitA, id);
+    const bool hi = hybrid ? a.high[static_cast<long long>(row) * a.sp + i] != 0 : false;
+    S.p_flag[i] = (hit ? 1 : 0) | (hi ? 2 : 0);
+  }
+  for (int c = tid; c < a.sc && has_pred; c += blockDim.x) {
+    bool kp;
+    if (a.variant == kVarUnion) {
+      kp = true;
+    } else if (a.pmode == kPredCompact) {
+      const long long id = load_id(a.rids, a.rids64, static_cast<long long>(row) * a.sc + c);
+      kp = id >= 0 && id < nblocks && bit_test(S.bitA, id);
+    } else {
+      // saved: every hit; hybrid: hits that were kept high.
+      const long long id = S.p_ids[c];
+      const bool hit = id >= 0 && bit_test(S.bitA, id);
+      kp = hit && (a.pmode == kPredSaved || (a.high[static_cast<long long>(row) * a.sp + c] != 0));
+    }
+    S.keep[c] = kp;
+  }
+  __syncthreads();
+
+  // ---- phase 1b (warp 0): counts, low_hit, extra-mass budget, queue
+  if (warp == 0) {
+    int low_hit = 0;
+    if (hybrid) {
+      for (int i = lane; i < a.sp; i += 32) low_hit |= ((S.p_flag[i] & 3) == 1);
+      low_hit = __any_sync(kFull, low_hit);
+    }
+    // wrong = low_hit & !hit & !high
+    int wrong_count = 0;
+    if (hybrid && low_hit) {
+      for (int i = lane; i < a.sp; i += 32) {
+        const bool w = (S.p_flag[i] & 3) == 0 && S.p_ids[i] >= 0;
+        if (w) S.p_flag[i] |= 4;
+        wrong_count += w;
+      }
+      wrong_count = warp_sum_int(wrong_count);
+    }
+    __syncwarp();
+    float lm = neg_inf();
+    int skip = 0;
+    float extra = 0.f;
+    if (hybrid && low_hit) lm = a.low_m[row];
+    const bool eps_variant = a.variant == kVarFused || a.variant == kVarSigned || a.variant == kVarSignedFused;
+    if (eps_variant && a.eps > 0.f && hybrid && low_hit && wrong_count > 0) {
+      // Reference: fused.py:104-112, signed_repair.py:60-73.
+      float rm = neg_inf();
+      for (int c = lane; c < a.sc; c += 32)
+        if (S.keep[c]) rm = fmaxf(rm, a.pm[static_cast<long long>(row) * a.sc + c]);
+      rm = warp_max(rm);
+      const float ref = fmaxf(rm, lm);
+      float wm = 0.f, den = 0.f;
+      for (int i = lane; i < a.sp; i += 32)
+        if (S.p_flag[i] & 4)
+          wm += expf(a.mass_m[static_cast<long long>(row) * a.sp + i] - ref) * a.mass_l[static_cast<long long>(row) * a.sp + i];
+      for (int c = lane; c < a.sc; c += 32)
+        if (S.keep[c])
+          den += expf(a.pm[static_cast<long long>(row) * a.sc + c] - ref) * a.pl[static_cast<long long>(row) * a.sc + c];
+      wm = warp_sum(wm);
+      den = warp_sum(den);
+      den += expf(lm - ref) * a.low_l[row];
+      extra = wm / den;
+      skip = extra <= a.eps;
+    }
+    // Queue: misses in A order, then (unless skipped) wrong-low in P order.
+    int n = 0;
+    for (int base = 0; base < a.sa; base += 32) {
+      const int i = base + lane;
+      const bool m = i < a.sa && S.a_miss[i];
+      const unsigned bal = __ballot_sync(kFull, m);
+      if (m) S.queue[n + __popc(bal & ((1u << lane) - 1))] = i;
+      n += __popc(bal);
+    }
+    const int miss_count = n;
+    if (hybrid && low_hit && !skip) {
+      for (int base = 0; base < a.sp; base += 32) {
+        const int i = base + lane;
+        const bool w = i < a.sp && (S.p_flag[i] & 4);
+        const unsigned bal = __ballot_sync(kFull, w);
+        if (w) S.queue[n + __popc(bal & ((1u << lane) - 1))] = a.sa + i;
+        n += __popc(bal);
+      }
+    }
+    if (lane == 0) {
+      rs.miss_count = miss_count;
+      rs.wrong_count = n - miss_count;
+      rs.queue_len = n;
+      rs.low_hit = low_hit;
+      rs.skip = skip;
+      rs.extra = extra;
+      rs.lm = lm;
+    }
+  }
+  // Per-warp aggregates start empty.
+  for (int i = tid; i < kNW * D; i += blockDim.x) { S.aggU[i] = 0.f; S.aggN[i] = 0.f; }
+  if (lane == 0) {
+    S.aggS[warp * 4 + 0] = neg_inf();
+    S.aggS[warp * 4 + 1] = 0.f;
+    S.aggS[warp * 4 + 2] = 0.f;
+    S.aggS[warp * 4 + 3] = 0.f;
+  }
+  __syncthreads();
+
+  const int neg_rule =
+      (a.variant == kVarFused || (a.variant == kVarSignedFused && a.pmode == kPredCompact) ||
+       (a.variant == kVarSplit && a.pmode == kPredCompact))
+          ? kNegPerToken
+          : kNegBlockRescale;
+  const float lm = rs.lm;
+  float* myU = S.aggU + warp * D;
+  float* myN = S.aggN + warp * D;
+  float* myS = S.aggS + warp * 4;
+
+  // q for this row, lane-owned dims.
+  constexpr int kQ = kFast ? DPL : 1;
+  float qf[kQ];
+  if constexpr (kFast) {
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) qf[j] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + lane * DPL + j);
+  }
+  // Generic path keeps q in the (unused) vecB scratch during job processing.
+  if constexpr (!kFast) {
+    for (int dd = tid; dd < D; dd += blockDim.x) S.vecB[dd] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + dd);
+    __syncthreads();
+  }
+
+  // ---- phase 2: retained states
+  if (has_pred) {
+    for (int c = warp; c < a.sc; c += kNW) {
+      if (!S.keep[c]) continue;
+      const long long j = static_cast<long long>(row) * a.sc + c;
+      const float mb = a.pm[j], lb = a.pl[j];
+      if constexpr (kFast) {
+        float ub[DPL];
+#pragma unroll
+        for (int t = 0; t < DPL; ++t) ub[t] = a.pu[j * D + lane * DPL + t];
+        agg_pos_merge(myS, myU, D, mb, lb, ub, DPL, lane, true);
+      } else {
+        float ub[32];
+        const int per = (D + 31) / 32;
+        for (int t = 0, dd = lane; t < per && t < 32; ++t, dd += 32) ub[t] = dd < D ? a.pu[j * D + dd] : 0.f;
+        agg_pos_merge(myS, myU, D, mb, lb, ub, per, lane, false);
+      }
+    }
+  }
+
+  // ---- phase 2b: queued blocks (and, in phase 4, the strict fallback)
+  unsigned phase_bits = 0;  // per-stage mbarrier parity, persists across passes
+  auto run_blocks = [&](int count, bool fallback_pass) {
+    // Job j of this warp: queue/A index = warp + j * kNW.
+    const int nchunks = (a.L.b + 31) / 32;
+    auto job_entry = [&](int k, long long& bid, bool& negative) {
+      const int e = fallback_pass ? k : S.queue[k];
+      negative = !fallback_pass && e >= a.sa;
+      bid = negative ? S.p_ids[e - a.sa] : S.a_ids[e];
+    };
+    auto job_valid = [&](int k) { return fallback_pass ? S.a_ids[k] >= 0 : true; };
+    if constexpr (kFast) {
+      constexpr int kChunkElems = 32 * 32 * DPL;
+      T* wst = stages + static_cast<size_t>(warp) * NST * (2 * kChunkElems);
+      uint64_t* bar = bars + warp * NST;
+      // Items: (job k, chunk c) for k = warp, warp + kNW, ...; issue ahead NST items.
+      int ik = warp, ic = 0;  // issue cursor
+      while (ik < count && !job_valid(ik)) ik += kNW;
+      auto issue = [&](int st) {
+        if (ik >= count) return;
+        if (lane == 0) {
+          long long bid; bool neg;
+          job_entry(ik, bid, neg);
+          const int t0 = ic * 32, ntok = min(32, a.L.b - t0);
+          T* ks = wst + static_cast<size_t>(st) * 2 * kChunkElems;
+          T* vs = ks + kChunkElems;
+          const unsigned bytes = static_cast<unsigned>(ntok * D * sizeof(T));
+          mbar_arrive_expect_tx(&bar[st], 2 * bytes);
+          const T* K = static_cast<const T*>(a.L.k);
+          const T* V = static_cast<const T*>(a.L.v);
+          if (a.L.page_table == nullptr) {
+            const long long o = block_seg(a.L, r, kv, bid, 0).elem_off + static_cast<long long>(t0) * D;
+            bulk_g2s(ks, K + o, bytes, &bar[st]);
+            bulk_g2s(vs, V + o, bytes, &bar[st]);
+          } else {
+            for (int t = t0; t < t0 + ntok;) {
+              const int pg = t / a.L.page_size, po = t - pg * a.L.page_size;
+              const int cnt = min(a.L.page_size - po, t0 + ntok - t);
+              const long long o = block_seg(a.L, r, kv, bid, pg).elem_off + static_cast<long long>(po) * D;
+              const unsigned sb = static_cast<unsigned>(cnt * D * sizeof(T));
+              bulk_g2s(ks + (t - t0) * D, K + o, sb, &bar[st]);
+              bulk_g2s(vs + (t - t0) * D, V + o, sb, &bar[st]);
+              t += cnt;
+            }
+          }
+        }
+        if (++ic == nchunks) {
+          ic = 0;
+          ik += kNW;
+          while (ik < count && !job_valid(ik)) ik += kNW;
+        }
+      };
+      for (int st = 0; st < NST; ++st) issue(st);
+      __syncwarp();
+      float m = neg_inf(), l = 0.f, u[DPL];
+      int item = 0;
+      (void)item;
+      for (int k = warp; k < count; k += kNW) {
+        if (!job_valid(k)) continue;
+        long long bid; bool neg;
+        job_entry(k, bid, neg);
+        const bool per_token = neg && neg_rule == kNegPerToken;
+        m = neg_inf(); l = 0.f;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) u[j] = 0.f;
+        for (int c = 0; c < nchunks; ++c, ++item) {
+          const int st = item % NST;
+          if (!mbar_wait(&bar[st], (phase_bits >> st) & 1u, a.status)) return;
+          phase_bits ^= 1u << st;
+          const int t0 = c * 32, ntok = min(32, a.L.b - t0);
+          const T* ks = wst + static_cast<size_t>(st) * 2 * kChunkElems;
+          const T* vs = ks + kChunkElems;
+          float p[32];
+#pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            p[t] = 0.f;
+            if (t < ntok) {
+              float kk[DPL];
+              load_vec<T, DPL>(ks + t * D + lane * DPL, kk);
+              float acc = 0.f;
+#pragma unroll
+              for (int j = 0; j < DPL; ++j) acc = fmaf(kk[j], qf[j], acc);
+              p[t] = acc;
+            }
+          }
+          transpose_reduce32(p, lane);
+          const float s = lane < ntok ? p[0] * a.scale : neg_inf();
+          float w;
+          if (per_token) {
+            w = lane < ntok ? expf(s - lm) : 0.f;
+            l += warp_sum(w);
+          } else {
+            const float mn = fmaxf(m, warp_max(s));
+            const float al = expf(m - mn);
+            w = lane < ntok ? expf(s - mn) : 0.f;
+            l = l * al + warp_sum(w);
+            m = mn;
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) u[j] *= al;
+          }
+#pragma unroll 4
+          for (int t = 0; t < ntok; ++t) {
+            const float wt = __shfl_sync(kFull, w, t);
+            float vv[DPL];
+            load_vec<T, DPL>(vs + t * D + lane * DPL, vv);
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) u[j] += wt * vv[j];
+          }
+          __syncwarp();
+          issue(st);
+        }
+        if (!neg) {
+          agg_pos_merge(myS, myU, D, m, l, u, DPL, lane, true);
+        } else {
+          const float f = per_token ? 1.f : expf(m - lm);
+#pragma unroll
+          for (int j = 0; j < DPL; ++j) myN[lane * DPL + j] += u[j] * f;
+          __syncwarp();
+          if (lane == 0) myS[2] += l * f;
+          __syncwarp();
+        }
+      }
+    } else {
+      // Generic: lane = token for QK (q from vecB), lane = dim for PV.
+      const T* K = static_cast<const T*>(a.L.k);
+      const T* V = static_cast<const T*>(a.L.v);
+      __shared__ float gw[kNW][32];
+      __shared__ long long go[kNW][32];
+      const int per = (D + 31) / 32;
+      for (int k = warp; k < count; k += kNW) {
+        if (!job_valid(k)) continue;
+        long long bid; bool neg;
+        job_entry(k, bid, neg);
+        const bool per_token = neg && neg_rule == kNegPerToken;
+        float m = neg_inf(), l = 0.f;
+        float u[32];
+        for (int t = 0; t < 32; ++t) u[t] = 0.f;
+        for (int t0 = 0; t0 < a.L.b; t0 += 32) {
+          const int t = t0 + lane, ntok = min(32, a.L.b - t0);
+          long long toff = 0;
+          float s = neg_inf();
+          if (t < a.L.b) {
+            int seg = 0, within = t;
+            if (a.L.page_table != nullptr) { seg = t / a.L.page_size; within = t - seg * a.L.page_size; }
+            toff = block_seg(a.L, r, kv, bid, seg).elem_off + static_cast<long long>(within) * D;
+            float acc = 0.f;
+            for (int dd = 0; dd < D; ++dd) acc = fmaf(to_f32(K[toff + dd]), S.vecB[dd], acc);
+            s = acc * a.scale;
+          }
+          float w, al = 1.f;
+          if (per_token) {
+            w = t < a.L.b ? expf(s - lm) : 0.f;
+            l += warp_sum(w);
+          } else {
+            const float mn = fmaxf(m, warp_max(s));
+            al = expf(m - mn);
+            w = t < a.L.b ? expf(s - mn) : 0.f;
+            l = l * al + warp_sum(w);
+            m = mn;
+          }
+          gw[warp][lane] = w;
+          go[warp][lane] = toff;
+          __syncwarp();
+          for (int i = 0, dd = lane; i < per && i < 32; ++i, dd += 32) {
+            if (dd >= D) break;
+            float acc = u[i] * al;
+            for (int tt = 0; tt < ntok; ++tt) acc += gw[warp][tt] * to_f32(V[go[warp][tt] + dd]);
+            u[i] = acc;
+          }
+          __syncwarp();
+        }
+        if (!neg) {
+          agg_pos_merge(myS, myU, D, m, l, u, per, lane, false);
+        } else {
+          const float f = per_token ? 1.f : expf(m - lm);
+          for (int i = 0, dd = lane; i < per && dd < D; ++i, dd += 32) myN[dd] += u[i] * f;
+          __syncwarp();
+          if (lane == 0) myS[2] += l * f;
+          __syncwarp();
+        }
+      }
+    }
+  };
+  run_blocks(rs.queue_len, false);
+  __syncthreads();
+
+  // ---- phase 3: combine warps (fixed order) and evaluate guards
+  if (tid == 0) {
+    float M = neg_inf();
+    for (int w = 0; w < kNW; ++w) M = fmaxf(M, S.aggS[w * 4]);
+    float Z = 0.f, Zn = 0.f;
+    for (int w = 0; w < kNW; ++w) {
+      if (S.aggS[w * 4] != neg_inf()) Z += expf(S.aggS[w * 4] - M) * S.aggS[w * 4 + 1];
+      Zn += S.aggS[w * 4 + 2];
+    }
+    sh_f[0] = M;
+    sh_f[1] = Z;
+    sh_f[2] = Zn;
+  }
+  __syncthreads();
+  const float Mp = sh_f[0], Zp = sh_f[1], Zn = sh_f[2];
+  // vecA = positive numerator at frame Mp; vecB = negative numerator (low frame)
+  for (int dd = tid; dd < D; dd += blockDim.x) {
+    float U = 0.f, N = 0.f;
+    for (int w = 0; w < kNW; ++w) {
+      const float Mw = S.aggS[w * 4];
+      if (Mw != neg_inf()) U += expf(Mw - Mp) * S.aggU[w * D + dd];
+      N += S.aggN[w * D + dd];
+    }
+    S.vecA[dd] = U;
+    S.vecB[dd] = N;
+  }
+  if (tid < 4) sh_count[tid] = 0;
+  __syncthreads();
+
+  const bool low_hit = rs.low_hit != 0;
+  float fraction = 1.f;
+  bool bad = false;
+  // Scalars of the final merge: out[d] = (cp * vecA[d] + cl * lowvec[d]) / z
+  float m_final, z_final, cp, cl_scale;
+  if (a.variant == kVarSplit && hybrid) {
+    // kernels.py:221-270: everything in the common frame m.
+    const float m = fmaxf(Mp, low_hit ? lm : neg_inf());
+    const float lowalpha = low_hit ? expf(lm - m) : 0.f;
+    const float ll = low_hit ? a.low_l[row] * lowalpha : 0.f;
+    const float removed = Zn * lowalpha;
+    const float remaining_mass = ll - removed;
+    fraction = ll > 0.f ? remaining_mass / fmaxf(ll, 1e-30f) : 1.f;
+    cp = Mp == neg_inf() ? 0.f : expf(Mp - m);
+    const float z = remaining_mass + cp * Zp;
+    int cancel = 0, invalid = 0;
+    for (int dd = tid; dd < D; dd += blockDim.x) {
+      const float lu = low_hit ? a.low_u[static_cast<long long>(row) * D + dd] * lowalpha : 0.f;
+      const float ru = S.vecB[dd] * lowalpha;
+      const float residual = lu - ru;
+      const float labs = low_hit ? a.low_abs[static_cast<long long>(row) * D + dd] * lowalpha : 0.f;
+      const float sc = labs + fabsf(ru);
+      cancel |= low_hit && (fabsf(residual) < a.cancel_tol * sc) && (sc > 0.f);
+      const float o = (residual + cp * S.vecA[dd]) / fmaxf(z, 1e-30f);
+      invalid |= !isfinite(o);
+    }
+    if (cancel) atomicOr(&sh_count[0], 1);
+    if (invalid) atomicOr(&sh_count[1], 1);
+    __syncthreads();
+    bad = (z <= 0.f) || (fraction < a.min_remaining) || (fraction != fraction) || isinf(z) || sh_count[0] ||
+          sh_count[1];
+    m_final = m;
+    z_final = fmaxf(z, 1e-30f);
+    cl_scale = lowalpha;
+  } else if (hybrid && a.variant != kVarSaved && a.variant != kVarUnion) {
+    // fused.py:94-166 / signed_repair.py:139-165 / signed_fused.py:325-354: low frame.
+    float mass = 0.f;
+    if (low_hit) {
+      const float ll = a.low_l[row];
+      mass = ll - Zn;
+      fraction = mass / ll;
+      int cancel = 0;
+      for (int dd = tid; dd < D; dd += blockDim.x) {
+        const float residual = a.low_u[static_cast<long long>(row) * D + dd] - S.vecB[dd];
+        const float sc = a.low_abs[static_cast<long long>(row) * D + dd] + fabsf(S.vecB[dd]);
+        cancel |= (fabsf(residual) < a.cancel_tol * sc) && (sc > 0.f);
+      }
+      if (cancel) atomicOr(&sh_count[0], 1);
+    }
+    const float m = fmaxf(Mp, low_hit ? lm : neg_inf());
+    const float ref = m == neg_inf() ? 0.f : m;
+    cp = Mp == neg_inf() ? 0.f : expf(Mp - ref);
+    const float lw = low_hit ? expf(lm - ref) : 0.f;
+    const float z = cp * Zp + lw * mass;
+    int invalid = 0;
+    for (int dd = tid; dd < D; dd += blockDim.x) {
+      const float resid = low_hit ? a.low_u[static_cast<long long>(row) * D + dd] - S.vecB[dd] : 0.f;
+      const float o = (cp * S.vecA[dd] + lw * resid) / z;
+      invalid |= !isfinite(o);
+    }
+    if (invalid) atomicOr(&sh_count[1], 1);
+    __syncthreads();
+    bad = (low_hit && ((fraction < a.min_remaining) || (fraction != fraction) || sh_count[0])) || (z <= 0.f) ||
+          isinf(z) || sh_count[1];
+    m_final = ref;
+    z_final = z;
+    cl_scale = lw;
+  } else {
+    // Saved / union / exact: plain LSE merge of retained states and misses.
+    __syncthreads();
+    cp = 1.f;
+    cl_scale = 0.f;
+    m_final = Mp;
+    z_final = Zp;
+  }
+
+  if (bad) {
+    // ---- phase 4: strict fallback over A, in this launch.
+    __syncthreads();
+    for (int i = tid; i < kNW * D; i += blockDim.x) S.aggU[i] = 0.f;
+    if (lane == 0) { S.aggS[warp * 4] = neg_inf(); S.aggS[warp * 4 + 1] = 0.f; }
+    if constexpr (!kFast) {
+      for (int dd = tid; dd < D; dd += blockDim.x) S.vecB[dd] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + dd);
+    }
+    __syncthreads();
+    run_blocks(a.sa, true);
+    __syncthreads();
+    if (tid == 0) {
+      float M = neg_inf();
+      for (int w = 0; w < kNW; ++w) M = fmaxf(M, S.aggS[w * 4]);
+      float Z = 0.f;
+      for (int w = 0; w < kNW; ++w)
+        if (S.aggS[w * 4] != neg_inf()) Z += expf(S.aggS[w * 4] - M) * S.aggS[w * 4 + 1];
+      sh_f[0] = M;
+      sh_f[1] = Z;
+    }
+    __syncthreads();
+    const float M = sh_f[0], Z = sh_f[1];
+    for (int dd = tid; dd < D; dd += blockDim.x) {
+      float U = 0.f;
+      for (int w = 0; w < kNW; ++w)
+        if (S.aggS[w * 4] != neg_inf()) U += expf(S.aggS[w * 4] - M) * S.aggU[w * D + dd];
+      a.out[static_cast<long long>(row) * D + dd] = U / Z;
+    }
+  } else {
+    for (int dd = tid; dd < D; dd += blockDim.x) {
+      float lowv = 0.f;
+      if (cl_scale != 0.f) lowv = a.low_u[static_cast<long long>(row) * D + dd] - S.vecB[dd];
+      a.out[static_cast<long long>(row) * D + dd] = (cp * S.vecA[dd] + cl_scale * lowv) / z_final;
+    }
+  }
+  (void)m_final;
+  if (tid == 0) {
+    if (a.fallback) a.fallback[row] = bad;
+    if (a.remaining) a.remaining[row] = fraction;
+    if (a.approx) a.approx[row] = rs.skip && !bad;
+    if (a.extra) a.extra[row] = (rs.skip && !bad) ? rs.extra : 0.f;
+    if (a.pos_out) a.pos_out[row] = rs.miss_count;
+    if (a.total_out) a.total_out[row] = rs.queue_len;
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+size_t repair_smem_bytes(const RepairArgs& a, int dpl, int elem, int nst) {
+  const int D = a.d;
+  size_t off = 0;
+  if (dpl > 0) off += static_cast<size_t>(kNW) * nst * 2 * 32 * D * elem;
+  const int nwords = (a.max_n + 31) / 32;
+  off += 2 * nwords * 4;
+  off = (off + 7) & ~size_t(7);
+  off += static_cast<size_t>(a.sa) * 8 + static_cast<size_t>(a.sp) * 8;
+  off += static_cast<size_t>(a.sa + a.sp) * 4;
+  off += static_cast<size_t>(2 * kNW * D + kNW * 4 + 2 * D) * 4;
+  off += a.sa + a.sp + a.sc;
+  return off;
+}
+
+template <typename T, int DPL>
+static int launch_repair_t(const RepairArgs& a, cudaStream_t stream) {
+  constexpr int NST = 2;
+  const size_t smem = repair_smem_bytes(a, DPL, sizeof(T), NST);
+  if (smem > 220 * 1024) return -2;
+  auto kern = repair_kernel<T, DPL, NST>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  kern<<<a.rows, kNW * 32, smem, stream>>>(a);
+  return static_cast<int>(cudaGetLastError());
+}
+
+template <typename T>
+static int launch_repair_dt(const RepairArgs& a, cudaStream_t stream) {
+  const uintptr_t pk = reinterpret_cast<uintptr_t>(a.L.k) | reinterpret_cast<uintptr_t>(a.L.v);
+  const bool aligned = (pk & 15) == 0 && (a.d * static_cast<int>(sizeof(T))) % 16 == 0 &&
+                       (a.L.page_table == nullptr || a.L.b % a.L.page_size == 0) && a.L.kv_request_stride % 8 == 0;
+  const size_t fast_stage = static_cast<size_t>(kNW) * 2 * 2 * 32 * a.d * sizeof(T);
+  if (aligned && fast_stage <= 160 * 1024) {
+    if (a.d == 64) return launch_repair_t<T, 2>(a, stream);
+    if (a.d == 128) return launch_repair_t<T, 4>(a, stream);
+    if (a.d == 256) return launch_repair_t<T, 8>(a, stream);
+  }
+  if (a.d > 1024) return -3;
+  return launch_repair_t<T, 0>(a, stream);
+}
+
+int launch_repair(const RepairArgs& a, int kv_dtype, cudaStream_t stream) {
+  if (a.rows == 0) return 0;
+  switch (kv_dtype) {
+    case kF32: return launch_repair_dt<float>(a, stream);
+    case kF16: return launch_repair_dt<__half>(a, stream);
+    default: return launch_repair_dt<__nv_bfloat16>(a, stream);
+  }
+}
+
+}  // namespace stk

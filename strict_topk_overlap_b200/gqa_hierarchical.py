@@ -1,0 +1,45 @@
+"""Tiny-block GQA attention with bounded on-chip merging.
+
+Drop-in for ``strict_topk.gqa_hierarchical`` (reference
+gqa_hierarchical.py:1-144). Per-block states keep the reference's layout;
+exact and repair reductions merge on chip inside one launch.
+"""
+from __future__ import annotations
+
+from . import _lib as L
+from . import gqa
+from .kernels import Prediction, _run_repair
+
+
+def partials(q, k, v, selected):
+    return gqa.partials(q, k, v, selected)
+
+
+def exact(q, k, v, selected):
+    gqa._shape(q, k, v, selected)
+    out, *_ = _run_repair(q, k, v, selected, None, None, L.VAR_SAVED)
+    return out
+
+
+def _repair(q, k, v, selected, predicted, state, shared):
+    h, n, b, d, group, sa = gqa._shape(q, k, v, selected)
+    gqa._validate_ids(q, predicted)
+    sp = predicted.shape[1]
+    if state.u.shape != (h, sp, d) or state.m.shape != (h, sp) or state.l.shape != (h, sp):
+        raise ValueError('prediction state shape does not match predicted blocks')
+    out, *_ = _run_repair(q, k, v, selected, predicted, Prediction(state, "saved"), L.VAR_SAVED)
+    return out
+
+
+def repair_saved(q, k, v, selected, predicted, state):
+    return _repair(q, k, v, selected, predicted, state, False)
+
+
+def repair_saved_shared(q, k, v, selected, predicted, state):
+    """Shared selection: every head has identical ordered IDs (caller-validated
+    contract). Membership is resolved per row on chip, so the result equals
+    repair_saved; attention states stay independent for every query head."""
+    return _repair(q, k, v, selected, predicted, state, True)
+
+
+select_blocks_shared = gqa.select_blocks_shared
