@@ -1,0 +1,142 @@
+"""Speculative decode-step orchestration: selector || speculation, then repair.
+
+``overlap_run`` is the drop-in for the reference's two-stream harness
+(benchmarks/run_benchmark.py:99-118): the selector runs on one side stream,
+speculation over the predicted IDs on another, the caller's stream joins both
+and runs the repair. ``SpeculativeDecoder`` packages one full decode step for
+fixed shapes and captures it (both branches and the join) in a CUDA graph, so
+a step is one graph launch; ``serial`` steps run select -> attention on one
+stream with the same kernels, which is the baseline the speculative path must
+beat.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import fused, gqa, gqa_light, kernels, signed_fused
+
+# method -> (prediction mode, repair entry point)
+METHODS = {
+    "saved": ("saved", "gqa"),                  # gqa.partials + gqa.repair_saved
+    "light": ("saved", "light"),                # gqa.partials + gqa_light.repair_saved_light
+    "compact": ("compact", "fused"),            # compact speculation + repair_fused
+    "repair_fused": ("hybrid", "fused"),        # hybrid speculation + repair_fused
+    "signed_fused": ("hybrid", "signed_fused"), # hybrid speculation + repair_signed_fused
+}
+
+
+def overlap_run(selector, speculative, finish, select_stream, predict_stream):
+    """Run selector() and speculative() concurrently, then finish(selected, state)
+    on the current stream (reference benchmarks/run_benchmark.py:99-118)."""
+    main = torch.cuda.current_stream()
+    select_stream.wait_stream(main)
+    predict_stream.wait_stream(main)
+    with torch.cuda.stream(select_stream):
+        a = selector()
+    with torch.cuda.stream(predict_stream):
+        state = speculative()
+    main.wait_stream(select_stream)
+    main.wait_stream(predict_stream)
+    a.record_stream(main)
+
+    def record(obj):
+        if isinstance(obj, torch.Tensor):
+            obj.record_stream(main)
+        elif hasattr(obj, "__dict__"):
+            for value in vars(obj).values():
+                record(value)
+    record(state)
+    return finish(a, state)
+
+
+@dataclass
+class StepSpec:
+    """One decode step's configuration."""
+    topk: int
+    method: str = "saved"
+    mass_threshold: float = 0.1
+    max_extra_mass: float = 0.0
+    min_remaining: float = 1e-3
+    cancellation_tol: float = 1e-5
+
+
+def _speculate_fn(spec, q, k, v, p):
+    mode, _ = METHODS[spec.method]
+    if mode == "saved":
+        return lambda: gqa.partials(q, k, v, p)
+    keep = spec.max_extra_mass > 0
+    return lambda: kernels.speculate(q, k, v, p, mode=mode, mass_threshold=spec.mass_threshold, keep_mass=keep)
+
+
+def _finish_fn(spec, q, k, v, p):
+    _, rep = METHODS[spec.method]
+    if rep == "gqa":
+        return lambda a, st: gqa.repair_saved(q, k, v, a, p, st)
+    if rep == "light":
+        return lambda a, st: gqa_light.repair_saved_light(q, k, v, a, p, st)
+    if rep == "fused":
+        return lambda a, pred: fused.repair_fused(q, k, v, a, p, pred, spec.min_remaining, spec.cancellation_tol,
+                                                  spec.max_extra_mass).output
+    return lambda a, pred: signed_fused.repair_signed_fused(q, k, v, a, p, pred, spec.min_remaining,
+                                                            spec.cancellation_tol, spec.max_extra_mass).output
+
+
+class SpeculativeDecoder:
+    """One speculative decode step over a fixed KV cache and static input
+    buffers ``q`` [Hq, D] and ``predicted`` [Hq, P] (copy new values into
+    them between steps). ``step()`` returns the FP32 output buffer [Hq, D];
+    ``selected`` holds the step's strict Top-K IDs.
+
+    With ``graph=True`` the whole step (both concurrent branches and the
+    repair) is captured once and replayed as one CUDA-graph launch."""
+
+    def __init__(self, q, k, v, lo, hi, predicted, spec: StepSpec, *, graph: bool = True, serial: bool = False):
+        self.q, self.k, self.v, self.lo, self.hi, self.predicted = q, k, v, lo, hi, predicted
+        self.spec = spec
+        self.serial = serial
+        self._sel_stream = torch.cuda.Stream(q.device)
+        self._pred_stream = torch.cuda.Stream(q.device)
+        self._selector = lambda: gqa.select_blocks(q, lo, hi, spec.topk)
+        self._spec = _speculate_fn(spec, q, k, v, predicted)
+        self._finish = _finish_fn(spec, q, k, v, predicted)
+        self.graph = None
+        self.out = None
+        self.selected = None
+        if graph:
+            self._capture()
+
+    def _run(self):
+        if self.serial:
+            a = self._selector()
+            return gqa.exact(self.q, self.k, self.v, a), a
+        sel_box = {}
+
+        def finish(a, st):
+            sel_box["a"] = a
+            return self._finish(a, st)
+        out = overlap_run(self._selector, self._spec, finish, self._sel_stream, self._pred_stream)
+        return out, sel_box["a"]
+
+    def _capture(self):
+        side = torch.cuda.Stream(self.q.device)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                self._run()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize(self.q.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out, self.selected = self._run()
+
+    def step(self):
+        if self.graph is not None:
+            self.graph.replay()
+            return self.out
+        self.out, self.selected = self._run()
+        return self.out
+
+    def close(self):
+        self.graph = None
