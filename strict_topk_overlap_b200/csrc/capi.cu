@@ -143,6 +143,7 @@ int stk_select_topk(const void* q, int q_dtype, const float* lo, const float* hi
   a.block_offsets = block_offsets; a.total_blocks = total_blocks;
   a.group_select = group_select; a.scores_f32 = nullptr;
   a.scores_f64 = static_cast<double*>(workspace);
+  a.status = status;
   int rc = launch_score(a, s);
   if (rc) return cuda_status(rc, "score");
   SelectArgs b{};

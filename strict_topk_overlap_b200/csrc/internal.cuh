@@ -29,6 +29,7 @@ struct ScoreArgs {
   int group_select;   // 1: write per-KV-group sums instead of per-head scores
   float* scores_f32;  // optional [hq, total_blocks]
   double* scores_f64; // optional [hq or hmeta (group), total_blocks]
+  int* status;
 };
 
 struct SelectArgs {
@@ -100,6 +101,7 @@ struct RepairArgs {
   int variant;
   float min_remaining, cancel_tol, eps;
   int max_n;  // upper bound of blocks per request (bitmap size)
+  int stage_pred;  // set by the launcher: the row's prediction numerators fit in shared memory
   float* out;                // [rows, d]
   unsigned char* fallback;   // [rows]
   float* remaining;          // [rows]

@@ -10,43 +10,29 @@
 //   gqa_hierarchical.py:99-130 (_match_ids, REPAIR packed partials, _groups)
 //   kernels.py:437-447       (exact_attention = repair with no prediction)
 //
-// One CTA per (request, query head) row. Phases:
-//   1. set difference A vs P through shared-memory bitmaps over block IDs;
-//      hit / miss / high / wrong-low flags; optional extra-mass budget (EPS);
-//      job queue = misses in A order, then wrong-low blocks in P order.
-//   2. warps stream queued blocks through a private TMA (cp.async.bulk) ring:
-//      misses are added (+) to a per-warp LSE state, wrong-low blocks are
-//      subtracted (-) from the low group in its own exponent frame, retained
-//      prediction states are merged in.
-//   3. warp states are merged in warp order; the variant's guards (remaining
-//      low mass, cancellation envelope, non-finite output) are evaluated.
+// One CTA (kNW warps) per (request, query head) row. Phases:
+//   0. the row's prediction numerators [SC, D] start streaming into shared
+//      memory (one bulk copy) while
+//   1. the set difference A vs P is taken through shared-memory bitmaps over
+//      block IDs: hit / miss / high / wrong-low flags, the optional
+//      extra-mass budget (EPS), and the job queue = misses in A order, then
+//      wrong-low blocks in P order;
+//   2. every warp starts the bulk copy of its first queued block, then all
+//      threads merge the retained prediction states (weights precomputed,
+//      threads over dims), then warps reduce their queued blocks: misses are
+//      added (+) to a per-warp LSE state, wrong-low blocks are subtracted (-)
+//      from the low group in its own exponent frame;
+//   3. per-warp states merge in a fixed order; the variant's guards (remaining
+//      low mass, cancellation envelope, non-finite output) are evaluated;
 //   4. a flagged row recomputes the strict selected set in the same launch.
 #include "internal.cuh"
 
 namespace stk {
 
-
-
-constexpr int kNW = 4;  // warps per CTA
+constexpr int kNW = 8;  // warps per CTA
 
 // Negative-job frame rules.
 enum NegRule : int { kNegPerToken = 0, kNegBlockRescale = 1 };
-
-struct RepairShared {
-  unsigned* bitA;
-  unsigned* bitP;
-  long long* a_ids;
-  long long* p_ids;
-  unsigned char* a_miss;
-  unsigned char* p_flag;  // bit0 hit, bit1 high, bit2 wrong
-  unsigned char* keep;
-  int* queue;
-  float* aggU;   // [kNW][d] positive numerators
-  float* aggN;   // [kNW][d] negative numerators (low frame)
-  float* aggS;   // [kNW][4]: posM, posZ, negZ, -
-  float* vecA;   // [d]
-  float* vecB;   // [d]
-};
 
 struct RowScalars {
   int miss_count, wrong_count, queue_len;
@@ -60,27 +46,7 @@ __device__ __forceinline__ bool bit_test(const unsigned* bits, long long i) {
   return (bits[i >> 5] >> (i & 31)) & 1u;
 }
 
-// ------------------------------------------------------------------ per-warp block engine
-
-// Accumulates a block (all chunks) into either the warp's positive LSE state
-// or its negative low-frame sums. `neg_rule` / `frame` only matter for negatives.
-template <typename T, int DPL>
-struct BlockAcc {
-  float m, l;
-  float u[DPL > 0 ? DPL : 1];
-};
-
-template <typename T, int DPL, int NST>
-struct WarpRing {
-  T* stages;
-  uint64_t* bar;
-  unsigned phase;
-  static constexpr int D = 32 * DPL;
-  static constexpr int kChunkElems = 32 * D;
-  static constexpr int kStageElems = 2 * kChunkElems;
-};
-
-// Merge a block state into the warp's positive aggregate (smem, lane-owned dims).
+// Merge a block state into a warp's positive aggregate (shared memory).
 __device__ __forceinline__ void agg_pos_merge(float* S, float* U, int d, float mb, float lb, const float* ub_lane,
                                               int dpl, int lane, bool lane_contig) {
   if (mb == neg_inf()) return;
@@ -104,12 +70,92 @@ __device__ __forceinline__ void agg_pos_merge(float* S, float* U, int d, float m
   __syncwarp();
 }
 
+struct RepairSmem {
+  float* pu;      // [sc, d] staged prediction numerators (or null)
+  float* pw;      // [sc] retained weights exp(pm - M_keep) (0 when not kept)
+  unsigned* bitA;
+  unsigned* bitP;
+  long long* a_ids;
+  long long* p_ids;
+  int* queue;
+  float* aggU;    // [kNW + 1][d]: per-warp positive numerators, then the retained aggregate
+  float* aggN;    // [kNW][d]: per-warp negative numerators (low frame)
+  float* aggS;    // [kNW + 1][4]: M, Z, Zneg, -
+  float* vecA;
+  float* vecB;
+  float* pm_s;    // [sc] retained maxima
+  float* pl_s;    // [sc] retained normalisers
+  float* mm_s;    // [sp] keep_mass maxima (budget)
+  float* ml_s;    // [sp] keep_mass normalisers (budget)
+  float* lu_s;    // [d] low-group numerator
+  float* la_s;    // [d] low-group absolute envelope
+  unsigned char* high_s;  // [sp]
+  unsigned char* a_miss;
+  unsigned char* p_flag;  // bit0 hit, bit1 high, bit2 wrong
+  unsigned char* keep;
+};
+
+template <int DPL, int NST, typename T>
+__host__ __device__ inline size_t repair_layout(const RepairArgs& a, RepairSmem* S, unsigned char* base) {
+  const int D = a.d;
+  size_t off = 0;
+  auto take = [&](size_t bytes, size_t align) {
+    off = (off + align - 1) & ~(align - 1);
+    const size_t at = off;
+    off += bytes;
+    return at;
+  };
+  const size_t stages = DPL > 0 ? static_cast<size_t>(kNW) * NST * 2 * 32 * D * sizeof(T) : 0;
+  take(stages, 128);
+  const size_t pu_at = a.stage_pred ? take(static_cast<size_t>(a.sc) * D * 4, 128) : 0;
+  const size_t pw_at = take(static_cast<size_t>(a.sc) * 4, 16);
+  const int nwords = (a.max_n + 31) / 32;
+  const size_t ba = take(nwords * 4, 16), bp = take(nwords * 4, 16);
+  const size_t ai = take(static_cast<size_t>(a.sa) * 8, 16), pi = take(static_cast<size_t>(a.sp) * 8, 16);
+  const size_t qu = take(static_cast<size_t>(a.sa + a.sp) * 4, 16);
+  const size_t au = take(static_cast<size_t>(kNW + 1) * D * 4, 16);
+  const size_t an = take(static_cast<size_t>(kNW) * D * 4, 16);
+  const size_t as = take(static_cast<size_t>(kNW + 1) * 16, 16);
+  const size_t va = take(D * 4, 16), vb = take(D * 4, 16);
+  const size_t pms = take(static_cast<size_t>(a.sc) * 4, 16), pls = take(static_cast<size_t>(a.sc) * 4, 16);
+  const size_t mms = take(static_cast<size_t>(a.sp) * 4, 16), mls = take(static_cast<size_t>(a.sp) * 4, 16);
+  const size_t lus = take(D * 4, 16), las = take(D * 4, 16);
+  const size_t hs = take(a.sp, 1);
+  const size_t am = take(a.sa, 1), pf = take(a.sp, 1), kp = take(a.sc, 1);
+  if (S != nullptr) {
+    S->pu = a.stage_pred ? reinterpret_cast<float*>(base + pu_at) : nullptr;
+    S->pw = reinterpret_cast<float*>(base + pw_at);
+    S->bitA = reinterpret_cast<unsigned*>(base + ba);
+    S->bitP = reinterpret_cast<unsigned*>(base + bp);
+    S->a_ids = reinterpret_cast<long long*>(base + ai);
+    S->p_ids = reinterpret_cast<long long*>(base + pi);
+    S->queue = reinterpret_cast<int*>(base + qu);
+    S->aggU = reinterpret_cast<float*>(base + au);
+    S->aggN = reinterpret_cast<float*>(base + an);
+    S->aggS = reinterpret_cast<float*>(base + as);
+    S->vecA = reinterpret_cast<float*>(base + va);
+    S->vecB = reinterpret_cast<float*>(base + vb);
+    S->pm_s = reinterpret_cast<float*>(base + pms);
+    S->pl_s = reinterpret_cast<float*>(base + pls);
+    S->mm_s = reinterpret_cast<float*>(base + mms);
+    S->ml_s = reinterpret_cast<float*>(base + mls);
+    S->lu_s = reinterpret_cast<float*>(base + lus);
+    S->la_s = reinterpret_cast<float*>(base + las);
+    S->high_s = base + hs;
+    S->a_miss = base + am;
+    S->p_flag = base + pf;
+    S->keep = base + kp;
+  }
+  return off;
+}
+
 // ------------------------------------------------------------------ kernel
 
 template <typename T, int DPL, int NST>
 __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ uint64_t bars[kNW * NST];
+  __shared__ uint64_t pbar;
   __shared__ RowScalars rs;
   __shared__ int sh_count[4];
   __shared__ float sh_f[8];
@@ -124,49 +170,63 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
   const bool hybrid = a.pmode == kPredHybrid || a.pmode == kPredCompact;
   const bool has_pred = a.pmode != kPredNone;
 
-  // ---- shared memory carve-up
-  size_t off = 0;
-  T* stages = nullptr;
-  const size_t stage_elems = kFast ? static_cast<size_t>(2) * 32 * D : 0;
-  if (kFast) {
-    stages = reinterpret_cast<T*>(smem);
-    off += kNW * NST * stage_elems * sizeof(T);
-  }
-  RepairShared S;
+  RepairSmem S;
+  repair_layout<DPL, NST, T>(a, &S, smem);
+  T* stages = reinterpret_cast<T*>(smem);
   const int nwords = (a.max_n + 31) / 32;
-  S.bitA = reinterpret_cast<unsigned*>(smem + off); off += nwords * 4;
-  S.bitP = reinterpret_cast<unsigned*>(smem + off); off += nwords * 4;
-  off = (off + 7) & ~size_t(7);
-  S.a_ids = reinterpret_cast<long long*>(smem + off); off += a.sa * 8;
-  S.p_ids = reinterpret_cast<long long*>(smem + off); off += a.sp * 8;
-  S.queue = reinterpret_cast<int*>(smem + off); off += (a.sa + a.sp) * 4;
-  S.aggU = reinterpret_cast<float*>(smem + off); off += kNW * D * 4;
-  S.aggN = reinterpret_cast<float*>(smem + off); off += kNW * D * 4;
-  S.aggS = reinterpret_cast<float*>(smem + off); off += kNW * 4 * 4;
-  S.vecA = reinterpret_cast<float*>(smem + off); off += D * 4;
-  S.vecB = reinterpret_cast<float*>(smem + off); off += D * 4;
-  S.a_miss = smem + off; off += a.sa;
-  S.p_flag = smem + off; off += a.sp;
-  S.keep = smem + off; off += a.sc;
 
-  // ---- phase 1: ids, bitmaps, flags
-  for (int i = tid; i < nwords; i += blockDim.x) { S.bitA[i] = 0; S.bitP[i] = 0; }
-  if (kFast && lane == 0) {
-    for (int st = 0; st < NST; ++st) mbar_init(&bars[warp * NST + st], 1);
+  // ---- phase 0: barriers; stream the row's prediction numerators in.
+  if (lane == 0) {
+    if (kFast)
+      for (int st = 0; st < NST; ++st) mbar_init(&bars[warp * NST + st], 1);
+    if (warp == 0) mbar_init(&pbar, 1);
     fence_barrier_init();
   }
   __syncthreads();
+  if (tid == 0 && a.stage_pred) {
+    const unsigned bytes = static_cast<unsigned>(a.sc) * D * 4;
+    mbar_arrive_expect_tx(&pbar, bytes);
+    bulk_g2s(S.pu, a.pu + static_cast<long long>(row) * a.sc * D, bytes, &pbar);
+  }
+
+  // ---- phase 1: every per-row global load in one independent pass.
+  const bool want_mass = hybrid && a.eps > 0.f && a.mass_m != nullptr;
+  for (int i = tid; i < nwords; i += blockDim.x) { S.bitA[i] = 0; S.bitP[i] = 0; }
+  for (int i = tid; i < a.sa; i += blockDim.x) S.a_ids[i] = load_id(a.sel, a.sel64, static_cast<long long>(row) * a.sa + i);
+  if (has_pred) {
+    const long long pr = static_cast<long long>(row) * a.sp, sr = static_cast<long long>(row) * a.sc;
+    for (int i = tid; i < a.sp; i += blockDim.x) {
+      S.p_ids[i] = load_id(a.pred, a.pred64, pr + i);
+      S.high_s[i] = hybrid ? a.high[pr + i] : 0;
+      if (want_mass) { S.mm_s[i] = a.mass_m[pr + i]; S.ml_s[i] = a.mass_l[pr + i]; }
+    }
+    for (int c = tid; c < a.sc; c += blockDim.x) {
+      S.pm_s[c] = a.pm[sr + c];
+      S.pl_s[c] = a.pl[sr + c];
+      if (a.pmode == kPredCompact) S.keep[c] = 0, S.pw[c] = 0.f;
+    }
+    if (a.pmode == kPredCompact)
+      for (int c = tid; c < a.sc; c += blockDim.x) {
+        // Compact retained IDs are checked against A after the bitmaps exist.
+        const long long id = load_id(a.rids, a.rids64, sr + c);
+        S.pw[c] = __int_as_float(static_cast<int>(id));  // staged temporarily
+      }
+    if (hybrid)
+      for (int dd = tid; dd < D; dd += blockDim.x) {
+        S.lu_s[dd] = a.low_u[static_cast<long long>(row) * D + dd];
+        S.la_s[dd] = a.low_abs[static_cast<long long>(row) * D + dd];
+      }
+  }
+  __syncthreads();
   for (int i = tid; i < a.sa; i += blockDim.x) {
-    long long id = load_id(a.sel, a.sel64, static_cast<long long>(row) * a.sa + i);
-    if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); id = -1; }
-    S.a_ids[i] = id;
+    long long id = S.a_ids[i];
+    if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); id = -1; S.a_ids[i] = -1; }
     if (id >= 0) atomicOr(&S.bitA[id >> 5], 1u << (id & 31));
   }
   if (has_pred) {
     for (int i = tid; i < a.sp; i += blockDim.x) {
-      long long id = load_id(a.pred, a.pred64, static_cast<long long>(row) * a.sp + i);
-      if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); id = -1; }
-      S.p_ids[i] = id;
+      long long id = S.p_ids[i];
+      if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); id = -1; S.p_ids[i] = -1; }
       if (id >= 0) atomicOr(&S.bitP[id >> 5], 1u << (id & 31));
     }
   }
@@ -178,34 +238,34 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
   for (int i = tid; i < a.sp && has_pred; i += blockDim.x) {
     const long long id = S.p_ids[i];
     const bool hit = id >= 0 && bit_test(S.bitA, id);
-    const bool hi = hybrid ? a.high[static_cast<long long>(row) * a.sp + i] != 0 : false;
-    S.p_flag[i] = (hit ? 1 : 0) | (hi ? 2 : 0);
+    S.p_flag[i] = (hit ? 1 : 0) | (S.high_s[i] ? 2 : 0);
   }
   for (int c = tid; c < a.sc && has_pred; c += blockDim.x) {
     bool kp;
     if (a.variant == kVarUnion) {
       kp = true;
     } else if (a.pmode == kPredCompact) {
-      const long long id = load_id(a.rids, a.rids64, static_cast<long long>(row) * a.sc + c);
+      const long long id = static_cast<long long>(__float_as_int(S.pw[c]));
       kp = id >= 0 && id < nblocks && bit_test(S.bitA, id);
     } else {
       // saved: every hit; hybrid: hits that were kept high.
       const long long id = S.p_ids[c];
       const bool hit = id >= 0 && bit_test(S.bitA, id);
-      kp = hit && (a.pmode == kPredSaved || (a.high[static_cast<long long>(row) * a.sp + c] != 0));
+      kp = hit && (a.pmode == kPredSaved || S.high_s[c] != 0);
     }
     S.keep[c] = kp;
+    S.pw[c] = kp ? S.pm_s[c] : neg_inf();
   }
   __syncthreads();
 
-  // ---- phase 1b (warp 0): counts, low_hit, extra-mass budget, queue
+  // ---- phase 1b (warp 0): counts, low_hit, extra-mass budget, queue;
+  //      (warp 1): retained-state weights.
   if (warp == 0) {
     int low_hit = 0;
     if (hybrid) {
       for (int i = lane; i < a.sp; i += 32) low_hit |= ((S.p_flag[i] & 3) == 1);
       low_hit = __any_sync(kFull, low_hit);
     }
-    // wrong = low_hit & !hit & !high
     int wrong_count = 0;
     if (hybrid && low_hit) {
       for (int i = lane; i < a.sp; i += 32) {
@@ -225,23 +285,20 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
       // Reference: fused.py:104-112, signed_repair.py:60-73.
       float rm = neg_inf();
       for (int c = lane; c < a.sc; c += 32)
-        if (S.keep[c]) rm = fmaxf(rm, a.pm[static_cast<long long>(row) * a.sc + c]);
+        if (S.keep[c]) rm = fmaxf(rm, S.pm_s[c]);
       rm = warp_max(rm);
       const float ref = fmaxf(rm, lm);
       float wm = 0.f, den = 0.f;
       for (int i = lane; i < a.sp; i += 32)
-        if (S.p_flag[i] & 4)
-          wm += expf(a.mass_m[static_cast<long long>(row) * a.sp + i] - ref) * a.mass_l[static_cast<long long>(row) * a.sp + i];
+        if (S.p_flag[i] & 4) wm += expf(S.mm_s[i] - ref) * S.ml_s[i];
       for (int c = lane; c < a.sc; c += 32)
-        if (S.keep[c])
-          den += expf(a.pm[static_cast<long long>(row) * a.sc + c] - ref) * a.pl[static_cast<long long>(row) * a.sc + c];
+        if (S.keep[c]) den += expf(S.pm_s[c] - ref) * S.pl_s[c];
       wm = warp_sum(wm);
       den = warp_sum(den);
       den += expf(lm - ref) * a.low_l[row];
       extra = wm / den;
       skip = extra <= a.eps;
     }
-    // Queue: misses in A order, then (unless skipped) wrong-low in P order.
     int n = 0;
     for (int base = 0; base < a.sa; base += 32) {
       const int i = base + lane;
@@ -269,14 +326,34 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
       rs.extra = extra;
       rs.lm = lm;
     }
+  } else if (warp == 1 && has_pred) {
+    // Retained aggregate scalars: M = max kept m, Z = sum exp(m - M) l, weights.
+    float M = neg_inf();
+    for (int c = lane; c < a.sc; c += 32) M = fmaxf(M, S.pw[c]);
+    M = warp_max(M);
+    float Z = 0.f;
+    for (int c = lane; c < a.sc; c += 32) {
+      const float w = S.keep[c] ? expf(S.pw[c] - M) : 0.f;
+      S.pw[c] = w;
+      if (S.keep[c]) Z += w * S.pl_s[c];
+    }
+    Z = warp_sum(Z);
+    if (lane == 0) {
+      S.aggS[kNW * 4 + 0] = M;
+      S.aggS[kNW * 4 + 1] = Z;
+    }
   }
-  // Per-warp aggregates start empty.
-  for (int i = tid; i < kNW * D; i += blockDim.x) { S.aggU[i] = 0.f; S.aggN[i] = 0.f; }
-  if (lane == 0) {
+  for (int i = tid; i < (kNW + 1) * D; i += blockDim.x) S.aggU[i] = 0.f;
+  for (int i = tid; i < kNW * D; i += blockDim.x) S.aggN[i] = 0.f;
+  if (lane == 0 && warp < kNW) {
     S.aggS[warp * 4 + 0] = neg_inf();
     S.aggS[warp * 4 + 1] = 0.f;
     S.aggS[warp * 4 + 2] = 0.f;
     S.aggS[warp * 4 + 3] = 0.f;
+  }
+  if (tid == 0 && !has_pred) {
+    S.aggS[kNW * 4 + 0] = neg_inf();
+    S.aggS[kNW * 4 + 1] = 0.f;
   }
   __syncthreads();
 
@@ -290,96 +367,83 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
   float* myN = S.aggN + warp * D;
   float* myS = S.aggS + warp * 4;
 
-  // q for this row, lane-owned dims.
   constexpr int kQ = kFast ? DPL : 1;
   float qf[kQ];
   if constexpr (kFast) {
 #pragma unroll
     for (int j = 0; j < DPL; ++j) qf[j] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + lane * DPL + j);
   }
-  // Generic path keeps q in the (unused) vecB scratch during job processing.
   if constexpr (!kFast) {
+    // The generic path keeps q in vecB while blocks are processed.
     for (int dd = tid; dd < D; dd += blockDim.x) S.vecB[dd] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + dd);
     __syncthreads();
   }
 
-  // ---- phase 2: retained states
-  if (has_pred) {
-    for (int c = warp; c < a.sc; c += kNW) {
-      if (!S.keep[c]) continue;
-      const long long j = static_cast<long long>(row) * a.sc + c;
-      const float mb = a.pm[j], lb = a.pl[j];
-      if constexpr (kFast) {
-        float ub[DPL];
-#pragma unroll
-        for (int t = 0; t < DPL; ++t) ub[t] = a.pu[j * D + lane * DPL + t];
-        agg_pos_merge(myS, myU, D, mb, lb, ub, DPL, lane, true);
+  // ---- per-warp block pipeline (fast path): items = (queue entry, chunk)
+  unsigned phase_bits = 0;
+  const int nchunks = (a.L.b + 31) / 32;
+  constexpr int kChunkElems = 32 * 32 * (DPL > 0 ? DPL : 1);
+  T* wst = stages + static_cast<size_t>(warp) * NST * (2 * kChunkElems);
+  uint64_t* wbar = bars + warp * NST;
+  int ik = warp, ic = 0;  // issue cursor
+  bool fallback_pass = false;
+  int count = 0;
+  auto job_entry = [&](int k, long long& bid, bool& negative) {
+    const int e = fallback_pass ? k : S.queue[k];
+    negative = !fallback_pass && e >= a.sa;
+    bid = negative ? S.p_ids[e - a.sa] : S.a_ids[e];
+  };
+  auto job_valid = [&](int k) { return fallback_pass ? S.a_ids[k] >= 0 : true; };
+  auto issue = [&](int st) {
+    if (ik >= count) return;
+    if (lane == 0) {
+      long long bid; bool neg;
+      job_entry(ik, bid, neg);
+      const int t0 = ic * 32, ntok = min(32, a.L.b - t0);
+      T* ks = wst + static_cast<size_t>(st) * 2 * kChunkElems;
+      T* vs = ks + kChunkElems;
+      const unsigned bytes = static_cast<unsigned>(ntok * D * sizeof(T));
+      mbar_arrive_expect_tx(&wbar[st], 2 * bytes);
+      const T* K = static_cast<const T*>(a.L.k);
+      const T* V = static_cast<const T*>(a.L.v);
+      if (a.L.page_table == nullptr) {
+        const long long o = block_seg(a.L, r, kv, bid, 0).elem_off + static_cast<long long>(t0) * D;
+        bulk_g2s(ks, K + o, bytes, &wbar[st]);
+        bulk_g2s(vs, V + o, bytes, &wbar[st]);
       } else {
-        float ub[32];
-        const int per = (D + 31) / 32;
-        for (int t = 0, dd = lane; t < per && t < 32; ++t, dd += 32) ub[t] = dd < D ? a.pu[j * D + dd] : 0.f;
-        agg_pos_merge(myS, myU, D, mb, lb, ub, per, lane, false);
+        for (int t = t0; t < t0 + ntok;) {
+          const int pg = t / a.L.page_size, po = t - pg * a.L.page_size;
+          const int cnt = min(a.L.page_size - po, t0 + ntok - t);
+          const long long o = block_seg(a.L, r, kv, bid, pg).elem_off + static_cast<long long>(po) * D;
+          const unsigned sb = static_cast<unsigned>(cnt * D * sizeof(T));
+          bulk_g2s(ks + (t - t0) * D, K + o, sb, &wbar[st]);
+          bulk_g2s(vs + (t - t0) * D, V + o, sb, &wbar[st]);
+          t += cnt;
+        }
       }
     }
-  }
-
-  // ---- phase 2b: queued blocks (and, in phase 4, the strict fallback)
-  unsigned phase_bits = 0;  // per-stage mbarrier parity, persists across passes
-  auto run_blocks = [&](int count, bool fallback_pass) {
-    // Job j of this warp: queue/A index = warp + j * kNW.
-    const int nchunks = (a.L.b + 31) / 32;
-    auto job_entry = [&](int k, long long& bid, bool& negative) {
-      const int e = fallback_pass ? k : S.queue[k];
-      negative = !fallback_pass && e >= a.sa;
-      bid = negative ? S.p_ids[e - a.sa] : S.a_ids[e];
-    };
-    auto job_valid = [&](int k) { return fallback_pass ? S.a_ids[k] >= 0 : true; };
-    if constexpr (kFast) {
-      constexpr int kChunkElems = 32 * 32 * DPL;
-      T* wst = stages + static_cast<size_t>(warp) * NST * (2 * kChunkElems);
-      uint64_t* bar = bars + warp * NST;
-      // Items: (job k, chunk c) for k = warp, warp + kNW, ...; issue ahead NST items.
-      int ik = warp, ic = 0;  // issue cursor
+    if (++ic == nchunks) {
+      ic = 0;
+      ik += kNW;
       while (ik < count && !job_valid(ik)) ik += kNW;
-      auto issue = [&](int st) {
-        if (ik >= count) return;
-        if (lane == 0) {
-          long long bid; bool neg;
-          job_entry(ik, bid, neg);
-          const int t0 = ic * 32, ntok = min(32, a.L.b - t0);
-          T* ks = wst + static_cast<size_t>(st) * 2 * kChunkElems;
-          T* vs = ks + kChunkElems;
-          const unsigned bytes = static_cast<unsigned>(ntok * D * sizeof(T));
-          mbar_arrive_expect_tx(&bar[st], 2 * bytes);
-          const T* K = static_cast<const T*>(a.L.k);
-          const T* V = static_cast<const T*>(a.L.v);
-          if (a.L.page_table == nullptr) {
-            const long long o = block_seg(a.L, r, kv, bid, 0).elem_off + static_cast<long long>(t0) * D;
-            bulk_g2s(ks, K + o, bytes, &bar[st]);
-            bulk_g2s(vs, V + o, bytes, &bar[st]);
-          } else {
-            for (int t = t0; t < t0 + ntok;) {
-              const int pg = t / a.L.page_size, po = t - pg * a.L.page_size;
-              const int cnt = min(a.L.page_size - po, t0 + ntok - t);
-              const long long o = block_seg(a.L, r, kv, bid, pg).elem_off + static_cast<long long>(po) * D;
-              const unsigned sb = static_cast<unsigned>(cnt * D * sizeof(T));
-              bulk_g2s(ks + (t - t0) * D, K + o, sb, &bar[st]);
-              bulk_g2s(vs + (t - t0) * D, V + o, sb, &bar[st]);
-              t += cnt;
-            }
-          }
-        }
-        if (++ic == nchunks) {
-          ic = 0;
-          ik += kNW;
-          while (ik < count && !job_valid(ik)) ik += kNW;
-        }
-      };
+    }
+  };
+  auto prefill = [&](int cnt, bool fb) {
+    fallback_pass = fb;
+    count = cnt;
+    ik = warp;
+    ic = 0;
+    while (ik < count && !job_valid(ik)) ik += kNW;
+    if constexpr (kFast) {
       for (int st = 0; st < NST; ++st) issue(st);
       __syncwarp();
-      float m = neg_inf(), l = 0.f, u[DPL];
+    }
+  };
+
+  auto consume = [&]() {
+    if constexpr (kFast) {
       int item = 0;
-      (void)item;
+      float m, l, u[DPL];
       for (int k = warp; k < count; k += kNW) {
         if (!job_valid(k)) continue;
         long long bid; bool neg;
@@ -390,7 +454,7 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
         for (int j = 0; j < DPL; ++j) u[j] = 0.f;
         for (int c = 0; c < nchunks; ++c, ++item) {
           const int st = item % NST;
-          if (!mbar_wait(&bar[st], (phase_bits >> st) & 1u, a.status)) return;
+          if (!mbar_wait(&wbar[st], (phase_bits >> st) & 1u, a.status)) return false;
           phase_bits ^= 1u << st;
           const int t0 = c * 32, ntok = min(32, a.L.b - t0);
           const T* ks = wst + static_cast<size_t>(st) * 2 * kChunkElems;
@@ -505,18 +569,42 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
         }
       }
     }
+    return true;
   };
-  run_blocks(rs.queue_len, false);
+
+  // ---- phase 2: start queued block copies, merge retained states, consume blocks.
+  prefill(rs.queue_len, false);
+  if (has_pred) {
+    if (a.stage_pred && !mbar_wait(&pbar, 0, a.status)) return;
+    float* keepU = S.aggU + kNW * D;
+    for (int dd = tid; dd < D; dd += blockDim.x) {
+      float acc = 0.f;
+      if (a.stage_pred) {
+        for (int c = 0; c < a.sc; ++c) {
+          const float w = S.pw[c];
+          if (w != 0.f) acc = fmaf(w, S.pu[c * D + dd], acc);
+        }
+      } else {
+        const float* pu = a.pu + static_cast<long long>(row) * a.sc * D + dd;
+        for (int c = 0; c < a.sc; ++c) {
+          const float w = S.pw[c];
+          if (w != 0.f) acc = fmaf(w, pu[static_cast<long long>(c) * D], acc);
+        }
+      }
+      keepU[dd] = acc;
+    }
+  }
+  if (!consume()) return;
   __syncthreads();
 
-  // ---- phase 3: combine warps (fixed order) and evaluate guards
+  // ---- phase 3: combine (fixed order: warps 0..kNW-1, then retained) and guards
   if (tid == 0) {
     float M = neg_inf();
-    for (int w = 0; w < kNW; ++w) M = fmaxf(M, S.aggS[w * 4]);
+    for (int w = 0; w <= kNW; ++w) M = fmaxf(M, S.aggS[w * 4]);
     float Z = 0.f, Zn = 0.f;
-    for (int w = 0; w < kNW; ++w) {
+    for (int w = 0; w <= kNW; ++w) {
       if (S.aggS[w * 4] != neg_inf()) Z += expf(S.aggS[w * 4] - M) * S.aggS[w * 4 + 1];
-      Zn += S.aggS[w * 4 + 2];
+      if (w < kNW) Zn += S.aggS[w * 4 + 2];
     }
     sh_f[0] = M;
     sh_f[1] = Z;
@@ -524,13 +612,12 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
   }
   __syncthreads();
   const float Mp = sh_f[0], Zp = sh_f[1], Zn = sh_f[2];
-  // vecA = positive numerator at frame Mp; vecB = negative numerator (low frame)
   for (int dd = tid; dd < D; dd += blockDim.x) {
     float U = 0.f, N = 0.f;
-    for (int w = 0; w < kNW; ++w) {
+    for (int w = 0; w <= kNW; ++w) {
       const float Mw = S.aggS[w * 4];
       if (Mw != neg_inf()) U += expf(Mw - Mp) * S.aggU[w * D + dd];
-      N += S.aggN[w * D + dd];
+      if (w < kNW) N += S.aggN[w * D + dd];
     }
     S.vecA[dd] = U;
     S.vecB[dd] = N;
@@ -541,8 +628,7 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
   const bool low_hit = rs.low_hit != 0;
   float fraction = 1.f;
   bool bad = false;
-  // Scalars of the final merge: out[d] = (cp * vecA[d] + cl * lowvec[d]) / z
-  float m_final, z_final, cp, cl_scale;
+  float z_final, cp, cl_scale;
   if (a.variant == kVarSplit && hybrid) {
     // kernels.py:221-270: everything in the common frame m.
     const float m = fmaxf(Mp, low_hit ? lm : neg_inf());
@@ -555,10 +641,10 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
     const float z = remaining_mass + cp * Zp;
     int cancel = 0, invalid = 0;
     for (int dd = tid; dd < D; dd += blockDim.x) {
-      const float lu = low_hit ? a.low_u[static_cast<long long>(row) * D + dd] * lowalpha : 0.f;
+      const float lu = low_hit ? S.lu_s[dd] * lowalpha : 0.f;
       const float ru = S.vecB[dd] * lowalpha;
       const float residual = lu - ru;
-      const float labs = low_hit ? a.low_abs[static_cast<long long>(row) * D + dd] * lowalpha : 0.f;
+      const float labs = low_hit ? S.la_s[dd] * lowalpha : 0.f;
       const float sc = labs + fabsf(ru);
       cancel |= low_hit && (fabsf(residual) < a.cancel_tol * sc) && (sc > 0.f);
       const float o = (residual + cp * S.vecA[dd]) / fmaxf(z, 1e-30f);
@@ -569,7 +655,6 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
     __syncthreads();
     bad = (z <= 0.f) || (fraction < a.min_remaining) || (fraction != fraction) || isinf(z) || sh_count[0] ||
           sh_count[1];
-    m_final = m;
     z_final = fmaxf(z, 1e-30f);
     cl_scale = lowalpha;
   } else if (hybrid && a.variant != kVarSaved && a.variant != kVarUnion) {
@@ -581,8 +666,8 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
       fraction = mass / ll;
       int cancel = 0;
       for (int dd = tid; dd < D; dd += blockDim.x) {
-        const float residual = a.low_u[static_cast<long long>(row) * D + dd] - S.vecB[dd];
-        const float sc = a.low_abs[static_cast<long long>(row) * D + dd] + fabsf(S.vecB[dd]);
+        const float residual = S.lu_s[dd] - S.vecB[dd];
+        const float sc = S.la_s[dd] + fabsf(S.vecB[dd]);
         cancel |= (fabsf(residual) < a.cancel_tol * sc) && (sc > 0.f);
       }
       if (cancel) atomicOr(&sh_count[0], 1);
@@ -594,7 +679,7 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
     const float z = cp * Zp + lw * mass;
     int invalid = 0;
     for (int dd = tid; dd < D; dd += blockDim.x) {
-      const float resid = low_hit ? a.low_u[static_cast<long long>(row) * D + dd] - S.vecB[dd] : 0.f;
+      const float resid = low_hit ? S.lu_s[dd] - S.vecB[dd] : 0.f;
       const float o = (cp * S.vecA[dd] + lw * resid) / z;
       invalid |= !isfinite(o);
     }
@@ -602,7 +687,6 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
     __syncthreads();
     bad = (low_hit && ((fraction < a.min_remaining) || (fraction != fraction) || sh_count[0])) || (z <= 0.f) ||
           isinf(z) || sh_count[1];
-    m_final = ref;
     z_final = z;
     cl_scale = lw;
   } else {
@@ -610,20 +694,21 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
     __syncthreads();
     cp = 1.f;
     cl_scale = 0.f;
-    m_final = Mp;
     z_final = Zp;
   }
 
   if (bad) {
     // ---- phase 4: strict fallback over A, in this launch.
     __syncthreads();
-    for (int i = tid; i < kNW * D; i += blockDim.x) S.aggU[i] = 0.f;
+    for (int i = tid; i < (kNW + 1) * D; i += blockDim.x) S.aggU[i] = 0.f;
     if (lane == 0) { S.aggS[warp * 4] = neg_inf(); S.aggS[warp * 4 + 1] = 0.f; }
+    if (tid == 0) { S.aggS[kNW * 4] = neg_inf(); S.aggS[kNW * 4 + 1] = 0.f; }
     if constexpr (!kFast) {
       for (int dd = tid; dd < D; dd += blockDim.x) S.vecB[dd] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + dd);
     }
     __syncthreads();
-    run_blocks(a.sa, true);
+    prefill(a.sa, true);
+    if (!consume()) return;
     __syncthreads();
     if (tid == 0) {
       float M = neg_inf();
@@ -645,11 +730,10 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
   } else {
     for (int dd = tid; dd < D; dd += blockDim.x) {
       float lowv = 0.f;
-      if (cl_scale != 0.f) lowv = a.low_u[static_cast<long long>(row) * D + dd] - S.vecB[dd];
+      if (cl_scale != 0.f) lowv = S.lu_s[dd] - S.vecB[dd];
       a.out[static_cast<long long>(row) * D + dd] = (cp * S.vecA[dd] + cl_scale * lowv) / z_final;
     }
   }
-  (void)m_final;
   if (tid == 0) {
     if (a.fallback) a.fallback[row] = bad;
     if (a.remaining) a.remaining[row] = fraction;
@@ -662,24 +746,18 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
 
 // ------------------------------------------------------------------ host side
 
-size_t repair_smem_bytes(const RepairArgs& a, int dpl, int elem, int nst) {
-  const int D = a.d;
-  size_t off = 0;
-  if (dpl > 0) off += static_cast<size_t>(kNW) * nst * 2 * 32 * D * elem;
-  const int nwords = (a.max_n + 31) / 32;
-  off += 2 * nwords * 4;
-  off = (off + 7) & ~size_t(7);
-  off += static_cast<size_t>(a.sa) * 8 + static_cast<size_t>(a.sp) * 8;
-  off += static_cast<size_t>(a.sa + a.sp) * 4;
-  off += static_cast<size_t>(2 * kNW * D + kNW * 4 + 2 * D) * 4;
-  off += a.sa + a.sp + a.sc;
-  return off;
-}
-
 template <typename T, int DPL>
-static int launch_repair_t(const RepairArgs& a, cudaStream_t stream) {
-  constexpr int NST = 2;
-  const size_t smem = repair_smem_bytes(a, DPL, sizeof(T), NST);
+static int launch_repair_t(RepairArgs a, cudaStream_t stream) {
+  constexpr int NST = 1;
+  const bool can_stage = a.pmode != kPredNone && a.d % 4 == 0 &&
+                         (reinterpret_cast<uintptr_t>(a.pu) & 15) == 0 &&
+                         static_cast<size_t>(a.sc) * a.d * 4 <= 64 * 1024;
+  a.stage_pred = can_stage ? 1 : 0;
+  size_t smem = repair_layout<DPL, NST, T>(a, nullptr, nullptr);
+  if (smem > 220 * 1024 && a.stage_pred) {
+    a.stage_pred = 0;
+    smem = repair_layout<DPL, NST, T>(a, nullptr, nullptr);
+  }
   if (smem > 220 * 1024) return -2;
   auto kern = repair_kernel<T, DPL, NST>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -692,11 +770,10 @@ static int launch_repair_dt(const RepairArgs& a, cudaStream_t stream) {
   const uintptr_t pk = reinterpret_cast<uintptr_t>(a.L.k) | reinterpret_cast<uintptr_t>(a.L.v);
   const bool aligned = (pk & 15) == 0 && (a.d * static_cast<int>(sizeof(T))) % 16 == 0 &&
                        (a.L.page_table == nullptr || a.L.b % a.L.page_size == 0) && a.L.kv_request_stride % 8 == 0;
-  const size_t fast_stage = static_cast<size_t>(kNW) * 2 * 2 * 32 * a.d * sizeof(T);
-  if (aligned && fast_stage <= 160 * 1024) {
+  const size_t fast_stage = static_cast<size_t>(kNW) * 2 * 32 * a.d * sizeof(T);
+  if (aligned && fast_stage <= 128 * 1024) {
     if (a.d == 64) return launch_repair_t<T, 2>(a, stream);
     if (a.d == 128) return launch_repair_t<T, 4>(a, stream);
-    if (a.d == 256) return launch_repair_t<T, 8>(a, stream);
   }
   if (a.d > 1024) return -3;
   return launch_repair_t<T, 0>(a, stream);

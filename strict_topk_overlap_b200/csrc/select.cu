@@ -15,15 +15,20 @@
 // Group ("shared") selection scores a KV head by the FP64 sum, in ascending
 // query-head order, of its query heads' scores.
 //
+// Scoring is HBM-bound on the metadata stream: each CTA pulls one tile of
+// lo/hi rows (one meta head, tn consecutive blocks) into shared memory with
+// two 1-D bulk copies, so every CTA's whole tile is in flight at once, then
+// reduces from shared memory.
+//
 // Top-K: per selection row, the K largest scores, ties to the lower block
 // index, written in ascending block-ID order. Radix select over 64-bit
-// order-preserving keys in shared memory (8-bit digits, leading common bits
-// skipped), followed by an index-ordered block scan that resolves ties.
+// order-preserving keys held in registers (8-bit digits, leading common bits
+// skipped, two barriers per digit), then one packed block scan that places
+// every selected ID at its ascending-order position.
 
 #include "internal.cuh"
 
 namespace stk {
-
 
 __device__ __forceinline__ int find_request(const int* offs, int R, int gb) {
   if (offs == nullptr) return 0;
@@ -35,104 +40,131 @@ __device__ __forceinline__ int find_request(const int* offs, int R, int gb) {
   return lo;
 }
 
-// One CTA: one meta head, TN consecutive global blocks, all G query heads of
-// that meta head. Pairs (row, g) are processed 32 at a time per warp.
+constexpr int kScoreThreads = 128;
+constexpr int kQReq = 2;  // requests whose q rows are staged per tile
+
+struct ScoreTile {
+  int tn;        // rows per tile
+  int bulk;      // lo/hi rows are 16-byte multiples and aligned
+};
+
 template <int C>
-__global__ void __launch_bounds__(256) score_kernel(ScoreArgs a, int tn) {
-  extern __shared__ double s64[];  // [tn * G]
+__global__ void __launch_bounds__(kScoreThreads) score_kernel(ScoreArgs a, ScoreTile t) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  __shared__ uint64_t bar;
+  __shared__ int req0;
   const int G = a.hq / a.hmeta;
+  const int D = a.d;
+  const int tn = t.tn;
   const int mh = blockIdx.y;
   const int row0 = blockIdx.x * tn;
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
+  const int nrows = min(tn, a.total_blocks - row0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nwarps = blockDim.x >> 5;
-  const int pairs = tn * G;
-  const int c = (a.d + 31) / 32;
+  float* slo = reinterpret_cast<float*>(sm);
+  float* shi = slo + static_cast<size_t>(tn) * D;
+  double* sq = reinterpret_cast<double*>(shi + static_cast<size_t>(tn) * D);  // [kQReq][G][D]
+  double* s64 = sq + static_cast<size_t>(kQReq) * G * D;                        // [tn * G]
+  int* srr = reinterpret_cast<int*>(s64 + static_cast<size_t>(tn) * G);          // [tn]
+  const long long moff = (static_cast<long long>(mh) * a.total_blocks + row0) * D;
 
-  for (int base = warp * 32; base < pairs; base += nwarps * 32) {
-    double part[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) part[i] = 0.0;
-    int last_row = -1;
-    float lo_v[C > 0 ? C : 1], hi_v[C > 0 ? C : 1];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int pair = base + i;
-      const int rloc = pair / G;
-      const int g = pair - rloc * G;
-      const int gb = row0 + rloc;
-      if (pair < pairs && gb < a.total_blocks) {
-        if (rloc != last_row) {
-          last_row = rloc;
-          const long long moff = (static_cast<long long>(mh) * a.total_blocks + gb) * a.d;
-          if constexpr (C == 4) {
-            float4 x = *reinterpret_cast<const float4*>(a.lo + moff + lane * 4);
-            float4 y = *reinterpret_cast<const float4*>(a.hi + moff + lane * 4);
-            lo_v[0] = x.x; lo_v[1] = x.y; lo_v[2] = x.z; lo_v[3] = x.w;
-            hi_v[0] = y.x; hi_v[1] = y.y; hi_v[2] = y.z; hi_v[3] = y.w;
-          } else if constexpr (C > 0) {
-#pragma unroll
-            for (int j = 0; j < C; ++j) {
-              const int dd = lane * C + j;
-              lo_v[j] = dd < a.d ? a.lo[moff + dd] : 0.f;
-              hi_v[j] = dd < a.d ? a.hi[moff + dd] : 0.f;
-            }
-          }
+  if (tid == 0) {
+    req0 = find_request(a.block_offsets, a.R, row0);
+    if (t.bulk) {
+      mbar_init(&bar, 1);
+      fence_barrier_init();
+      const unsigned bytes = static_cast<unsigned>(nrows) * D * 4;
+      mbar_arrive_expect_tx(&bar, 2 * bytes);
+      bulk_g2s(slo, a.lo + moff, bytes, &bar);
+      bulk_g2s(shi, a.hi + moff, bytes, &bar);
+    }
+  }
+  __syncthreads();
+  if (!t.bulk) {
+    for (int i = tid; i < nrows * D; i += blockDim.x) {
+      slo[i] = a.lo[moff + i];
+      shi[i] = a.hi[moff + i];
+    }
+  }
+  const int r0 = req0;
+  for (int i = tid; i < kQReq * G * D; i += blockDim.x) {
+    const int rr = i / (G * D), rem = i - rr * G * D;
+    const int g = rem / D, dd = rem - g * D;
+    const int r = r0 + rr;
+    sq[i] = r < a.R ? static_cast<double>(load_any(a.q, a.q_dtype, (static_cast<long long>(r) * a.hq + mh * G + g) * D + dd))
+                    : 0.0;
+  }
+  if (t.bulk && !mbar_wait(&bar, 0, a.status)) return;
+  __syncthreads();
+
+  // Per-row request index relative to r0 (tiles rarely span requests).
+  for (int rl = tid; rl < nrows; rl += blockDim.x) srr[rl] = find_request(a.block_offsets, a.R, row0 + rl) - r0;
+  __syncthreads();
+
+  // Each warp takes a contiguous run of (row, head) pairs; lanes own dims.
+  // Lane partial: FP64 FMA chain over its dims (each product is exact, so
+  // fma(q, b, acc) rounds exactly like acc + q*b); then the xor butterfly.
+  const int pairs = nrows * G;
+  const int c = (D + 31) / 32;
+  const int per_warp = (pairs + nwarps - 1) / nwarps;
+  const int p_beg = warp * per_warp, p_end = min(pairs, p_beg + per_warp);
+  int rloc = p_beg / G, g = p_beg - rloc * G;
+#pragma unroll 4
+  for (int pair = p_beg; pair < p_end; ++pair) {
+    const float* lr = slo + rloc * D;
+    const float* hr = shi + rloc * D;
+    const int rr = srr[rloc];
+    double acc = 0.0;
+    if (rr < kQReq) {
+      const double* qr = sq + (rr * G + g) * D;
+      if constexpr (C == 4) {
+        const float4 l4 = *reinterpret_cast<const float4*>(lr + lane * 4);
+        const float4 h4 = *reinterpret_cast<const float4*>(hr + lane * 4);
+        const double2 q01 = *reinterpret_cast<const double2*>(qr + lane * 4);
+        const double2 q23 = *reinterpret_cast<const double2*>(qr + lane * 4 + 2);
+        acc = __fma_rn(q01.x, static_cast<double>(q01.x >= 0.0 ? h4.x : l4.x), acc);
+        acc = __fma_rn(q01.y, static_cast<double>(q01.y >= 0.0 ? h4.y : l4.y), acc);
+        acc = __fma_rn(q23.x, static_cast<double>(q23.x >= 0.0 ? h4.z : l4.z), acc);
+        acc = __fma_rn(q23.y, static_cast<double>(q23.y >= 0.0 ? h4.w : l4.w), acc);
+      } else {
+        for (int dd = lane * c; dd < min((lane + 1) * c, D); ++dd) {
+          const double qv = qr[dd];
+          acc = __fma_rn(qv, static_cast<double>(qv >= 0.0 ? hr[dd] : lr[dd]), acc);
         }
-        const int r = find_request(a.block_offsets, a.R, gb);
-        const long long qoff = (static_cast<long long>(r) * a.hq + mh * G + g) * a.d;
-        double acc = 0.0;
-        if constexpr (C > 0) {
-#pragma unroll
-          for (int j = 0; j < C; ++j) {
-            const int dd = lane * C + j;
-            if (dd < a.d) {
-              const float qv = load_any(a.q, a.q_dtype, qoff + dd);
-              const float bv = qv >= 0.f ? hi_v[j] : lo_v[j];
-              acc = __dadd_rn(acc, __dmul_rn(static_cast<double>(qv), static_cast<double>(bv)));
-            }
-          }
-        } else {
-          const long long moff = (static_cast<long long>(mh) * a.total_blocks + gb) * a.d;
-          for (int dd = lane * c; dd < min((lane + 1) * c, a.d); ++dd) {
-            const float qv = load_any(a.q, a.q_dtype, qoff + dd);
-            const float bv = qv >= 0.f ? a.hi[moff + dd] : a.lo[moff + dd];
-            acc = __dadd_rn(acc, __dmul_rn(static_cast<double>(qv), static_cast<double>(bv)));
-          }
-        }
-        part[i] = acc;
+      }
+    } else {
+      // Tile spans more requests than are staged: read q from global memory.
+      const long long qoff = (static_cast<long long>(r0 + rr) * a.hq + mh * G + g) * D;
+      for (int dd = lane * c; dd < min((lane + 1) * c, D); ++dd) {
+        const double qv = static_cast<double>(load_any(a.q, a.q_dtype, qoff + dd));
+        acc = __fma_rn(qv, static_cast<double>(qv >= 0.0 ? hr[dd] : lr[dd]), acc);
       }
     }
-    transpose_reduce32(part, lane);
-    const int pair = base + lane;
-    if (pair < pairs) s64[pair] = part[0];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(kFull, acc, off));
+    if (lane == 0) s64[pair] = acc;
+    if (++g == G) { g = 0; ++rloc; }
   }
   __syncthreads();
 
-  // Outputs.
-  for (int pair = threadIdx.x; pair < pairs; pair += blockDim.x) {
-    const int rloc = pair / G;
-    const int g = pair - rloc * G;
-    const int gb = row0 + rloc;
-    if (gb >= a.total_blocks) continue;
+  for (int pair = tid; pair < pairs; pair += blockDim.x) {
+    const int rl = pair / G, g = pair - rl * G;
+    const int gb = row0 + rl;
     const int h = mh * G + g;
     const double s = s64[pair];
     if (a.scores_f32) a.scores_f32[static_cast<long long>(h) * a.total_blocks + gb] = __double2float_rn(s);
     if (a.scores_f64 && !a.group_select) a.scores_f64[static_cast<long long>(h) * a.total_blocks + gb] = s;
   }
   if (a.scores_f64 && a.group_select) {
-    for (int rloc = threadIdx.x; rloc < tn; rloc += blockDim.x) {
-      const int gb = row0 + rloc;
-      if (gb >= a.total_blocks) continue;
+    for (int rl = tid; rl < nrows; rl += blockDim.x) {
       double acc = 0.0;
-      for (int g = 0; g < G; ++g) acc = __dadd_rn(acc, s64[rloc * G + g]);
-      a.scores_f64[static_cast<long long>(mh) * a.total_blocks + gb] = acc;
+      for (int g = 0; g < G; ++g) acc = __dadd_rn(acc, s64[rl * G + g]);
+      a.scores_f64[static_cast<long long>(mh) * a.total_blocks + row0 + rl] = acc;
     }
   }
 }
 
 // ------------------------------------------------------------------ Top-K
-
 
 __device__ __forceinline__ unsigned long long order_key(double x) {
   unsigned long long b = static_cast<unsigned long long>(__double_as_longlong(x + 0.0));
@@ -145,236 +177,237 @@ __device__ __forceinline__ unsigned long long warp_or64(unsigned long long x) {
   return x;
 }
 
-// Block-wide exclusive scan of one int per thread (blockDim.x <= 1024).
-__device__ __forceinline__ int block_exclusive_scan(int x, int* warp_tot, int* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
-  int inc = x;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    int y = __shfl_up_sync(kFull, inc, o);
-    if (lane >= o) inc += y;
-  }
-  if (lane == 31) warp_tot[warp] = inc;
-  __syncthreads();
-  if (warp == 0) {
-    int t = lane < nw ? warp_tot[lane] : 0;
-    int ti = t;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      int y = __shfl_up_sync(kFull, ti, o);
-      if (lane >= o) ti += y;
-    }
-    if (lane < nw) warp_tot[lane] = ti - t;
-    if (lane == 31) *total = ti;
-  }
-  __syncthreads();
-  const int res = inc - x + warp_tot[warp];
-  __syncthreads();
-  return res;
-}
-
-// Selection core shared by the plain and the candidate-merge kernels:
-// `keys` holds n ordered keys in shared memory, `idx_of(i)` maps a position to
-// the ID written out. Positions are ordered by (key desc, id asc) when the
-// caller lays out positions in ascending-ID order.
-template <typename IdOf>
-__device__ void select_core(const unsigned long long* keys, int n, int topk, IdOf idx_of, int* ids_out,
-                            unsigned long long* keys_out) {
-  __shared__ unsigned hist[256];
-  __shared__ int sh_bin, sh_above, sh_count;
-  __shared__ unsigned long long sh_or;
-  __shared__ int warp_tot[32];
-  __shared__ int sh_total;
+// Radix select over E register-resident keys per thread; thread t owns
+// positions [t*E, t*E+E). Writes the chosen positions' IDs (id_of) in
+// ascending position order.
+template <int E, typename IdOf>
+__device__ void select_registers(const unsigned long long (&key)[E], int n, int topk, IdOf id_of, int* out,
+                                 unsigned long long* keys_out) {
+  __shared__ unsigned hist[2][256];
+  __shared__ unsigned long long sh_or, sh_k0;
+  __shared__ int sh_bin, sh_above, sh_cnt;
+  __shared__ unsigned warp_tot[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int T = blockDim.x;
+  const int nw = blockDim.x >> 5;
+  const int beg = tid * E;
 
-  // Common leading bits.
-  const unsigned long long k0 = keys[0];
-  unsigned long long diff = 0;
-  for (int i = tid; i < n; i += T) diff |= keys[i] ^ k0;
-  diff = warp_or64(diff);
-  if (tid == 0) sh_or = 0;
+  if (tid == 0) { sh_or = 0; sh_k0 = key[0]; }
+  for (int i = tid; i < 512; i += blockDim.x) (&hist[0][0])[i] = 0;
   __syncthreads();
-  if (lane == 0) atomicOr(&sh_or, diff);
+  const unsigned long long k0 = sh_k0;
+  unsigned long long diff = 0;
+#pragma unroll
+  for (int j = 0; j < E; ++j)
+    if (beg + j < n) diff |= key[j] ^ k0;
+  diff = warp_or64(diff);
+  if (lane == 0 && diff) atomicOr(&sh_or, diff);
   __syncthreads();
   diff = sh_or;
 
-  unsigned long long prefix = 0, mask = 0;
+  unsigned long long prefix, mask;
   int kk = topk;
-  bool take_all_eq = false;
+  bool take_all = false;
   if (diff == 0) {
     mask = ~0ull;
     prefix = k0;
-    take_all_eq = (kk == n);
   } else {
     const int hb = 63 - __clzll(diff);
     mask = (hb == 63) ? 0ull : ~((2ull << hb) - 1ull);
     prefix = k0 & mask;
+    int buf = 0;
     for (int shift = (hb / 8) * 8; shift >= 0; shift -= 8) {
-      for (int i = tid; i < 256; i += T) hist[i] = 0;
-      __syncthreads();
-      for (int i = tid; i < n; i += T) {
-        const unsigned long long k = keys[i];
-        if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 0xFF], 1u);
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        // Lanes holding the same digit add once (warp-aggregated atomics).
+        const bool cand = beg + j < n && (key[j] & mask) == prefix;
+        const unsigned digit = cand ? static_cast<unsigned>((key[j] >> shift) & 0xFF) : 0xFFFFFFFFu;
+        const unsigned grp = __match_any_sync(kFull, digit);
+        if (cand && lane == __ffs(grp) - 1) atomicAdd(&hist[buf][digit], static_cast<unsigned>(__popc(grp)));
       }
       __syncthreads();
       if (warp == 0) {
-        // Suffix scan from the top bin downwards: lane l owns bins [255-8l-7, 255-8l].
-        int local[8];
-        int sum = 0;
+        unsigned local[8];
+        unsigned sum = 0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) { local[j] = hist[255 - (lane * 8 + j)]; sum += local[j]; }
-        int inc = sum;
+        for (int j = 0; j < 8; ++j) { local[j] = hist[buf][255 - (lane * 8 + j)]; sum += local[j]; }
+        unsigned inc = sum;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-          int y = __shfl_up_sync(kFull, inc, o);
+          const unsigned y = __shfl_up_sync(kFull, inc, o);
           if (lane >= o) inc += y;
         }
-        const int excl = inc - sum;
-        const bool crosses = (excl < kk) && (inc >= kk);
+        const unsigned excl = inc - sum;
+        const bool crosses = excl < static_cast<unsigned>(kk) && inc >= static_cast<unsigned>(kk);
         const unsigned who = __ballot_sync(kFull, crosses);
         if (lane == __ffs(who) - 1) {
-          int run = excl;
+          unsigned run = excl;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            if (run + local[j] >= kk) {
+            if (run + local[j] >= static_cast<unsigned>(kk)) {
               sh_bin = 255 - (lane * 8 + j);
-              sh_above = run;
-              sh_count = local[j];
+              sh_above = static_cast<int>(run);
+              sh_cnt = static_cast<int>(local[j]);
               break;
             }
             run += local[j];
           }
         }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) hist[buf ^ 1][lane * 8 + j] = 0;
       }
       __syncthreads();
-      const int bin = sh_bin, above = sh_above, cnt = sh_count;
-      __syncthreads();
-      prefix |= static_cast<unsigned long long>(bin) << shift;
+      prefix |= static_cast<unsigned long long>(sh_bin) << shift;
       mask |= 0xFFull << shift;
-      kk -= above;
-      if (cnt == kk) { take_all_eq = true; break; }
+      kk -= sh_above;
+      const int cnt = sh_cnt;
+      buf ^= 1;
+      if (cnt == kk) { take_all = true; break; }
     }
   }
+  if (take_all) kk = n;
 
-  // Resolve: key above the region -> selected; in region -> selected if
-  // take_all_eq, else the kk lowest positions.
-  const int E = (n + T - 1) / T;
-  const int beg = min(tid * E, n), end = min(beg + E, n);
-  int n_eq = 0;
-  for (int i = beg; i < end; ++i) n_eq += ((keys[i] & mask) == prefix);
-  int eq_rank = block_exclusive_scan(n_eq, warp_tot, &sh_total);
-  int n_sel = 0;
-  {
-    int er = eq_rank;
-    for (int i = beg; i < end; ++i) {
-      const unsigned long long km = keys[i] & mask;
-      bool s = km > prefix;
-      if (km == prefix) { s = take_all_eq || er < kk; ++er; }
-      n_sel += s;
+  // Packed scan: (#above, #in-region) before this thread's first position.
+  unsigned n_gt = 0, n_eq = 0;
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    if (beg + j < n) {
+      const unsigned long long km = key[j] & mask;
+      n_gt += km > prefix;
+      n_eq += km == prefix;
     }
   }
-  int pos = block_exclusive_scan(n_sel, warp_tot, &sh_total);
-  {
-    int er = eq_rank;
-    for (int i = beg; i < end; ++i) {
-      const unsigned long long km = keys[i] & mask;
+  const unsigned packed = (n_gt << 16) | n_eq;
+  unsigned inc = packed;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_up_sync(kFull, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) warp_tot[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    const unsigned t = lane < nw ? warp_tot[lane] : 0u;
+    unsigned ti = t;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned y = __shfl_up_sync(kFull, ti, o);
+      if (lane >= o) ti += y;
+    }
+    if (lane < nw) warp_tot[lane] = ti - t;
+  }
+  __syncthreads();
+  const unsigned excl = inc - packed + warp_tot[warp];
+  unsigned gt_before = excl >> 16, eq_before = excl & 0xFFFFu;
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    if (beg + j < n) {
+      const unsigned long long km = key[j] & mask;
       bool s = km > prefix;
-      if (km == prefix) { s = take_all_eq || er < kk; ++er; }
-      if (s && pos < topk) {
-        ids_out[pos] = idx_of(i);
-        if (keys_out) keys_out[pos] = keys[i];
-        ++pos;
+      if (km == prefix) s = static_cast<int>(eq_before) < kk;
+      if (s) {
+        const int pos = static_cast<int>(gt_before) + min(static_cast<int>(eq_before), kk);
+        if (pos < topk) {
+          out[pos] = id_of(beg + j);
+          if (keys_out) keys_out[pos] = key[j];
+        }
       }
+      gt_before += km > prefix;
+      eq_before += km == prefix;
     }
   }
 }
 
+template <int E>
 __global__ void __launch_bounds__(512) select_topk_kernel(SelectArgs a) {
-  extern __shared__ unsigned long long skeys[];
   const int row = blockIdx.x;
   const int r = row / a.hsel, hs = row - r * a.hsel;
   const int off = a.block_offsets ? a.block_offsets[r] : 0;
   const int n = a.block_offsets ? a.block_offsets[r + 1] - off : a.n;
-  const double* src = a.scores + static_cast<long long>(hs) * a.total_blocks + off;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) skeys[i] = order_key(src[i]);
-  __syncthreads();
-  if (n < a.topk) {
+  if (n < a.topk || n > static_cast<int>(blockDim.x) * E) {
     if (threadIdx.x == 0) report(a.status, kStatusShapeOverflow);
     return;
   }
+  const double* src = a.scores + static_cast<long long>(hs) * a.total_blocks + off;
+  unsigned long long key[E];
+  const int beg = threadIdx.x * E;
+#pragma unroll
+  for (int j = 0; j < E; ++j) key[j] = beg + j < n ? order_key(src[beg + j]) : 0ull;
   const int base = a.id_base;
-  select_core(skeys, n, a.topk, [base](int i) { return base + i; },
-              a.ids_out + static_cast<long long>(row) * a.topk,
-              a.keys_out ? a.keys_out + static_cast<long long>(row) * a.topk : nullptr);
+  select_registers<E>(key, n, a.topk, [base](int i) { return base + i; },
+                      a.ids_out + static_cast<long long>(row) * a.topk,
+                      a.keys_out ? a.keys_out + static_cast<long long>(row) * a.topk : nullptr);
 }
 
 // Candidate merge (context-parallel and segmented selection): each row has
-// `ncand` (key, id) candidates gathered from several shards, laid out in
-// ascending-ID order (each shard's list is ascending and shards own
-// increasing ID ranges), so position order equals ID order and the same
-// selection core resolves ties toward the lower ID.
-
+// `ncand` (key, id) candidates gathered from several shards in ascending-ID
+// order (each shard's list is ascending and shards own increasing ID
+// ranges), so position order equals ID order and the same selection resolves
+// ties toward the lower ID.
+template <int E>
 __global__ void __launch_bounds__(512) merge_candidates_kernel(MergeArgs a) {
-  extern __shared__ unsigned long long smem[];
-  unsigned long long* skeys = smem;                    // ncand
-  int* sids = reinterpret_cast<int*>(smem + a.ncand);  // ncand
   const int row = blockIdx.x;
-  const unsigned long long* ksrc = a.keys + static_cast<long long>(row) * a.ncand;
-  const int* isrc = a.ids + static_cast<long long>(row) * a.ncand;
-  for (int i = threadIdx.x; i < a.ncand; i += blockDim.x) {
-    skeys[i] = ksrc[i];
-    sids[i] = isrc[i];
-  }
-  __syncthreads();
-  if (a.ncand < a.topk) {
+  const int n = a.ncand;
+  if (n < a.topk || n > static_cast<int>(blockDim.x) * E) {
     if (threadIdx.x == 0) report(a.status, kStatusShapeOverflow);
     return;
   }
-  select_core(skeys, a.ncand, a.topk, [sids](int i) { return sids[i]; },
-              a.ids_out + static_cast<long long>(row) * a.topk, nullptr);
+  const unsigned long long* ksrc = a.keys + static_cast<long long>(row) * n;
+  const int* isrc = a.ids + static_cast<long long>(row) * n;
+  unsigned long long key[E];
+  const int beg = threadIdx.x * E;
+#pragma unroll
+  for (int j = 0; j < E; ++j) key[j] = beg + j < n ? ksrc[beg + j] : 0ull;
+  select_registers<E>(key, n, a.topk, [isrc](int i) { return isrc[i]; },
+                      a.ids_out + static_cast<long long>(row) * a.topk, nullptr);
 }
 
 // ------------------------------------------------------------------ host side
 
 int launch_score(const ScoreArgs& a, cudaStream_t stream) {
   const int G = a.hq / a.hmeta;
-  const int tn = max(1, 512 / G);
-  const int tiles = (a.total_blocks + tn - 1) / tn;
-  dim3 grid(tiles, a.hmeta);
-  const size_t smem = static_cast<size_t>(tn) * G * sizeof(double);
-  const int c = (a.d + 31) / 32;
+  ScoreTile t;
+  t.tn = max(4, min(64, (128 + G - 1) / G));
   const bool aligned = ((reinterpret_cast<uintptr_t>(a.lo) | reinterpret_cast<uintptr_t>(a.hi)) & 15) == 0;
-  const bool vec4 = (c == 4) && (a.d == 128) && aligned;
-  if (vec4) {
-    score_kernel<4><<<grid, 256, smem, stream>>>(a, tn);
-  } else if (c <= 8 && a.d == c * 32) {
-    switch (c) {
-      case 1: score_kernel<1><<<grid, 256, smem, stream>>>(a, tn); break;
-      case 2: score_kernel<2><<<grid, 256, smem, stream>>>(a, tn); break;
-      case 8: score_kernel<8><<<grid, 256, smem, stream>>>(a, tn); break;
-      default: score_kernel<0><<<grid, 256, smem, stream>>>(a, tn); break;
-    }
+  t.bulk = aligned && (a.d % 4 == 0);
+  const int tiles = (a.total_blocks + t.tn - 1) / t.tn;
+  dim3 grid(tiles, a.hmeta);
+  const size_t smem = static_cast<size_t>(t.tn) * a.d * 4 * 2 + static_cast<size_t>(kQReq) * G * a.d * 8 +
+                      static_cast<size_t>(t.tn) * G * 8 + static_cast<size_t>(t.tn) * 4 + 16;
+  if (smem > 200 * 1024) return -1;
+  if (a.d == 128) {
+    cudaFuncSetAttribute(score_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    score_kernel<4><<<grid, kScoreThreads, smem, stream>>>(a, t);
   } else {
-    score_kernel<0><<<grid, 256, smem, stream>>>(a, tn);
+    cudaFuncSetAttribute(score_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    score_kernel<0><<<grid, kScoreThreads, smem, stream>>>(a, t);
   }
   return static_cast<int>(cudaGetLastError());
 }
 
 int launch_select(const SelectArgs& a, int max_n, cudaStream_t stream) {
-  const size_t smem = static_cast<size_t>(max_n) * sizeof(unsigned long long);
-  if (smem > 200 * 1024) return -1;
-  cudaFuncSetAttribute(select_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  const int threads = max_n >= 4096 ? 512 : (max_n >= 1024 ? 256 : 128);
-  select_topk_kernel<<<a.R * a.hsel, threads, smem, stream>>>(a);
+  const int rows = a.R * a.hsel;
+  if (max_n <= 1024) {
+    select_topk_kernel<8><<<rows, 128, 0, stream>>>(a);
+  } else if (max_n <= 4096) {
+    select_topk_kernel<16><<<rows, 256, 0, stream>>>(a);
+  } else if (max_n <= 16384) {
+    select_topk_kernel<32><<<rows, 512, 0, stream>>>(a);
+  } else {
+    return -1;
+  }
   return static_cast<int>(cudaGetLastError());
 }
 
 int launch_merge_candidates(const MergeArgs& a, cudaStream_t stream) {
-  const size_t smem = static_cast<size_t>(a.ncand) * (sizeof(unsigned long long) + sizeof(int));
-  if (smem > 200 * 1024) return -1;
-  cudaFuncSetAttribute(merge_candidates_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  merge_candidates_kernel<<<a.rows, 256, smem, stream>>>(a);
+  if (a.ncand <= 1024) {
+    merge_candidates_kernel<8><<<a.rows, 128, 0, stream>>>(a);
+  } else if (a.ncand <= 4096) {
+    merge_candidates_kernel<16><<<a.rows, 256, 0, stream>>>(a);
+  } else if (a.ncand <= 16384) {
+    merge_candidates_kernel<32><<<a.rows, 512, 0, stream>>>(a);
+  } else {
+    return -1;
+  }
   return static_cast<int>(cudaGetLastError());
 }
 

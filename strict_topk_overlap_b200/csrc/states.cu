@@ -80,192 +80,268 @@ __device__ __forceinline__ void write_inactive(const JobArgs& a, long long job, 
 }
 
 // ------------------------------------------------------------------ fast path
+// Warp-specialised: warp 0 resolves jobs and streams each active block's K/V
+// (one stage = one whole block) into shared-memory stages with 1-D bulk
+// copies; ncons consumer warps reduce them. Job j of the CTA goes to consumer
+// c = j % ncons, which owns stages [c*kps, (c+1)*kps) and takes its jobs in
+// order through them, so every stage has exactly one producer and one
+// consumer and each mbarrier advances one phase at a time (a waiter can never
+// be two phases ahead, which would alias the parity). full[s] completes when
+// a stage's bytes landed; empty[s] when its consumer is done with it.
 
-template <typename T, int DPL, int MODE, int NST>
-__global__ void __launch_bounds__(128) jobs_fast_kernel(JobArgs a) {
+constexpr int kCons = 12;
+constexpr int kWsThreads = 32 * (kCons + 1);
+
+template <typename T, int DPL, int MODE>
+__global__ void __launch_bounds__(kWsThreads, 1) jobs_fast_kernel(JobArgs a, int kps, int ncons) {
   constexpr int D = 32 * DPL;
-  constexpr int kChunkElems = 32 * D;
   constexpr bool kWantV = MODE != kModeMass;
-  constexpr int kStageElems = kChunkElems * (kWantV ? 2 : 1);
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  __shared__ uint64_t bars[4 * NST];
-  __shared__ int info_row[4 * NST], info_slot[4 * NST], info_chunk[4 * NST];
-  __shared__ long long info_bid[4 * NST];
+  __shared__ uint64_t full_bar[64], empty_bar[64];
+  __shared__ int info_row[64], info_slot[64];
+  __shared__ long long info_bid[64];
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int wpc = blockDim.x >> 5;
-  T* stages = reinterpret_cast<T*>(smem_raw) + static_cast<size_t>(warp) * NST * kStageElems;
-  uint64_t* bar = bars + warp * NST;
-  int* irow = info_row + warp * NST;
-  int* islot = info_slot + warp * NST;
-  int* ichunk = info_chunk + warp * NST;
-  long long* ibid = info_bid + warp * NST;
+  const int B = a.L.b;
+  const size_t stage_elems = static_cast<size_t>(B) * D * (kWantV ? 2 : 1);
+  T* stages = reinterpret_cast<T*>(smem_raw);
+  const int NS = kps * ncons;
 
-  if (lane == 0) {
-    for (int st = 0; st < NST; ++st) mbar_init(&bar[st], 1);
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < NS; ++st) {
+      mbar_init(&full_bar[st], 1);
+      mbar_init(&empty_bar[st], 1);
+    }
     fence_barrier_init();
   }
-  __syncwarp();
+  __syncthreads();
 
   const long long njobs = static_cast<long long>(a.rows) * a.s;
-  const long long W = static_cast<long long>(gridDim.x) * wpc;
-  const int nchunks = (a.L.b + 31) / 32;
-  const int nseg_page = (a.L.page_table != nullptr) ? a.L.page_size : 0;
-
-  // Issue cursor (uniform across the warp).
-  long long ijob = static_cast<long long>(blockIdx.x) * wpc + warp;
-  int ichunk_cur = 0;
-  JobInfo iinfo;
-  auto advance_to_active = [&](bool first) {
-    if (!first) {
-      if (++ichunk_cur < nchunks) return;
-      ichunk_cur = 0;
-      ijob += W;
-    }
-    while (ijob < njobs) {
-      iinfo = resolve_job(a, ijob, lane);
-      if (iinfo.active) return;
-      write_inactive(a, ijob, lane);
-      ijob += W;
-    }
-  };
-  auto issue = [&](int st) {
-    if (ijob >= njobs) {
-      if (lane == 0) irow[st] = -1;
-      return;
-    }
-    if (lane == 0) {
-      const int r = iinfo.row / a.hq;
-      const int kv = (iinfo.row - r * a.hq) / a.g;
-      const int t0 = ichunk_cur * 32;
-      const int ntok = min(32, a.L.b - t0);
-      irow[st] = iinfo.row;
-      islot[st] = iinfo.slot;
-      ichunk[st] = ichunk_cur;
-      ibid[st] = iinfo.bid;
-      T* ks = stages + static_cast<size_t>(st) * kStageElems;
-      T* vs = ks + kChunkElems;
-      const unsigned bytes = static_cast<unsigned>(ntok * D * sizeof(T));
-      mbar_arrive_expect_tx(&bar[st], kWantV ? 2 * bytes : bytes);
-      const T* K = static_cast<const T*>(a.L.k);
-      const T* V = static_cast<const T*>(a.L.v);
-      if (nseg_page == 0) {
-        const BlockSeg sg = block_seg(a.L, r, kv, iinfo.bid, 0);
-        const long long off = sg.elem_off + static_cast<long long>(t0) * D;
-        bulk_g2s(ks, K + off, bytes, &bar[st]);
-        if (kWantV) bulk_g2s(vs, V + off, bytes, &bar[st]);
-      } else {
-        for (int t = t0; t < t0 + ntok;) {
-          const int pg = t / nseg_page, o = t - pg * nseg_page;
-          const int cnt = min(nseg_page - o, t0 + ntok - t);
-          const BlockSeg sg = block_seg(a.L, r, kv, iinfo.bid, pg);
-          const long long off = sg.elem_off + static_cast<long long>(o) * D;
-          const unsigned sb = static_cast<unsigned>(cnt * D * sizeof(T));
-          bulk_g2s(ks + (t - t0) * D, K + off, sb, &bar[st]);
-          if (kWantV) bulk_g2s(vs + (t - t0) * D, V + off, sb, &bar[st]);
-          t += cnt;
+  if (warp == 0) {
+    // ---------------- producer
+    long long item = 0;  // CTA-local job index
+    const T* K = static_cast<const T*>(a.L.k);
+    const T* V = static_cast<const T*>(a.L.v);
+    const unsigned bytes = static_cast<unsigned>(B) * D * sizeof(T);
+    // Item -> (consumer, its local index, stage, phase).
+    auto stage_of = [&](long long it, long long& jc) {
+      const int c = static_cast<int>(it % ncons);
+      jc = it / ncons;
+      return c * kps + static_cast<int>(jc % kps);
+    };
+    auto acquire = [&](int st, long long jc) -> bool {
+      if (jc >= kps) return mbar_wait(&empty_bar[st], static_cast<unsigned>((jc / kps - 1) & 1), a.status);
+      return true;
+    };
+    auto issue_job = [&](int row, int slot, long long bid) -> bool {
+      long long jc;
+      const int st = stage_of(item, jc);
+      if (!acquire(st, jc)) return false;
+      if (lane == 0) {
+        info_row[st] = row;
+        info_slot[st] = slot;
+        info_bid[st] = bid;
+        const int r = row / a.hq;
+        const int kv = (row - r * a.hq) / a.g;
+        T* ks = stages + st * stage_elems;
+        T* vs = ks + static_cast<size_t>(B) * D;
+        mbar_arrive_expect_tx(&full_bar[st], kWantV ? 2 * bytes : bytes);
+        const int nseg = block_nseg(a.L);
+        for (int sg = 0; sg < nseg; ++sg) {
+          const BlockSeg seg = block_seg(a.L, r, kv, bid, sg);
+          const unsigned sb = static_cast<unsigned>(seg.tokens) * D * sizeof(T);
+          const size_t dst = static_cast<size_t>(sg) * seg.tokens * D;
+          bulk_g2s(ks + dst, K + seg.elem_off, sb, &full_bar[st]);
+          if (kWantV) bulk_g2s(vs + dst, V + seg.elem_off, sb, &full_bar[st]);
         }
       }
+      __syncwarp();
+      ++item;
+      return true;
+    };
+    if (a.pred != nullptr) {
+      // Slot search in pred: resolve one job at a time with the whole warp.
+      for (long long job = blockIdx.x; job < njobs; job += gridDim.x) {
+        const JobInfo ji = resolve_job(a, job, lane);
+        if (!ji.active) { write_inactive(a, job, lane); continue; }
+        if (!issue_job(ji.row, ji.slot, ji.bid)) return;
+      }
+    } else {
+      // Lanes resolve up to 32 jobs at once; the active ones are then issued
+      // in job order, one per lane, in rounds of at most NS items so that no
+      // lane ever waits on a stage more than one phase ahead.
+      const long long stride = static_cast<long long>(gridDim.x);
+      for (long long g0 = blockIdx.x; g0 < njobs; g0 += 32 * stride) {
+        const long long job = g0 + lane * stride;
+        int row = 0, slot = 0;
+        long long bid = -1;
+        bool act = false;
+        if (job < njobs) {
+          row = static_cast<int>(job / a.s);
+          slot = static_cast<int>(job - static_cast<long long>(row) * a.s);
+          bid = load_id(a.ids, a.ids64, job);
+          act = true;
+          if (a.active_mode == 1) act = a.active[row] != 0;
+          else if (a.active_mode == 2) act = a.active[job] != 0;
+          if (a.active_invert) act = !act;
+          if (bid < 0) act = false;
+          if (act && bid >= request_blocks(a.L, row / a.hq)) {
+            report(a.status, kStatusBadBlockId);
+            act = false;
+          }
+          if (!act) {
+            // Inactive slot: (-inf, 0, 0) as the reference writes.
+            if (a.mode != kModeFixed) {
+              a.m[job] = neg_inf();
+              a.l[job] = 0.f;
+              if (a.mode == kModeFull)
+                for (int dd = 0; dd < D; ++dd) a.u[job * D + dd] = 0.f;
+            } else {
+              if (a.l) a.l[job] = 0.f;
+              for (int dd = 0; dd < D; ++dd) {
+                a.u[job * D + dd] = 0.f;
+                if (a.uabs) a.uabs[job * D + dd] = 0.f;
+              }
+            }
+          }
+        }
+        const unsigned act_mask = __ballot_sync(kFull, act);
+        const int rank = __popc(act_mask & ((1u << lane) - 1));  // order among active lanes
+        const int nact = __popc(act_mask);
+        for (int r0 = 0; r0 < nact; r0 += NS) {
+          if (act && rank >= r0 && rank < r0 + NS) {
+            const long long it = item + rank;
+            long long jc;
+            const int st = stage_of(it, jc);
+            if (acquire(st, jc)) {
+              info_row[st] = row;
+              info_slot[st] = slot;
+              info_bid[st] = bid;
+              const int r = row / a.hq;
+              const int kv = (row - r * a.hq) / a.g;
+              T* ks = stages + st * stage_elems;
+              T* vs = ks + static_cast<size_t>(B) * D;
+              mbar_arrive_expect_tx(&full_bar[st], kWantV ? 2 * bytes : bytes);
+              const int nseg = block_nseg(a.L);
+              for (int sg = 0; sg < nseg; ++sg) {
+                const BlockSeg seg = block_seg(a.L, r, kv, bid, sg);
+                const unsigned sb = static_cast<unsigned>(seg.tokens) * D * sizeof(T);
+                const size_t dst = static_cast<size_t>(sg) * seg.tokens * D;
+                bulk_g2s(ks + dst, K + seg.elem_off, sb, &full_bar[st]);
+                if (kWantV) bulk_g2s(vs + dst, V + seg.elem_off, sb, &full_bar[st]);
+              }
+            }
+          }
+          __syncwarp();
+        }
+        item += nact;
+      }
     }
-    advance_to_active(false);
-  };
+    // One end marker per consumer (ncons consecutive items cover every consumer).
+    for (int c = 0; c < ncons; ++c, ++item) {
+      long long jc;
+      const int st = stage_of(item, jc);
+      if (!acquire(st, jc)) return;
+      if (lane == 0) {
+        info_row[st] = -1;
+        mbar_arrive(&full_bar[st]);
+      }
+      __syncwarp();
+    }
+    return;
+  }
 
-  advance_to_active(true);
-#pragma unroll 1
-  for (int st = 0; st < NST; ++st) issue(st);
-  __syncwarp();
-
-  unsigned phase = 0;  // bit st = parity of stage st
+  // ---------------- consumers
+  const int cw = warp - 1;
+  if (cw >= ncons) return;
   float qf[DPL];
   int q_row = -1;
-  float m = neg_inf(), l = 0.f;
-  float u[DPL], ua[DPL];
-  float frame = 0.f;
-
 #pragma unroll 1
-  for (long long item = 0;; ++item) {
-    const int st = static_cast<int>(item % NST);
-    __syncwarp();
-    const int row = irow[st];
-    if (row < 0) break;
-    const int slot = islot[st], chunk = ichunk[st];
-    if (!mbar_wait(&bar[st], (phase >> st) & 1u, a.status)) return;
-    phase ^= 1u << st;
-    const int t0 = chunk * 32;
-    const int ntok = min(32, a.L.b - t0);
-    if (chunk == 0) {
-      if (row != q_row) {
-        q_row = row;
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) qf[j] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + lane * DPL + j);
-      }
-      m = neg_inf();
-      l = 0.f;
-#pragma unroll
-      for (int j = 0; j < DPL; ++j) { u[j] = 0.f; ua[j] = 0.f; }
-      if (MODE == kModeFixed) frame = a.frame[row];
+  for (long long jc = 0;; ++jc) {
+    const int st = cw * kps + static_cast<int>(jc % kps);
+    if (!mbar_wait(&full_bar[st], static_cast<unsigned>((jc / kps) & 1), a.status)) return;
+    const int row = info_row[st];
+    if (row < 0) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[st]);
+      break;
     }
-    const T* ks = stages + static_cast<size_t>(st) * kStageElems;
-    const T* vs = ks + kChunkElems;
-
-    float p[32];
+    const int slot = info_slot[st];
+    if (row != q_row) {
+      q_row = row;
 #pragma unroll
-    for (int t = 0; t < 32; ++t) {
-      p[t] = 0.f;
-      if (t < ntok) {
-        float kv[DPL];
-        load_vec<T, DPL>(ks + t * D + lane * DPL, kv);
-        float acc = 0.f;
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) acc = fmaf(kv[j], qf[j], acc);
-        p[t] = acc;
-      }
+      for (int j = 0; j < DPL; ++j) qf[j] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + lane * DPL + j);
     }
-    transpose_reduce32(p, lane);
-    const float s = lane < ntok ? p[0] * a.scale : neg_inf();
-
-    float w;
-    if (MODE == kModeFixed) {
-      w = lane < ntok ? expf(s - frame) : 0.f;
-      l += warp_sum(w);
-    } else {
-      const float mc = warp_max(s);
-      const float mn = fmaxf(m, mc);
-      const float alpha = expf(m - mn);
-      w = lane < ntok ? expf(s - mn) : 0.f;
-      l = l * alpha + warp_sum(w);
-      m = mn;
+    const float frame = MODE == kModeFixed ? a.frame[row] : 0.f;
+    const T* kst = stages + st * stage_elems;
+    const T* vst = kst + static_cast<size_t>(B) * D;
+    float m = neg_inf(), l = 0.f;
+    float u[DPL], ua[DPL];
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) { u[j] = 0.f; ua[j] = 0.f; }
+    for (int t0 = 0; t0 < B; t0 += 32) {
+      const int ntok = min(32, B - t0);
+      const T* ks = kst + static_cast<size_t>(t0) * D;
+      const T* vs = vst + static_cast<size_t>(t0) * D;
+      float p[32];
+#pragma unroll
+      for (int t = 0; t < 32; ++t) {
+        p[t] = 0.f;
+        if (t < ntok) {
+          float kv[DPL];
+          load_vec<T, DPL>(ks + t * D + lane * DPL, kv);
+          float acc = 0.f;
+#pragma unroll
+          for (int j = 0; j < DPL; ++j) acc = fmaf(kv[j], qf[j], acc);
+          p[t] = acc;
+        }
+      }
+      transpose_reduce32(p, lane);
+      const float s = lane < ntok ? p[0] * a.scale : neg_inf();
+      float w;
+      if (MODE == kModeFixed) {
+        w = lane < ntok ? expf(s - frame) : 0.f;
+        l += warp_sum(w);
+      } else {
+        const float mn = fmaxf(m, warp_max(s));
+        const float alpha = expf(m - mn);
+        w = lane < ntok ? expf(s - mn) : 0.f;
+        l = l * alpha + warp_sum(w);
+        m = mn;
+        if (kWantV) {
+#pragma unroll
+          for (int j = 0; j < DPL; ++j) u[j] *= alpha;
+        }
+      }
       if (kWantV) {
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) u[j] *= alpha;
-      }
-    }
-    if (kWantV) {
 #pragma unroll 4
-      for (int t = 0; t < ntok; ++t) {
-        const float wt = __shfl_sync(kFull, w, t);
-        float vv[DPL];
-        load_vec<T, DPL>(vs + t * D + lane * DPL, vv);
+        for (int t = 0; t < ntok; ++t) {
+          const float wt = __shfl_sync(kFull, w, t);
+          float vv[DPL];
+          load_vec<T, DPL>(vs + t * D + lane * DPL, vv);
 #pragma unroll
-        for (int j = 0; j < DPL; ++j) {
-          const float prod = wt * vv[j];
-          u[j] += prod;
-          if (MODE == kModeFixed) ua[j] += fabsf(prod);
+          for (int j = 0; j < DPL; ++j) {
+            const float prod = wt * vv[j];
+            u[j] += prod;
+            if (MODE == kModeFixed) ua[j] += fabsf(prod);
+          }
         }
       }
     }
     __syncwarp();
-    // Stage consumed: refill it before writing results.
-    issue(st);
-
-    if (chunk == (a.L.b + 31) / 32 - 1) {
-      const long long job = static_cast<long long>(row) * a.s + slot;
-      if (MODE != kModeFixed) {
-        if (lane == 0) { a.m[job] = m; a.l[job] = l; }
-      } else if (lane == 0 && a.l) {
-        a.l[job] = l;
-      }
-      if (kWantV) {
+    if (lane == 0) mbar_arrive(&empty_bar[st]);
+    const long long job = static_cast<long long>(row) * a.s + slot;
+    if (MODE != kModeFixed) {
+      if (lane == 0) { a.m[job] = m; a.l[job] = l; }
+    } else if (lane == 0 && a.l) {
+      a.l[job] = l;
+    }
+    if (kWantV) {
+      if constexpr (DPL == 4) {
+        *reinterpret_cast<float4*>(a.u + job * D + lane * 4) = make_float4(u[0], u[1], u[2], u[3]);
+        if (MODE == kModeFixed && a.uabs)
+          *reinterpret_cast<float4*>(a.uabs + job * D + lane * 4) = make_float4(ua[0], ua[1], ua[2], ua[3]);
+      } else {
 #pragma unroll
         for (int j = 0; j < DPL; ++j) {
           a.u[job * D + lane * DPL + j] = u[j];
@@ -371,36 +447,49 @@ __global__ void __launch_bounds__(128) jobs_generic_kernel(JobArgs a) {
 
 // ------------------------------------------------------------------ epilogues
 
-// merge_partials (kernels.py:74-91): one CTA per row, threads over dims.
-__global__ void merge_kernel(const float* m, const float* l, const float* u, const unsigned char* include, int s,
-                             int d, float* out) {
-  const int row = blockIdx.x;
-  __shared__ float sM;
+// merge_partials (kernels.py:74-91): one CTA per row. Warp 0 forms the
+// weights exp(m - M) (M = max included m, or 0 if none); threads then reduce
+// the numerators over slots with coalesced loads, eight slots in flight.
+__global__ void __launch_bounds__(256) merge_kernel(const float* m, const float* l, const float* u,
+                                                   const unsigned char* include, int s, int d, float* out) {
+  extern __shared__ __align__(16) float msm[];  // w[s]
   __shared__ float sZ;
-  if (threadIdx.x == 0) {
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
+  float* w = msm;
+  const long long base = static_cast<long long>(row) * s;
+  if (tid < 32) {
     float M = neg_inf();
-    for (int i = 0; i < s; ++i) {
-      const bool inc = include == nullptr || include[static_cast<long long>(row) * s + i];
-      if (inc) M = fmaxf(M, m[static_cast<long long>(row) * s + i]);
+    for (int i = lane; i < s; i += 32) {
+      const bool inc = include == nullptr || include[base + i];
+      if (inc) M = fmaxf(M, m[base + i]);
     }
+    M = warp_max(M);
     if (M == neg_inf()) M = 0.f;
     float z = 0.f;
-    for (int i = 0; i < s; ++i) {
-      const bool inc = include == nullptr || include[static_cast<long long>(row) * s + i];
-      if (inc) z += expf(m[static_cast<long long>(row) * s + i] - M) * l[static_cast<long long>(row) * s + i];
+    for (int i = lane; i < s; i += 32) {
+      const bool inc = include == nullptr || include[base + i];
+      const float wi = inc ? expf(m[base + i] - M) : 0.f;
+      w[i] = wi;
+      if (inc) z += wi * l[base + i];
     }
-    sM = M;
-    sZ = fmaxf(z, 1e-30f);
+    z = warp_sum(z);
+    if (lane == 0) sZ = fmaxf(z, 1e-30f);
   }
   __syncthreads();
-  const float M = sM, z = sZ;
-  for (int dd = threadIdx.x; dd < d; dd += blockDim.x) {
+  const float z = sZ;
+  for (int dd = tid; dd < d; dd += blockDim.x) {
+    const float* ur = u + base * d + dd;
     float acc = 0.f;
-    for (int i = 0; i < s; ++i) {
-      const long long j = static_cast<long long>(row) * s + i;
-      const bool inc = include == nullptr || include[j];
-      if (inc) acc += expf(m[j] - M) * u[j * d + dd];
+    int i = 0;
+    for (; i + 8 <= s; i += 8) {
+      float x[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[j] = ur[static_cast<long long>(i + j) * d];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc = fmaf(w[i + j], x[j], acc);
     }
+    for (; i < s; ++i) acc = fmaf(w[i], ur[static_cast<long long>(i) * d], acc);
     out[static_cast<long long>(row) * d + dd] = acc / z;
   }
 }
@@ -502,11 +591,14 @@ __global__ void slot_sum_kernel(const float* x, const float* y, int s, int d, fl
 
 // ------------------------------------------------------------------ host side
 
+static size_t ws_stage_bytes(const JobArgs& a, int elem) {
+  return static_cast<size_t>(a.L.b) * a.d * elem * (a.mode == kModeMass ? 1 : 2);
+}
+
 static bool fast_eligible(const JobArgs& a, int elem) {
   if (a.d != 64 && a.d != 128 && a.d != 256) return false;
-  // Four warps with at least one stage each must fit the shared-memory plan.
-  const size_t stage = static_cast<size_t>(32) * a.d * elem * (a.mode == kModeMass ? 1 : 2);
-  if (4 * stage > 200 * 1024) return false;
+  // At least four whole-block stages must fit the shared-memory plan.
+  if (4 * ws_stage_bytes(a, elem) > 200 * 1024) return false;
   const uintptr_t pk = reinterpret_cast<uintptr_t>(a.L.k), pv = reinterpret_cast<uintptr_t>(a.L.v);
   if ((pk | pv) & 15) return false;
   if ((a.d * elem) % 16) return false;
@@ -516,24 +608,20 @@ static bool fast_eligible(const JobArgs& a, int elem) {
 }
 
 template <typename T, int DPL, int MODE>
-constexpr size_t fast_stage_bytes() {
-  return static_cast<size_t>(32) * 32 * DPL * sizeof(T) * (MODE == kModeMass ? 1 : 2);
-}
-
-template <typename T, int DPL, int MODE>
 static int launch_fast_t(const JobArgs& a, int num_sms, cudaStream_t stream) {
-  constexpr size_t kStage = fast_stage_bytes<T, DPL, MODE>();
-  constexpr int NST = (4 * 3 * kStage <= 200 * 1024) ? 3 : ((4 * 2 * kStage <= 200 * 1024) ? 2 : 1);
-  const size_t stage = kStage;
-  const size_t smem = stage * NST * 4;
-  auto kern = jobs_fast_kernel<T, DPL, MODE, NST>;
+  const size_t stage = ws_stage_bytes(a, sizeof(T));
+  const size_t cap = (200 * 1024) / stage;
+  const int nst = static_cast<int>(cap < 64 ? cap : 64);
+  const int ncons = nst < kCons ? nst : kCons;   // every consumer owns >= 1 stage
+  const int kps = nst / ncons;                   // stages per consumer
+  const size_t smem = stage * kps * ncons;
+  auto kern = jobs_fast_kernel<T, DPL, MODE>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   const long long njobs = static_cast<long long>(a.rows) * a.s;
-  long long ctas = (njobs + 3) / 4;
-  const long long cap = static_cast<long long>(num_sms) * (smem <= 110 * 1024 ? 2 : 1);
-  if (ctas > cap) ctas = cap;
+  long long ctas = (njobs + ncons - 1) / ncons;
+  if (ctas > num_sms) ctas = num_sms;
   if (ctas < 1) ctas = 1;
-  kern<<<static_cast<unsigned>(ctas), 128, smem, stream>>>(a);
+  kern<<<static_cast<unsigned>(ctas), kWsThreads, smem, stream>>>(a, kps, ncons);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -577,7 +665,10 @@ int launch_jobs(const JobArgs& a, int kv_dtype, int num_sms, cudaStream_t stream
 
 int launch_merge(const float* m, const float* l, const float* u, const unsigned char* include, int rows, int s, int d,
                  float* out, cudaStream_t stream) {
-  merge_kernel<<<rows, 128, 0, stream>>>(m, l, u, include, s, d, out);
+  const size_t smem = static_cast<size_t>(s) * 4;
+  if (smem > 200 * 1024) return -1;
+  cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  merge_kernel<<<rows, 256, smem, stream>>>(m, l, u, include, s, d, out);
   return static_cast<int>(cudaGetLastError());
 }
 
