@@ -66,7 +66,7 @@ extern "C" {
 #define STK_PRED_NONE 3
 
 /* repair variants */
-#define STK_VAR_SPLIT 0         /* kernels.py:554-600  repair()              */
+#define STK_VAR_SPLIT 0         /* kernels.py:504-550  repair()              */
 #define STK_VAR_FUSED 1         /* fused.py:176-220    repair_fused()        */
 #define STK_VAR_SIGNED 2        /* signed_repair.py:175-232 repair_signed()  */
 #define STK_VAR_SIGNED_FUSED 3  /* signed_fused.py:148-193 repair_signed_fused() */
@@ -123,7 +123,7 @@ STK_API const char* stk_last_error(void);
 STK_API int stk_device_sm_count(int device);
 
 /* Fused min/max query-sign bound scores, FP64 fixed-order sum rounded to FP32.
- * Replaces selector.py:30-45 block_scores() (_score, selector.py:8-20) and the
+ * Replaces selector.py:23-38 block_scores() (_score, selector.py:8-20) and the
  * scoring half of gqa.py:145-161 (_bound_score, gqa.py:15-26).
  * q [hq, d] (q_dtype); lo/hi [hmeta, n, d] FP32 with hq % hmeta == 0;
  * scores [hq, n] FP32. */
@@ -134,7 +134,7 @@ STK_API int stk_bound_scores(const void* q, int q_dtype, const float* lo, const 
 STK_API size_t stk_select_workspace_bytes(int sel_heads, int total_blocks);
 
 /* Score + strict Top-K, ties to the lower block ID, IDs ascending per row.
- * Replaces selector.py:48-50 select_blocks() and gqa.py:145-161
+ * Replaces selector.py:41-43 select_blocks() and gqa.py:145-161
  * select_blocks() (torch.topk at selector.py:43 / gqa.py:161).
  * q [R, hq, d]; lo/hi [hmeta, total_blocks, d]; requests own block ranges
  * block_offsets[r]..block_offsets[r+1] (or [0, n) when NULL, R == 1).
@@ -166,12 +166,12 @@ STK_API int stk_block_states(const stk_kv* kv, const void* q, int q_dtype, int r
                      float* uabs, int32_t* status, void* stream);
 
 /* LSE merge of per-slot states with an optional include mask.
- * Replaces kernels.py:487-492 merge_partials() (_merge, kernels.py:74-91). */
+ * Replaces kernels.py:437-442 merge_partials() (_merge, kernels.py:74-91). */
 STK_API int stk_merge_states(const float* m, const float* l, const float* u, const uint8_t* include, int rows, int s, int d,
                      float* out, void* stream);
 
 /* Full speculation for one prediction mode.
- * Replaces kernels.py:500-551 speculate() incl. _group (kernels.py:94-117) and
+ * Replaces kernels.py:450-501 speculate() incl. _group (kernels.py:94-117) and
  * the compact pipeline (_mass_only, _compact_group, _compact_values).
  * Outputs follow stk_prediction: state m/l/u [rows, sc]; high [rows, sp];
  * retained_ids [rows, sc]; low m/l [rows], low u/abs [rows, d];
@@ -186,12 +186,12 @@ STK_API int stk_speculate(const stk_kv* kv, const void* q, int q_dtype, int rows
 
 /* One-launch repair: set difference, signed recompute of misses and
  * wrong-low blocks, guarded LSE merge, in-launch strict fallback.
- * Replaces kernels.py:554-600 repair(), fused.py:176-220 repair_fused(),
+ * Replaces kernels.py:504-550 repair(), fused.py:176-220 repair_fused(),
  * signed_repair.py:175-232 repair_signed(), signed_fused.py:148-193
  * repair_signed_fused(), gqa.py:164-193 repair_saved()/repair_union(),
- * gqa_light.py:63-92 repair_saved_light()/auto, gqa_hierarchical.py:207-236
+ * gqa_light.py:63-92 repair_saved_light()/auto, gqa_hierarchical.py:111-144
  * repair_saved()/repair_saved_shared(); with pred_state->mode ==
- * STK_PRED_NONE it is kernels.py:495-497 exact_attention() / gqa.py:140-142. */
+ * STK_PRED_NONE it is kernels.py:445-447 exact_attention() / gqa.py:140-142. */
 STK_API int stk_repair(const stk_kv* kv, const void* q, int q_dtype, int rows, int hq, const void* sel, int sel64, int sa,
                const void* pred, int pred64, int sp, const stk_prediction* pred_state, int variant,
                float min_remaining, float cancellation_tol, float max_extra_mass, int max_blocks,

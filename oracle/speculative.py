@@ -93,14 +93,14 @@ def online(X, h, bids, m=NEG_INF, z=F(0.), u=None):
 
 
 def compact_capacity(s, tau):
-    """kernels.py:535."""
+    """kernels.py:485."""
     return s if tau <= 1 / s else min(s, int(1 / tau) + 1)
 
 
 # --------------------------------------------------------------------------- speculate
 
 def speculate(q, k, v, predicted, mode="saved", tau=0.1, keep_mass=False):
-    """kernels.py:500-551. Returns a dict of FP32/bool/int arrays."""
+    """kernels.py:450-501. Returns a dict of FP32/bool/int arrays."""
     X = Inputs(q, k, v)
     P = np.asarray(predicted).astype(np.int64)
     h, s = P.shape
@@ -267,7 +267,7 @@ def _strict(X, i, A):
 
 
 def _repair_split(X, i, A, P, pred, mn, tol, eps, variant):
-    """kernels.py:554-600: membership, miss partials, merge in the common frame, fallback."""
+    """kernels.py:504-550: membership, miss partials, merge in the common frame, fallback."""
     hit_p, miss = _membership(A, P)
     mode = pred["mode"]
     if mode == "saved":  # _saved_merge, kernels.py:196-218

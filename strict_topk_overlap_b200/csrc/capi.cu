@@ -231,11 +231,11 @@ int stk_speculate(const stk_kv* kv, const void* q, int q_dtype, int rows, int hq
   rc = launch_compact_group(mass_m, mass_l, pred, pred64, rows, sp, sc, mass_threshold, high, retained_ids, low_m,
                             low_l, overflow, st);
   if (rc) return cuda_status(rc, "compact_group");
-  // Pass 2a: retained high blocks, full states (kernels.py:387-406).
+  // Pass 2a: retained high blocks, full states (kernels.py:337-356).
   rc = stk_block_states(kv, q, q_dtype, rows, hq, retained_ids, pred64, sc, nullptr, 0, 0, nullptr, 0, 0, nullptr,
                         STK_MODE_FULL, nullptr, state_m, state_l, state_u, nullptr, status, stream);
   if (rc) return rc;
-  // Pass 2b: low blocks per token at low_m, then per-row sums (kernels.py:370-386).
+  // Pass 2b: low blocks per token at low_m, then per-row sums (kernels.py:320-336).
   float* su = static_cast<float*>(workspace);
   float* sa = su + static_cast<size_t>(rows) * sp * d;
   rc = stk_block_states(kv, q, q_dtype, rows, hq, pred, pred64, sp, high, 2, 1, nullptr, 0, 0, nullptr,

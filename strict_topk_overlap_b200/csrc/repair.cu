@@ -630,7 +630,7 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
   bool bad = false;
   float z_final, cp, cl_scale;
   if (a.variant == kVarSplit && hybrid) {
-    // kernels.py:221-270: everything in the common frame m.
+    // kernels.py:172-221: everything in the common frame m.
     const float m = fmaxf(Mp, low_hit ? lm : neg_inf());
     const float lowalpha = low_hit ? expf(lm - m) : 0.f;
     const float ll = low_hit ? a.low_l[row] * lowalpha : 0.f;
@@ -658,7 +658,7 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
     z_final = fmaxf(z, 1e-30f);
     cl_scale = lowalpha;
   } else if (hybrid && a.variant != kVarSaved && a.variant != kVarUnion) {
-    // fused.py:94-166 / signed_repair.py:139-165 / signed_fused.py:325-354: low frame.
+    // fused.py:94-166 / signed_repair.py:139-165 / signed_fused.py:90-125: low frame.
     float mass = 0.f;
     if (low_hit) {
       const float ll = a.low_l[row];

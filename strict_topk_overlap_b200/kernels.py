@@ -50,7 +50,7 @@ class RepairResult:
 
 
 def _shape(q, k, v, ids):
-    """Shape contract of kernels.py:460-467 (AssertionError on violation),
+    """Shape contract of kernels.py:410-417 (AssertionError on violation),
     widened to native GQA: Q heads must be a multiple of K/V heads."""
     assert q.is_cuda and k.is_cuda and v.is_cuda and ids.is_cuda
     assert q.ndim == 2 and k.ndim == 4 and v.shape == k.shape
@@ -91,7 +91,7 @@ def block_partials(q, k, v, ids, active=None):
     """Each block's m, sum exp(logit-m), sum exp(logit-m)*V (all FP32).
 
     ``active`` ([H] or [H,S] bool) marks blocks to compute; inactive slots hold
-    (-inf, 0, 0) (reference kernels.py:475-484)."""
+    (-inf, 0, 0) (reference kernels.py:425-434)."""
     h, n, b, d, s = _shape(q, k, v, ids)
     state = _allocate_state(h, s, d, q.device)
     if active is not None:
@@ -101,7 +101,7 @@ def block_partials(q, k, v, ids, active=None):
 
 def merge_partials(state, include=None):
     """LSE merge of states [H,S] (+ optional include mask) -> FP32 [H,D]
-    (reference kernels.py:487-492)."""
+    (reference kernels.py:437-442)."""
     h, s, d = state.u.shape
     out = torch.empty((h, d), device=state.u.device, dtype=torch.float32)
     if include is not None:
@@ -118,7 +118,7 @@ def exact_attention(q, k, v, selected):
 
 
 def compact_capacity(s: int, mass_threshold: float) -> int:
-    """Retained-slot capacity of compact mode (reference kernels.py:535)."""
+    """Retained-slot capacity of compact mode (reference kernels.py:485)."""
     return s if mass_threshold <= 1 / s else min(s, int(1 / mass_threshold) + 1)
 
 
@@ -128,7 +128,7 @@ def speculate(q, k, v, predicted, mode='saved', mass_threshold=0.1, *, keep_mass
     saved: per-block states; hybrid: per-block states plus high mask and a
     low-mass aggregate with its absolute numerator envelope; compact: a
     K-only statistics pass, capacity-bounded retained states and a per-token
-    low aggregate (reference kernels.py:500-551). ``keep_mass`` exposes the
+    low aggregate (reference kernels.py:450-501). ``keep_mass`` exposes the
     per-block maxima and normalizers in predicted order.
     """
     if mode not in ('saved', 'hybrid', 'compact'):
@@ -214,7 +214,7 @@ def repair(q, k, v, selected, predicted, prediction, min_remaining=1.e-3, cancel
     """Restore exact selected-set semantics; conservative guards recompute QKV.
 
     Remaining is the residual low-group denominator over the original one, in
-    the merge's common exponent frame (reference kernels.py:554-600). A wholly
+    the merge's common exponent frame (reference kernels.py:504-550). A wholly
     rejected low group is discarded directly without subtraction. Single launch.
     """
     h, n, b, d, sa = _shape(q, k, v, selected)

@@ -14,7 +14,7 @@ from . import _lib as L
 
 
 def _validate(q, lo, hi):
-    """Argument checks of selector.py:30-40 (same ValueError messages)."""
+    """Argument checks of selector.py:23-33 (same ValueError messages)."""
     if lo.ndim != 3 or hi.shape != lo.shape:
         raise ValueError("lo and hi must have the same [heads, blocks, dim] shape")
     h, n, d = lo.shape

@@ -87,7 +87,7 @@ def ref_fp64(q, k, v, ids, include=None):
 
 
 def block_scores_ref(q, lo, hi):
-    """selector.block_scores without its CUDA-device check (selector.py:30-45)."""
+    """selector.block_scores without its CUDA-device check (selector.py:23-38)."""
     import triton
     h, n, d = lo.shape
     scores = torch.empty((h, n), dtype=torch.float32)
