@@ -147,6 +147,30 @@ STK_API int stk_select_topk(const void* q, int q_dtype, const float* lo, const f
                     int id_base, int32_t* ids_out, unsigned long long* keys_out, void* workspace,
                     size_t workspace_bytes, int32_t* status, void* stream);
 
+/* Capacity of the library's own score scratch, in scores (rows x blocks). */
+#define STK_SELECT_STATIC_MAX_SCORES (1 << 20)
+
+/* stk_select_topk for callers that cannot allocate device memory: a decode
+ * loop that must not call cudaMalloc (it may synchronise the device, and it
+ * is not allowed while the stream is being captured), or a plugin host that
+ * passes only inputs and outputs. No counterpart in the reference (whose
+ * selector allocates its scores with torch). Same arguments and results as
+ * stk_select_topk, without workspace / workspace_bytes: the FP64 scores go
+ * to one static device array of STK_SELECT_STATIC_MAX_SCORES doubles (8 MiB,
+ * held by every GPU that loads the library until the process exits).
+ * Selections needing more than that ((group_select ? hmeta : hq) x
+ * total_blocks scores) return STK_EWS. Allocates nothing: no cudaMalloc,
+ * cudaFree or allocating library call. The first call on each device looks
+ * up the array's device address (cudaGetSymbolAddress) with that device
+ * current, so make it before any stream capture. Every call on a device
+ * shares the one array and leaves its scores in it: calls whose kernels
+ * overlap on the GPU (other streams, other threads) race and must be
+ * ordered by the caller. */
+STK_API int stk_select_topk_static(const void* q, int q_dtype, const float* lo, const float* hi, int R, int hq,
+                                   int hmeta, int n, const int32_t* block_offsets, int total_blocks, int max_blocks,
+                                   int d, int topk, int group_select, int id_base, int32_t* ids_out,
+                                   unsigned long long* keys_out, int32_t* status, void* stream);
+
 /* Merge shard-local Top-K candidates (ascending IDs per row) into the global
  * strict Top-K. New: the context-parallel exchange of the decode path. */
 STK_API int stk_merge_candidates(const unsigned long long* keys, const int32_t* ids, int rows, int ncand, int topk,

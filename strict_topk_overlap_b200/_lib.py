@@ -26,7 +26,7 @@ _DTYPES = {torch.float32: STK_F32, torch.float16: STK_F16, torch.bfloat16: STK_B
 # Exported symbols, exactly those declared in include/strict_topk_b200.h.
 SYMBOLS = (
     "stk_abi_version", "stk_last_error", "stk_device_sm_count", "stk_bound_scores",
-    "stk_select_workspace_bytes", "stk_select_topk", "stk_merge_candidates", "stk_block_states",
+    "stk_select_workspace_bytes", "stk_select_topk", "stk_select_topk_static", "stk_merge_candidates", "stk_block_states",
     "stk_merge_states", "stk_speculate_workspace_bytes", "stk_speculate", "stk_repair", "stk_touch_kv",
 )
 
@@ -60,6 +60,7 @@ _SIGS = {
     "stk_bound_scores": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _P]),
     "stk_select_workspace_bytes": (_SZ, [_I, _I]),
     "stk_select_topk": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _SZ, _P, _P]),
+    "stk_select_topk_static": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
     "stk_merge_candidates": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
     "stk_block_states": (_I, [C.POINTER(StkKV), _P, _I, _I, _I, _P, _I, _I, _P, _I, _I, _P, _I, _I, _P, _I, _P,
                               _P, _P, _P, _P, _P, _P]),

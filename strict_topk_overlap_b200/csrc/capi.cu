@@ -7,6 +7,7 @@
 #include <atomic>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "internal.cuh"
@@ -298,3 +299,71 @@ int stk_touch_kv(const stk_kv* kv, int rows, int hq, const void* ids, int ids64,
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ selection without a caller workspace
+//
+// Some callers cannot hand this library a device workspace: a host whose
+// decode loop must not call cudaMalloc (it can synchronise the whole device
+// and stall the other streams of the step, and it is not allowed while the
+// stream is being captured), or a plugin interface that passes only input and
+// output buffers. For them the FP64 score scratch of stk_select_topk lives in
+// one file-scope device array instead. Every GPU that loads this library
+// holds the array (STK_SELECT_STATIC_MAX_SCORES doubles, 8 MiB) until the
+// process exits.
+//
+// In host code `g_select_scores` names a host-side stand-in, not device
+// memory, so it is never passed to a kernel. Its device address is looked up
+// once per device with cudaGetSymbolAddress, on the first call made while
+// that device is current, and cached.
+namespace {
+static __device__ __align__(256) double g_select_scores[STK_SELECT_STATIC_MAX_SCORES];
+
+std::mutex g_static_setup;
+std::atomic<void*> g_select_scores_addr[kMaxDevices];
+
+int static_scores_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(STK_EINVAL, "device %d beyond the %d this library tracks", dev, kMaxDevices);
+  void* p = g_select_scores_addr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    std::lock_guard<std::mutex> lock(g_static_setup);
+    p = g_select_scores_addr[dev].load(std::memory_order_acquire);
+    if (p == nullptr) {
+      e = cudaGetSymbolAddress(&p, g_select_scores);
+      if (e != cudaSuccess || p == nullptr)
+        return fail(e != cudaSuccess ? static_cast<int>(e) : STK_EINVAL, "cudaGetSymbolAddress(select scratch): %s",
+                    cudaGetErrorString(e));
+      g_select_scores_addr[dev].store(p, std::memory_order_release);
+    }
+  }
+  *out = p;
+  return 0;
+}
+}  // namespace
+
+extern "C" int stk_select_topk_static(const void* q, int q_dtype, const float* lo, const float* hi, int R, int hq,
+                                      int hmeta, int n, const int32_t* block_offsets, int total_blocks,
+                                      int max_blocks, int d, int topk, int group_select, int id_base,
+                                      int32_t* ids_out, unsigned long long* keys_out, int32_t* status,
+                                      void* stream) {
+  if (R <= 0 || hq <= 0 || hmeta <= 0 || hq % hmeta) return fail(STK_EINVAL, "bad select shape");
+  if (block_offsets == nullptr) total_blocks = n;
+  if (total_blocks <= 0) return fail(STK_EINVAL, "bad select shape");
+  const int hsel = group_select ? hmeta : hq;
+  const size_t need = stk_select_workspace_bytes(hsel, total_blocks);
+  const size_t have = sizeof(double) * static_cast<size_t>(STK_SELECT_STATIC_MAX_SCORES);
+  if (need > have)
+    return fail(STK_EWS,
+                "selection of %d rows x %d blocks needs %zu bytes of score scratch; the static scratch holds %zu "
+                "(STK_SELECT_STATIC_MAX_SCORES = %d scores); use stk_select_topk with a workspace",
+                hsel, total_blocks, need, have, STK_SELECT_STATIC_MAX_SCORES);
+  void* scratch = nullptr;
+  const int rc = static_scores_address(&scratch);
+  if (rc) return rc;
+  // The score pass writes every slot the Top-K pass reads, so nothing in the
+  // shared array has to start at zero.
+  return stk_select_topk(q, q_dtype, lo, hi, R, hq, hmeta, n, block_offsets, total_blocks, max_blocks, d, topk,
+                         group_select, id_base, ids_out, keys_out, scratch, have, status, stream);
+}
