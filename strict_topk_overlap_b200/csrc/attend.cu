@@ -1,0 +1,359 @@
+// Exact / saved / union attention over a row's selected blocks, one launch.
+//
+// Replaces, for the plain-LSE-merge repairs (no guards):
+//   kernels.py:437-447       exact_attention / merge_partials(block_partials)
+//   gqa.py:29-104,140-142    gqa.exact, REPAIR _partial + _merge_repair
+//                            (repair_saved, repair_union)
+//   gqa_light.py:10-60       _repair_light (saved semantics)
+//   gqa_hierarchical.py:99-144 exact / repair_saved / repair_saved_shared
+//
+// One thread-block cluster of CS CTAs (kAW warps each) serves one
+// (request, query head) row:
+//   1. every CTA loads the row's selected IDs A (and predicted IDs P), marks
+//      P in a shared-memory bitmap and lists the blocks to compute in A
+//      order — all of A (exact) or A minus P (saved, union);
+//   2. CTA c takes list entries c, c + CS, ...: it asks L2 for all of their
+//      blocks (cp.async.bulk.prefetch.L2), then each warp streams its entries
+//      through a private stage with bulk copies and folds each block's state
+//      into a per-warp LSE state; the CTA also folds retained prediction
+//      slots c, c + CS, ... (saved: P slots whose ID is in A; union: all);
+//   3. each CTA pushes its partial (M, Z, U[D]) into rank 0's shared memory
+//      with distributed-shared-memory stores; after one cluster barrier rank
+//      0 merges the CS partials in rank order and writes the row's output.
+// Waits on bulk copies are bounded; a warp whose wait ran out records the
+// status and stops, and its CTA still reaches the cluster barrier.
+#include <cooperative_groups.h>
+
+#include "block_state.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace stk {
+
+constexpr int kAW = 4;           // warps per CTA
+constexpr int kAttendCluster = 8;
+
+struct AttendSmem {
+  long long* a_ids;  // [sa]
+  long long* p_ids;  // [sp]
+  unsigned* bitA;    // [nwords]
+  unsigned* bitP;    // [nwords]
+  int* list;         // [sa] entries (indices into A) to compute
+  float* qv;         // [d]
+  float* wU;         // [kAW][d] per-warp numerators
+  float* pushU;      // [CS][d] partial numerators pushed by each CTA (rank 0's copy is read)
+  float* pushS;      // [CS][2] partial (M, Z)
+};
+
+template <int DPH, typename T>
+__host__ __device__ inline size_t attend_layout(const RepairArgs& a, int cs, AttendSmem* S, unsigned char* base) {
+  const int D = a.d;
+  size_t off = 0;
+  auto take = [&](size_t bytes, size_t align) {
+    off = (off + align - 1) & ~(align - 1);
+    const size_t at = off;
+    off += bytes;
+    return at;
+  };
+  const size_t st = take(static_cast<size_t>(kAW) * 2 * 32 * D * sizeof(T), 128);
+  (void)st;
+  const int nwords = (a.max_n + 31) / 32;
+  const size_t ai = take(static_cast<size_t>(a.sa) * 8, 16), pi = take(static_cast<size_t>(a.sp) * 8, 16);
+  const size_t ba = take(static_cast<size_t>(nwords) * 4, 16), bp = take(static_cast<size_t>(nwords) * 4, 16);
+  const size_t li = take(static_cast<size_t>(a.sa) * 4, 16);
+  const size_t qv = take(static_cast<size_t>(D) * 4, 16);
+  const size_t wu = take(static_cast<size_t>(kAW) * D * 4, 16);
+  const size_t pu = take(static_cast<size_t>(cs) * D * 4, 16);
+  const size_t ps = take(static_cast<size_t>(cs) * 8, 16);
+  if (S != nullptr) {
+    S->a_ids = reinterpret_cast<long long*>(base + ai);
+    S->p_ids = reinterpret_cast<long long*>(base + pi);
+    S->bitA = reinterpret_cast<unsigned*>(base + ba);
+    S->bitP = reinterpret_cast<unsigned*>(base + bp);
+    S->list = reinterpret_cast<int*>(base + li);
+    S->qv = reinterpret_cast<float*>(base + qv);
+    S->wU = reinterpret_cast<float*>(base + wu);
+    S->pushU = reinterpret_cast<float*>(base + pu);
+    S->pushS = reinterpret_cast<float*>(base + ps);
+  }
+  return off;
+}
+
+// One warp folds a block state (m, l, u in half-warp layout) into its
+// running LSE state (wm, wl in registers; numerators in smem row U).
+template <int DPH>
+__device__ __forceinline__ void fold_state(float& wm, float& wl, float* U, float m, float l, const float (&u)[DPH],
+                                           int lane) {
+  if (m == neg_inf()) return;
+  const float mn = fmaxf(wm, m);
+  const float a1 = wm == neg_inf() ? 0.f : expf(wm - mn), a2 = expf(m - mn);
+  if (lane < 16) {
+#pragma unroll
+    for (int j = 0; j < DPH; ++j) {
+      float* p = U + lane * DPH + j;
+      *p = *p * a1 + u[j] * a2;
+    }
+  }
+  wl = wl * a1 + l * a2;
+  wm = mn;
+}
+
+template <typename T, int DPH, bool FULL32>
+__global__ void __launch_bounds__(kAW * 32) attend_kernel(RepairArgs a) {
+  constexpr int D = 16 * DPH;
+  constexpr int kChunk = 32 * D;  // elements of one 32-token chunk of K (or V)
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ uint64_t bar[kAW];
+  __shared__ int sh_cnt[kAW + 1];
+  __shared__ float sh_w[kAW][2];
+  __shared__ float sh_keep[2];
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int CS = static_cast<int>(cluster.num_blocks());
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row = blockIdx.x / CS;
+  const int r = row / a.hq;
+  const int kv = (row - r * a.hq) / a.g;
+  const int nblocks = request_blocks(a.L, r);
+  const bool has_pred = a.pmode != kPredNone;
+
+  AttendSmem S;
+  attend_layout<DPH, T>(a, CS, &S, smem);
+  T* stage = reinterpret_cast<T*>(smem) + static_cast<size_t>(warp) * 2 * kChunk;
+  uint64_t* mb = &bar[warp];
+  const int nwords = (a.max_n + 31) / 32;
+
+  // ---- 1. IDs, q, bitmaps, the list of blocks to compute.
+  if (lane == 0) {
+    mbar_init(mb, 1);
+    fence_barrier_init();
+  }
+  for (int i = tid; i < a.sa; i += blockDim.x) S.a_ids[i] = load_id(a.sel, a.sel64, static_cast<long long>(row) * a.sa + i);
+  if (has_pred)
+    for (int i = tid; i < a.sp; i += blockDim.x)
+      S.p_ids[i] = load_id(a.pred, a.pred64, static_cast<long long>(row) * a.sp + i);
+  for (int dd = tid; dd < D; dd += blockDim.x) S.qv[dd] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + dd);
+  for (int i = tid; i < nwords; i += blockDim.x) { S.bitA[i] = 0u; S.bitP[i] = 0u; }
+  for (int i = tid; i < kAW * D; i += blockDim.x) S.wU[i] = 0.f;
+  __syncthreads();
+  for (int i = tid; i < a.sa; i += blockDim.x) {
+    const long long id = S.a_ids[i];
+    if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); S.a_ids[i] = -1; continue; }
+    atomicOr(&S.bitA[id >> 5], 1u << (id & 31));
+  }
+  if (has_pred)
+    for (int i = tid; i < a.sp; i += blockDim.x) {
+      const long long id = S.p_ids[i];
+      if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); S.p_ids[i] = -1; continue; }
+      atomicOr(&S.bitP[id >> 5], 1u << (id & 31));
+    }
+  __syncthreads();
+  // List = A entries to compute, in A order (block-wide ballot prefix).
+  int total = 0;
+  for (int base = 0; base < a.sa; base += blockDim.x) {
+    const int i = base + tid;
+    bool need = false;
+    if (i < a.sa) {
+      const long long id = S.a_ids[i];
+      need = id >= 0 && !(has_pred && ((S.bitP[id >> 5] >> (id & 31)) & 1u));
+    }
+    const unsigned bal = __ballot_sync(kFull, need);
+    if (lane == 0) sh_cnt[warp] = __popc(bal);
+    __syncthreads();
+    int before = total;
+    for (int w = 0; w < warp; ++w) before += sh_cnt[w];
+    if (need) S.list[before + __popc(bal & ((1u << lane) - 1))] = i;
+    for (int w = 0; w < kAW; ++w) total += sh_cnt[w];
+    __syncthreads();
+  }
+  const int count = total;
+
+  // ---- 2. this CTA's share: L2 prefetch, first copies, retained slots, blocks.
+  for (int k = rank + CS * tid; k < count; k += CS * blockDim.x)
+    prefetch_block<T>(a.L, r, kv, S.a_ids[S.list[k]], true);
+  const int nchunks = (a.L.b + 31) / 32;
+  const int kfirst = rank + CS * warp, kstep = CS * kAW;
+  const unsigned chunk_bytes_full = 32u * D * sizeof(T);
+  auto issue = [&](int k, int c) {
+    const long long bid = S.a_ids[S.list[k]];
+    const int t0 = c * 32, ntok = FULL32 ? 32 : min(32, a.L.b - t0);
+    T* ks = stage;
+    T* vs = stage + kChunk;
+    const unsigned bytes = FULL32 ? chunk_bytes_full : static_cast<unsigned>(ntok * D * sizeof(T));
+    mbar_arrive_expect_tx(mb, 2 * bytes);
+    const T* K = static_cast<const T*>(a.L.k);
+    const T* V = static_cast<const T*>(a.L.v);
+    if (a.L.page_table == nullptr) {
+      const long long o = block_seg(a.L, r, kv, bid, 0).elem_off + static_cast<long long>(t0) * D;
+      bulk_g2s(ks, K + o, bytes, mb);
+      bulk_g2s(vs, V + o, bytes, mb);
+    } else {
+      for (int t = t0; t < t0 + ntok;) {
+        const int pg = t / a.L.page_size, po = t - pg * a.L.page_size;
+        const int cnt = min(a.L.page_size - po, t0 + ntok - t);
+        const long long o = block_seg(a.L, r, kv, bid, pg).elem_off + static_cast<long long>(po) * D;
+        const unsigned sb = static_cast<unsigned>(cnt * D * sizeof(T));
+        bulk_g2s(ks + (t - t0) * D, K + o, sb, mb);
+        bulk_g2s(vs + (t - t0) * D, V + o, sb, mb);
+        t += cnt;
+      }
+    }
+  };
+  if (kfirst < count && lane == 0) issue(kfirst, 0);
+
+  // Retained prediction slots of this CTA (saved: hits; union: every slot),
+  // weights relative to the CTA's own maximum.
+  if (has_pred) {
+    if (warp == 0) {
+      float M = neg_inf();
+      for (int c = rank + CS * lane; c < a.sp; c += CS * 32) {
+        const long long id = S.p_ids[c];
+        const bool keep = id >= 0 && (a.variant == kVarUnion || ((S.bitA[id >> 5] >> (id & 31)) & 1u));
+        if (keep) M = fmaxf(M, a.pm[static_cast<long long>(row) * a.sc + c]);
+      }
+      M = warp_max(M);
+      float Z = 0.f;
+      for (int c = rank + CS * lane; c < a.sp; c += CS * 32) {
+        const long long id = S.p_ids[c];
+        const bool keep = id >= 0 && (a.variant == kVarUnion || ((S.bitA[id >> 5] >> (id & 31)) & 1u));
+        if (keep) Z += expf(a.pm[static_cast<long long>(row) * a.sc + c] - M) * a.pl[static_cast<long long>(row) * a.sc + c];
+      }
+      Z = warp_sum(Z);
+      if (lane == 0) { sh_keep[0] = M; sh_keep[1] = Z; }
+    }
+    __syncthreads();
+  } else if (tid == 0) {
+    sh_keep[0] = neg_inf();
+    sh_keep[1] = 0.f;
+  }
+
+  float qf[DPH];
+#pragma unroll
+  for (int j = 0; j < DPH; ++j) qf[j] = S.qv[(lane & 15) * DPH + j];
+  float wm = neg_inf(), wl = 0.f;
+  float* myU = S.wU + warp * D;
+  unsigned phase = 0;
+  bool ok = true;
+#pragma unroll 1
+  for (int k = kfirst; k < count && ok; k += kstep) {
+    float m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
+#pragma unroll
+    for (int j = 0; j < DPH; ++j) { u[j] = 0.f; ua[j] = 0.f; }
+#pragma unroll 1
+    for (int c = 0; c < nchunks; ++c) {
+      ok = mbar_wait(mb, phase, a.status);
+      phase ^= 1u;
+      if (!ok) break;
+      const int ntok = FULL32 ? 32 : min(32, a.L.b - c * 32);
+      warp_block_state<T, DPH, kModeFull, FULL32>(stage, stage + kChunk, ntok, qf, a.scale, 0.f, m, l, u, ua, lane);
+      __syncwarp();
+      // Stage free: the next chunk of this block, or this warp's next block.
+      if (lane == 0) {
+        if (c + 1 < nchunks) issue(k, c + 1);
+        else if (k + kstep < count) issue(k + kstep, 0);
+      }
+    }
+    if (ok) fold_state<DPH>(wm, wl, myU, m, l, u, lane);
+  }
+  if (lane == 0) { sh_w[warp][0] = wm; sh_w[warp][1] = wl; }
+  __syncthreads();
+
+  // ---- 3. CTA partial -> rank 0 (distributed shared memory), merge there.
+  float M = sh_keep[0];
+  for (int w = 0; w < kAW; ++w) M = fmaxf(M, sh_w[w][0]);
+  float* dstU = cluster.map_shared_rank(S.pushU, 0) + rank * D;
+  const float* pu = has_pred ? a.pu + static_cast<long long>(row) * a.sc * D : nullptr;
+  for (int dd = tid; dd < D; dd += blockDim.x) {
+    float U = 0.f;
+    for (int w = 0; w < kAW; ++w)
+      if (sh_w[w][0] != neg_inf()) U += expf(sh_w[w][0] - M) * S.wU[w * D + dd];
+    if (has_pred && sh_keep[0] != neg_inf()) {
+      // Retained numerators of this CTA's slots, weighted at M.
+      float R = 0.f;
+      for (int c = rank; c < a.sp; c += CS) {
+        const long long id = S.p_ids[c];
+        const bool keep = id >= 0 && (a.variant == kVarUnion || ((S.bitA[id >> 5] >> (id & 31)) & 1u));
+        if (keep) R = fmaf(expf(a.pm[static_cast<long long>(row) * a.sc + c] - M), pu[static_cast<long long>(c) * D + dd], R);
+      }
+      U += R;
+    }
+    dstU[dd] = U;
+  }
+  if (tid == 0) {
+    float Z = sh_keep[0] != neg_inf() ? expf(sh_keep[0] - M) * sh_keep[1] : 0.f;
+    for (int w = 0; w < kAW; ++w)
+      if (sh_w[w][0] != neg_inf()) Z += expf(sh_w[w][0] - M) * sh_w[w][1];
+    float* dstS = cluster.map_shared_rank(S.pushS, 0) + rank * 2;
+    dstS[0] = M;
+    dstS[1] = Z;
+  }
+  cluster.sync();
+  if (rank != 0) return;
+  float GM = neg_inf();
+  for (int c = 0; c < CS; ++c) GM = fmaxf(GM, S.pushS[c * 2]);
+  float GZ = 0.f;
+  for (int c = 0; c < CS; ++c)
+    if (S.pushS[c * 2] != neg_inf()) GZ += expf(S.pushS[c * 2] - GM) * S.pushS[c * 2 + 1];
+  for (int dd = tid; dd < D; dd += blockDim.x) {
+    float U = 0.f;
+    for (int c = 0; c < CS; ++c)
+      if (S.pushS[c * 2] != neg_inf()) U += expf(S.pushS[c * 2] - GM) * S.pushU[c * D + dd];
+    a.out[static_cast<long long>(row) * D + dd] = U / fmaxf(GZ, 1e-30f);
+  }
+  if (tid == 0) {
+    if (a.fallback) a.fallback[row] = 0;
+    if (a.remaining) a.remaining[row] = 1.f;
+    if (a.approx) a.approx[row] = 0;
+    if (a.extra) a.extra[row] = 0.f;
+    if (a.pos_out) a.pos_out[row] = count;
+    if (a.total_out) a.total_out[row] = count;
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+template <typename T, int DPH>
+static int launch_attend_t(const RepairArgs& a, cudaStream_t stream) {
+  const int jobs = a.sa;
+  int cs = (jobs + kAW - 1) / kAW;
+  if (cs > kAttendCluster) cs = kAttendCluster;
+  if (cs < 1) cs = 1;
+  const size_t smem = attend_layout<DPH, T>(a, cs, nullptr, nullptr);
+  if (smem > 220 * 1024) return -2;
+  auto kern = a.L.b % 32 == 0 ? attend_kernel<T, DPH, true> : attend_kernel<T, DPH, false>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.rows) * cs, 1, 1);
+  cfg.blockDim = dim3(kAW * 32, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kern, a));
+}
+
+// Returns 1 when the fast attend kernel does not apply (the caller then uses
+// the general repair kernel), else the launch status.
+int launch_attend(const RepairArgs& a, int kv_dtype, cudaStream_t stream) {
+  const bool plain = a.pmode == kPredNone || (a.pmode == kPredSaved && (a.variant == kVarSaved || a.variant == kVarUnion));
+  if (!plain || a.rows == 0) return 1;
+  if (a.pmode == kPredSaved && a.sc != a.sp) return 1;
+  const int esz = kv_dtype == kF32 ? 4 : 2;
+  const uintptr_t pk = reinterpret_cast<uintptr_t>(a.L.k) | reinterpret_cast<uintptr_t>(a.L.v);
+  const bool aligned = (pk & 15) == 0 && (a.d * esz) % 16 == 0 &&
+                       (a.L.page_table == nullptr || a.L.b % a.L.page_size == 0) && a.L.kv_request_stride % 8 == 0;
+  if (!aligned || (a.d != 64 && a.d != 128)) return 1;
+  switch (kv_dtype) {
+    case kF32: return a.d == 64 ? launch_attend_t<float, 4>(a, stream) : launch_attend_t<float, 8>(a, stream);
+    case kF16: return a.d == 64 ? launch_attend_t<__half, 4>(a, stream) : launch_attend_t<__half, 8>(a, stream);
+    default: return a.d == 64 ? launch_attend_t<__nv_bfloat16, 4>(a, stream) : launch_attend_t<__nv_bfloat16, 8>(a, stream);
+  }
+}
+
+}  // namespace stk

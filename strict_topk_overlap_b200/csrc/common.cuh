@@ -102,6 +102,25 @@ __device__ __forceinline__ void load_vec(const T* p, float (&out)[N]) {
   }
 }
 
+// q row slice [off, off + N) of a runtime-dtype tensor, widened to FP32.
+template <int N>
+__device__ __forceinline__ void load_q(const void* q, int dtype, long long off, float (&out)[N]) {
+#pragma unroll
+  for (int j = 0; j < N; ++j) out[j] = load_any(q, dtype, off + j);
+}
+
+// Store N consecutive floats (16-byte aligned when N % 4 == 0).
+template <int N>
+__device__ __forceinline__ void store_vec(float* p, const float (&v)[N]) {
+  if constexpr (N % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < N; i += 4) *reinterpret_cast<float4*>(p + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) p[i] = v[i];
+  }
+}
+
 // ---------------------------------------------------------------- warp math
 __device__ __forceinline__ float warp_max(float x) {
 #pragma unroll
@@ -167,6 +186,13 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
       : "memory");
 }
 
+// Ask L2 to fetch `bytes` (16-byte aligned, multiple of 16) starting at
+// `src`; no completion is tracked. Later bulk copies of the same bytes then
+// hit L2 instead of waiting a full DRAM round trip.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -174,19 +200,42 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
   unsigned ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+      : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }
 
-// Bounded wait: each try_wait suspends for up to ~1 ms of hardware time; the
-// loop gives up after kWaitTries attempts (far above any legal copy time).
-constexpr int kWaitTries = 4000;
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Timeline probes: compiled in only with -DSTK_TRACE (a profiling build of
+// the library); otherwise they vanish. STK_TRACE_AT(buf, i) stores the
+// global nanosecond timer at buf[i].
+#ifdef STK_TRACE
+#define STK_TRACE_AT(buf, i) ((buf)[(i)] = global_ns())
+#else
+#define STK_TRACE_AT(buf, i) ((void)0)
+#endif
+
+// Bounded wait: try_wait (which itself blocks for a short, system-defined
+// time) until the phase completes, giving up once kWaitNs of wall time have
+// passed (far above any legal copy time); a wait that gives up records
+// kStatusWaitTimeout and returns false.
+constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, int* status) {
-  for (int i = 0; i < kWaitTries; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  while (true) {
     if (mbar_try_wait(bar, parity)) return true;
+#ifdef STK_WAIT_BACKOFF
+    __nanosleep(STK_WAIT_BACKOFF);
+#endif
+    if (global_ns() - t0 > kWaitNs) break;
   }
   report(status, kStatusWaitTimeout);
   return false;

@@ -129,5 +129,7 @@ int launch_slot_sum(const float* x, const float* y, int rows, int s, int d, floa
 int launch_touch(const KVLayout& L, int rows, int hq, int g, const void* ids, int ids64, int s, float* out,
                  int kv_dtype, cudaStream_t stream);
 int launch_repair(const RepairArgs& a, int kv_dtype, cudaStream_t stream);
+// Exact / saved / union (plain LSE merge) fast path; returns 1 when it does not apply.
+int launch_attend(const RepairArgs& a, int kv_dtype, cudaStream_t stream);
 
 }  // namespace stk

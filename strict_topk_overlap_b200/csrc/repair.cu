@@ -10,26 +10,53 @@
 //   gqa_hierarchical.py:99-130 (_match_ids, REPAIR packed partials, _groups)
 //   kernels.py:437-447       (exact_attention = repair with no prediction)
 //
-// One CTA (kNW warps) per (request, query head) row. Phases:
-//   0. the row's prediction numerators [SC, D] start streaming into shared
-//      memory (one bulk copy) while
-//   1. the set difference A vs P is taken through shared-memory bitmaps over
-//      block IDs: hit / miss / high / wrong-low flags, the optional
-//      extra-mass budget (EPS), and the job queue = misses in A order, then
-//      wrong-low blocks in P order;
-//   2. every warp starts the bulk copy of its first queued block, then all
-//      threads merge the retained prediction states (weights precomputed,
-//      threads over dims), then warps reduce their queued blocks: misses are
-//      added (+) to a per-warp LSE state, wrong-low blocks are subtracted (-)
-//      from the low group in its own exponent frame;
-//   3. per-warp states merge in a fixed order; the variant's guards (remaining
-//      low mass, cancellation envelope, non-finite output) are evaluated;
-//   4. a flagged row recomputes the strict selected set in the same launch.
-#include "internal.cuh"
+// One thread-block cluster of CS CTAs (kNW warps each, CS <= 8 chosen on the
+// host) serves one (request, query head) row. Phases:
+//   1. every CTA of the cluster takes the row's set difference A vs P through
+//      shared-memory bitmaps over block IDs — hit / miss / high / wrong-low
+//      flags, the optional extra-mass budget (EPS) and the job queue (misses
+//      in A order, then wrong-low blocks in P order) — so every CTA holds the
+//      same queue without talking to the others;
+//   2. CTA c takes queue entries c, c + CS, c + 2 CS, ...: it asks L2 for all
+//      of their blocks at once (cp.async.bulk.prefetch.L2), then each warp
+//      streams its entries through a private shared-memory stage with bulk
+//      copies and reduces them — misses are added (+) to a per-warp LSE
+//      state, wrong-low blocks subtracted (-) from the low group in its own
+//      exponent frame — while the CTA's threads merge retained prediction
+//      slots c, c + CS, ... (weights relative to the row's retained maximum);
+//   3. per-warp states merge into one CTA partial; after a cluster barrier
+//      every CTA reads all CS partials through distributed shared memory in
+//      rank order, so every CTA holds bit-identical row totals and takes the
+//      same guard decision (remaining low mass, cancellation envelope,
+//      non-finite output); rank 0 writes the outputs;
+//   4. a flagged row recomputes the strict selected set across the cluster,
+//      in this launch.
+// Waits on bulk copies are bounded; a warp whose wait ran out records the
+// status, stops issuing work and its CTA still takes part in every cluster
+// barrier.
+#include <cooperative_groups.h>
+
+#include "block_state.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace stk {
 
-constexpr int kNW = 8;  // warps per CTA
+constexpr int kNW = 4;          // warps per CTA
+constexpr int kMaxCluster = 8;  // CTAs per row (portable cluster size)
+
+#ifdef STK_TRACE
+// [cta][8] timeline of the repair kernel (profiling builds only).
+static __device__ unsigned long long g_repair_trace[4096 * 8];
+extern "C" __attribute__((visibility("default"))) void* stk_trace_repair() {
+  void* p = nullptr;
+  cudaGetSymbolAddress(&p, g_repair_trace);
+  return p;
+}
+#define RT(ev) do { if (blockIdx.x < 4096 && threadIdx.x == 0) STK_TRACE_AT(g_repair_trace, blockIdx.x * 8 + (ev)); } while (0)
+#else
+#define RT(ev) ((void)0)
+#endif
 
 // Negative-job frame rules.
 enum NegRule : int { kNegPerToken = 0, kNegBlockRescale = 1 };
@@ -55,10 +82,12 @@ __device__ __forceinline__ void agg_pos_merge(float* S, float* U, int d, float m
   const float a1 = expf(M - Mn), a2 = expf(mb - Mn);
   __syncwarp();
   if (lane_contig) {
-    for (int j = 0; j < dpl; ++j) {
-      const int dd = lane * dpl + j;
-      if (dd < d) U[dd] = U[dd] * a1 + ub_lane[j] * a2;
-    }
+    // Half-warp layout: lanes 16h + i hold dims [i*dpl, (i+1)*dpl) (halves agree).
+    if (lane < 16)
+      for (int j = 0; j < dpl; ++j) {
+        const int dd = lane * dpl + j;
+        if (dd < d) U[dd] = U[dd] * a1 + ub_lane[j] * a2;
+      }
   } else {
     for (int j = 0, dd = lane; dd < d; ++j, dd += 32) U[dd] = U[dd] * a1 + ub_lane[j] * a2;
   }
@@ -71,31 +100,34 @@ __device__ __forceinline__ void agg_pos_merge(float* S, float* U, int d, float m
 }
 
 struct RepairSmem {
-  float* pu;      // [sc, d] staged prediction numerators (or null)
   float* pw;      // [sc] retained weights exp(pm - M_keep) (0 when not kept)
   unsigned* bitA;
   unsigned* bitP;
   long long* a_ids;
   long long* p_ids;
   int* queue;
-  float* aggU;    // [kNW + 1][d]: per-warp positive numerators, then the retained aggregate
+  float* aggU;    // [kNW + 1][d]: per-warp positive numerators, then the retained share
   float* aggN;    // [kNW][d]: per-warp negative numerators (low frame)
   float* aggS;    // [kNW + 1][4]: M, Z, Zneg, -
-  float* vecA;
-  float* vecB;
+  float* vecA;    // [d] CTA partial: positive numerator (read by the cluster)
+  float* vecB;    // [d] CTA partial: negative numerator (read by the cluster)
+  float* cS;      // [4] CTA partial scalars: M, Z, Zneg, - (read by the cluster)
+  float* gU;      // [d] row total positive numerator
+  float* gN;      // [d] row total negative numerator
   float* pm_s;    // [sc] retained maxima
   float* pl_s;    // [sc] retained normalisers
   float* mm_s;    // [sp] keep_mass maxima (budget)
   float* ml_s;    // [sp] keep_mass normalisers (budget)
   float* lu_s;    // [d] low-group numerator
   float* la_s;    // [d] low-group absolute envelope
+  float* qv;      // [d] q as FP32
   unsigned char* high_s;  // [sp]
   unsigned char* a_miss;
   unsigned char* p_flag;  // bit0 hit, bit1 high, bit2 wrong
   unsigned char* keep;
 };
 
-template <int DPL, int NST, typename T>
+template <int DPH, int NST, typename T>
 __host__ __device__ inline size_t repair_layout(const RepairArgs& a, RepairSmem* S, unsigned char* base) {
   const int D = a.d;
   size_t off = 0;
@@ -105,9 +137,8 @@ __host__ __device__ inline size_t repair_layout(const RepairArgs& a, RepairSmem*
     off += bytes;
     return at;
   };
-  const size_t stages = DPL > 0 ? static_cast<size_t>(kNW) * NST * 2 * 32 * D * sizeof(T) : 0;
+  const size_t stages = DPH > 0 ? static_cast<size_t>(kNW) * NST * 2 * 32 * D * sizeof(T) : 0;
   take(stages, 128);
-  const size_t pu_at = a.stage_pred ? take(static_cast<size_t>(a.sc) * D * 4, 128) : 0;
   const size_t pw_at = take(static_cast<size_t>(a.sc) * 4, 16);
   const int nwords = (a.max_n + 31) / 32;
   const size_t ba = take(nwords * 4, 16), bp = take(nwords * 4, 16);
@@ -116,14 +147,14 @@ __host__ __device__ inline size_t repair_layout(const RepairArgs& a, RepairSmem*
   const size_t au = take(static_cast<size_t>(kNW + 1) * D * 4, 16);
   const size_t an = take(static_cast<size_t>(kNW) * D * 4, 16);
   const size_t as = take(static_cast<size_t>(kNW + 1) * 16, 16);
-  const size_t va = take(D * 4, 16), vb = take(D * 4, 16);
+  const size_t va = take(D * 4, 16), vb = take(D * 4, 16), cs = take(16, 16);
+  const size_t gu = take(D * 4, 16), gn = take(D * 4, 16);
   const size_t pms = take(static_cast<size_t>(a.sc) * 4, 16), pls = take(static_cast<size_t>(a.sc) * 4, 16);
   const size_t mms = take(static_cast<size_t>(a.sp) * 4, 16), mls = take(static_cast<size_t>(a.sp) * 4, 16);
-  const size_t lus = take(D * 4, 16), las = take(D * 4, 16);
+  const size_t lus = take(D * 4, 16), las = take(D * 4, 16), qs = take(D * 4, 16);
   const size_t hs = take(a.sp, 1);
   const size_t am = take(a.sa, 1), pf = take(a.sp, 1), kp = take(a.sc, 1);
   if (S != nullptr) {
-    S->pu = a.stage_pred ? reinterpret_cast<float*>(base + pu_at) : nullptr;
     S->pw = reinterpret_cast<float*>(base + pw_at);
     S->bitA = reinterpret_cast<unsigned*>(base + ba);
     S->bitP = reinterpret_cast<unsigned*>(base + bp);
@@ -135,12 +166,16 @@ __host__ __device__ inline size_t repair_layout(const RepairArgs& a, RepairSmem*
     S->aggS = reinterpret_cast<float*>(base + as);
     S->vecA = reinterpret_cast<float*>(base + va);
     S->vecB = reinterpret_cast<float*>(base + vb);
+    S->cS = reinterpret_cast<float*>(base + cs);
+    S->gU = reinterpret_cast<float*>(base + gu);
+    S->gN = reinterpret_cast<float*>(base + gn);
     S->pm_s = reinterpret_cast<float*>(base + pms);
     S->pl_s = reinterpret_cast<float*>(base + pls);
     S->mm_s = reinterpret_cast<float*>(base + mms);
     S->ml_s = reinterpret_cast<float*>(base + mls);
     S->lu_s = reinterpret_cast<float*>(base + lus);
     S->la_s = reinterpret_cast<float*>(base + las);
+    S->qv = reinterpret_cast<float*>(base + qs);
     S->high_s = base + hs;
     S->a_miss = base + am;
     S->p_flag = base + pf;
@@ -151,43 +186,42 @@ __host__ __device__ inline size_t repair_layout(const RepairArgs& a, RepairSmem*
 
 // ------------------------------------------------------------------ kernel
 
-template <typename T, int DPL, int NST>
+template <typename T, int DPH, int NST, bool FULL32>
 __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ uint64_t bars[kNW * NST];
-  __shared__ uint64_t pbar;
   __shared__ RowScalars rs;
   __shared__ int sh_count[4];
   __shared__ float sh_f[8];
+  __shared__ int sh_failed;
 
-  constexpr bool kFast = DPL > 0;
-  const int D = kFast ? 32 * DPL : a.d;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int CS = static_cast<int>(cluster.num_blocks());
+  const int rank = static_cast<int>(cluster.block_rank());
+
+  constexpr bool kFast = DPH > 0;
+  const int D = kFast ? 16 * DPH : a.d;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int row = blockIdx.x;
+  const int row = blockIdx.x / CS;
   const int r = row / a.hq;
   const int kv = (row - r * a.hq) / a.g;
   const int nblocks = request_blocks(a.L, r);
   const bool hybrid = a.pmode == kPredHybrid || a.pmode == kPredCompact;
   const bool has_pred = a.pmode != kPredNone;
 
+  RT(0);
   RepairSmem S;
-  repair_layout<DPL, NST, T>(a, &S, smem);
+  repair_layout<DPH, NST, T>(a, &S, smem);
   T* stages = reinterpret_cast<T*>(smem);
   const int nwords = (a.max_n + 31) / 32;
 
-  // ---- phase 0: barriers; stream the row's prediction numerators in.
+  // ---- phase 0: barriers.
   if (lane == 0) {
     if (kFast)
       for (int st = 0; st < NST; ++st) mbar_init(&bars[warp * NST + st], 1);
-    if (warp == 0) mbar_init(&pbar, 1);
     fence_barrier_init();
   }
-  __syncthreads();
-  if (tid == 0 && a.stage_pred) {
-    const unsigned bytes = static_cast<unsigned>(a.sc) * D * 4;
-    mbar_arrive_expect_tx(&pbar, bytes);
-    bulk_g2s(S.pu, a.pu + static_cast<long long>(row) * a.sc * D, bytes, &pbar);
-  }
+  if (tid == 0) sh_failed = 0;
 
   // ---- phase 1: every per-row global load in one independent pass.
   const bool want_mass = hybrid && a.eps > 0.f && a.mass_m != nullptr;
@@ -217,7 +251,9 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
         S.la_s[dd] = a.low_abs[static_cast<long long>(row) * D + dd];
       }
   }
+  for (int dd = tid; dd < D; dd += blockDim.x) S.qv[dd] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + dd);
   __syncthreads();
+  RT(1);
   for (int i = tid; i < a.sa; i += blockDim.x) {
     long long id = S.a_ids[i];
     if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); id = -1; S.a_ids[i] = -1; }
@@ -259,7 +295,7 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
   __syncthreads();
 
   // ---- phase 1b (warp 0): counts, low_hit, extra-mass budget, queue;
-  //      (warp 1): retained-state weights.
+  //      (warp 1): retained-state weights and this CTA's share of their mass.
   if (warp == 0) {
     int low_hit = 0;
     if (hybrid) {
@@ -327,7 +363,8 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
       rs.lm = lm;
     }
   } else if (warp == 1 && has_pred) {
-    // Retained aggregate scalars: M = max kept m, Z = sum exp(m - M) l, weights.
+    // Retained weights relative to the row's retained maximum M (the same in
+    // every CTA); this CTA's share of Z covers slots rank, rank + CS, ...
     float M = neg_inf();
     for (int c = lane; c < a.sc; c += 32) M = fmaxf(M, S.pw[c]);
     M = warp_max(M);
@@ -335,7 +372,7 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
     for (int c = lane; c < a.sc; c += 32) {
       const float w = S.keep[c] ? expf(S.pw[c] - M) : 0.f;
       S.pw[c] = w;
-      if (S.keep[c]) Z += w * S.pl_s[c];
+      if (S.keep[c] && c % CS == rank) Z += w * S.pl_s[c];
     }
     Z = warp_sum(Z);
     if (lane == 0) {
@@ -367,26 +404,24 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
   float* myN = S.aggN + warp * D;
   float* myS = S.aggS + warp * 4;
 
-  constexpr int kQ = kFast ? DPL : 1;
+  constexpr int kQ = kFast ? DPH : 1;
   float qf[kQ];
   if constexpr (kFast) {
 #pragma unroll
-    for (int j = 0; j < DPL; ++j) qf[j] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + lane * DPL + j);
-  }
-  if constexpr (!kFast) {
-    // The generic path keeps q in vecB while blocks are processed.
-    for (int dd = tid; dd < D; dd += blockDim.x) S.vecB[dd] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + dd);
-    __syncthreads();
+    for (int j = 0; j < DPH; ++j) qf[j] = S.qv[(lane & 15) * DPH + j];
   }
 
-  // ---- per-warp block pipeline (fast path): items = (queue entry, chunk)
+  // ---- per-warp block pipeline. Queue entry k belongs to CTA k % CS and,
+  // within it, to warp (k / CS) % kNW; items = (entry, 32-token chunk).
+  const int kfirst = rank + CS * warp, kstep = CS * kNW;
   unsigned phase_bits = 0;
   const int nchunks = (a.L.b + 31) / 32;
-  constexpr int kChunkElems = 32 * 32 * (DPL > 0 ? DPL : 1);
+  constexpr int kChunkElems = 32 * 16 * (DPH > 0 ? DPH : 1);
   T* wst = stages + static_cast<size_t>(warp) * NST * (2 * kChunkElems);
   uint64_t* wbar = bars + warp * NST;
-  int ik = warp, ic = 0;  // issue cursor
+  int ik = kfirst, ic = 0;  // issue cursor
   bool fallback_pass = false;
+  bool warp_failed = false;
   int count = 0;
   auto job_entry = [&](int k, long long& bid, bool& negative) {
     const int e = fallback_pass ? k : S.queue[k];
@@ -424,16 +459,28 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
     }
     if (++ic == nchunks) {
       ic = 0;
-      ik += kNW;
-      while (ik < count && !job_valid(ik)) ik += kNW;
+      ik += kstep;
+      while (ik < count && !job_valid(ik)) ik += kstep;
     }
   };
+  // Start a pass over `cnt` entries: every thread asks L2 for one of this
+  // CTA's blocks, then each warp issues its first chunk copies.
   auto prefill = [&](int cnt, bool fb) {
     fallback_pass = fb;
     count = cnt;
-    ik = warp;
+    if constexpr (kFast) {
+      for (int i = tid;; i += blockDim.x) {
+        const int k = rank + CS * i;
+        if (k >= cnt) break;
+        if (!job_valid(k)) continue;
+        long long bid; bool neg;
+        job_entry(k, bid, neg);
+        prefetch_block<T>(a.L, r, kv, bid, true);
+      }
+    }
+    ik = kfirst;
     ic = 0;
-    while (ik < count && !job_valid(ik)) ik += kNW;
+    while (ik < count && !job_valid(ik)) ik += kstep;
     if constexpr (kFast) {
       for (int st = 0; st < NST; ++st) issue(st);
       __syncwarp();
@@ -443,80 +490,50 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
   auto consume = [&]() {
     if constexpr (kFast) {
       int item = 0;
-      float m, l, u[DPL];
-      for (int k = warp; k < count; k += kNW) {
+      float m, l, u[DPH], ua[DPH];
+      for (int k = kfirst; k < count; k += kstep) {
         if (!job_valid(k)) continue;
         long long bid; bool neg;
         job_entry(k, bid, neg);
         const bool per_token = neg && neg_rule == kNegPerToken;
         m = neg_inf(); l = 0.f;
 #pragma unroll
-        for (int j = 0; j < DPL; ++j) u[j] = 0.f;
+        for (int j = 0; j < DPH; ++j) { u[j] = 0.f; ua[j] = 0.f; }
         for (int c = 0; c < nchunks; ++c, ++item) {
           const int st = item % NST;
           if (!mbar_wait(&wbar[st], (phase_bits >> st) & 1u, a.status)) return false;
           phase_bits ^= 1u << st;
           const int t0 = c * 32, ntok = min(32, a.L.b - t0);
           const T* ks = wst + static_cast<size_t>(st) * 2 * kChunkElems;
-          const T* vs = ks + kChunkElems;
-          float p[32];
-#pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            p[t] = 0.f;
-            if (t < ntok) {
-              float kk[DPL];
-              load_vec<T, DPL>(ks + t * D + lane * DPL, kk);
-              float acc = 0.f;
-#pragma unroll
-              for (int j = 0; j < DPL; ++j) acc = fmaf(kk[j], qf[j], acc);
-              p[t] = acc;
-            }
-          }
-          transpose_reduce32(p, lane);
-          const float s = lane < ntok ? p[0] * a.scale : neg_inf();
-          float w;
-          if (per_token) {
-            w = lane < ntok ? expf(s - lm) : 0.f;
-            l += warp_sum(w);
-          } else {
-            const float mn = fmaxf(m, warp_max(s));
-            const float al = expf(m - mn);
-            w = lane < ntok ? expf(s - mn) : 0.f;
-            l = l * al + warp_sum(w);
-            m = mn;
-#pragma unroll
-            for (int j = 0; j < DPL; ++j) u[j] *= al;
-          }
-#pragma unroll 4
-          for (int t = 0; t < ntok; ++t) {
-            const float wt = __shfl_sync(kFull, w, t);
-            float vv[DPL];
-            load_vec<T, DPL>(vs + t * D + lane * DPL, vv);
-#pragma unroll
-            for (int j = 0; j < DPL; ++j) u[j] += wt * vv[j];
-          }
+          if (per_token)
+            warp_block_state<T, DPH, kModeFixed, FULL32>(ks, ks + kChunkElems, ntok, qf, a.scale, lm, m, l, u, ua, lane);
+          else
+            warp_block_state<T, DPH, kModeFull, FULL32>(ks, ks + kChunkElems, ntok, qf, a.scale, 0.f, m, l, u, ua, lane);
+          (void)t0;
           __syncwarp();
           issue(st);
         }
         if (!neg) {
-          agg_pos_merge(myS, myU, D, m, l, u, DPL, lane, true);
+          agg_pos_merge(myS, myU, D, m, l, u, DPH, lane, true);
         } else {
           const float f = per_token ? 1.f : expf(m - lm);
+          if (lane < 16) {
 #pragma unroll
-          for (int j = 0; j < DPL; ++j) myN[lane * DPL + j] += u[j] * f;
+            for (int j = 0; j < DPH; ++j) myN[lane * DPH + j] += u[j] * f;
+          }
           __syncwarp();
           if (lane == 0) myS[2] += l * f;
           __syncwarp();
         }
       }
     } else {
-      // Generic: lane = token for QK (q from vecB), lane = dim for PV.
+      // Generic: lane = token for QK (q from qv), lane = dim for PV.
       const T* K = static_cast<const T*>(a.L.k);
       const T* V = static_cast<const T*>(a.L.v);
       __shared__ float gw[kNW][32];
       __shared__ long long go[kNW][32];
       const int per = (D + 31) / 32;
-      for (int k = warp; k < count; k += kNW) {
+      for (int k = kfirst; k < count; k += kstep) {
         if (!job_valid(k)) continue;
         long long bid; bool neg;
         job_entry(k, bid, neg);
@@ -533,7 +550,7 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
             if (a.L.page_table != nullptr) { seg = t / a.L.page_size; within = t - seg * a.L.page_size; }
             toff = block_seg(a.L, r, kv, bid, seg).elem_off + static_cast<long long>(within) * D;
             float acc = 0.f;
-            for (int dd = 0; dd < D; ++dd) acc = fmaf(to_f32(K[toff + dd]), S.vecB[dd], acc);
+            for (int dd = 0; dd < D; ++dd) acc = fmaf(to_f32(K[toff + dd]), S.qv[dd], acc);
             s = acc * a.scale;
           }
           float w, al = 1.f;
@@ -572,58 +589,96 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
     return true;
   };
 
-  // ---- phase 2: start queued block copies, merge retained states, consume blocks.
+  // Per-warp aggregates (+ the retained share) -> this CTA's partial.
+  auto cta_partial = [&](bool with_retained) {
+    const int nagg = with_retained ? kNW + 1 : kNW;
+    if (tid == 0) {
+      float M = neg_inf();
+      for (int w = 0; w < nagg; ++w) M = fmaxf(M, S.aggS[w * 4]);
+      float Z = 0.f, Zn = 0.f;
+      for (int w = 0; w < nagg; ++w) {
+        if (S.aggS[w * 4] != neg_inf()) Z += expf(S.aggS[w * 4] - M) * S.aggS[w * 4 + 1];
+        if (w < kNW) Zn += S.aggS[w * 4 + 2];
+      }
+      S.cS[0] = M;
+      S.cS[1] = Z;
+      S.cS[2] = Zn;
+      sh_f[4] = M;
+    }
+    __syncthreads();
+    const float M = sh_f[4];
+    for (int dd = tid; dd < D; dd += blockDim.x) {
+      float U = 0.f, N = 0.f;
+      for (int w = 0; w < nagg; ++w) {
+        const float Mw = S.aggS[w * 4];
+        if (Mw != neg_inf()) U += expf(Mw - M) * S.aggU[w * D + dd];
+        if (w < kNW) N += S.aggN[w * D + dd];
+      }
+      S.vecA[dd] = U;
+      S.vecB[dd] = N;
+    }
+  };
+  // Row totals from every CTA's partial, in rank order (distributed shared
+  // memory), into sh_f[0..2] and gU / gN. Ends with a cluster barrier, after
+  // which no CTA reads another's partial any more.
+  auto cluster_totals = [&]() {
+    cluster.sync();
+    if (tid == 0) {
+      float M = neg_inf();
+      for (int c = 0; c < CS; ++c) M = fmaxf(M, cluster.map_shared_rank(S.cS, c)[0]);
+      float Z = 0.f, Zn = 0.f;
+      for (int c = 0; c < CS; ++c) {
+        const float* cs = cluster.map_shared_rank(S.cS, c);
+        if (cs[0] != neg_inf()) Z += expf(cs[0] - M) * cs[1];
+        Zn += cs[2];
+      }
+      sh_f[0] = M;
+      sh_f[1] = Z;
+      sh_f[2] = Zn;
+    }
+    __syncthreads();
+    const float M = sh_f[0];
+    for (int dd = tid; dd < D; dd += blockDim.x) {
+      float U = 0.f, N = 0.f;
+      for (int c = 0; c < CS; ++c) {
+        const float Mc = cluster.map_shared_rank(S.cS, c)[0];
+        if (Mc != neg_inf()) U += expf(Mc - M) * cluster.map_shared_rank(S.vecA, c)[dd];
+        N += cluster.map_shared_rank(S.vecB, c)[dd];
+      }
+      S.gU[dd] = U;
+      S.gN[dd] = N;
+    }
+    cluster.sync();
+  };
+
+  // ---- phase 2: prefetch + first copies, retained share, then queued blocks.
+  RT(2);
   prefill(rs.queue_len, false);
+  RT(3);
   if (has_pred) {
-    if (a.stage_pred && !mbar_wait(&pbar, 0, a.status)) return;
     float* keepU = S.aggU + kNW * D;
+    const float* pu = a.pu + static_cast<long long>(row) * a.sc * D;
     for (int dd = tid; dd < D; dd += blockDim.x) {
       float acc = 0.f;
-      if (a.stage_pred) {
-        for (int c = 0; c < a.sc; ++c) {
-          const float w = S.pw[c];
-          if (w != 0.f) acc = fmaf(w, S.pu[c * D + dd], acc);
-        }
-      } else {
-        const float* pu = a.pu + static_cast<long long>(row) * a.sc * D + dd;
-        for (int c = 0; c < a.sc; ++c) {
-          const float w = S.pw[c];
-          if (w != 0.f) acc = fmaf(w, pu[static_cast<long long>(c) * D], acc);
-        }
+      for (int c = rank; c < a.sc; c += CS) {
+        const float w = S.pw[c];
+        if (w != 0.f) acc = fmaf(w, pu[static_cast<long long>(c) * D + dd], acc);
       }
       keepU[dd] = acc;
     }
   }
-  if (!consume()) return;
+  if (!consume()) warp_failed = true;
+  RT(4);
   __syncthreads();
 
-  // ---- phase 3: combine (fixed order: warps 0..kNW-1, then retained) and guards
-  if (tid == 0) {
-    float M = neg_inf();
-    for (int w = 0; w <= kNW; ++w) M = fmaxf(M, S.aggS[w * 4]);
-    float Z = 0.f, Zn = 0.f;
-    for (int w = 0; w <= kNW; ++w) {
-      if (S.aggS[w * 4] != neg_inf()) Z += expf(S.aggS[w * 4] - M) * S.aggS[w * 4 + 1];
-      if (w < kNW) Zn += S.aggS[w * 4 + 2];
-    }
-    sh_f[0] = M;
-    sh_f[1] = Z;
-    sh_f[2] = Zn;
-  }
-  __syncthreads();
-  const float Mp = sh_f[0], Zp = sh_f[1], Zn = sh_f[2];
-  for (int dd = tid; dd < D; dd += blockDim.x) {
-    float U = 0.f, N = 0.f;
-    for (int w = 0; w <= kNW; ++w) {
-      const float Mw = S.aggS[w * 4];
-      if (Mw != neg_inf()) U += expf(Mw - Mp) * S.aggU[w * D + dd];
-      if (w < kNW) N += S.aggN[w * D + dd];
-    }
-    S.vecA[dd] = U;
-    S.vecB[dd] = N;
-  }
+  // ---- phase 3: CTA partial, cluster totals, guards (identical in every CTA).
+  cta_partial(true);
+  RT(5);
+  cluster_totals();
+  RT(6);
   if (tid < 4) sh_count[tid] = 0;
   __syncthreads();
+  const float Mp = sh_f[0], Zp = sh_f[1], Zn = sh_f[2];
 
   const bool low_hit = rs.low_hit != 0;
   float fraction = 1.f;
@@ -642,12 +697,12 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
     int cancel = 0, invalid = 0;
     for (int dd = tid; dd < D; dd += blockDim.x) {
       const float lu = low_hit ? S.lu_s[dd] * lowalpha : 0.f;
-      const float ru = S.vecB[dd] * lowalpha;
+      const float ru = S.gN[dd] * lowalpha;
       const float residual = lu - ru;
       const float labs = low_hit ? S.la_s[dd] * lowalpha : 0.f;
       const float sc = labs + fabsf(ru);
       cancel |= low_hit && (fabsf(residual) < a.cancel_tol * sc) && (sc > 0.f);
-      const float o = (residual + cp * S.vecA[dd]) / fmaxf(z, 1e-30f);
+      const float o = (residual + cp * S.gU[dd]) / fmaxf(z, 1e-30f);
       invalid |= !isfinite(o);
     }
     if (cancel) atomicOr(&sh_count[0], 1);
@@ -666,8 +721,8 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
       fraction = mass / ll;
       int cancel = 0;
       for (int dd = tid; dd < D; dd += blockDim.x) {
-        const float residual = S.lu_s[dd] - S.vecB[dd];
-        const float sc = S.la_s[dd] + fabsf(S.vecB[dd]);
+        const float residual = S.lu_s[dd] - S.gN[dd];
+        const float sc = S.la_s[dd] + fabsf(S.gN[dd]);
         cancel |= (fabsf(residual) < a.cancel_tol * sc) && (sc > 0.f);
       }
       if (cancel) atomicOr(&sh_count[0], 1);
@@ -679,8 +734,8 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
     const float z = cp * Zp + lw * mass;
     int invalid = 0;
     for (int dd = tid; dd < D; dd += blockDim.x) {
-      const float resid = low_hit ? S.lu_s[dd] - S.vecB[dd] : 0.f;
-      const float o = (cp * S.vecA[dd] + lw * resid) / z;
+      const float resid = low_hit ? S.lu_s[dd] - S.gN[dd] : 0.f;
+      const float o = (cp * S.gU[dd] + lw * resid) / z;
       invalid |= !isfinite(o);
     }
     if (invalid) atomicOr(&sh_count[1], 1);
@@ -691,50 +746,37 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
     cl_scale = lw;
   } else {
     // Saved / union / exact: plain LSE merge of retained states and misses.
-    __syncthreads();
     cp = 1.f;
     cl_scale = 0.f;
     z_final = Zp;
   }
 
   if (bad) {
-    // ---- phase 4: strict fallback over A, in this launch.
-    __syncthreads();
+    // ---- phase 4: strict fallback over A, spread over the cluster (every
+    // CTA took the same decision, so every CTA reaches the same barriers).
     for (int i = tid; i < (kNW + 1) * D; i += blockDim.x) S.aggU[i] = 0.f;
-    if (lane == 0) { S.aggS[warp * 4] = neg_inf(); S.aggS[warp * 4 + 1] = 0.f; }
-    if (tid == 0) { S.aggS[kNW * 4] = neg_inf(); S.aggS[kNW * 4 + 1] = 0.f; }
-    if constexpr (!kFast) {
-      for (int dd = tid; dd < D; dd += blockDim.x) S.vecB[dd] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + dd);
+    if (lane == 0) { S.aggS[warp * 4] = neg_inf(); S.aggS[warp * 4 + 1] = 0.f; S.aggS[warp * 4 + 2] = 0.f; }
+    __syncthreads();
+    if (!warp_failed) {
+      prefill(a.sa, true);
+      if (!consume()) warp_failed = true;
     }
     __syncthreads();
-    prefill(a.sa, true);
-    if (!consume()) return;
-    __syncthreads();
-    if (tid == 0) {
-      float M = neg_inf();
-      for (int w = 0; w < kNW; ++w) M = fmaxf(M, S.aggS[w * 4]);
-      float Z = 0.f;
-      for (int w = 0; w < kNW; ++w)
-        if (S.aggS[w * 4] != neg_inf()) Z += expf(S.aggS[w * 4] - M) * S.aggS[w * 4 + 1];
-      sh_f[0] = M;
-      sh_f[1] = Z;
+    cta_partial(false);
+    cluster_totals();
+    if (rank == 0) {
+      const float Z = sh_f[1];
+      for (int dd = tid; dd < D; dd += blockDim.x) a.out[static_cast<long long>(row) * D + dd] = S.gU[dd] / Z;
     }
-    __syncthreads();
-    const float M = sh_f[0], Z = sh_f[1];
-    for (int dd = tid; dd < D; dd += blockDim.x) {
-      float U = 0.f;
-      for (int w = 0; w < kNW; ++w)
-        if (S.aggS[w * 4] != neg_inf()) U += expf(S.aggS[w * 4] - M) * S.aggU[w * D + dd];
-      a.out[static_cast<long long>(row) * D + dd] = U / Z;
-    }
-  } else {
+  } else if (rank == 0) {
     for (int dd = tid; dd < D; dd += blockDim.x) {
       float lowv = 0.f;
-      if (cl_scale != 0.f) lowv = S.lu_s[dd] - S.vecB[dd];
-      a.out[static_cast<long long>(row) * D + dd] = (cp * S.vecA[dd] + cl_scale * lowv) / z_final;
+      if (cl_scale != 0.f) lowv = S.lu_s[dd] - S.gN[dd];
+      a.out[static_cast<long long>(row) * D + dd] = (cp * S.gU[dd] + cl_scale * lowv) / z_final;
     }
   }
-  if (tid == 0) {
+  RT(7);
+  if (rank == 0 && tid == 0) {
     if (a.fallback) a.fallback[row] = bad;
     if (a.remaining) a.remaining[row] = fraction;
     if (a.approx) a.approx[row] = rs.skip && !bad;
@@ -742,27 +784,44 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
     if (a.pos_out) a.pos_out[row] = rs.miss_count;
     if (a.total_out) a.total_out[row] = rs.queue_len;
   }
+  (void)sh_failed;
 }
 
 // ------------------------------------------------------------------ host side
 
-template <typename T, int DPL>
+// CTAs per row: enough warps for the row's largest pass (A for a strict
+// fallback or exact attention, P for wrong-low blocks) at one block per warp,
+// up to the portable cluster size.
+static int repair_cluster_size(const RepairArgs& a) {
+  const int jobs = a.sa > a.sp ? a.sa : a.sp;
+  int cs = (jobs + kNW - 1) / kNW;
+  if (cs > kMaxCluster) cs = kMaxCluster;
+  if (cs < 1) cs = 1;
+  return cs;
+}
+
+template <typename T, int DPH>
 static int launch_repair_t(RepairArgs a, cudaStream_t stream) {
   constexpr int NST = 1;
-  const bool can_stage = a.pmode != kPredNone && a.d % 4 == 0 &&
-                         (reinterpret_cast<uintptr_t>(a.pu) & 15) == 0 &&
-                         static_cast<size_t>(a.sc) * a.d * 4 <= 64 * 1024;
-  a.stage_pred = can_stage ? 1 : 0;
-  size_t smem = repair_layout<DPL, NST, T>(a, nullptr, nullptr);
-  if (smem > 220 * 1024 && a.stage_pred) {
-    a.stage_pred = 0;
-    smem = repair_layout<DPL, NST, T>(a, nullptr, nullptr);
-  }
+  a.stage_pred = 0;
+  const size_t smem = repair_layout<DPH, NST, T>(a, nullptr, nullptr);
   if (smem > 220 * 1024) return -2;
-  auto kern = repair_kernel<T, DPL, NST>;
+  auto kern = a.L.b % 32 == 0 ? repair_kernel<T, DPH, NST, true> : repair_kernel<T, DPH, NST, false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  kern<<<a.rows, kNW * 32, smem, stream>>>(a);
-  return static_cast<int>(cudaGetLastError());
+  const int cs = repair_cluster_size(a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.rows) * cs, 1, 1);
+  cfg.blockDim = dim3(kNW * 32, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kern, a));
 }
 
 template <typename T>
@@ -772,8 +831,8 @@ static int launch_repair_dt(const RepairArgs& a, cudaStream_t stream) {
                        (a.L.page_table == nullptr || a.L.b % a.L.page_size == 0) && a.L.kv_request_stride % 8 == 0;
   const size_t fast_stage = static_cast<size_t>(kNW) * 2 * 32 * a.d * sizeof(T);
   if (aligned && fast_stage <= 128 * 1024) {
-    if (a.d == 64) return launch_repair_t<T, 2>(a, stream);
-    if (a.d == 128) return launch_repair_t<T, 4>(a, stream);
+    if (a.d == 64) return launch_repair_t<T, 4>(a, stream);
+    if (a.d == 128) return launch_repair_t<T, 8>(a, stream);
   }
   if (a.d > 1024) return -3;
   return launch_repair_t<T, 0>(a, stream);
@@ -781,6 +840,8 @@ static int launch_repair_dt(const RepairArgs& a, cudaStream_t stream) {
 
 int launch_repair(const RepairArgs& a, int kv_dtype, cudaStream_t stream) {
   if (a.rows == 0) return 0;
+  const int rc = launch_attend(a, kv_dtype, stream);
+  if (rc != 1) return rc;
   switch (kv_dtype) {
     case kF32: return launch_repair_dt<float>(a, stream);
     case kF16: return launch_repair_dt<__half>(a, stream);

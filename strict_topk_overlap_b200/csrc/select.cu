@@ -49,7 +49,7 @@ struct ScoreTile {
 };
 
 template <int C>
-__global__ void __launch_bounds__(kScoreThreads) score_kernel(ScoreArgs a, ScoreTile t) {
+__global__ void __launch_bounds__(kScoreThreads) score_generic_kernel(ScoreArgs a, ScoreTile t) {
   extern __shared__ __align__(16) unsigned char sm[];
   __shared__ uint64_t bar;
   __shared__ int req0;
@@ -164,6 +164,179 @@ __global__ void __launch_bounds__(kScoreThreads) score_kernel(ScoreArgs a, Score
   }
 }
 
+
+// ------------------------------------------------------------------ tiled scorer
+// The fast scorer for D = 32 * C (C = 2, 4, 8). One CTA scores kTileBlocks
+// consecutive blocks of one meta head for all G query heads of that head.
+// Each warp owns 8 blocks; lane = part * 8 + b (part 0..3, b = block in warp).
+//
+// Bit-exact restatement of the fixed order above: write p[c] for the lane-c
+// partial of the reference order (dims [cC, cC+C), sequential FP64 FMA). The
+// xor butterfly over offsets 16, 8, 4, 2, 1 is, from any lane's point of
+// view, the balanced binary tree over the leaves L_k = p[bitrev5(k)] taken in
+// order k = 0..31 (the pair at offset 16 is (L_2i, L_2i+1), at offset 8 the
+// pairs of those, ...); FP64 addition is commutative, so every lane ends with
+// the same value and so does this tree. Part j here reduces the subtree of
+// leaves k in [8j, 8j+8) with a 3-level stack, and two shuffle levels (xor 8:
+// parts 0+1, 2+3; xor 16: the halves) finish it.
+//
+// lo/hi rows are staged with one 1-D bulk copy per row into rows padded to
+// D + 4 floats, so the 8 lanes of a shared-memory phase (same part, 8
+// blocks) hit 8 different bank quads; q rows are FP64 in shared memory and
+// read as broadcasts.
+
+constexpr int kTileWarps = 4;
+constexpr int kTileBlocks = 8 * kTileWarps;
+constexpr int kTileRowGroup = 4;  // query heads reduced together per lo/hi chunk load
+
+__device__ __forceinline__ int bitrev5(int k) { return static_cast<int>(__brev(static_cast<unsigned>(k)) >> 27); }
+
+// Leaf value for a row whose request's q is not staged (tiles that span more
+// than kQReq requests, i.e. requests shorter than a tile): q from global
+// memory. Kept out of line so that the hot loop stays small.
+template <int C>
+__device__ __noinline__ double leaf_global_q(const ScoreArgs& a, long long qoff, const float* lo_c, const float* hi_c) {
+  double v = 0.0;
+  for (int e = 0; e < C; ++e) {
+    const double qv = static_cast<double>(load_any(a.q, a.q_dtype, qoff + e));
+    v = __fma_rn(qv, static_cast<double>(qv >= 0.0 ? hi_c[e] : lo_c[e]), v);
+  }
+  return v;
+}
+
+template <int C, bool G4>
+__global__ void __launch_bounds__(kTileWarps * 32) score_tiled_kernel(ScoreArgs a, int bulk) {
+  constexpr int D = 32 * C;
+  constexpr int RS = D + 4;  // padded row stride (floats)
+  extern __shared__ __align__(16) unsigned char sm[];
+  __shared__ uint64_t bar;
+  __shared__ int req0;
+  const int G = a.hq / a.hmeta;
+  const int mh = blockIdx.y;
+  const int row0 = blockIdx.x * kTileBlocks;
+  const int nrows = min(kTileBlocks, a.total_blocks - row0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* slo = reinterpret_cast<float*>(sm);
+  float* shi = slo + kTileBlocks * RS;
+  double* sq = reinterpret_cast<double*>(shi + kTileBlocks * RS);  // [kQReq][G][D]
+  double* sgrp = sq + static_cast<size_t>(kQReq) * G * D;             // [kTileBlocks] group sums
+  const long long moff = (static_cast<long long>(mh) * a.total_blocks + row0) * D;
+
+  if (tid == 0) {
+    req0 = find_request(a.block_offsets, a.R, row0);
+    if (bulk) {
+      mbar_init(&bar, 1);
+      fence_barrier_init();
+      mbar_arrive_expect_tx(&bar, static_cast<unsigned>(2 * nrows * D * 4));
+    }
+  }
+  __syncthreads();
+  if (bulk) {
+    if (warp == 0) {
+      for (int rr = lane; rr < nrows; rr += 32) {
+        bulk_g2s(slo + rr * RS, a.lo + moff + static_cast<long long>(rr) * D, D * 4, &bar);
+        bulk_g2s(shi + rr * RS, a.hi + moff + static_cast<long long>(rr) * D, D * 4, &bar);
+      }
+    }
+  } else {
+    for (int i = tid; i < nrows * D; i += blockDim.x) {
+      const int rr = i / D, dd = i - rr * D;
+      slo[rr * RS + dd] = a.lo[moff + i];
+      shi[rr * RS + dd] = a.hi[moff + i];
+    }
+  }
+  const int r0 = req0;
+  for (int i = tid; i < kQReq * G * D; i += blockDim.x) {
+    const int rr = i / (G * D), rem = i - rr * G * D;
+    const int g = rem / D, dd = rem - g * D;
+    const int r = r0 + rr;
+    sq[i] = r < a.R ? static_cast<double>(load_any(a.q, a.q_dtype, (static_cast<long long>(r) * a.hq + mh * G + g) * D + dd))
+                    : 0.0;
+  }
+  if (bulk && !mbar_wait(&bar, 0, a.status)) return;
+  __syncthreads();
+
+  const int part = lane >> 3, b = lane & 7;
+  const int rl = warp * 8 + b;  // tile row of this lane
+  const bool live = rl < nrows;
+  const int gb = row0 + rl;
+  const int rr = live ? find_request(a.block_offsets, a.R, gb) - r0 : 0;
+  const float* lr = slo + rl * RS;
+  const float* hr = shi + rl * RS;
+  double grp = 0.0;
+
+#pragma unroll 1
+  for (int g0 = 0; g0 < G; g0 += kTileRowGroup) {
+    const int ng = G4 ? kTileRowGroup : min(kTileRowGroup, G - g0);
+    double st[kTileRowGroup][3];
+    double leaf_done[kTileRowGroup];
+#pragma unroll
+    for (int kl = 0; kl < 8; ++kl) {
+      const int c = bitrev5(part * 8 + kl);
+      float lo_c[C], hi_c[C];
+#pragma unroll
+      for (int e = 0; e < C; e += (C >= 4 ? 4 : 2)) {
+        if constexpr (C >= 4) {
+          const float4 x = *reinterpret_cast<const float4*>(lr + c * C + e);
+          const float4 y = *reinterpret_cast<const float4*>(hr + c * C + e);
+          lo_c[e] = x.x; lo_c[e + 1] = x.y; lo_c[e + 2] = x.z; lo_c[e + 3] = x.w;
+          hi_c[e] = y.x; hi_c[e + 1] = y.y; hi_c[e + 2] = y.z; hi_c[e + 3] = y.w;
+        } else {
+          const float2 x = *reinterpret_cast<const float2*>(lr + c * C + e);
+          const float2 y = *reinterpret_cast<const float2*>(hr + c * C + e);
+          lo_c[e] = x.x; lo_c[e + 1] = x.y;
+          hi_c[e] = y.x; hi_c[e + 1] = y.y;
+        }
+      }
+#pragma unroll
+      for (int gi = 0; gi < kTileRowGroup; ++gi) {
+        if (G4 || gi < ng) {
+          double v = 0.0;
+          if (rr < kQReq) {
+            const double* qr = sq + (rr * G + g0 + gi) * D + c * C;
+#pragma unroll
+            for (int e = 0; e < C; ++e) {
+              const double qv = qr[e];
+              v = __fma_rn(qv, static_cast<double>(qv >= 0.0 ? hi_c[e] : lo_c[e]), v);
+            }
+          } else {
+            v = leaf_global_q<C>(a, (static_cast<long long>(r0 + rr) * a.hq + mh * G + g0 + gi) * D + c * C, lo_c,
+                                 hi_c);
+          }
+          // Balanced-tree push of leaf kl (levels resolved at compile time).
+          if ((kl & 1) == 0) {
+            st[gi][0] = v;
+          } else {
+            v = __dadd_rn(st[gi][0], v);
+            if ((kl & 2) == 0) {
+              st[gi][1] = v;
+            } else {
+              v = __dadd_rn(st[gi][1], v);
+              if ((kl & 4) == 0) st[gi][2] = v;
+              else leaf_done[gi] = __dadd_rn(st[gi][2], v);
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int gi = 0; gi < kTileRowGroup; ++gi) {
+      double v = (G4 || gi < ng) ? leaf_done[gi] : 0.0;
+      v = __dadd_rn(v, __shfl_xor_sync(kFull, v, 8));
+      v = __dadd_rn(v, __shfl_xor_sync(kFull, v, 16));
+      if ((G4 || gi < ng) && part == 0 && live) {
+        const int h = mh * G + g0 + gi;
+        if (a.scores_f32) a.scores_f32[static_cast<long long>(h) * a.total_blocks + gb] = __double2float_rn(v);
+        if (a.scores_f64 && !a.group_select) a.scores_f64[static_cast<long long>(h) * a.total_blocks + gb] = v;
+        grp = __dadd_rn(grp, v);
+      }
+    }
+  }
+  if (a.scores_f64 && a.group_select && part == 0 && live)
+    a.scores_f64[static_cast<long long>(mh) * a.total_blocks + gb] = grp;
+  (void)sgrp;
+}
+
 // ------------------------------------------------------------------ Top-K
 
 __device__ __forceinline__ unsigned long long order_key(double x) {
@@ -179,20 +352,29 @@ __device__ __forceinline__ unsigned long long warp_or64(unsigned long long x) {
 
 // Radix select over E register-resident keys per thread; thread t owns
 // positions [t*E, t*E+E). Writes the chosen positions' IDs (id_of) in
-// ascending position order.
+// ascending position order; ties (equal keys) go to the lower position.
+//
+// MSB-first 8-bit digits over the bits in which the keys differ (the common
+// prefix is skipped). Each pass builds per-warp histograms with shared-memory
+// atomics, then all threads scan the 256 bins from the top to find the bin
+// holding the K-th key; the pass loop ends as soon as that bin's keys are all
+// selected. A final block scan places every selected ID at its ascending
+// output position.
+constexpr int kSelMaxWarps = 16;
+
 template <int E, typename IdOf>
 __device__ void select_registers(const unsigned long long (&key)[E], int n, int topk, IdOf id_of, int* out,
                                  unsigned long long* keys_out) {
-  __shared__ unsigned hist[2][256];
+  __shared__ unsigned hist[kSelMaxWarps][256];
   __shared__ unsigned long long sh_or, sh_k0;
   __shared__ int sh_bin, sh_above, sh_cnt;
-  __shared__ unsigned warp_tot[32];
+  __shared__ unsigned warp_tot[kSelMaxWarps];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nw = blockDim.x >> 5;
   const int beg = tid * E;
+  const int bpt = 256 / static_cast<int>(blockDim.x) > 0 ? 256 / static_cast<int>(blockDim.x) : 1;  // bins per thread
 
   if (tid == 0) { sh_or = 0; sh_k0 = key[0]; }
-  for (int i = tid; i < 512; i += blockDim.x) (&hist[0][0])[i] = 0;
   __syncthreads();
   const unsigned long long k0 = sh_k0;
   unsigned long long diff = 0;
@@ -214,53 +396,54 @@ __device__ void select_registers(const unsigned long long (&key)[E], int n, int 
     const int hb = 63 - __clzll(diff);
     mask = (hb == 63) ? 0ull : ~((2ull << hb) - 1ull);
     prefix = k0 & mask;
-    int buf = 0;
     for (int shift = (hb / 8) * 8; shift >= 0; shift -= 8) {
+      unsigned* hw = hist[warp];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) hw[lane * 8 + i] = 0u;
+      __syncwarp();
 #pragma unroll
       for (int j = 0; j < E; ++j) {
-        // Lanes holding the same digit add once (warp-aggregated atomics).
-        const bool cand = beg + j < n && (key[j] & mask) == prefix;
-        const unsigned digit = cand ? static_cast<unsigned>((key[j] >> shift) & 0xFF) : 0xFFFFFFFFu;
-        const unsigned grp = __match_any_sync(kFull, digit);
-        if (cand && lane == __ffs(grp) - 1) atomicAdd(&hist[buf][digit], static_cast<unsigned>(__popc(grp)));
+        if (beg + j < n && (key[j] & mask) == prefix)
+          atomicAdd(&hw[static_cast<unsigned>((key[j] >> shift) & 0xFF)], 1u);
       }
       __syncthreads();
-      if (warp == 0) {
-        unsigned local[8];
-        unsigned sum = 0;
+      // Thread t scans bins 255 - t*bpt, 255 - t*bpt - 1, ... (descending).
+      unsigned local = 0;
+      for (int i = 0; i < bpt; ++i) {
+        const int bin = 255 - (tid * bpt + i);
+        if (bin >= 0)
+          for (int w = 0; w < nw; ++w) local += hist[w][bin];
+      }
+      unsigned inc = local;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) { local[j] = hist[buf][255 - (lane * 8 + j)]; sum += local[j]; }
-        unsigned inc = sum;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const unsigned y = __shfl_up_sync(kFull, inc, o);
-          if (lane >= o) inc += y;
-        }
-        const unsigned excl = inc - sum;
-        const bool crosses = excl < static_cast<unsigned>(kk) && inc >= static_cast<unsigned>(kk);
-        const unsigned who = __ballot_sync(kFull, crosses);
-        if (lane == __ffs(who) - 1) {
-          unsigned run = excl;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            if (run + local[j] >= static_cast<unsigned>(kk)) {
-              sh_bin = 255 - (lane * 8 + j);
-              sh_above = static_cast<int>(run);
-              sh_cnt = static_cast<int>(local[j]);
-              break;
-            }
-            run += local[j];
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(kFull, inc, o);
+        if (lane >= o) inc += y;
+      }
+      if (lane == 31) warp_tot[warp] = inc;
+      __syncthreads();
+      unsigned excl = inc - local;
+      for (int w = 0; w < warp; ++w) excl += warp_tot[w];
+      if (excl < static_cast<unsigned>(kk) && excl + local >= static_cast<unsigned>(kk)) {
+        unsigned run = excl;
+        for (int i = 0; i < bpt; ++i) {
+          const int bin = 255 - (tid * bpt + i);
+          unsigned c = 0;
+          for (int w = 0; w < nw; ++w) c += hist[w][bin];
+          if (run + c >= static_cast<unsigned>(kk)) {
+            sh_bin = bin;
+            sh_above = static_cast<int>(run);
+            sh_cnt = static_cast<int>(c);
+            break;
           }
+          run += c;
         }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) hist[buf ^ 1][lane * 8 + j] = 0;
       }
       __syncthreads();
       prefix |= static_cast<unsigned long long>(sh_bin) << shift;
       mask |= 0xFFull << shift;
       kk -= sh_above;
       const int cnt = sh_cnt;
-      buf ^= 1;
       if (cnt == kk) { take_all = true; break; }
     }
   }
@@ -283,20 +466,11 @@ __device__ void select_registers(const unsigned long long (&key)[E], int n, int 
     const unsigned y = __shfl_up_sync(kFull, inc, o);
     if (lane >= o) inc += y;
   }
+  __syncthreads();
   if (lane == 31) warp_tot[warp] = inc;
   __syncthreads();
-  if (warp == 0) {
-    const unsigned t = lane < nw ? warp_tot[lane] : 0u;
-    unsigned ti = t;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const unsigned y = __shfl_up_sync(kFull, ti, o);
-      if (lane >= o) ti += y;
-    }
-    if (lane < nw) warp_tot[lane] = ti - t;
-  }
-  __syncthreads();
-  const unsigned excl = inc - packed + warp_tot[warp];
+  unsigned excl = inc - packed;
+  for (int w = 0; w < warp; ++w) excl += warp_tot[w];
   unsigned gt_before = excl >> 16, eq_before = excl & 0xFFFFu;
 #pragma unroll
   for (int j = 0; j < E; ++j) {
@@ -365,22 +539,34 @@ __global__ void __launch_bounds__(512) merge_candidates_kernel(MergeArgs a) {
 
 int launch_score(const ScoreArgs& a, cudaStream_t stream) {
   const int G = a.hq / a.hmeta;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(a.lo) | reinterpret_cast<uintptr_t>(a.hi)) & 15) == 0;
+  if (a.d == 64 || a.d == 128 || a.d == 256) {
+    const int rs = a.d + 4;
+    const size_t smem = static_cast<size_t>(2) * kTileBlocks * rs * 4 + static_cast<size_t>(kQReq) * G * a.d * 8 +
+                        static_cast<size_t>(kTileBlocks) * 8;
+    if (smem <= 200 * 1024) {
+      const int tiles = (a.total_blocks + kTileBlocks - 1) / kTileBlocks;
+      dim3 grid(tiles, a.hmeta);
+      const int bulk = aligned ? 1 : 0;
+      const bool g4 = G % kTileRowGroup == 0;
+      auto kern = a.d == 64 ? (g4 ? score_tiled_kernel<2, true> : score_tiled_kernel<2, false>)
+                            : (a.d == 128 ? (g4 ? score_tiled_kernel<4, true> : score_tiled_kernel<4, false>)
+                                          : (g4 ? score_tiled_kernel<8, true> : score_tiled_kernel<8, false>));
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      kern<<<grid, kTileWarps * 32, smem, stream>>>(a, bulk);
+      return static_cast<int>(cudaGetLastError());
+    }
+  }
   ScoreTile t;
   t.tn = max(4, min(64, (128 + G - 1) / G));
-  const bool aligned = ((reinterpret_cast<uintptr_t>(a.lo) | reinterpret_cast<uintptr_t>(a.hi)) & 15) == 0;
   t.bulk = aligned && (a.d % 4 == 0);
   const int tiles = (a.total_blocks + t.tn - 1) / t.tn;
   dim3 grid(tiles, a.hmeta);
   const size_t smem = static_cast<size_t>(t.tn) * a.d * 4 * 2 + static_cast<size_t>(kQReq) * G * a.d * 8 +
                       static_cast<size_t>(t.tn) * G * 8 + static_cast<size_t>(t.tn) * 4 + 16;
   if (smem > 200 * 1024) return -1;
-  if (a.d == 128) {
-    cudaFuncSetAttribute(score_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    score_kernel<4><<<grid, kScoreThreads, smem, stream>>>(a, t);
-  } else {
-    cudaFuncSetAttribute(score_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    score_kernel<0><<<grid, kScoreThreads, smem, stream>>>(a, t);
-  }
+  cudaFuncSetAttribute(score_generic_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  score_generic_kernel<0><<<grid, kScoreThreads, smem, stream>>>(a, t);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -388,8 +574,12 @@ int launch_select(const SelectArgs& a, int max_n, cudaStream_t stream) {
   const int rows = a.R * a.hsel;
   if (max_n <= 1024) {
     select_topk_kernel<8><<<rows, 128, 0, stream>>>(a);
+  } else if (max_n <= 2048) {
+    select_topk_kernel<8><<<rows, 256, 0, stream>>>(a);
   } else if (max_n <= 4096) {
     select_topk_kernel<16><<<rows, 256, 0, stream>>>(a);
+  } else if (max_n <= 8192) {
+    select_topk_kernel<16><<<rows, 512, 0, stream>>>(a);
   } else if (max_n <= 16384) {
     select_topk_kernel<32><<<rows, 512, 0, stream>>>(a);
   } else {

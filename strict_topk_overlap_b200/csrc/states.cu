@@ -6,16 +6,13 @@
 // :384-407 (_wrong_aggregate); gqa.py:29-59 (_partial incl. REPAIR slot
 // search); gqa_hierarchical.py:22-52 (_packed_partials, per-block states).
 //
-// Design: one warp owns one (row, block) job at a time. Each warp keeps a
-// private ring of NST shared-memory stages; lane 0 streams 32-token K/V
-// chunks into them with 1-D bulk copies (cp.async.bulk) completed on a
-// per-stage mbarrier, while the whole warp reduces the previous chunk:
-//   QK : lane l owns dims [l*DPL, (l+1)*DPL); 32 token partials are reduced
-//        with one transposed butterfly, leaving token t's logit in lane t;
-//   PV : lane l accumulates its DPL output dims over the chunk's tokens.
-// Misaligned or odd shapes take a plain-load generic kernel with the same math.
+// Design: persistent CTAs whose warps each stream one (row, block) job at a
+// time through a private shared-memory stage (bulk copies on an mbarrier,
+// L2 prefetch ahead) and reduce it with half-warp 128-bit tiles (see
+// block_state.cuh); misaligned or odd shapes take a plain-load generic kernel
+// with the same math.
 
-#include "internal.cuh"
+#include "block_state.cuh"
 
 namespace stk {
 
@@ -80,275 +77,203 @@ __device__ __forceinline__ void write_inactive(const JobArgs& a, long long job, 
 }
 
 // ------------------------------------------------------------------ fast path
-// Warp-specialised: warp 0 resolves jobs and streams each active block's K/V
-// (one stage = one whole block) into shared-memory stages with 1-D bulk
-// copies; ncons consumer warps reduce them. Job j of the CTA goes to consumer
-// c = j % ncons, which owns stages [c*kps, (c+1)*kps) and takes its jobs in
-// order through them, so every stage has exactly one producer and one
-// consumer and each mbarrier advances one phase at a time (a waiter can never
-// be two phases ahead, which would alias the parity). full[s] completes when
-// a stage's bytes landed; empty[s] when its consumer is done with it.
+// Persistent CTAs, one per SM. CTA c owns the contiguous job range
+// [njobs*c/C, njobs*(c+1)/C), so consecutive jobs mostly share a row (and q).
+// Warp w of the CTA serves jobs j0 + w, j0 + w + nw, ... by itself:
+//   * 32 of its jobs at a time are resolved lane-parallel (one lane per job:
+//     row, block id, activity), so metadata costs one load round trip per 32
+//     jobs; lanes also ask L2 for the first kWarpPrefetch of those blocks
+//     (cp.async.bulk.prefetch.L2) and each later job is prefetched
+//     kWarpPrefetch jobs ahead, so DRAM sees the range's traffic early while
+//     a warp's single stage only has to cover an L2 round trip;
+//   * lane 0 streams the current job's whole K/V block into the warp's stage
+//     with bulk copies (one per page segment) on the warp's mbarrier, and the
+//     warp reduces it with half-warp 128-bit tiles (warp_block_state).
 
-constexpr int kCons = 12;
-constexpr int kWsThreads = 32 * (kCons + 1);
+constexpr int kFastMaxWarps = 16;
+constexpr int kWarpPrefetch = 3;
+constexpr int kQRowsStaged = 4;  // q rows of a CTA's range staged in shared memory up front
+// Dynamic shared memory the stages may use: the 227 KB per-block maximum
+// less this kernel's static arrays (barriers, staged q rows).
+constexpr size_t kFastStageBudget = 232448 - 4096;
 
-template <typename T, int DPL, int MODE>
-__global__ void __launch_bounds__(kWsThreads, 1) jobs_fast_kernel(JobArgs a, int kps, int ncons) {
-  constexpr int D = 32 * DPL;
+#ifdef STK_TRACE
+// [cta][warp][8] timeline of the block-state kernel (profiling builds only).
+static __device__ unsigned long long g_jobs_trace[148 * kFastMaxWarps * 8];
+extern "C" __attribute__((visibility("default"))) void* stk_trace_jobs() {
+  void* p = nullptr;
+  cudaGetSymbolAddress(&p, g_jobs_trace);
+  return p;
+}
+#define JT(ev) do { if (blockIdx.x < 148 && lane == 0) STK_TRACE_AT(g_jobs_trace, (blockIdx.x * kFastMaxWarps + warp) * 8 + (ev)); } while (0)
+#else
+#define JT(ev) ((void)0)
+#endif
+
+template <typename T, int DPH, int MODE, bool FULL32>
+__global__ void __launch_bounds__(kFastMaxWarps * 32, 1) jobs_fast_kernel(JobArgs a) {
+  constexpr int D = 16 * DPH;
   constexpr bool kWantV = MODE != kModeMass;
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  __shared__ uint64_t full_bar[64], empty_bar[64];
-  __shared__ int info_row[64], info_slot[64];
-  __shared__ long long info_bid[64];
+  __shared__ uint64_t bar[kFastMaxWarps];
+  __shared__ __align__(16) float sq[kQRowsStaged * D];
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = blockDim.x >> 5;
   const int B = a.L.b;
   const size_t stage_elems = static_cast<size_t>(B) * D * (kWantV ? 2 : 1);
-  T* stages = reinterpret_cast<T*>(smem_raw);
-  const int NS = kps * ncons;
+  T* stage = reinterpret_cast<T*>(smem_raw) + warp * stage_elems;
+  uint64_t* mb = &bar[warp];
+  const unsigned bytes = static_cast<unsigned>(B) * D * sizeof(T) * (kWantV ? 2u : 1u);
 
-  if (threadIdx.x == 0) {
-    for (int st = 0; st < NS; ++st) {
-      mbar_init(&full_bar[st], 1);
-      mbar_init(&empty_bar[st], 1);
-    }
+  const int njobs = a.rows * a.s;
+  const int j0 = static_cast<int>(static_cast<long long>(njobs) * blockIdx.x / gridDim.x);
+  const int j1 = static_cast<int>(static_cast<long long>(njobs) * (blockIdx.x + 1) / gridDim.x);
+  const int mine = j1 - j0 > warp ? (j1 - j0 - warp + nw - 1) / nw : 0;  // jobs of this warp
+  JT(0);
+  if (lane == 0) {
+    mbar_init(mb, 1);
     fence_barrier_init();
   }
-  __syncthreads();
+  // The q rows of this range are loaded before any KV traffic is queued
+  // (a load issued behind the range's bulk traffic waits for all of it).
+  const int row_first = j1 > j0 ? j0 / a.s : 0;
+  const int nq = j1 > j0 ? min(kQRowsStaged, (j1 - 1) / a.s - row_first + 1) : 0;
+  for (int i = threadIdx.x; i < nq * D; i += blockDim.x)
+    sq[i] = load_any(a.q, a.q_dtype, static_cast<long long>(row_first) * D + i);
 
-  const long long njobs = static_cast<long long>(a.rows) * a.s;
-  if (warp == 0) {
-    // ---------------- producer
-    long long item = 0;  // CTA-local job index
-    const T* K = static_cast<const T*>(a.L.k);
-    const T* V = static_cast<const T*>(a.L.v);
-    const unsigned bytes = static_cast<unsigned>(B) * D * sizeof(T);
-    // Item -> (consumer, its local index, stage, phase).
-    auto stage_of = [&](long long it, long long& jc) {
-      const int c = static_cast<int>(it % ncons);
-      jc = it / ncons;
-      return c * kps + static_cast<int>(jc % kps);
-    };
-    auto acquire = [&](int st, long long jc) -> bool {
-      if (jc >= kps) return mbar_wait(&empty_bar[st], static_cast<unsigned>((jc / kps - 1) & 1), a.status);
-      return true;
-    };
-    auto issue_job = [&](int row, int slot, long long bid) -> bool {
-      long long jc;
-      const int st = stage_of(item, jc);
-      if (!acquire(st, jc)) return false;
-      if (lane == 0) {
-        info_row[st] = row;
-        info_slot[st] = slot;
-        info_bid[st] = bid;
-        const int r = row / a.hq;
-        const int kv = (row - r * a.hq) / a.g;
-        T* ks = stages + st * stage_elems;
-        T* vs = ks + static_cast<size_t>(B) * D;
-        mbar_arrive_expect_tx(&full_bar[st], kWantV ? 2 * bytes : bytes);
-        const int nseg = block_nseg(a.L);
-        for (int sg = 0; sg < nseg; ++sg) {
-          const BlockSeg seg = block_seg(a.L, r, kv, bid, sg);
-          const unsigned sb = static_cast<unsigned>(seg.tokens) * D * sizeof(T);
-          const size_t dst = static_cast<size_t>(sg) * seg.tokens * D;
-          bulk_g2s(ks + dst, K + seg.elem_off, sb, &full_bar[st]);
-          if (kWantV) bulk_g2s(vs + dst, V + seg.elem_off, sb, &full_bar[st]);
-        }
+  // Lane-parallel resolution of this warp's jobs [base, base + 32).
+  long long lb = -1;  // lane's block id, -1 when inactive
+  int lrow = 0;
+  auto resolve = [&](int base) {
+    const int k = base + lane;
+    lb = -1;
+    lrow = 0;
+    if (k < mine) {
+      const int job = j0 + warp + k * nw;
+      const int row = job / a.s;
+      lrow = row;
+      long long bid = load_id(a.ids, a.ids64, job);
+      bool act = bid >= 0;
+      if (a.active_mode == 1) act = act && ((a.active[row] != 0) != (a.active_invert != 0));
+      else if (a.active_mode == 2) act = act && ((a.active[job] != 0) != (a.active_invert != 0));
+      else if (a.active_invert) act = false;
+      if (act && bid >= request_blocks(a.L, row / a.hq)) {
+        report(a.status, kStatusBadBlockId);
+        act = false;
       }
-      __syncwarp();
-      ++item;
-      return true;
-    };
-    if (a.pred != nullptr) {
-      // Slot search in pred: resolve one job at a time with the whole warp.
-      for (long long job = blockIdx.x; job < njobs; job += gridDim.x) {
-        const JobInfo ji = resolve_job(a, job, lane);
-        if (!ji.active) { write_inactive(a, job, lane); continue; }
-        if (!issue_job(ji.row, ji.slot, ji.bid)) return;
+      lb = act ? bid : -1;
+    }
+  };
+  auto issue = [&](long long bid, int row) {
+    const int r = row / a.hq;
+    mbar_arrive_expect_tx(mb, bytes);
+    issue_block_copy<T>(a.L, r, (row - r * a.hq) / a.g, bid, stage, kWantV, mb);
+  };
+  auto prefetch_lane = [&]() {
+    if (lb >= 0) {
+      const int r = lrow / a.hq;
+      prefetch_block<T>(a.L, r, (lrow - r * a.hq) / a.g, lb, kWantV);
+    }
+  };
+
+  int base = 0;
+  resolve(0);
+  __syncthreads();  // q rows staged
+  // First copy as early as possible, then the L2 window.
+  long long cb = __shfl_sync(kFull, lb, 0);
+  int crow = __shfl_sync(kFull, lrow, 0);
+  if (mine > 0 && cb >= 0 && lane == 0) issue(cb, crow);
+  if (lane >= 1 && lane < kWarpPrefetch) prefetch_lane();
+  JT(1);
+
+  unsigned phase = 0;
+  float qf[DPH];
+  int q_row = -1;
+  int it = 0;
+#pragma unroll 1
+  for (int k = 0; k < mine; ++k) {
+    const int job = j0 + warp + k * nw;
+    // Metadata of job k + 1 (next batch when k + 1 crosses it).
+    if (k + 1 - base == 32) {
+      base += 32;
+      resolve(base);
+      if (lane < kWarpPrefetch) prefetch_lane();
+    }
+    const int nsrc = (k + 1 - base) & 31;
+    const long long nb = __shfl_sync(kFull, lb, nsrc);
+    const int nrow = __shfl_sync(kFull, lrow, nsrc);
+    const bool has_next = k + 1 < mine;
+    // Keep the L2 window kWarpPrefetch jobs ahead.
+    if (k + kWarpPrefetch < mine && k + kWarpPrefetch - base < 32 && k + kWarpPrefetch - base >= kWarpPrefetch &&
+        lane == k + kWarpPrefetch - base)
+      prefetch_lane();
+    if (cb < 0) {
+      // Inactive slot: (-inf, 0, 0) as the reference writes; repair scratch keeps no state.
+      if (a.pred == nullptr) {
+        if (MODE != kModeFixed) {
+          if (lane == 0) { a.m[job] = neg_inf(); a.l[job] = 0.f; }
+          if (MODE == kModeFull && lane < 16) {
+            float z[DPH];
+#pragma unroll
+            for (int j = 0; j < DPH; ++j) z[j] = 0.f;
+            store_vec<DPH>(a.u + static_cast<long long>(job) * D + lane * DPH, z);
+          }
+        } else {
+          if (lane == 0 && a.l) a.l[job] = 0.f;
+          if (lane < 16) {
+            float z[DPH];
+#pragma unroll
+            for (int j = 0; j < DPH; ++j) z[j] = 0.f;
+            store_vec<DPH>(a.u + static_cast<long long>(job) * D + lane * DPH, z);
+            if (a.uabs) store_vec<DPH>(a.uabs + static_cast<long long>(job) * D + lane * DPH, z);
+          }
+        }
       }
     } else {
-      // Lanes resolve up to 32 jobs at once; the active ones are then issued
-      // in job order, one per lane, in rounds of at most NS items so that no
-      // lane ever waits on a stage more than one phase ahead.
-      const long long stride = static_cast<long long>(gridDim.x);
-      for (long long g0 = blockIdx.x; g0 < njobs; g0 += 32 * stride) {
-        const long long job = g0 + lane * stride;
-        int row = 0, slot = 0;
-        long long bid = -1;
-        bool act = false;
-        if (job < njobs) {
-          row = static_cast<int>(job / a.s);
-          slot = static_cast<int>(job - static_cast<long long>(row) * a.s);
-          bid = load_id(a.ids, a.ids64, job);
-          act = true;
-          if (a.active_mode == 1) act = a.active[row] != 0;
-          else if (a.active_mode == 2) act = a.active[job] != 0;
-          if (a.active_invert) act = !act;
-          if (bid < 0) act = false;
-          if (act && bid >= request_blocks(a.L, row / a.hq)) {
-            report(a.status, kStatusBadBlockId);
-            act = false;
-          }
-          if (!act) {
-            // Inactive slot: (-inf, 0, 0) as the reference writes.
-            if (a.mode != kModeFixed) {
-              a.m[job] = neg_inf();
-              a.l[job] = 0.f;
-              if (a.mode == kModeFull)
-                for (int dd = 0; dd < D; ++dd) a.u[job * D + dd] = 0.f;
-            } else {
-              if (a.l) a.l[job] = 0.f;
-              for (int dd = 0; dd < D; ++dd) {
-                a.u[job * D + dd] = 0.f;
-                if (a.uabs) a.uabs[job * D + dd] = 0.f;
-              }
-            }
-          }
+      if (crow != q_row) {
+        q_row = crow;
+        if (crow - row_first < nq) {
+#pragma unroll
+          for (int j = 0; j < DPH; ++j) qf[j] = sq[(crow - row_first) * D + (lane & 15) * DPH + j];
+        } else {
+          load_q<DPH>(a.q, a.q_dtype, static_cast<long long>(crow) * D + (lane & 15) * DPH, qf);
         }
-        const unsigned act_mask = __ballot_sync(kFull, act);
-        const int rank = __popc(act_mask & ((1u << lane) - 1));  // order among active lanes
-        const int nact = __popc(act_mask);
-        for (int r0 = 0; r0 < nact; r0 += NS) {
-          if (act && rank >= r0 && rank < r0 + NS) {
-            const long long it = item + rank;
-            long long jc;
-            const int st = stage_of(it, jc);
-            if (acquire(st, jc)) {
-              info_row[st] = row;
-              info_slot[st] = slot;
-              info_bid[st] = bid;
-              const int r = row / a.hq;
-              const int kv = (row - r * a.hq) / a.g;
-              T* ks = stages + st * stage_elems;
-              T* vs = ks + static_cast<size_t>(B) * D;
-              mbar_arrive_expect_tx(&full_bar[st], kWantV ? 2 * bytes : bytes);
-              const int nseg = block_nseg(a.L);
-              for (int sg = 0; sg < nseg; ++sg) {
-                const BlockSeg seg = block_seg(a.L, r, kv, bid, sg);
-                const unsigned sb = static_cast<unsigned>(seg.tokens) * D * sizeof(T);
-                const size_t dst = static_cast<size_t>(sg) * seg.tokens * D;
-                bulk_g2s(ks + dst, K + seg.elem_off, sb, &full_bar[st]);
-                if (kWantV) bulk_g2s(vs + dst, V + seg.elem_off, sb, &full_bar[st]);
-              }
-            }
-          }
-          __syncwarp();
-        }
-        item += nact;
       }
-    }
-    // One end marker per consumer (ncons consecutive items cover every consumer).
-    for (int c = 0; c < ncons; ++c, ++item) {
-      long long jc;
-      const int st = stage_of(item, jc);
-      if (!acquire(st, jc)) return;
-      if (lane == 0) {
-        info_row[st] = -1;
-        mbar_arrive(&full_bar[st]);
-      }
+      const float frame = MODE == kModeFixed ? a.frame[crow] : 0.f;
+      if (it < 1) JT(2);
+      const bool ok = mbar_wait(mb, phase, a.status);
+      phase ^= 1u;
+      if (it < 2) JT(3 + 3 * it);
+      if (!ok) return;  // the copy may still be landing: leave this CTA's stage alone
+      float m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
+#pragma unroll
+      for (int j = 0; j < DPH; ++j) { u[j] = 0.f; ua[j] = 0.f; }
+      warp_block_state<T, DPH, MODE, FULL32>(stage, stage + static_cast<size_t>(B) * D, B, qf, a.scale, frame, m, l, u, ua,
+                                     lane);
       __syncwarp();
-    }
-    return;
-  }
-
-  // ---------------- consumers
-  const int cw = warp - 1;
-  if (cw >= ncons) return;
-  float qf[DPL];
-  int q_row = -1;
-#pragma unroll 1
-  for (long long jc = 0;; ++jc) {
-    const int st = cw * kps + static_cast<int>(jc % kps);
-    if (!mbar_wait(&full_bar[st], static_cast<unsigned>((jc / kps) & 1), a.status)) return;
-    const int row = info_row[st];
-    if (row < 0) {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty_bar[st]);
-      break;
-    }
-    const int slot = info_slot[st];
-    if (row != q_row) {
-      q_row = row;
-#pragma unroll
-      for (int j = 0; j < DPL; ++j) qf[j] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + lane * DPL + j);
-    }
-    const float frame = MODE == kModeFixed ? a.frame[row] : 0.f;
-    const T* kst = stages + st * stage_elems;
-    const T* vst = kst + static_cast<size_t>(B) * D;
-    float m = neg_inf(), l = 0.f;
-    float u[DPL], ua[DPL];
-#pragma unroll
-    for (int j = 0; j < DPL; ++j) { u[j] = 0.f; ua[j] = 0.f; }
-    for (int t0 = 0; t0 < B; t0 += 32) {
-      const int ntok = min(32, B - t0);
-      const T* ks = kst + static_cast<size_t>(t0) * D;
-      const T* vs = vst + static_cast<size_t>(t0) * D;
-      float p[32];
-#pragma unroll
-      for (int t = 0; t < 32; ++t) {
-        p[t] = 0.f;
-        if (t < ntok) {
-          float kv[DPL];
-          load_vec<T, DPL>(ks + t * D + lane * DPL, kv);
-          float acc = 0.f;
-#pragma unroll
-          for (int j = 0; j < DPL; ++j) acc = fmaf(kv[j], qf[j], acc);
-          p[t] = acc;
-        }
+      if (it == 0) JT(5);
+      // The stage is free: start the next job's copy before writing results.
+      if (has_next && nb >= 0 && lane == 0) issue(nb, nrow);
+      if (MODE != kModeFixed) {
+        if (lane == 0) { a.m[job] = m; a.l[job] = l; }
+      } else if (lane == 0 && a.l) {
+        a.l[job] = l;
       }
-      transpose_reduce32(p, lane);
-      const float s = lane < ntok ? p[0] * a.scale : neg_inf();
-      float w;
-      if (MODE == kModeFixed) {
-        w = lane < ntok ? expf(s - frame) : 0.f;
-        l += warp_sum(w);
-      } else {
-        const float mn = fmaxf(m, warp_max(s));
-        const float alpha = expf(m - mn);
-        w = lane < ntok ? expf(s - mn) : 0.f;
-        l = l * alpha + warp_sum(w);
-        m = mn;
-        if (kWantV) {
-#pragma unroll
-          for (int j = 0; j < DPL; ++j) u[j] *= alpha;
-        }
+      if (kWantV && lane < 16) {
+        store_vec<DPH>(a.u + static_cast<long long>(job) * D + lane * DPH, u);
+        if (MODE == kModeFixed && a.uabs) store_vec<DPH>(a.uabs + static_cast<long long>(job) * D + lane * DPH, ua);
       }
-      if (kWantV) {
-#pragma unroll 4
-        for (int t = 0; t < ntok; ++t) {
-          const float wt = __shfl_sync(kFull, w, t);
-          float vv[DPL];
-          load_vec<T, DPL>(vs + t * D + lane * DPL, vv);
-#pragma unroll
-          for (int j = 0; j < DPL; ++j) {
-            const float prod = wt * vv[j];
-            u[j] += prod;
-            if (MODE == kModeFixed) ua[j] += fabsf(prod);
-          }
-        }
-      }
+      if (it < 2) JT(4 + 3 * it);
+      ++it;
+      cb = nb;
+      crow = nrow;
+      continue;
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[st]);
-    const long long job = static_cast<long long>(row) * a.s + slot;
-    if (MODE != kModeFixed) {
-      if (lane == 0) { a.m[job] = m; a.l[job] = l; }
-    } else if (lane == 0 && a.l) {
-      a.l[job] = l;
-    }
-    if (kWantV) {
-      if constexpr (DPL == 4) {
-        *reinterpret_cast<float4*>(a.u + job * D + lane * 4) = make_float4(u[0], u[1], u[2], u[3]);
-        if (MODE == kModeFixed && a.uabs)
-          *reinterpret_cast<float4*>(a.uabs + job * D + lane * 4) = make_float4(ua[0], ua[1], ua[2], ua[3]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) {
-          a.u[job * D + lane * DPL + j] = u[j];
-          if (MODE == kModeFixed && a.uabs) a.uabs[job * D + lane * DPL + j] = ua[j];
-        }
-      }
-    }
+    // Inactive current job: the next copy has not been issued yet.
+    if (has_next && nb >= 0 && lane == 0) issue(nb, nrow);
+    cb = nb;
+    crow = nrow;
   }
 }
 
@@ -597,6 +522,8 @@ static size_t ws_stage_bytes(const JobArgs& a, int elem) {
 
 static bool fast_eligible(const JobArgs& a, int elem) {
   if (a.d != 64 && a.d != 128 && a.d != 256) return false;
+  if (a.pred != nullptr) return false;  // slot search: generic kernel
+  if (static_cast<long long>(a.rows) * a.s > 0x7fffffffll) return false;
   // At least four whole-block stages must fit the shared-memory plan.
   if (4 * ws_stage_bytes(a, elem) > 200 * 1024) return false;
   const uintptr_t pk = reinterpret_cast<uintptr_t>(a.L.k), pv = reinterpret_cast<uintptr_t>(a.L.v);
@@ -607,30 +534,29 @@ static bool fast_eligible(const JobArgs& a, int elem) {
   return true;
 }
 
-template <typename T, int DPL, int MODE>
+template <typename T, int DPH, int MODE>
 static int launch_fast_t(const JobArgs& a, int num_sms, cudaStream_t stream) {
   const size_t stage = ws_stage_bytes(a, sizeof(T));
-  const size_t cap = (200 * 1024) / stage;
-  const int nst = static_cast<int>(cap < 64 ? cap : 64);
-  const int ncons = nst < kCons ? nst : kCons;   // every consumer owns >= 1 stage
-  const int kps = nst / ncons;                   // stages per consumer
-  const size_t smem = stage * kps * ncons;
-  auto kern = jobs_fast_kernel<T, DPL, MODE>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  size_t nw = kFastStageBudget / stage;
+  if (nw > kFastMaxWarps) nw = kFastMaxWarps;
   const long long njobs = static_cast<long long>(a.rows) * a.s;
-  long long ctas = (njobs + ncons - 1) / ncons;
-  if (ctas > num_sms) ctas = num_sms;
+  long long ctas = num_sms;
+  // Small problems: fewer CTAs so that no warp is left without a job.
+  if (njobs < static_cast<long long>(num_sms) * static_cast<long long>(nw)) ctas = (njobs + nw - 1) / nw;
   if (ctas < 1) ctas = 1;
-  kern<<<static_cast<unsigned>(ctas), kWsThreads, smem, stream>>>(a, kps, ncons);
+  const size_t smem = stage * nw;
+  auto kern = a.L.b % 32 == 0 ? jobs_fast_kernel<T, DPH, MODE, true> : jobs_fast_kernel<T, DPH, MODE, false>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  kern<<<static_cast<unsigned>(ctas), static_cast<unsigned>(nw * 32), smem, stream>>>(a);
   return static_cast<int>(cudaGetLastError());
 }
 
 template <typename T, int MODE>
 static int launch_fast_d(const JobArgs& a, int num_sms, cudaStream_t stream) {
   switch (a.d) {
-    case 64: return launch_fast_t<T, 2, MODE>(a, num_sms, stream);
-    case 128: return launch_fast_t<T, 4, MODE>(a, num_sms, stream);
-    default: return launch_fast_t<T, 8, MODE>(a, num_sms, stream);
+    case 64: return launch_fast_t<T, 4, MODE>(a, num_sms, stream);
+    case 128: return launch_fast_t<T, 8, MODE>(a, num_sms, stream);
+    default: return launch_fast_t<T, 16, MODE>(a, num_sms, stream);
   }
 }
 

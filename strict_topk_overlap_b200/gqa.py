@@ -44,8 +44,11 @@ def partials(q, k, v, ids):
 
 
 def exact(q, k, v, selected):
-    """Attend to the selected blocks using parallel partials and a merge."""
-    return merge_partials(partials(q, k, v, selected))
+    """Attend to the selected blocks: per-block partials merged on chip, in one
+    launch (the reference's partials + merge, gqa.py:140-142)."""
+    _shape(q, k, v, selected)
+    out, *_ = _run_repair(q, k, v, selected, None, None, L.VAR_SAVED)
+    return out
 
 
 def select_blocks(q, lo, hi, topk):

@@ -113,8 +113,11 @@ def merge_partials(state, include=None):
 
 
 def exact_attention(q, k, v, selected):
-    """Split-block, selected-set baseline, with the same FP32 accumulation."""
-    return merge_partials(block_partials(q, k, v, selected))
+    """Split-block, selected-set baseline, with the same FP32 accumulation:
+    per-block partials merged on chip in one launch (kernels.py:445-447)."""
+    _shape(q, k, v, selected)
+    out, *_ = _run_repair(q, k, v, selected, None, None, L.VAR_SAVED)
+    return out
 
 
 def compact_capacity(s: int, mass_threshold: float) -> int:
