@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true",
                     help="short run for profiler captures: no clock window, e2e, sweep or CPU baseline")
+    ap.add_argument("--eager", action="store_true",
+                    help="launch each step's kernels directly instead of replaying a CUDA graph (for per-kernel "
+                         "profiler launch lists)")
     return ap.parse_args()
 
 
@@ -271,8 +274,10 @@ def main():
     nsets = args.sets
     sets = [make_set(args.seed + 1000 * rank + i, args.overlap, device) for i in range(nsets)]
     spec = StepSpec(topk=TOPK, method=args.method, max_extra_mass=0.0)
-    dec = [SpeculativeDecoder(s["q"], s["k"], s["v"], s["lo"], s["hi"], s["p"], spec) for s in sets]
-    ser = [SpeculativeDecoder(s["q"], s["k"], s["v"], s["lo"], s["hi"], s["p"], spec, serial=True) for s in sets]
+    graph = not args.eager
+    dec = [SpeculativeDecoder(s["q"], s["k"], s["v"], s["lo"], s["hi"], s["p"], spec, graph=graph) for s in sets]
+    ser = [SpeculativeDecoder(s["q"], s["k"], s["v"], s["lo"], s["hi"], s["p"], spec, serial=True, graph=graph)
+           for s in sets]
     # Correctness gate before timing: speculative == serial within bf16 tolerance, IDs identical.
     for d_, s_ in zip(dec, ser):
         o1 = d_.step().clone()
@@ -282,10 +287,10 @@ def main():
         assert (o1 - o2).abs().max().item() <= 2e-3, "speculative and serial outputs differ"
 
     def spec_step(i):
-        dec[i % nsets].graph.replay()
+        dec[i % nsets].step()
 
     def serial_step(i):
-        ser[i % nsets].graph.replay()
+        ser[i % nsets].step()
 
     hbm_peak, peak_kind = peaks()
     # Warm-up (untimed), then a ~1 s load window so clock samples see steady state.

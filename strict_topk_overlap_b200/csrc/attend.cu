@@ -18,8 +18,10 @@
 //      into a per-warp LSE state; the CTA also folds retained prediction
 //      slots c, c + CS, ... (saved: P slots whose ID is in A; union: all);
 //   3. each CTA pushes its partial (M, Z, U[D]) into rank 0's shared memory
-//      with distributed-shared-memory stores; after one cluster barrier rank
-//      0 merges the CS partials in rank order and writes the row's output.
+//      with distributed-shared-memory stores (after a split cluster barrier,
+//      armed at kernel start, confirms every CTA of the cluster has started);
+//      after one more cluster barrier rank 0 merges the CS partials in rank
+//      order and writes the row's output.
 // Waits on bulk copies are bounded; a warp whose wait ran out records the
 // status and stops, and its CTA still reaches the cluster barrier.
 #include <cooperative_groups.h>
@@ -33,6 +35,19 @@ namespace stk {
 constexpr int kAW = 4;           // warps per CTA
 constexpr int kAttendCluster = 8;
 
+#ifdef STK_TRACE
+// [cta][8] timeline of the attend kernel (profiling builds only).
+static __device__ unsigned long long g_attend_trace[4096 * 8];
+extern "C" __attribute__((visibility("default"))) void* stk_trace_attend() {
+  void* p = nullptr;
+  cudaGetSymbolAddress(&p, g_attend_trace);
+  return p;
+}
+#define AT(ev) do { if (blockIdx.x < 4096 && threadIdx.x == 0) STK_TRACE_AT(g_attend_trace, blockIdx.x * 8 + (ev)); } while (0)
+#else
+#define AT(ev) ((void)0)
+#endif
+
 struct AttendSmem {
   long long* a_ids;  // [sa]
   long long* p_ids;  // [sp]
@@ -43,6 +58,9 @@ struct AttendSmem {
   float* wU;         // [kAW][d] per-warp numerators
   float* pushU;      // [CS][d] partial numerators pushed by each CTA (rank 0's copy is read)
   float* pushS;      // [CS][2] partial (M, Z)
+  float* rm;         // [ns] retained-slot maxima of this CTA's slots rank, rank + CS, ...
+  float* rl;         // [ns] retained-slot normalisers
+  float* ru;         // [ns][d] retained-slot numerators
 };
 
 template <int DPH, typename T>
@@ -65,6 +83,9 @@ __host__ __device__ inline size_t attend_layout(const RepairArgs& a, int cs, Att
   const size_t wu = take(static_cast<size_t>(kAW) * D * 4, 16);
   const size_t pu = take(static_cast<size_t>(cs) * D * 4, 16);
   const size_t ps = take(static_cast<size_t>(cs) * 8, 16);
+  const int ns = a.pmode == kPredNone ? 0 : (a.sp + cs - 1) / cs;
+  const size_t rm = take(static_cast<size_t>(ns) * 4, 16), rl = take(static_cast<size_t>(ns) * 4, 16);
+  const size_t ru = take(static_cast<size_t>(ns) * D * 4, 16);
   if (S != nullptr) {
     S->a_ids = reinterpret_cast<long long*>(base + ai);
     S->p_ids = reinterpret_cast<long long*>(base + pi);
@@ -75,6 +96,9 @@ __host__ __device__ inline size_t attend_layout(const RepairArgs& a, int cs, Att
     S->wU = reinterpret_cast<float*>(base + wu);
     S->pushU = reinterpret_cast<float*>(base + pu);
     S->pushS = reinterpret_cast<float*>(base + ps);
+    S->rm = reinterpret_cast<float*>(base + rm);
+    S->rl = reinterpret_cast<float*>(base + rl);
+    S->ru = reinterpret_cast<float*>(base + ru);
   }
   return off;
 }
@@ -111,6 +135,12 @@ __global__ void __launch_bounds__(kAW * 32) attend_kernel(RepairArgs a) {
   cg::cluster_group cluster = cg::this_cluster();
   const int CS = static_cast<int>(cluster.num_blocks());
   const int rank = static_cast<int>(cluster.block_rank());
+  // A launch whose cluster shape differs from the host's plan (rows x CS
+  // CTAs in clusters of CS) would map CTAs to the wrong rows: refuse it.
+  if (CS != a.cluster || gridDim.x != static_cast<unsigned>(a.rows) * a.cluster) {
+    if (threadIdx.x == 0) report(a.status, kStatusShapeOverflow);
+    return;
+  }
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = blockIdx.x / CS;
   const int r = row / a.hq;
@@ -124,30 +154,57 @@ __global__ void __launch_bounds__(kAW * 32) attend_kernel(RepairArgs a) {
   uint64_t* mb = &bar[warp];
   const int nwords = (a.max_n + 31) / 32;
 
+  // Announce this CTA to the cluster (its shared memory is live); the
+  // matching wait comes before the first remote store into rank 0.
+  AT(0);
+  pdl_release();
+  cluster_arrive_relaxed();
+
   // ---- 1. IDs, q, bitmaps, the list of blocks to compute.
+  // Everything except the selected IDs A is ready when this kernel starts
+  // (q and P come from the host or from kernels this launch fully depends
+  // on); it is loaded before waiting for the preceding kernel, which may be
+  // the one writing A. These small loads also go out before any of this
+  // kernel's bulk traffic (a load issued behind it waits for all of it).
   if (lane == 0) {
     mbar_init(mb, 1);
     fence_barrier_init();
   }
-  for (int i = tid; i < a.sa; i += blockDim.x) S.a_ids[i] = load_id(a.sel, a.sel64, static_cast<long long>(row) * a.sa + i);
+  for (int i = tid; i < nwords; i += blockDim.x) { S.bitA[i] = 0u; S.bitP[i] = 0u; }
+  for (int i = tid; i < kAW * D; i += blockDim.x) S.wU[i] = 0.f;
   if (has_pred)
     for (int i = tid; i < a.sp; i += blockDim.x)
       S.p_ids[i] = load_id(a.pred, a.pred64, static_cast<long long>(row) * a.sp + i);
   for (int dd = tid; dd < D; dd += blockDim.x) S.qv[dd] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + dd);
-  for (int i = tid; i < nwords; i += blockDim.x) { S.bitA[i] = 0u; S.bitP[i] = 0u; }
-  for (int i = tid; i < kAW * D; i += blockDim.x) S.wU[i] = 0.f;
-  __syncthreads();
-  for (int i = tid; i < a.sa; i += blockDim.x) {
-    const long long id = S.a_ids[i];
-    if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); S.a_ids[i] = -1; continue; }
-    atomicOr(&S.bitA[id >> 5], 1u << (id & 31));
+  // This CTA's prediction slots rank, rank + CS, ...
+  const int ns = has_pred ? (a.sp - rank + CS - 1) / CS : 0;
+  if (has_pred) {
+    const long long sr = static_cast<long long>(row) * a.sc;
+    for (int i = tid; i < ns; i += blockDim.x) {
+      S.rm[i] = a.pm[sr + rank + i * CS];
+      S.rl[i] = a.pl[sr + rank + i * CS];
+    }
+    for (int i = tid; i < ns * D; i += blockDim.x) {
+      const int si = i / D, dd = i - si * D;
+      S.ru[i] = a.pu[(sr + rank + si * CS) * D + dd];
+    }
   }
+  __syncthreads();
   if (has_pred)
     for (int i = tid; i < a.sp; i += blockDim.x) {
       const long long id = S.p_ids[i];
       if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); S.p_ids[i] = -1; continue; }
       atomicOr(&S.bitP[id >> 5], 1u << (id & 31));
     }
+  pdl_wait();  // A may come from the preceding kernel
+  for (int i = tid; i < a.sa; i += blockDim.x) S.a_ids[i] = load_id(a.sel, a.sel64, static_cast<long long>(row) * a.sa + i);
+  __syncthreads();
+  AT(1);
+  for (int i = tid; i < a.sa; i += blockDim.x) {
+    const long long id = S.a_ids[i];
+    if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); S.a_ids[i] = -1; continue; }
+    atomicOr(&S.bitA[id >> 5], 1u << (id & 31));
+  }
   __syncthreads();
   // List = A entries to compute, in A order (block-wide ballot prefix).
   int total = 0;
@@ -168,6 +225,7 @@ __global__ void __launch_bounds__(kAW * 32) attend_kernel(RepairArgs a) {
     __syncthreads();
   }
   const int count = total;
+  AT(2);
 
   // ---- 2. this CTA's share: L2 prefetch, first copies, retained slots, blocks.
   for (int k = rank + CS * tid; k < count; k += CS * blockDim.x)
@@ -201,24 +259,24 @@ __global__ void __launch_bounds__(kAW * 32) attend_kernel(RepairArgs a) {
     }
   };
   if (kfirst < count && lane == 0) issue(kfirst, 0);
+  AT(3);
 
   // Retained prediction slots of this CTA (saved: hits; union: every slot),
   // weights relative to the CTA's own maximum.
   if (has_pred) {
     if (warp == 0) {
+      // keep flags into rm: -inf marks a slot that is not retained.
       float M = neg_inf();
-      for (int c = rank + CS * lane; c < a.sp; c += CS * 32) {
-        const long long id = S.p_ids[c];
+      for (int i = lane; i < ns; i += 32) {
+        const long long id = S.p_ids[rank + i * CS];
         const bool keep = id >= 0 && (a.variant == kVarUnion || ((S.bitA[id >> 5] >> (id & 31)) & 1u));
-        if (keep) M = fmaxf(M, a.pm[static_cast<long long>(row) * a.sc + c]);
+        if (!keep) S.rm[i] = neg_inf();
+        M = fmaxf(M, S.rm[i]);
       }
       M = warp_max(M);
       float Z = 0.f;
-      for (int c = rank + CS * lane; c < a.sp; c += CS * 32) {
-        const long long id = S.p_ids[c];
-        const bool keep = id >= 0 && (a.variant == kVarUnion || ((S.bitA[id >> 5] >> (id & 31)) & 1u));
-        if (keep) Z += expf(a.pm[static_cast<long long>(row) * a.sc + c] - M) * a.pl[static_cast<long long>(row) * a.sc + c];
-      }
+      for (int i = lane; i < ns; i += 32)
+        if (S.rm[i] != neg_inf()) Z += expf(S.rm[i] - M) * S.rl[i];
       Z = warp_sum(Z);
       if (lane == 0) { sh_keep[0] = M; sh_keep[1] = Z; }
     }
@@ -257,13 +315,15 @@ __global__ void __launch_bounds__(kAW * 32) attend_kernel(RepairArgs a) {
     if (ok) fold_state<DPH>(wm, wl, myU, m, l, u, lane);
   }
   if (lane == 0) { sh_w[warp][0] = wm; sh_w[warp][1] = wl; }
+  AT(4);
   __syncthreads();
+  AT(5);
 
   // ---- 3. CTA partial -> rank 0 (distributed shared memory), merge there.
   float M = sh_keep[0];
   for (int w = 0; w < kAW; ++w) M = fmaxf(M, sh_w[w][0]);
+  cluster_wait();  // every CTA of the cluster has started
   float* dstU = cluster.map_shared_rank(S.pushU, 0) + rank * D;
-  const float* pu = has_pred ? a.pu + static_cast<long long>(row) * a.sc * D : nullptr;
   for (int dd = tid; dd < D; dd += blockDim.x) {
     float U = 0.f;
     for (int w = 0; w < kAW; ++w)
@@ -271,11 +331,8 @@ __global__ void __launch_bounds__(kAW * 32) attend_kernel(RepairArgs a) {
     if (has_pred && sh_keep[0] != neg_inf()) {
       // Retained numerators of this CTA's slots, weighted at M.
       float R = 0.f;
-      for (int c = rank; c < a.sp; c += CS) {
-        const long long id = S.p_ids[c];
-        const bool keep = id >= 0 && (a.variant == kVarUnion || ((S.bitA[id >> 5] >> (id & 31)) & 1u));
-        if (keep) R = fmaf(expf(a.pm[static_cast<long long>(row) * a.sc + c] - M), pu[static_cast<long long>(c) * D + dd], R);
-      }
+      for (int i = 0; i < ns; ++i)
+        if (S.rm[i] != neg_inf()) R = fmaf(expf(S.rm[i] - M), S.ru[i * D + dd], R);
       U += R;
     }
     dstU[dd] = U;
@@ -288,7 +345,9 @@ __global__ void __launch_bounds__(kAW * 32) attend_kernel(RepairArgs a) {
     dstS[0] = M;
     dstS[1] = Z;
   }
+  AT(6);
   cluster.sync();
+  AT(7);
   if (rank != 0) return;
   float GM = neg_inf();
   for (int c = 0; c < CS; ++c) GM = fmaxf(GM, S.pushS[c * 2]);
@@ -314,28 +373,17 @@ __global__ void __launch_bounds__(kAW * 32) attend_kernel(RepairArgs a) {
 // ------------------------------------------------------------------ host side
 
 template <typename T, int DPH>
-static int launch_attend_t(const RepairArgs& a, cudaStream_t stream) {
+static int launch_attend_t(RepairArgs a, cudaStream_t stream) {
   const int jobs = a.sa;
   int cs = (jobs + kAW - 1) / kAW;
   if (cs > kAttendCluster) cs = kAttendCluster;
   if (cs < 1) cs = 1;
+  a.cluster = cs;
   const size_t smem = attend_layout<DPH, T>(a, cs, nullptr, nullptr);
   if (smem > 220 * 1024) return -2;
   auto kern = a.L.b % 32 == 0 ? attend_kernel<T, DPH, true> : attend_kernel<T, DPH, false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(a.rows) * cs, 1, 1);
-  cfg.blockDim = dim3(kAW * 32, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cs;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return static_cast<int>(cudaLaunchKernelEx(&cfg, kern, a));
+  return launch_pdl(kern, dim3(static_cast<unsigned>(a.rows) * cs), dim3(kAW * 32), smem, stream, cs, a);
 }
 
 // Returns 1 when the fast attend kernel does not apply (the caller then uses

@@ -241,6 +241,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, int* s
   return false;
 }
 
+// ---------------------------------------------------------------- clusters
+// Split cluster barrier. The CTAs of a cluster are co-scheduled but need not
+// have started when a sibling runs, so a CTA arrives here first thing and
+// waits before its first distributed-shared-memory access; the next
+// cluster-wide barrier then starts a new phase. Every thread of every CTA
+// must execute each arrive and wait once (warp-converged).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while
+// its predecessor on the stream is still running; pdl_wait() blocks until
+// that predecessor has completed and its writes are visible (a no-op for an
+// ordinary launch). pdl_release() lets this kernel's own dependents launch
+// early. Code before pdl_wait() must not read the predecessor's outputs.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- KV layout
 // Addressing for one (request, kv head, block). A block is `nseg` segments of
 // `seg_tokens` contiguous tokens; dense layouts have one segment per block,

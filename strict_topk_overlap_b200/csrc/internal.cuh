@@ -1,5 +1,7 @@
 // Internal argument structs and launchers shared by the library's translation units.
 #pragma once
+#include <utility>
+
 #include "common.cuh"
 
 namespace stk {
@@ -102,6 +104,7 @@ struct RepairArgs {
   float min_remaining, cancel_tol, eps;
   int max_n;  // upper bound of blocks per request (bitmap size)
   int stage_pred;  // set by the launcher: the row's prediction numerators fit in shared memory
+  int cluster;     // set by the launcher: CTAs per row (the launch's cluster size)
   float* out;                // [rows, d]
   unsigned char* fallback;   // [rows]
   float* remaining;          // [rows]
@@ -111,6 +114,34 @@ struct RepairArgs {
   int* total_out;            // [rows] or null
   int* status;
 };
+
+// Launch `kern` with programmatic stream serialization: it may begin while
+// the previous kernel on `stream` finishes (it must call pdl_wait() before
+// reading that kernel's outputs). Optional cluster size (x) when cluster > 0.
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, int cluster,
+                      Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+  if (cluster > 0) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+}
 
 int launch_score(const ScoreArgs& a, cudaStream_t stream);
 int launch_select(const SelectArgs& a, int max_n, cudaStream_t stream);

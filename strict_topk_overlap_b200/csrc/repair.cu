@@ -199,6 +199,12 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
   const int CS = static_cast<int>(cluster.num_blocks());
   const int rank = static_cast<int>(cluster.block_rank());
 
+  // A launch whose cluster shape differs from the host's plan (rows x CS
+  // CTAs in clusters of CS) would map CTAs to the wrong rows: refuse it.
+  if (CS != a.cluster || gridDim.x != static_cast<unsigned>(a.rows) * a.cluster) {
+    if (threadIdx.x == 0) report(a.status, kStatusShapeOverflow);
+    return;
+  }
   constexpr bool kFast = DPH > 0;
   const int D = kFast ? 16 * DPH : a.d;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -809,6 +815,7 @@ static int launch_repair_t(RepairArgs a, cudaStream_t stream) {
   auto kern = a.L.b % 32 == 0 ? repair_kernel<T, DPH, NST, true> : repair_kernel<T, DPH, NST, false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   const int cs = repair_cluster_size(a);
+  a.cluster = cs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(a.rows) * cs, 1, 1);
   cfg.blockDim = dim3(kNW * 32, 1, 1);

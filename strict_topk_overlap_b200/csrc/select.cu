@@ -30,6 +30,27 @@
 
 namespace stk {
 
+#ifdef STK_TRACE
+// [cta][8] timeline of the Top-K kernel (profiling builds only).
+static __device__ unsigned long long g_topk_trace[4096 * 8];
+extern "C" __attribute__((visibility("default"))) void* stk_trace_topk() {
+  void* p = nullptr;
+  cudaGetSymbolAddress(&p, g_topk_trace);
+  return p;
+}
+#define KT(ev) do { if (blockIdx.x < 4096 && threadIdx.x == 0) STK_TRACE_AT(g_topk_trace, blockIdx.x * 8 + (ev)); } while (0)
+static __device__ unsigned long long g_score_trace[4096 * 4];
+extern "C" __attribute__((visibility("default"))) void* stk_trace_score() {
+  void* p = nullptr;
+  cudaGetSymbolAddress(&p, g_score_trace);
+  return p;
+}
+#define ST(ev) do { unsigned _b = blockIdx.y * gridDim.x + blockIdx.x; if (_b < 4096 && threadIdx.x == 0) STK_TRACE_AT(g_score_trace, _b * 4 + (ev)); } while (0)
+#else
+#define KT(ev) ((void)0)
+#define ST(ev) ((void)0)
+#endif
+
 __device__ __forceinline__ int find_request(const int* offs, int R, int gb) {
   if (offs == nullptr) return 0;
   int lo = 0, hi = R - 1;
@@ -218,53 +239,78 @@ __global__ void __launch_bounds__(kTileWarps * 32) score_tiled_kernel(ScoreArgs 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float* slo = reinterpret_cast<float*>(sm);
   float* shi = slo + kTileBlocks * RS;
-  double* sq = reinterpret_cast<double*>(shi + kTileBlocks * RS);  // [kQReq][G][D]
-  double* sgrp = sq + static_cast<size_t>(kQReq) * G * D;             // [kTileBlocks] group sums
+  // q split by sign: qp = q where q >= 0 (else +0), qn = q where q < 0 (else +0),
+  // as FP64 rows [kQReq][G][D] each.
+  double* qp = reinterpret_cast<double*>(shi + kTileBlocks * RS);
+  double* qn = qp + static_cast<size_t>(kQReq) * G * D;
   const long long moff = (static_cast<long long>(mh) * a.total_blocks + row0) * D;
+  ST(0);
+  pdl_release();  // the Top-K kernel may launch now; it waits for this grid to finish
 
-  if (tid == 0) {
-    req0 = find_request(a.block_offsets, a.R, row0);
-    if (bulk) {
-      mbar_init(&bar, 1);
-      fence_barrier_init();
-      mbar_arrive_expect_tx(&bar, static_cast<unsigned>(2 * nrows * D * 4));
+  // q first: a load issued behind the tile's bulk copies would wait for them.
+  const int r0 = find_request(a.block_offsets, a.R, row0);
+  constexpr int kQPer = 8;  // q elements per thread per pass
+  for (int i0 = 0; i0 < kQReq * G * D; i0 += kQPer * static_cast<int>(blockDim.x)) {
+    float qv[kQPer];
+#pragma unroll
+    for (int e = 0; e < kQPer; ++e) {
+      const int i = i0 + e * blockDim.x + tid;
+      qv[e] = 0.f;
+      if (i < kQReq * G * D) {
+        const int rr = i / (G * D), rem = i - rr * G * D;
+        if (r0 + rr < a.R) qv[e] = load_any(a.q, a.q_dtype, (static_cast<long long>(r0 + rr) * a.hq + mh * G) * D + rem);
+      }
     }
-  }
-  __syncthreads();
-  if (bulk) {
-    if (warp == 0) {
+    if (i0 == 0 && tid == 0) {
+      req0 = r0;
+      if (bulk) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+        mbar_arrive_expect_tx(&bar, static_cast<unsigned>(2 * nrows * D * 4));
+      }
+    }
+    if (i0 == 0) __syncthreads();
+    if (i0 == 0 && bulk && warp == 0) {
       for (int rr = lane; rr < nrows; rr += 32) {
         bulk_g2s(slo + rr * RS, a.lo + moff + static_cast<long long>(rr) * D, D * 4, &bar);
         bulk_g2s(shi + rr * RS, a.hi + moff + static_cast<long long>(rr) * D, D * 4, &bar);
       }
     }
-  } else {
+#pragma unroll
+    for (int e = 0; e < kQPer; ++e) {
+      const int i = i0 + e * blockDim.x + tid;
+      if (i < kQReq * G * D) {
+        // q >= 0 picks hi: -0.0 goes with the non-negative side, as in the reference.
+        const bool pos = qv[e] >= 0.f;
+        qp[i] = pos ? static_cast<double>(qv[e]) : 0.0;
+        qn[i] = pos ? 0.0 : static_cast<double>(qv[e]);
+      }
+    }
+  }
+  if (!bulk) {
     for (int i = tid; i < nrows * D; i += blockDim.x) {
       const int rr = i / D, dd = i - rr * D;
       slo[rr * RS + dd] = a.lo[moff + i];
       shi[rr * RS + dd] = a.hi[moff + i];
     }
   }
-  const int r0 = req0;
-  for (int i = tid; i < kQReq * G * D; i += blockDim.x) {
-    const int rr = i / (G * D), rem = i - rr * G * D;
-    const int g = rem / D, dd = rem - g * D;
-    const int r = r0 + rr;
-    sq[i] = r < a.R ? static_cast<double>(load_any(a.q, a.q_dtype, (static_cast<long long>(r) * a.hq + mh * G + g) * D + dd))
-                    : 0.0;
-  }
+  ST(1);
   if (bulk && !mbar_wait(&bar, 0, a.status)) return;
   __syncthreads();
+  ST(2);
 
   const int part = lane >> 3, b = lane & 7;
   const int rl = warp * 8 + b;  // tile row of this lane
   const bool live = rl < nrows;
   const int gb = row0 + rl;
-  const int rr = live ? find_request(a.block_offsets, a.R, gb) - r0 : 0;
+  const int rr = live ? find_request(a.block_offsets, a.R, gb) - req0 : 0;
   const float* lr = slo + rl * RS;
   const float* hr = shi + rl * RS;
   double grp = 0.0;
 
+  // Per element: fma(qn, lo, fma(qp, hi, v)). One of qp / qn is zero, and
+  // fma(0, x, t) == t for finite x, so this rounds exactly like
+  // fma(q, q >= 0 ? hi : lo, v) without a select.
 #pragma unroll 1
   for (int g0 = 0; g0 < G; g0 += kTileRowGroup) {
     const int ng = G4 ? kTileRowGroup : min(kTileRowGroup, G - g0);
@@ -273,7 +319,7 @@ __global__ void __launch_bounds__(kTileWarps * 32) score_tiled_kernel(ScoreArgs 
 #pragma unroll
     for (int kl = 0; kl < 8; ++kl) {
       const int c = bitrev5(part * 8 + kl);
-      float lo_c[C], hi_c[C];
+      double lo_c[C], hi_c[C];
 #pragma unroll
       for (int e = 0; e < C; e += (C >= 4 ? 4 : 2)) {
         if constexpr (C >= 4) {
@@ -293,15 +339,15 @@ __global__ void __launch_bounds__(kTileWarps * 32) score_tiled_kernel(ScoreArgs 
         if (G4 || gi < ng) {
           double v = 0.0;
           if (rr < kQReq) {
-            const double* qr = sq + (rr * G + g0 + gi) * D + c * C;
+            const int qo = (rr * G + g0 + gi) * D + c * C;
 #pragma unroll
-            for (int e = 0; e < C; ++e) {
-              const double qv = qr[e];
-              v = __fma_rn(qv, static_cast<double>(qv >= 0.0 ? hi_c[e] : lo_c[e]), v);
-            }
+            for (int e = 0; e < C; ++e) v = __fma_rn(qn[qo + e], lo_c[e], __fma_rn(qp[qo + e], hi_c[e], v));
           } else {
-            v = leaf_global_q<C>(a, (static_cast<long long>(r0 + rr) * a.hq + mh * G + g0 + gi) * D + c * C, lo_c,
-                                 hi_c);
+            float lf[C], hf[C];
+#pragma unroll
+            for (int e = 0; e < C; ++e) { lf[e] = static_cast<float>(lo_c[e]); hf[e] = static_cast<float>(hi_c[e]); }
+            v = leaf_global_q<C>(a, (static_cast<long long>(req0 + rr) * a.hq + mh * G + g0 + gi) * D + c * C, lf,
+                                 hf);
           }
           // Balanced-tree push of leaf kl (levels resolved at compile time).
           if ((kl & 1) == 0) {
@@ -334,7 +380,7 @@ __global__ void __launch_bounds__(kTileWarps * 32) score_tiled_kernel(ScoreArgs 
   }
   if (a.scores_f64 && a.group_select && part == 0 && live)
     a.scores_f64[static_cast<long long>(mh) * a.total_blocks + gb] = grp;
-  (void)sgrp;
+  ST(3);
 }
 
 // ------------------------------------------------------------------ Top-K
@@ -354,25 +400,27 @@ __device__ __forceinline__ unsigned long long warp_or64(unsigned long long x) {
 // positions [t*E, t*E+E). Writes the chosen positions' IDs (id_of) in
 // ascending position order; ties (equal keys) go to the lower position.
 //
-// MSB-first 8-bit digits over the bits in which the keys differ (the common
-// prefix is skipped). Each pass builds per-warp histograms with shared-memory
-// atomics, then all threads scan the 256 bins from the top to find the bin
-// holding the K-th key; the pass loop ends as soon as that bin's keys are all
-// selected. A final block scan places every selected ID at its ascending
-// output position.
+// MSB-first 4-bit digits over the bits in which the keys differ (the common
+// prefix is skipped). A pass needs no atomics and no shuffles: every thread
+// counts its candidate keys per digit in two 64-bit registers of 8-bit
+// fields, repacks them as eight 32-bit words of 16-bit fields, and each word
+// is summed over the warp by one redux.sync; warp 0 adds the warps' counts
+// and scans the 16 bins from the top to find the bin holding the K-th key.
+// The pass loop ends as soon as that bin's keys are all selected. A final
+// block scan places every selected ID at its ascending output position.
 constexpr int kSelMaxWarps = 16;
 
 template <int E, typename IdOf>
 __device__ void select_registers(const unsigned long long (&key)[E], int n, int topk, IdOf id_of, int* out,
                                  unsigned long long* keys_out) {
-  __shared__ unsigned hist[kSelMaxWarps][256];
+  static_assert(E <= 255, "per-thread digit counts use 8-bit fields");
+  __shared__ unsigned wc[kSelMaxWarps][8];
   __shared__ unsigned long long sh_or, sh_k0;
   __shared__ int sh_bin, sh_above, sh_cnt;
   __shared__ unsigned warp_tot[kSelMaxWarps];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nw = blockDim.x >> 5;
   const int beg = tid * E;
-  const int bpt = 256 / static_cast<int>(blockDim.x) > 0 ? 256 / static_cast<int>(blockDim.x) : 1;  // bins per thread
 
   if (tid == 0) { sh_or = 0; sh_k0 = key[0]; }
   __syncthreads();
@@ -385,6 +433,10 @@ __device__ void select_registers(const unsigned long long (&key)[E], int n, int 
   if (lane == 0 && diff) atomicOr(&sh_or, diff);
   __syncthreads();
   diff = sh_or;
+#ifdef STK_TRACE
+  if (tid == 0 && blockIdx.x < 4096) g_topk_trace[blockIdx.x * 8 + 3] = global_ns();
+  int npass = 0;
+#endif
 
   unsigned long long prefix, mask;
   int kk = topk;
@@ -396,57 +448,70 @@ __device__ void select_registers(const unsigned long long (&key)[E], int n, int 
     const int hb = 63 - __clzll(diff);
     mask = (hb == 63) ? 0ull : ~((2ull << hb) - 1ull);
     prefix = k0 & mask;
-    for (int shift = (hb / 8) * 8; shift >= 0; shift -= 8) {
-      unsigned* hw = hist[warp];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) hw[lane * 8 + i] = 0u;
-      __syncwarp();
+#pragma unroll 1
+    for (int shift = (hb / 4) * 4; shift >= 0; shift -= 4) {
+      unsigned long long lo8 = 0, hi8 = 0;  // bins 0..7 / 8..15, 8-bit fields
 #pragma unroll
       for (int j = 0; j < E; ++j) {
-        if (beg + j < n && (key[j] & mask) == prefix)
-          atomicAdd(&hw[static_cast<unsigned>((key[j] >> shift) & 0xFF)], 1u);
+        if (beg + j < n && (key[j] & mask) == prefix) {
+          const unsigned d = static_cast<unsigned>(key[j] >> shift) & 15u;
+          const unsigned long long inc = 1ull << ((d & 7u) * 8u);
+          if (d < 8) lo8 += inc; else hi8 += inc;
+        }
       }
-      __syncthreads();
-      // Thread t scans bins 255 - t*bpt, 255 - t*bpt - 1, ... (descending).
-      unsigned local = 0;
-      for (int i = 0; i < bpt; ++i) {
-        const int bin = 255 - (tid * bpt + i);
-        if (bin >= 0)
-          for (int w = 0; w < nw; ++w) local += hist[w][bin];
-      }
-      unsigned inc = local;
+      // Repack as 16-bit fields (bins 2i, 2i+1 in word i) and sum over the warp.
+      unsigned w[8];
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const unsigned y = __shfl_up_sync(kFull, inc, o);
-        if (lane >= o) inc += y;
+      for (int i = 0; i < 4; ++i) {
+        const unsigned xl = static_cast<unsigned>(lo8 >> (16 * i)), xh = static_cast<unsigned>(hi8 >> (16 * i));
+        w[i] = (xl & 0xffu) | ((xl & 0xff00u) << 8);
+        w[4 + i] = (xh & 0xffu) | ((xh & 0xff00u) << 8);
       }
-      if (lane == 31) warp_tot[warp] = inc;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[i] = __reduce_add_sync(kFull, w[i]);
+      if (lane == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) wc[warp][i] = w[i];
+      }
       __syncthreads();
-      unsigned excl = inc - local;
-      for (int w = 0; w < warp; ++w) excl += warp_tot[w];
-      if (excl < static_cast<unsigned>(kk) && excl + local >= static_cast<unsigned>(kk)) {
-        unsigned run = excl;
-        for (int i = 0; i < bpt; ++i) {
-          const int bin = 255 - (tid * bpt + i);
-          unsigned c = 0;
-          for (int w = 0; w < nw; ++w) c += hist[w][bin];
-          if (run + c >= static_cast<unsigned>(kk)) {
-            sh_bin = bin;
-            sh_above = static_cast<int>(run);
-            sh_cnt = static_cast<int>(c);
-            break;
-          }
-          run += c;
+      if (warp == 0) {
+        // Lane i (< 16) takes bin 15 - i, so an inclusive lane scan counts keys
+        // in bins >= 15 - i.
+        unsigned cnt = 0;
+        if (lane < 16) {
+          const int bin = 15 - lane;
+          for (int ww = 0; ww < nw; ++ww) cnt += (wc[ww][bin >> 1] >> ((bin & 1) * 16)) & 0xffffu;
+        }
+        unsigned inc = cnt;
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) {
+          const unsigned y = __shfl_up_sync(kFull, inc, o);
+          if (lane >= o) inc += y;
+        }
+        const unsigned excl = inc - cnt;
+        if (lane < 16 && excl < static_cast<unsigned>(kk) && inc >= static_cast<unsigned>(kk)) {
+          sh_bin = 15 - lane;
+          sh_above = static_cast<int>(excl);
+          sh_cnt = static_cast<int>(cnt);
         }
       }
       __syncthreads();
       prefix |= static_cast<unsigned long long>(sh_bin) << shift;
-      mask |= 0xFFull << shift;
+      mask |= 0xFull << shift;
       kk -= sh_above;
       const int cnt = sh_cnt;
+#ifdef STK_TRACE
+      ++npass;
+#endif
       if (cnt == kk) { take_all = true; break; }
     }
   }
+#ifdef STK_TRACE
+  if (tid == 0 && blockIdx.x < 4096) {
+    g_topk_trace[blockIdx.x * 8 + 4] = global_ns();
+    g_topk_trace[blockIdx.x * 8 + 5] = npass;
+  }
+#endif
   if (take_all) kk = n;
 
   // Packed scan: (#above, #in-region) before this thread's first position.
@@ -491,8 +556,12 @@ __device__ void select_registers(const unsigned long long (&key)[E], int n, int 
   }
 }
 
+
 template <int E>
 __global__ void __launch_bounds__(512) select_topk_kernel(SelectArgs a) {
+  KT(0);
+  pdl_release();
+  pdl_wait();  // scores come from the preceding scoring kernel
   const int row = blockIdx.x;
   const int r = row / a.hsel, hs = row - r * a.hsel;
   const int off = a.block_offsets ? a.block_offsets[r] : 0;
@@ -506,10 +575,12 @@ __global__ void __launch_bounds__(512) select_topk_kernel(SelectArgs a) {
   const int beg = threadIdx.x * E;
 #pragma unroll
   for (int j = 0; j < E; ++j) key[j] = beg + j < n ? order_key(src[beg + j]) : 0ull;
+  KT(1);
   const int base = a.id_base;
   select_registers<E>(key, n, a.topk, [base](int i) { return base + i; },
                       a.ids_out + static_cast<long long>(row) * a.topk,
                       a.keys_out ? a.keys_out + static_cast<long long>(row) * a.topk : nullptr);
+  KT(2);
 }
 
 // Candidate merge (context-parallel and segmented selection): each row has
@@ -542,8 +613,7 @@ int launch_score(const ScoreArgs& a, cudaStream_t stream) {
   const bool aligned = ((reinterpret_cast<uintptr_t>(a.lo) | reinterpret_cast<uintptr_t>(a.hi)) & 15) == 0;
   if (a.d == 64 || a.d == 128 || a.d == 256) {
     const int rs = a.d + 4;
-    const size_t smem = static_cast<size_t>(2) * kTileBlocks * rs * 4 + static_cast<size_t>(kQReq) * G * a.d * 8 +
-                        static_cast<size_t>(kTileBlocks) * 8;
+    const size_t smem = static_cast<size_t>(2) * kTileBlocks * rs * 4 + static_cast<size_t>(2) * kQReq * G * a.d * 8;
     if (smem <= 200 * 1024) {
       const int tiles = (a.total_blocks + kTileBlocks - 1) / kTileBlocks;
       dim3 grid(tiles, a.hmeta);
@@ -572,20 +642,12 @@ int launch_score(const ScoreArgs& a, cudaStream_t stream) {
 
 int launch_select(const SelectArgs& a, int max_n, cudaStream_t stream) {
   const int rows = a.R * a.hsel;
-  if (max_n <= 1024) {
-    select_topk_kernel<8><<<rows, 128, 0, stream>>>(a);
-  } else if (max_n <= 2048) {
-    select_topk_kernel<8><<<rows, 256, 0, stream>>>(a);
-  } else if (max_n <= 4096) {
-    select_topk_kernel<16><<<rows, 256, 0, stream>>>(a);
-  } else if (max_n <= 8192) {
-    select_topk_kernel<16><<<rows, 512, 0, stream>>>(a);
-  } else if (max_n <= 16384) {
-    select_topk_kernel<32><<<rows, 512, 0, stream>>>(a);
-  } else {
-    return -1;
-  }
-  return static_cast<int>(cudaGetLastError());
+  if (max_n <= 1024) return launch_pdl(select_topk_kernel<4>, dim3(rows), dim3(256), 0, stream, 0, a);
+  if (max_n <= 2048) return launch_pdl(select_topk_kernel<4>, dim3(rows), dim3(512), 0, stream, 0, a);
+  if (max_n <= 4096) return launch_pdl(select_topk_kernel<8>, dim3(rows), dim3(512), 0, stream, 0, a);
+  if (max_n <= 8192) return launch_pdl(select_topk_kernel<16>, dim3(rows), dim3(512), 0, stream, 0, a);
+  if (max_n <= 16384) return launch_pdl(select_topk_kernel<32>, dim3(rows), dim3(512), 0, stream, 0, a);
+  return -1;
 }
 
 int launch_merge_candidates(const MergeArgs& a, cudaStream_t stream) {

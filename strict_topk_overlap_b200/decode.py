@@ -96,7 +96,9 @@ class SpeculativeDecoder:
         self.q, self.k, self.v, self.lo, self.hi, self.predicted = q, k, v, lo, hi, predicted
         self.spec = spec
         self.serial = serial
-        self._sel_stream = torch.cuda.Stream(q.device)
+        # The selector is the critical path (score -> Top-K -> repair): its
+        # stream gets the higher priority when both branches want SMs.
+        self._sel_stream = torch.cuda.Stream(q.device, priority=-1)
         self._pred_stream = torch.cuda.Stream(q.device)
         self._selector = lambda: gqa.select_blocks(q, lo, hi, spec.topk)
         self._spec = _speculate_fn(spec, q, k, v, predicted)
