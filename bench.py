@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true",
                     help="short run for profiler captures: no clock window, e2e, sweep or CPU baseline")
+    ap.add_argument("--graph-steps", type=int, default=8,
+                    help="decode steps per CUDA graph in the timed loops (one per input set, like the attention "
+                         "calls of consecutive layers of one token step); 1 = one graph per step")
     ap.add_argument("--eager", action="store_true",
                     help="launch each step's kernels directly instead of replaying a CUDA graph (for per-kernel "
                          "profiler launch lists)")
@@ -269,7 +272,7 @@ def main():
     from strict_topk_overlap_b200 import _lib
     _lib.load()
     from strict_topk import gqa
-    from strict_topk_overlap_b200.decode import SpeculativeDecoder, StepSpec
+    from strict_topk_overlap_b200.decode import SpeculativeDecoder, StepSpec, capture_steps
 
     nsets = args.sets
     sets = [make_set(args.seed + 1000 * rank + i, args.overlap, device) for i in range(nsets)]
@@ -286,25 +289,40 @@ def main():
         assert torch.equal(d_.selected.cpu(), s_.selected.cpu())
         assert (o1 - o2).abs().max().item() <= 2e-3, "speculative and serial outputs differ"
 
-    def spec_step(i):
-        dec[i % nsets].step()
+    # Timed loops: graphs of `gsteps` consecutive decode steps (one per input
+    # set); a call of spec_step / serial_step runs one such graph.
+    gsteps = max(1, min(args.graph_steps, nsets)) if graph else 1
+    if gsteps > 1:
+        gspec = [capture_steps([dec[(j + i) % nsets] for i in range(gsteps)])[0] for j in range(0, nsets, gsteps)]
+        gser = [capture_steps([ser[(j + i) % nsets] for i in range(gsteps)])[0] for j in range(0, nsets, gsteps)]
 
-    def serial_step(i):
-        ser[i % nsets].step()
+        def spec_step(i):
+            gspec[i % len(gspec)].replay()
+
+        def serial_step(i):
+            gser[i % len(gser)].replay()
+    else:
+        def spec_step(i):
+            dec[i % nsets].step()
+
+        def serial_step(i):
+            ser[i % nsets].step()
+    ncalls = max(1, args.steps // gsteps)
+    args.steps = ncalls * gsteps
 
     hbm_peak, peak_kind = peaks()
     # Warm-up (untimed), then a ~1 s load window so clock samples see steady state.
-    for i in range(args.warmup):
+    for i in range(max(args.warmup // gsteps, 3)):
         spec_step(i)
     torch.cuda.synchronize()
     with ClockSampler(local if not args.quick else -1) as clk:
         t_end = time.perf_counter() + (0.0 if args.quick else 1.0)
         while time.perf_counter() < t_end:
-            for i in range(200):
+            for i in range(200 // gsteps + 1):
                 spec_step(i)
             torch.cuda.synchronize()
         barrier(world)
-        ms = time_loop(spec_step, args.steps, device)
+        ms = time_loop(spec_step, ncalls, device)
         barrier(world)
     ms = max_over_ranks(ms, world, device)
     us_step = ms * 1e3 / args.steps
@@ -312,8 +330,16 @@ def main():
     clocks = clk.summary()
 
     # Serial baseline with the same kernels (same rotation), outside the main region.
-    ms_ser = max_over_ranks(time_loop(serial_step, args.steps, device), world, device)
+    for i in range(3):
+        serial_step(i)
+    ms_ser = max_over_ranks(time_loop(serial_step, ncalls, device), world, device)
     us_ser = ms_ser * 1e3 / args.steps
+    # Context: one CUDA graph per step (graph-launch cost paid every step).
+    single = {}
+    if graph and gsteps > 1 and not args.quick:
+        n1 = min(args.steps, 2000)
+        single = {"spec_us": time_loop(lambda i: dec[i % nsets].step(), n1, device) * 1e3 / n1,
+                  "serial_us": time_loop(lambda i: ser[i % nsets].step(), n1, device) * 1e3 / n1}
 
     # Roofline of the dominant kernel: predicted-block attention (block states over P).
     s0 = sets[0]
@@ -321,15 +347,28 @@ def main():
     blk = B * D * 2
     pstates = [None] * nsets
 
-    def partials_only(i):
-        s = sets[i % nsets]
-        pstates[i % nsets] = gqa.partials(s["q"], s["k"], s["v"], s["p"])
+    # The dominant kernel timed alone: one CUDA graph of `nsets` launches
+    # (one per input set, so no launch finds its KV in L2), replayed; CUDA
+    # events on the launching stream around the replays.
+    def partials_all():
+        for i in range(nsets):
+            s = sets[i]
+            pstates[i] = gqa.partials(s["q"], s["k"], s["v"], s["p"])
 
-    for i in range(50):
-        partials_only(i)
-    nrep = 20 if args.quick else max(200, min(args.steps, 5000))
-    ms_part = time_loop(partials_only, nrep, device, torch.cuda.current_stream())
-    us_part = ms_part * 1e3 / nrep
+    if graph:
+        partials_all()
+        torch.cuda.synchronize()
+        gpart = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gpart):
+            partials_all()
+        run_part = lambda i: gpart.replay()  # noqa: E731
+    else:
+        run_part = lambda i: partials_all()  # noqa: E731
+    for i in range(5):
+        run_part(i)
+    nrep = 3 if args.quick else max(50, min(args.steps // nsets, 1000))
+    ms_part = time_loop(run_part, nrep, device, torch.cuda.current_stream())
+    us_part = ms_part * 1e3 / (nrep * nsets)
     upred = statistics.mean(unique_blocks(s["p"].cpu(), g) for s in sets)
     part_bytes = 2 * blk * upred + HQ * D * 2 + HQ * TOPK * 4 + HQ * TOPK * (D + 2) * 4
     achieved = part_bytes / (us_part * 1e-6) / 1e9
@@ -408,8 +447,11 @@ def main():
                                    "K=64, bf16", "method": args.method, "predicted_overlap": args.overlap,
                        "l2": f"{nsets} rotating input sets x {(2 * HKV * BLOCKS * B * D * 2 + 2 * HKV * BLOCKS * D * 4) / 2**20:.0f} MiB (> 126 MB L2)",
                        "parallelism": f"request replicas x{world} (no collective in the data path)",
-                       "graph": "one CUDA graph per step (selector || speculation, then repair)"},
+                       "graph": (f"{gsteps} decode steps per CUDA graph (one per input set, replayed; selector || "
+                                 "speculation, then repair, in each step)") if gsteps > 1 else
+                                "one CUDA graph per step (selector || speculation, then repair)"},
             "serial_us_per_step": us_ser, "speedup_vs_serial": us_ser / us_step,
+            "one_graph_per_step_us": single or None,
             "step_algorithmic_bytes": step_bytes, "serial_algorithmic_bytes": serial_bytes,
             "step_hbm_frac": step_bytes / (us_step * 1e-6) / 1e9 / hbm_peak,
             "serial_hbm_frac": serial_bytes / (us_ser * 1e-6) / 1e9 / hbm_peak,

@@ -370,6 +370,229 @@ __global__ void __launch_bounds__(kAW * 32) attend_kernel(RepairArgs a) {
   }
 }
 
+// ------------------------------------------------------------------ saved repair, one CTA per row
+// The low-latency form of the saved / union repair (reference gqa_light.py:
+// one program per query head): one CTA of kLW warps per row, no cluster.
+// Everything except A — predicted IDs, q, and the row's prediction states
+// (m, l and the numerators, staged into shared memory) — is loaded before
+// waiting for the preceding kernel (the one writing A); then A's misses are
+// listed, each warp streams its misses through a private stage, the CTA's
+// threads fold the retained states (saved: P slots whose ID is in A; union:
+// all), and one merge in warp order writes the row's output.
+constexpr int kLW = 8;
+
+template <typename T, int DPH, bool FULL32>
+__global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
+  constexpr int D = 16 * DPH;
+  constexpr int kChunk = 32 * D;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ uint64_t bar[kLW];
+  __shared__ int sh_cnt[kLW];
+  __shared__ float sh_w[kLW + 1][2];
+  __shared__ int sh_total;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row = blockIdx.x;
+  const int r = row / a.hq;
+  const int kv = (row - r * a.hq) / a.g;
+  const int nblocks = request_blocks(a.L, r);
+  const int nwords = (a.max_n + 31) / 32;
+  pdl_release();
+
+  // Shared memory: stages [kLW][2][32][D] T, then the row's bookkeeping.
+  T* stage = reinterpret_cast<T*>(smem) + static_cast<size_t>(warp) * 2 * kChunk;
+  size_t off = static_cast<size_t>(kLW) * 2 * kChunk * sizeof(T);
+  auto carve = [&](size_t bytes) {
+    off = (off + 15) & ~size_t(15);
+    unsigned char* p = smem + off;
+    off += bytes;
+    return p;
+  };
+  float* pu_s = reinterpret_cast<float*>(carve(static_cast<size_t>(a.sp) * D * 4));  // [sp][D]
+  float* pm_s = reinterpret_cast<float*>(carve(static_cast<size_t>(a.sp) * 4));
+  float* pl_s = reinterpret_cast<float*>(carve(static_cast<size_t>(a.sp) * 4));
+  long long* p_ids = reinterpret_cast<long long*>(carve(static_cast<size_t>(a.sp) * 8));
+  long long* a_ids = reinterpret_cast<long long*>(carve(static_cast<size_t>(a.sa) * 8));
+  unsigned* bitA = reinterpret_cast<unsigned*>(carve(static_cast<size_t>(nwords) * 4));
+  unsigned* bitP = reinterpret_cast<unsigned*>(carve(static_cast<size_t>(nwords) * 4));
+  int* list = reinterpret_cast<int*>(carve(static_cast<size_t>(a.sa) * 4));
+  float* qv = reinterpret_cast<float*>(carve(static_cast<size_t>(D) * 4));
+  float* wU = reinterpret_cast<float*>(carve(static_cast<size_t>(kLW + 1) * D * 4));
+
+  if (lane == 0) {
+    mbar_init(&bar[warp], 1);
+    fence_barrier_init();
+  }
+  // ---- before the wait: everything but A.
+  const long long sr = static_cast<long long>(row) * a.sp;
+  for (int i = tid; i < nwords; i += blockDim.x) { bitA[i] = 0u; bitP[i] = 0u; }
+  for (int i = tid; i < a.sp; i += blockDim.x) {
+    p_ids[i] = load_id(a.pred, a.pred64, sr + i);
+    pm_s[i] = a.pm[sr + i];
+    pl_s[i] = a.pl[sr + i];
+  }
+  for (int dd = tid; dd < D; dd += blockDim.x) qv[dd] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + dd);
+  {
+    const float4* src = reinterpret_cast<const float4*>(a.pu + sr * D);
+    float4* dst = reinterpret_cast<float4*>(pu_s);
+    for (int i = tid; i < a.sp * D / 4; i += blockDim.x) dst[i] = src[i];
+  }
+  __syncthreads();
+  for (int i = tid; i < a.sp; i += blockDim.x) {
+    const long long id = p_ids[i];
+    if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); p_ids[i] = -1; continue; }
+    atomicOr(&bitP[id >> 5], 1u << (id & 31));
+  }
+  pdl_wait();  // A comes from the preceding kernel
+  for (int i = tid; i < a.sa; i += blockDim.x) {
+    long long id = load_id(a.sel, a.sel64, static_cast<long long>(row) * a.sa + i);
+    if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); id = -1; }
+    a_ids[i] = id;
+    if (id >= 0) atomicOr(&bitA[id >> 5], 1u << (id & 31));
+  }
+  __syncthreads();
+  // Misses (A entries not in P), in A order.
+  if (warp == 0) {
+    int n = 0;
+    for (int base = 0; base < a.sa; base += 32) {
+      const int i = base + lane;
+      bool miss = false;
+      if (i < a.sa) {
+        const long long id = a_ids[i];
+        miss = id >= 0 && !((bitP[id >> 5] >> (id & 31)) & 1u);
+      }
+      const unsigned bal = __ballot_sync(kFull, miss);
+      if (miss) list[n + __popc(bal & ((1u << lane) - 1))] = i;
+      n += __popc(bal);
+    }
+    if (lane == 0) sh_total = n;
+  }
+  __syncthreads();
+  const int count = sh_total;
+
+  const int nchunks = (a.L.b + 31) / 32;
+  auto issue = [&](int k, int c) {
+    const long long bid = a_ids[list[k]];
+    const int t0 = c * 32, ntok = FULL32 ? 32 : min(32, a.L.b - t0);
+    const unsigned bytes = static_cast<unsigned>(ntok * D * sizeof(T));
+    mbar_arrive_expect_tx(&bar[warp], 2 * bytes);
+    const T* K = static_cast<const T*>(a.L.k);
+    const T* V = static_cast<const T*>(a.L.v);
+    if (a.L.page_table == nullptr) {
+      const long long o = block_seg(a.L, r, kv, bid, 0).elem_off + static_cast<long long>(t0) * D;
+      bulk_g2s(stage, K + o, bytes, &bar[warp]);
+      bulk_g2s(stage + kChunk, V + o, bytes, &bar[warp]);
+    } else {
+      for (int t = t0; t < t0 + ntok;) {
+        const int pg = t / a.L.page_size, po = t - pg * a.L.page_size;
+        const int cnt = min(a.L.page_size - po, t0 + ntok - t);
+        const long long o = block_seg(a.L, r, kv, bid, pg).elem_off + static_cast<long long>(po) * D;
+        const unsigned sb = static_cast<unsigned>(cnt * D * sizeof(T));
+        bulk_g2s(stage + (t - t0) * D, K + o, sb, &bar[warp]);
+        bulk_g2s(stage + kChunk + (t - t0) * D, V + o, sb, &bar[warp]);
+        t += cnt;
+      }
+    }
+  };
+  if (warp < count && lane == 0) issue(warp, 0);
+  // Later misses (beyond one per warp) are prefetched into L2 now.
+  for (int k = kLW + tid; k < count; k += blockDim.x) prefetch_block<T>(a.L, r, kv, a_ids[list[k]], true);
+
+  // Retained slots (warp-parallel over slots, threads over dims after).
+  if (warp == kLW - 1) {
+    float M = neg_inf();
+    for (int c = lane; c < a.sp; c += 32) {
+      const long long id = p_ids[c];
+      const bool keep = id >= 0 && (a.variant == kVarUnion || ((bitA[id >> 5] >> (id & 31)) & 1u));
+      if (!keep) pm_s[c] = neg_inf();
+      M = fmaxf(M, pm_s[c]);
+    }
+    M = warp_max(M);
+    // pl_s becomes the slot weight exp(m - M) (0 for slots not retained).
+    float Z = 0.f;
+    for (int c = lane; c < a.sp; c += 32) {
+      const float w = pm_s[c] != neg_inf() ? expf(pm_s[c] - M) : 0.f;
+      Z += w * pl_s[c];
+      pl_s[c] = w;
+    }
+    Z = warp_sum(Z);
+    if (lane == 0) { sh_w[kLW][0] = M; sh_w[kLW][1] = Z; }
+  }
+  float qf[DPH];
+#pragma unroll
+  for (int j = 0; j < DPH; ++j) qf[j] = qv[(lane & 15) * DPH + j];
+  float wm = neg_inf(), wl = 0.f;
+  float* myU = wU + warp * D;
+  for (int dd = lane; dd < D; dd += 32) myU[dd] = 0.f;
+  __syncwarp();
+  unsigned phase = 0;
+  bool ok = true;
+#pragma unroll 1
+  for (int k = warp; k < count && ok; k += kLW) {
+    float m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
+#pragma unroll
+    for (int j = 0; j < DPH; ++j) { u[j] = 0.f; ua[j] = 0.f; }
+#pragma unroll 1
+    for (int c = 0; c < nchunks; ++c) {
+      ok = mbar_wait(&bar[warp], phase, a.status);
+      phase ^= 1u;
+      if (!ok) break;
+      const int ntok = FULL32 ? 32 : min(32, a.L.b - c * 32);
+      warp_block_state<T, DPH, kModeFull, FULL32>(stage, stage + kChunk, ntok, qf, a.scale, 0.f, m, l, u, ua, lane);
+      __syncwarp();
+      if (lane == 0) {
+        if (c + 1 < nchunks) issue(k, c + 1);
+        else if (k + kLW < count) issue(k + kLW, 0);
+      }
+    }
+    if (ok) fold_state<DPH>(wm, wl, myU, m, l, u, lane);
+  }
+  if (lane == 0) { sh_w[warp][0] = wm; sh_w[warp][1] = wl; }
+  __syncthreads();
+  // Final merge: warps in order, then the retained slots.
+  float M = sh_w[kLW][0];
+  for (int w = 0; w < kLW; ++w) M = fmaxf(M, sh_w[w][0]);
+  float Z = sh_w[kLW][0] != neg_inf() ? expf(sh_w[kLW][0] - M) * sh_w[kLW][1] : 0.f;
+  for (int w = 0; w < kLW; ++w)
+    if (sh_w[w][0] != neg_inf()) Z += expf(sh_w[w][0] - M) * sh_w[w][1];
+  const float kscale = sh_w[kLW][0] != neg_inf() ? expf(sh_w[kLW][0] - M) : 0.f;
+  for (int dd = tid; dd < D; dd += blockDim.x) {
+    float U = 0.f;
+    for (int w = 0; w < kLW; ++w)
+      if (sh_w[w][0] != neg_inf()) U += expf(sh_w[w][0] - M) * wU[w * D + dd];
+    if (kscale != 0.f) {
+      float R = 0.f;
+      for (int c = 0; c < a.sp; ++c)
+        if (pl_s[c] != 0.f) R = fmaf(pl_s[c], pu_s[c * D + dd], R);
+      U += kscale * R;
+    }
+    a.out[static_cast<long long>(row) * D + dd] = U / fmaxf(Z, 1e-30f);
+  }
+  if (tid == 0) {
+    if (a.fallback) a.fallback[row] = 0;
+    if (a.remaining) a.remaining[row] = 1.f;
+    if (a.approx) a.approx[row] = 0;
+    if (a.extra) a.extra[row] = 0.f;
+    if (a.pos_out) a.pos_out[row] = count;
+    if (a.total_out) a.total_out[row] = count;
+  }
+}
+
+template <typename T, int DPH>
+static int launch_light_t(const RepairArgs& a, cudaStream_t stream) {
+  const int nwords = (a.max_n + 31) / 32;
+  const int D = a.d;
+  size_t smem = static_cast<size_t>(kLW) * 2 * 32 * D * sizeof(T);
+  auto add = [&](size_t b) { smem = ((smem + 15) & ~size_t(15)) + b; };
+  add(static_cast<size_t>(a.sp) * D * 4); add(static_cast<size_t>(a.sp) * 4); add(static_cast<size_t>(a.sp) * 4);
+  add(static_cast<size_t>(a.sp) * 8); add(static_cast<size_t>(a.sa) * 8); add(static_cast<size_t>(nwords) * 4);
+  add(static_cast<size_t>(nwords) * 4); add(static_cast<size_t>(a.sa) * 4); add(static_cast<size_t>(D) * 4);
+  add(static_cast<size_t>(kLW + 1) * D * 4);
+  if (smem > 225 * 1024) return 1;
+  auto kern = a.L.b % 32 == 0 ? light_kernel<T, DPH, true> : light_kernel<T, DPH, false>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  return launch_pdl(kern, dim3(static_cast<unsigned>(a.rows)), dim3(kLW * 32), smem, stream, 0, a);
+}
+
 // ------------------------------------------------------------------ host side
 
 template <typename T, int DPH>
@@ -397,6 +620,14 @@ int launch_attend(const RepairArgs& a, int kv_dtype, cudaStream_t stream) {
   const bool aligned = (pk & 15) == 0 && (a.d * esz) % 16 == 0 &&
                        (a.L.page_table == nullptr || a.L.b % a.L.page_size == 0) && a.L.kv_request_stride % 8 == 0;
   if (!aligned || (a.d != 64 && a.d != 128)) return 1;
+  // Saved / union with a prediction: the one-CTA-per-row form when its stages
+  // and the row's staged prediction states fit in shared memory.
+  if (a.pmode == kPredSaved && kv_dtype != kF32 && (reinterpret_cast<uintptr_t>(a.pu) & 15) == 0) {
+    const int rc = kv_dtype == kF16 ? (a.d == 64 ? launch_light_t<__half, 4>(a, stream) : launch_light_t<__half, 8>(a, stream))
+                                    : (a.d == 64 ? launch_light_t<__nv_bfloat16, 4>(a, stream)
+                                                 : launch_light_t<__nv_bfloat16, 8>(a, stream));
+    if (rc != 1) return rc;
+  }
   switch (kv_dtype) {
     case kF32: return a.d == 64 ? launch_attend_t<float, 4>(a, stream) : launch_attend_t<float, 8>(a, stream);
     case kF16: return a.d == 64 ? launch_attend_t<__half, 4>(a, stream) : launch_attend_t<__half, 8>(a, stream);

@@ -383,6 +383,7 @@ __global__ void __launch_bounds__(kTileWarps * 32) score_tiled_kernel(ScoreArgs 
   ST(3);
 }
 
+
 // ------------------------------------------------------------------ Top-K
 
 __device__ __forceinline__ unsigned long long order_key(double x) {
@@ -401,22 +402,66 @@ __device__ __forceinline__ unsigned long long warp_or64(unsigned long long x) {
 // ascending position order; ties (equal keys) go to the lower position.
 //
 // MSB-first 4-bit digits over the bits in which the keys differ (the common
-// prefix is skipped). A pass needs no atomics and no shuffles: every thread
-// counts its candidate keys per digit in two 64-bit registers of 8-bit
-// fields, repacks them as eight 32-bit words of 16-bit fields, and each word
-// is summed over the warp by one redux.sync; warp 0 adds the warps' counts
-// and scans the 16 bins from the top to find the bin holding the K-th key.
-// The pass loop ends as soon as that bin's keys are all selected. A final
-// block scan places every selected ID at its ascending output position.
+// prefix is skipped). One pass = one block barrier: every thread counts its
+// candidate keys per digit in 8-bit fields, repacks them as eight 32-bit
+// words of 16-bit fields summed over the warp by redux.sync, lane 0 stores
+// the warp's counts (double-buffered by pass parity), and after the barrier
+// every warp adds the warps' counts itself and finds the bin holding the
+// K-th key, so no second barrier is needed. Once the boundary bin holds at
+// most one key per thread, its keys are compacted into shared memory and the
+// remaining passes run over that short list. The loop ends as soon as the
+// boundary bin's keys are all selected. A final block scan places every
+// selected ID at its ascending output position.
 constexpr int kSelMaxWarps = 16;
+
+// Given this thread's per-digit counts (8-bit fields, bins 0..7 in lo8,
+// 8..15 in hi8), sum them over the block and return (bin, keys above it,
+// keys in it) for the K-th largest; `buf` is this pass's count buffer.
+__device__ __forceinline__ void radix_boundary(unsigned long long lo8, unsigned long long hi8, unsigned (*buf)[8],
+                                               int kk, int& bin, int& above, int& cnt) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  unsigned w[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const unsigned xl = static_cast<unsigned>(lo8 >> (16 * i)), xh = static_cast<unsigned>(hi8 >> (16 * i));
+    w[i] = (xl & 0xffu) | ((xl & 0xff00u) << 8);
+    w[4 + i] = (xh & 0xffu) | ((xh & 0xff00u) << 8);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w[i] = __reduce_add_sync(kFull, w[i]);
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) buf[warp][i] = w[i];
+  }
+  __syncthreads();
+  // Lane i (< 16) takes bin 15 - i: an inclusive lane scan counts keys in
+  // bins >= 15 - i. Every warp does this (same result), no second barrier.
+  unsigned c = 0;
+  if (lane < 16) {
+    const int b = 15 - lane;
+    for (int ww = 0; ww < nw; ++ww) c += (buf[ww][b >> 1] >> ((b & 1) * 16)) & 0xffffu;
+  }
+  unsigned inc = c;
+#pragma unroll
+  for (int o = 1; o < 16; o <<= 1) {
+    const unsigned y = __shfl_up_sync(kFull, inc, o);
+    if (lane >= o) inc += y;
+  }
+  const unsigned excl = inc - c;
+  const unsigned hit = __ballot_sync(kFull, lane < 16 && excl < static_cast<unsigned>(kk) && inc >= static_cast<unsigned>(kk));
+  const int src = hit ? __ffs(hit) - 1 : 0;  // exactly one lane crosses when kk <= candidates
+  bin = 15 - src;
+  above = static_cast<int>(__shfl_sync(kFull, excl, src));
+  cnt = static_cast<int>(__shfl_sync(kFull, c, src));
+}
 
 template <int E, typename IdOf>
 __device__ void select_registers(const unsigned long long (&key)[E], int n, int topk, IdOf id_of, int* out,
                                  unsigned long long* keys_out) {
   static_assert(E <= 255, "per-thread digit counts use 8-bit fields");
-  __shared__ unsigned wc[kSelMaxWarps][8];
+  __shared__ unsigned wc[2][kSelMaxWarps][8];
   __shared__ unsigned long long sh_or, sh_k0;
-  __shared__ int sh_bin, sh_above, sh_cnt;
+  __shared__ unsigned long long clist[512];  // compacted boundary-bin keys (<= one per thread)
   __shared__ unsigned warp_tot[kSelMaxWarps];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nw = blockDim.x >> 5;
@@ -448,62 +493,61 @@ __device__ void select_registers(const unsigned long long (&key)[E], int n, int 
     const int hb = 63 - __clzll(diff);
     mask = (hb == 63) ? 0ull : ~((2ull << hb) - 1ull);
     prefix = k0 & mask;
+    int shift = (hb / 4) * 4;
+    int parity = 0;
+    bool compacted = false;
+    int nlist = 0;
 #pragma unroll 1
-    for (int shift = (hb / 4) * 4; shift >= 0; shift -= 4) {
-      unsigned long long lo8 = 0, hi8 = 0;  // bins 0..7 / 8..15, 8-bit fields
+    for (; shift >= 0; shift -= 4, parity ^= 1) {
+      unsigned long long lo8 = 0, hi8 = 0;
+      if (!compacted) {
 #pragma unroll
-      for (int j = 0; j < E; ++j) {
-        if (beg + j < n && (key[j] & mask) == prefix) {
-          const unsigned d = static_cast<unsigned>(key[j] >> shift) & 15u;
+        for (int j = 0; j < E; ++j) {
+          if (beg + j < n && (key[j] & mask) == prefix) {
+            const unsigned d = static_cast<unsigned>(key[j] >> shift) & 15u;
+            const unsigned long long inc = 1ull << ((d & 7u) * 8u);
+            if (d < 8) lo8 += inc; else hi8 += inc;
+          }
+        }
+      } else if (tid < nlist) {
+        const unsigned long long kt = clist[tid];
+        if ((kt & mask) == prefix) {
+          const unsigned d = static_cast<unsigned>(kt >> shift) & 15u;
           const unsigned long long inc = 1ull << ((d & 7u) * 8u);
           if (d < 8) lo8 += inc; else hi8 += inc;
         }
       }
-      // Repack as 16-bit fields (bins 2i, 2i+1 in word i) and sum over the warp.
-      unsigned w[8];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const unsigned xl = static_cast<unsigned>(lo8 >> (16 * i)), xh = static_cast<unsigned>(hi8 >> (16 * i));
-        w[i] = (xl & 0xffu) | ((xl & 0xff00u) << 8);
-        w[4 + i] = (xh & 0xffu) | ((xh & 0xff00u) << 8);
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) w[i] = __reduce_add_sync(kFull, w[i]);
-      if (lane == 0) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) wc[warp][i] = w[i];
-      }
-      __syncthreads();
-      if (warp == 0) {
-        // Lane i (< 16) takes bin 15 - i, so an inclusive lane scan counts keys
-        // in bins >= 15 - i.
-        unsigned cnt = 0;
-        if (lane < 16) {
-          const int bin = 15 - lane;
-          for (int ww = 0; ww < nw; ++ww) cnt += (wc[ww][bin >> 1] >> ((bin & 1) * 16)) & 0xffffu;
-        }
-        unsigned inc = cnt;
-#pragma unroll
-        for (int o = 1; o < 16; o <<= 1) {
-          const unsigned y = __shfl_up_sync(kFull, inc, o);
-          if (lane >= o) inc += y;
-        }
-        const unsigned excl = inc - cnt;
-        if (lane < 16 && excl < static_cast<unsigned>(kk) && inc >= static_cast<unsigned>(kk)) {
-          sh_bin = 15 - lane;
-          sh_above = static_cast<int>(excl);
-          sh_cnt = static_cast<int>(cnt);
-        }
-      }
-      __syncthreads();
-      prefix |= static_cast<unsigned long long>(sh_bin) << shift;
+      int bin, above, cnt;
+      radix_boundary(lo8, hi8, wc[parity], kk, bin, above, cnt);
+      prefix |= static_cast<unsigned long long>(bin) << shift;
       mask |= 0xFull << shift;
-      kk -= sh_above;
-      const int cnt = sh_cnt;
+      kk -= above;
 #ifdef STK_TRACE
       ++npass;
 #endif
       if (cnt == kk) { take_all = true; break; }
+      if (!compacted && cnt <= static_cast<int>(blockDim.x) && cnt <= 512 && shift >= 4) {
+        // Compact the boundary bin's keys (prefix now includes this digit).
+        unsigned mine = 0;
+#pragma unroll
+        for (int j = 0; j < E; ++j) mine += (beg + j < n && (key[j] & mask) == prefix) ? 1u : 0u;
+        unsigned inc = mine;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const unsigned y = __shfl_up_sync(kFull, inc, o);
+          if (lane >= o) inc += y;
+        }
+        if (lane == 31) warp_tot[warp] = inc;
+        __syncthreads();
+        unsigned pos = inc - mine;
+        for (int w2 = 0; w2 < warp; ++w2) pos += warp_tot[w2];
+#pragma unroll
+        for (int j = 0; j < E; ++j)
+          if (beg + j < n && (key[j] & mask) == prefix) clist[pos++] = key[j];
+        nlist = cnt;
+        compacted = true;
+        __syncthreads();
+      }
     }
   }
 #ifdef STK_TRACE

@@ -93,11 +93,11 @@ __device__ __forceinline__ void write_inactive(const JobArgs& a, long long job, 
 constexpr int kFastMaxWarps = 16;
 constexpr int kWarpPrefetch = 3;
 constexpr int kQRowsStaged = 4;  // q rows of a CTA's range staged in shared memory up front
-// Dynamic shared memory the stages may use: 160 KB, so that a scoring and a
-// Top-K CTA of a concurrently running selector still fit on the same SM
+// Dynamic shared memory the stages may use: 144 KB, so that scoring and
+// Top-K CTAs of a concurrently running selector still fit on the same SM
 // (speculation overlaps selection; a kernel holding every SM's shared
 // memory would serialise them).
-constexpr size_t kFastStageBudget = 160 * 1024;
+constexpr size_t kFastStageBudget = 144 * 1024;
 
 #ifdef STK_TRACE
 // [cta][warp][8] timeline of the block-state kernel (profiling builds only).

@@ -29,7 +29,13 @@ METHODS = {
 
 def overlap_run(selector, speculative, finish, select_stream, predict_stream):
     """Run selector() and speculative() concurrently, then finish(selected, state)
-    on the current stream (reference benchmarks/run_benchmark.py:99-118)."""
+    (reference benchmarks/run_benchmark.py:99-118); the current stream waits
+    for the result.
+
+    The finish runs on the selector's stream, directly behind the Top-K
+    kernel: the repair kernel is launched for programmatic dependent launch,
+    so it starts while Top-K drains instead of paying a kernel-boundary gap
+    (its dependency on the speculation stream stays an ordinary one)."""
     main = torch.cuda.current_stream()
     select_stream.wait_stream(main)
     predict_stream.wait_stream(main)
@@ -37,18 +43,21 @@ def overlap_run(selector, speculative, finish, select_stream, predict_stream):
         a = selector()
     with torch.cuda.stream(predict_stream):
         state = speculative()
-    main.wait_stream(select_stream)
-    main.wait_stream(predict_stream)
-    a.record_stream(main)
 
-    def record(obj):
+    def record(obj, stream):
         if isinstance(obj, torch.Tensor):
-            obj.record_stream(main)
+            obj.record_stream(stream)
         elif hasattr(obj, "__dict__"):
             for value in vars(obj).values():
-                record(value)
-    record(state)
-    return finish(a, state)
+                record(value, stream)
+    with torch.cuda.stream(select_stream):
+        select_stream.wait_stream(predict_stream)
+        record(state, select_stream)
+        out = finish(a, state)
+    main.wait_stream(select_stream)
+    record(out, main)
+    a.record_stream(main)
+    return out
 
 
 @dataclass
@@ -142,3 +151,29 @@ class SpeculativeDecoder:
 
     def close(self):
         self.graph = None
+
+
+def capture_steps(decoders):
+    """One CUDA graph that runs one decode step of every decoder in turn (for
+    example the attention of consecutive layers of one token step, which a
+    model replays as one graph). Returns (graph, outputs, selections): the
+    buffers this graph writes, one per decoder. The decoders' own single-step
+    graphs and buffers are left as they were."""
+    dev = decoders[0].q.device
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            for d in decoders:
+                d._run()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    outs, sels = [], []
+    with torch.cuda.graph(graph):
+        for d in decoders:
+            out, sel = d._run()
+            outs.append(out)
+            sels.append(sel)
+    return graph, outs, sels
+
