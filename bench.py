@@ -159,6 +159,16 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(loaded), "power_w_max": peak_power}
 
 
+def traffic_of(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu capture
+    (profiles/roofline_traffic.json), or None."""
+    p = ROOT / "profiles" / "roofline_traffic.json"
+    try:
+        return json.loads(p.read_text())[kernel]["dram_bytes_per_launch"]
+    except (OSError, KeyError, ValueError):
+        return None
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -458,7 +468,7 @@ def main():
             "roofline": {"bound": "hbm", "kernel": "jobs_fast_kernel (predicted-block attention, gqa.partials)",
                          "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                          "peak_kind": peak_kind, "us_per_launch": us_part, "bytes_per_launch": part_bytes,
-                         "traffic": None},
+                         "traffic": traffic_of("jobs_fast_kernel")},
             "clocks": clocks,
             "e2e": {"value": e2e_value, "unit": "decode-steps/s", "h2d_bytes_per_step": HQ * D * 2 + HQ * TOPK * 4,
                     "d2h_bytes_per_step": HQ * D * 4},
