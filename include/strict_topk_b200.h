@@ -194,6 +194,14 @@ STK_API int stk_block_states(const stk_kv* kv, const void* q, int q_dtype, int r
 STK_API int stk_merge_states(const float* m, const float* l, const float* u, const uint8_t* include, int rows, int s, int d,
                      float* out, void* stream);
 
+/* LSE reduction of per-slot states to one unnormalised state per row:
+ * m_out = max over included slots of m (-inf when none), l_out = sum exp(m - m_out) l,
+ * u_out = sum exp(m - m_out) u. New: the per-shard reduction of the
+ * context-parallel path, whose rows' states are then exchanged between
+ * shards and merged with stk_merge_states (kernels.py:74-91 semantics). */
+STK_API int stk_reduce_states(const float* m, const float* l, const float* u, const uint8_t* include, int rows, int s,
+                      int d, float* m_out, float* l_out, float* u_out, void* stream);
+
 /* Full speculation for one prediction mode.
  * Replaces kernels.py:450-501 speculate() incl. _group (kernels.py:94-117) and
  * the compact pipeline (_mass_only, _compact_group, _compact_values).

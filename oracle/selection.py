@@ -81,3 +81,12 @@ def shard_select(q, lo, hi, k, shards):
     sc = np.concatenate(cand_scores, axis=1)
     pick = np.lexsort((ids, -sc), axis=1)[:, :k]
     return np.sort(np.take_along_axis(ids, pick, axis=1), axis=1).astype(np.int32)
+
+
+def order_keys(scores):
+    """64-bit order keys of FP64 scores: unsigned-integer order equals score
+    order (-0 folded to +0). The candidate exchange format of the
+    context-parallel path (new; the reference selects on one GPU)."""
+    b = (np.asarray(scores, dtype=np.float64) + 0.0).view(np.uint64)
+    neg = (b >> np.uint64(63)) != 0
+    return np.where(neg, ~b, b | np.uint64(1 << 63))

@@ -193,6 +193,15 @@ int stk_merge_states(const float* m, const float* l, const float* u, const uint8
   return cuda_status(launch_merge(m, l, u, include, rows, s, d, out, static_cast<cudaStream_t>(stream)), "merge");
 }
 
+int stk_reduce_states(const float* m, const float* l, const float* u, const uint8_t* include, int rows, int s, int d,
+                      float* m_out, float* l_out, float* u_out, void* stream) {
+  if (!m || !l || !u || !m_out || !l_out || !u_out || rows <= 0 || s <= 0 || d <= 0)
+    return fail(STK_EINVAL, "bad reduce arguments");
+  return cuda_status(launch_reduce_states(m, l, u, include, rows, s, d, m_out, l_out, u_out,
+                                          static_cast<cudaStream_t>(stream)),
+                     "reduce_states");
+}
+
 size_t stk_speculate_workspace_bytes(int rows, int sp, int d, int mode) {
   if (mode != STK_PRED_COMPACT) return 0;
   // Fixed-frame low aggregation: per-slot u and |w v| rows.

@@ -149,6 +149,8 @@ int launch_merge_candidates(const MergeArgs& a, cudaStream_t stream);
 int launch_jobs(const JobArgs& a, int kv_dtype, int num_sms, cudaStream_t stream);
 int launch_merge(const float* m, const float* l, const float* u, const unsigned char* include, int rows, int s, int d,
                  float* out, cudaStream_t stream);
+int launch_reduce_states(const float* m, const float* l, const float* u, const unsigned char* include, int rows,
+                         int s, int d, float* m_out, float* l_out, float* u_out, cudaStream_t stream);
 int launch_hybrid_group(const float* m, const float* l, const float* u, int rows, int s, int d, float tau,
                         unsigned char* high, float* low_m, float* low_l, float* low_u, float* low_abs,
                         cudaStream_t stream);

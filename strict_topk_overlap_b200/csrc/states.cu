@@ -421,6 +421,57 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* m, const float*
   }
 }
 
+// LSE reduction that keeps the state unnormalised: per row, M = max over
+// included slots of m (-inf when none), Z = sum exp(m - M) l, U = sum exp(m - M) u.
+// The context-parallel path reduces each shard's per-block states to one
+// state per row this way before the shards' states are exchanged.
+__global__ void __launch_bounds__(256) reduce_states_kernel(const float* m, const float* l, const float* u,
+                                                            const unsigned char* include, int s, int d, float* m_out,
+                                                            float* l_out, float* u_out) {
+  extern __shared__ __align__(16) float rsm[];  // w[s]
+  __shared__ float sM;
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
+  float* w = rsm;
+  const long long base = static_cast<long long>(row) * s;
+  if (tid < 32) {
+    float M = neg_inf();
+    for (int i = lane; i < s; i += 32)
+      if (include == nullptr || include[base + i]) M = fmaxf(M, m[base + i]);
+    M = warp_max(M);
+    float z = 0.f;
+    for (int i = lane; i < s; i += 32) {
+      const bool inc = (include == nullptr || include[base + i]) && m[base + i] != neg_inf();
+      const float wi = inc ? expf(m[base + i] - M) : 0.f;
+      w[i] = wi;
+      z += wi * (inc ? l[base + i] : 0.f);
+    }
+    z = warp_sum(z);
+    if (lane == 0) {
+      sM = M;
+      m_out[row] = M;
+      l_out[row] = z;
+    }
+  }
+  __syncthreads();
+  for (int dd = tid; dd < d; dd += blockDim.x) {
+    const float* ur = u + base * d + dd;
+    float acc = 0.f;
+    for (int i = 0; i < s; ++i)
+      if (w[i] != 0.f) acc = fmaf(w[i], ur[static_cast<long long>(i) * d], acc);
+    u_out[static_cast<long long>(row) * d + dd] = acc;
+  }
+}
+
+int launch_reduce_states(const float* m, const float* l, const float* u, const unsigned char* include, int rows,
+                         int s, int d, float* m_out, float* l_out, float* u_out, cudaStream_t stream) {
+  const size_t smem = static_cast<size_t>(s) * 4;
+  if (smem > 200 * 1024) return -1;
+  cudaFuncSetAttribute(reduce_states_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  reduce_states_kernel<<<rows, 256, smem, stream>>>(m, l, u, include, s, d, m_out, l_out, u_out);
+  return static_cast<int>(cudaGetLastError());
+}
+
 // Hybrid grouping (kernels.py:94-117): high = mass >= tau * total mass,
 // low aggregate at low_m = max low m, absolute numerator envelope.
 __global__ void hybrid_group_kernel(const float* m, const float* l, const float* u, int s, int d, float tau,
