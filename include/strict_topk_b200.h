@@ -229,6 +229,25 @@ STK_API int stk_repair(const stk_kv* kv, const void* q, int q_dtype, int rows, i
                float min_remaining, float cancellation_tol, float max_extra_mass, int max_blocks,
                const stk_repair_out* out, int32_t* status, void* stream);
 
+/* Workspace (bytes) for stk_speculative_step: selection scratch plus the
+ * predicted blocks' FP32 states. */
+STK_API size_t stk_speculative_step_workspace_bytes(int hq, int n, int sp, int d);
+
+/* One speculative decode step of one dense request ([hkv, n, b, d] K/V,
+ * [hkv, n, d] lo/hi, per-head selection) on one stream: bound scores ->
+ * strict Top-K (selected [hq, topk], ascending) -> FP32 states of the
+ * predicted blocks pred [hq, sp] -> saved repair into out [hq, d] FP32.
+ * The predicted-block states are launched as the programmatic dependent of
+ * the Top-K kernel, so their K/V traffic overlaps the selection instead of
+ * running on a second stream, and the repair follows without a stream join.
+ * Results equal stk_select_topk + stk_block_states + stk_repair(SAVED) in
+ * sequence. Replaces the two-stream harness of
+ * benchmarks/run_benchmark.py:99-118 (selector || gqa.partials, then
+ * gqa.repair_saved, gqa.py:128-137 / 164-188) for the saved method. */
+STK_API int stk_speculative_step(const stk_kv* kv, const void* q, int q_dtype, const float* lo, const float* hi, int hq,
+                                 int topk, const void* pred, int pred64, int sp, int32_t* selected, float* out,
+                                 void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
 /* Prefetch baseline: read predicted K/V, write per-tile checksums.
  * Replaces kernels.py:553-560 touch_kv() (_touch, kernels.py:250-260).
  * out [rows, s, ceil(b * d / 1024)] FP32. */

@@ -27,7 +27,8 @@ _DTYPES = {torch.float32: STK_F32, torch.float16: STK_F16, torch.bfloat16: STK_B
 SYMBOLS = (
     "stk_abi_version", "stk_last_error", "stk_device_sm_count", "stk_bound_scores",
     "stk_select_workspace_bytes", "stk_select_topk", "stk_select_topk_static", "stk_merge_candidates", "stk_block_states",
-    "stk_merge_states", "stk_reduce_states", "stk_speculate_workspace_bytes", "stk_speculate", "stk_repair", "stk_touch_kv",
+    "stk_merge_states", "stk_reduce_states", "stk_speculate_workspace_bytes", "stk_speculate", "stk_repair",
+    "stk_speculative_step_workspace_bytes", "stk_speculative_step", "stk_touch_kv",
 )
 
 
@@ -71,6 +72,8 @@ _SIGS = {
                            _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
     "stk_repair": (_I, [C.POINTER(StkKV), _P, _I, _I, _I, _P, _I, _I, _P, _I, _I, C.POINTER(StkPrediction), _I, _F,
                         _F, _F, _I, C.POINTER(StkRepairOut), _P, _P]),
+    "stk_speculative_step_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
+    "stk_speculative_step": (_I, [C.POINTER(StkKV), _P, _I, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _SZ, _P, _P]),
     "stk_touch_kv": (_I, [C.POINTER(StkKV), _I, _I, _P, _I, _I, _P, _P]),
 }
 

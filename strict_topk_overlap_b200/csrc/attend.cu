@@ -178,7 +178,7 @@ __global__ void __launch_bounds__(kAW * 32) attend_kernel(RepairArgs a) {
   for (int dd = tid; dd < D; dd += blockDim.x) S.qv[dd] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + dd);
   // This CTA's prediction slots rank, rank + CS, ...
   const int ns = has_pred ? (a.sp - rank + CS - 1) / CS : 0;
-  if (has_pred) {
+  auto load_states = [&]() {
     const long long sr = static_cast<long long>(row) * a.sc;
     for (int i = tid; i < ns; i += blockDim.x) {
       S.rm[i] = a.pm[sr + rank + i * CS];
@@ -188,7 +188,8 @@ __global__ void __launch_bounds__(kAW * 32) attend_kernel(RepairArgs a) {
       const int si = i / D, dd = i - si * D;
       S.ru[i] = a.pu[(sr + rank + si * CS) * D + dd];
     }
-  }
+  };
+  if (has_pred && !a.chain) load_states();
   __syncthreads();
   if (has_pred)
     for (int i = tid; i < a.sp; i += blockDim.x) {
@@ -196,8 +197,9 @@ __global__ void __launch_bounds__(kAW * 32) attend_kernel(RepairArgs a) {
       if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); S.p_ids[i] = -1; continue; }
       atomicOr(&S.bitP[id >> 5], 1u << (id & 31));
     }
-  pdl_wait();  // A may come from the preceding kernel
+  pdl_wait();  // A (and, chained, the prediction states) may come from the preceding kernel
   for (int i = tid; i < a.sa; i += blockDim.x) S.a_ids[i] = load_id(a.sel, a.sel64, static_cast<long long>(row) * a.sa + i);
+  if (has_pred && a.chain) load_states();
   __syncthreads();
   AT(1);
   for (int i = tid; i < a.sa; i += blockDim.x) {
@@ -373,21 +375,23 @@ __global__ void __launch_bounds__(kAW * 32) attend_kernel(RepairArgs a) {
 // ------------------------------------------------------------------ saved repair, one CTA per row
 // The low-latency form of the saved / union repair (reference gqa_light.py:
 // one program per query head): one CTA of kLW warps per row, no cluster.
-// Everything except A — predicted IDs, q, and the row's prediction states
-// (m, l and the numerators, staged into shared memory) — is loaded before
-// waiting for the preceding kernel (the one writing A); then A's misses are
-// listed, each warp streams its misses through a private stage, the CTA's
-// threads fold the retained states (saved: P slots whose ID is in A; union:
-// all), and one merge in warp order writes the row's output.
+// Predicted IDs and q are loaded before waiting for the preceding kernel
+// (the one writing A), and so are the prediction states' m and l unless
+// that kernel also wrote them (a.chain). After the wait A's misses are
+// listed and each warp starts streaming its first miss through a private
+// stage; while those copies land, every warp folds its share of the
+// retained slots' numerators (saved: P slots whose ID is in A; union: all)
+// straight from global memory, then reduces its misses; one merge in warp
+// order writes the row's output.
 constexpr int kLW = 8;
 
 template <typename T, int DPH, bool FULL32>
 __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
   constexpr int D = 16 * DPH;
   constexpr int kChunk = 32 * D;
+  constexpr int kDL = D / 32;  // dims per lane in the retained fold
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ uint64_t bar[kLW];
-  __shared__ int sh_cnt[kLW];
   __shared__ float sh_w[kLW + 1][2];
   __shared__ int sh_total;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -396,6 +400,7 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
   const int kv = (row - r * a.hq) / a.g;
   const int nblocks = request_blocks(a.L, r);
   const int nwords = (a.max_n + 31) / 32;
+  AT(0);
   pdl_release();
 
   // Shared memory: stages [kLW][2][32][D] T, then the row's bookkeeping.
@@ -407,7 +412,6 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
     off += bytes;
     return p;
   };
-  float* pu_s = reinterpret_cast<float*>(carve(static_cast<size_t>(a.sp) * D * 4));  // [sp][D]
   float* pm_s = reinterpret_cast<float*>(carve(static_cast<size_t>(a.sp) * 4));
   float* pl_s = reinterpret_cast<float*>(carve(static_cast<size_t>(a.sp) * 4));
   long long* p_ids = reinterpret_cast<long long*>(carve(static_cast<size_t>(a.sp) * 8));
@@ -416,33 +420,34 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
   unsigned* bitP = reinterpret_cast<unsigned*>(carve(static_cast<size_t>(nwords) * 4));
   int* list = reinterpret_cast<int*>(carve(static_cast<size_t>(a.sa) * 4));
   float* qv = reinterpret_cast<float*>(carve(static_cast<size_t>(D) * 4));
-  float* wU = reinterpret_cast<float*>(carve(static_cast<size_t>(kLW + 1) * D * 4));
+  float* wU = reinterpret_cast<float*>(carve(static_cast<size_t>(kLW) * D * 4));  // miss numerators per warp
+  float* wR = reinterpret_cast<float*>(carve(static_cast<size_t>(kLW) * D * 4));  // retained numerators per warp
 
   if (lane == 0) {
     mbar_init(&bar[warp], 1);
     fence_barrier_init();
   }
-  // ---- before the wait: everything but A.
+  // ---- before the wait: everything the preceding kernel does not write.
   const long long sr = static_cast<long long>(row) * a.sp;
+  auto load_ml = [&]() {
+    for (int i = tid; i < a.sp; i += blockDim.x) {
+      pm_s[i] = a.pm[sr + i];
+      pl_s[i] = a.pl[sr + i];
+    }
+  };
   for (int i = tid; i < nwords; i += blockDim.x) { bitA[i] = 0u; bitP[i] = 0u; }
-  for (int i = tid; i < a.sp; i += blockDim.x) {
-    p_ids[i] = load_id(a.pred, a.pred64, sr + i);
-    pm_s[i] = a.pm[sr + i];
-    pl_s[i] = a.pl[sr + i];
-  }
+  for (int i = tid; i < a.sp; i += blockDim.x) p_ids[i] = load_id(a.pred, a.pred64, sr + i);
   for (int dd = tid; dd < D; dd += blockDim.x) qv[dd] = load_any(a.q, a.q_dtype, static_cast<long long>(row) * D + dd);
-  {
-    const float4* src = reinterpret_cast<const float4*>(a.pu + sr * D);
-    float4* dst = reinterpret_cast<float4*>(pu_s);
-    for (int i = tid; i < a.sp * D / 4; i += blockDim.x) dst[i] = src[i];
-  }
+  if (!a.chain) load_ml();
   __syncthreads();
   for (int i = tid; i < a.sp; i += blockDim.x) {
     const long long id = p_ids[i];
     if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); p_ids[i] = -1; continue; }
     atomicOr(&bitP[id >> 5], 1u << (id & 31));
   }
-  pdl_wait();  // A comes from the preceding kernel
+  pdl_wait();  // A (and, chained, the prediction states) come from the preceding kernel
+  AT(1);
+  if (a.chain) load_ml();
   for (int i = tid; i < a.sa; i += blockDim.x) {
     long long id = load_id(a.sel, a.sel64, static_cast<long long>(row) * a.sa + i);
     if (id < 0 || id >= nblocks) { report(a.status, kStatusBadBlockId); id = -1; }
@@ -468,6 +473,7 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
   }
   __syncthreads();
   const int count = sh_total;
+  AT(2);
 
   const int nchunks = (a.L.b + 31) / 32;
   auto issue = [&](int k, int c) {
@@ -494,29 +500,60 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
     }
   };
   if (warp < count && lane == 0) issue(warp, 0);
+  AT(3);
   // Later misses (beyond one per warp) are prefetched into L2 now.
   for (int k = kLW + tid; k < count; k += blockDim.x) prefetch_block<T>(a.L, r, kv, a_ids[list[k]], true);
 
-  // Retained slots (warp-parallel over slots, threads over dims after).
+  // Retained slots while the copies land: every warp finds their max Mr;
+  // warp w folds slots w, w + kLW, ... with weights exp(m - Mr); the last
+  // warp also records (Mr, Zr).
+  float Mr = neg_inf();
+  auto kept = [&](int c) {
+    const long long id = p_ids[c];
+    return id >= 0 && (a.variant == kVarUnion || ((bitA[id >> 5] >> (id & 31)) & 1u));
+  };
+  for (int c = lane; c < a.sp; c += 32)
+    if (kept(c)) Mr = fmaxf(Mr, pm_s[c]);
+  Mr = warp_max(Mr);
   if (warp == kLW - 1) {
-    float M = neg_inf();
-    for (int c = lane; c < a.sp; c += 32) {
-      const long long id = p_ids[c];
-      const bool keep = id >= 0 && (a.variant == kVarUnion || ((bitA[id >> 5] >> (id & 31)) & 1u));
-      if (!keep) pm_s[c] = neg_inf();
-      M = fmaxf(M, pm_s[c]);
-    }
-    M = warp_max(M);
-    // pl_s becomes the slot weight exp(m - M) (0 for slots not retained).
-    float Z = 0.f;
-    for (int c = lane; c < a.sp; c += 32) {
-      const float w = pm_s[c] != neg_inf() ? expf(pm_s[c] - M) : 0.f;
-      Z += w * pl_s[c];
-      pl_s[c] = w;
-    }
-    Z = warp_sum(Z);
-    if (lane == 0) { sh_w[kLW][0] = M; sh_w[kLW][1] = Z; }
+    float Zr = 0.f;
+    for (int c = lane; c < a.sp; c += 32)
+      if (kept(c) && pm_s[c] != neg_inf()) Zr += expf(pm_s[c] - Mr) * pl_s[c];
+    Zr = warp_sum(Zr);
+    if (lane == 0) { sh_w[kLW][0] = Mr; sh_w[kLW][1] = Zr; }
   }
+  {
+    // Eight slots' numerators are loaded before any is used (one memory
+    // round trip per eight slots, not one per slot).
+    constexpr int kBatch = 8;
+    float R[kDL];
+#pragma unroll
+    for (int j = 0; j < kDL; ++j) R[j] = 0.f;
+    for (int c0 = warp; c0 < a.sp; c0 += kLW * kBatch) {
+      float v[kBatch][kDL], w[kBatch];
+#pragma unroll
+      for (int t = 0; t < kBatch; ++t) {
+        const int c = c0 + t * kLW;
+        w[t] = 0.f;
+        if (c < a.sp) {
+          const float* pu = a.pu + (sr + c) * D;
+#pragma unroll
+          for (int j = 0; j < kDL; ++j) v[t][j] = pu[j * 32 + lane];
+          if (kept(c) && pm_s[c] != neg_inf()) w[t] = expf(pm_s[c] - Mr);
+        } else {
+#pragma unroll
+          for (int j = 0; j < kDL; ++j) v[t][j] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < kBatch; ++t)
+#pragma unroll
+        for (int j = 0; j < kDL; ++j) R[j] = fmaf(w[t], v[t][j], R[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < kDL; ++j) wR[warp * D + j * 32 + lane] = R[j];
+  }
+
   float qf[DPH];
 #pragma unroll
   for (int j = 0; j < DPH; ++j) qf[j] = qv[(lane & 15) * DPH + j];
@@ -548,6 +585,7 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
   }
   if (lane == 0) { sh_w[warp][0] = wm; sh_w[warp][1] = wl; }
   __syncthreads();
+  AT(4);
   // Final merge: warps in order, then the retained slots.
   float M = sh_w[kLW][0];
   for (int w = 0; w < kLW; ++w) M = fmaxf(M, sh_w[w][0]);
@@ -561,8 +599,7 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
       if (sh_w[w][0] != neg_inf()) U += expf(sh_w[w][0] - M) * wU[w * D + dd];
     if (kscale != 0.f) {
       float R = 0.f;
-      for (int c = 0; c < a.sp; ++c)
-        if (pl_s[c] != 0.f) R = fmaf(pl_s[c], pu_s[c * D + dd], R);
+      for (int w = 0; w < kLW; ++w) R += wR[w * D + dd];
       U += kscale * R;
     }
     a.out[static_cast<long long>(row) * D + dd] = U / fmaxf(Z, 1e-30f);
@@ -575,6 +612,7 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
     if (a.pos_out) a.pos_out[row] = count;
     if (a.total_out) a.total_out[row] = count;
   }
+  AT(7);
 }
 
 template <typename T, int DPH>
@@ -583,13 +621,14 @@ static int launch_light_t(const RepairArgs& a, cudaStream_t stream) {
   const int D = a.d;
   size_t smem = static_cast<size_t>(kLW) * 2 * 32 * D * sizeof(T);
   auto add = [&](size_t b) { smem = ((smem + 15) & ~size_t(15)) + b; };
-  add(static_cast<size_t>(a.sp) * D * 4); add(static_cast<size_t>(a.sp) * 4); add(static_cast<size_t>(a.sp) * 4);
+  add(static_cast<size_t>(a.sp) * 4); add(static_cast<size_t>(a.sp) * 4);
   add(static_cast<size_t>(a.sp) * 8); add(static_cast<size_t>(a.sa) * 8); add(static_cast<size_t>(nwords) * 4);
   add(static_cast<size_t>(nwords) * 4); add(static_cast<size_t>(a.sa) * 4); add(static_cast<size_t>(D) * 4);
-  add(static_cast<size_t>(kLW + 1) * D * 4);
+  add(static_cast<size_t>(kLW) * D * 4); add(static_cast<size_t>(kLW) * D * 4);
   if (smem > 225 * 1024) return 1;
   auto kern = a.L.b % 32 == 0 ? light_kernel<T, DPH, true> : light_kernel<T, DPH, false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  prefer_shared(kern);
   return launch_pdl(kern, dim3(static_cast<unsigned>(a.rows)), dim3(kLW * 32), smem, stream, 0, a);
 }
 
@@ -606,6 +645,7 @@ static int launch_attend_t(RepairArgs a, cudaStream_t stream) {
   if (smem > 220 * 1024) return -2;
   auto kern = a.L.b % 32 == 0 ? attend_kernel<T, DPH, true> : attend_kernel<T, DPH, false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  prefer_shared(kern);
   return launch_pdl(kern, dim3(static_cast<unsigned>(a.rows) * cs), dim3(kAW * 32), smem, stream, cs, a);
 }
 

@@ -145,13 +145,24 @@ int stk_select_topk(const void* q, int q_dtype, const float* lo, const float* hi
   a.group_select = group_select; a.scores_f32 = nullptr;
   a.scores_f64 = static_cast<double*>(workspace);
   a.status = status;
-  int rc = launch_score(a, s);
-  if (rc) return cuda_status(rc, "score");
   SelectArgs b{};
   b.scores = static_cast<const double*>(workspace);
   b.R = R; b.hsel = hsel; b.topk = topk; b.n = n;
   b.block_offsets = block_offsets; b.total_blocks = total_blocks;
   b.id_base = id_base; b.ids_out = ids_out; b.keys_out = keys_out; b.status = status;
+  // Two-stage selection (FP32 score intervals, exact FP64 only at the
+  // boundary) where an interval scorer exists; the FP64 scorer otherwise.
+  // Both give the strict Top-K of the same FP64 fixed-order scores.
+  int rc = launch_bounds(a, static_cast<float2*>(workspace), s);
+  if (rc == 0) {
+    b.bounds = static_cast<float2*>(workspace);
+    b.q = q; b.q_dtype = q_dtype; b.lo = lo; b.hi = hi;
+    b.hq = hq; b.hmeta = hmeta; b.d = d; b.group_select = group_select;
+    return cuda_status(launch_select_bounded(b, max_blocks, s), "select");
+  }
+  if (rc != 1) return cuda_status(rc, "bound scores");
+  rc = launch_score(a, s);
+  if (rc) return cuda_status(rc, "score");
   return cuda_status(launch_select(b, max_blocks, s), "select");
 }
 
@@ -296,6 +307,70 @@ int stk_repair(const stk_kv* kv, const void* q, int q_dtype, int rows, int hq, c
   a.extra = out->extra; a.pos_out = out->positive_jobs; a.total_out = out->total_jobs;
   a.status = status;
   return cuda_status(launch_repair(a, kv->kv_dtype, static_cast<cudaStream_t>(stream)), "repair");
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+size_t stk_speculative_step_workspace_bytes(int hq, int n, int sp, int d) {
+  if (hq <= 0 || n <= 0 || sp <= 0 || d <= 0) return 0;
+  const size_t slots = static_cast<size_t>(hq) * sp;
+  return align256(stk_select_workspace_bytes(hq, n)) + 2 * align256(slots * sizeof(float)) +
+         align256(slots * d * sizeof(float));
+}
+
+int stk_speculative_step(const stk_kv* kv, const void* q, int q_dtype, const float* lo, const float* hi, int hq,
+                         int topk, const void* pred, int pred64, int sp, int32_t* selected, float* out,
+                         void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  int rc = check_kv(kv, hq);
+  if (rc) return rc;
+  if (kv->page_table || kv->block_offsets) return fail(STK_EINVAL, "speculative_step takes one dense request");
+  if (!q || !lo || !hi || !pred || !selected || !out || !workspace || !valid_dtype(q_dtype))
+    return fail(STK_EINVAL, "null pointer or unsupported q dtype");
+  if (sp <= 0) return fail(STK_EINVAL, "empty prediction");
+  const int n = kv->n, d = kv->d;
+  if (workspace_bytes < stk_speculative_step_workspace_bytes(hq, n, sp, d))
+    return fail(STK_EWS, "speculative_step workspace too small");
+  unsigned char* w = static_cast<unsigned char*>(workspace);
+  const size_t sel_bytes = stk_select_workspace_bytes(hq, n);
+  const size_t slots = static_cast<size_t>(hq) * sp;
+  float* pm = reinterpret_cast<float*>(w + align256(sel_bytes));
+  float* pl = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(pm) + align256(slots * sizeof(float)));
+  float* pu = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(pl) + align256(slots * sizeof(float)));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // 1. Bound scores and strict Top-K (the scorer, then the Top-K kernel as its dependent).
+  rc = stk_select_topk(q, q_dtype, lo, hi, 1, hq, kv->hkv, n, nullptr, n, n, d, topk, 0, 0, selected, nullptr, w,
+                       sel_bytes, status, stream);
+  if (rc) return rc;
+  // 2. States of the predicted blocks, launched as the Top-K kernel's
+  //    dependent: it starts as soon as every Top-K CTA is running and streams
+  //    the predicted K/V while the selection finishes, then holds its own
+  //    completion until the Top-K grid's.
+  JobArgs a{};
+  a.L = make_layout(kv);
+  a.q = q; a.q_dtype = q_dtype;
+  a.rows = hq; a.hq = hq; a.g = hq / kv->hkv; a.d = d; a.scale = attn_scale(d);
+  a.ids = pred; a.ids64 = pred64; a.s = sp;
+  a.mode = STK_MODE_FULL; a.m = pm; a.l = pl; a.u = pu; a.status = status;
+  a.chain = 1;
+  a.sm_skip = hq;  // one Top-K CTA per selection row
+  rc = launch_jobs(a, kv->kv_dtype, sm_count_current(), st);
+  if (rc) return cuda_status(rc, "block_states (chained)");
+  // 3. Saved repair (reuse predicted hits, compute selected misses, merge),
+  //    the states' dependent: its wait covers both the states and Top-K.
+  RepairArgs r{};
+  r.L = a.L;
+  r.q = q; r.q_dtype = q_dtype;
+  r.rows = hq; r.hq = hq; r.g = a.g; r.d = d; r.scale = a.scale;
+  r.sel = selected; r.sel64 = 0; r.sa = topk;
+  r.pred = pred; r.pred64 = pred64; r.sp = sp;
+  r.pmode = STK_PRED_SAVED; r.sc = sp;
+  r.pm = pm; r.pl = pl; r.pu = pu;
+  r.variant = STK_VAR_SAVED;
+  r.max_n = n;
+  r.out = out;
+  r.status = status;
+  r.chain = 1;
+  return cuda_status(launch_repair(r, kv->kv_dtype, st), "repair (chained)");
 }
 
 int stk_touch_kv(const stk_kv* kv, int rows, int hq, const void* ids, int ids64, int s, float* out, void* stream) {

@@ -44,6 +44,14 @@ struct SelectArgs {
   int* ids_out;              // [R * hsel, topk], ascending
   unsigned long long* keys_out;  // optional: [R * hsel, topk] ordered keys of the chosen IDs
   int* status;
+  // Two-stage selection (bounds != null): FP32 score intervals from the
+  // interval scorer, exact FP64 scores recomputed for boundary blocks only.
+  float2* bounds;  // [hsel, total_blocks] (lower, upper); reused as key scratch
+  const void* q;
+  int q_dtype;
+  const float* lo;
+  const float* hi;
+  int hq, hmeta, d, group_select;
 };
 
 struct MergeArgs {
@@ -75,6 +83,15 @@ struct JobArgs {
   float* u;                     // [rows, s, d] (full, fixed)
   float* uabs;                  // [rows, s, d] (fixed, optional)
   int* status;
+  // 1: launched as the programmatic dependent of a kernel whose outputs it
+  // does not read (the Top-K of the same decode step): lets its own
+  // dependent launch at once and waits for that kernel before exiting, so
+  // that its completion implies the predecessor's.
+  int chain;
+  // Chained launches: SMs left to the predecessor (one per Top-K row); the
+  // persistent grid takes the others, with stages sized so that its CTAs do
+  // not share an SM with a Top-K CTA.
+  int sm_skip;
 };
 
 struct RepairArgs {
@@ -113,6 +130,9 @@ struct RepairArgs {
   int* pos_out;              // [rows] or null
   int* total_out;            // [rows] or null
   int* status;
+  // 1: the prediction states (pm, pl, pu) come from the immediately
+  // preceding kernel on the stream, so they are read after pdl_wait().
+  int chain;
 };
 
 // Launch `kern` with programmatic stream serialization: it may begin while
@@ -143,8 +163,22 @@ inline int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
   return static_cast<int>(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
 }
 
+// Ask for the largest shared-memory carveout for `kern`. The kernels of one
+// decode step share SMs (a dependent launch starts while its predecessor
+// runs), and an SM whose L1/shared split was set for small-smem CTAs cannot
+// take a large-smem CTA until it has drained.
+template <typename... KArgs>
+inline void prefer_shared(void (*kern)(KArgs...)) {
+  cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+}
+
 int launch_score(const ScoreArgs& a, cudaStream_t stream);
 int launch_select(const SelectArgs& a, int max_n, cudaStream_t stream);
+// Two-stage selection: returns 1 (nothing launched) when the shape has no
+// interval-scorer kernel (d not in {64, 128, 256}, unaligned metadata, or
+// more than 16 query heads per KV head).
+int launch_bounds(const ScoreArgs& a, float2* bounds, cudaStream_t stream);
+int launch_select_bounded(const SelectArgs& a, int max_n, cudaStream_t stream);
 int launch_merge_candidates(const MergeArgs& a, cudaStream_t stream);
 int launch_jobs(const JobArgs& a, int kv_dtype, int num_sms, cudaStream_t stream);
 int launch_merge(const float* m, const float* l, const float* u, const unsigned char* include, int rows, int s, int d,

@@ -814,6 +814,7 @@ static int launch_repair_t(RepairArgs a, cudaStream_t stream) {
   if (smem > 220 * 1024) return -2;
   auto kern = a.L.b % 32 == 0 ? repair_kernel<T, DPH, NST, true> : repair_kernel<T, DPH, NST, false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  prefer_shared(kern);
   const int cs = repair_cluster_size(a);
   a.cluster = cs;
   cudaLaunchConfig_t cfg = {};

@@ -650,6 +650,471 @@ __global__ void __launch_bounds__(512) merge_candidates_kernel(MergeArgs a) {
                       a.ids_out + static_cast<long long>(row) * a.topk, nullptr);
 }
 
+// ------------------------------------------------------------------ two-stage selection
+// Stage 1, the interval scorer: the FP32 score s of every (row, block) with
+// the same q-sign bound, and a rigorous radius e, written as the interval
+// [s - e, s + e] rounded outward. The exact FP64 fixed-order score lies in
+// it. Each lane sums D/4 dims with FP32 FMA (exact products, one rounding per
+// step) and two shuffle levels finish the sum, so every term passes through
+// at most D/4 + 2 roundings and |s - S| <= gamma_{D/4+2} * sum_d |q_d b_d|
+// (recursive-summation bound, Higham, "Accuracy and Stability of Numerical
+// Algorithms", 2nd ed., eq. 4.4; gamma_k = k u / (1 - k u), u = 2^-24), and
+// sum_d |q_d b_d| <= ||q||_1 * max_d max(|lo_d|, |hi_d|), with ||q||_1 summed
+// under upward rounding. The radius takes 2 (D/4 + 2) u, which also covers
+// the FP64 score's own roundings (relative 2^-53 each) and, for group
+// selection, the FP64 sum over the group; an absolute 2^-118 covers
+// underflow. Non-finite inputs give the interval (-inf, +inf).
+//
+// Stage 2, per selection row: with T the K-th largest lower end and U the
+// (K+1)-th largest upper end, a block whose upper end is below T is beaten
+// by K blocks (out); a block whose lower end is above U can be beaten, or
+// tied from a lower index, only by blocks whose upper end exceeds U — at most
+// K of them, itself included — so it is in. Only the remaining blocks, whose
+// intervals straddle the boundary (typically none to a few per row), get
+// their exact FP64 score, recomputed in the fixed order above from q and
+// lo/hi, and the best K - #in of them by (score, lower index) complete the
+// selection: the result is the strict Top-K of the FP64 scores. T and U are
+// located in 2048-bin histograms of a monotone map of the interval ends over
+// the row's range; comparing bins instead of values keeps both tests
+// conservative, so no radix passes over 64-bit keys are needed.
+
+constexpr int kBWarps = 4;
+constexpr int kBTile = kBWarps * 8;  // blocks per CTA: 8 per warp, 4 lanes per block
+
+// Per-lane FP32 sum of query head mh * G + g (and the lane's largest
+// metadata magnitude) for lanes whose request's q is not staged (tiles that
+// span more than kQReq requests): q and metadata from global memory.
+template <int C>
+__device__ __forceinline__ float2 bound_lane_global(const ScoreArgs& a, int r, int mh, int G, int g, long long gb,
+                                                 int p) {
+  constexpr int D = 32 * C;
+  const float* lr = a.lo + (static_cast<long long>(mh) * a.total_blocks + gb) * D;
+  const float* hr = a.hi + (static_cast<long long>(mh) * a.total_blocks + gb) * D;
+  const long long qoff = (static_cast<long long>(r) * a.hq + mh * G + g) * D;
+  float m = 0.f, s = 0.f;
+  for (int i = 0; i < D / 16; ++i) {
+    for (int e = 0; e < 4; ++e) {
+      const int dd = 4 * (p + 4 * i) + e;
+      const float l = lr[dd], h = hr[dd];
+      m = fmaxf(m, fmaxf(fabsf(l), fabsf(h)));
+      const float qv = load_any(a.q, a.q_dtype, qoff + dd);
+      s = fmaf(qv, qv >= 0.f ? h : l, s);
+    }
+  }
+  return make_float2(s, m);
+}
+
+template <int C, int GM>
+__global__ void __launch_bounds__(kBWarps * 32) bound_interval_kernel(ScoreArgs a, float2* __restrict__ out) {
+  constexpr int D = 32 * C;
+  constexpr int NI = D / 16;           // 16-byte chunks per lane per metadata row
+  constexpr int NBAT = NI < 8 ? NI : 8;  // chunks in flight per batch
+  constexpr float kErrFactor = 2.f * (D / 4 + 2) * 0x1p-24f;
+  extern __shared__ __align__(16) float qs[];  // [kQReq][G][D] q as float, then [kQReq][G] ||q||_1
+  const int G = a.hq / a.hmeta;
+  const int mh = blockIdx.y;
+  const int row0 = blockIdx.x * kBTile;
+  const int nrows = min(kBTile, a.total_blocks - row0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nq = kQReq * G * D;
+  float* qn1 = qs + nq;
+  ST(0);
+  pdl_release();  // the Top-K kernel may launch now; it waits for this grid to finish
+
+  // q first: loads issued behind the metadata stream would wait for it.
+  const int r0 = find_request(a.block_offsets, a.R, row0);
+  constexpr int kQPer = 8;
+  float qv[kQPer];
+#pragma unroll
+  for (int e = 0; e < kQPer; ++e) {
+    const int i = e * blockDim.x + tid;
+    qv[e] = 0.f;
+    if (i < nq) {
+      const int rr = i / (G * D), rem = i - rr * G * D;
+      if (r0 + rr < a.R) qv[e] = load_any(a.q, a.q_dtype, (static_cast<long long>(r0 + rr) * a.hq + mh * G) * D + rem);
+    }
+  }
+#ifdef STK_QFIRST
+  __syncthreads();  // every warp's q loads are issued before any metadata load
+#endif
+  // This lane's block (b) and quarter (p): chunks p, p + 4, p + 8, ... of the row.
+  const int b = lane >> 2, p = lane & 3;
+  const int rl = warp * 8 + b;
+  const bool live = rl < nrows;
+  const long long gb = row0 + (live ? rl : 0);
+  const float4* L4 = reinterpret_cast<const float4*>(a.lo + (static_cast<long long>(mh) * a.total_blocks + gb) * D);
+  const float4* H4 = reinterpret_cast<const float4*>(a.hi + (static_cast<long long>(mh) * a.total_blocks + gb) * D);
+  float4 lv[NBAT], hv[NBAT];
+#pragma unroll
+  for (int i = 0; i < NBAT; ++i) {
+    lv[i] = live ? __ldg(L4 + p + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    hv[i] = live ? __ldg(H4 + p + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int e = 0; e < kQPer; ++e) {
+    const int i = e * blockDim.x + tid;
+    if (i < nq) qs[i] = qv[e];
+  }
+  for (int i = kQPer * blockDim.x + tid; i < nq; i += blockDim.x) {  // large groups only
+    const int rr = i / (G * D), rem = i - rr * G * D;
+    qs[i] = r0 + rr < a.R ? load_any(a.q, a.q_dtype, (static_cast<long long>(r0 + rr) * a.hq + mh * G) * D + rem) : 0.f;
+  }
+  __syncthreads();
+  // ||q||_1 per staged row, rounded up at every step.
+  for (int t = warp; t < kQReq * G; t += kBWarps) {
+    float sum = 0.f;
+    for (int dd = lane; dd < D; dd += 32) sum = __fadd_ru(sum, fabsf(qs[t * D + dd]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum = __fadd_ru(sum, __shfl_xor_sync(kFull, sum, o));
+    if (lane == 0) qn1[t] = sum;
+  }
+  __syncthreads();
+  ST(1);
+
+  const int rr = (live && a.block_offsets) ? find_request(a.block_offsets, a.R, static_cast<int>(gb)) - r0 : 0;
+  float s[GM];
+#pragma unroll
+  for (int g = 0; g < GM; ++g) s[g] = 0.f;
+  float mabs = 0.f;
+  const bool staged = rr < kQReq;
+  if (__all_sync(kFull, staged)) {
+    const float* qrow = qs + rr * G * D;
+#pragma unroll
+    for (int bat = 0; bat < NI / NBAT; ++bat) {
+      if (bat > 0) {
+#pragma unroll
+        for (int i = 0; i < NBAT; ++i) {
+          lv[i] = live ? __ldg(L4 + p + 4 * (bat * NBAT + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          hv[i] = live ? __ldg(H4 + p + 4 * (bat * NBAT + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < NBAT; ++i) {
+        const float4 l = lv[i], h = hv[i];
+        mabs = fmaxf(mabs, fmaxf(fmaxf(fabsf(l.x), fabsf(h.x)), fmaxf(fabsf(l.y), fabsf(h.y))));
+        mabs = fmaxf(mabs, fmaxf(fmaxf(fabsf(l.z), fabsf(h.z)), fmaxf(fabsf(l.w), fabsf(h.w))));
+        const int off = 4 * (p + 4 * (bat * NBAT + i));
+#pragma unroll
+        for (int g = 0; g < GM; ++g) {
+          if (g < G) {
+            const float4 qq = *reinterpret_cast<const float4*>(qrow + g * D + off);
+            s[g] = fmaf(qq.x, qq.x >= 0.f ? h.x : l.x, s[g]);
+            s[g] = fmaf(qq.y, qq.y >= 0.f ? h.y : l.y, s[g]);
+            s[g] = fmaf(qq.z, qq.z >= 0.f ? h.z : l.z, s[g]);
+            s[g] = fmaf(qq.w, qq.w >= 0.f ? h.w : l.w, s[g]);
+          }
+        }
+      }
+    }
+  } else if (live) {
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      if (g < G) {
+        const float2 sm = bound_lane_global<C>(a, r0 + rr, mh, G, g, gb, p);
+        s[g] = sm.x;
+        mabs = sm.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < GM; ++g) {
+    s[g] += __shfl_xor_sync(kFull, s[g], 1);
+    s[g] += __shfl_xor_sync(kFull, s[g], 2);
+  }
+  mabs = fmaxf(mabs, __shfl_xor_sync(kFull, mabs, 1));
+  mabs = fmaxf(mabs, __shfl_xor_sync(kFull, mabs, 2));
+  ST(2);
+  if (!live) return;
+  const float inf = __int_as_float(0x7f800000);
+  if (!a.group_select) {
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      if (g < G && (g & 3) == p) {
+        const float qn = staged ? qn1[rr * G + g] : inf;
+        const float e = __fadd_ru(__fmul_ru(__fmul_ru(qn, mabs), kErrFactor), 0x1p-118f);
+        float2 iv = make_float2(__fsub_rd(s[g], e), __fadd_ru(s[g], e));
+        if (!(iv.x <= iv.y)) iv = make_float2(-inf, inf);
+        out[static_cast<long long>(mh * G + g) * a.total_blocks + gb] = iv;
+      }
+    }
+  } else if (p == 0) {
+    float gl = 0.f, gu = 0.f;
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      if (g < G) {
+        const float qn = staged ? qn1[rr * G + g] : inf;
+        const float e = __fadd_ru(__fmul_ru(__fmul_ru(qn, mabs), kErrFactor), 0x1p-118f);
+        gl = __fadd_rd(gl, __fsub_rd(s[g], e));
+        gu = __fadd_ru(gu, __fadd_ru(s[g], e));
+      }
+    }
+    float2 iv = make_float2(gl, gu);
+    if (!(iv.x <= iv.y)) iv = make_float2(-inf, inf);
+    out[static_cast<long long>(mh) * a.total_blocks + gb] = iv;
+  }
+  ST(3);
+}
+
+// Exact FP64 score of (request r, query head h, metadata row gb) in the
+// fixed order of the file header: lane l sums dims [l*c, (l+1)*c) with FP64
+// FMA from zero, then the xor butterfly 16, 8, 4, 2, 1. Warp-collective.
+__device__ __forceinline__ double exact_head_score(const SelectArgs& a, int r, int h, long long gb, int lane) {
+  const int D = a.d, c = (D + 31) / 32;
+  const int G = a.hq / a.hmeta;
+  const long long qoff = (static_cast<long long>(r) * a.hq + h) * D;
+  const long long moff = (static_cast<long long>(h / G) * a.total_blocks + gb) * D;
+  double acc = 0.0;
+  const int d1 = min((lane + 1) * c, D);
+  for (int dd = lane * c; dd < d1; ++dd) {
+    const double qv = static_cast<double>(load_any(a.q, a.q_dtype, qoff + dd));
+    acc = __fma_rn(qv, static_cast<double>(qv >= 0.0 ? a.hi[moff + dd] : a.lo[moff + dd]), acc);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(kFull, acc, off));
+  return acc;
+}
+
+// Exact order key of selection row hs (a query head, or a KV head summing
+// its query heads' scores in ascending order) at metadata row gb.
+__device__ __forceinline__ unsigned long long exact_row_key(const SelectArgs& a, int r, int hs, long long gb,
+                                                            int lane) {
+  if (!a.group_select) return order_key(exact_head_score(a, r, hs, gb, lane));
+  const int G = a.hq / a.hmeta;
+  double grp = 0.0;
+  for (int g = 0; g < G; ++g) grp = __dadd_rn(grp, exact_head_score(a, r, hs * G + g, gb, lane));
+  return order_key(grp);
+}
+
+constexpr int kHistBins = 2048;
+constexpr int kUncMax = 256;  // straddling blocks resolved by ranking; more take the radix path
+constexpr unsigned char kClsOut = 0, kClsIn = 1, kClsUnc = 2;
+
+__device__ __forceinline__ int hist_bin(float x, float mn, float scale) {
+  const int b = __float2int_rd((x - mn) * scale);  // monotone in x; NaN (0 * inf) maps to 0
+  return min(kHistBins - 1, max(0, b));
+}
+
+// Block-wide exclusive scan of one unsigned per thread (blockDim <= 512);
+// returns the exclusive prefix and writes the block total to *total.
+__device__ __forceinline__ unsigned block_exclusive_scan(unsigned v, unsigned* wsum, unsigned* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  unsigned inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_up_sync(kFull, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) wsum[warp] = inc;
+  __syncthreads();
+  unsigned before = 0, all = 0;
+  for (int w = 0; w < nw; ++w) {
+    const unsigned x = wsum[w];
+    before += w < warp ? x : 0u;
+    all += x;
+  }
+  *total = all;
+  return before + inc - v;
+}
+
+template <int E>
+__global__ void __launch_bounds__(512, 1) select_bounded_kernel(SelectArgs a) {
+  __shared__ unsigned hist[kHistBins];  // low 16 bits: lower ends; high 16 bits: upper ends
+  __shared__ unsigned wsum[2][kSelMaxWarps];
+  __shared__ float wmn[kSelMaxWarps], wmx[kSelMaxWarps];
+  __shared__ int s_bt, s_bu;
+  __shared__ int unc_pos[kUncMax];
+  __shared__ unsigned long long unc_key[kUncMax];
+  __shared__ unsigned char unc_sel[kUncMax];
+  __shared__ unsigned char cls_s[512 * E];
+  KT(0);
+#ifdef STK_TRACE
+  const long long c_start = clock64();
+#endif
+  pdl_release();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nw = blockDim.x >> 5;
+  const int row = blockIdx.x;
+  const int r = row / a.hsel, hs = row - r * a.hsel;
+  const int off = a.block_offsets ? a.block_offsets[r] : 0;
+  const int n = a.block_offsets ? a.block_offsets[r + 1] - off : a.n;
+  const int K = a.topk;
+  if (n < K || n > static_cast<int>(blockDim.x) * E) {
+    pdl_wait();
+    if (tid == 0) report(a.status, kStatusShapeOverflow);
+    return;
+  }
+  int* out = a.ids_out + static_cast<long long>(row) * K;
+  float2* src = a.bounds + static_cast<long long>(hs) * a.total_blocks + off;
+  const int beg = tid * E;
+  const float inf = __int_as_float(0x7f800000);
+
+  {
+    for (int i = tid; i < kHistBins; i += blockDim.x) hist[i] = 0u;
+    if (tid == 0) { s_bt = 0; s_bu = 0; }
+    pdl_wait();  // bounds come from the preceding interval scorer
+    float lo_[E], up_[E];
+    float mn = inf, mx = -inf;
+#pragma unroll
+    for (int j = 0; j < E; ++j) {
+      lo_[j] = inf;
+      up_[j] = -inf;
+      if (beg + j < n) {
+        const float2 v = src[beg + j];
+        lo_[j] = v.x;
+        up_[j] = v.y;
+        if (v.x > -inf) mn = fminf(mn, v.x);
+        if (v.y < inf) mx = fmaxf(mx, v.y);
+      }
+    }
+    KT(1);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(kFull, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+    }
+    if (lane == 0) { wmn[warp] = mn; wmx[warp] = mx; }
+    __syncthreads();
+    mn = wmn[0];
+    mx = wmx[0];
+    for (int w = 1; w < nw; ++w) { mn = fminf(mn, wmn[w]); mx = fmaxf(mx, wmx[w]); }
+    KT(4);
+    float scale = 0.f;
+    if (mx > mn) scale = fminf(static_cast<float>(kHistBins) / (mx - mn), 0x1p100f);
+    if (!(mn < inf)) mn = 0.f;
+
+    if (n == K) {
+      // Everything is selected.
+      for (int i = tid; i < n; i += blockDim.x) out[i] = a.id_base + i;
+    } else {
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        if (beg + j < n) {
+          atomicAdd(&hist[hist_bin(lo_[j], mn, scale)], 1u);
+          atomicAdd(&hist[hist_bin(up_[j], mn, scale)], 1u << 16);
+        }
+      }
+      __syncthreads();
+      KT(5);
+      // Suffix counts: thread t owns bins [kHistBins - (t+1)*per, kHistBins - t*per), scanned downward.
+      const int per = kHistBins / blockDim.x;
+      const int top = kHistBins - 1 - tid * per;
+      unsigned loc = 0;
+      for (int i = 0; i < per; ++i) loc += hist[top - i];
+      unsigned tot;
+      unsigned c = block_exclusive_scan(loc, wsum[0], &tot);
+      for (int i = 0; i < per; ++i) {
+        const unsigned h = hist[top - i];
+        const unsigned lo_before = c & 0xffffu, up_before = c >> 16;
+        c += h;
+        if (lo_before < static_cast<unsigned>(K) && (c & 0xffffu) >= static_cast<unsigned>(K)) s_bt = top - i;
+        if (up_before < static_cast<unsigned>(K + 1) && (c >> 16) >= static_cast<unsigned>(K + 1)) s_bu = top - i;
+      }
+      __syncthreads();
+      KT(6);
+      const int bt = s_bt, bu = s_bu;
+      // Classify: in (lower-end bin above U's bin), out (upper-end bin below T's bin), straddling.
+      unsigned char cls[E];
+      unsigned n_in = 0, n_unc = 0;
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        cls[j] = kClsOut;
+        if (beg + j < n) {
+          if (hist_bin(lo_[j], mn, scale) > bu) cls[j] = kClsIn;
+          else if (hist_bin(up_[j], mn, scale) >= bt) cls[j] = kClsUnc;
+          n_in += cls[j] == kClsIn;
+          n_unc += cls[j] == kClsUnc;
+        }
+      }
+      const unsigned packed = (n_in << 16) | n_unc;
+      const unsigned ex = block_exclusive_scan(packed, wsum[1], &tot);
+      const int total_in = static_cast<int>(tot >> 16), total_unc = static_cast<int>(tot & 0xffffu);
+      int need = K - total_in;
+      if (need < 0 || need > total_unc) {  // cannot happen for valid intervals
+        if (tid == 0) report(a.status, kStatusShapeOverflow);
+        need = max(0, min(need, total_unc));
+      }
+      KT(2);
+      if (need < total_unc && total_unc > kUncMax) {
+        // Many straddling blocks (ties, flat metadata): exact keys for all of
+        // them, written over the row's bounds slots (every thread has read its
+        // own), then the radix select over keys in = max, out = 0, straddling
+        // = exact (sure-in blocks are at most K, so all of them are taken).
+#pragma unroll
+        for (int j = 0; j < E; ++j)
+          if (beg + j < n) cls_s[beg + j] = cls[j];
+        __syncthreads();
+        unsigned long long* scratch = reinterpret_cast<unsigned long long*>(src);
+        for (int pos = warp; pos < n; pos += nw) {
+          if (cls_s[pos] != kClsUnc) continue;
+          const unsigned long long k = exact_row_key(a, r, hs, static_cast<long long>(off) + pos, lane);
+          if (lane == 0) scratch[pos] = k;
+        }
+        __syncthreads();
+        unsigned long long key[E];
+#pragma unroll
+        for (int j = 0; j < E; ++j)
+          key[j] = cls[j] == kClsIn ? ~0ull : (cls[j] == kClsUnc ? scratch[beg + j] : 0ull);
+        const int base = a.id_base;
+        select_registers<E>(key, n, K, [base](int i) { return base + i; }, out, nullptr);
+      } else {
+        unsigned idx = ex & 0xffffu;
+        if (need < total_unc) {
+#pragma unroll
+          for (int j = 0; j < E; ++j) {
+            if (cls[j] == kClsUnc) unc_pos[idx++] = beg + j;
+          }
+          __syncthreads();
+          for (int t = warp; t < total_unc; t += nw) {
+            const unsigned long long k = exact_row_key(a, r, hs, static_cast<long long>(off) + unc_pos[t], lane);
+            if (lane == 0) unc_key[t] = k;
+          }
+          __syncthreads();
+          for (int t = tid; t < total_unc; t += blockDim.x) {
+            const unsigned long long kt = unc_key[t];
+            int rank = 0;
+            for (int j = 0; j < total_unc; ++j) {
+              const unsigned long long kj = unc_key[j];
+              rank += (kj > kt || (kj == kt && j < t)) ? 1 : 0;
+            }
+            unc_sel[t] = rank < need ? 1 : 0;
+          }
+          __syncthreads();
+        }
+        // Final flags and ascending output positions.
+        idx = ex & 0xffffu;
+        unsigned mine = 0;
+        bool sel[E];
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+          sel[j] = cls[j] == kClsIn;
+          if (cls[j] == kClsUnc) {
+            sel[j] = need == total_unc ? true : unc_sel[idx] != 0;
+            ++idx;
+          }
+          mine += sel[j] ? 1u : 0u;
+        }
+        unsigned all;
+        unsigned pos = block_exclusive_scan(mine, wsum[0], &all);
+#pragma unroll
+        for (int j = 0; j < E; ++j)
+          if (sel[j]) out[pos++] = a.id_base + beg + j;
+      }
+    }
+  }
+  if (a.keys_out) {
+    __syncthreads();  // this CTA's ID writes are visible to the whole CTA
+    for (int t = warp; t < K; t += nw) {
+      const int pos = out[t] - a.id_base;
+      const unsigned long long k = exact_row_key(a, r, hs, static_cast<long long>(off) + pos, lane);
+      if (lane == 0) a.keys_out[static_cast<long long>(row) * K + t] = k;
+    }
+  }
+  KT(3);
+#ifdef STK_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 4096) g_topk_trace[blockIdx.x * 8 + 7] = clock64() - c_start;
+#endif
+}
+
 // ------------------------------------------------------------------ host side
 
 int launch_score(const ScoreArgs& a, cudaStream_t stream) {
@@ -667,6 +1132,7 @@ int launch_score(const ScoreArgs& a, cudaStream_t stream) {
                             : (a.d == 128 ? (g4 ? score_tiled_kernel<4, true> : score_tiled_kernel<4, false>)
                                           : (g4 ? score_tiled_kernel<8, true> : score_tiled_kernel<8, false>));
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      prefer_shared(kern);
       kern<<<grid, kTileWarps * 32, smem, stream>>>(a, bulk);
       return static_cast<int>(cudaGetLastError());
     }
@@ -684,13 +1150,49 @@ int launch_score(const ScoreArgs& a, cudaStream_t stream) {
   return static_cast<int>(cudaGetLastError());
 }
 
+template <int E>
+static int launch_topk_e(const SelectArgs& a, int threads, cudaStream_t stream) {
+  prefer_shared(select_topk_kernel<E>);
+  return launch_pdl(select_topk_kernel<E>, dim3(a.R * a.hsel), dim3(threads), 0, stream, 0, a);
+}
+
 int launch_select(const SelectArgs& a, int max_n, cudaStream_t stream) {
-  const int rows = a.R * a.hsel;
-  if (max_n <= 1024) return launch_pdl(select_topk_kernel<4>, dim3(rows), dim3(256), 0, stream, 0, a);
-  if (max_n <= 2048) return launch_pdl(select_topk_kernel<4>, dim3(rows), dim3(512), 0, stream, 0, a);
-  if (max_n <= 4096) return launch_pdl(select_topk_kernel<8>, dim3(rows), dim3(512), 0, stream, 0, a);
-  if (max_n <= 8192) return launch_pdl(select_topk_kernel<16>, dim3(rows), dim3(512), 0, stream, 0, a);
-  if (max_n <= 16384) return launch_pdl(select_topk_kernel<32>, dim3(rows), dim3(512), 0, stream, 0, a);
+  if (max_n <= 1024) return launch_topk_e<4>(a, 256, stream);
+  if (max_n <= 2048) return launch_topk_e<4>(a, 512, stream);
+  if (max_n <= 4096) return launch_topk_e<8>(a, 512, stream);
+  if (max_n <= 8192) return launch_topk_e<16>(a, 512, stream);
+  if (max_n <= 16384) return launch_topk_e<32>(a, 512, stream);
+  return -1;
+}
+
+int launch_bounds(const ScoreArgs& a, float2* bounds, cudaStream_t stream) {
+  const int G = a.hq / a.hmeta;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(a.lo) | reinterpret_cast<uintptr_t>(a.hi)) & 15) == 0;
+  if (!aligned || G > 16 || (a.d != 64 && a.d != 128 && a.d != 256)) return 1;
+  const size_t smem = (static_cast<size_t>(kQReq) * G * a.d + kQReq * G) * 4;
+  const dim3 grid((a.total_blocks + kBTile - 1) / kBTile, a.hmeta);
+  void (*kern)(ScoreArgs, float2*);
+  if (a.d == 64) kern = G <= 4 ? bound_interval_kernel<2, 4> : bound_interval_kernel<2, 16>;
+  else if (a.d == 128) kern = G <= 4 ? bound_interval_kernel<4, 4> : bound_interval_kernel<4, 16>;
+  else kern = G <= 4 ? bound_interval_kernel<8, 4> : bound_interval_kernel<8, 16>;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  prefer_shared(kern);
+  kern<<<grid, kBWarps * 32, smem, stream>>>(a, bounds);
+  return static_cast<int>(cudaGetLastError());
+}
+
+template <int E>
+static int launch_bounded_e(const SelectArgs& a, int threads, cudaStream_t stream) {
+  prefer_shared(select_bounded_kernel<E>);
+  return launch_pdl(select_bounded_kernel<E>, dim3(a.R * a.hsel), dim3(threads), 0, stream, 0, a);
+}
+
+int launch_select_bounded(const SelectArgs& a, int max_n, cudaStream_t stream) {
+  if (max_n <= 1024) return launch_bounded_e<4>(a, 256, stream);
+  if (max_n <= 2048) return launch_bounded_e<4>(a, 512, stream);
+  if (max_n <= 4096) return launch_bounded_e<8>(a, 512, stream);
+  if (max_n <= 8192) return launch_bounded_e<16>(a, 512, stream);
+  if (max_n <= 16384) return launch_bounded_e<32>(a, 512, stream);
   return -1;
 }
 

@@ -82,22 +82,27 @@ __device__ __forceinline__ void write_inactive(const JobArgs& a, long long job, 
 // Warp w of the CTA serves jobs j0 + w, j0 + w + nw, ... by itself:
 //   * 32 of its jobs at a time are resolved lane-parallel (one lane per job:
 //     row, block id, activity), so metadata costs one load round trip per 32
-//     jobs; lanes also ask L2 for the first kWarpPrefetch of those blocks
-//     (cp.async.bulk.prefetch.L2) and each later job is prefetched
-//     kWarpPrefetch jobs ahead, so DRAM sees the range's traffic early while
-//     a warp's single stage only has to cover an L2 round trip;
-//   * lane 0 streams the current job's whole K/V block into the warp's stage
-//     with bulk copies (one per page segment) on the warp's mbarrier, and the
-//     warp reduces it with half-warp 128-bit tiles (warp_block_state).
+//     jobs;
+//   * the warp owns NS stages (a ring): the K/V blocks of its first NS jobs
+//     are copied at once (lane 0, bulk copies, one per page segment, on the
+//     stage's mbarrier), and the copy of job k + NS is issued into job k's
+//     stage as soon as job k has been reduced, so with NS = 2 the next block
+//     is landing while the current one is reduced; jobs further ahead are
+//     prefetched into L2 (cp.async.bulk.prefetch.L2) kWarpPrefetch deep;
+//   * the warp reduces each block with half-warp 128-bit tiles
+//     (warp_block_state).
 
 constexpr int kFastMaxWarps = 16;
 constexpr int kWarpPrefetch = 3;
 constexpr int kQRowsStaged = 4;  // q rows of a CTA's range staged in shared memory up front
-// Dynamic shared memory the stages may use: 144 KB, so that scoring and
-// Top-K CTAs of a concurrently running selector still fit on the same SM
-// (speculation overlaps selection; a kernel holding every SM's shared
-// memory would serialise them).
-constexpr size_t kFastStageBudget = 144 * 1024;
+// Dynamic shared memory the stages may use: 192 KB, so that a Top-K CTA of a
+// selector that runs beside this kernel (a speculative step launches it
+// behind Top-K) still fits on the same SM.
+constexpr size_t kFastStageBudget = 192 * 1024;
+// Chained behind Top-K: stages large enough (with this kernel's static
+// shared memory) that a CTA never shares an SM with a Top-K CTA, whose SMs
+// the grid leaves free.
+constexpr size_t kChainStageBudget = 224 * 1024;
 
 #ifdef STK_TRACE
 // [cta][warp][8] timeline of the block-state kernel (profiling builds only).
@@ -112,20 +117,20 @@ extern "C" __attribute__((visibility("default"))) void* stk_trace_jobs() {
 #define JT(ev) ((void)0)
 #endif
 
-template <typename T, int DPH, int MODE, bool FULL32>
+template <typename T, int DPH, int MODE, bool FULL32, int NS>
 __global__ void __launch_bounds__(kFastMaxWarps * 32, 1) jobs_fast_kernel(JobArgs a) {
   constexpr int D = 16 * DPH;
   constexpr bool kWantV = MODE != kModeMass;
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  __shared__ uint64_t bar[kFastMaxWarps];
+  __shared__ uint64_t bar[kFastMaxWarps * NS];
   __shared__ __align__(16) float sq[kQRowsStaged * D];
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nw = blockDim.x >> 5;
   const int B = a.L.b;
   const size_t stage_elems = static_cast<size_t>(B) * D * (kWantV ? 2 : 1);
-  T* stage = reinterpret_cast<T*>(smem_raw) + warp * stage_elems;
-  uint64_t* mb = &bar[warp];
+  T* stages = reinterpret_cast<T*>(smem_raw) + static_cast<size_t>(warp) * NS * stage_elems;
+  uint64_t* mb = &bar[warp * NS];
   const unsigned bytes = static_cast<unsigned>(B) * D * sizeof(T) * (kWantV ? 2u : 1u);
 
   const int njobs = a.rows * a.s;
@@ -133,8 +138,9 @@ __global__ void __launch_bounds__(kFastMaxWarps * 32, 1) jobs_fast_kernel(JobArg
   const int j1 = static_cast<int>(static_cast<long long>(njobs) * (blockIdx.x + 1) / gridDim.x);
   const int mine = j1 - j0 > warp ? (j1 - j0 - warp + nw - 1) / nw : 0;  // jobs of this warp
   JT(0);
-  if (lane == 0) {
-    mbar_init(mb, 1);
+  if (a.chain) pdl_release();
+  if (lane < NS) {
+    mbar_init(&mb[lane], 1);
     fence_barrier_init();
   }
   // The q rows of this range are loaded before any KV traffic is queued
@@ -167,10 +173,10 @@ __global__ void __launch_bounds__(kFastMaxWarps * 32, 1) jobs_fast_kernel(JobArg
       lb = act ? bid : -1;
     }
   };
-  auto issue = [&](long long bid, int row) {
+  auto issue = [&](int slot, long long bid, int row) {
     const int r = row / a.hq;
-    mbar_arrive_expect_tx(mb, bytes);
-    issue_block_copy<T>(a.L, r, (row - r * a.hq) / a.g, bid, stage, kWantV, mb);
+    mbar_arrive_expect_tx(&mb[slot], bytes);
+    issue_block_copy<T>(a.L, r, (row - r * a.hq) / a.g, bid, stages + slot * stage_elems, kWantV, &mb[slot]);
   };
   auto prefetch_lane = [&]() {
     if (lb >= 0) {
@@ -181,35 +187,47 @@ __global__ void __launch_bounds__(kFastMaxWarps * 32, 1) jobs_fast_kernel(JobArg
 
   int base = 0;
   resolve(0);
-  __syncthreads();  // q rows staged
-  // First copy as early as possible, then the L2 window.
-  long long cb = __shfl_sync(kFull, lb, 0);
-  int crow = __shfl_sync(kFull, lrow, 0);
-  if (mine > 0 && cb >= 0 && lane == 0) issue(cb, crow);
-  if (lane >= 1 && lane < kWarpPrefetch) prefetch_lane();
+  __syncthreads();  // q rows staged, barriers initialised
+  // Ring of the next NS jobs (k .. k + NS - 1): block id (-1 inactive) and row.
+  long long fb[NS];
+  int fr[NS];
+#pragma unroll
+  for (int i = 0; i < NS; ++i) {
+    fb[i] = __shfl_sync(kFull, lb, i);
+    fr[i] = __shfl_sync(kFull, lrow, i);
+    if (i >= mine) fb[i] = -1;
+    if (fb[i] >= 0 && lane == 0) issue(i, fb[i], fr[i]);
+  }
+  // L2 window: jobs NS .. NS + kWarpPrefetch - 2 now, then one per job.
+  if (lane >= NS && lane < NS + kWarpPrefetch - 1) prefetch_lane();
   JT(1);
 
-  unsigned phase = 0;
+  unsigned phase = 0;  // bit s: parity of stage s's next completion
   float qf[DPH];
   int q_row = -1;
   int it = 0;
 #pragma unroll 1
   for (int k = 0; k < mine; ++k) {
     const int job = j0 + warp + k * nw;
-    // Metadata of job k + 1 (next batch when k + 1 crosses it).
-    if (k + 1 - base == 32) {
-      base += 32;
-      resolve(base);
-      if (lane < kWarpPrefetch) prefetch_lane();
+    const int slot = k % NS;
+    const long long cb = fb[0];
+    const int crow = fr[0];
+    // The job that will reuse this stage: k + NS.
+    const int kk = k + NS;
+    long long nb = -1;
+    int nrow = 0;
+    if (kk < mine) {
+      if (kk - base == 32) {
+        base += 32;
+        resolve(base);
+      }
+      nb = __shfl_sync(kFull, lb, kk - base);
+      nrow = __shfl_sync(kFull, lrow, kk - base);
     }
-    const int nsrc = (k + 1 - base) & 31;
-    const long long nb = __shfl_sync(kFull, lb, nsrc);
-    const int nrow = __shfl_sync(kFull, lrow, nsrc);
-    const bool has_next = k + 1 < mine;
-    // Keep the L2 window kWarpPrefetch jobs ahead.
-    if (k + kWarpPrefetch < mine && k + kWarpPrefetch - base < 32 && k + kWarpPrefetch - base >= kWarpPrefetch &&
-        lane == k + kWarpPrefetch - base)
-      prefetch_lane();
+    {
+      const int pf = k + NS + kWarpPrefetch - 1 - base;
+      if (k + NS + kWarpPrefetch - 1 < mine && pf >= 0 && pf < 32 && lane == pf) prefetch_lane();
+    }
     if (cb < 0) {
       // Inactive slot: (-inf, 0, 0) as the reference writes; repair scratch keeps no state.
       if (a.pred == nullptr) {
@@ -232,6 +250,8 @@ __global__ void __launch_bounds__(kFastMaxWarps * 32, 1) jobs_fast_kernel(JobArg
           }
         }
       }
+      // The stage is idle: start job k + NS's copy.
+      if (nb >= 0 && lane == 0) issue(slot, nb, nrow);
     } else {
       if (crow != q_row) {
         q_row = crow;
@@ -244,19 +264,23 @@ __global__ void __launch_bounds__(kFastMaxWarps * 32, 1) jobs_fast_kernel(JobArg
       }
       const float frame = MODE == kModeFixed ? a.frame[crow] : 0.f;
       if (it < 1) JT(2);
-      const bool ok = mbar_wait(mb, phase, a.status);
-      phase ^= 1u;
+      const bool ok = mbar_wait(&mb[slot], (phase >> slot) & 1u, a.status);
+      phase ^= 1u << slot;
       if (it < 2) JT(3 + 3 * it);
-      if (!ok) return;  // the copy may still be landing: leave this CTA's stage alone
+      if (!ok) {  // the copies may still be landing: leave this CTA's stages alone
+        if (a.chain) pdl_wait();
+        return;
+      }
+      const T* stage = stages + slot * stage_elems;
       float m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
 #pragma unroll
       for (int j = 0; j < DPH; ++j) { u[j] = 0.f; ua[j] = 0.f; }
-      warp_block_state<T, DPH, MODE, FULL32>(stage, stage + static_cast<size_t>(B) * D, B, qf, a.scale, frame, m, l, u, ua,
-                                     lane);
+      warp_block_state<T, DPH, MODE, FULL32>(stage, stage + static_cast<size_t>(B) * D, B, qf, a.scale, frame, m, l,
+                                             u, ua, lane);
       __syncwarp();
       if (it == 0) JT(5);
-      // The stage is free: start the next job's copy before writing results.
-      if (has_next && nb >= 0 && lane == 0) issue(nb, nrow);
+      // The stage is free: start job k + NS's copy before writing results.
+      if (nb >= 0 && lane == 0) issue(slot, nb, nrow);
       if (MODE != kModeFixed) {
         if (lane == 0) { a.m[job] = m; a.l[job] = l; }
       } else if (lane == 0 && a.l) {
@@ -268,15 +292,17 @@ __global__ void __launch_bounds__(kFastMaxWarps * 32, 1) jobs_fast_kernel(JobArg
       }
       if (it < 2) JT(4 + 3 * it);
       ++it;
-      cb = nb;
-      crow = nrow;
-      continue;
     }
-    // Inactive current job: the next copy has not been issued yet.
-    if (has_next && nb >= 0 && lane == 0) issue(nb, nrow);
-    cb = nb;
-    crow = nrow;
+    // Advance the ring.
+#pragma unroll
+    for (int i = 0; i + 1 < NS; ++i) {
+      fb[i] = fb[i + 1];
+      fr[i] = fr[i + 1];
+    }
+    fb[NS - 1] = nb;
+    fr[NS - 1] = nrow;
   }
+  if (a.chain) pdl_wait();  // this grid completes only after its predecessor
 }
 
 // ------------------------------------------------------------------ generic path
@@ -297,6 +323,7 @@ __global__ void __launch_bounds__(128) jobs_generic_kernel(JobArgs a) {
   const T* K = static_cast<const T*>(a.L.k);
   const T* V = static_cast<const T*>(a.L.v);
   const bool want_v = a.mode != kModeMass;
+  if (a.chain) pdl_release();
 
   for (long long job = static_cast<long long>(blockIdx.x) * wpc + warp; job < njobs; job += W) {
     const JobInfo ji = resolve_job(a, job, lane);
@@ -370,6 +397,7 @@ __global__ void __launch_bounds__(128) jobs_generic_kernel(JobArgs a) {
       }
     }
   }
+  if (a.chain) pdl_wait();  // this grid completes only after its predecessor
 }
 
 // ------------------------------------------------------------------ epilogues
@@ -587,21 +615,34 @@ static bool fast_eligible(const JobArgs& a, int elem) {
   return true;
 }
 
-template <typename T, int DPH, int MODE>
-static int launch_fast_t(const JobArgs& a, int num_sms, cudaStream_t stream) {
-  const size_t stage = ws_stage_bytes(a, sizeof(T));
-  size_t nw = kFastStageBudget / stage;
+static size_t stage_budget(const JobArgs& a) { return a.chain ? kChainStageBudget : kFastStageBudget; }
+
+template <typename T, int DPH, int MODE, int NS>
+static int launch_fast_ns(const JobArgs& a, int num_sms, cudaStream_t stream) {
+  const size_t stage = ws_stage_bytes(a, sizeof(T)) * NS;
+  size_t nw = stage_budget(a) / stage;
   if (nw > kFastMaxWarps) nw = kFastMaxWarps;
   const long long njobs = static_cast<long long>(a.rows) * a.s;
   long long ctas = num_sms;
+  if (a.chain && a.sm_skip > 0 && a.sm_skip <= num_sms / 2) ctas = num_sms - a.sm_skip;
   // Small problems: fewer CTAs so that no warp is left without a job.
-  if (njobs < static_cast<long long>(num_sms) * static_cast<long long>(nw)) ctas = (njobs + nw - 1) / nw;
+  if (njobs < ctas * static_cast<long long>(nw)) ctas = (njobs + nw - 1) / nw;
   if (ctas < 1) ctas = 1;
   const size_t smem = stage * nw;
-  auto kern = a.L.b % 32 == 0 ? jobs_fast_kernel<T, DPH, MODE, true> : jobs_fast_kernel<T, DPH, MODE, false>;
+  auto kern = a.L.b % 32 == 0 ? jobs_fast_kernel<T, DPH, MODE, true, NS> : jobs_fast_kernel<T, DPH, MODE, false, NS>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  prefer_shared(kern);
+  if (a.chain) return launch_pdl(kern, dim3(static_cast<unsigned>(ctas)), dim3(static_cast<unsigned>(nw * 32)), smem,
+                                 stream, 0, a);
   kern<<<static_cast<unsigned>(ctas), static_cast<unsigned>(nw * 32), smem, stream>>>(a);
   return static_cast<int>(cudaGetLastError());
+}
+
+// Two stages per warp when at least 4 warps still fit the budget, else one.
+template <typename T, int DPH, int MODE>
+static int launch_fast_t(const JobArgs& a, int num_sms, cudaStream_t stream) {
+  if (stage_budget(a) / (2 * ws_stage_bytes(a, sizeof(T))) >= 4) return launch_fast_ns<T, DPH, MODE, 2>(a, num_sms, stream);
+  return launch_fast_ns<T, DPH, MODE, 1>(a, num_sms, stream);
 }
 
 template <typename T, int MODE>
@@ -629,6 +670,7 @@ static int launch_jobs_t(const JobArgs& a, int num_sms, cudaStream_t stream) {
   const long long cap = static_cast<long long>(num_sms) * 8;
   if (ctas > cap) ctas = cap;
   if (ctas < 1) ctas = 1;
+  if (a.chain) return launch_pdl(jobs_generic_kernel<T>, dim3(static_cast<unsigned>(ctas)), dim3(128), smem, stream, 0, a);
   jobs_generic_kernel<T><<<static_cast<unsigned>(ctas), 128, smem, stream>>>(a);
   return static_cast<int>(cudaGetLastError());
 }

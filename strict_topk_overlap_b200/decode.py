@@ -3,18 +3,24 @@
 ``overlap_run`` is the drop-in for the reference's two-stream harness
 (benchmarks/run_benchmark.py:99-118): the selector runs on one side stream,
 speculation over the predicted IDs on another, the caller's stream joins both
-and runs the repair. ``SpeculativeDecoder`` packages one full decode step for
-fixed shapes and captures it (both branches and the join) in a CUDA graph, so
-a step is one graph launch; ``serial`` steps run select -> attention on one
-stream with the same kernels, which is the baseline the speculative path must
-beat.
+and runs the repair. ``speculative_step`` is the B200 form of the same step
+for the saved method: one stream, one chain of programmatically dependent
+launches (scorer -> Top-K -> predicted-block states -> repair) in which the
+predicted K/V stream starts while Top-K runs and the repair needs no stream
+join. ``SpeculativeDecoder`` packages one full decode step for fixed shapes
+and captures it in a CUDA graph, so a step is one graph launch; ``serial``
+steps run select -> attention on one stream with the same kernels, which is
+the baseline the speculative path must beat.
 """
 from __future__ import annotations
 
 from dataclasses import dataclass
 
+import ctypes as C
+
 import torch
 
+from . import _lib as L
 from . import fused, gqa, gqa_light, kernels, signed_fused
 
 # method -> (prediction mode, repair entry point)
@@ -60,6 +66,30 @@ def overlap_run(selector, speculative, finish, select_stream, predict_stream):
     return out
 
 
+def speculative_step(q, k, v, lo, hi, predicted, topk, *, out=None, selected=None, workspace=None):
+    """One saved-method speculative step on the current stream in one launch
+    chain (stk_speculative_step): returns (output FP32 [Hq, D], selected
+    int32 [Hq, topk]). Equal to gqa.select_blocks, gqa.partials and
+    gqa.repair_saved in sequence."""
+    hq, d = q.shape
+    hkv, n, b, _ = k.shape
+    sp = predicted.shape[1]
+    lib = L.load()
+    if out is None:
+        out = torch.empty((hq, d), device=q.device, dtype=torch.float32)
+    if selected is None:
+        selected = torch.empty((hq, topk), device=q.device, dtype=torch.int32)
+    need = lib.stk_speculative_step_workspace_bytes(hq, n, sp, d)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty((need,), device=q.device, dtype=torch.uint8)
+    kv = L.kv_struct(k, v)
+    rc = lib.stk_speculative_step(C.byref(kv), q.data_ptr(), L.dtype_code(q), lo.data_ptr(), hi.data_ptr(), hq, topk,
+                                  predicted.data_ptr(), L.id_is64(predicted), sp, selected.data_ptr(), out.data_ptr(),
+                                  workspace.data_ptr(), need, L.status_ptr(), L.stream_of(q))
+    L.check(rc, "speculative_step")
+    return out, selected
+
+
 @dataclass
 class StepSpec:
     """One decode step's configuration."""
@@ -101,10 +131,18 @@ class SpeculativeDecoder:
     With ``graph=True`` the whole step (both concurrent branches and the
     repair) is captured once and replayed as one CUDA-graph launch."""
 
-    def __init__(self, q, k, v, lo, hi, predicted, spec: StepSpec, *, graph: bool = True, serial: bool = False):
+    def __init__(self, q, k, v, lo, hi, predicted, spec: StepSpec, *, graph: bool = True, serial: bool = False,
+                 chained: bool = True):
         self.q, self.k, self.v, self.lo, self.hi, self.predicted = q, k, v, lo, hi, predicted
         self.spec = spec
         self.serial = serial
+        # The saved method runs as one launch chain on one stream; the other
+        # methods (and chained=False) use the two-stream harness.
+        self.chained = chained and spec.method in ("saved", "light")
+        self._ws = None
+        if self.chained:
+            need = L.load().stk_speculative_step_workspace_bytes(q.shape[0], k.shape[1], predicted.shape[1], q.shape[1])
+            self._ws = torch.empty((need,), device=q.device, dtype=torch.uint8)
         # The selector is the critical path (score -> Top-K -> repair): its
         # stream gets the higher priority when both branches want SMs.
         self._sel_stream = torch.cuda.Stream(q.device, priority=-1)
@@ -122,6 +160,9 @@ class SpeculativeDecoder:
         if self.serial:
             a = self._selector()
             return gqa.exact(self.q, self.k, self.v, a), a
+        if self.chained:
+            return speculative_step(self.q, self.k, self.v, self.lo, self.hi, self.predicted, self.spec.topk,
+                                    workspace=self._ws)
         sel_box = {}
 
         def finish(a, st):
