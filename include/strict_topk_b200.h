@@ -130,7 +130,9 @@ STK_API int stk_device_sm_count(int device);
 STK_API int stk_bound_scores(const void* q, int q_dtype, const float* lo, const float* hi, int hq, int hmeta, int n, int d,
                      float* scores, void* stream);
 
-/* Workspace (bytes) for stk_select_topk: FP64 scores of every selection row. */
+/* Workspace (bytes) for stk_select_topk: one 8-byte slot per (selection row,
+ * block) — an FP32 score interval, or an FP64 score where no interval
+ * scorer applies. */
 STK_API size_t stk_select_workspace_bytes(int sel_heads, int total_blocks);
 
 /* Score + strict Top-K, ties to the lower block ID, IDs ascending per row.
@@ -155,8 +157,8 @@ STK_API int stk_select_topk(const void* q, int q_dtype, const float* lo, const f
  * is not allowed while the stream is being captured), or a plugin host that
  * passes only inputs and outputs. No counterpart in the reference (whose
  * selector allocates its scores with torch). Same arguments and results as
- * stk_select_topk, without workspace / workspace_bytes: the FP64 scores go
- * to one static device array of STK_SELECT_STATIC_MAX_SCORES doubles (8 MiB,
+ * stk_select_topk, without workspace / workspace_bytes: the 8-byte score
+ * slots go to one static device array of STK_SELECT_STATIC_MAX_SCORES slots (8 MiB,
  * held by every GPU that loads the library until the process exits).
  * Selections needing more than that ((group_select ? hmeta : hq) x
  * total_blocks scores) return STK_EWS. Allocates nothing: no cudaMalloc,
@@ -247,6 +249,41 @@ STK_API size_t stk_speculative_step_workspace_bytes(int hq, int n, int sp, int d
 STK_API int stk_speculative_step(const stk_kv* kv, const void* q, int q_dtype, const float* lo, const float* hi, int hq,
                                  int topk, const void* pred, int pred64, int sp, int32_t* selected, float* out,
                                  void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
+/* Per-block K bounds: lo/hi [hkv, total, d] FP32 = min / max over each
+ * block's tokens (NaN propagates). total = n for one dense request (R == 1,
+ * block_offsets NULL) or total_blocks for block_offsets layouts (paged or
+ * batched dense). Replaces the prefill-time k.amin(dim=2).float(),
+ * k.amax(dim=2).float() of benchmarks/run_benchmark.py:42-43 and
+ * experiments/trace_replay.py:68. */
+STK_API int stk_build_metadata(const stk_kv* kv, int R, int total_blocks, float* lo, float* hi, int32_t* status,
+                               void* stream);
+
+/* Decode-loop append: for each request r, write k_new / v_new [R, hkv, d]
+ * (the cache's dtype) as token positions[r] of the request (block
+ * positions[r] / b, slot positions[r] % b) and fold the key into that
+ * block's lo/hi (the block's first token resets them), so metadata never has
+ * to be rebuilt. The cache described by kv must be writable. New: the
+ * reference builds metadata once, outside its timed region. */
+STK_API int stk_append_token(const stk_kv* kv, int R, int total_blocks, const void* k_new, const void* v_new,
+                             const int32_t* positions, float* lo, float* hi, int32_t* status, void* stream);
+
+#define STK_PREDICT_PREVIOUS_STEP 0
+#define STK_PREDICT_PREVIOUS_LAYER 1
+#define STK_PREDICT_RANK_INTERLEAVE 2
+
+/* Predicted block IDs for the next decode step, on the device. Replaces the
+ * policies of experiments/hisparse_cache_trace.py:40-57 predict() and
+ * experiments/predictor_rank_trace.py:37-48 interleave() (previous step's
+ * ranking; previous layer's ranking; alternating unique IDs, the step's
+ * first). step_ids [rows, ks] / layer_ids [rows, kl] are selection rows;
+ * with keys (stk_select_topk keys_out) they are ranked best first, ties to
+ * the lower position, else taken in their given order. out [rows, budget];
+ * a slot that no list can fill is -1 (the reference raises when an
+ * interleave source runs out; here the other source fills the slot). */
+STK_API int stk_predict(int policy, const int32_t* step_ids, const unsigned long long* step_keys, int ks,
+                        const int32_t* layer_ids, const unsigned long long* layer_keys, int kl, int rows,
+                        int n_blocks, int budget, int32_t* out, int32_t* status, void* stream);
 
 /* Prefetch baseline: read predicted K/V, write per-tile checksums.
  * Replaces kernels.py:553-560 touch_kv() (_touch, kernels.py:250-260).

@@ -17,6 +17,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libstk_sm100.so"
 
 STK_F32, STK_F16, STK_BF16 = 0, 1, 2
 MODE_FULL, MODE_MASS, MODE_FIXED = 0, 1, 2
+PREDICT_PREVIOUS_STEP, PREDICT_PREVIOUS_LAYER, PREDICT_RANK_INTERLEAVE = 0, 1, 2
 PRED_SAVED, PRED_HYBRID, PRED_COMPACT, PRED_NONE = 0, 1, 2, 3
 VAR_SPLIT, VAR_FUSED, VAR_SIGNED, VAR_SIGNED_FUSED, VAR_SAVED, VAR_UNION = 0, 1, 2, 3, 4, 5
 PRED_MODES = {"saved": PRED_SAVED, "hybrid": PRED_HYBRID, "compact": PRED_COMPACT}
@@ -28,7 +29,8 @@ SYMBOLS = (
     "stk_abi_version", "stk_last_error", "stk_device_sm_count", "stk_bound_scores",
     "stk_select_workspace_bytes", "stk_select_topk", "stk_select_topk_static", "stk_merge_candidates", "stk_block_states",
     "stk_merge_states", "stk_reduce_states", "stk_speculate_workspace_bytes", "stk_speculate", "stk_repair",
-    "stk_speculative_step_workspace_bytes", "stk_speculative_step", "stk_touch_kv",
+    "stk_speculative_step_workspace_bytes", "stk_speculative_step", "stk_build_metadata", "stk_append_token",
+    "stk_predict", "stk_touch_kv",
 )
 
 
@@ -74,6 +76,9 @@ _SIGS = {
                         _F, _F, _I, C.POINTER(StkRepairOut), _P, _P]),
     "stk_speculative_step_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "stk_speculative_step": (_I, [C.POINTER(StkKV), _P, _I, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _SZ, _P, _P]),
+    "stk_build_metadata": (_I, [C.POINTER(StkKV), _I, _I, _P, _P, _P, _P]),
+    "stk_append_token": (_I, [C.POINTER(StkKV), _I, _I, _P, _P, _P, _P, _P, _P, _P]),
+    "stk_predict": (_I, [_I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P, _P, _P]),
     "stk_touch_kv": (_I, [C.POINTER(StkKV), _I, _I, _P, _I, _I, _P, _P]),
 }
 

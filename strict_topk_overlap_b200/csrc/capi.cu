@@ -373,6 +373,53 @@ int stk_speculative_step(const stk_kv* kv, const void* q, int q_dtype, const flo
   return cuda_status(launch_repair(r, kv->kv_dtype, st), "repair (chained)");
 }
 
+static int metadata_rows(const stk_kv* kv, int R, int total) {
+  if (kv->block_offsets == nullptr) return R == 1 ? kv->n : -1;
+  return total;
+}
+
+int stk_build_metadata(const stk_kv* kv, int R, int total_blocks, float* lo, float* hi, int32_t* status,
+                       void* stream) {
+  int rc = check_kv(kv, kv ? kv->hkv : 1);
+  if (rc) return rc;
+  if (!lo || !hi) return fail(STK_EINVAL, "null metadata output");
+  if (R <= 0) return fail(STK_EINVAL, "R must be positive");
+  const int total = metadata_rows(kv, R, total_blocks);
+  if (total <= 0) return fail(STK_EINVAL, "one dense request (R == 1) or block_offsets with total_blocks > 0 expected");
+  (void)status;
+  return cuda_status(launch_build_metadata(make_layout(kv), R, total, kv->kv_dtype, lo, hi,
+                                           static_cast<cudaStream_t>(stream)),
+                     "build_metadata");
+}
+
+int stk_append_token(const stk_kv* kv, int R, int total_blocks, const void* k_new, const void* v_new,
+                     const int32_t* positions, float* lo, float* hi, int32_t* status, void* stream) {
+  int rc = check_kv(kv, kv ? kv->hkv : 1);
+  if (rc) return rc;
+  if (!k_new || !v_new || !positions || !lo || !hi) return fail(STK_EINVAL, "null pointer");
+  if (R <= 0) return fail(STK_EINVAL, "R must be positive");
+  const int total = metadata_rows(kv, R, total_blocks);
+  if (total <= 0) return fail(STK_EINVAL, "one dense request (R == 1) or block_offsets with total_blocks > 0 expected");
+  return cuda_status(launch_append_token(make_layout(kv), R, total, kv->kv_dtype, k_new, v_new, positions, lo, hi,
+                                         status, static_cast<cudaStream_t>(stream)),
+                     "append_token");
+}
+
+int stk_predict(int policy, const int32_t* step_ids, const unsigned long long* step_keys, int ks,
+                const int32_t* layer_ids, const unsigned long long* layer_keys, int kl, int rows, int n_blocks,
+                int budget, int32_t* out, int32_t* status, void* stream) {
+  if (policy < STK_PREDICT_PREVIOUS_STEP || policy > STK_PREDICT_RANK_INTERLEAVE) return fail(STK_EINVAL, "bad policy");
+  if (rows <= 0 || budget <= 0 || n_blocks <= 0 || !out) return fail(STK_EINVAL, "bad predict shape");
+  const bool need_step = policy != STK_PREDICT_PREVIOUS_LAYER, need_layer = policy != STK_PREDICT_PREVIOUS_STEP;
+  if (need_step && (!step_ids || ks <= 0)) return fail(STK_EINVAL, "previous-step IDs required");
+  if (need_layer && (!layer_ids || kl <= 0)) return fail(STK_EINVAL, "previous-layer IDs required");
+  return cuda_status(launch_predict(policy, need_step ? step_ids : nullptr, need_step ? step_keys : nullptr,
+                                    need_step ? ks : 0, need_layer ? layer_ids : nullptr,
+                                    need_layer ? layer_keys : nullptr, need_layer ? kl : 0, rows, n_blocks, budget,
+                                    out, status, static_cast<cudaStream_t>(stream)),
+                     "predict");
+}
+
 int stk_touch_kv(const stk_kv* kv, int rows, int hq, const void* ids, int ids64, int s, float* out, void* stream) {
   int rc = check_kv(kv, hq);
   if (rc) return rc;

@@ -10,6 +10,8 @@ enum JobMode : int { kModeFull = 0, kModeMass = 1, kModeFixed = 2 };
 
 enum PredMode : int { kPredSaved = 0, kPredHybrid = 1, kPredCompact = 2, kPredNone = 3 };
 
+enum PredictPolicy : int { kPredictPreviousStep = 0, kPredictPreviousLayer = 1, kPredictRankInterleave = 2 };
+
 enum Variant : int {
   kVarSplit = 0,        // kernels.repair: guards in the common frame
   kVarFused = 1,        // fused.repair_fused: negatives per token at low_m
@@ -180,6 +182,12 @@ int launch_select(const SelectArgs& a, int max_n, cudaStream_t stream);
 int launch_bounds(const ScoreArgs& a, float2* bounds, cudaStream_t stream);
 int launch_select_bounded(const SelectArgs& a, int max_n, cudaStream_t stream);
 int launch_merge_candidates(const MergeArgs& a, cudaStream_t stream);
+int launch_build_metadata(const KVLayout& L, int R, int total, int kv_dtype, float* lo, float* hi, cudaStream_t stream);
+int launch_append_token(const KVLayout& L, int R, int total, int kv_dtype, const void* k_new, const void* v_new,
+                        const int* pos, float* lo, float* hi, int* status, cudaStream_t stream);
+int launch_predict(int policy, const int* step_ids, const unsigned long long* step_keys, int ks, const int* layer_ids,
+                   const unsigned long long* layer_keys, int kl, int rows, int n_blocks, int budget, int* out,
+                   int* status, cudaStream_t stream);
 int launch_jobs(const JobArgs& a, int kv_dtype, int num_sms, cudaStream_t stream);
 int launch_merge(const float* m, const float* l, const float* u, const unsigned char* include, int rows, int s, int d,
                  float* out, cudaStream_t stream);
