@@ -437,10 +437,11 @@ int stk_touch_kv(const stk_kv* kv, int rows, int hq, const void* ids, int ids64,
 // decode loop must not call cudaMalloc (it can synchronise the whole device
 // and stall the other streams of the step, and it is not allowed while the
 // stream is being captured), or a plugin interface that passes only input and
-// output buffers. For them the FP64 score scratch of stk_select_topk lives in
-// one file-scope device array instead. Every GPU that loads this library
-// holds the array (STK_SELECT_STATIC_MAX_SCORES doubles, 8 MiB) until the
-// process exits.
+// output buffers. For them the score scratch of stk_select_topk (one 8-byte
+// slot per row and block: an FP32 score interval, an exact order key, or an
+// FP64 score) lives in one file-scope device array instead. Every GPU that
+// loads this library holds the array (STK_SELECT_STATIC_MAX_SCORES slots,
+// 8 MiB) until the process exits.
 //
 // In host code `g_select_scores` names a host-side stand-in, not device
 // memory, so it is never passed to a kernel. Its device address is looked up
