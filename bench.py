@@ -58,6 +58,10 @@ def parse():
     ap.add_argument("--graph-steps", type=int, default=8,
                     help="decode steps per CUDA graph in the timed loops (one per input set, like the attention "
                          "calls of consecutive layers of one token step); 1 = one graph per step")
+    ap.add_argument("--workload", choices=("c1", "batched"), default="c1",
+                    help="c1: BASELINE config 1 (default, the headline); batched: BASELINE config 3, a batch of "
+                         "paged requests split across the ranks")
+    ap.add_argument("--requests", type=int, default=64, help="batched workload: requests in the whole batch")
     ap.add_argument("--eager", action="store_true",
                     help="launch each step's kernels directly instead of replaying a CUDA graph (for per-kernel "
                          "profiler launch lists)")
@@ -271,10 +275,126 @@ def run_reference(args):
 
 # ----------------------------------------------------------------------------- our arm
 
+def run_batched(args):
+    """a batch of `--requests` requests (context U[8192, 32768]
+    tokens, multiple of 32; 16 query / 8 KV heads, D 128, bf16; paged KV, page
+    16, 32-token blocks; K 64; per-request predicted overlap ~ Beta(8, 2)).
+    Requests are split across ranks by greedy LPT on context length
+    (paged.shard_requests); each rank builds its own page pool and decodes its
+    requests, with no collective in the data path. A step is one batched
+    speculative step (selection || predicted-block states, then saved repair,
+    one CUDA graph); the serial step is selection then exact attention. Each
+    rank's KV (~5 GB at N=1) is far above L2. value = requests decoded per
+    second over the whole job (all ranks), from the max over ranks."""
+    import torch
+    rank, world, local = dist_setup("nccl")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    from strict_topk_overlap_b200 import paged
+    from strict_topk_overlap_b200.decode import overlap_run
+    HQB, PAGE = 16, 16
+    gen = torch.Generator().manual_seed(args.seed + 3)
+    lengths = [int(x) // 32 * 32 for x in (8192 + torch.rand(args.requests, generator=gen) * (32768 - 8192)).tolist()]
+    torch.manual_seed(args.seed + 5)
+    overlaps = torch.distributions.Beta(8.0, 2.0).sample((args.requests,)).tolist()
+    mine = paged.shard_requests(lengths, world)[rank]
+    ks, vs, qs = [], [], []
+    for r in mine:
+        g = torch.Generator(device=device).manual_seed(args.seed * 1000 + r)
+        n = lengths[r] // B
+        k = torch.randn(HKV, n, B, D, device=device, generator=g)
+        k += torch.randn(HKV, n, 1, D, device=device, generator=g) * 0.5
+        ks.append(k.to(torch.bfloat16))
+        vs.append(torch.randn(HKV, n, B, D, device=device, generator=g).to(torch.bfloat16))
+        qs.append(torch.randn(HQB, D, device=device, generator=g).to(torch.bfloat16))
+        del k
+    cache = paged.build_paged_cache(ks, vs, PAGE, generator=torch.Generator().manual_seed(args.seed + 11),
+                                    device=device)
+    del ks, vs
+    q = torch.cat(qs, 0).contiguous()
+    a = paged.select_blocks(q, cache, TOPK).cpu()
+    pg = torch.Generator().manual_seed(args.seed + 17)
+    rows = []
+    for i, row in enumerate(a.tolist()):
+        r = mine[i // HQB]
+        n = lengths[r] // B
+        nswap = round((1 - overlaps[r]) * TOPK)
+        chosen = set(row)
+        cand = torch.randperm(n, generator=pg).tolist()
+        repl = [x for x in cand if x not in chosen][:nswap]
+        for j, x in zip(torch.randperm(TOPK, generator=pg)[:nswap].tolist(), repl):
+            row[j] = x
+        rows.append(row)
+    p = torch.tensor(rows, dtype=torch.int32, device=device)
+    s_sel = torch.cuda.Stream(device, priority=-1)
+    s_pred = torch.cuda.Stream(device)
+
+    def spec():
+        return overlap_run(lambda: paged.select_blocks(q, cache, TOPK), lambda: paged.partials(q, cache, p),
+                           lambda sel, st: paged.repair_saved(q, cache, sel, p, st), s_sel, s_pred)
+
+    def serial():
+        return paged.exact(q, cache, paged.select_blocks(q, cache, TOPK))
+
+    graphs = {}
+    for name, fn in (("spec", spec), ("serial", serial)):
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out = fn()
+        graphs[name] = (g, out)
+    graphs["spec"][0].replay()
+    graphs["serial"][0].replay()
+    torch.cuda.synchronize()
+    assert (graphs["spec"][1] - graphs["serial"][1]).abs().max().item() <= 2e-3
+    steps = max(1, min(args.steps, 400))
+    for i in range(max(args.warmup, 3)):
+        graphs["spec"][0].replay()
+    with ClockSampler(local if not args.quick else -1) as clk:
+        barrier(world)
+        ms = time_loop(lambda i: graphs["spec"][0].replay(), steps, device)
+        barrier(world)
+    ms = max_over_ranks(ms, world, device)
+    for i in range(3):
+        graphs["serial"][0].replay()
+    barrier(world)
+    ms_ser = max_over_ranks(time_loop(lambda i: graphs["serial"][0].replay(), steps, device), world, device)
+    hbm_peak, peak_kind = peaks()
+    tokens = sum(lengths[r] for r in mine)
+    if rank == 0:
+        line = {
+            "metric": "batched decode steps (score+topk+spec attn+repair), requests decoded per second",
+            "value": args.requests * steps / (ms / 1e3), "unit": "requests/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; BASELINE config 3 distribution)",
+            "config": {"workload": f"BASELINE config 3: {args.requests} paged requests, context U[8192, 32768], "
+                                   "16q/8kv, D128, page 16, 32-token blocks, K=64, overlap ~ Beta(8,2), bf16",
+                       "parallelism": f"requests split across {world} rank(s) by LPT, no collective",
+                       "l2": f"rank 0 holds {tokens} tokens of KV ({tokens * HKV * D * 4 / 2**30:.1f} GiB, > L2)",
+                       "graph": "one CUDA graph per batched step"},
+            "serial_ms_per_step": ms_ser / steps, "speedup_vs_serial": ms_ser / ms,
+            "clocks": clk.summary(), "peak_gbs": hbm_peak, "peak_kind": peak_kind,
+        }
+        print(json.dumps(line), flush=True)
+    graphs.clear()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "batched":
+        return run_batched(args)
     import torch
     rank, world, local = dist_setup("nccl")
     device = torch.device("cuda", local)
@@ -457,9 +577,9 @@ def main():
                                    "K=64, bf16", "method": args.method, "predicted_overlap": args.overlap,
                        "l2": f"{nsets} rotating input sets x {(2 * HKV * BLOCKS * B * D * 2 + 2 * HKV * BLOCKS * D * 4) / 2**20:.0f} MiB (> 126 MB L2)",
                        "parallelism": f"request replicas x{world} (no collective in the data path)",
-                       "graph": (f"{gsteps} decode steps per CUDA graph (one per input set, replayed; selector || "
-                                 "speculation, then repair, in each step)") if gsteps > 1 else
-                                "one CUDA graph per step (selector || speculation, then repair)"},
+                       "graph": (f"{gsteps} decode steps per CUDA graph (one per input set, replayed; each step one "
+                                 "launch chain: scorer, Top-K, predicted-block states, repair)") if gsteps > 1 else
+                                "one CUDA graph per step (scorer, Top-K, predicted-block states, repair)"},
             "serial_us_per_step": us_ser, "speedup_vs_serial": us_ser / us_step,
             "one_graph_per_step_us": single or None,
             "step_algorithmic_bytes": step_bytes, "serial_algorithmic_bytes": serial_bytes,

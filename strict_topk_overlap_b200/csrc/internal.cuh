@@ -91,8 +91,9 @@ struct JobArgs {
   // that its completion implies the predecessor's.
   int chain;
   // Chained launches: SMs left to the predecessor (one per Top-K row); the
-  // persistent grid takes the others, with stages sized so that its CTAs do
-  // not share an SM with a Top-K CTA.
+  // persistent grid takes the others (a CTA of this kernel and a 512-thread
+  // Top-K CTA together exceed an SM's registers, so they could not share an
+  // SM anyway, and a static job range waiting for one would hold the grid).
   int sm_skip;
 };
 

@@ -95,14 +95,11 @@ __device__ __forceinline__ void write_inactive(const JobArgs& a, long long job, 
 constexpr int kFastMaxWarps = 16;
 constexpr int kWarpPrefetch = 3;
 constexpr int kQRowsStaged = 4;  // q rows of a CTA's range staged in shared memory up front
-// Dynamic shared memory the stages may use: 192 KB, so that a Top-K CTA of a
-// selector that runs beside this kernel (a speculative step launches it
-// behind Top-K) still fits on the same SM.
-constexpr size_t kFastStageBudget = 192 * 1024;
-// Chained behind Top-K: stages large enough (with this kernel's static
-// shared memory) that a CTA never shares an SM with a Top-K CTA, whose SMs
-// the grid leaves free.
-constexpr size_t kChainStageBudget = 224 * 1024;
+// Dynamic shared memory the stages may use: 144 KB (9 warps of 16 KiB stages
+// at C1), so that the CTAs of a selector that runs beside this kernel still
+// fit on the same SM; measured on cold inputs, more stage memory per CTA
+// (192 or 224 KB) was not faster.
+constexpr size_t kFastStageBudget = 144 * 1024;
 
 #ifdef STK_TRACE
 // [cta][warp][8] timeline of the block-state kernel (profiling builds only).
@@ -501,34 +498,44 @@ int launch_reduce_states(const float* m, const float* l, const float* u, const u
 }
 
 // Hybrid grouping (kernels.py:94-117): high = mass >= tau * total mass,
-// low aggregate at low_m = max low m, absolute numerator envelope.
+// low aggregate at low_m = max low m, absolute numerator envelope. Warp 0
+// takes the row's slots 32 at a time (lane-parallel loads, warp max / sum
+// reductions), so the row costs a few memory round trips, not one per slot;
+// then every thread folds dims.
 __global__ void hybrid_group_kernel(const float* m, const float* l, const float* u, int s, int d, float tau,
                                     unsigned char* high, float* low_m, float* low_l, float* low_u, float* low_abs) {
   extern __shared__ float hs[];  // alpha[s]
   const int row = blockIdx.x;
+  const int lane = threadIdx.x & 31;
   const long long base = static_cast<long long>(row) * s;
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {
     float gm = neg_inf();
-    for (int i = 0; i < s; ++i) gm = fmaxf(gm, m[base + i]);
+    for (int i = lane; i < s; i += 32) gm = fmaxf(gm, m[base + i]);
+    gm = warp_max(gm);
     float total = 0.f;
-    for (int i = 0; i < s; ++i) total += expf(m[base + i] - gm) * l[base + i];
+    for (int i = lane; i < s; i += 32) total += expf(m[base + i] - gm) * l[base + i];
+    total = warp_sum(total);
     float lm = neg_inf();
-    for (int i = 0; i < s; ++i) {
+    for (int i = lane; i < s; i += 32) {
       const float mass = expf(m[base + i] - gm) * l[base + i];
       const bool hi = mass >= tau * total;
       high[base + i] = hi;
       hs[i] = hi ? 0.f : 1.f;
       if (!hi) lm = fmaxf(lm, m[base + i]);
     }
+    lm = warp_max(lm);
     if (lm == neg_inf()) lm = 0.f;
     float zz = 0.f;
-    for (int i = 0; i < s; ++i) {
+    for (int i = lane; i < s; i += 32) {
       const float al = hs[i] != 0.f ? expf(m[base + i] - lm) : 0.f;
       hs[i] = al;
       zz += al * l[base + i];
     }
-    low_m[row] = lm;
-    low_l[row] = zz;
+    zz = warp_sum(zz);
+    if (lane == 0) {
+      low_m[row] = lm;
+      low_l[row] = zz;
+    }
   }
   __syncthreads();
   for (int dd = threadIdx.x; dd < d; dd += blockDim.x) {
@@ -545,39 +552,53 @@ __global__ void hybrid_group_kernel(const float* m, const float* l, const float*
 }
 
 // Compact grouping (kernels.py:281-309): capacity-C packing of high blocks in
-// predicted order with overflow spilled to the low group.
+// predicted order with overflow spilled to the low group. One warp per row,
+// slots 32 at a time; the high blocks' ranks in predicted order come from a
+// ballot prefix count carried across the chunks.
 __global__ void compact_group_kernel(const float* pm, const float* pl, const void* pred, int pred64, int s, int c,
                                      float tau, unsigned char* high, void* rids, float* low_m, float* low_l,
                                      unsigned char* overflow) {
   const int row = blockIdx.x;
-  if (threadIdx.x != 0) return;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x >= 32) return;
   const long long base = static_cast<long long>(row) * s;
   float gm = neg_inf();
-  for (int i = 0; i < s; ++i) gm = fmaxf(gm, pm[base + i]);
+  for (int i = lane; i < s; i += 32) gm = fmaxf(gm, pm[base + i]);
+  gm = warp_max(gm);
   float total = 0.f;
-  for (int i = 0; i < s; ++i) total += expf(pm[base + i] - gm) * pl[base + i];
-  int count = 0;
-  for (int i = 0; i < s; ++i) count += (expf(pm[base + i] - gm) * pl[base + i]) >= tau * total;
-  overflow[row] = count > c;
-  int rank = 0;
-  for (int cc = 0; cc < c; ++cc) store_id(rids, pred64, static_cast<long long>(row) * c + cc, -1);
+  for (int i = lane; i < s; i += 32) total += expf(pm[base + i] - gm) * pl[base + i];
+  total = warp_sum(total);
+  for (int cc = lane; cc < c; cc += 32) store_id(rids, pred64, static_cast<long long>(row) * c + cc, -1);
+  __syncwarp();
+  int rank = 0;  // high blocks before this chunk
   float lm = neg_inf();
-  for (int i = 0; i < s; ++i) {
-    bool hi = (expf(pm[base + i] - gm) * pl[base + i]) >= tau * total;
+  for (int i0 = 0; i0 < s; i0 += 32) {
+    const int i = i0 + lane;
+    bool hi = false;
+    if (i < s) hi = (expf(pm[base + i] - gm) * pl[base + i]) >= tau * total;
+    const unsigned bal = __ballot_sync(kFull, hi);
+    const int my = rank + __popc(bal & ((1u << lane) - 1)) + 1;  // 1-based rank among high blocks
     if (hi) {
-      ++rank;
-      if (rank <= c) store_id(rids, pred64, static_cast<long long>(row) * c + rank - 1, load_id(pred, pred64, base + i));
+      if (my <= c) store_id(rids, pred64, static_cast<long long>(row) * c + my - 1, load_id(pred, pred64, base + i));
       else hi = false;
     }
-    high[base + i] = hi;
-    if (!hi) lm = fmaxf(lm, pm[base + i]);
+    if (i < s) {
+      high[base + i] = hi;
+      if (!hi) lm = fmaxf(lm, pm[base + i]);
+    }
+    rank += __popc(bal);
   }
+  if (lane == 0) overflow[row] = rank > c;
+  lm = warp_max(lm);
   if (lm == neg_inf()) lm = 0.f;
   float ll = 0.f;
-  for (int i = 0; i < s; ++i)
+  for (int i = lane; i < s; i += 32)
     if (!high[base + i]) ll += expf(pm[base + i] - lm) * pl[base + i];
-  low_m[row] = lm;
-  low_l[row] = ll;
+  ll = warp_sum(ll);
+  if (lane == 0) {
+    low_m[row] = lm;
+    low_l[row] = ll;
+  }
 }
 
 // Sum per-slot vectors in slot order: out[row, :] = sum_i x[row, i, :].
@@ -615,12 +636,11 @@ static bool fast_eligible(const JobArgs& a, int elem) {
   return true;
 }
 
-static size_t stage_budget(const JobArgs& a) { return a.chain ? kChainStageBudget : kFastStageBudget; }
 
 template <typename T, int DPH, int MODE, int NS>
 static int launch_fast_ns(const JobArgs& a, int num_sms, cudaStream_t stream) {
   const size_t stage = ws_stage_bytes(a, sizeof(T)) * NS;
-  size_t nw = stage_budget(a) / stage;
+  size_t nw = kFastStageBudget / stage;
   if (nw > kFastMaxWarps) nw = kFastMaxWarps;
   const long long njobs = static_cast<long long>(a.rows) * a.s;
   long long ctas = num_sms;
@@ -638,10 +658,11 @@ static int launch_fast_ns(const JobArgs& a, int num_sms, cudaStream_t stream) {
   return static_cast<int>(cudaGetLastError());
 }
 
-// Two stages per warp when at least 4 warps still fit the budget, else one.
+// One stage per warp. Measured on cold inputs (C1), two stages per warp with
+// half the warps were slower (11.3 µs against 10.9 µs per launch): with the
+// L2 window already pulling later jobs, more warps beat deeper rings.
 template <typename T, int DPH, int MODE>
 static int launch_fast_t(const JobArgs& a, int num_sms, cudaStream_t stream) {
-  if (stage_budget(a) / (2 * ws_stage_bytes(a, sizeof(T))) >= 4) return launch_fast_ns<T, DPH, MODE, 2>(a, num_sms, stream);
   return launch_fast_ns<T, DPH, MODE, 1>(a, num_sms, stream);
 }
 
