@@ -475,14 +475,35 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
   const int count = sh_total;
   AT(2);
 
-  const int nchunks = (a.L.b + 31) / 32;
-  auto issue = [&](int k, int c) {
-    const long long bid = a_ids[list[k]];
+  // Blocks shorter than a 32-token chunk (e.g. 4-token blocks) are gathered
+  // mp = 32 / B misses to a stage: the misses are folded into one state
+  // anyway, so one reduction covers them all.
+  const int mp = (!FULL32 && a.L.b < 32 && 32 % a.L.b == 0) ? 32 / a.L.b : 1;
+  const int ngroups = (count + mp - 1) / mp;
+  const int nchunks = mp > 1 ? 1 : (a.L.b + 31) / 32;
+  auto issue = [&](int kg, int c) {
+    const T* K = static_cast<const T*>(a.L.k);
+    const T* V = static_cast<const T*>(a.L.v);
+    if (mp > 1) {
+      const int k0 = kg * mp, nk = min(mp, count - k0);
+      mbar_arrive_expect_tx(&bar[warp], static_cast<unsigned>(2 * nk * a.L.b * D * sizeof(T)));
+      const int nseg = block_nseg(a.L);
+      for (int j = 0; j < nk; ++j) {
+        const long long bid = a_ids[list[k0 + j]];
+        for (int sg = 0; sg < nseg; ++sg) {
+          const BlockSeg seg = block_seg(a.L, r, kv, bid, sg);
+          const unsigned sb = static_cast<unsigned>(seg.tokens * D * sizeof(T));
+          const size_t dst = static_cast<size_t>(j * a.L.b + sg * seg.tokens) * D;
+          bulk_g2s(stage + dst, K + seg.elem_off, sb, &bar[warp]);
+          bulk_g2s(stage + kChunk + dst, V + seg.elem_off, sb, &bar[warp]);
+        }
+      }
+      return;
+    }
+    const long long bid = a_ids[list[kg]];
     const int t0 = c * 32, ntok = FULL32 ? 32 : min(32, a.L.b - t0);
     const unsigned bytes = static_cast<unsigned>(ntok * D * sizeof(T));
     mbar_arrive_expect_tx(&bar[warp], 2 * bytes);
-    const T* K = static_cast<const T*>(a.L.k);
-    const T* V = static_cast<const T*>(a.L.v);
     if (a.L.page_table == nullptr) {
       const long long o = block_seg(a.L, r, kv, bid, 0).elem_off + static_cast<long long>(t0) * D;
       bulk_g2s(stage, K + o, bytes, &bar[warp]);
@@ -499,10 +520,10 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
       }
     }
   };
-  if (warp < count && lane == 0) issue(warp, 0);
+  if (warp < ngroups && lane == 0) issue(warp, 0);
   AT(3);
-  // Later misses (beyond one per warp) are prefetched into L2 now.
-  for (int k = kLW + tid; k < count; k += blockDim.x) prefetch_block<T>(a.L, r, kv, a_ids[list[k]], true);
+  // Later misses (beyond one stage per warp) are prefetched into L2 now.
+  for (int k = kLW * mp + tid; k < count; k += blockDim.x) prefetch_block<T>(a.L, r, kv, a_ids[list[k]], true);
 
   // Retained slots while the copies land: every warp finds their max Mr;
   // warp w folds slots w, w + kLW, ... with weights exp(m - Mr); the last
@@ -564,7 +585,7 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
   unsigned phase = 0;
   bool ok = true;
 #pragma unroll 1
-  for (int k = warp; k < count && ok; k += kLW) {
+  for (int k = warp; k < ngroups && ok; k += kLW) {
     float m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
 #pragma unroll
     for (int j = 0; j < DPH; ++j) { u[j] = 0.f; ua[j] = 0.f; }
@@ -573,12 +594,12 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
       ok = mbar_wait(&bar[warp], phase, a.status);
       phase ^= 1u;
       if (!ok) break;
-      const int ntok = FULL32 ? 32 : min(32, a.L.b - c * 32);
+      const int ntok = mp > 1 ? a.L.b * min(mp, count - k * mp) : (FULL32 ? 32 : min(32, a.L.b - c * 32));
       warp_block_state<T, DPH, kModeFull, FULL32>(stage, stage + kChunk, ntok, qf, a.scale, 0.f, m, l, u, ua, lane);
       __syncwarp();
       if (lane == 0) {
         if (c + 1 < nchunks) issue(k, c + 1);
-        else if (k + kLW < count) issue(k + kLW, 0);
+        else if (k + kLW < ngroups) issue(k + kLW, 0);
       }
     }
     if (ok) fold_state<DPH>(wm, wl, myU, m, l, u, lane);

@@ -885,8 +885,46 @@ __device__ __forceinline__ unsigned long long exact_row_key(const SelectArgs& a,
   return order_key(grp);
 }
 
+// The same exact key with the row's query heads staged in shared memory as
+// FP32 (qsm [heads][D], heads = G for group rows, else 1) and the block's
+// metadata loaded once for all heads: one memory round trip per block. For
+// the interval path only (D <= 256, so each lane owns at most 8 dims).
+__device__ __forceinline__ unsigned long long exact_row_key_staged(const SelectArgs& a, int hs, long long gb, int lane,
+                                                                   const float* qsm) {
+  const int D = a.d, c = (D + 31) / 32;
+  const int G = a.hq / a.hmeta;
+  const int heads = a.group_select ? G : 1;
+  const int mh = a.group_select ? hs : hs / G;
+  const long long moff = (static_cast<long long>(mh) * a.total_blocks + gb) * D;
+  float lo_r[8], hi_r[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int dd = lane * c + e;
+    lo_r[e] = (e < c && dd < D) ? a.lo[moff + dd] : 0.f;
+    hi_r[e] = (e < c && dd < D) ? a.hi[moff + dd] : 0.f;
+  }
+  double grp = 0.0;
+  for (int g = 0; g < heads; ++g) {
+    double acc = 0.0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int dd = lane * c + e;
+      if (e < c && dd < D) {
+        const double qv = static_cast<double>(qsm[g * D + dd]);
+        acc = __fma_rn(qv, static_cast<double>(qv >= 0.0 ? hi_r[e] : lo_r[e]), acc);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(kFull, acc, off));
+    if (!a.group_select) return order_key(acc);
+    grp = __dadd_rn(grp, acc);
+  }
+  return order_key(grp);
+}
+
 constexpr int kHistBins = 2048;
 constexpr int kUncMax = 256;  // straddling blocks resolved by ranking; more take the radix path
+constexpr int kQStage = 2048;  // staged query floats per Top-K CTA (heads x D)
 constexpr unsigned char kClsOut = 0, kClsIn = 1, kClsUnc = 2;
 
 __device__ __forceinline__ int hist_bin(float x, float mn, float scale) {
@@ -926,6 +964,7 @@ __global__ void __launch_bounds__(512, 1) select_bounded_kernel(SelectArgs a) {
   __shared__ unsigned long long unc_key[kUncMax];
   __shared__ unsigned char unc_sel[kUncMax];
   __shared__ unsigned char cls_s[512 * E];
+  __shared__ __align__(16) float qsm[kQStage];  // the row's query heads, FP32, for exact rescoring
   KT(0);
 #ifdef STK_TRACE
   const long long c_start = clock64();
@@ -947,10 +986,21 @@ __global__ void __launch_bounds__(512, 1) select_bounded_kernel(SelectArgs a) {
   float2* src = a.bounds + static_cast<long long>(hs) * a.total_blocks + off;
   const int beg = tid * E;
   const float inf = __int_as_float(0x7f800000);
+  const int G = a.hq / a.hmeta;
+  const int q_heads = a.group_select ? G : 1;
+  const bool q_staged = q_heads * a.d <= kQStage;
+  auto row_key = [&](long long gb) {
+    return q_staged ? exact_row_key_staged(a, hs, gb, lane, qsm) : exact_row_key(a, r, hs, gb, lane);
+  };
 
   {
     for (int i = tid; i < kHistBins; i += blockDim.x) hist[i] = 0u;
     if (tid == 0) { s_bt = 0; s_bu = 0; }
+    if (q_staged) {
+      // q is an input, not the scorer's output: staged before the wait.
+      const long long q0 = (static_cast<long long>(r) * a.hq + (a.group_select ? hs * G : hs)) * a.d;
+      for (int i = tid; i < q_heads * a.d; i += blockDim.x) qsm[i] = load_any(a.q, a.q_dtype, q0 + i);
+    }
     pdl_wait();  // bounds come from the preceding interval scorer
     float lo_[E], up_[E];
     float mn = inf, mx = -inf;
@@ -1046,7 +1096,7 @@ __global__ void __launch_bounds__(512, 1) select_bounded_kernel(SelectArgs a) {
         unsigned long long* scratch = reinterpret_cast<unsigned long long*>(src);
         for (int pos = warp; pos < n; pos += nw) {
           if (cls_s[pos] != kClsUnc) continue;
-          const unsigned long long k = exact_row_key(a, r, hs, static_cast<long long>(off) + pos, lane);
+          const unsigned long long k = row_key(static_cast<long long>(off) + pos);
           if (lane == 0) scratch[pos] = k;
         }
         __syncthreads();
@@ -1065,7 +1115,7 @@ __global__ void __launch_bounds__(512, 1) select_bounded_kernel(SelectArgs a) {
           }
           __syncthreads();
           for (int t = warp; t < total_unc; t += nw) {
-            const unsigned long long k = exact_row_key(a, r, hs, static_cast<long long>(off) + unc_pos[t], lane);
+            const unsigned long long k = row_key(static_cast<long long>(off) + unc_pos[t]);
             if (lane == 0) unc_key[t] = k;
           }
           __syncthreads();
@@ -1105,7 +1155,7 @@ __global__ void __launch_bounds__(512, 1) select_bounded_kernel(SelectArgs a) {
     __syncthreads();  // this CTA's ID writes are visible to the whole CTA
     for (int t = warp; t < K; t += nw) {
       const int pos = out[t] - a.id_base;
-      const unsigned long long k = exact_row_key(a, r, hs, static_cast<long long>(off) + pos, lane);
+      const unsigned long long k = row_key(static_cast<long long>(off) + pos);
       if (lane == 0) a.keys_out[static_cast<long long>(row) * K + t] = k;
     }
   }

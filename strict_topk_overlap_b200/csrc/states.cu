@@ -659,8 +659,10 @@ static int launch_fast_ns(const JobArgs& a, int num_sms, cudaStream_t stream) {
 }
 
 // One stage per warp. Measured on cold inputs (C1), two stages per warp with
-// half the warps were slower (11.3 µs against 10.9 µs per launch): with the
-// L2 window already pulling later jobs, more warps beat deeper rings.
+// half the warps were slower (11.3 µs against 10.9 µs per launch); with the
+// L2 window already pulling later jobs, more warps beat deeper rings. For
+// 4-token blocks an eight-stage ring was slower still
+// (114 µs against 73 µs per launch).
 template <typename T, int DPH, int MODE>
 static int launch_fast_t(const JobArgs& a, int num_sms, cudaStream_t stream) {
   return launch_fast_ns<T, DPH, MODE, 1>(a, num_sms, stream);

@@ -8,7 +8,7 @@ from __future__ import annotations
 
 from . import _lib as L
 from . import gqa
-from .kernels import Prediction, _run_repair
+from .kernels import Prediction, _run_repair, merge_partials
 
 
 def partials(q, k, v, selected):
@@ -16,7 +16,14 @@ def partials(q, k, v, selected):
 
 
 def exact(q, k, v, selected):
-    gqa._shape(q, k, v, selected)
+    """Attention over the selected blocks. Tiny blocks (<= 8 tokens: the
+    shape this module serves) take the reference's own structure,
+    per-block states then one merge (gqa_hierarchical.py:111-112, 99-109), where the
+    state kernel keeps eight blocks in flight per warp; larger blocks use the
+    one-launch attention."""
+    h, n, b, d, group, sa = gqa._shape(q, k, v, selected)
+    if b <= 8:
+        return merge_partials(gqa.partials(q, k, v, selected))
     out, *_ = _run_repair(q, k, v, selected, None, None, L.VAR_SAVED)
     return out
 

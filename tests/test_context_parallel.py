@@ -225,3 +225,56 @@ def test_context_parallel_device_emulated_ranks(world):
         so, ssel = spec[r]
         assert np.array_equal(ssel.numpy(), ids)
         assert (so - o).abs().max().item() <= 1e-5
+
+
+def _nccl_worker(rank, world, port, out):
+    import cases as C
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        hq, hkv, n, b, d, topk = 32, 8, 512, 64, 128, 64
+        q, k, v, lo, hi = C.synthetic_kv(hq, hkv, n, b, d, torch.bfloat16, seed=4)
+        s, e = shard_range(n, rank, world)
+        dev = torch.device("cuda", rank)
+        sh = [t[:, s:e].contiguous().to(dev) for t in (k, v, lo, hi)]
+        o, sel = decode_step(q.to(dev), *sh, topk, n)
+        torch.cuda.synchronize()
+        out.put((rank, o.cpu().numpy(), sel.cpu().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_context_parallel_over_nccl_two_gpus():
+    """Two processes, one GPU each, exchanging candidates and states with NCCL:
+    selection bit-identical to single-GPU selection on both ranks, output
+    within the bf16 bar of the FP64 oracle."""
+    import cases as C
+    from oracle import attention as OA
+    from oracle import selection as OS
+    hq, hkv, n, b, d, topk = 32, 8, 512, 64, 128, 64
+    q, k, v, lo, hi = C.synthetic_kv(hq, hkv, n, b, d, torch.bfloat16, seed=4)
+    ids = OS.select_blocks(q.float().numpy(), lo.numpy(), hi.numpy(), topk)
+    ref = OA.attention_fp64(q.float().numpy(), k.float().numpy(), v.float().numpy(), ids)
+    ctx = mp.get_context("spawn")
+    qu = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, qu)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        r, o, sel = qu.get(timeout=240)
+        got[r] = (o, sel)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(2):
+        o, sel = got[r]
+        assert np.array_equal(sel, ids)
+        assert (np.abs(o - ref) <= 2e-3 + 1e-2 * np.abs(ref)).all()
