@@ -79,6 +79,9 @@ def dist_setup(backend):
     if world > 1:
         from datetime import timedelta
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        # NCCL writes its debug output (its version banner included) to stdout;
+        # rank 0's stdout is the JSON line only.
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         if backend == "nccl":
             torch.cuda.set_device(local)
             dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
