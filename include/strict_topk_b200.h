@@ -285,6 +285,20 @@ STK_API int stk_predict(int policy, const int32_t* step_ids, const unsigned long
                         const int32_t* layer_ids, const unsigned long long* layer_keys, int kl, int rows,
                         int n_blocks, int budget, int32_t* out, int32_t* status, void* stream);
 
+/* Workspace (bytes) for stk_group_attention. */
+STK_API size_t stk_group_attention_workspace_bytes(int hq, int sa, int b, int d);
+
+/* Attention of every query head over its KV group's shared block list, on
+ * the tensor cores: the hq / hkv (<= 16) query heads of a KV head form one
+ * MMA tile, so each listed K/V block is read once per group. One dense
+ * request, q and K/V both bf16 or both f16, d 64 or 128, b dividing 256;
+ * group_ids [hkv, sa] int32; out [hq, d] FP32 (normalised). Replaces, for
+ * shared lists (select_blocks_shared), the per-head partials and merge of
+ * gqa_hierarchical.py:55-112 and gqa.py:140-142. */
+STK_API int stk_group_attention(const stk_kv* kv, const void* q, int q_dtype, int hq, const int32_t* group_ids,
+                                int sa, float* out, void* workspace, size_t workspace_bytes, int32_t* status,
+                                void* stream);
+
 /* Prefetch baseline: read predicted K/V, write per-tile checksums.
  * Replaces kernels.py:553-560 touch_kv() (_touch, kernels.py:250-260).
  * out [rows, s, ceil(b * d / 1024)] FP32. */

@@ -30,7 +30,7 @@ SYMBOLS = (
     "stk_select_workspace_bytes", "stk_select_topk", "stk_select_topk_static", "stk_merge_candidates", "stk_block_states",
     "stk_merge_states", "stk_reduce_states", "stk_speculate_workspace_bytes", "stk_speculate", "stk_repair",
     "stk_speculative_step_workspace_bytes", "stk_speculative_step", "stk_build_metadata", "stk_append_token",
-    "stk_predict", "stk_touch_kv",
+    "stk_predict", "stk_group_attention_workspace_bytes", "stk_group_attention", "stk_touch_kv",
 )
 
 
@@ -79,6 +79,8 @@ _SIGS = {
     "stk_build_metadata": (_I, [C.POINTER(StkKV), _I, _I, _P, _P, _P, _P]),
     "stk_append_token": (_I, [C.POINTER(StkKV), _I, _I, _P, _P, _P, _P, _P, _P, _P]),
     "stk_predict": (_I, [_I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P, _P, _P]),
+    "stk_group_attention_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
+    "stk_group_attention": (_I, [C.POINTER(StkKV), _P, _I, _I, _P, _I, _P, _P, _SZ, _P, _P]),
     "stk_touch_kv": (_I, [C.POINTER(StkKV), _I, _I, _P, _I, _I, _P, _P]),
 }
 

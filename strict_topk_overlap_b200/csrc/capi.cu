@@ -420,6 +420,40 @@ int stk_predict(int policy, const int32_t* step_ids, const unsigned long long* s
                      "predict");
 }
 
+size_t stk_group_attention_workspace_bytes(int hq, int sa, int b, int d) {
+  if (hq <= 0 || sa <= 0 || b <= 0 || d <= 0) return 0;
+  const size_t slots = static_cast<size_t>(hq) * group_mma_splits(sa, b);
+  return align256(slots * sizeof(float)) * 2 + align256(slots * d * sizeof(float));
+}
+
+int stk_group_attention(const stk_kv* kv, const void* q, int q_dtype, int hq, const int32_t* group_ids, int sa,
+                        float* out, void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  int rc = check_kv(kv, hq);
+  if (rc) return rc;
+  if (!q || !group_ids || !out || !workspace) return fail(STK_EINVAL, "null pointer");
+  if (kv->page_table || kv->block_offsets) return fail(STK_EINVAL, "group attention takes one dense request");
+  if (q_dtype != kv->kv_dtype || (q_dtype != STK_BF16 && q_dtype != STK_F16))
+    return fail(STK_EINVAL, "group attention needs q and K/V in the same 16-bit type (bf16 or f16)");
+  if (kv->d != 64 && kv->d != 128) return fail(STK_EDIM, "group attention supports head dim 64 or 128, not %d", kv->d);
+  const int G = hq / kv->hkv;
+  if (G > 16) return fail(STK_EINVAL, "group attention tiles at most 16 query heads per KV head, not %d", G);
+  if (256 % kv->b) return fail(STK_EINVAL, "block size %d must divide 256", kv->b);
+  if (sa <= 0) return fail(STK_EINVAL, "empty block list");
+  if ((reinterpret_cast<uintptr_t>(kv->k) | reinterpret_cast<uintptr_t>(kv->v)) & 15)
+    return fail(STK_EINVAL, "K/V must be 16-byte aligned");
+  if (workspace_bytes < stk_group_attention_workspace_bytes(hq, sa, kv->b, kv->d))
+    return fail(STK_EWS, "group attention workspace too small");
+  const int splits = group_mma_splits(sa, kv->b);
+  const size_t slots = static_cast<size_t>(hq) * splits;
+  float* m = static_cast<float*>(workspace);
+  float* l = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(m) + align256(slots * sizeof(float)));
+  float* u = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(l) + align256(slots * sizeof(float)));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = launch_group_mma(make_layout(kv), kv->kv_dtype, q, G, group_ids, sa, attn_scale(kv->d), m, l, u, status, st);
+  if (rc) return cuda_status(rc, "group attention");
+  return cuda_status(launch_merge(m, l, u, nullptr, hq, splits, kv->d, out, st), "group attention merge");
+}
+
 int stk_touch_kv(const stk_kv* kv, int rows, int hq, const void* ids, int ids64, int s, float* out, void* stream) {
   int rc = check_kv(kv, hq);
   if (rc) return rc;

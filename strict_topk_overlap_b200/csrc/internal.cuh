@@ -183,6 +183,10 @@ int launch_select(const SelectArgs& a, int max_n, cudaStream_t stream);
 int launch_bounds(const ScoreArgs& a, float2* bounds, cudaStream_t stream);
 int launch_select_bounded(const SelectArgs& a, int max_n, cudaStream_t stream);
 int launch_merge_candidates(const MergeArgs& a, cudaStream_t stream);
+size_t group_mma_smem(int d, int esize);
+int group_mma_splits(int sa, int b);
+int launch_group_mma(const KVLayout& L, int kv_dtype, const void* q, int G, const int* ids, int sa, float scale,
+                     float* m, float* l, float* u, int* status, cudaStream_t stream);
 int launch_build_metadata(const KVLayout& L, int R, int total, int kv_dtype, float* lo, float* hi, cudaStream_t stream);
 int launch_append_token(const KVLayout& L, int R, int total, int kv_dtype, const void* k_new, const void* v_new,
                         const int* pos, float* lo, float* hi, int* status, cudaStream_t stream);

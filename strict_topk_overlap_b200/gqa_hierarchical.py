@@ -6,6 +6,10 @@ exact and repair reductions merge on chip inside one launch.
 """
 from __future__ import annotations
 
+import ctypes as C
+
+import torch
+
 from . import _lib as L
 from . import gqa
 from .kernels import Prediction, _run_repair, merge_partials
@@ -50,3 +54,28 @@ def repair_saved_shared(q, k, v, selected, predicted, state):
 
 
 select_blocks_shared = gqa.select_blocks_shared
+
+
+def exact_shared(q, k, v, group_selected):
+    """Attention of every query head over its KV group's shared block list
+    group_selected [Hkv, S] (the rows select_blocks_shared repeats per head),
+    on the tensor cores: the Hq / Hkv (<= 16) heads of a group form one MMA
+    tile, so each listed block is read once per group. q and K/V both bf16 or
+    both f16, D 64 or 128. Equals exact(q, k, v, group rows repeated per
+    head) within FP32 rounding."""
+    if group_selected.ndim != 2 or group_selected.dtype != torch.int32 or not group_selected.is_contiguous():
+        raise ValueError("group_selected must be a contiguous int32 [Hkv, S] tensor")
+    hq, d = q.shape
+    hkv, n, b, _ = k.shape
+    if group_selected.shape[0] != hkv or q.dtype != k.dtype or q.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("expected one list per KV head and q, K, V of one 16-bit dtype")
+    sa = group_selected.shape[1]
+    out = torch.empty((hq, d), device=q.device, dtype=torch.float32)
+    lib = L.load()
+    ws_bytes = lib.stk_group_attention_workspace_bytes(hq, sa, b, d)
+    ws = torch.empty((ws_bytes,), device=q.device, dtype=torch.uint8)
+    kv = L.kv_struct(k, v)
+    rc = lib.stk_group_attention(C.byref(kv), q.data_ptr(), L.dtype_code(q), hq, group_selected.data_ptr(), sa,
+                                 out.data_ptr(), ws.data_ptr(), ws_bytes, L.status_ptr(), L.stream_of(q))
+    L.check(rc, "group_attention")
+    return out
