@@ -497,6 +497,9 @@ int launch_reduce_states(const float* m, const float* l, const float* u, const u
   return static_cast<int>(cudaGetLastError());
 }
 
+// Slots whose per-dimension loads the grouping kernels issue together.
+constexpr int kSlotBatch = 16;
+
 // Hybrid grouping (kernels.py:94-117): high = mass >= tau * total mass,
 // low aggregate at low_m = max low m, absolute numerator envelope. Warp 0
 // takes the row's slots 32 at a time (lane-parallel loads, warp max / sum
@@ -538,9 +541,24 @@ __global__ void hybrid_group_kernel(const float* m, const float* l, const float*
     }
   }
   __syncthreads();
+  // Slot order is kept (the sums are sequential in i); the loads are issued
+  // kSlotBatch at a time, so a row costs s / kSlotBatch round trips to the
+  // just-written states, not s.
   for (int dd = threadIdx.x; dd < d; dd += blockDim.x) {
     float uv = 0.f, ua = 0.f;
-    for (int i = 0; i < s; ++i) {
+    int i = 0;
+    for (; i + kSlotBatch <= s; i += kSlotBatch) {
+      float x[kSlotBatch];
+#pragma unroll
+      for (int j = 0; j < kSlotBatch; ++j) x[j] = u[(base + i + j) * d + dd];
+#pragma unroll
+      for (int j = 0; j < kSlotBatch; ++j) {
+        const float al = hs[i + j];
+        uv += al * x[j];
+        ua += al * fabsf(x[j]);
+      }
+    }
+    for (; i < s; ++i) {
       const float al = hs[i];
       const float x = u[(base + i) * d + dd];
       uv += al * x;
@@ -606,7 +624,22 @@ __global__ void slot_sum_kernel(const float* x, const float* y, int s, int d, fl
   const int row = blockIdx.x;
   for (int dd = threadIdx.x; dd < d; dd += blockDim.x) {
     float ax = 0.f, ay = 0.f;
-    for (int i = 0; i < s; ++i) {
+    int i = 0;
+    for (; i + kSlotBatch <= s; i += kSlotBatch) {  // batched loads, sums in slot order
+      float bx[kSlotBatch], by[kSlotBatch];
+#pragma unroll
+      for (int t = 0; t < kSlotBatch; ++t) {
+        const long long j = (static_cast<long long>(row) * s + i + t) * d + dd;
+        bx[t] = x[j];
+        by[t] = y ? y[j] : 0.f;
+      }
+#pragma unroll
+      for (int t = 0; t < kSlotBatch; ++t) {
+        ax += bx[t];
+        if (y) ay += by[t];
+      }
+    }
+    for (; i < s; ++i) {
       const long long j = (static_cast<long long>(row) * s + i) * d + dd;
       ax += x[j];
       if (y) ay += y[j];
