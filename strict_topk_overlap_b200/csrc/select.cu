@@ -663,7 +663,11 @@ __global__ void __launch_bounds__(512) merge_candidates_kernel(MergeArgs a) {
 // under upward rounding. The radius takes 2 (D/4 + 2) u, which also covers
 // the FP64 score's own roundings (relative 2^-53 each) and, for group
 // selection, the FP64 sum over the group; an absolute 2^-118 covers
-// underflow. Non-finite inputs give the interval (-inf, +inf).
+// underflow. Non-finite inputs give the interval (-inf, +inf). A CTA's
+// metadata (32 consecutive rows of one head: two contiguous ranges of lo and
+// hi) lands in shared memory through two bulk copies on one mbarrier, so the
+// whole tile is one DRAM request per array instead of 16 register loads per
+// lane.
 //
 // Stage 2, per selection row: with T the K-th largest lower end and U the
 // (K+1)-th largest upper end, a block whose upper end is below T is beaten
@@ -718,8 +722,22 @@ __global__ void __launch_bounds__(kBWarps * 32) bound_interval_kernel(ScoreArgs 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nq = kQReq * G * D;
   float* qn1 = qs + nq;
+  // The tile's metadata rows, [kBTile][D] lo then hi: two contiguous ranges
+  // of the metadata, each brought in by one bulk copy.
+  float* slo = qs + ((nq + kQReq * G + 3) & ~3);
+  float* shi = slo + kBTile * D;
+  __shared__ uint64_t meta_bar;
   ST(0);
   pdl_release();  // the Top-K kernel may launch now; it waits for this grid to finish
+  if (threadIdx.x == 0) {
+    mbar_init(&meta_bar, 1);
+    fence_barrier_init();
+    const unsigned bytes = static_cast<unsigned>(nrows * D * sizeof(float));
+    const long long moff = (static_cast<long long>(mh) * a.total_blocks + row0) * D;
+    mbar_arrive_expect_tx(&meta_bar, 2 * bytes);
+    bulk_g2s(slo, a.lo + moff, bytes, &meta_bar);
+    bulk_g2s(shi, a.hi + moff, bytes, &meta_bar);
+  }
 
   // q first: loads issued behind the metadata stream would wait for it.
   const int r0 = find_request(a.block_offsets, a.R, row0);
@@ -742,14 +760,9 @@ __global__ void __launch_bounds__(kBWarps * 32) bound_interval_kernel(ScoreArgs 
   const int rl = warp * 8 + b;
   const bool live = rl < nrows;
   const long long gb = row0 + (live ? rl : 0);
-  const float4* L4 = reinterpret_cast<const float4*>(a.lo + (static_cast<long long>(mh) * a.total_blocks + gb) * D);
-  const float4* H4 = reinterpret_cast<const float4*>(a.hi + (static_cast<long long>(mh) * a.total_blocks + gb) * D);
+  const float4* L4 = reinterpret_cast<const float4*>(slo + (live ? rl : 0) * D);
+  const float4* H4 = reinterpret_cast<const float4*>(shi + (live ? rl : 0) * D);
   float4 lv[NBAT], hv[NBAT];
-#pragma unroll
-  for (int i = 0; i < NBAT; ++i) {
-    lv[i] = live ? __ldg(L4 + p + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    hv[i] = live ? __ldg(H4 + p + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
 #pragma unroll
   for (int e = 0; e < kQPer; ++e) {
     const int i = e * blockDim.x + tid;
@@ -770,6 +783,7 @@ __global__ void __launch_bounds__(kBWarps * 32) bound_interval_kernel(ScoreArgs 
   }
   __syncthreads();
   ST(1);
+  if (!mbar_wait(&meta_bar, 0, a.status)) return;  // bounded; the status records a wait that gave up
 
   const int rr = (live && a.block_offsets) ? find_request(a.block_offsets, a.R, static_cast<int>(gb)) - r0 : 0;
   float s[GM];
@@ -781,12 +795,10 @@ __global__ void __launch_bounds__(kBWarps * 32) bound_interval_kernel(ScoreArgs 
     const float* qrow = qs + rr * G * D;
 #pragma unroll
     for (int bat = 0; bat < NI / NBAT; ++bat) {
-      if (bat > 0) {
 #pragma unroll
-        for (int i = 0; i < NBAT; ++i) {
-          lv[i] = live ? __ldg(L4 + p + 4 * (bat * NBAT + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
-          hv[i] = live ? __ldg(H4 + p + 4 * (bat * NBAT + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+      for (int i = 0; i < NBAT; ++i) {
+        lv[i] = live ? L4[p + 4 * (bat * NBAT + i)] : make_float4(0.f, 0.f, 0.f, 0.f);
+        hv[i] = live ? H4[p + 4 * (bat * NBAT + i)] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int i = 0; i < NBAT; ++i) {
@@ -1219,7 +1231,9 @@ int launch_bounds(const ScoreArgs& a, float2* bounds, cudaStream_t stream) {
   const int G = a.hq / a.hmeta;
   const bool aligned = ((reinterpret_cast<uintptr_t>(a.lo) | reinterpret_cast<uintptr_t>(a.hi)) & 15) == 0;
   if (!aligned || G > 16 || (a.d != 64 && a.d != 128 && a.d != 256)) return 1;
-  const size_t smem = (static_cast<size_t>(kQReq) * G * a.d + kQReq * G) * 4;
+  // q rows and their norms (rounded up to 16 bytes), then the tile's lo and hi rows.
+  const size_t smem = (((static_cast<size_t>(kQReq) * G * a.d + kQReq * G) + 3) & ~static_cast<size_t>(3)) * 4 +
+                      static_cast<size_t>(2) * kBTile * a.d * 4;
   const dim3 grid((a.total_blocks + kBTile - 1) / kBTile, a.hmeta);
   void (*kern)(ScoreArgs, float2*);
   if (a.d == 64) kern = G <= 4 ? bound_interval_kernel<2, 4> : bound_interval_kernel<2, 16>;
