@@ -353,6 +353,7 @@ int stk_speculative_step(const stk_kv* kv, const void* q, int q_dtype, const flo
   a.mode = STK_MODE_FULL; a.m = pm; a.l = pl; a.u = pu; a.status = status;
   a.chain = 1;
   a.sm_skip = hq;  // one Top-K CTA per selection row
+  a.l2_lean = 1;   // no L2 window: the Top-K kernel beside it is latency-bound
   rc = launch_jobs(a, kv->kv_dtype, sm_count_current(), st);
   if (rc) return cuda_status(rc, "block_states (chained)");
   // 3. Saved repair (reuse predicted hits, compute selected misses, merge),

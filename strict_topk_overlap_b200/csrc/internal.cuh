@@ -95,6 +95,10 @@ struct JobArgs {
   // Top-K CTA together exceed an SM's registers, so they could not share an
   // SM anyway, and a static job range waiting for one would hold the grid).
   int sm_skip;
+  // 1: no L2 prefetch beyond the copy ring. In the chained step the Top-K
+  // kernel runs beside this one, and its latency-bound phases slow down under
+  // a deeper flood of outstanding requests.
+  int l2_lean;
 };
 
 struct RepairArgs {

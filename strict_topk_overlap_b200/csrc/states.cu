@@ -195,8 +195,10 @@ __global__ void __launch_bounds__(kFastMaxWarps * 32, 1) jobs_fast_kernel(JobArg
     if (i >= mine) fb[i] = -1;
     if (fb[i] >= 0 && lane == 0) issue(i, fb[i], fr[i]);
   }
-  // L2 window: jobs NS .. NS + kWarpPrefetch - 2 now, then one per job.
-  if (lane >= NS && lane < NS + kWarpPrefetch - 1) prefetch_lane();
+  // L2 window: jobs NS .. NS + win - 1 now, then one per job (job k + NS
+  // is asked for at the start of job k either way).
+  const int win = a.l2_lean ? 0 : kWarpPrefetch - 1;
+  if (lane >= NS && lane < NS + win) prefetch_lane();
   JT(1);
 
   unsigned phase = 0;  // bit s: parity of stage s's next completion
@@ -222,8 +224,8 @@ __global__ void __launch_bounds__(kFastMaxWarps * 32, 1) jobs_fast_kernel(JobArg
       nrow = __shfl_sync(kFull, lrow, kk - base);
     }
     {
-      const int pf = k + NS + kWarpPrefetch - 1 - base;
-      if (k + NS + kWarpPrefetch - 1 < mine && pf >= 0 && pf < 32 && lane == pf) prefetch_lane();
+      const int pf = k + NS + win - base;
+      if (k + NS + win < mine && pf >= 0 && pf < 32 && lane == pf) prefetch_lane();
     }
     if (cb < 0) {
       // Inactive slot: (-inf, 0, 0) as the reference writes; repair scratch keeps no state.
