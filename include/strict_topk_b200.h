@@ -250,6 +250,28 @@ STK_API int stk_speculative_step(const stk_kv* kv, const void* q, int q_dtype, c
                                  int topk, const void* pred, int pred64, int sp, int32_t* selected, float* out,
                                  void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
+/* Workspace (bytes) for stk_speculative_step_hybrid: the saved step's
+ * workspace plus the hybrid grouping's high mask and low aggregate. */
+STK_API size_t stk_speculative_step_hybrid_workspace_bytes(int hq, int n, int sp, int d);
+
+/* The hybrid methods' speculative step of one dense request on one stream:
+ * bound scores -> strict Top-K (selected [hq, topk]) -> FP32 states of the
+ * predicted blocks (the Top-K kernel's programmatic dependent, as in
+ * stk_speculative_step) -> hybrid grouping with threshold mass_threshold ->
+ * repair with variant STK_VAR_FUSED (fused.py:176-220 repair_fused) or
+ * STK_VAR_SIGNED_FUSED (signed_fused.py:148-193 repair_signed_fused) into
+ * out. The prediction keeps its mass (keep_mass=True aliases the states'
+ * m and l, kernels.py:450-477), so max_extra_mass > 0 is accepted. Results
+ * equal stk_select_topk + stk_speculate(STK_PRED_HYBRID) + stk_repair in
+ * sequence. Replaces the two-stream harness of
+ * benchmarks/run_benchmark.py:99-118 for the repair_fused / signed_fused
+ * methods. */
+STK_API int stk_speculative_step_hybrid(const stk_kv* kv, const void* q, int q_dtype, const float* lo, const float* hi,
+                                        int hq, int topk, const void* pred, int pred64, int sp, float mass_threshold,
+                                        int variant, float min_remaining, float cancellation_tol,
+                                        float max_extra_mass, int32_t* selected, const stk_repair_out* out,
+                                        void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
 /* Per-block K bounds: lo/hi [hkv, total, d] FP32 = min / max over each
  * block's tokens (NaN propagates). total = n for one dense request (R == 1,
  * block_offsets NULL) or total_blocks for block_offsets layouts (paged or

@@ -374,6 +374,76 @@ int stk_speculative_step(const stk_kv* kv, const void* q, int q_dtype, const flo
   return cuda_status(launch_repair(r, kv->kv_dtype, st), "repair (chained)");
 }
 
+size_t stk_speculative_step_hybrid_workspace_bytes(int hq, int n, int sp, int d) {
+  if (hq <= 0 || n <= 0 || sp <= 0 || d <= 0) return 0;
+  const size_t slots = static_cast<size_t>(hq) * sp;
+  return stk_speculative_step_workspace_bytes(hq, n, sp, d) + align256(slots) + 2 * align256(hq * sizeof(float)) +
+         2 * align256(static_cast<size_t>(hq) * d * sizeof(float));
+}
+
+int stk_speculative_step_hybrid(const stk_kv* kv, const void* q, int q_dtype, const float* lo, const float* hi, int hq,
+                                int topk, const void* pred, int pred64, int sp, float mass_threshold, int variant,
+                                float min_remaining, float cancellation_tol, float max_extra_mass, int32_t* selected,
+                                const stk_repair_out* out, void* workspace, size_t workspace_bytes, int32_t* status,
+                                void* stream) {
+  int rc = check_kv(kv, hq);
+  if (rc) return rc;
+  if (kv->page_table || kv->block_offsets) return fail(STK_EINVAL, "speculative_step_hybrid takes one dense request");
+  if (!q || !lo || !hi || !pred || !selected || !out || !out->out || !workspace || !valid_dtype(q_dtype))
+    return fail(STK_EINVAL, "null pointer or unsupported q dtype");
+  if (sp <= 0) return fail(STK_EINVAL, "empty prediction");
+  if (variant != STK_VAR_FUSED && variant != STK_VAR_SIGNED_FUSED)
+    return fail(STK_EINVAL, "speculative_step_hybrid repairs with STK_VAR_FUSED or STK_VAR_SIGNED_FUSED");
+  if (!(mass_threshold >= 0.f && mass_threshold <= 1.f)) return fail(STK_EINVAL, "mass_threshold must be in [0,1]");
+  if (!(max_extra_mass >= 0.f && max_extra_mass <= 1.f)) return fail(STK_EINVAL, "max_extra_mass must be in [0, 1]");
+  const int n = kv->n, d = kv->d;
+  if (workspace_bytes < stk_speculative_step_hybrid_workspace_bytes(hq, n, sp, d))
+    return fail(STK_EWS, "speculative_step_hybrid workspace too small");
+  unsigned char* w = static_cast<unsigned char*>(workspace);
+  const size_t sel_bytes = stk_select_workspace_bytes(hq, n);
+  const size_t slots = static_cast<size_t>(hq) * sp;
+  float* pm = reinterpret_cast<float*>(w + align256(sel_bytes));
+  float* pl = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(pm) + align256(slots * sizeof(float)));
+  float* pu = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(pl) + align256(slots * sizeof(float)));
+  uint8_t* high = reinterpret_cast<uint8_t*>(w + stk_speculative_step_workspace_bytes(hq, n, sp, d));
+  float* low_m = reinterpret_cast<float*>(high + align256(slots));
+  float* low_l = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(low_m) + align256(hq * sizeof(float)));
+  float* low_u = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(low_l) + align256(hq * sizeof(float)));
+  float* low_abs = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(low_u) +
+                                            align256(static_cast<size_t>(hq) * d * sizeof(float)));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // 1. Bound scores and strict Top-K.
+  rc = stk_select_topk(q, q_dtype, lo, hi, 1, hq, kv->hkv, n, nullptr, n, n, d, topk, 0, 0, selected, nullptr, w,
+                       sel_bytes, status, stream);
+  if (rc) return rc;
+  // 2. Predicted blocks' full states as the Top-K kernel's dependent, as in
+  //    stk_speculative_step.
+  JobArgs a{};
+  a.L = make_layout(kv);
+  a.q = q; a.q_dtype = q_dtype;
+  a.rows = hq; a.hq = hq; a.g = hq / kv->hkv; a.d = d; a.scale = attn_scale(d);
+  a.ids = pred; a.ids64 = pred64; a.s = sp;
+  a.mode = STK_MODE_FULL; a.m = pm; a.l = pl; a.u = pu; a.status = status;
+  a.chain = 1;
+  a.sm_skip = hq;
+  a.l2_lean = 1;
+  rc = launch_jobs(a, kv->kv_dtype, sm_count_current(), st);
+  if (rc) return cuda_status(rc, "block_states (chained)");
+  // 3. Hybrid grouping (kernels.py:94-117), in stream order after the states
+  //    (whose completion follows the Top-K grid's).
+  rc = launch_hybrid_group(pm, pl, pu, hq, sp, d, mass_threshold, high, low_m, low_l, low_u, low_abs, st);
+  if (rc) return cuda_status(rc, "hybrid_group");
+  // 4. Fused or signed-fused repair. keep_mass aliases the states' (m, l)
+  //    (kernels.py:450-477), which the extra-mass budget reads.
+  stk_prediction ps{};
+  ps.mode = STK_PRED_HYBRID; ps.sc = sp;
+  ps.m = pm; ps.l = pl; ps.u = pu; ps.high = high;
+  ps.low_m = low_m; ps.low_l = low_l; ps.low_u = low_u; ps.low_abs = low_abs;
+  ps.mass_m = pm; ps.mass_l = pl;
+  return stk_repair(kv, q, q_dtype, hq, hq, selected, 0, topk, pred, pred64, sp, &ps, variant, min_remaining,
+                    cancellation_tol, max_extra_mass, n, out, status, stream);
+}
+
 static int metadata_rows(const stk_kv* kv, int R, int total) {
   if (kv->block_offsets == nullptr) return R == 1 ? kv->n : -1;
   return total;

@@ -90,6 +90,38 @@ def speculative_step(q, k, v, lo, hi, predicted, topk, *, out=None, selected=Non
     return out, selected
 
 
+def speculative_step_hybrid(q, k, v, lo, hi, predicted, topk, *, variant="repair_fused", mass_threshold=0.1,
+                            min_remaining=1e-3, cancellation_tol=1e-5, max_extra_mass=0.0, out=None, selected=None,
+                            workspace=None):
+    """One hybrid-method speculative step on the current stream in one launch
+    chain (stk_speculative_step_hybrid): returns (output FP32 [Hq, D],
+    selected int32 [Hq, topk]). ``variant`` "repair_fused" equals
+    gqa.select_blocks, kernels.speculate(mode='hybrid', keep_mass=True) and
+    fused.repair_fused in sequence; "signed_fused" ends with
+    signed_fused.repair_signed_fused instead."""
+    hq, d = q.shape
+    hkv, n, b, _ = k.shape
+    sp = predicted.shape[1]
+    var = {"repair_fused": L.VAR_FUSED, "signed_fused": L.VAR_SIGNED_FUSED}[variant]
+    lib = L.load()
+    if out is None:
+        out = torch.empty((hq, d), device=q.device, dtype=torch.float32)
+    if selected is None:
+        selected = torch.empty((hq, topk), device=q.device, dtype=torch.int32)
+    need = lib.stk_speculative_step_hybrid_workspace_bytes(hq, n, sp, d)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty((need,), device=q.device, dtype=torch.uint8)
+    kv = L.kv_struct(k, v)
+    res = L.StkRepairOut(out.data_ptr(), None, None, None, None, None, None)
+    rc = lib.stk_speculative_step_hybrid(
+        C.byref(kv), q.data_ptr(), L.dtype_code(q), lo.data_ptr(), hi.data_ptr(), hq, topk, predicted.data_ptr(),
+        L.id_is64(predicted), sp, float(mass_threshold), var, float(min_remaining), float(cancellation_tol),
+        float(max_extra_mass), selected.data_ptr(), C.byref(res), workspace.data_ptr(), need, L.status_ptr(),
+        L.stream_of(q))
+    L.check(rc, "speculative_step_hybrid")
+    return out, selected
+
+
 @dataclass
 class StepSpec:
     """One decode step's configuration."""
@@ -136,12 +168,15 @@ class SpeculativeDecoder:
         self.q, self.k, self.v, self.lo, self.hi, self.predicted = q, k, v, lo, hi, predicted
         self.spec = spec
         self.serial = serial
-        # The saved method runs as one launch chain on one stream; the other
-        # methods (and chained=False) use the two-stream harness.
-        self.chained = chained and spec.method in ("saved", "light")
+        # The saved and hybrid (repair_fused, signed_fused) methods run as one
+        # launch chain on one stream; compact (and chained=False) uses the
+        # two-stream harness.
+        self.chained = chained and spec.method in ("saved", "light", "repair_fused", "signed_fused")
         self._ws = None
         if self.chained:
-            need = L.load().stk_speculative_step_workspace_bytes(q.shape[0], k.shape[1], predicted.shape[1], q.shape[1])
+            ws_fn = (L.load().stk_speculative_step_workspace_bytes if spec.method in ("saved", "light")
+                     else L.load().stk_speculative_step_hybrid_workspace_bytes)
+            need = ws_fn(q.shape[0], k.shape[1], predicted.shape[1], q.shape[1])
             self._ws = torch.empty((need,), device=q.device, dtype=torch.uint8)
         # The selector is the critical path (score -> Top-K -> repair): its
         # stream gets the higher priority when both branches want SMs.
@@ -160,6 +195,12 @@ class SpeculativeDecoder:
         if self.serial:
             a = self._selector()
             return gqa.exact(self.q, self.k, self.v, a), a
+        if self.chained and self.spec.method in ("repair_fused", "signed_fused"):
+            sp = self.spec
+            return speculative_step_hybrid(self.q, self.k, self.v, self.lo, self.hi, self.predicted, sp.topk,
+                                           variant=sp.method, mass_threshold=sp.mass_threshold,
+                                           min_remaining=sp.min_remaining, cancellation_tol=sp.cancellation_tol,
+                                           max_extra_mass=sp.max_extra_mass, workspace=self._ws)
         if self.chained:
             return speculative_step(self.q, self.k, self.v, self.lo, self.hi, self.predicted, self.spec.topk,
                                     workspace=self._ws)
