@@ -265,10 +265,12 @@ int stk_speculate(const stk_kv* kv, const void* q, int q_dtype, int rows, int hq
   return cuda_status(launch_slot_sum(su, sa, rows, sp, d, low_u, low_abs, st), "slot_sum");
 }
 
-int stk_repair(const stk_kv* kv, const void* q, int q_dtype, int rows, int hq, const void* sel, int sel64, int sa,
-               const void* pred, int pred64, int sp, const stk_prediction* ps, int variant, float min_remaining,
-               float cancellation_tol, float max_extra_mass, int max_blocks, const stk_repair_out* out,
-               int32_t* status, void* stream) {
+// stk_repair's body; chain = 1 launches the repair as the programmatic
+// dependent of the preceding kernel (the chained hybrid step).
+static int repair_entry(const stk_kv* kv, const void* q, int q_dtype, int rows, int hq, const void* sel, int sel64,
+                        int sa, const void* pred, int pred64, int sp, const stk_prediction* ps, int variant,
+                        float min_remaining, float cancellation_tol, float max_extra_mass, int max_blocks,
+                        const stk_repair_out* out, int32_t* status, void* stream, int chain) {
   int rc = check_kv(kv, hq);
   if (rc) return rc;
   if (!q || !sel || !out || !out->out || !valid_dtype(q_dtype)) return fail(STK_EINVAL, "bad repair pointers");
@@ -306,7 +308,16 @@ int stk_repair(const stk_kv* kv, const void* q, int q_dtype, int rows, int hq, c
   a.out = out->out; a.fallback = out->fallback; a.remaining = out->remaining; a.approx = out->approx;
   a.extra = out->extra; a.pos_out = out->positive_jobs; a.total_out = out->total_jobs;
   a.status = status;
+  a.chain = chain;
   return cuda_status(launch_repair(a, kv->kv_dtype, static_cast<cudaStream_t>(stream)), "repair");
+}
+
+int stk_repair(const stk_kv* kv, const void* q, int q_dtype, int rows, int hq, const void* sel, int sel64, int sa,
+               const void* pred, int pred64, int sp, const stk_prediction* ps, int variant, float min_remaining,
+               float cancellation_tol, float max_extra_mass, int max_blocks, const stk_repair_out* out,
+               int32_t* status, void* stream) {
+  return repair_entry(kv, q, q_dtype, rows, hq, sel, sel64, sa, pred, pred64, sp, ps, variant, min_remaining,
+                      cancellation_tol, max_extra_mass, max_blocks, out, status, stream, 0);
 }
 
 static size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -429,19 +440,20 @@ int stk_speculative_step_hybrid(const stk_kv* kv, const void* q, int q_dtype, co
   a.l2_lean = 1;
   rc = launch_jobs(a, kv->kv_dtype, sm_count_current(), st);
   if (rc) return cuda_status(rc, "block_states (chained)");
-  // 3. Hybrid grouping (kernels.py:94-117), in stream order after the states
-  //    (whose completion follows the Top-K grid's).
-  rc = launch_hybrid_group(pm, pl, pu, hq, sp, d, mass_threshold, high, low_m, low_l, low_u, low_abs, st);
+  // 3. Hybrid grouping (kernels.py:94-117) as the states' programmatic
+  //    dependent: it waits for their grid, whose completion follows Top-K's.
+  rc = launch_hybrid_group(pm, pl, pu, hq, sp, d, mass_threshold, high, low_m, low_l, low_u, low_abs, st, true);
   if (rc) return cuda_status(rc, "hybrid_group");
-  // 4. Fused or signed-fused repair. keep_mass aliases the states' (m, l)
+  // 4. Fused or signed-fused repair, the grouping's programmatic dependent
+  //    (it also reads A, written before the states completed). keep_mass aliases the states' (m, l)
   //    (kernels.py:450-477), which the extra-mass budget reads.
   stk_prediction ps{};
   ps.mode = STK_PRED_HYBRID; ps.sc = sp;
   ps.m = pm; ps.l = pl; ps.u = pu; ps.high = high;
   ps.low_m = low_m; ps.low_l = low_l; ps.low_u = low_u; ps.low_abs = low_abs;
   ps.mass_m = pm; ps.mass_l = pl;
-  return stk_repair(kv, q, q_dtype, hq, hq, selected, 0, topk, pred, pred64, sp, &ps, variant, min_remaining,
-                    cancellation_tol, max_extra_mass, n, out, status, stream);
+  return repair_entry(kv, q, q_dtype, hq, hq, selected, 0, topk, pred, pred64, sp, &ps, variant, min_remaining,
+                      cancellation_tol, max_extra_mass, n, out, status, stream, 1);
 }
 
 static int metadata_rows(const stk_kv* kv, int R, int total) {

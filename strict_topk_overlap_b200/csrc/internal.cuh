@@ -138,7 +138,9 @@ struct RepairArgs {
   int* total_out;            // [rows] or null
   int* status;
   // 1: the prediction states (pm, pl, pu) come from the immediately
-  // preceding kernel on the stream, so they are read after pdl_wait().
+  // preceding kernel on the stream, so they are read after pdl_wait(); the
+  // cluster repair kernel is then launched as a programmatic dependent and
+  // waits before its first load.
   int chain;
 };
 
@@ -202,9 +204,11 @@ int launch_merge(const float* m, const float* l, const float* u, const unsigned 
                  float* out, cudaStream_t stream);
 int launch_reduce_states(const float* m, const float* l, const float* u, const unsigned char* include, int rows,
                          int s, int d, float* m_out, float* l_out, float* u_out, cudaStream_t stream);
+// chain: launched as the programmatic dependent of the preceding kernel
+// (the kernel waits for it before reading the states).
 int launch_hybrid_group(const float* m, const float* l, const float* u, int rows, int s, int d, float tau,
                         unsigned char* high, float* low_m, float* low_l, float* low_u, float* low_abs,
-                        cudaStream_t stream);
+                        cudaStream_t stream, bool chain = false);
 int launch_compact_group(const float* pm, const float* pl, const void* pred, int pred64, int rows, int s, int c,
                          float tau, unsigned char* high, void* rids, float* low_m, float* low_l,
                          unsigned char* overflow, cudaStream_t stream);

@@ -216,6 +216,7 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
   const bool has_pred = a.pmode != kPredNone;
 
   RT(0);
+  if (a.chain) pdl_wait();  // programmatic dependent: inputs come from the preceding kernel
   RepairSmem S;
   repair_layout<DPH, NST, T>(a, &S, smem);
   T* stages = reinterpret_cast<T*>(smem);
@@ -664,11 +665,27 @@ __global__ void __launch_bounds__(kNW * 32) repair_kernel(RepairArgs a) {
   if (has_pred) {
     float* keepU = S.aggU + kNW * D;
     const float* pu = a.pu + static_cast<long long>(row) * a.sc * D;
+    // The CTA's slots are loaded kKeepBatch at a time (in bounds whatever
+    // the weight) and folded in slot order, skipping zero weights as before:
+    // one round trip to the states per batch instead of one per slot.
+    constexpr int kKeepBatch = 8;
     for (int dd = tid; dd < D; dd += blockDim.x) {
       float acc = 0.f;
-      for (int c = rank; c < a.sc; c += CS) {
-        const float w = S.pw[c];
-        if (w != 0.f) acc = fmaf(w, pu[static_cast<long long>(c) * D + dd], acc);
+      for (int c0 = rank; c0 < a.sc; c0 += CS * kKeepBatch) {
+        float x[kKeepBatch];
+#pragma unroll
+        for (int t = 0; t < kKeepBatch; ++t) {
+          const int c = c0 + t * CS;
+          x[t] = c < a.sc ? pu[static_cast<long long>(c) * D + dd] : 0.f;
+        }
+#pragma unroll
+        for (int t = 0; t < kKeepBatch; ++t) {
+          const int c = c0 + t * CS;
+          if (c < a.sc) {
+            const float w = S.pw[c];
+            if (w != 0.f) acc = fmaf(w, x[t], acc);
+          }
+        }
       }
       keepU[dd] = acc;
     }
@@ -817,6 +834,8 @@ static int launch_repair_t(RepairArgs a, cudaStream_t stream) {
   prefer_shared(kern);
   const int cs = repair_cluster_size(a);
   a.cluster = cs;
+  if (a.chain)
+    return launch_pdl(kern, dim3(static_cast<unsigned>(a.rows) * cs), dim3(kNW * 32), smem, stream, cs, a);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(a.rows) * cs, 1, 1);
   cfg.blockDim = dim3(kNW * 32, 1, 1);

@@ -500,41 +500,53 @@ int launch_reduce_states(const float* m, const float* l, const float* u, const u
 }
 
 // Slots whose per-dimension loads the grouping kernels issue together.
-constexpr int kSlotBatch = 16;
+constexpr int kSlotBatch = 32;
 
 // Hybrid grouping (kernels.py:94-117): high = mass >= tau * total mass,
-// low aggregate at low_m = max low m, absolute numerator envelope. Warp 0
-// takes the row's slots 32 at a time (lane-parallel loads, warp max / sum
-// reductions), so the row costs a few memory round trips, not one per slot;
-// then every thread folds dims.
+// low aggregate at low_m = max low m, absolute numerator envelope. The
+// row's (m, l) are staged in shared memory in one pass; warp 0 takes the
+// slots 32 at a time (warp max / sum reductions); then every thread folds
+// dims.
 __global__ void hybrid_group_kernel(const float* m, const float* l, const float* u, int s, int d, float tau,
                                     unsigned char* high, float* low_m, float* low_l, float* low_u, float* low_abs) {
-  extern __shared__ float hs[];  // alpha[s]
+  extern __shared__ float hs[];  // alpha[s], then the row's m[s] and l[s]
+  float* ms = hs + s;
+  float* ls = ms + s;
   const int row = blockIdx.x;
   const int lane = threadIdx.x & 31;
   const long long base = static_cast<long long>(row) * s;
+  // Launched as a programmatic dependent (chained step): the states come
+  // from the preceding kernel. Both calls are no-ops in a plain launch.
+  pdl_release();
+  pdl_wait();
+  // The row's (m, l) are read from global memory once, by every thread.
+  for (int i = threadIdx.x; i < s; i += blockDim.x) {
+    ms[i] = m[base + i];
+    ls[i] = l[base + i];
+  }
+  __syncthreads();
   if (threadIdx.x < 32) {
     float gm = neg_inf();
-    for (int i = lane; i < s; i += 32) gm = fmaxf(gm, m[base + i]);
+    for (int i = lane; i < s; i += 32) gm = fmaxf(gm, ms[i]);
     gm = warp_max(gm);
     float total = 0.f;
-    for (int i = lane; i < s; i += 32) total += expf(m[base + i] - gm) * l[base + i];
+    for (int i = lane; i < s; i += 32) total += expf(ms[i] - gm) * ls[i];
     total = warp_sum(total);
     float lm = neg_inf();
     for (int i = lane; i < s; i += 32) {
-      const float mass = expf(m[base + i] - gm) * l[base + i];
+      const float mass = expf(ms[i] - gm) * ls[i];
       const bool hi = mass >= tau * total;
       high[base + i] = hi;
       hs[i] = hi ? 0.f : 1.f;
-      if (!hi) lm = fmaxf(lm, m[base + i]);
+      if (!hi) lm = fmaxf(lm, ms[i]);
     }
     lm = warp_max(lm);
     if (lm == neg_inf()) lm = 0.f;
     float zz = 0.f;
     for (int i = lane; i < s; i += 32) {
-      const float al = hs[i] != 0.f ? expf(m[base + i] - lm) : 0.f;
+      const float al = hs[i] != 0.f ? expf(ms[i] - lm) : 0.f;
       hs[i] = al;
-      zz += al * l[base + i];
+      zz += al * ls[i];
     }
     zz = warp_sum(zz);
     if (lane == 0) {
@@ -753,9 +765,14 @@ int launch_merge(const float* m, const float* l, const float* u, const unsigned 
 
 int launch_hybrid_group(const float* m, const float* l, const float* u, int rows, int s, int d, float tau,
                         unsigned char* high, float* low_m, float* low_l, float* low_u, float* low_abs,
-                        cudaStream_t stream) {
-  hybrid_group_kernel<<<rows, 128, s * sizeof(float), stream>>>(m, l, u, s, d, tau, high, low_m, low_l, low_u,
-                                                                  low_abs);
+                        cudaStream_t stream, bool chain) {
+  const size_t smem = static_cast<size_t>(s) * 3 * sizeof(float);
+  if (smem > 48 * 1024) cudaFuncSetAttribute(hybrid_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+  if (chain)
+    return launch_pdl(hybrid_group_kernel, dim3(rows), dim3(128), smem, stream, 0, m, l, u, s, d, tau, high, low_m,
+                      low_l, low_u, low_abs);
+  hybrid_group_kernel<<<rows, 128, smem, stream>>>(m, l, u, s, d, tau, high, low_m, low_l, low_u, low_abs);
   return static_cast<int>(cudaGetLastError());
 }
 
