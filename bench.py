@@ -3,21 +3,30 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--method saved|light|compact|repair_fused|signed_fused] [--overlap 0.9]
 
-Workload: one request, 32 query / 8 KV heads, head dim
-128, bf16, 65,536-token context in 32-token blocks (2,048 blocks), K = 64,
-predicted list = true Top-K with round((1 - overlap) * 64) IDs swapped for
-seeded-random unselected blocks. Synthetic seeded inputs (Q ~ N(0,1);
+Headline workload: one request, 32 query / 8 KV heads,
+head dim 128, bf16, 65,536-token context in 32-token blocks (2,048 blocks),
+K = 64, predicted list = true Top-K with round((1 - overlap) * 64) IDs swapped
+for seeded-random unselected blocks. Synthetic seeded inputs (Q ~ N(0,1);
 K = N(0,1) + per-block N(0, 0.5^2) bias; V ~ N(0,1)); metadata lo/hi is the
 per-block min/max of K, built outside timing.
 
-A step is one full speculative decode step (strict Top-K selection ||
-predicted-block attention, then repair), replayed as one CUDA graph. Steps
-rotate over ``--sets`` independent input sets (default 8 x ~272 MiB, far
-above the 126 MB L2), so no step finds its KV in L2.
+A step is one full speculative decode step (strict Top-K selection and
+predicted-block attention, then repair). The timed region runs exactly K steps
+(``--steps``) bracketed by a barrier and a device synchronisation; it is
+repeated until the repeats cover >= 200 ms, and the line reports the median
+repeat (``repeats`` gives the count). Steps rotate over ``--sets``
+independent input sets (default 8 x ~272 MiB, far above the 126 MB L2), so no
+step finds its KV in L2.
 
-With N > 1 (torchrun, one process per GPU) every rank decodes its own
-request (weak scaling, no collective in the data path); the timed region is
-bracketed by barriers and the reported time is the max over ranks.
+With N > 1 (torchrun, one process per GPU) every rank decodes its own config-1
+request (weak scaling, no collective in the data path); times are the max over
+ranks. The same line also carries, measured at the same N:
+  * ``batched``: BASELINE config 3, a batch of 64 paged requests split across
+    the N ranks by LPT (strong scaling, no collective), strict and relaxed
+    (max_extra_mass = 0.01);
+  * ``context_parallel``: BASELINE config 4, one 524,288-token request whose
+    blocks are split across the N ranks, exchanged with two NCCL all-gathers,
+    with its IDs checked bit for bit against single-GPU selection.
 """
 from __future__ import annotations
 
@@ -39,13 +48,14 @@ sys.path.insert(0, str(ROOT))
 HQ, HKV, D, BLOCKS, B, TOPK = 32, 8, 128, 2048, 32, 64
 METRIC = "decode-step µs (score+topk+spec attn+repair) vs serial; HBM GB/s % of peak"
 LAUNCHES_PER_STEP = {"saved": 4, "light": 4, "compact": 8, "repair_fused": 5, "signed_fused": 5}
+MIN_TIMED_MS = 200.0
 
 
 def parse():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
-    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--method", default="saved")
     ap.add_argument("--overlap", type=float, default=0.9)
@@ -53,15 +63,18 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--sweep", action="store_true", help="also time every method at overlap 1.0/0.9/0.75")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batched", action="store_true", help="skip the config-3 object")
+    ap.add_argument("--no-cp", action="store_true", help="skip the config-4 object")
     ap.add_argument("--quick", action="store_true",
-                    help="short run for profiler captures: no clock window, e2e, sweep or CPU baseline")
+                    help="short run for profiler captures: no clock window, repeats, e2e, sweep, CPU baseline, "
+                         "config-3 or config-4 objects")
     ap.add_argument("--graph-steps", type=int, default=8,
                     help="decode steps per CUDA graph in the timed loops (one per input set, like the attention "
                          "calls of consecutive layers of one token step); 1 = one graph per step")
-    ap.add_argument("--workload", choices=("c1", "batched"), default="c1",
-                    help="c1: BASELINE config 1 (default, the headline); batched: BASELINE config 3, a batch of "
-                         "paged requests split across the ranks")
-    ap.add_argument("--requests", type=int, default=64, help="batched workload: requests in the whole batch")
+    ap.add_argument("--workload", choices=("c1", "batched", "cp"), default="c1",
+                    help="c1: BASELINE config 1 (default, the headline, with the config-3 and config-4 objects); "
+                         "batched / cp: only the config-3 / config-4 measurement, as its own line")
+    ap.add_argument("--requests", type=int, default=64, help="config 3: requests in the whole batch")
     ap.add_argument("--eager", action="store_true",
                     help="launch each step's kernels directly instead of replaying a CUDA graph (for per-kernel "
                          "profiler launch lists)")
@@ -98,14 +111,18 @@ def barrier(world):
         dist.barrier()
 
 
-def max_over_ranks(x, world, device):
+def all_reduce(x, world, device, op="max"):
     if world == 1:
         return x
     import torch
     import torch.distributed as dist
     t = torch.tensor([x], dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t, op={"max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN, "sum": dist.ReduceOp.SUM}[op])
     return float(t.item())
+
+
+def max_over_ranks(x, world, device):
+    return all_reduce(x, world, device, "max")
 
 
 class ClockSampler:
@@ -184,6 +201,37 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def time_loop(fn, steps, device, stream=None):
+    """CUDA-event time (ms) of fn(0) .. fn(steps - 1), synchronised on both sides."""
+    import torch
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    start.record(stream)
+    for i in range(steps):
+        fn(i)
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end)
+
+
+def timed_repeats(run_k, world, device, min_ms=MIN_TIMED_MS, max_repeats=1000, quick=False):
+    """Time run_k() (which runs exactly the K timed steps) bracketed by a
+    barrier and a device synchronisation on both sides, max over ranks;
+    repeat until the repeats cover min_ms. Every rank sees the same maxima,
+    so every rank takes the same number of repeats (and collectives)."""
+    import torch
+    reps = []
+    while True:
+        barrier(world)
+        torch.cuda.synchronize(device)
+        ms = time_loop(lambda _: run_k(), 1, device)
+        barrier(world)
+        reps.append(max_over_ranks(ms, world, device))
+        if quick or sum(reps) >= min_ms or len(reps) >= max_repeats:
+            return reps
+
+
 # ----------------------------------------------------------------------------- workload
 
 def make_set(seed, overlap, device):
@@ -198,19 +246,26 @@ def make_set(seed, overlap, device):
     v = torch.randn(HKV, BLOCKS, B, D, device=device, generator=g).to(torch.bfloat16)
     lo, hi = k.amin(dim=2).float(), k.amax(dim=2).float()
     a = gqa.select_blocks(q, lo, hi, TOPK).cpu()
-    nswap = round((1 - overlap) * TOPK)
-    gen = torch.Generator().manual_seed(seed + 7919)
-    rows = []
-    for row in a.tolist():
-        chosen = set(row)
-        pool = [x for x in range(BLOCKS) if x not in chosen]
-        repl = [pool[i] for i in torch.randperm(len(pool), generator=gen)[:nswap].tolist()]
-        pos = torch.randperm(TOPK, generator=gen)[:nswap].tolist()
-        for j, r in zip(pos, repl):
-            row[j] = r
-        rows.append(row)
-    p = torch.tensor(rows, dtype=torch.int32, device=device)
+    p = swap_rows(a, BLOCKS, round((1 - overlap) * TOPK), seed + 7919).to(device)
     return {"q": q, "k": k, "v": v, "lo": lo, "hi": hi, "p": p, "a": a}
+
+
+def swap_rows(a, n_blocks, nswap, seed, blocks_of_row=None):
+    """Predicted list: each row of ``a`` with ``nswap`` IDs replaced by
+    seeded-random unselected blocks of the row's request."""
+    import torch
+    gen = torch.Generator().manual_seed(seed)
+    rows = []
+    for i, row in enumerate(a.tolist()):
+        n = blocks_of_row(i) if blocks_of_row else n_blocks
+        ns = nswap(i) if callable(nswap) else nswap
+        chosen = set(row)
+        cand = torch.randperm(n, generator=gen).tolist()
+        repl = [x for x in cand if x not in chosen][:ns]
+        for j, x in zip(torch.randperm(len(row), generator=gen)[:ns].tolist(), repl):
+            row[j] = x
+        rows.append(row)
+    return torch.tensor(rows, dtype=torch.int32)
 
 
 def unique_blocks(ids, g):
@@ -222,17 +277,20 @@ def unique_blocks(ids, g):
     return total
 
 
-def time_loop(fn, steps, device, stream=None):
+def graph_of(fn, device):
+    """Warm fn up on a side stream, then capture it in a CUDA graph; returns (graph, fn's result)."""
     import torch
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize(device)
-    start.record(stream)
-    for i in range(steps):
-        fn(i)
-    end.record(stream)
-    end.synchronize()
-    return start.elapsed_time(end)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = fn()
+    return g, out
 
 
 # ----------------------------------------------------------------------------- reference arm
@@ -276,30 +334,28 @@ def run_reference(args):
     return 0
 
 
-# ----------------------------------------------------------------------------- our arm
+# ----------------------------------------------------------------------------- config 3 (batched)
 
-def run_batched(args):
-    """a batch of `--requests` requests (context U[8192, 32768]
-    tokens, multiple of 32; 16 query / 8 KV heads, D 128, bf16; paged KV, page
-    16, 32-token blocks; K 64; per-request predicted overlap ~ Beta(8, 2)).
-    Requests are split across ranks by greedy LPT on context length
-    (paged.shard_requests); each rank builds its own page pool and decodes its
-    requests, with no collective in the data path. A step is one batched
-    speculative step (selection || predicted-block states, then saved repair,
-    one CUDA graph); the serial step is selection then exact attention. Each
-    rank's KV (~5 GB at N=1) is far above L2. value = requests decoded per
-    second over the whole job (all ranks), from the max over ranks."""
+def measure_batched(args, rank, world, device, quick=False):
+    """a batch of ``--requests`` requests (context
+    U[8192, 32768] tokens, multiple of 32; 16 query / 8 KV heads, D 128, bf16;
+    paged KV, page 16, 32-token blocks; K 64; per-request predicted overlap ~
+    Beta(8, 2)). Requests are split across ranks by greedy LPT on context
+    length (paged.shard_requests); each rank builds its own page pool and
+    decodes its requests, with no collective in the data path. A step is one
+    batched decode step of the whole batch (one CUDA graph per rank); the
+    serial step is selection then exact attention. Strict: saved speculation
+    + saved repair; relaxed: hybrid speculation + fused repair with
+    max_extra_mass = 0.01. Each rank's KV (~5 GB at N=1) is far above L2.
+    Returns the object for the JSON line (rank 0) with times as max over ranks."""
     import torch
-    rank, world, local = dist_setup("nccl")
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
     from strict_topk_overlap_b200 import paged
     from strict_topk_overlap_b200.decode import overlap_run
     HQB, PAGE = 16, 16
     gen = torch.Generator().manual_seed(args.seed + 3)
     lengths = [int(x) // 32 * 32 for x in (8192 + torch.rand(args.requests, generator=gen) * (32768 - 8192)).tolist()]
-    torch.manual_seed(args.seed + 5)
-    overlaps = torch.distributions.Beta(8.0, 2.0).sample((args.requests,)).tolist()
+    import numpy as np
+    overlaps = np.random.default_rng(args.seed + 5).beta(8.0, 2.0, args.requests).tolist()
     mine = paged.shard_requests(lengths, world)[rank]
     ks, vs, qs = [], [], []
     for r in mine:
@@ -316,88 +372,175 @@ def run_batched(args):
     del ks, vs
     q = torch.cat(qs, 0).contiguous()
     a = paged.select_blocks(q, cache, TOPK).cpu()
-    pg = torch.Generator().manual_seed(args.seed + 17)
-    rows = []
-    for i, row in enumerate(a.tolist()):
-        r = mine[i // HQB]
-        n = lengths[r] // B
-        nswap = round((1 - overlaps[r]) * TOPK)
-        chosen = set(row)
-        cand = torch.randperm(n, generator=pg).tolist()
-        repl = [x for x in cand if x not in chosen][:nswap]
-        for j, x in zip(torch.randperm(TOPK, generator=pg)[:nswap].tolist(), repl):
-            row[j] = x
-        rows.append(row)
-    p = torch.tensor(rows, dtype=torch.int32, device=device)
+    p = swap_rows(a, 0, lambda i: round((1 - overlaps[mine[i // HQB]]) * TOPK), args.seed + 17,
+                  blocks_of_row=lambda i: lengths[mine[i // HQB]] // B).to(device)
     s_sel = torch.cuda.Stream(device, priority=-1)
     s_pred = torch.cuda.Stream(device)
+    eps = 0.01
 
     def spec():
         return overlap_run(lambda: paged.select_blocks(q, cache, TOPK), lambda: paged.partials(q, cache, p),
                            lambda sel, st: paged.repair_saved(q, cache, sel, p, st), s_sel, s_pred)
 
+    def relaxed():
+        return overlap_run(lambda: paged.select_blocks(q, cache, TOPK),
+                           lambda: paged.speculate(q, cache, p, mode="hybrid", mass_threshold=0.1, keep_mass=True),
+                           lambda sel, pr: paged.repair_fused(q, cache, sel, p, pr, max_extra_mass=eps).output,
+                           s_sel, s_pred)
+
     def serial():
         return paged.exact(q, cache, paged.select_blocks(q, cache, TOPK))
 
-    graphs = {}
-    for name, fn in (("spec", spec), ("serial", serial)):
-        side = torch.cuda.Stream(device)
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            for _ in range(2):
-                fn()
-        torch.cuda.current_stream().wait_stream(side)
-        torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            out = fn()
-        graphs[name] = (g, out)
-    graphs["spec"][0].replay()
-    graphs["serial"][0].replay()
-    torch.cuda.synchronize()
+    graphs = {name: graph_of(fn, device) for name, fn in (("spec", spec), ("relaxed", relaxed), ("serial", serial))}
+    for g, _ in graphs.values():
+        g.replay()
+    torch.cuda.synchronize(device)
     assert (graphs["spec"][1] - graphs["serial"][1]).abs().max().item() <= 2e-3
-    steps = max(1, min(args.steps, 400))
-    for i in range(max(args.warmup, 3)):
-        graphs["spec"][0].replay()
-    with ClockSampler(local if not args.quick else -1) as clk:
-        barrier(world)
-        ms = time_loop(lambda i: graphs["spec"][0].replay(), steps, device)
-        barrier(world)
-    ms = max_over_ranks(ms, world, device)
-    for i in range(3):
-        graphs["serial"][0].replay()
-    barrier(world)
-    ms_ser = max_over_ranks(time_loop(lambda i: graphs["serial"][0].replay(), steps, device), world, device)
-    hbm_peak, peak_kind = peaks()
+    steps = 5 if quick else 50
+    times = {}
+    for name, (g, _) in graphs.items():
+        for _ in range(3):
+            g.replay()
+
+        def run_k(g=g):
+            for _ in range(steps):
+                g.replay()
+        reps = timed_repeats(run_k, world, device, min_ms=50.0, quick=quick)
+        times[name] = statistics.median(reps) / steps
+    # Algorithmic bytes of the whole batch's speculative step (sum over ranks).
+    blk = B * D * 2
+    total_blocks = sum(lengths[r] // B for r in mine)
+    ap = a.numpy()
+    pn = p.cpu().numpy()
+    g_ = HQB // HKV
+    upred = unique_blocks(torch.from_numpy(pn), g_)
+    miss = sum(len(set(x) - set(y)) for x, y in zip(ap.tolist(), pn.tolist()))
+    step_bytes = 2 * HKV * total_blocks * D * 4 + 2 * blk * upred + 2 * blk * miss + q.numel() * 2 + q.numel() * 4
+    step_bytes = all_reduce(step_bytes, world, device, "sum")
+    hbm_peak, _ = peaks()
     tokens = sum(lengths[r] for r in mine)
-    if rank == 0:
-        line = {
-            "metric": "batched decode steps (score+topk+spec attn+repair), requests decoded per second",
-            "value": args.requests * steps / (ms / 1e3), "unit": "requests/s", "n_gpus": world, "steps": steps,
-            "warmup": args.warmup, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; BASELINE config 3 distribution)",
-            "config": {"workload": f"BASELINE config 3: {args.requests} paged requests, context U[8192, 32768], "
-                                   "16q/8kv, D128, page 16, 32-token blocks, K=64, overlap ~ Beta(8,2), bf16",
-                       "parallelism": f"requests split across {world} rank(s) by LPT, no collective",
-                       "l2": f"rank 0 holds {tokens} tokens of KV ({tokens * HKV * D * 4 / 2**30:.1f} GiB, > L2)",
-                       "graph": "one CUDA graph per batched step"},
-            "serial_ms_per_step": ms_ser / steps, "speedup_vs_serial": ms_ser / ms,
-            "clocks": clk.summary(), "peak_gbs": hbm_peak, "peak_kind": peak_kind,
-        }
-        print(json.dumps(line), flush=True)
+    tok_max = all_reduce(tokens, world, device, "max")
+    out = {
+        "workload": f"BASELINE config 3: {args.requests} paged requests, context U[8192, 32768] tokens, 16q/8kv, "
+                    "D128, page 16, 32-token blocks, K=64, overlap ~ Beta(8,2), bf16",
+        "parallelism": f"requests split across {world} rank(s) by LPT, no collective", "ranks": world,
+        "scaling": "strong", "steps_per_repeat": steps,
+        "requests_per_s": args.requests / (times["spec"] / 1e3),
+        "us_per_step": times["spec"] * 1e3, "serial_us_per_step": times["serial"] * 1e3,
+        "speedup_vs_serial": times["serial"] / times["spec"],
+        "relaxed": {"max_extra_mass": eps, "us_per_step": times["relaxed"] * 1e3,
+                    "requests_per_s": args.requests / (times["relaxed"] / 1e3),
+                    "speedup_vs_serial": times["serial"] / times["relaxed"]},
+        "step_algorithmic_bytes": step_bytes,
+        "hbm_frac": step_bytes / (times["spec"] * 1e-3) / 1e9 / (world * hbm_peak),
+        "max_rank_tokens": int(tok_max),
+    }
     graphs.clear()
+    return out
+
+
+# ----------------------------------------------------------------------------- config 4 (context parallel)
+
+def measure_cp(args, rank, world, device, quick=False):
+    """one request of 524,288 tokens (8192 blocks of 64),
+    32 query / 8 KV heads, D 128, bf16, K 256, predicted overlap 0.7, its
+    blocks split evenly across the ranks (context_parallel.decode_step:
+    shard-local candidates -> NCCL all-gather -> global Top-K -> owned
+    states -> NCCL all-gather -> merge). Every rank generates the whole
+    request from one seed, keeps its shard and the full metadata, and checks
+    the step's IDs bit for bit against a single-GPU selection of the whole
+    request. Times: µs per step (max over ranks) and the two all-gathers of a
+    step timed alone."""
+    import torch
+    from strict_topk import gqa
+    from strict_topk_overlap_b200.context_parallel import ProcessGroupComm, decode_step, shard_range
+    hq, hkv, n, b, d, topk = 32, 8, 8192, 64, 128, 256
+    g = torch.Generator(device=device).manual_seed(args.seed + 4444)
+    q = torch.randn(hq, d, device=device, generator=g).to(torch.bfloat16)
+    s, e = shard_range(n, rank, world)
+    ks, vs, los, his = [], [], [], []
+    for h in range(hkv):  # one KV head at a time keeps the FP32 temporaries small
+        kh = torch.randn(n, b, d, device=device, generator=g)
+        kh += torch.randn(n, 1, d, device=device, generator=g) * 0.5
+        kh = kh.to(torch.bfloat16)
+        vh = torch.randn(n, b, d, device=device, generator=g).to(torch.bfloat16)
+        los.append(kh.amin(dim=1).float())
+        his.append(kh.amax(dim=1).float())
+        ks.append(kh[s:e].clone())
+        vs.append(vh[s:e].clone())
+        del kh, vh
+    k = torch.stack(ks).contiguous()
+    v = torch.stack(vs).contiguous()
+    lo_full = torch.stack(los).contiguous()
+    hi_full = torch.stack(his).contiguous()
+    del ks, vs, los, his
+    lo, hi = lo_full[:, s:e].contiguous(), hi_full[:, s:e].contiguous()
+    single = gqa.select_blocks(q, lo_full, hi_full, topk)
+    pred = swap_rows(single.cpu(), n, round(0.3 * topk), args.seed + 45).to(device)
+    comm = ProcessGroupComm()
+    side = torch.cuda.Stream(device)
+    out, sel = decode_step(q, k, v, lo, hi, topk, n, predicted=pred, comm=comm, side_stream=side)
+    torch.cuda.synchronize(device)
+    exact_ids = all_reduce(float(torch.equal(sel, single)), world, device, "min") == 1.0
+    steps = 5 if quick else 20
+
+    def run_k(strict=False):
+        for _ in range(steps):
+            decode_step(q, k, v, lo, hi, topk, n, predicted=None if strict else pred, comm=comm, side_stream=side)
+    for _ in range(3):
+        run_k()
+    reps = timed_repeats(run_k, world, device, min_ms=50.0, quick=quick)
+    us = statistics.median(reps) / steps * 1e3
+    reps_s = timed_repeats(lambda: run_k(strict=True), world, device, min_ms=50.0, quick=quick)
+    us_strict = statistics.median(reps_s) / steps * 1e3
+    # The step's exchanges alone: candidates (keys int64 + IDs int32) and states (m, l, u FP32).
+    keys = torch.zeros((hq, topk), dtype=torch.int64, device=device)
+    ids = torch.zeros((hq, topk), dtype=torch.int32, device=device)
+    ms_, ls_ = torch.zeros(hq, device=device), torch.zeros(hq, device=device)
+    us_ = torch.zeros((hq, d), device=device)
+
+    def exchange():
+        for _ in range(steps):
+            for t in (keys, ids, ms_, ls_, us_):
+                comm.all_gather(t)
+    exchange()
+    reps_c = timed_repeats(exchange, world, device, min_ms=20.0, quick=quick)
+    coll_us = statistics.median(reps_c) / steps * 1e3
+    return {
+        "workload": "BASELINE config 4: 1 request, 524288 tokens in 8192 blocks of 64, 32q/8kv, D128, K=256, "
+                    "overlap 0.7, bf16",
+        "parallelism": f"context split over {world} rank(s), NCCL all-gathers of candidates and (m, l, u) states",
+        "ranks": world, "scaling": "strong", "steps_per_repeat": steps,
+        "us_per_step": us, "strict_us_per_step": us_strict,
+        "collective_us_per_step": coll_us if world > 1 else 0.0,
+        "ids_bit_exact_vs_1gpu": bool(exact_ids),
+        "launch": "eager (host-orchestrated; each all-gather is one NCCL call per tensor)",
+    }
+
+
+def run_single_workload(args):
+    import torch
+    rank, world, local = dist_setup("nccl")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    fn = measure_batched if args.workload == "batched" else measure_cp
+    obj = fn(args, rank, world, device, quick=args.quick)
+    if rank == 0:
+        print(json.dumps({"workload": args.workload, "n_gpus": world, **obj}), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
     return 0
 
 
+# ----------------------------------------------------------------------------- config 1 (headline)
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
-    if args.workload == "batched":
-        return run_batched(args)
+    if args.workload != "c1":
+        return run_single_workload(args)
     import torch
     rank, world, local = dist_setup("nccl")
     device = torch.device("cuda", local)
@@ -422,60 +565,50 @@ def main():
         assert torch.equal(d_.selected.cpu(), s_.selected.cpu())
         assert (o1 - o2).abs().max().item() <= 2e-3, "speculative and serial outputs differ"
 
-    # Timed loops: graphs of `gsteps` consecutive decode steps (one per input
-    # set); a call of spec_step / serial_step runs one such graph.
+    # Exactly K steps per timed region: K // gsteps graphs of `gsteps`
+    # consecutive decode steps (one per input set), then K % gsteps
+    # single-step graphs, continuing the rotation.
     gsteps = max(1, min(args.graph_steps, nsets)) if graph else 1
+    K = max(1, args.steps)
     if gsteps > 1:
         gspec = [capture_steps([dec[(j + i) % nsets] for i in range(gsteps)])[0] for j in range(0, nsets, gsteps)]
         gser = [capture_steps([ser[(j + i) % nsets] for i in range(gsteps)])[0] for j in range(0, nsets, gsteps)]
-
-        def spec_step(i):
-            gspec[i % len(gspec)].replay()
-
-        def serial_step(i):
-            gser[i % len(gser)].replay()
     else:
-        def spec_step(i):
-            dec[i % nsets].step()
+        gspec = gser = None
 
-        def serial_step(i):
-            ser[i % nsets].step()
-    ncalls = max(1, args.steps // gsteps)
-    args.steps = ncalls * gsteps
+    def run_steps(decs, graphs, count):
+        full, rest = divmod(count, gsteps) if graphs else (0, count)
+        for i in range(full):
+            graphs[i % len(graphs)].replay()
+        for i in range(rest):
+            decs[(full * gsteps + i) % nsets].step()
 
     hbm_peak, peak_kind = peaks()
-    # Warm-up (untimed), then a ~1 s load window so clock samples see steady state.
-    for i in range(max(args.warmup // gsteps, 3)):
-        spec_step(i)
+    run_steps(dec, gspec, max(args.warmup, 3 * gsteps))
     torch.cuda.synchronize()
     with ClockSampler(local if not args.quick else -1) as clk:
         t_end = time.perf_counter() + (0.0 if args.quick else 1.0)
         while time.perf_counter() < t_end:
-            for i in range(200 // gsteps + 1):
-                spec_step(i)
+            run_steps(dec, gspec, 200)
             torch.cuda.synchronize()
-        barrier(world)
-        ms = time_loop(spec_step, ncalls, device)
-        barrier(world)
-    ms = max_over_ranks(ms, world, device)
-    us_step = ms * 1e3 / args.steps
-    value = world * args.steps / (ms / 1e3)
+        reps = timed_repeats(lambda: run_steps(dec, gspec, K), world, device, quick=args.quick)
+    ms = statistics.median(reps)
+    us_step = ms * 1e3 / K
+    value = world * K / (ms / 1e3)
     clocks = clk.summary()
 
-    # Serial baseline with the same kernels (same rotation), outside the main region.
-    for i in range(3):
-        serial_step(i)
-    ms_ser = max_over_ranks(time_loop(serial_step, ncalls, device), world, device)
-    us_ser = ms_ser * 1e3 / args.steps
+    # Serial baseline with the same kernels (same rotation and repeats).
+    run_steps(ser, gser, 3 * gsteps)
+    reps_ser = timed_repeats(lambda: run_steps(ser, gser, K), world, device, quick=args.quick)
+    us_ser = statistics.median(reps_ser) * 1e3 / K
     # Context: one CUDA graph per step (graph-launch cost paid every step).
     single = {}
     if graph and gsteps > 1 and not args.quick:
-        n1 = min(args.steps, 2000)
+        n1 = min(K * 10, 2000)
         single = {"spec_us": time_loop(lambda i: dec[i % nsets].step(), n1, device) * 1e3 / n1,
                   "serial_us": time_loop(lambda i: ser[i % nsets].step(), n1, device) * 1e3 / n1}
 
     # Roofline of the dominant kernel: predicted-block attention (block states over P).
-    s0 = sets[0]
     g = HQ // HKV
     blk = B * D * 2
     pstates = [None] * nsets
@@ -499,11 +632,13 @@ def main():
         run_part = lambda i: partials_all()  # noqa: E731
     for i in range(5):
         run_part(i)
-    nrep = 3 if args.quick else max(50, min(args.steps // nsets, 1000))
+    nrep = 3 if args.quick else max(50, min(K // nsets, 1000))
     ms_part = time_loop(run_part, nrep, device, torch.cuda.current_stream())
     us_part = ms_part * 1e3 / (nrep * nsets)
     upred = statistics.mean(unique_blocks(s["p"].cpu(), g) for s in sets)
-    part_bytes = 2 * blk * upred + HQ * D * 2 + HQ * TOPK * 4 + HQ * TOPK * (D + 2) * 4
+    # Algorithmic bytes: unique (KV head, block) K+V of P, Q and the IDs read;
+    # the per-block states written are intermediate and not counted.
+    part_bytes = 2 * blk * upred + HQ * D * 2 + HQ * TOPK * 4
     achieved = part_bytes / (us_part * 1e-6) / 1e9
 
     # Whole-step algorithmic bytes (score + predicted + misses), for context.
@@ -514,28 +649,41 @@ def main():
     step_bytes = score_bytes + 2 * blk * upred + 2 * blk * miss + HQ * D * 4
     serial_bytes = score_bytes + 2 * blk * ua + HQ * D * 4
 
-    # End to end through the public API with host buffers: pinned q and P in,
-    # output back to the host every step.
-    hq_pin = [s["q"].cpu().pin_memory() for s in sets]
-    hp_pin = [s["p"].cpu().pin_memory() for s in sets]
-    hout = torch.empty(HQ, D, dtype=torch.float32).pin_memory()
+    # End to end through the public API with host buffers: each step's graph
+    # copies q and P in from pinned host memory, runs the step and copies the
+    # output back to pinned host memory; the host reads every step's output
+    # (double-buffered: it waits for step i - 1's copy while step i runs).
+    e2e_value = None
+    if graph and not args.quick:
+        hq_pin = [s["q"].cpu().pin_memory() for s in sets]
+        hp_pin = [s["p"].cpu().pin_memory() for s in sets]
+        hout = [torch.empty(HQ, D, dtype=torch.float32).pin_memory() for _ in range(nsets)]
+        for j in range(nsets):
+            dec[j].bind_host(hq_pin[j], hp_pin[j], hout[j])
+        evs = [torch.cuda.Event() for _ in range(nsets)]
 
-    def e2e_step(i):
-        j = i % nsets
-        dec[j].q.copy_(hq_pin[j], non_blocking=True)
-        dec[j].predicted.copy_(hp_pin[j], non_blocking=True)
-        out = dec[j].step()
-        hout.copy_(out, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+        def e2e_steps(count):
+            sink = 0.0
+            for i in range(count):
+                j = i % nsets
+                dec[j].step_host()
+                evs[j].record()
+                jp = (i - 1) % nsets
+                if i > 0:
+                    evs[jp].synchronize()
+                    sink += float(hout[jp][0, 0])
+            torch.cuda.current_stream().synchronize()
+            return sink
 
-    for i in range(20):
-        e2e_step(i)
-    n_e2e = 20 if args.quick else max(100, min(args.steps, 5000))
-    t0 = time.perf_counter()
-    for i in range(n_e2e):
-        e2e_step(i)
-    e2e_s = max_over_ranks(time.perf_counter() - t0, world, device)
-    e2e_value = world * n_e2e / e2e_s
+        e2e_steps(20)
+        n_e2e = max(200, min(K, 5000))
+        barrier(world)
+        t0 = time.perf_counter()
+        e2e_steps(n_e2e)
+        e2e_s = max_over_ranks(time.perf_counter() - t0, world, device)
+        e2e_value = world * n_e2e / e2e_s
+        # The single-step graphs must be replayed again below: re-prime them.
+        torch.cuda.synchronize()
 
     sweep = {}
     if args.sweep and not args.quick:
@@ -555,9 +703,20 @@ def main():
                                               "speedup": round(b_ / a_, 3)}
                 del dd, rr, ss
 
+    # Config 3 and config 4 at the same N (every rank takes part).
+    batched = cp = None
+    if not args.quick and not args.no_batched:
+        del pstates
+        batched = measure_batched(args, rank, world, device)
+        torch.cuda.empty_cache()
+    if not args.quick and not args.no_cp:
+        cp = measure_cp(args, rank, world, device)
+        torch.cuda.empty_cache()
+
     cpu = None
     if rank == 0 and not args.no_cpu_baseline and not args.quick:
         from oracle.cpu_path import serial_step as cpu_step
+        s0 = sets[0]
         torch.set_num_threads(os.cpu_count() or 1)
         cq, ck, cv, clo, chi = (s0[x].cpu() for x in ("q", "k", "v", "lo", "hi"))
         cpu_step(cq, ck, cv, clo, chi, TOPK)
@@ -572,17 +731,19 @@ def main():
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "decode-steps/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "us_per_step": us_step,
+            "metric": METRIC, "value": value, "unit": "decode-steps/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": ms / K, "us_per_step": us_step,
+            "repeats": len(reps), "timed_ms_total": sum(reps), "repeat_ms_min_max": [min(reps), max(reps)],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded; BASELINE config 1 distribution)",
             "config": {"workload": "BASELINE config 1: 1 request, 32q/8kv, D128, 65536 tokens, 32-token blocks, "
                                    "K=64, bf16", "method": args.method, "predicted_overlap": args.overlap,
                        "l2": f"{nsets} rotating input sets x {(2 * HKV * BLOCKS * B * D * 2 + 2 * HKV * BLOCKS * D * 4) / 2**20:.0f} MiB (> 126 MB L2)",
                        "parallelism": f"request replicas x{world} (no collective in the data path)",
+                       "timing": (f"each repeat: exactly {K} steps between barrier + synchronize, CUDA events, max "
+                                  f"over ranks; repeated to >= {MIN_TIMED_MS:.0f} ms, median reported"),
                        "graph": (f"{gsteps} decode steps per CUDA graph (one per input set, replayed; each step one "
-                                 "launch chain: scorer, Top-K, predicted-block states, repair)") if gsteps > 1 else
-                                "one CUDA graph per step (scorer, Top-K, predicted-block states, repair)"},
+                                 "launch chain)") if gsteps > 1 else "one CUDA graph per step"},
             "serial_us_per_step": us_ser, "speedup_vs_serial": us_ser / us_step,
             "one_graph_per_step_us": single or None,
             "step_algorithmic_bytes": step_bytes, "serial_algorithmic_bytes": serial_bytes,
@@ -594,10 +755,16 @@ def main():
                          "traffic": traffic_of("jobs_fast_kernel")},
             "clocks": clocks,
             "e2e": {"value": e2e_value, "unit": "decode-steps/s", "h2d_bytes_per_step": HQ * D * 2 + HQ * TOPK * 4,
-                    "d2h_bytes_per_step": HQ * D * 4},
-            "gpu_launches": LAUNCHES_PER_STEP.get(args.method, 4) * args.steps,
+                    "d2h_bytes_per_step": HQ * D * 4,
+                    "path": "SpeculativeDecoder.bind_host/step_host: pinned H2D of q and P, the step and the D2H of "
+                            "the output in one graph per step; the host reads every step's output"},
+            "gpu_launches": LAUNCHES_PER_STEP.get(args.method, 4) * K * len(reps),
             "cpu_baseline": cpu,
         }
+        if batched:
+            line["batched"] = batched
+        if cp:
+            line["context_parallel"] = cp
         if sweep:
             line["sweep"] = sweep
         print(json.dumps(line), flush=True)

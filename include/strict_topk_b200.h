@@ -122,6 +122,25 @@ STK_API int stk_abi_version(void);
 STK_API const char* stk_last_error(void);
 STK_API int stk_device_sm_count(int device);
 
+/* Limit of every bounded device wait in this library's kernels (a wait on a
+ * bulk copy's mbarrier), in nanoseconds of the GPU's global timer, for the
+ * current device; the default is 2 s, far above any legal copy time. A wait
+ * that runs out writes STK_STATUS_WAIT_TIMEOUT to the call's status word,
+ * waits once more (same limit) for copies still in flight on that barrier,
+ * and its kernel returns without its results; treat the outputs of that call
+ * (and of calls ordered after it on the stream) as invalid. New: no
+ * counterpart in the reference, whose Triton kernels have no bounded waits.
+ * Synchronous (it writes a device constant): call it outside stream capture
+ * and while no kernel of this library runs on the device. */
+STK_API int stk_set_wait_limit_ns(unsigned long long ns);
+
+/* Exercises the bounded-wait path without a fault: one CTA arms an mbarrier
+ * for 16 bytes that no copy will deliver and waits on it with the current
+ * limit, so the wait runs out, STK_STATUS_WAIT_TIMEOUT is written to *status
+ * and the kernel returns (after about twice the limit). It issues no copy and
+ * touches no other memory. New: a test hook with no reference counterpart. */
+STK_API int stk_check_wait_timeout(int32_t* status, void* stream);
+
 /* Fused min/max query-sign bound scores, FP64 fixed-order sum rounded to FP32.
  * Replaces selector.py:23-38 block_scores() (_score, selector.py:8-20) and the
  * scoring half of gqa.py:145-161 (_bound_score, gqa.py:15-26).
@@ -162,9 +181,11 @@ STK_API int stk_select_topk(const void* q, int q_dtype, const float* lo, const f
  * held by every GPU that loads the library until the process exits).
  * Selections needing more than that ((group_select ? hmeta : hq) x
  * total_blocks scores) return STK_EWS. Allocates nothing: no cudaMalloc,
- * cudaFree or allocating library call. The first call on each device looks
- * up the array's device address (cudaGetSymbolAddress) with that device
- * current, so make it before any stream capture. Every call on a device
+ * cudaFree or allocating library call. The first call on each device (and
+ * the first after that device's context is re-created, e.g. by
+ * cudaDeviceReset) looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current, so make it before any
+ * stream capture. Every call on a device
  * shares the one array and leaves its scores in it: calls whose kernels
  * overlap on the GPU (other streams, other threads) race and must be
  * ordered by the caller. */

@@ -217,6 +217,27 @@ def _eps_decision(pred, i, keep, wrong, lm, eps):
     return bool(extra <= F(eps)), extra
 
 
+def _guard_margin(fraction=None, mn=None, residual=None, scale=None, tol=None, extra=None, eps=None):
+    """How close a row's guard inputs sit to their thresholds: the smallest of
+    |fraction - min_remaining|, min over dims with scale > 0 of
+    | |residual| - tol * scale | / scale, and |extra - eps| / eps (each only
+    where the guard was evaluated); inf when no guard applies. Summation
+    orders differ between this restatement and any kernel, so a decision
+    whose margin is within a few FP32 roundings may legitimately differ."""
+    m = np.inf
+    if fraction is not None and np.isfinite(fraction):
+        m = min(m, abs(float(fraction) - float(mn)))
+    if residual is not None:
+        sc = np.asarray(scale, np.float64)
+        pos = sc > 0
+        if pos.any():
+            r = np.abs(np.asarray(residual, np.float64)[pos])
+            m = min(m, float((np.abs(r - float(tol) * sc[pos]) / sc[pos]).min()))
+    if extra is not None and eps is not None and eps > 0:
+        m = min(m, abs(float(extra) - float(eps)) / float(eps))
+    return m
+
+
 def repair(variant, q, k, v, selected, predicted, pred, min_remaining=1e-3, cancellation_tol=1e-5,
            max_extra_mass=0.):
     """Dispatch to one variant: 'split' | 'fused' | 'signed' | 'signed_fused' | 'saved' | 'union'."""
@@ -225,11 +246,11 @@ def repair(variant, q, k, v, selected, predicted, pred, min_remaining=1e-3, canc
     P = np.asarray(predicted).astype(np.int64)
     fn = {"split": _repair_split, "fused": _repair_fused, "signed": _repair_signed,
           "signed_fused": _repair_signed, "saved": _repair_saved, "union": _repair_saved}[variant]
-    res = {k_: [] for k_ in ("output", "fallback", "remaining", "approx", "extra", "pos", "total")}
+    res = {k_: [] for k_ in ("output", "fallback", "remaining", "approx", "extra", "pos", "total", "margin")}
     for i in range(X.h):
         r = fn(X, i, A[i], P[i], pred, F(min_remaining), F(cancellation_tol), F(max_extra_mass), variant)
         for k_ in res:
-            res[k_].append(r.get(k_, 0))
+            res[k_].append(r.get(k_, np.inf if k_ == "margin" else 0))
     out = {k_: np.array(v_) for k_, v_ in res.items()}
     out["output"] = out["output"].astype(np.float32)
     return out
@@ -328,9 +349,10 @@ def _repair_split(X, i, A, P, pred, mn, tol, eps, variant):
         out = (u / max(z, F(1e-30))).astype(np.float32)
     bad = bool(z <= 0 or fraction < mn or np.isnan(fraction) or np.isinf(z) or cancel
                or (~np.isfinite(out)).any())
+    margin = _guard_margin(fraction, mn, residual, scale, tol) if low_hit else np.inf
     if bad:
         out = _strict(X, i, A)
-    return {"output": out, "fallback": bad, "remaining": float(fraction)}
+    return {"output": out, "fallback": bad, "remaining": float(fraction), "margin": margin}
 
 
 def _repair_fused(X, i, A, P, pred, mn, tol, eps, variant):
@@ -345,6 +367,7 @@ def _repair_fused(X, i, A, P, pred, mn, tol, eps, variant):
     retained_m = F(pm.max()) if pm.size else NEG_INF
     fraction, bad, mass, lm, skip, extra = F(1.), False, F(0.), NEG_INF, False, F(0.)
     residual = np.zeros(X.d, np.float32)
+    margin = np.inf
     if hybrid and low_hit:
         lm = F(pred["low_m"][i])
         ll = F(pred["low_l"][i])
@@ -360,6 +383,7 @@ def _repair_fused(X, i, A, P, pred, mn, tol, eps, variant):
         scale = (pred["low_abs"][i] + np.abs(removed_u)).astype(np.float32)
         cancel = bool(((np.abs(residual) < tol * scale) & (scale > 0)).any())
         bad = bool(fraction < mn or np.isnan(fraction) or cancel)
+        margin = _guard_margin(fraction, mn, residual, scale, tol, extra if eps > 0 and wrong.any() else None, eps)
     m = F(max(retained_m, lm))
     ref = F(0.) if m == NEG_INF else m
     alpha = _exp(pm - ref)
@@ -381,7 +405,7 @@ def _repair_fused(X, i, A, P, pred, mn, tol, eps, variant):
         bad = bad or bad_output
     approx = skip and not bad
     return {"output": out, "fallback": bad, "remaining": float(fraction), "approx": approx,
-            "extra": float(extra) if approx else 0.0}
+            "extra": float(extra) if approx else 0.0, "margin": margin}
 
 
 def _repair_signed(X, i, A, P, pred, mn, tol, eps, variant):
@@ -395,7 +419,8 @@ def _repair_signed(X, i, A, P, pred, mn, tol, eps, variant):
     keep = _keep(pred, i, A, hit, high)
     skip, extra = False, F(0.)
     lm = F(pred["low_m"][i]) if hybrid else NEG_INF
-    if hybrid and eps > 0 and wrong.any():
+    decided = bool(hybrid and eps > 0 and wrong.any())
+    if decided:
         skip, extra = _eps_decision(pred, i, keep, wrong, lm, eps)
         wrong = wrong & (not skip)
     pos = int(miss.sum())
@@ -417,6 +442,7 @@ def _repair_signed(X, i, A, P, pred, mn, tol, eps, variant):
     pl = np.where(keep, pred["l"][i], F(0.)).astype(np.float32)
     pu = np.where(keep[:, None], pred["u"][i], F(0.)).astype(np.float32)
     fraction, bad = F(1.), False
+    margin = np.inf
     low_m, low_z, low_u = NEG_INF, F(0.), np.zeros(X.d, np.float32)
     if hybrid and low_hit:
         low_m = lm
@@ -434,6 +460,7 @@ def _repair_signed(X, i, A, P, pred, mn, tol, eps, variant):
         scale = (pred["low_abs"][i] + np.abs(delta_u)).astype(np.float32)
         cancel = bool(((np.abs(low_u) < tol * scale) & (scale > 0)).any())
         bad = bool(fraction < mn or np.isnan(fraction) or cancel)
+        margin = _guard_margin(fraction, mn, low_u, scale, tol, extra if eps > 0 and decided else None, eps)
     posm = [cm for cm, _, _, sg in jobs if sg > 0]
     m = F(max([pm.max() if pm.size else NEG_INF] + posm + [low_m]))
     px = _exp(pm - m)
@@ -455,4 +482,4 @@ def _repair_signed(X, i, A, P, pred, mn, tol, eps, variant):
             out = _strict(X, i, A)
     approx = skip and not bad
     return {"output": out, "fallback": bad, "remaining": float(fraction), "approx": approx,
-            "extra": float(extra) if approx else 0.0, "pos": pos, "total": total}
+            "extra": float(extra) if approx else 0.0, "pos": pos, "total": total, "margin": margin}

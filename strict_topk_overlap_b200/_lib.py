@@ -26,7 +26,8 @@ _DTYPES = {torch.float32: STK_F32, torch.float16: STK_F16, torch.bfloat16: STK_B
 
 # Exported symbols, exactly those declared in include/strict_topk_b200.h.
 SYMBOLS = (
-    "stk_abi_version", "stk_last_error", "stk_device_sm_count", "stk_bound_scores",
+    "stk_abi_version", "stk_last_error", "stk_device_sm_count", "stk_set_wait_limit_ns", "stk_check_wait_timeout",
+    "stk_bound_scores",
     "stk_select_workspace_bytes", "stk_select_topk", "stk_select_topk_static", "stk_merge_candidates", "stk_block_states",
     "stk_merge_states", "stk_reduce_states", "stk_speculate_workspace_bytes", "stk_speculate", "stk_repair",
     "stk_speculative_step_workspace_bytes", "stk_speculative_step", "stk_speculative_step_hybrid_workspace_bytes",
@@ -61,6 +62,8 @@ _SIGS = {
     "stk_abi_version": (_I, []),
     "stk_last_error": (C.c_char_p, []),
     "stk_device_sm_count": (_I, [_I]),
+    "stk_set_wait_limit_ns": (_I, [C.c_ulonglong]),
+    "stk_check_wait_timeout": (_I, [_P, _P]),
     "stk_bound_scores": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _P]),
     "stk_select_workspace_bytes": (_SZ, [_I, _I]),
     "stk_select_topk": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _SZ, _P, _P]),

@@ -696,4 +696,6 @@ int launch_attend(const RepairArgs& a, int kv_dtype, cudaStream_t stream) {
   }
 }
 
+int set_wait_limit_attend(unsigned long long ns) { return set_wait_limit_this_unit(ns); }
+
 }  // namespace stk

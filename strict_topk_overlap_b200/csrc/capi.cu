@@ -1,6 +1,7 @@
 // extern "C" entry points of libstk_sm100.so (declared in include/strict_topk_b200.h).
 // Host-side validation, argument packing and launch orchestration only; all
 // arithmetic lives in select.cu, states.cu and repair.cu.
+#include <cuda.h>
 #include <math.h>
 #include <stdarg.h>
 
@@ -52,6 +53,26 @@ int sm_count_current() {
   return v;
 }
 
+std::atomic<int> g_smem_optin[kMaxDevices];
+
+// Largest dynamic shared memory a CTA may opt in to on the current device.
+int smem_optin_current() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 227 * 1024;
+  int v = g_smem_optin[dev].load(std::memory_order_relaxed);
+  if (v <= 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || v <= 0)
+      v = 227 * 1024;
+    g_smem_optin[dev].store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
+// The hybrid grouping stages a row's (m, l, weight) per predicted slot.
+bool hybrid_group_fits(int sp) {
+  return static_cast<size_t>(sp) * 3 * sizeof(float) <= static_cast<size_t>(smem_optin_current());
+}
+
 bool valid_dtype(int t) { return t == STK_F32 || t == STK_F16 || t == STK_BF16; }
 
 KVLayout make_layout(const stk_kv* kv) {
@@ -85,6 +106,20 @@ int check_kv(const stk_kv* kv, int hq) {
 }
 
 float attn_scale(int d) { return static_cast<float>(1.0 / sqrt(static_cast<double>(d))); }
+
+// Test hook of the bounded-wait path: arm a barrier for bytes no copy will
+// bring and wait on it; mbar_wait gives up after the current limit, records
+// kStatusWaitTimeout and returns. No copy is issued, so nothing is in flight
+// when the CTA exits.
+__global__ void wait_probe_kernel(int* status) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    mbar_arrive_expect_tx(&bar, 16);
+    (void)mbar_wait(&bar, 0, status);
+  }
+}
 }  // namespace
 
 extern "C" {
@@ -97,6 +132,23 @@ int stk_device_sm_count(int device) {
   int v = 0;
   if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return -1;
   return v;
+}
+
+int stk_set_wait_limit_ns(unsigned long long ns) {
+  if (ns == 0) return fail(STK_EINVAL, "the wait limit must be positive");
+  int (*const setters[])(unsigned long long) = {set_wait_limit_select, set_wait_limit_states, set_wait_limit_repair,
+                                                set_wait_limit_attend, set_wait_limit_group_mma};
+  for (auto set : setters) {
+    const int rc = set(ns);
+    if (rc) return cuda_status(rc, "set wait limit");
+  }
+  return cuda_status(set_wait_limit_this_unit(ns), "set wait limit");
+}
+
+int stk_check_wait_timeout(int32_t* status, void* stream) {
+  if (!status) return fail(STK_EINVAL, "status word required");
+  wait_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(status);
+  return cuda_status(static_cast<int>(cudaGetLastError()), "wait probe");
 }
 
 int stk_bound_scores(const void* q, int q_dtype, const float* lo, const float* hi, int hq, int hmeta, int n, int d,
@@ -230,6 +282,8 @@ int stk_speculate(const stk_kv* kv, const void* q, int q_dtype, int rows, int hq
   if (rows <= 0 || rows % hq || sp <= 0) return fail(STK_EINVAL, "bad speculate shape");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int d = kv->d;
+  if (mode == STK_PRED_HYBRID && !hybrid_group_fits(sp))
+    return fail(STK_ESMEM, "hybrid grouping of %d predicted blocks per row exceeds the shared-memory plan", sp);
   if (mode == STK_PRED_SAVED || mode == STK_PRED_HYBRID) {
     rc = stk_block_states(kv, q, q_dtype, rows, hq, pred, pred64, sp, nullptr, 0, 0, nullptr, 0, 0, nullptr,
                           STK_MODE_FULL, nullptr, state_m, state_l, state_u, nullptr, status, stream);
@@ -407,6 +461,8 @@ int stk_speculative_step_hybrid(const stk_kv* kv, const void* q, int q_dtype, co
     return fail(STK_EINVAL, "speculative_step_hybrid repairs with STK_VAR_FUSED or STK_VAR_SIGNED_FUSED");
   if (!(mass_threshold >= 0.f && mass_threshold <= 1.f)) return fail(STK_EINVAL, "mass_threshold must be in [0,1]");
   if (!(max_extra_mass >= 0.f && max_extra_mass <= 1.f)) return fail(STK_EINVAL, "max_extra_mass must be in [0, 1]");
+  if (!hybrid_group_fits(sp))
+    return fail(STK_ESMEM, "hybrid grouping of %d predicted blocks per row exceeds the shared-memory plan", sp);
   const int n = kv->n, d = kv->d;
   if (workspace_bytes < stk_speculative_step_hybrid_workspace_bytes(hq, n, sp, d))
     return fail(STK_EWS, "speculative_step_hybrid workspace too small");
@@ -562,32 +618,66 @@ int stk_touch_kv(const stk_kv* kv, int rows, int hq, const void* ids, int ids64,
 //
 // In host code `g_select_scores` names a host-side stand-in, not device
 // memory, so it is never passed to a kernel. Its device address is looked up
-// once per device with cudaGetSymbolAddress, on the first call made while
-// that device is current, and cached.
+// with cudaGetSymbolAddress on the first call made while a device is current
+// and cached together with the identity of that device's context; when the
+// context differs (after cudaDeviceReset, the module is loaded again), the
+// address is looked up again.
 namespace {
 static __device__ __align__(256) double g_select_scores[STK_SELECT_STATIC_MAX_SCORES];
 
 std::mutex g_static_setup;
-std::atomic<void*> g_select_scores_addr[kMaxDevices];
+void* g_select_scores_addr[kMaxDevices];
+unsigned long long g_select_scores_ctx[kMaxDevices];
+
+// Identity of the calling thread's current context (0 when none is current
+// yet), through the driver entry points the runtime hands out.
+int current_context_id(unsigned long long* id) {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(f);
+  });
+  *id = 0;
+  if (!get_current || !get_id) return fail(STK_EINVAL, "driver context queries unavailable");
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS) return fail(STK_EINVAL, "cuCtxGetCurrent failed");
+  if (ctx == nullptr) return 0;
+  if (get_id(ctx, id) != CUDA_SUCCESS) return fail(STK_EINVAL, "cuCtxGetId failed");
+  return 0;
+}
 
 int static_scores_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return fail(STK_EINVAL, "device %d beyond the %d this library tracks", dev, kMaxDevices);
-  void* p = g_select_scores_addr[dev].load(std::memory_order_acquire);
-  if (p == nullptr) {
-    std::lock_guard<std::mutex> lock(g_static_setup);
-    p = g_select_scores_addr[dev].load(std::memory_order_acquire);
-    if (p == nullptr) {
-      e = cudaGetSymbolAddress(&p, g_select_scores);
-      if (e != cudaSuccess || p == nullptr)
-        return fail(e != cudaSuccess ? static_cast<int>(e) : STK_EINVAL, "cudaGetSymbolAddress(select scratch): %s",
-                    cudaGetErrorString(e));
-      g_select_scores_addr[dev].store(p, std::memory_order_release);
-    }
+  unsigned long long ctx = 0;
+  int rc = current_context_id(&ctx);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lock(g_static_setup);
+  if (ctx == 0 || g_select_scores_addr[dev] == nullptr || g_select_scores_ctx[dev] != ctx) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_select_scores);  // initialises the context when none is current
+    if (e != cudaSuccess || p == nullptr)
+      return fail(e != cudaSuccess ? static_cast<int>(e) : STK_EINVAL, "cudaGetSymbolAddress(select scratch): %s",
+                  cudaGetErrorString(e));
+    rc = current_context_id(&ctx);
+    if (rc) return rc;
+    g_select_scores_addr[dev] = p;
+    g_select_scores_ctx[dev] = ctx;
   }
-  *out = p;
+  *out = g_select_scores_addr[dev];
   return 0;
 }
 }  // namespace

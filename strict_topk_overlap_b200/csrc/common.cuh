@@ -223,11 +223,22 @@ __device__ __forceinline__ unsigned long long global_ns() {
 #endif
 
 // Bounded wait: try_wait (which itself blocks for a short, system-defined
-// time) until the phase completes, giving up once kWaitNs of wall time have
-// passed (far above any legal copy time); a wait that gives up records
-// kStatusWaitTimeout and returns false.
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, int* status) {
+// time) until the phase completes, giving up once c_wait_ns of wall time
+// have passed (default 2 s, far above any legal copy time); a wait that gives
+// up records kStatusWaitTimeout, then waits once more, with the same limit,
+// for the copies still in flight on that barrier (so that its caller does not
+// leave shared memory that a late copy could still write), and returns false.
+//
+// The limit is a runtime value: one copy per translation unit (internal
+// linkage), all of them written by stk_set_wait_limit_ns for the current
+// device through set_wait_limit_this_unit().
+static __constant__ unsigned long long c_wait_ns = 2000000000ull;
+
+static inline int set_wait_limit_this_unit(unsigned long long ns) {
+  return static_cast<int>(cudaMemcpyToSymbol(c_wait_ns, &ns, sizeof(ns)));
+}
+
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, unsigned parity, unsigned long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   while (true) {
@@ -235,9 +246,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, int* s
 #ifdef STK_WAIT_BACKOFF
     __nanosleep(STK_WAIT_BACKOFF);
 #endif
-    if (global_ns() - t0 > kWaitNs) break;
+    if (global_ns() - t0 > limit) return false;
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, int* status) {
+  const unsigned long long limit = c_wait_ns;
+  if (mbar_wait_for(bar, parity, limit)) return true;
   report(status, kStatusWaitTimeout);
+  mbar_wait_for(bar, parity, limit);  // drain: bounded as well
   return false;
 }
 

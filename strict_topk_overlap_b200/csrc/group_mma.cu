@@ -293,4 +293,6 @@ int launch_group_mma(const KVLayout& L, int kv_dtype, const void* q, int G, cons
   return static_cast<int>(cudaGetLastError());
 }
 
+int set_wait_limit_group_mma(unsigned long long ns) { return set_wait_limit_this_unit(ns); }
+
 }  // namespace stk

@@ -181,6 +181,14 @@ inline void prefer_shared(void (*kern)(KArgs...)) {
   cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
 }
 
+// Each translation unit's copy of the bounded-wait limit (common.cuh
+// c_wait_ns), written for the current device.
+int set_wait_limit_select(unsigned long long ns);
+int set_wait_limit_states(unsigned long long ns);
+int set_wait_limit_repair(unsigned long long ns);
+int set_wait_limit_attend(unsigned long long ns);
+int set_wait_limit_group_mma(unsigned long long ns);
+
 int launch_score(const ScoreArgs& a, cudaStream_t stream);
 int launch_select(const SelectArgs& a, int max_n, cudaStream_t stream);
 // Two-stage selection: returns 1 (nothing launched) when the shape has no

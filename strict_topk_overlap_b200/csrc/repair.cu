@@ -876,4 +876,6 @@ int launch_repair(const RepairArgs& a, int kv_dtype, cudaStream_t stream) {
   }
 }
 
+int set_wait_limit_repair(unsigned long long ns) { return set_wait_limit_this_unit(ns); }
+
 }  // namespace stk

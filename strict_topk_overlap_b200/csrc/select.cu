@@ -1273,4 +1273,6 @@ int launch_merge_candidates(const MergeArgs& a, cudaStream_t stream) {
   return static_cast<int>(cudaGetLastError());
 }
 
+int set_wait_limit_select(unsigned long long ns) { return set_wait_limit_this_unit(ns); }
+
 }  // namespace stk

@@ -266,7 +266,14 @@ __global__ void __launch_bounds__(kFastMaxWarps * 32, 1) jobs_fast_kernel(JobArg
       const bool ok = mbar_wait(&mb[slot], (phase >> slot) & 1u, a.status);
       phase ^= 1u << slot;
       if (it < 2) JT(3 + 3 * it);
-      if (!ok) {  // the copies may still be landing: leave this CTA's stages alone
+      if (!ok) {
+        // The ring's later jobs may have copies in flight too: wait for them
+        // (bounded) before this warp stops using its stages.
+#pragma unroll
+        for (int i = 1; i < NS; ++i) {
+          const int st2 = (k + i) % NS;
+          if (fb[i] >= 0) mbar_wait_for(&mb[st2], (phase >> st2) & 1u, c_wait_ns);
+        }
         if (a.chain) pdl_wait();
         return;
       }
@@ -832,5 +839,7 @@ int launch_touch(const KVLayout& L, int rows, int hq, int g, const void* ids, in
   }
   return static_cast<int>(cudaGetLastError());
 }
+
+int set_wait_limit_states(unsigned long long ns) { return set_wait_limit_this_unit(ns); }
 
 }  // namespace stk

@@ -186,6 +186,7 @@ class SpeculativeDecoder:
         self._spec = _speculate_fn(spec, q, k, v, predicted)
         self._finish = _finish_fn(spec, q, k, v, predicted)
         self.graph = None
+        self.host_graph = None
         self.out = None
         self.selected = None
         if graph:
@@ -231,8 +232,44 @@ class SpeculativeDecoder:
         self.out, self.selected = self._run()
         return self.out
 
+    def bind_host(self, q_host, predicted_host, out_host):
+        """Capture the step together with its host I/O: copies of ``q_host``
+        and ``predicted_host`` (pinned host tensors shaped like ``q`` and
+        ``predicted``) into the device inputs, the step, and a copy of the
+        output into the pinned ``out_host``, as one CUDA graph that
+        ``step_host()`` replays. The copies are stream-ordered; the host
+        reads ``out_host`` after synchronising with the stream (or an event
+        recorded after ``step_host()``)."""
+        for t, want in ((q_host, self.q), (predicted_host, self.predicted)):
+            if t.shape != want.shape or t.dtype != want.dtype or t.is_cuda or not t.is_pinned():
+                raise ValueError("host inputs must be pinned CPU tensors shaped like the device inputs")
+        if out_host.is_cuda or not out_host.is_pinned() or out_host.dtype != torch.float32 or \
+                out_host.shape != (self.q.shape[0], self.q.shape[1]):
+            raise ValueError("out_host must be a pinned FP32 CPU tensor [Hq, D]")
+
+        def run():
+            self.q.copy_(q_host, non_blocking=True)
+            self.predicted.copy_(predicted_host, non_blocking=True)
+            out, sel = self._run()
+            out_host.copy_(out, non_blocking=True)
+            return out, sel
+        side = torch.cuda.Stream(self.q.device)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            run()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize(self.q.device)
+        self.host_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.host_graph):
+            self.host_out, self.host_selected = run()
+
+    def step_host(self):
+        """Replay the graph captured by ``bind_host``."""
+        self.host_graph.replay()
+
     def close(self):
         self.graph = None
+        self.host_graph = None
 
 
 def capture_steps(decoders):

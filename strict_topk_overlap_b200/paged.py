@@ -202,7 +202,7 @@ def speculate(q, cache: PagedKVCache, predicted, mode="saved", mass_threshold=0.
 
 
 def _repair(q, cache, selected, predicted, prediction, variant, *, min_remaining=1e-3, cancellation_tol=1e-5,
-            max_extra_mass=0., want_approx=False):
+            max_extra_mass=0., want_approx=False, want_jobs=False):
     hq = _check_q(q, cache)
     _check_ids(selected, q)
     if predicted is not None:
@@ -214,10 +214,12 @@ def _repair(q, cache, selected, predicted, prediction, variant, *, min_remaining
     remaining = torch.empty((rows,), device=dev, dtype=torch.float32)
     approx = torch.empty_like(fallback) if want_approx else None
     extra = torch.empty_like(remaining) if want_approx else None
+    pos = torch.empty((rows,), device=dev, dtype=torch.int32) if want_jobs else None
+    total = torch.empty_like(pos) if want_jobs else None
     kv = cache.kv()
     ps = _prediction_struct(prediction)
     ro = L.StkRepairOut(out.data_ptr(), fallback.data_ptr(), remaining.data_ptr(), L.ptr(approx), L.ptr(extra),
-                        None, None)
+                        L.ptr(pos), L.ptr(total))
     sp = predicted.shape[1] if predicted is not None else 0
     rc = L.load().stk_repair(
         C.byref(kv), q.data_ptr(), L.dtype_code(q), rows, hq, selected.data_ptr(), L.id_is64(selected),
@@ -225,6 +227,8 @@ def _repair(q, cache, selected, predicted, prediction, variant, *, min_remaining
         variant, float(min_remaining), float(cancellation_tol), float(max_extra_mass), cache.max_blocks,
         C.byref(ro), L.status_ptr(), L.stream_of(q))
     L.check(rc, "repair (batched)")
+    if want_jobs:
+        return out, fallback, remaining, approx, extra, pos, total
     return out, fallback, remaining, approx, extra
 
 
@@ -254,6 +258,23 @@ def repair_fused(q, cache: PagedKVCache, selected, predicted, prediction, min_re
         res.approximate_heads = approx
         res.extra_mass_bound = extra
     return res
+
+
+def repair_signed_fused(q, cache: PagedKVCache, selected, predicted, prediction, min_remaining=1.e-3,
+                        cancellation_tol=1.e-5, max_extra_mass=0.):
+    """Signed add/erase repair with inline strict fallback (semantics of
+    signed_fused.repair_signed_fused, per row), relaxed by ``max_extra_mass``
+    when it is positive; also returns the positive / total job counts."""
+    from .signed_repair import SignedRepairResult
+    if not 0 <= max_extra_mass <= 1:
+        raise ValueError("max_extra_mass must be in [0, 1]")
+    if max_extra_mass > 0 and prediction.mode != "saved" and prediction.mass_m is None:
+        raise ValueError("positive max_extra_mass requires speculate(..., keep_mass=True)")
+    out, fallback, remaining, approx, extra, pos, total = _repair(
+        q, cache, selected, predicted, prediction, L.VAR_SIGNED_FUSED, min_remaining=min_remaining,
+        cancellation_tol=cancellation_tol, max_extra_mass=max_extra_mass, want_approx=max_extra_mass > 0,
+        want_jobs=True)
+    return SignedRepairResult(out, fallback, remaining, approx, extra, pos, total)
 
 
 # ----------------------------------------------------------------------------- sharding

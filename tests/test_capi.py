@@ -57,6 +57,9 @@ def test_host_validation_without_gpu(lib):
     kv = L.StkKV(1, 1, 2, 3, 10, 32, 128, None, None, 0, 0)
     assert lib.stk_touch_kv(C.byref(kv), 4, 4, 1, 0, 1, 1, None) == -1  # 4 % 3 != 0
     assert b"divisible" in lib.stk_last_error()
+    # The wait-limit setter and the wait probe validate before touching a device.
+    assert lib.stk_set_wait_limit_ns(0) == -1 and b"positive" in lib.stk_last_error()
+    assert lib.stk_check_wait_timeout(None, None) == -1
 
 
 def test_no_cpu_fallback_in_product():

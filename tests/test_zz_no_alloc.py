@@ -62,6 +62,34 @@ def test_static_select_matches_workspace_select(group_select):
         assert int(got_ids.min()) >= 0
 
 
+def test_static_select_allocates_nothing():
+    """After the first call (which looks up the array's address), further
+    calls leave the device's free memory unchanged: the library allocates
+    nothing for them. Outputs are allocated before the measurement."""
+    from strict_topk_overlap_b200 import _lib as L
+    lib = L.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    q, k, v, lo, hi = cases.synthetic_kv(32, 8, 2048, 32, 128, torch.bfloat16, seed=3)
+    qd, lod, hid = q.to(dev), lo.to(dev), hi.to(dev)
+    ids = torch.empty((32, 64), device=dev, dtype=torch.int32)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+
+    def call():
+        rc = lib.stk_select_topk_static(qd.data_ptr(), L.dtype_code(qd), lod.data_ptr(), hid.data_ptr(), 1, 32, 8,
+                                        2048, None, 2048, 2048, 128, 64, 0, 0, ids.data_ptr(), None, None, stream)
+        assert rc == 0, lib.stk_last_error().decode()
+
+    call()
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info(dev)
+    for _ in range(2):
+        call()
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info(dev)
+    assert free_after == free_before, (free_before, free_after)
+
+
 def test_static_select_rejects_oversize():
     from strict_topk_overlap_b200 import _lib as L
     lib = L.load()
