@@ -271,6 +271,36 @@ STK_API int stk_speculative_step(const stk_kv* kv, const void* q, int q_dtype, c
                                  int topk, const void* pred, int pred64, int sp, int32_t* selected, float* out,
                                  void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
+/* Workspace (bytes) for stk_decode_step: a control block of
+ * (hkv + 2 hq + 1) 32-bit counters, then one 8-byte score slot per (query
+ * head, block) and the block states of `slots` blocks per query head
+ * (slots = sp for a speculative step, topk for a serial one). */
+STK_API size_t stk_decode_step_workspace_bytes(int hq, int hkv, int n, int slots, int d);
+
+/* The whole decode step in one persistent, cooperative launch (one CTA per
+ * SM; CTAs wait for one another through the workspace's counters, every wait
+ * bounded by the library's wait limit).
+ * With pred (sp > 0): the speculative saved step — the strict Top-K
+ * selection, the states of the predicted blocks computed while the selection
+ * runs, and the saved repair (hits reused, misses computed) — equal to
+ * stk_speculative_step. Replaces the reference's overlapped step
+ * (benchmarks/run_benchmark.py:99-118: selector.py:41-43 / gqa.py:145-161
+ * select_blocks || gqa.py:128-137 partials, then gqa.py:186-188
+ * repair_saved).
+ * With pred == NULL (sp == 0): the serial step — selection, then exact
+ * attention over the selected blocks (run_benchmark.py:139,
+ * critical_path.py:110: gqa.py:140-142 exact(select_blocks(...))).
+ * One dense request; D = 128, 32-token blocks, 16-bit K/V, at most 16 query
+ * heads per KV head and 4096 query values (hq * d), topk <= n <= 4096,
+ * topk and sp <= 256, fewer than half as many query heads as SMs; other
+ * shapes return STK_ESMEM and take stk_speculative_step / stk_select_topk +
+ * stk_repair. The workspace must be zero before its first use (e.g. one
+ * cudaMemset after allocation); every call leaves its control block zero
+ * again. Calls sharing a workspace must be ordered on one stream. */
+STK_API int stk_decode_step(const stk_kv* kv, const void* q, int q_dtype, const float* lo, const float* hi, int hq,
+                            int topk, const void* pred, int pred64, int sp, int32_t* selected, float* out,
+                            void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
 /* Workspace (bytes) for stk_speculative_step_hybrid: the saved step's
  * workspace plus the hybrid grouping's high mask and low aggregate. */
 STK_API size_t stk_speculative_step_hybrid_workspace_bytes(int hq, int n, int sp, int d);

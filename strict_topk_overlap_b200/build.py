@@ -18,7 +18,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 OUT_DIR = PKG / "_lib"
 LIB = OUT_DIR / "libstk_sm100.so"
-SOURCES = ["select.cu", "states.cu", "repair.cu", "attend.cu", "metadata.cu", "group_mma.cu", "capi.cu"]
+SOURCES = ["select.cu", "states.cu", "repair.cu", "attend.cu", "metadata.cu", "group_mma.cu", "step.cu", "capi.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "--extended-lambda",
          "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "-diag-suppress", "177,550"]

@@ -137,7 +137,7 @@ int stk_device_sm_count(int device) {
 int stk_set_wait_limit_ns(unsigned long long ns) {
   if (ns == 0) return fail(STK_EINVAL, "the wait limit must be positive");
   int (*const setters[])(unsigned long long) = {set_wait_limit_select, set_wait_limit_states, set_wait_limit_repair,
-                                                set_wait_limit_attend, set_wait_limit_group_mma};
+                                                set_wait_limit_attend, set_wait_limit_group_mma, set_wait_limit_step};
   for (auto set : setters) {
     const int rc = set(ns);
     if (rc) return cuda_status(rc, "set wait limit");
@@ -437,6 +437,60 @@ int stk_speculative_step(const stk_kv* kv, const void* q, int q_dtype, const flo
   r.status = status;
   r.chain = 1;
   return cuda_status(launch_repair(r, kv->kv_dtype, st), "repair (chained)");
+}
+
+static size_t decode_step_ctrl_bytes(int hq, int hkv) {
+  return align256(static_cast<size_t>(hkv + 2 * hq + 1) * sizeof(unsigned));
+}
+
+size_t stk_decode_step_workspace_bytes(int hq, int hkv, int n, int slots, int d) {
+  if (hq <= 0 || hkv <= 0 || n <= 0 || slots <= 0 || d <= 0) return 0;
+  const size_t s = static_cast<size_t>(hq) * slots;
+  return decode_step_ctrl_bytes(hq, hkv) + align256(stk_select_workspace_bytes(hq, n)) +
+         2 * align256(s * sizeof(float)) + align256(s * d * sizeof(float));
+}
+
+int stk_decode_step(const stk_kv* kv, const void* q, int q_dtype, const float* lo, const float* hi, int hq, int topk,
+                    const void* pred, int pred64, int sp, int32_t* selected, float* out, void* workspace,
+                    size_t workspace_bytes, int32_t* status, void* stream) {
+  int rc = check_kv(kv, hq);
+  if (rc) return rc;
+  if (kv->page_table || kv->block_offsets || kv->kv_request_stride) return fail(STK_EINVAL, "decode_step takes one dense request");
+  if (!q || !lo || !hi || !selected || !out || !workspace || !valid_dtype(q_dtype))
+    return fail(STK_EINVAL, "null pointer or unsupported q dtype");
+  if ((pred == nullptr) != (sp == 0) || sp < 0) return fail(STK_EINVAL, "pred and sp > 0 go together (sp = 0: serial)");
+  const int n = kv->n, d = kv->d;
+  if (topk <= 0 || topk > n) return fail(STK_EINVAL, "topk %d outside [1, %d]", topk, n);
+  const int nsm = sm_count_current();
+  if (const char* why = decode_step_unsupported(hq, kv->hkv, n, kv->b, d, kv->kv_dtype, topk, sp, nsm))
+    return fail(STK_ESMEM, "%s", why);
+  if (decode_step_smem(hq) + 40 * 1024 > static_cast<size_t>(smem_optin_current()))
+    return fail(STK_ESMEM, "the fused step's shared memory exceeds this device's limit");
+  const uintptr_t align = reinterpret_cast<uintptr_t>(lo) | reinterpret_cast<uintptr_t>(hi) |
+                          reinterpret_cast<uintptr_t>(kv->k) | reinterpret_cast<uintptr_t>(kv->v);
+  if (align & 15) return fail(STK_EINVAL, "lo, hi, K and V must be 16-byte aligned");
+  const int slots = sp > 0 ? sp : topk;
+  if (workspace_bytes < stk_decode_step_workspace_bytes(hq, kv->hkv, n, slots, d))
+    return fail(STK_EWS, "decode_step workspace too small");
+  unsigned char* w = static_cast<unsigned char*>(workspace);
+  StepArgs a{};
+  a.q = q; a.q_dtype = q_dtype; a.lo = lo; a.hi = hi; a.k = kv->k; a.v = kv->v;
+  a.hq = hq; a.hkv = kv->hkv; a.n = n; a.topk = topk;
+  a.pred = pred; a.pred64 = pred64; a.sp = sp;
+  a.selected = selected; a.out = out;
+  a.ctrl = reinterpret_cast<unsigned*>(w);
+  w += decode_step_ctrl_bytes(hq, kv->hkv);
+  a.bounds = reinterpret_cast<float2*>(w);
+  w += align256(stk_select_workspace_bytes(hq, n));
+  const size_t s = static_cast<size_t>(hq) * slots;
+  a.sm = reinterpret_cast<float*>(w);
+  w += align256(s * sizeof(float));
+  a.sl = reinterpret_cast<float*>(w);
+  w += align256(s * sizeof(float));
+  a.su = reinterpret_cast<float*>(w);
+  a.status = status;
+  a.scale = attn_scale(d);
+  return cuda_status(launch_decode_step(a, kv->kv_dtype, nsm, static_cast<cudaStream_t>(stream)), "decode_step");
 }
 
 size_t stk_speculative_step_hybrid_workspace_bytes(int hq, int n, int sp, int d) {

@@ -144,6 +144,30 @@ struct RepairArgs {
   int chain;
 };
 
+// The fused decode step (step.cu): one dense request, D = 128, 32-token
+// blocks, 16-bit K/V. sp = 0 runs the serial step (selection, then
+// attention over the selected blocks).
+struct StepArgs {
+  const void* q;  // [hq, D]
+  int q_dtype;
+  const float* lo;  // [hkv, n, D]
+  const float* hi;
+  const void* k;  // [hkv, n, B, D]
+  const void* v;
+  int hq, hkv, n, topk;
+  const void* pred;  // [hq, sp] predicted IDs; null (sp = 0) for the serial step
+  int pred64, sp;
+  int* selected;   // [hq, topk] out, ascending
+  float* out;      // [hq, D] out
+  float2* bounds;  // [hq, n] score intervals
+  float* sm;       // [hq, S] block states, S = sp (speculative) or topk (serial)
+  float* sl;
+  float* su;       // [hq, S, D]
+  unsigned* ctrl;  // [hkv + 2 hq + 1]
+  int* status;
+  float scale;
+};
+
 // Launch `kern` with programmatic stream serialization: it may begin while
 // the previous kernel on `stream` finishes (it must call pdl_wait() before
 // reading that kernel's outputs). Optional cluster size (x) when cluster > 0.
@@ -188,6 +212,7 @@ int set_wait_limit_states(unsigned long long ns);
 int set_wait_limit_repair(unsigned long long ns);
 int set_wait_limit_attend(unsigned long long ns);
 int set_wait_limit_group_mma(unsigned long long ns);
+int set_wait_limit_step(unsigned long long ns);
 
 int launch_score(const ScoreArgs& a, cudaStream_t stream);
 int launch_select(const SelectArgs& a, int max_n, cudaStream_t stream);
@@ -227,5 +252,12 @@ int launch_touch(const KVLayout& L, int rows, int hq, int g, const void* ids, in
 int launch_repair(const RepairArgs& a, int kv_dtype, cudaStream_t stream);
 // Exact / saved / union (plain LSE merge) fast path; returns 1 when it does not apply.
 int launch_attend(const RepairArgs& a, int kv_dtype, cudaStream_t stream);
+// The fused decode step: dynamic shared memory per CTA, the reason a shape
+// is outside its plan (null when it fits), and the cooperative launch (one
+// CTA per SM).
+size_t decode_step_smem(int hq);
+const char* decode_step_unsupported(int hq, int hkv, int n, int b, int d, int kv_dtype, int topk, int sp,
+                                    int num_sms);
+int launch_decode_step(const StepArgs& a, int kv_dtype, int num_sms, cudaStream_t stream);
 
 }  // namespace stk

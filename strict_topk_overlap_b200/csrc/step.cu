@@ -1,0 +1,534 @@
+// The whole decode step in one persistent, cooperative launch.
+//
+// Replaces, for one dense request (D = 128, 32-token blocks, 16-bit K/V):
+//   * the speculative saved step of the reference harness
+//     (benchmarks/run_benchmark.py:99-118): selection (selector.py:8-43,
+//     gqa.py:15-26,145-161) || predicted-block states (kernels.py:42-71,
+//     gqa.py:29-59,128-137), then the saved repair (gqa.py:62-104,186-188);
+//   * the serial step (critical_path.py:110, run_benchmark.py:139):
+//     selection, then exact attention over the selected blocks
+//     (kernels.py:445-447, gqa.py:140-142).
+//
+// Why one launch: at decode sizes every stage is latency-bound. Launched
+// separately, each kernel pays a launch, a cold instruction cache and a grid
+// drain before its successor's wait returns; the predicted-block stream can
+// only overlap the Top-K kernel's latency. Here the metadata stream, the
+// predicted-block stream and the per-row selections run concurrently on all
+// SMs, and each row's repair starts as soon as its own inputs are ready.
+//
+// Grid: one CTA per SM, launched cooperatively so that every CTA is resident
+// and a CTA may wait for another's progress (each such wait is bounded by
+// the library's wait limit and reports STK_STATUS_WAIT_TIMEOUT when it runs
+// out). The last hq CTAs are row CTAs: CTA grid - hq + r scores its share
+// of the metadata, selects row r's strict Top-K (the second stage of the
+// two-stage selection, topk.cuh) and finishes row r. The other CTAs score
+// their share of the metadata, then compute per-block states: of the
+// predicted blocks (speculative step, from the start), or of the selected
+// blocks as each row's selection is published (serial step).
+//
+// Inside a CTA, warp 15 issues 1-D bulk copies into a ring of 16 KiB stages
+// (each on a "full" mbarrier with the copy's byte count) in item order:
+// first the CTA's metadata items (16 blocks of one KV head: their lo rows,
+// then their hi rows), then its block items (one block's K then V). Warps
+// 0..14 take the items round-robin, reduce them and release each stage on
+// its "empty" mbarrier. The small loads (q, predicted IDs) are issued before
+// any bulk copy: a load queued behind the bulk stream waits for all of it.
+//
+// Cross-CTA progress goes through counters in the workspace's control
+// block, which must be zero before the first call on a workspace; the last
+// CTA to finish a call zeroes it again:
+//   ctrl[mh]                metadata items done for KV head mh,
+//   ctrl[hkv + r]           block states done for row r,
+//   ctrl[hkv + hq + r]      row r's selection published (serial step),
+//   ctrl[hkv + 2 hq]        CTAs finished.
+// A writer publishes after its global writes with a fence and an atomic add;
+// a reader waits with acquire loads and reads the data through L2.
+
+#include "block_state.cuh"
+#include "topk.cuh"
+
+namespace stk {
+
+constexpr int kStepThreads = 512;
+constexpr int kStepWarps = kStepThreads / 32;
+constexpr int kStepProducer = kStepWarps - 1;  // issues the bulk copies
+constexpr int kStepConsumers = kStepWarps - 1;
+constexpr int kStepStages = 10;
+constexpr int kStepD = 128;
+constexpr int kStepB = 32;
+constexpr int kStepDPH = kStepD / 16;
+constexpr int kStageBytes = 2 * kStepB * kStepD * 2;            // one 16-bit K+V block: 16 KiB
+constexpr int kMetaItemBlocks = kStageBytes / (2 * kStepD * 4);  // 16 blocks of FP32 lo + hi
+constexpr int kStepMaxList = 256;                                // topk and predicted-list limit
+constexpr int kStepMaxBlocks = 4096;                             // blocks per request limit
+
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// One thread: wait until *p >= target, bounded by the library's wait limit.
+__device__ bool wait_count(const unsigned* p, unsigned target) {
+  if (ld_acquire_gpu(p) >= target) return true;
+  const unsigned long long t0 = global_ns(), limit = c_wait_ns;
+  while (ld_acquire_gpu(p) < target) {
+    __nanosleep(64);
+    if (global_ns() - t0 > limit) return false;
+  }
+  return true;
+}
+
+// One thread, after the writes it publishes are ordered before it (warp or
+// CTA barrier): make them visible GPU-wide, then count.
+__device__ __forceinline__ void publish(unsigned* p) {
+  __threadfence();
+  atomicAdd(p, 1u);
+}
+
+// Fold a block state (m, l, u) into a running LSE state (wm, wl, wu).
+__device__ __forceinline__ void fold_state(float& wm, float& wl, float (&wu)[kStepDPH], float m, float l,
+                                           const float (&u)[kStepDPH]) {
+  if (!(m > neg_inf())) return;
+  const float M = fmaxf(wm, m);
+  const float a = expf(wm - M);
+  const float b = expf(m - M);
+  wl = wl * a + l * b;
+#pragma unroll
+  for (int j = 0; j < kStepDPH; ++j) wu[j] = wu[j] * a + u[j] * b;
+  wm = M;
+}
+
+template <typename T, int E, int GM>
+__global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a) {
+  constexpr int D = kStepD;
+  constexpr int DPH = kStepDPH;
+  constexpr int NS = kStepStages;
+  constexpr float kErrFactor = 2.f * (D / 4 + 2) * 0x1p-24f;  // the interval scorer's radius (select.cu)
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ uint64_t full_bar[NS], empty_bar[NS];
+  __shared__ int item_ok[NS];
+  __shared__ volatile int s_abort;
+  __shared__ int s_sel[kStepMaxList], s_pid[kStepMaxList], s_miss[kStepMaxList], s_hit[kStepMaxList];
+  __shared__ int s_nmiss, s_nhit;
+  __shared__ unsigned s_pmask[kStepMaxBlocks / 32], s_amask[kStepMaxBlocks / 32];
+  __shared__ float s_wm[kStepWarps], s_wl[kStepWarps];
+  __shared__ __align__(16) float s_wu[kStepWarps][D];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int hq = a.hq, hkv = a.hkv, n = a.n, K = a.topk;
+  const int G = hq / hkv;
+  const int grid = gridDim.x;
+  const int first_row_cta = grid - hq;
+  const bool row_cta = static_cast<int>(blockIdx.x) >= first_row_cta;
+  const int row = row_cta ? static_cast<int>(blockIdx.x) - first_row_cta : -1;
+  const bool serial = a.sp == 0;
+  const int S = serial ? K : a.sp;
+  const int ipH = (n + kMetaItemBlocks - 1) / kMetaItemBlocks;  // metadata items per KV head
+  const int n_meta = hkv * ipH;
+  const int my_meta = static_cast<int>(blockIdx.x) < n_meta ? (n_meta - 1 - static_cast<int>(blockIdx.x)) / grid + 1 : 0;
+  const long long J = static_cast<long long>(hq) * S;
+  const int j0 = row_cta ? 0 : static_cast<int>(J * blockIdx.x / first_row_cta);
+  const int j1 = row_cta ? 0 : static_cast<int>(J * (blockIdx.x + 1) / first_row_cta);
+  const int my_jobs = j1 - j0;
+  const int n_items = my_meta + my_jobs;
+  unsigned* head_done = a.ctrl;
+  unsigned* row_states = a.ctrl + hkv;
+  unsigned* row_ready = a.ctrl + hkv + hq;
+  unsigned* ctas_done = a.ctrl + hkv + 2 * hq;
+
+  float* qs = reinterpret_cast<float*>(smem);  // [hq][D] FP32
+  float* qn1 = qs + hq * D;                     // [hq] ||q||_1, rounded up
+  unsigned char* pool = smem + ((static_cast<size_t>(hq) * D + hq) * 4 + 127) / 128 * 128;
+  const T* Kp = static_cast<const T*>(a.k);
+  const T* Vp = static_cast<const T*>(a.v);
+  constexpr unsigned kBlockBytes = kStepB * D * sizeof(T);
+
+  // ---------------------------------------------------------------- set-up
+  if (tid == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    fence_barrier_init();
+    s_abort = 0;
+  }
+  // Small loads first (q, the row's predicted IDs, the producer's job IDs).
+  for (int i = tid; i < hq * D; i += kStepThreads) qs[i] = load_any(a.q, a.q_dtype, i);
+  if (row_cta && !serial)
+    for (int i = tid; i < a.sp; i += kStepThreads)
+      s_pid[i] = static_cast<int>(load_id(a.pred, a.pred64, static_cast<long long>(row) * a.sp + i));
+  long long lid = -1;  // producer lane: ID of job j0 + jb + lane (speculative step)
+  int jb = 0;
+  if (warp == kStepProducer && !serial && lane < my_jobs) lid = load_id(a.pred, a.pred64, j0 + lane);
+  __syncthreads();
+  for (int t = warp; t < hq; t += kStepWarps) {
+    float sum = 0.f;
+    for (int dd = lane; dd < D; dd += 32) sum = __fadd_ru(sum, fabsf(qs[t * D + dd]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum = __fadd_ru(sum, __shfl_xor_sync(kFull, sum, o));
+    if (lane == 0) qn1[t] = sum;
+  }
+  __syncthreads();
+
+  // ---------------------------------------------------------------- producer
+  // Issues item `it` into stage it % NS once the consumer of item it - NS has
+  // released it. An item it cannot fill (a bad ID, or after an abort) is
+  // completed without a copy and flagged, so that its consumer skips it.
+  auto produce = [&](int it, int kind, int mh_or_row, long long first, long long id) {
+    const int st = it % NS;
+    if (it >= NS && !mbar_wait(&empty_bar[st], ((it / NS) - 1) & 1u, a.status)) s_abort = 1;
+    unsigned char* stage = pool + static_cast<size_t>(st) * kStageBytes;
+    if (kind == 0) {  // metadata: rows [first, first + nb) of KV head mh
+      const int nb = min(kMetaItemBlocks, n - static_cast<int>(first));
+      const unsigned bytes = static_cast<unsigned>(nb) * D * 4;
+      const long long off = (static_cast<long long>(mh_or_row) * n + first) * D;
+      item_ok[st] = 1;
+      mbar_arrive_expect_tx(&full_bar[st], 2 * bytes);
+      bulk_g2s(stage, a.lo + off, bytes, &full_bar[st]);
+      bulk_g2s(stage + kStageBytes / 2, a.hi + off, bytes, &full_bar[st]);
+    } else if (id >= 0 && id < n && !s_abort) {  // one block of KV head mh_or_row
+      const long long off = (static_cast<long long>(mh_or_row) * n + id) * kStepB * D;
+      item_ok[st] = 1;
+      mbar_arrive_expect_tx(&full_bar[st], 2 * kBlockBytes);
+      bulk_g2s(stage, Kp + off, kBlockBytes, &full_bar[st]);
+      bulk_g2s(stage + kBlockBytes, Vp + off, kBlockBytes, &full_bar[st]);
+    } else {
+      if (id >= n) report(a.status, kStatusBadBlockId);
+      item_ok[st] = 0;
+      mbar_arrive(&full_bar[st]);
+    }
+  };
+
+  if (warp == kStepProducer) {
+    for (int it = 0; it < n_items; ++it) {
+      if (it < my_meta) {
+        if (lane == 0) {
+          const int m = static_cast<int>(blockIdx.x) + it * grid;
+          produce(it, 0, m / ipH, static_cast<long long>(m % ipH) * kMetaItemBlocks, 0);
+        }
+      } else {
+        const int jl = it - my_meta;  // this CTA's job index
+        const int job = j0 + jl;
+        const int r = job / S, slot = job - r * S;
+        long long id = -1;
+        if (!serial) {
+          if (jl - jb == 32) {
+            jb += 32;
+            lid = jb + lane < my_jobs ? load_id(a.pred, a.pred64, j0 + jb + lane) : -1;
+          }
+          id = __shfl_sync(kFull, lid, jl - jb);
+        } else if (lane == 0) {
+          if (!s_abort && !wait_count(&row_ready[r], 1)) {
+            report(a.status, kStatusWaitTimeout);
+            s_abort = 1;
+          }
+          if (!s_abort) id = __ldcg(a.selected + static_cast<long long>(r) * K + slot);
+        }
+        if (lane == 0) produce(it, 1, r / G, 0, id);
+      }
+      __syncwarp();
+    }
+  } else {
+    // -------------------------------------------------------------- consumers
+    for (int it = warp; it < n_items; it += kStepConsumers) {
+      const int st = it % NS;
+      const bool landed = mbar_wait(&full_bar[st], (it / NS) & 1u, a.status);
+      if (!landed) s_abort = 1;
+      const bool ok = landed && item_ok[st] != 0;
+      const unsigned char* stage = pool + static_cast<size_t>(st) * kStageBytes;
+      if (it < my_meta) {
+        // Score intervals of up to 16 blocks of KV head mh for its G query
+        // heads, 8 blocks per pass; lane = block * 4 + quarter of D, the
+        // lane mapping, error bound and rounding of bound_interval_kernel.
+        const int m = static_cast<int>(blockIdx.x) + it * grid;
+        const int mh = m / ipH;
+        const int b0 = (m % ipH) * kMetaItemBlocks;
+        const int nb = min(kMetaItemBlocks, n - b0);
+        const float* slo = reinterpret_cast<const float*>(stage);
+        const float* shi = reinterpret_cast<const float*>(stage + kStageBytes / 2);
+        const float* qrow = qs + mh * G * D;
+        const int p = lane & 3;
+        if (ok) {
+#pragma unroll 1
+          for (int pass = 0; pass < kMetaItemBlocks / 8; ++pass) {
+            const int b = pass * 8 + (lane >> 2);
+            const bool live = b < nb;
+            const float4* L4 = reinterpret_cast<const float4*>(slo + (live ? b : 0) * D);
+            const float4* H4 = reinterpret_cast<const float4*>(shi + (live ? b : 0) * D);
+            float s[GM];
+#pragma unroll
+            for (int g = 0; g < GM; ++g) s[g] = 0.f;
+            float mabs = 0.f;
+#pragma unroll
+            for (int i = 0; i < D / 16; ++i) {
+              const float4 l = live ? L4[p + 4 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
+              const float4 h = live ? H4[p + 4 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
+              mabs = fmaxf(mabs, fmaxf(fmaxf(fabsf(l.x), fabsf(h.x)), fmaxf(fabsf(l.y), fabsf(h.y))));
+              mabs = fmaxf(mabs, fmaxf(fmaxf(fabsf(l.z), fabsf(h.z)), fmaxf(fabsf(l.w), fabsf(h.w))));
+              const int off = 4 * (p + 4 * i);
+#pragma unroll
+              for (int g = 0; g < GM; ++g) {
+                if (g < G) {
+                  const float4 qq = *reinterpret_cast<const float4*>(qrow + g * D + off);
+                  s[g] = fmaf(qq.x, qq.x >= 0.f ? h.x : l.x, s[g]);
+                  s[g] = fmaf(qq.y, qq.y >= 0.f ? h.y : l.y, s[g]);
+                  s[g] = fmaf(qq.z, qq.z >= 0.f ? h.z : l.z, s[g]);
+                  s[g] = fmaf(qq.w, qq.w >= 0.f ? h.w : l.w, s[g]);
+                }
+              }
+            }
+#pragma unroll
+            for (int g = 0; g < GM; ++g) {
+              s[g] += __shfl_xor_sync(kFull, s[g], 1);
+              s[g] += __shfl_xor_sync(kFull, s[g], 2);
+            }
+            mabs = fmaxf(mabs, __shfl_xor_sync(kFull, mabs, 1));
+            mabs = fmaxf(mabs, __shfl_xor_sync(kFull, mabs, 2));
+            if (live) {
+              const float inf = __int_as_float(0x7f800000);
+#pragma unroll
+              for (int g = 0; g < GM; ++g) {
+                if (g < G && (g & 3) == p) {
+                  const float e = __fadd_ru(__fmul_ru(__fmul_ru(qn1[mh * G + g], mabs), kErrFactor), 0x1p-118f);
+                  float2 iv = make_float2(__fsub_rd(s[g], e), __fadd_ru(s[g], e));
+                  if (!(iv.x <= iv.y)) iv = make_float2(-inf, inf);
+                  a.bounds[static_cast<long long>(mh * G + g) * n + b0 + b] = iv;
+                }
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&empty_bar[st]);
+          publish(&head_done[mh]);
+        }
+      } else {
+        // One block's softmax state for (row r, slot).
+        const int job = j0 + (it - my_meta);
+        const int r = job / S, slot = job - r * S;
+        float m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
+#pragma unroll
+        for (int j = 0; j < DPH; ++j) { u[j] = 0.f; ua[j] = 0.f; }
+        if (ok) {
+          float qf[DPH];
+#pragma unroll
+          for (int j = 0; j < DPH; ++j) qf[j] = qs[r * D + (lane & 15) * DPH + j];
+          const T* ks = reinterpret_cast<const T*>(stage);
+          warp_block_state<T, DPH, kModeFull, true>(ks, ks + kStepB * D, kStepB, qf, a.scale, 0.f, m, l, u, ua, lane);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[st]);
+        const long long o = static_cast<long long>(r) * S + slot;
+        if (lane == 0) {
+          a.sm[o] = m;
+          a.sl[o] = l;
+        }
+        if (lane < 16) store_vec<DPH>(a.su + o * D + lane * DPH, u);
+        __syncwarp();
+        if (lane == 0) publish(&row_states[r]);
+      }
+    }
+  }
+
+  // ---------------------------------------------------------------- row CTAs
+  __syncthreads();
+  if (row_cta) {
+    const int mh = row / G;
+    if (tid == 0 && !s_abort && !wait_count(&head_done[mh], static_cast<unsigned>(ipH))) {
+      report(a.status, kStatusWaitTimeout);
+      s_abort = 1;
+    }
+    __syncthreads();
+    if (!s_abort) {
+      SelectArgs sa{};
+      sa.R = 1; sa.hsel = hq; sa.topk = K; sa.n = n; sa.block_offsets = nullptr; sa.total_blocks = n;
+      sa.id_base = 0; sa.ids_out = a.selected; sa.keys_out = nullptr; sa.status = a.status;
+      sa.bounds = a.bounds; sa.q = a.q; sa.q_dtype = a.q_dtype; sa.lo = a.lo; sa.hi = a.hi;
+      sa.hq = hq; sa.hmeta = hkv; sa.d = D; sa.group_select = 0;
+      bounded_select_core<E>(sa, row, qs + row * D, true);
+    }
+    __syncthreads();
+    for (int i = tid; i < K; i += kStepThreads) s_sel[i] = a.selected[static_cast<long long>(row) * K + i];
+    if (serial && tid == 0 && !s_abort) publish(&row_ready[row]);
+    __syncthreads();
+
+    float wm = neg_inf(), wl = 0.f, wu[DPH];
+#pragma unroll
+    for (int j = 0; j < DPH; ++j) wu[j] = 0.f;
+    int n_fold;        // retained states to fold
+    const int* fold_slot;
+    if (!serial) {
+      // Saved repair: misses (A not in P) computed here, hits (P slots in A)
+      // taken from the block states the other CTAs wrote.
+      for (int i = tid; i < (n + 31) / 32; i += kStepThreads) { s_pmask[i] = 0u; s_amask[i] = 0u; }
+      __syncthreads();
+      for (int i = tid; i < a.sp; i += kStepThreads) {
+        const int id = s_pid[i];
+        if (id >= 0 && id < n) atomicOr(&s_pmask[id >> 5], 1u << (id & 31));
+      }
+      for (int i = tid; i < K; i += kStepThreads) {
+        const int id = s_sel[i];
+        if (id >= 0 && id < n) atomicOr(&s_amask[id >> 5], 1u << (id & 31));
+      }
+      __syncthreads();
+      if (warp == 0) {
+        int nm = 0;
+        for (int b = 0; b < K; b += 32) {
+          const int id = b + lane < K ? s_sel[b + lane] : -1;
+          const bool miss = id >= 0 && !((s_pmask[id >> 5] >> (id & 31)) & 1u);
+          const unsigned bal = __ballot_sync(kFull, miss);
+          if (miss) s_miss[nm + __popc(bal & ((1u << lane) - 1u))] = id;
+          nm += __popc(bal);
+        }
+        int nh = 0;
+        for (int b = 0; b < a.sp; b += 32) {
+          const int id = b + lane < a.sp ? s_pid[b + lane] : -1;
+          const bool hit = id >= 0 && id < n && ((s_amask[id >> 5] >> (id & 31)) & 1u);
+          const unsigned bal = __ballot_sync(kFull, hit);
+          if (hit) s_hit[nh + __popc(bal & ((1u << lane) - 1u))] = b + lane;
+          nh += __popc(bal);
+        }
+        if (lane == 0) { s_nmiss = nm; s_nhit = nh; }
+      }
+      __syncthreads();
+      const int nmiss = s_abort ? 0 : s_nmiss;
+      if (warp == kStepProducer) {
+        for (int i = 0; i < nmiss; ++i) {
+          if (lane == 0) produce(n_items + i, 1, mh, 0, s_miss[i]);
+          __syncwarp();
+        }
+      } else {
+        for (int i = warp; i < nmiss; i += kStepConsumers) {
+          const int it = n_items + i;
+          const int st = it % NS;
+          const bool landed = mbar_wait(&full_bar[st], (it / NS) & 1u, a.status);
+          if (!landed) s_abort = 1;
+          if (landed && item_ok[st]) {
+            float qf[DPH], m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
+#pragma unroll
+            for (int j = 0; j < DPH; ++j) { qf[j] = qs[row * D + (lane & 15) * DPH + j]; u[j] = 0.f; ua[j] = 0.f; }
+            const T* ks = reinterpret_cast<const T*>(pool + static_cast<size_t>(st) * kStageBytes);
+            warp_block_state<T, DPH, kModeFull, true>(ks, ks + kStepB * D, kStepB, qf, a.scale, 0.f, m, l, u, ua,
+                                                      lane);
+            fold_state(wm, wl, wu, m, l, u);
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty_bar[st]);
+        }
+      }
+      n_fold = s_nhit;
+      fold_slot = s_hit;
+    } else {
+      n_fold = K;
+      fold_slot = nullptr;
+    }
+    // The row's block states (all S of them) are complete.
+    if (tid == 0 && !s_abort && !wait_count(&row_states[row], static_cast<unsigned>(S))) {
+      report(a.status, kStatusWaitTimeout);
+      s_abort = 1;
+    }
+    __syncthreads();
+    if (!s_abort) {
+      for (int i = warp; i < n_fold; i += kStepWarps) {
+        const int slot = fold_slot ? fold_slot[i] : i;
+        const long long o = static_cast<long long>(row) * S + slot;
+        const float m = __ldcg(a.sm + o), l = __ldcg(a.sl + o);
+        float u[DPH];
+        const float4* up = reinterpret_cast<const float4*>(a.su + o * D + (lane & 15) * DPH);
+#pragma unroll
+        for (int j = 0; j < DPH / 4; ++j) {
+          const float4 x = __ldcg(up + j);
+          u[4 * j] = x.x; u[4 * j + 1] = x.y; u[4 * j + 2] = x.z; u[4 * j + 3] = x.w;
+        }
+        fold_state(wm, wl, wu, m, l, u);
+      }
+    }
+    if (lane == 0) { s_wm[warp] = wm; s_wl[warp] = wl; }
+    if (lane < 16) store_vec<DPH>(&s_wu[warp][lane * DPH], wu);
+    __syncthreads();
+    if (tid < D && !s_abort) {
+      float M = neg_inf();
+      for (int w = 0; w < kStepWarps; ++w) M = fmaxf(M, s_wm[w]);
+      float Z = 0.f, U = 0.f;
+      for (int w = 0; w < kStepWarps; ++w) {
+        if (s_wm[w] > neg_inf()) {
+          const float x = expf(s_wm[w] - M);
+          Z += x * s_wl[w];
+          U += x * s_wu[w][tid];
+        }
+      }
+      a.out[static_cast<long long>(row) * D + tid] = U / fmaxf(Z, 1e-30f);
+    }
+  }
+
+  // ---------------------------------------------------------------- exit
+  // Every wait of this CTA is over; the last CTA to get here zeroes the
+  // control block for the next call.
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(ctas_done, 1u) == static_cast<unsigned>(grid) - 1) {
+      for (int i = 0; i < hkv + 2 * hq; ++i) atomicExch(a.ctrl + i, 0u);
+      atomicExch(ctas_done, 0u);
+      __threadfence();
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+size_t decode_step_smem(int hq) {
+  return ((static_cast<size_t>(hq) * kStepD + hq) * 4 + 127) / 128 * 128 +
+         static_cast<size_t>(kStepStages) * kStageBytes;
+}
+
+const char* decode_step_unsupported(int hq, int hkv, int n, int b, int d, int kv_dtype, int topk, int sp,
+                                    int num_sms) {
+  if (d != kStepD || b != kStepB) return "the fused step takes head dim 128 and 32-token blocks";
+  if (kv_dtype != kBF16 && kv_dtype != kF16) return "the fused step takes 16-bit K/V";
+  if (hq % hkv != 0 || hq / hkv > 16) return "the fused step takes at most 16 query heads per KV head";
+  if (static_cast<size_t>(hq) * kStepD > 4096) return "the fused step stages at most 4096 query values";
+  if (n > kStepMaxBlocks || n < topk) return "the fused step takes topk <= blocks <= 4096";
+  if (topk > kStepMaxList || sp > kStepMaxList) return "the fused step takes lists of at most 256 blocks";
+  if (2 * hq >= num_sms) return "the fused step needs more than two SMs per query head";
+  return nullptr;
+}
+
+template <typename T, int E, int GM>
+static int launch_step_t(const StepArgs& a, int num_sms, cudaStream_t stream) {
+  auto kern = decode_step_kernel<T, E, GM>;
+  const size_t smem = decode_step_smem(a.hq);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return static_cast<int>(e);
+  prefer_shared(kern);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_sms);
+  cfg.blockDim = dim3(kStepThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kern, a));
+}
+
+template <typename T>
+static int launch_step_d(const StepArgs& a, int num_sms, cudaStream_t stream) {
+  const int G = a.hq / a.hkv;
+  if (a.n <= 2048) return G <= 4 ? launch_step_t<T, 4, 4>(a, num_sms, stream) : launch_step_t<T, 4, 16>(a, num_sms, stream);
+  return G <= 4 ? launch_step_t<T, 8, 4>(a, num_sms, stream) : launch_step_t<T, 8, 16>(a, num_sms, stream);
+}
+
+int launch_decode_step(const StepArgs& a, int kv_dtype, int num_sms, cudaStream_t stream) {
+  return kv_dtype == kBF16 ? launch_step_d<__nv_bfloat16>(a, num_sms, stream)
+                           : launch_step_d<__half>(a, num_sms, stream);
+}
+
+int set_wait_limit_step(unsigned long long ns) { return set_wait_limit_this_unit(ns); }
+
+}  // namespace stk

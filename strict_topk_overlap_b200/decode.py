@@ -122,6 +122,49 @@ def speculative_step_hybrid(q, k, v, lo, hi, predicted, topk, *, variant="repair
     return out, selected
 
 
+STK_ESMEM = -2
+
+
+def decode_step_workspace(q, k, topk, predicted=None):
+    """A zeroed workspace for ``decode_step`` (its control block must start at
+    zero; every call leaves it zero again)."""
+    slots = predicted.shape[1] if predicted is not None else topk
+    need = L.load().stk_decode_step_workspace_bytes(q.shape[0], k.shape[0], k.shape[1], slots, q.shape[1])
+    return torch.zeros((max(need, 1),), device=q.device, dtype=torch.uint8)
+
+
+def decode_step(q, k, v, lo, hi, topk, predicted=None, *, out=None, selected=None, workspace=None, strict=True):
+    """One decode step as one persistent, cooperative launch (stk_decode_step).
+
+    With ``predicted`` [Hq, P]: the speculative saved step — equal to
+    gqa.select_blocks, gqa.partials and gqa.repair_saved in sequence (and to
+    ``speculative_step``). Without it: the serial step, equal to
+    gqa.exact(q, k, v, gqa.select_blocks(q, lo, hi, topk)). Returns (output
+    FP32 [Hq, D], selected int32 [Hq, topk]). ``workspace`` must come from
+    ``decode_step_workspace`` (zeroed) or have been used by an earlier call
+    of the same shape. Shapes outside the fused kernel's plan (see
+    stk_decode_step) raise RuntimeError, or return None with strict=False."""
+    hq, d = q.shape
+    hkv, n, b, _ = k.shape
+    sp = predicted.shape[1] if predicted is not None else 0
+    lib = L.load()
+    if out is None:
+        out = torch.empty((hq, d), device=q.device, dtype=torch.float32)
+    if selected is None:
+        selected = torch.empty((hq, topk), device=q.device, dtype=torch.int32)
+    if workspace is None:
+        workspace = decode_step_workspace(q, k, topk, predicted)
+    kv = L.kv_struct(k, v)
+    rc = lib.stk_decode_step(C.byref(kv), q.data_ptr(), L.dtype_code(q), lo.data_ptr(), hi.data_ptr(), hq, topk,
+                             L.ptr(predicted), L.id_is64(predicted) if predicted is not None else 0, sp,
+                             selected.data_ptr(), out.data_ptr(), workspace.data_ptr(), workspace.numel(),
+                             L.status_ptr(), L.stream_of(q))
+    if rc == STK_ESMEM and not strict:
+        return None
+    L.check(rc, "decode_step")
+    return out, selected
+
+
 @dataclass
 class StepSpec:
     """One decode step's configuration."""
@@ -164,10 +207,14 @@ class SpeculativeDecoder:
     repair) is captured once and replayed as one CUDA-graph launch."""
 
     def __init__(self, q, k, v, lo, hi, predicted, spec: StepSpec, *, graph: bool = True, serial: bool = False,
-                 chained: bool = True):
+                 chained: bool = True, fused: bool = True):
         self.q, self.k, self.v, self.lo, self.hi, self.predicted = q, k, v, lo, hi, predicted
         self.spec = spec
         self.serial = serial
+        # The saved method and the serial step run as one persistent launch
+        # (decode_step) where the shape fits its plan.
+        self.fused = fused and (serial or spec.method in ("saved", "light"))
+        self._fws = decode_step_workspace(q, k, spec.topk, None if serial else predicted) if self.fused else None
         # The saved and hybrid (repair_fused, signed_fused) methods run as one
         # launch chain on one stream; compact (and chained=False) uses the
         # two-stream harness.
@@ -193,6 +240,12 @@ class SpeculativeDecoder:
             self._capture()
 
     def _run(self):
+        if self.fused:
+            res = decode_step(self.q, self.k, self.v, self.lo, self.hi, self.spec.topk,
+                              None if self.serial else self.predicted, workspace=self._fws, strict=False)
+            if res is not None:
+                return res
+            self.fused = False  # outside the fused kernel's plan: the launch chains below
         if self.serial:
             a = self._selector()
             return gqa.exact(self.q, self.k, self.v, a), a
