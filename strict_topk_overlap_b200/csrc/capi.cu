@@ -464,8 +464,6 @@ int stk_decode_step(const stk_kv* kv, const void* q, int q_dtype, const float* l
   const int nsm = sm_count_current();
   if (const char* why = decode_step_unsupported(hq, kv->hkv, n, kv->b, d, kv->kv_dtype, topk, sp, nsm))
     return fail(STK_ESMEM, "%s", why);
-  if (decode_step_smem(hq) + 40 * 1024 > static_cast<size_t>(smem_optin_current()))
-    return fail(STK_ESMEM, "the fused step's shared memory exceeds this device's limit");
   const uintptr_t align = reinterpret_cast<uintptr_t>(lo) | reinterpret_cast<uintptr_t>(hi) |
                           reinterpret_cast<uintptr_t>(kv->k) | reinterpret_cast<uintptr_t>(kv->v);
   if (align & 15) return fail(STK_EINVAL, "lo, hi, K and V must be 16-byte aligned");
@@ -490,7 +488,9 @@ int stk_decode_step(const stk_kv* kv, const void* q, int q_dtype, const float* l
   a.su = reinterpret_cast<float*>(w);
   a.status = status;
   a.scale = attn_scale(d);
-  return cuda_status(launch_decode_step(a, kv->kv_dtype, nsm, static_cast<cudaStream_t>(stream)), "decode_step");
+  rc = launch_decode_step(a, kv->kv_dtype, nsm, static_cast<cudaStream_t>(stream));
+  if (rc < 0) return fail(STK_ESMEM, "the fused step's shared memory exceeds this device's limit");
+  return cuda_status(rc, "decode_step");
 }
 
 size_t stk_speculative_step_hybrid_workspace_bytes(int hq, int n, int sp, int d) {

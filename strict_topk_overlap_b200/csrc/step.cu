@@ -26,13 +26,18 @@
 // predicted blocks (speculative step, from the start), or of the selected
 // blocks as each row's selection is published (serial step).
 //
-// Inside a CTA, warp 15 issues 1-D bulk copies into a ring of 16 KiB stages
-// (each on a "full" mbarrier with the copy's byte count) in item order:
-// first the CTA's metadata items (16 blocks of one KV head: their lo rows,
-// then their hi rows), then its block items (one block's K then V). Warps
-// 0..14 take the items round-robin, reduce them and release each stage on
-// its "empty" mbarrier. The small loads (q, predicted IDs) are issued before
-// any bulk copy: a load queued behind the bulk stream waits for all of it.
+// Inside a CTA, warp 11 issues 1-D bulk copies into a ring of 11 stages of
+// 16 KiB (each on a "full" mbarrier with the copy's byte count) in item
+// order: first the CTA's metadata items (16 blocks of one KV head: their lo
+// rows, then their hi rows), then its block items (one block's K then V).
+// Item it goes to stage it % 11 and is reduced by warp it % 11, which then
+// releases the stage on its "empty" mbarrier: each stage has one consumer
+// warp, which therefore waits on the stage's phases one after the other (a
+// parity wait cannot tell a phase from the one two phases later, so two
+// warps must never take turns on one stage). Warps 12..15 join for the
+// selection and the row's repair. The small loads (q, predicted IDs) are
+// issued before any bulk copy: a load queued behind the bulk stream waits
+// for all of it.
 //
 // Cross-CTA progress goes through counters in the workspace's control
 // block, which must be zero before the first call on a workspace; the last
@@ -51,9 +56,8 @@ namespace stk {
 
 constexpr int kStepThreads = 512;
 constexpr int kStepWarps = kStepThreads / 32;
-constexpr int kStepProducer = kStepWarps - 1;  // issues the bulk copies
-constexpr int kStepConsumers = kStepWarps - 1;
-constexpr int kStepStages = 10;
+constexpr int kStepStages = 11;               // ring stages = consumer warps 0..10
+constexpr int kStepProducer = kStepStages;     // warp 11 issues the bulk copies
 constexpr int kStepD = 128;
 constexpr int kStepB = 32;
 constexpr int kStepDPH = kStepD / 16;
@@ -230,9 +234,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
       }
       __syncwarp();
     }
-  } else {
+  } else if (warp < NS) {
     // -------------------------------------------------------------- consumers
-    for (int it = warp; it < n_items; it += kStepConsumers) {
+    for (int it = warp; it < n_items; it += NS) {
       const int st = it % NS;
       const bool landed = mbar_wait(&full_bar[st], (it / NS) & 1u, a.status);
       if (!landed) s_abort = 1;
@@ -400,8 +404,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
           if (lane == 0) produce(n_items + i, 1, mh, 0, s_miss[i]);
           __syncwarp();
         }
-      } else {
-        for (int i = warp; i < nmiss; i += kStepConsumers) {
+      } else if (warp < NS) {
+        // Item n_items + i belongs to warp (n_items + i) % NS, like every item of the ring.
+        for (int i = (warp - n_items % NS + NS) % NS; i < nmiss; i += NS) {
           const int it = n_items + i;
           const int st = it % NS;
           const bool landed = mbar_wait(&full_bar[st], (it / NS) & 1u, a.status);
@@ -501,7 +506,14 @@ template <typename T, int E, int GM>
 static int launch_step_t(const StepArgs& a, int num_sms, cudaStream_t stream) {
   auto kern = decode_step_kernel<T, E, GM>;
   const size_t smem = decode_step_smem(a.hq);
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  cudaFuncAttributes fa;
+  int dev = 0, optin = 0;
+  cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+  if (e == cudaSuccess) e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (fa.sharedSizeBytes + smem > static_cast<size_t>(optin)) return -1;  // outside the plan on this device
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return static_cast<int>(e);
   prefer_shared(kern);
   cudaLaunchConfig_t cfg = {};
