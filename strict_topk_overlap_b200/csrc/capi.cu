@@ -446,8 +446,9 @@ static size_t decode_step_ctrl_bytes(int hq, int hkv) {
 size_t stk_decode_step_workspace_bytes(int hq, int hkv, int n, int slots, int d) {
   if (hq <= 0 || hkv <= 0 || n <= 0 || slots <= 0 || d <= 0) return 0;
   const size_t s = static_cast<size_t>(hq) * slots;
-  return decode_step_ctrl_bytes(hq, hkv) + align256(stk_select_workspace_bytes(hq, n)) +
-         2 * align256(s * sizeof(float)) + align256(s * d * sizeof(float));
+  return decode_step_ctrl_bytes(hq, hkv) + 2 * align256(stk_select_workspace_bytes(hq, n)) +
+         align256(static_cast<size_t>(hq) * n * sizeof(int32_t)) + 2 * align256(s * sizeof(float)) +
+         align256(s * d * sizeof(float));
 }
 
 int stk_decode_step(const stk_kv* kv, const void* q, int q_dtype, const float* lo, const float* hi, int hq, int topk,
@@ -465,8 +466,9 @@ int stk_decode_step(const stk_kv* kv, const void* q, int q_dtype, const float* l
   if (const char* why = decode_step_unsupported(hq, kv->hkv, n, kv->b, d, kv->kv_dtype, topk, sp, nsm))
     return fail(STK_ESMEM, "%s", why);
   const uintptr_t align = reinterpret_cast<uintptr_t>(lo) | reinterpret_cast<uintptr_t>(hi) |
-                          reinterpret_cast<uintptr_t>(kv->k) | reinterpret_cast<uintptr_t>(kv->v);
-  if (align & 15) return fail(STK_EINVAL, "lo, hi, K and V must be 16-byte aligned");
+                          reinterpret_cast<uintptr_t>(kv->k) | reinterpret_cast<uintptr_t>(kv->v) |
+                          reinterpret_cast<uintptr_t>(q);
+  if (align & 15) return fail(STK_EINVAL, "q, lo, hi, K and V must be 16-byte aligned");
   const int slots = sp > 0 ? sp : topk;
   if (workspace_bytes < stk_decode_step_workspace_bytes(hq, kv->hkv, n, slots, d))
     return fail(STK_EWS, "decode_step workspace too small");
@@ -480,6 +482,10 @@ int stk_decode_step(const stk_kv* kv, const void* q, int q_dtype, const float* l
   w += decode_step_ctrl_bytes(hq, kv->hkv);
   a.bounds = reinterpret_cast<float2*>(w);
   w += align256(stk_select_workspace_bytes(hq, n));
+  a.warm_bounds = reinterpret_cast<float2*>(w);
+  w += align256(stk_select_workspace_bytes(hq, n));
+  a.warm_ids = reinterpret_cast<int*>(w);
+  w += align256(static_cast<size_t>(hq) * n * sizeof(int32_t));
   const size_t s = static_cast<size_t>(hq) * slots;
   a.sm = reinterpret_cast<float*>(w);
   w += align256(s * sizeof(float));

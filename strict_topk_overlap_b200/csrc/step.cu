@@ -66,6 +66,22 @@ constexpr int kMetaItemBlocks = kStageBytes / (2 * kStepD * 4);  // 16 blocks of
 constexpr int kStepMaxList = 256;                                // topk and predicted-list limit
 constexpr int kStepMaxBlocks = 4096;                             // blocks per request limit
 
+#ifdef STK_TRACE
+// [cta][16] timeline of the fused step (profiling builds only).
+static __device__ unsigned long long g_step_trace[256 * 16];
+extern "C" __attribute__((visibility("default"))) int stk_trace_step_read(void* host, size_t bytes, int clear) {
+  int rc = static_cast<int>(cudaMemcpyFromSymbol(host, g_step_trace, bytes));
+  if (!rc && clear) {
+    static unsigned long long zeros[256 * 16];
+    rc = static_cast<int>(cudaMemcpyToSymbol(g_step_trace, zeros, sizeof(zeros)));
+  }
+  return rc;
+}
+#define SPT(ev) do { if (blockIdx.x < 256) STK_TRACE_AT(g_step_trace, blockIdx.x * 16 + (ev)); } while (0)
+#else
+#define SPT(ev) ((void)0)
+#endif
+
 
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
   unsigned v;
@@ -104,6 +120,39 @@ __device__ __forceinline__ void fold_state(float& wm, float& wl, float (&wu)[kSt
   wm = M;
 }
 
+// Warm the instruction cache of a row CTA's later phases while the other
+// CTAs score the metadata: a selection over a synthetic row (distinct,
+// well-separated scores: the common path without straddlers) written to the
+// row's own warm-up slots, and one block reduction per consumer warp over
+// whatever its stage holds. Nothing here reaches the step's outputs.
+template <typename T, int E>
+__device__ __forceinline__ void warm_row_cta(const StepArgs& a, int row, const float* qrow, unsigned char* pool,
+                                             int warp, int lane, float* sink) {
+  const int n = a.n;
+  float2* wb = a.warm_bounds + static_cast<long long>(row) * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float x = static_cast<float>(n - i);
+    wb[i] = make_float2(x, x);
+  }
+  __threadfence();
+  __syncthreads();
+  SelectArgs wa{};
+  wa.R = 1; wa.hsel = a.hq; wa.topk = a.topk; wa.n = n; wa.block_offsets = nullptr; wa.total_blocks = n;
+  wa.id_base = 0; wa.ids_out = a.warm_ids; wa.keys_out = nullptr; wa.status = nullptr;
+  wa.bounds = a.warm_bounds; wa.q = a.q; wa.q_dtype = a.q_dtype; wa.lo = a.lo; wa.hi = a.hi;
+  wa.hq = a.hq; wa.hmeta = a.hkv; wa.d = kStepD; wa.group_select = 0;
+  bounded_select_core<E>(wa, row, qrow, true);
+  if (warp < kStepStages) {
+    constexpr int DPH = kStepDPH;
+    float qf[DPH], m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
+#pragma unroll
+    for (int j = 0; j < DPH; ++j) { qf[j] = qrow[(lane & 15) * DPH + j]; u[j] = 0.f; ua[j] = 0.f; }
+    const T* ks = reinterpret_cast<const T*>(pool + static_cast<size_t>(warp) * kStageBytes);
+    warp_block_state<T, DPH, kModeFull, true>(ks, ks + kStepB * kStepD, kStepB, qf, a.scale, 0.f, m, l, u, ua, lane);
+    if (m == 1234.5f && l == 0.5f) sink[0] = u[0];  // keeps the pass; never true for a finite block of logits
+  }
+}
+
 template <typename T, int E, int GM>
 __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a) {
   constexpr int D = kStepD;
@@ -119,22 +168,24 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
   __shared__ unsigned s_pmask[kStepMaxBlocks / 32], s_amask[kStepMaxBlocks / 32];
   __shared__ float s_wm[kStepWarps], s_wl[kStepWarps];
   __shared__ __align__(16) float s_wu[kStepWarps][D];
+  __shared__ float s_sink[1];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int hq = a.hq, hkv = a.hkv, n = a.n, K = a.topk;
   const int G = hq / hkv;
   const int grid = gridDim.x;
-  const int first_row_cta = grid - hq;
-  const bool row_cta = static_cast<int>(blockIdx.x) >= first_row_cta;
-  const int row = row_cta ? static_cast<int>(blockIdx.x) - first_row_cta : -1;
+  const int W = grid - hq;  // work CTAs; CTA W + r is row r's CTA
+  const bool row_cta = static_cast<int>(blockIdx.x) >= W;
+  const int row = row_cta ? static_cast<int>(blockIdx.x) - W : -1;
   const bool serial = a.sp == 0;
   const int S = serial ? K : a.sp;
   const int ipH = (n + kMetaItemBlocks - 1) / kMetaItemBlocks;  // metadata items per KV head
   const int n_meta = hkv * ipH;
-  const int my_meta = static_cast<int>(blockIdx.x) < n_meta ? (n_meta - 1 - static_cast<int>(blockIdx.x)) / grid + 1 : 0;
+  // Work CTA c: metadata items c, c + W, ... and jobs [j0, j1) of the hq * S (row, slot) jobs.
+  const int my_meta = row_cta ? 0 : (static_cast<int>(blockIdx.x) < n_meta ? (n_meta - 1 - static_cast<int>(blockIdx.x)) / W + 1 : 0);
   const long long J = static_cast<long long>(hq) * S;
-  const int j0 = row_cta ? 0 : static_cast<int>(J * blockIdx.x / first_row_cta);
-  const int j1 = row_cta ? 0 : static_cast<int>(J * (blockIdx.x + 1) / first_row_cta);
+  const int j0 = row_cta ? 0 : static_cast<int>(J * blockIdx.x / W);
+  const int j1 = row_cta ? 0 : static_cast<int>(J * (blockIdx.x + 1) / W);
   const int my_jobs = j1 - j0;
   const int n_items = my_meta + my_jobs;
   unsigned* head_done = a.ctrl;
@@ -150,6 +201,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
   constexpr unsigned kBlockBytes = kStepB * D * sizeof(T);
 
   // ---------------------------------------------------------------- set-up
+  if (tid == 0) SPT(0);
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full_bar[i], 1);
@@ -158,42 +210,25 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
     fence_barrier_init();
     s_abort = 0;
   }
-  // Small loads first (q, the row's predicted IDs, the producer's job IDs).
-  for (int i = tid; i < hq * D; i += kStepThreads) qs[i] = load_any(a.q, a.q_dtype, i);
-  if (row_cta && !serial)
-    for (int i = tid; i < a.sp; i += kStepThreads)
-      s_pid[i] = static_cast<int>(load_id(a.pred, a.pred64, static_cast<long long>(row) * a.sp + i));
-  long long lid = -1;  // producer lane: ID of job j0 + jb + lane (speculative step)
-  int jb = 0;
-  if (warp == kStepProducer && !serial && lane < my_jobs) lid = load_id(a.pred, a.pred64, j0 + lane);
-  __syncthreads();
-  for (int t = warp; t < hq; t += kStepWarps) {
-    float sum = 0.f;
-    for (int dd = lane; dd < D; dd += 32) sum = __fadd_ru(sum, fabsf(qs[t * D + dd]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum = __fadd_ru(sum, __shfl_xor_sync(kFull, sum, o));
-    if (lane == 0) qn1[t] = sum;
-  }
   __syncthreads();
 
-  // ---------------------------------------------------------------- producer
   // Issues item `it` into stage it % NS once the consumer of item it - NS has
   // released it. An item it cannot fill (a bad ID, or after an abort) is
   // completed without a copy and flagged, so that its consumer skips it.
-  auto produce = [&](int it, int kind, int mh_or_row, long long first, long long id) {
+  auto produce = [&](int it, int kind, int mh, long long first, long long id) {
     const int st = it % NS;
     if (it >= NS && !mbar_wait(&empty_bar[st], ((it / NS) - 1) & 1u, a.status)) s_abort = 1;
     unsigned char* stage = pool + static_cast<size_t>(st) * kStageBytes;
     if (kind == 0) {  // metadata: rows [first, first + nb) of KV head mh
       const int nb = min(kMetaItemBlocks, n - static_cast<int>(first));
       const unsigned bytes = static_cast<unsigned>(nb) * D * 4;
-      const long long off = (static_cast<long long>(mh_or_row) * n + first) * D;
+      const long long off = (static_cast<long long>(mh) * n + first) * D;
       item_ok[st] = 1;
       mbar_arrive_expect_tx(&full_bar[st], 2 * bytes);
       bulk_g2s(stage, a.lo + off, bytes, &full_bar[st]);
       bulk_g2s(stage + kStageBytes / 2, a.hi + off, bytes, &full_bar[st]);
-    } else if (id >= 0 && id < n && !s_abort) {  // one block of KV head mh_or_row
-      const long long off = (static_cast<long long>(mh_or_row) * n + id) * kStepB * D;
+    } else if (id >= 0 && id < n && !s_abort) {  // one block of KV head mh
+      const long long off = (static_cast<long long>(mh) * n + id) * kStepB * D;
       item_ok[st] = 1;
       mbar_arrive_expect_tx(&full_bar[st], 2 * kBlockBytes);
       bulk_g2s(stage, Kp + off, kBlockBytes, &full_bar[st]);
@@ -204,157 +239,253 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
       mbar_arrive(&full_bar[st]);
     }
   };
+  auto meta_item = [&](int it, int& mh, int& b0) {
+    const int m = static_cast<int>(blockIdx.x) + it * W;
+    mh = m / ipH;
+    b0 = (m % ipH) * kMetaItemBlocks;
+  };
 
-  if (warp == kStepProducer) {
-    for (int it = 0; it < n_items; ++it) {
-      if (it < my_meta) {
-        if (lane == 0) {
-          const int m = static_cast<int>(blockIdx.x) + it * grid;
-          produce(it, 0, m / ipH, static_cast<long long>(m % ipH) * kMetaItemBlocks, 0);
-        }
+  // The small loads are issued first and consumed after the bulk copies are
+  // queued: q (16 bytes per thread), the predicted IDs of this CTA's first
+  // jobs (producer lanes) or of its row (row CTA).
+  const int qvals = row_cta ? D : hq * D;
+  const long long q0 = row_cta ? static_cast<long long>(row) * D : 0;
+  const int qper = a.q_dtype == kF32 ? 4 : 8;  // values per 16-byte load
+  float qv[2][8];
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const int i = (c * kStepThreads + tid) * qper;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) qv[c][e] = 0.f;
+    if (i < qvals) {
+      const uint4 x = __ldg(reinterpret_cast<const uint4*>(static_cast<const unsigned char*>(a.q) +
+                                                           (q0 + i) * (a.q_dtype == kF32 ? 4 : 2)));
+      if (a.q_dtype == kF32) {
+        qv[c][0] = __uint_as_float(x.x); qv[c][1] = __uint_as_float(x.y);
+        qv[c][2] = __uint_as_float(x.z); qv[c][3] = __uint_as_float(x.w);
       } else {
-        const int jl = it - my_meta;  // this CTA's job index
-        const int job = j0 + jl;
-        const int r = job / S, slot = job - r * S;
-        long long id = -1;
-        if (!serial) {
-          if (jl - jb == 32) {
-            jb += 32;
-            lid = jb + lane < my_jobs ? load_id(a.pred, a.pred64, j0 + jb + lane) : -1;
-          }
-          id = __shfl_sync(kFull, lid, jl - jb);
-        } else if (lane == 0) {
-          if (!s_abort && !wait_count(&row_ready[r], 1)) {
-            report(a.status, kStatusWaitTimeout);
-            s_abort = 1;
-          }
-          if (!s_abort) id = __ldcg(a.selected + static_cast<long long>(r) * K + slot);
-        }
-        if (lane == 0) produce(it, 1, r / G, 0, id);
-      }
-      __syncwarp();
-    }
-  } else if (warp < NS) {
-    // -------------------------------------------------------------- consumers
-    for (int it = warp; it < n_items; it += NS) {
-      const int st = it % NS;
-      const bool landed = mbar_wait(&full_bar[st], (it / NS) & 1u, a.status);
-      if (!landed) s_abort = 1;
-      const bool ok = landed && item_ok[st] != 0;
-      const unsigned char* stage = pool + static_cast<size_t>(st) * kStageBytes;
-      if (it < my_meta) {
-        // Score intervals of up to 16 blocks of KV head mh for its G query
-        // heads, 8 blocks per pass; lane = block * 4 + quarter of D, the
-        // lane mapping, error bound and rounding of bound_interval_kernel.
-        const int m = static_cast<int>(blockIdx.x) + it * grid;
-        const int mh = m / ipH;
-        const int b0 = (m % ipH) * kMetaItemBlocks;
-        const int nb = min(kMetaItemBlocks, n - b0);
-        const float* slo = reinterpret_cast<const float*>(stage);
-        const float* shi = reinterpret_cast<const float*>(stage + kStageBytes / 2);
-        const float* qrow = qs + mh * G * D;
-        const int p = lane & 3;
-        if (ok) {
-#pragma unroll 1
-          for (int pass = 0; pass < kMetaItemBlocks / 8; ++pass) {
-            const int b = pass * 8 + (lane >> 2);
-            const bool live = b < nb;
-            const float4* L4 = reinterpret_cast<const float4*>(slo + (live ? b : 0) * D);
-            const float4* H4 = reinterpret_cast<const float4*>(shi + (live ? b : 0) * D);
-            float s[GM];
+        const unsigned w4[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-            for (int g = 0; g < GM; ++g) s[g] = 0.f;
-            float mabs = 0.f;
-#pragma unroll
-            for (int i = 0; i < D / 16; ++i) {
-              const float4 l = live ? L4[p + 4 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
-              const float4 h = live ? H4[p + 4 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
-              mabs = fmaxf(mabs, fmaxf(fmaxf(fabsf(l.x), fabsf(h.x)), fmaxf(fabsf(l.y), fabsf(h.y))));
-              mabs = fmaxf(mabs, fmaxf(fmaxf(fabsf(l.z), fabsf(h.z)), fmaxf(fabsf(l.w), fabsf(h.w))));
-              const int off = 4 * (p + 4 * i);
-#pragma unroll
-              for (int g = 0; g < GM; ++g) {
-                if (g < G) {
-                  const float4 qq = *reinterpret_cast<const float4*>(qrow + g * D + off);
-                  s[g] = fmaf(qq.x, qq.x >= 0.f ? h.x : l.x, s[g]);
-                  s[g] = fmaf(qq.y, qq.y >= 0.f ? h.y : l.y, s[g]);
-                  s[g] = fmaf(qq.z, qq.z >= 0.f ? h.z : l.z, s[g]);
-                  s[g] = fmaf(qq.w, qq.w >= 0.f ? h.w : l.w, s[g]);
-                }
-              }
-            }
-#pragma unroll
-            for (int g = 0; g < GM; ++g) {
-              s[g] += __shfl_xor_sync(kFull, s[g], 1);
-              s[g] += __shfl_xor_sync(kFull, s[g], 2);
-            }
-            mabs = fmaxf(mabs, __shfl_xor_sync(kFull, mabs, 1));
-            mabs = fmaxf(mabs, __shfl_xor_sync(kFull, mabs, 2));
-            if (live) {
-              const float inf = __int_as_float(0x7f800000);
-#pragma unroll
-              for (int g = 0; g < GM; ++g) {
-                if (g < G && (g & 3) == p) {
-                  const float e = __fadd_ru(__fmul_ru(__fmul_ru(qn1[mh * G + g], mabs), kErrFactor), 0x1p-118f);
-                  float2 iv = make_float2(__fsub_rd(s[g], e), __fadd_ru(s[g], e));
-                  if (!(iv.x <= iv.y)) iv = make_float2(-inf, inf);
-                  a.bounds[static_cast<long long>(mh * G + g) * n + b0 + b] = iv;
-                }
-              }
-            }
+        for (int e = 0; e < 4; ++e) {
+          if (a.q_dtype == kBF16) {
+            qv[c][2 * e] = __uint_as_float(w4[e] << 16);
+            qv[c][2 * e + 1] = __uint_as_float(w4[e] & 0xffff0000u);
+          } else {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[e]));
+            qv[c][2 * e] = f.x;
+            qv[c][2 * e + 1] = f.y;
           }
         }
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&empty_bar[st]);
-          publish(&head_done[mh]);
-        }
-      } else {
-        // One block's softmax state for (row r, slot).
-        const int job = j0 + (it - my_meta);
-        const int r = job / S, slot = job - r * S;
-        float m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
-#pragma unroll
-        for (int j = 0; j < DPH; ++j) { u[j] = 0.f; ua[j] = 0.f; }
-        if (ok) {
-          float qf[DPH];
-#pragma unroll
-          for (int j = 0; j < DPH; ++j) qf[j] = qs[r * D + (lane & 15) * DPH + j];
-          const T* ks = reinterpret_cast<const T*>(stage);
-          warp_block_state<T, DPH, kModeFull, true>(ks, ks + kStepB * D, kStepB, qf, a.scale, 0.f, m, l, u, ua, lane);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_bar[st]);
-        const long long o = static_cast<long long>(r) * S + slot;
-        if (lane == 0) {
-          a.sm[o] = m;
-          a.sl[o] = l;
-        }
-        if (lane < 16) store_vec<DPH>(a.su + o * D + lane * DPH, u);
-        __syncwarp();
-        if (lane == 0) publish(&row_states[r]);
       }
     }
   }
-
-  // ---------------------------------------------------------------- row CTAs
+  long long lid = -1;  // producer lane: predicted ID of job j0 + jb + lane
+  int jb = 0;
+  if (warp == kStepProducer && !serial && lane < my_jobs) lid = load_id(a.pred, a.pred64, j0 + lane);
+  if (row_cta && !serial)
+    for (int i = tid; i < a.sp; i += kStepThreads)
+      s_pid[i] = static_cast<int>(load_id(a.pred, a.pred64, static_cast<long long>(row) * a.sp + i));
+  // Metadata items into the free stages at once, one producer lane each.
+  const int n_first = min(my_meta, NS);
+  if (warp == kStepProducer && lane < n_first) {
+    int mh, b0;
+    meta_item(lane, mh, b0);
+    produce(lane, 0, mh, b0, 0);
+  }
+  if (tid == 0) SPT(2);
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const int i = (c * kStepThreads + tid) * qper;
+    if (i < qvals)
+      for (int e = 0; e < qper; ++e) qs[q0 + i + e] = qv[c][e];
+  }
   __syncthreads();
-  if (row_cta) {
+  for (int t = row_cta ? row : warp; t < (row_cta ? row + 1 : hq); t += kStepWarps) {
+    if (row_cta && warp != 0) break;
+    float sum = 0.f;
+    for (int dd = lane; dd < D; dd += 32) sum = __fadd_ru(sum, fabsf(qs[t * D + dd]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum = __fadd_ru(sum, __shfl_xor_sync(kFull, sum, o));
+    if (lane == 0) qn1[t] = sum;
+  }
+  __syncthreads();
+  if (tid == 0) SPT(1);
+
+  if (!row_cta) {
+    // ------------------------------------------------------------ work CTA
+    if (warp == kStepProducer) {
+      int ready_row = -1;  // serial: rows whose selection this warp has seen published
+      long long sid = -1;  // serial: selected ID of job sb + lane
+      int sb = -1;
+      for (int it = n_first; it < n_items; ++it) {
+        if (it < my_meta) {
+          if (lane == 0) {
+            int mh, b0;
+            meta_item(it, mh, b0);
+            produce(it, 0, mh, b0, 0);
+          }
+        } else {
+          const int jl = it - my_meta;  // this CTA's job index
+          const int job = j0 + jl;
+          const int r = job / S;
+          long long id = -1;
+          if (!serial) {
+            if (jl - jb == 32) {
+              jb += 32;
+              lid = jb + lane < my_jobs ? load_id(a.pred, a.pred64, j0 + jb + lane) : -1;
+            }
+            id = __shfl_sync(kFull, lid, jl - jb);
+          } else {
+            if (r > ready_row) {
+              if (lane == 0 && !s_abort && !wait_count(&row_ready[r], 1)) {
+                report(a.status, kStatusWaitTimeout);
+                s_abort = 1;
+              }
+              __syncwarp();
+              ready_row = r;
+              sb = -1;
+            }
+            if (sb < 0 || job - sb >= 32) {
+              // The selected IDs of the next 32 jobs of row r (job = r * K + slot).
+              sb = job;
+              const int jj = job + lane;
+              sid = (!s_abort && jj < j1 && jj / S == r) ? __ldcg(a.selected + jj) : -1;
+            }
+            id = __shfl_sync(kFull, sid, job - sb);
+          }
+          if (lane == 0) produce(it, 1, r / G, 0, id);
+        }
+        if (lane == 0 && it == my_meta) SPT(3);
+        __syncwarp();
+      }
+      if (lane == 0) SPT(4);
+    } else if (warp < NS) {
+      // Consumers: item it belongs to warp it % NS (one consumer per stage).
+      if (lane == 0 && warp == 0) SPT(12);
+      for (int it = warp; it < n_items; it += NS) {
+        const int st = it % NS;
+        const bool landed = mbar_wait(&full_bar[st], (it / NS) & 1u, a.status);
+        if (lane == 0 && it == 0) SPT(13);
+        if (!landed) s_abort = 1;
+        const bool ok = landed && item_ok[st] != 0;
+        const unsigned char* stage = pool + static_cast<size_t>(st) * kStageBytes;
+        if (it < my_meta) {
+          // Score intervals of up to 16 blocks of KV head mh for its G query
+          // heads, 8 blocks per pass; lane = block * 4 + quarter of D, with
+          // the lane mapping, error bound and rounding of bound_interval_kernel.
+          int mh, b0;
+          meta_item(it, mh, b0);
+          const int nb = min(kMetaItemBlocks, n - b0);
+          const float* slo = reinterpret_cast<const float*>(stage);
+          const float* shi = reinterpret_cast<const float*>(stage + kStageBytes / 2);
+          const float* qrow = qs + mh * G * D;
+          const int p = lane & 3;
+          if (ok) {
+#pragma unroll 1
+            for (int pass = 0; pass < kMetaItemBlocks / 8; ++pass) {
+              const int b = pass * 8 + (lane >> 2);
+              const bool live = b < nb;
+              const float4* L4 = reinterpret_cast<const float4*>(slo + (live ? b : 0) * D);
+              const float4* H4 = reinterpret_cast<const float4*>(shi + (live ? b : 0) * D);
+              float s[GM];
+#pragma unroll
+              for (int g = 0; g < GM; ++g) s[g] = 0.f;
+              float mabs = 0.f;
+#pragma unroll
+              for (int i = 0; i < D / 16; ++i) {
+                const float4 l = live ? L4[p + 4 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 h = live ? H4[p + 4 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                mabs = fmaxf(mabs, fmaxf(fmaxf(fabsf(l.x), fabsf(h.x)), fmaxf(fabsf(l.y), fabsf(h.y))));
+                mabs = fmaxf(mabs, fmaxf(fmaxf(fabsf(l.z), fabsf(h.z)), fmaxf(fabsf(l.w), fabsf(h.w))));
+                const int off = 4 * (p + 4 * i);
+#pragma unroll
+                for (int g = 0; g < GM; ++g) {
+                  if (g < G) {
+                    const float4 qq = *reinterpret_cast<const float4*>(qrow + g * D + off);
+                    s[g] = fmaf(qq.x, qq.x >= 0.f ? h.x : l.x, s[g]);
+                    s[g] = fmaf(qq.y, qq.y >= 0.f ? h.y : l.y, s[g]);
+                    s[g] = fmaf(qq.z, qq.z >= 0.f ? h.z : l.z, s[g]);
+                    s[g] = fmaf(qq.w, qq.w >= 0.f ? h.w : l.w, s[g]);
+                  }
+                }
+              }
+#pragma unroll
+              for (int g = 0; g < GM; ++g) {
+                s[g] += __shfl_xor_sync(kFull, s[g], 1);
+                s[g] += __shfl_xor_sync(kFull, s[g], 2);
+              }
+              mabs = fmaxf(mabs, __shfl_xor_sync(kFull, mabs, 1));
+              mabs = fmaxf(mabs, __shfl_xor_sync(kFull, mabs, 2));
+              if (live) {
+                const float inf = __int_as_float(0x7f800000);
+#pragma unroll
+                for (int g = 0; g < GM; ++g) {
+                  if (g < G && (g & 3) == p) {
+                    const float e = __fadd_ru(__fmul_ru(__fmul_ru(qn1[mh * G + g], mabs), kErrFactor), 0x1p-118f);
+                    float2 iv = make_float2(__fsub_rd(s[g], e), __fadd_ru(s[g], e));
+                    if (!(iv.x <= iv.y)) iv = make_float2(-inf, inf);
+                    a.bounds[static_cast<long long>(mh * G + g) * n + b0 + b] = iv;
+                  }
+                }
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&empty_bar[st]);
+            publish(&head_done[mh]);
+          }
+        } else {
+          // One block's softmax state for (row r, slot).
+          const int job = j0 + (it - my_meta);
+          const int r = job / S, slot = job - r * S;
+          float m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
+#pragma unroll
+          for (int j = 0; j < DPH; ++j) { u[j] = 0.f; ua[j] = 0.f; }
+          if (ok) {
+            float qf[DPH];
+#pragma unroll
+            for (int j = 0; j < DPH; ++j) qf[j] = qs[r * D + (lane & 15) * DPH + j];
+            const T* ks = reinterpret_cast<const T*>(stage);
+            warp_block_state<T, DPH, kModeFull, true>(ks, ks + kStepB * D, kStepB, qf, a.scale, 0.f, m, l, u, ua,
+                                                      lane);
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty_bar[st]);
+          const long long o = static_cast<long long>(r) * S + slot;
+          if (lane == 0) {
+            a.sm[o] = m;
+            a.sl[o] = l;
+          }
+          if (lane < 16) store_vec<DPH>(a.su + o * D + lane * DPH, u);
+          __syncwarp();
+          if (lane == 0) publish(&row_states[r]);
+        }
+      }
+      if (lane == 0 && warp == 0) SPT(14);
+    }
+  } else {
+    // ------------------------------------------------------------ row CTA
+    const float* qrow = qs + row * D;
     const int mh = row / G;
+    warm_row_cta<T, E>(a, row, qrow, pool, warp, lane, s_sink);
+    if (tid == 0) SPT(5);
     if (tid == 0 && !s_abort && !wait_count(&head_done[mh], static_cast<unsigned>(ipH))) {
       report(a.status, kStatusWaitTimeout);
       s_abort = 1;
     }
     __syncthreads();
+    if (tid == 0) SPT(6);
     if (!s_abort) {
       SelectArgs sa{};
       sa.R = 1; sa.hsel = hq; sa.topk = K; sa.n = n; sa.block_offsets = nullptr; sa.total_blocks = n;
       sa.id_base = 0; sa.ids_out = a.selected; sa.keys_out = nullptr; sa.status = a.status;
       sa.bounds = a.bounds; sa.q = a.q; sa.q_dtype = a.q_dtype; sa.lo = a.lo; sa.hi = a.hi;
       sa.hq = hq; sa.hmeta = hkv; sa.d = D; sa.group_select = 0;
-      bounded_select_core<E>(sa, row, qs + row * D, true);
+      bounded_select_core<E>(sa, row, qrow, true);
     }
     __syncthreads();
+    if (tid == 0) SPT(7);
     for (int i = tid; i < K; i += kStepThreads) s_sel[i] = a.selected[static_cast<long long>(row) * K + i];
     if (serial && tid == 0 && !s_abort) publish(&row_ready[row]);
     __syncthreads();
@@ -362,11 +493,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
     float wm = neg_inf(), wl = 0.f, wu[DPH];
 #pragma unroll
     for (int j = 0; j < DPH; ++j) wu[j] = 0.f;
-    int n_fold;        // retained states to fold
-    const int* fold_slot;
+    int n_fold = K;  // retained states to fold
+    const int* fold_slot = nullptr;
     if (!serial) {
       // Saved repair: misses (A not in P) computed here, hits (P slots in A)
-      // taken from the block states the other CTAs wrote.
+      // taken from the block states the work CTAs wrote.
       for (int i = tid; i < (n + 31) / 32; i += kStepThreads) { s_pmask[i] = 0u; s_amask[i] = 0u; }
       __syncthreads();
       for (int i = tid; i < a.sp; i += kStepThreads) {
@@ -399,22 +530,22 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
       }
       __syncthreads();
       const int nmiss = s_abort ? 0 : s_nmiss;
+      // Misses through the ring (items 0 .. nmiss - 1 of this CTA).
       if (warp == kStepProducer) {
-        for (int i = 0; i < nmiss; ++i) {
-          if (lane == 0) produce(n_items + i, 1, mh, 0, s_miss[i]);
+        if (lane < min(nmiss, NS)) produce(lane, 1, mh, 0, s_miss[lane]);
+        for (int i = NS; i < nmiss; ++i) {
+          if (lane == 0) produce(i, 1, mh, 0, s_miss[i]);
           __syncwarp();
         }
       } else if (warp < NS) {
-        // Item n_items + i belongs to warp (n_items + i) % NS, like every item of the ring.
-        for (int i = (warp - n_items % NS + NS) % NS; i < nmiss; i += NS) {
-          const int it = n_items + i;
+        for (int it = warp; it < nmiss; it += NS) {
           const int st = it % NS;
           const bool landed = mbar_wait(&full_bar[st], (it / NS) & 1u, a.status);
           if (!landed) s_abort = 1;
           if (landed && item_ok[st]) {
             float qf[DPH], m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
 #pragma unroll
-            for (int j = 0; j < DPH; ++j) { qf[j] = qs[row * D + (lane & 15) * DPH + j]; u[j] = 0.f; ua[j] = 0.f; }
+            for (int j = 0; j < DPH; ++j) { qf[j] = qrow[(lane & 15) * DPH + j]; u[j] = 0.f; ua[j] = 0.f; }
             const T* ks = reinterpret_cast<const T*>(pool + static_cast<size_t>(st) * kStageBytes);
             warp_block_state<T, DPH, kModeFull, true>(ks, ks + kStepB * D, kStepB, qf, a.scale, 0.f, m, l, u, ua,
                                                       lane);
@@ -426,29 +557,50 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
       }
       n_fold = s_nhit;
       fold_slot = s_hit;
-    } else {
-      n_fold = K;
-      fold_slot = nullptr;
     }
-    // The row's block states (all S of them) are complete.
-    if (tid == 0 && !s_abort && !wait_count(&row_states[row], static_cast<unsigned>(S))) {
-      report(a.status, kStatusWaitTimeout);
-      s_abort = 1;
+    if (tid == 0) SPT(8);
+    // The row's S block states are complete: bring their numerators into
+    // shared memory with one bulk copy (S x D FP32, after the misses' stages
+    // are drained), and their (m, l) with plain loads through L2.
+    __syncthreads();
+    float* st_u = reinterpret_cast<float*>(pool);
+    float* st_m = reinterpret_cast<float*>(pool + static_cast<size_t>(S) * D * 4);
+    float* st_l = st_m + S;
+    __shared__ uint64_t fold_bar;
+    if (tid == 0) {
+      if (!s_abort && !wait_count(&row_states[row], static_cast<unsigned>(S))) {
+        report(a.status, kStatusWaitTimeout);
+        s_abort = 1;
+      }
+      SPT(9);
+      mbar_init(&fold_bar, 1);
+      fence_barrier_init();
+      if (!s_abort) {
+        // The numerators were written by other CTAs (generic proxy) and are
+        // read here by the bulk-copy (async) proxy.
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        const unsigned bytes = static_cast<unsigned>(S) * D * 4;
+        mbar_arrive_expect_tx(&fold_bar, bytes);
+        bulk_g2s(st_u, a.su + static_cast<long long>(row) * S * D, bytes, &fold_bar);
+      }
     }
+    __syncthreads();
+    if (!s_abort) {
+      for (int i = tid; i < S; i += kStepThreads) {
+        st_m[i] = __ldcg(a.sm + static_cast<long long>(row) * S + i);
+        st_l[i] = __ldcg(a.sl + static_cast<long long>(row) * S + i);
+      }
+    }
+    const bool have_u = !s_abort && mbar_wait(&fold_bar, 0, a.status);
+    if (!have_u) s_abort = 1;
     __syncthreads();
     if (!s_abort) {
       for (int i = warp; i < n_fold; i += kStepWarps) {
         const int slot = fold_slot ? fold_slot[i] : i;
-        const long long o = static_cast<long long>(row) * S + slot;
-        const float m = __ldcg(a.sm + o), l = __ldcg(a.sl + o);
         float u[DPH];
-        const float4* up = reinterpret_cast<const float4*>(a.su + o * D + (lane & 15) * DPH);
 #pragma unroll
-        for (int j = 0; j < DPH / 4; ++j) {
-          const float4 x = __ldcg(up + j);
-          u[4 * j] = x.x; u[4 * j + 1] = x.y; u[4 * j + 2] = x.z; u[4 * j + 3] = x.w;
-        }
-        fold_state(wm, wl, wu, m, l, u);
+        for (int j = 0; j < DPH; ++j) u[j] = st_u[slot * D + (lane & 15) * DPH + j];
+        fold_state(wm, wl, wu, st_m[slot], st_l[slot], u);
       }
     }
     if (lane == 0) { s_wm[warp] = wm; s_wl[warp] = wl; }
@@ -467,12 +619,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
       }
       a.out[static_cast<long long>(row) * D + tid] = U / fmaxf(Z, 1e-30f);
     }
+    if (tid == 0) SPT(10);
   }
 
   // ---------------------------------------------------------------- exit
   // Every wait of this CTA is over; the last CTA to get here zeroes the
   // control block for the next call.
   __syncthreads();
+  if (tid == 0) SPT(11);
   if (tid == 0) {
     __threadfence();
     if (atomicAdd(ctas_done, 1u) == static_cast<unsigned>(grid) - 1) {
@@ -498,6 +652,9 @@ const char* decode_step_unsupported(int hq, int hkv, int n, int b, int d, int kv
   if (static_cast<size_t>(hq) * kStepD > 4096) return "the fused step stages at most 4096 query values";
   if (n > kStepMaxBlocks || n < topk) return "the fused step takes topk <= blocks <= 4096";
   if (topk > kStepMaxList || sp > kStepMaxList) return "the fused step takes lists of at most 256 blocks";
+  const int slots = sp > 0 ? sp : topk;
+  if (static_cast<size_t>(slots) * (kStepD + 2) * 4 > static_cast<size_t>(kStepStages) * kStageBytes)
+    return "the fused step folds at most 336 block states per row";
   if (2 * hq >= num_sms) return "the fused step needs more than two SMs per query head";
   return nullptr;
 }
