@@ -24,6 +24,8 @@ ranks. The same line also carries, measured at the same N:
   * ``batched``: BASELINE config 3, a batch of 64 paged requests split across
     the N ranks by LPT (strong scaling, no collective), strict and relaxed
     (max_extra_mass = 0.01);
+  * ``hierarchical``: BASELINE config 2 (96 q / 8 KV heads, 4-token blocks,
+    K 512 shared per group) through the gqa_hierarchical API, per call;
   * ``context_parallel``: BASELINE config 4, one 524,288-token request whose
     blocks are split across the N ranks, exchanged with two NCCL all-gathers,
     with its IDs checked bit for bit against single-GPU selection.
@@ -65,15 +67,16 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the config-3 object")
     ap.add_argument("--no-cp", action="store_true", help="skip the config-4 object")
+    ap.add_argument("--no-c2", action="store_true", help="skip the config-2 object")
     ap.add_argument("--quick", action="store_true",
                     help="short run for profiler captures: no clock window, repeats, e2e, sweep, CPU baseline, "
                          "config-3 or config-4 objects")
     ap.add_argument("--graph-steps", type=int, default=8,
                     help="decode steps per CUDA graph in the timed loops (one per input set, like the attention "
                          "calls of consecutive layers of one token step); 1 = one graph per step")
-    ap.add_argument("--workload", choices=("c1", "batched", "cp"), default="c1",
-                    help="c1: BASELINE config 1 (default, the headline, with the config-3 and config-4 objects); "
-                         "batched / cp: only the config-3 / config-4 measurement, as its own line")
+    ap.add_argument("--workload", choices=("c1", "c2", "batched", "cp"), default="c1",
+                    help="c1: BASELINE config 1 (default, the headline, with the config-2, -3 and -4 objects); "
+                         "c2 / batched / cp: only the config-2 / -3 / -4 measurement, as its own line")
     ap.add_argument("--requests", type=int, default=64, help="config 3: requests in the whole batch")
     ap.add_argument("--eager", action="store_true",
                     help="launch each step's kernels directly instead of replaying a CUDA graph (for per-kernel "
@@ -518,13 +521,78 @@ def measure_cp(args, rank, world, device, quick=False):
     }
 
 
+# ----------------------------------------------------------------------------- config 2 (wide GQA, tiny blocks)
+
+def measure_c2(args, device, quick=False):
+    """96 query / 8 KV heads (12 per group), D 128, bf16,
+    32,768 tokens in 8192 blocks of 4, K = 512 blocks shared per group,
+    predicted overlap 0.8, through the reference's gqa_hierarchical API:
+    shared selection, partials over P, repair_saved_shared (the speculative
+    step's parts), exact over A (the serial step's attention), and the
+    tensor-core exact_shared. Each call is timed alone in a CUDA graph of
+    `nset` calls on rotating input sets (> L2), CUDA events."""
+    import torch
+    from strict_topk import gqa_hierarchical as GH
+    hq, hkv, n, b, d, topk = 96, 8, 8192, 4, 128, 512
+    g = hq // hkv
+    nset = 4
+    sets = []
+    for i in range(nset):
+        gen = torch.Generator(device=device).manual_seed(args.seed + 200 + i)
+        q = torch.randn(hq, d, device=device, generator=gen).to(torch.bfloat16)
+        k = (torch.randn(hkv, n, b, d, device=device, generator=gen)
+             + torch.randn(hkv, n, 1, d, device=device, generator=gen) * 0.5).to(torch.bfloat16)
+        v = torch.randn(hkv, n, b, d, device=device, generator=gen).to(torch.bfloat16)
+        lo, hi = k.amin(dim=2).float(), k.amax(dim=2).float()
+        a = GH.select_blocks_shared(q, lo, hi, topk)
+        pg = swap_rows(a[::g].cpu(), n, round(0.2 * topk), args.seed + 300 + i)
+        p = pg.repeat_interleave(g, dim=0).contiguous().to(device)
+        sets.append(dict(q=q, k=k, v=v, lo=lo, hi=hi, a=a, p=p, ag=a[::g].contiguous(),
+                         st=GH.partials(q, k, v, p)))
+    calls = {
+        "select_shared": lambda s: GH.select_blocks_shared(s["q"], s["lo"], s["hi"], topk),
+        "partials": lambda s: GH.partials(s["q"], s["k"], s["v"], s["p"]),
+        "repair_saved_shared": lambda s: GH.repair_saved_shared(s["q"], s["k"], s["v"], s["a"], s["p"], s["st"]),
+        "exact": lambda s: GH.exact(s["q"], s["k"], s["v"], s["a"]),
+        "exact_shared": lambda s: GH.exact_shared(s["q"], s["k"], s["v"], s["ag"]),
+    }
+    res = {}
+    for name, fn in calls.items():
+        gr, _ = graph_of(lambda: [fn(s) for s in sets], device)
+        for _ in range(3):
+            gr.replay()
+        nrep = 3 if quick else 30
+        ms = time_loop(lambda i: gr.replay(), nrep, device)
+        res[name] = ms * 1e3 / (nrep * nset)
+        del gr
+    hbm_peak, _ = peaks()
+    meta = 2 * hkv * n * d * 4
+    kv_sel = 2 * hkv * topk * b * d * 2  # unique K+V of the group-shared selection
+    miss = sum(len(set(x) - set(y)) for x, y in zip(sets[0]["ag"].tolist(), sets[0]["p"][::g].tolist()))
+    out = {"workload": "BASELINE config 2: 96q/8kv, D128, 8192 blocks of 4 tokens, K=512 shared per group, "
+                       "overlap 0.8, bf16", "us": {k: round(v, 2) for k, v in res.items()},
+           "algorithmic_bytes": {"select_shared": meta, "exact": kv_sel, "partials": kv_sel,
+                                 "repair_saved_shared": 2 * b * d * 2 * miss},
+           "hbm_frac": {"select_shared": meta / (res["select_shared"] * 1e-6) / 1e9 / hbm_peak,
+                        "exact": kv_sel / (res["exact"] * 1e-6) / 1e9 / hbm_peak,
+                        "exact_shared": kv_sel / (res["exact_shared"] * 1e-6) / 1e9 / hbm_peak},
+           "step_us": {"speculative": res["select_shared"] + max(0.0, res["partials"]) + res["repair_saved_shared"],
+                       "serial": res["select_shared"] + res["exact"]},
+           "timing": f"each call alone, CUDA graph of {nset} calls on rotating inputs (> L2), CUDA events"}
+    del sets
+    return out
+
+
 def run_single_workload(args):
     import torch
     rank, world, local = dist_setup("nccl")
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    fn = measure_batched if args.workload == "batched" else measure_cp
-    obj = fn(args, rank, world, device, quick=args.quick)
+    if args.workload == "c2":
+        obj = measure_c2(args, device, quick=args.quick)
+    else:
+        fn = measure_batched if args.workload == "batched" else measure_cp
+        obj = fn(args, rank, world, device, quick=args.quick)
     if rank == 0:
         print(json.dumps({"workload": args.workload, "n_gpus": world, **obj}), flush=True)
     if world > 1:
@@ -703,10 +771,16 @@ def main():
                                               "speedup": round(b_ / a_, 3)}
                 del dd, rr, ss
 
-    # Config 3 and config 4 at the same N (every rank takes part).
+    # Config 2 on each rank's own GPU (rank 0 reports it); config 3 and
+    # config 4 at the same N (every rank takes part).
+    c2 = None
+    if not args.quick and not args.no_c2:
+        del pstates
+        pstates = None
+        c2 = measure_c2(args, device)
+        torch.cuda.empty_cache()
     batched = cp = None
     if not args.quick and not args.no_batched:
-        del pstates
         batched = measure_batched(args, rank, world, device)
         torch.cuda.empty_cache()
     if not args.quick and not args.no_cp:
@@ -761,6 +835,8 @@ def main():
             "gpu_launches": LAUNCHES_PER_STEP.get(args.method, 4) * K * len(reps),
             "cpu_baseline": cpu,
         }
+        if c2:
+            line["hierarchical"] = c2
         if batched:
             line["batched"] = batched
         if cp:

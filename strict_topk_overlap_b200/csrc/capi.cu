@@ -446,9 +446,8 @@ static size_t decode_step_ctrl_bytes(int hq, int hkv) {
 size_t stk_decode_step_workspace_bytes(int hq, int hkv, int n, int slots, int d) {
   if (hq <= 0 || hkv <= 0 || n <= 0 || slots <= 0 || d <= 0) return 0;
   const size_t s = static_cast<size_t>(hq) * slots;
-  return decode_step_ctrl_bytes(hq, hkv) + 2 * align256(stk_select_workspace_bytes(hq, n)) +
-         align256(static_cast<size_t>(hq) * n * sizeof(int32_t)) + 2 * align256(s * sizeof(float)) +
-         align256(s * d * sizeof(float));
+  return decode_step_ctrl_bytes(hq, hkv) + align256(stk_select_workspace_bytes(hq, n)) +
+         2 * align256(s * sizeof(float)) + align256(s * d * sizeof(float));
 }
 
 int stk_decode_step(const stk_kv* kv, const void* q, int q_dtype, const float* lo, const float* hi, int hq, int topk,
@@ -482,10 +481,6 @@ int stk_decode_step(const stk_kv* kv, const void* q, int q_dtype, const float* l
   w += decode_step_ctrl_bytes(hq, kv->hkv);
   a.bounds = reinterpret_cast<float2*>(w);
   w += align256(stk_select_workspace_bytes(hq, n));
-  a.warm_bounds = reinterpret_cast<float2*>(w);
-  w += align256(stk_select_workspace_bytes(hq, n));
-  a.warm_ids = reinterpret_cast<int*>(w);
-  w += align256(static_cast<size_t>(hq) * n * sizeof(int32_t));
   const size_t s = static_cast<size_t>(hq) * slots;
   a.sm = reinterpret_cast<float*>(w);
   w += align256(s * sizeof(float));

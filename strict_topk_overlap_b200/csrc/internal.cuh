@@ -160,8 +160,6 @@ struct StepArgs {
   int* selected;   // [hq, topk] out, ascending
   float* out;      // [hq, D] out
   float2* bounds;  // [hq, n] score intervals
-  float2* warm_bounds;  // [hq, n] synthetic intervals of the row CTAs' warm-up selection
-  int* warm_ids;        // [hq, topk] its (discarded) IDs
   float* sm;       // [hq, S] block states, S = sp (speculative) or topk (serial)
   float* sl;
   float* su;       // [hq, S, D]

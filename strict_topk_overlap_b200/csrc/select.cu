@@ -650,8 +650,8 @@ __global__ void __launch_bounds__(kBWarps * 32) bound_interval_kernel(ScoreArgs 
   ST(3);
 }
 
-template <int E>
-__global__ void __launch_bounds__(512, 1) select_bounded_kernel(SelectArgs a) {
+template <int E, int NT>
+__global__ void __launch_bounds__(NT, 1) select_bounded_kernel(SelectArgs a) {
   __shared__ __align__(16) float qsm[kQStage];  // the row's query heads, FP32, for exact rescoring
   KT(0);
   pdl_release();
@@ -660,7 +660,7 @@ __global__ void __launch_bounds__(512, 1) select_bounded_kernel(SelectArgs a) {
   const int r = row / a.hsel, hs = row - r * a.hsel;
   const int off = a.block_offsets ? a.block_offsets[r] : 0;
   const int n = a.block_offsets ? a.block_offsets[r + 1] - off : a.n;
-  if (n < a.topk || n > static_cast<int>(blockDim.x) * E) {
+  if (n < a.topk || n > NT * E) {
     pdl_wait();
     if (tid == 0) report(a.status, kStatusShapeOverflow);
     return;
@@ -671,10 +671,10 @@ __global__ void __launch_bounds__(512, 1) select_bounded_kernel(SelectArgs a) {
   if (q_staged) {
     // q is an input, not the scorer's output: staged before the wait.
     const long long q0 = (static_cast<long long>(r) * a.hq + (a.group_select ? hs * G : hs)) * a.d;
-    for (int i = tid; i < q_heads * a.d; i += blockDim.x) qsm[i] = load_any(a.q, a.q_dtype, q0 + i);
+    for (int i = tid; i < q_heads * a.d; i += NT) qsm[i] = load_any(a.q, a.q_dtype, q0 + i);
   }
   pdl_wait();  // bounds come from the preceding interval scorer
-  bounded_select_core<E>(a, row, qsm, q_staged);
+  bounded_select_core<E, NT>(a, row, qsm, q_staged);
   KT(3);
 }
 
@@ -746,18 +746,18 @@ int launch_bounds(const ScoreArgs& a, float2* bounds, cudaStream_t stream) {
   return static_cast<int>(cudaGetLastError());
 }
 
-template <int E>
-static int launch_bounded_e(const SelectArgs& a, int threads, cudaStream_t stream) {
-  prefer_shared(select_bounded_kernel<E>);
-  return launch_pdl(select_bounded_kernel<E>, dim3(a.R * a.hsel), dim3(threads), 0, stream, 0, a);
+template <int E, int NT>
+static int launch_bounded_e(const SelectArgs& a, cudaStream_t stream) {
+  prefer_shared(select_bounded_kernel<E, NT>);
+  return launch_pdl(select_bounded_kernel<E, NT>, dim3(a.R * a.hsel), dim3(NT), 0, stream, 0, a);
 }
 
 int launch_select_bounded(const SelectArgs& a, int max_n, cudaStream_t stream) {
-  if (max_n <= 1024) return launch_bounded_e<4>(a, 256, stream);
-  if (max_n <= 2048) return launch_bounded_e<4>(a, 512, stream);
-  if (max_n <= 4096) return launch_bounded_e<8>(a, 512, stream);
-  if (max_n <= 8192) return launch_bounded_e<16>(a, 512, stream);
-  if (max_n <= 16384) return launch_bounded_e<32>(a, 512, stream);
+  if (max_n <= 1024) return launch_bounded_e<4, 256>(a, stream);
+  if (max_n <= 2048) return launch_bounded_e<4, 512>(a, stream);
+  if (max_n <= 4096) return launch_bounded_e<8, 512>(a, stream);
+  if (max_n <= 8192) return launch_bounded_e<16, 512>(a, stream);
+  if (max_n <= 16384) return launch_bounded_e<32, 512>(a, stream);
   return -1;
 }
 

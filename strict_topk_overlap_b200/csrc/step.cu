@@ -19,12 +19,12 @@
 // Grid: one CTA per SM, launched cooperatively so that every CTA is resident
 // and a CTA may wait for another's progress (each such wait is bounded by
 // the library's wait limit and reports STK_STATUS_WAIT_TIMEOUT when it runs
-// out). The last hq CTAs are row CTAs: CTA grid - hq + r scores its share
-// of the metadata, selects row r's strict Top-K (the second stage of the
-// two-stage selection, topk.cuh) and finishes row r. The other CTAs score
-// their share of the metadata, then compute per-block states: of the
-// predicted blocks (speculative step, from the start), or of the selected
-// blocks as each row's selection is published (serial step).
+// out). Every CTA scores its share of the metadata. The last hq CTAs are
+// row CTAs: CTA grid - hq + r then selects row r's strict Top-K (the second
+// stage of the two-stage selection, topk.cuh) and finishes row r. The other
+// (work) CTAs then compute per-block states: of the predicted blocks
+// (speculative step, right behind their metadata), or of the selected blocks
+// as each row's selection is published (serial step).
 //
 // Inside a CTA, warp 11 issues 1-D bulk copies into a ring of 11 stages of
 // 16 KiB (each on a "full" mbarrier with the copy's byte count) in item
@@ -50,6 +50,18 @@
 // a reader waits with acquire loads and reads the data through L2.
 
 #include "block_state.cuh"
+#include "common.cuh"
+
+#ifdef STK_TRACE
+namespace stk {
+// [cta][32] timeline of the fused step (profiling builds only).
+static __device__ unsigned long long g_step_trace[256 * 32];
+static __device__ long long g_step_clk[256 * 8];
+}  // namespace stk
+// Phases of the selection inside the fused step: events 16 + ev, thread 0
+// (global timer), and the SM cycle counter beside it.
+#define STK_TOPK_PROBE(ev) do { if (threadIdx.x == 0 && blockIdx.x < 256) { STK_TRACE_AT(stk::g_step_trace, blockIdx.x * 32 + 16 + (ev)); stk::g_step_clk[blockIdx.x * 8 + (ev)] = clock64(); } } while (0)
+#endif
 #include "topk.cuh"
 
 namespace stk {
@@ -67,17 +79,18 @@ constexpr int kStepMaxList = 256;                                // topk and pre
 constexpr int kStepMaxBlocks = 4096;                             // blocks per request limit
 
 #ifdef STK_TRACE
-// [cta][16] timeline of the fused step (profiling builds only).
-static __device__ unsigned long long g_step_trace[256 * 16];
+extern "C" __attribute__((visibility("default"))) int stk_trace_step_clk(void* host) {
+  return static_cast<int>(cudaMemcpyFromSymbol(host, g_step_clk, sizeof(g_step_clk)));
+}
 extern "C" __attribute__((visibility("default"))) int stk_trace_step_read(void* host, size_t bytes, int clear) {
   int rc = static_cast<int>(cudaMemcpyFromSymbol(host, g_step_trace, bytes));
   if (!rc && clear) {
-    static unsigned long long zeros[256 * 16];
+    static unsigned long long zeros[256 * 32];
     rc = static_cast<int>(cudaMemcpyToSymbol(g_step_trace, zeros, sizeof(zeros)));
   }
   return rc;
 }
-#define SPT(ev) do { if (blockIdx.x < 256) STK_TRACE_AT(g_step_trace, blockIdx.x * 16 + (ev)); } while (0)
+#define SPT(ev) do { if (blockIdx.x < 256) STK_TRACE_AT(g_step_trace, blockIdx.x * 32 + (ev)); } while (0)
 #else
 #define SPT(ev) ((void)0)
 #endif
@@ -120,36 +133,87 @@ __device__ __forceinline__ void fold_state(float& wm, float& wl, float (&wu)[kSt
   wm = M;
 }
 
-// Warm the instruction cache of a row CTA's later phases while the other
-// CTAs score the metadata: a selection over a synthetic row (distinct,
-// well-separated scores: the common path without straddlers) written to the
-// row's own warm-up slots, and one block reduction per consumer warp over
-// whatever its stage holds. Nothing here reaches the step's outputs.
-template <typename T, int E>
-__device__ __forceinline__ void warm_row_cta(const StepArgs& a, int row, const float* qrow, unsigned char* pool,
-                                             int warp, int lane, float* sink) {
-  const int n = a.n;
-  float2* wb = a.warm_bounds + static_cast<long long>(row) * n;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float x = static_cast<float>(n - i);
-    wb[i] = make_float2(x, x);
-  }
-  __threadfence();
-  __syncthreads();
-  SelectArgs wa{};
-  wa.R = 1; wa.hsel = a.hq; wa.topk = a.topk; wa.n = n; wa.block_offsets = nullptr; wa.total_blocks = n;
-  wa.id_base = 0; wa.ids_out = a.warm_ids; wa.keys_out = nullptr; wa.status = nullptr;
-  wa.bounds = a.warm_bounds; wa.q = a.q; wa.q_dtype = a.q_dtype; wa.lo = a.lo; wa.hi = a.hi;
-  wa.hq = a.hq; wa.hmeta = a.hkv; wa.d = kStepD; wa.group_select = 0;
-  bounded_select_core<E>(wa, row, qrow, true);
-  if (warp < kStepStages) {
-    constexpr int DPH = kStepDPH;
-    float qf[DPH], m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
+// Score intervals of one metadata item: up to 16 blocks of KV head mh for
+// its G query heads, staged as lo rows [16][D] then hi rows [16][D]. Lane =
+// block-in-half * 4 + quarter of D, and every lane takes one block of each
+// half (bA and bA + 8), so the query chunks it loads serve two blocks and it
+// keeps 2 G independent sums. Per block and head the sum, its radius and the
+// rounding are those of bound_interval_kernel (select.cu): each lane sums its
+// D / 4 dims in order with FP32 FMA, two shuffle levels finish the sum, and
+// the interval is widened by 2 (D/4 + 2) u ||q||_1 max|lo, hi| + 2^-118 and
+// rounded outward.
+template <int GM>
+__device__ __forceinline__ void score_item(const StepArgs& a, const float* slo, const float* shi, const float* qs,
+                                           const float* qn1, int mh, int b0, int nb, int G, int lane) {
+  constexpr int D = kStepD;
+  constexpr float kErrFactor = 2.f * (D / 4 + 2) * 0x1p-24f;
+  const int p = lane & 3;
+  const int bA = lane >> 2, bB = bA + 8;
+  const bool liveA = bA < nb, liveB = bB < nb;
+  const float4* LA = reinterpret_cast<const float4*>(slo + (liveA ? bA : 0) * D);
+  const float4* HA = reinterpret_cast<const float4*>(shi + (liveA ? bA : 0) * D);
+  const float4* LB = reinterpret_cast<const float4*>(slo + (liveB ? bB : 0) * D);
+  const float4* HB = reinterpret_cast<const float4*>(shi + (liveB ? bB : 0) * D);
+  const float* qrow = qs + mh * G * D;
+  float sA[GM], sB[GM];
 #pragma unroll
-    for (int j = 0; j < DPH; ++j) { qf[j] = qrow[(lane & 15) * DPH + j]; u[j] = 0.f; ua[j] = 0.f; }
-    const T* ks = reinterpret_cast<const T*>(pool + static_cast<size_t>(warp) * kStageBytes);
-    warp_block_state<T, DPH, kModeFull, true>(ks, ks + kStepB * kStepD, kStepB, qf, a.scale, 0.f, m, l, u, ua, lane);
-    if (m == 1234.5f && l == 0.5f) sink[0] = u[0];  // keeps the pass; never true for a finite block of logits
+  for (int g = 0; g < GM; ++g) { sA[g] = 0.f; sB[g] = 0.f; }
+  float mA = 0.f, mB = 0.f;
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < D / 16; ++i) {
+    const int c = p + 4 * i;
+    const float4 la = liveA ? LA[c] : z, ha = liveA ? HA[c] : z;
+    const float4 lb = liveB ? LB[c] : z, hb = liveB ? HB[c] : z;
+    mA = fmaxf(mA, fmaxf(fmaxf(fabsf(la.x), fabsf(ha.x)), fmaxf(fabsf(la.y), fabsf(ha.y))));
+    mA = fmaxf(mA, fmaxf(fmaxf(fabsf(la.z), fabsf(ha.z)), fmaxf(fabsf(la.w), fabsf(ha.w))));
+    mB = fmaxf(mB, fmaxf(fmaxf(fabsf(lb.x), fabsf(hb.x)), fmaxf(fabsf(lb.y), fabsf(hb.y))));
+    mB = fmaxf(mB, fmaxf(fmaxf(fabsf(lb.z), fabsf(hb.z)), fmaxf(fabsf(lb.w), fabsf(hb.w))));
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      if (g < G) {
+        const float4 qq = *reinterpret_cast<const float4*>(qrow + g * D + 4 * c);
+        sA[g] = fmaf(qq.x, qq.x >= 0.f ? ha.x : la.x, sA[g]);
+        sB[g] = fmaf(qq.x, qq.x >= 0.f ? hb.x : lb.x, sB[g]);
+        sA[g] = fmaf(qq.y, qq.y >= 0.f ? ha.y : la.y, sA[g]);
+        sB[g] = fmaf(qq.y, qq.y >= 0.f ? hb.y : lb.y, sB[g]);
+        sA[g] = fmaf(qq.z, qq.z >= 0.f ? ha.z : la.z, sA[g]);
+        sB[g] = fmaf(qq.z, qq.z >= 0.f ? hb.z : lb.z, sB[g]);
+        sA[g] = fmaf(qq.w, qq.w >= 0.f ? ha.w : la.w, sA[g]);
+        sB[g] = fmaf(qq.w, qq.w >= 0.f ? hb.w : lb.w, sB[g]);
+      }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < GM; ++g) {
+    sA[g] += __shfl_xor_sync(kFull, sA[g], 1);
+    sB[g] += __shfl_xor_sync(kFull, sB[g], 1);
+    sA[g] += __shfl_xor_sync(kFull, sA[g], 2);
+    sB[g] += __shfl_xor_sync(kFull, sB[g], 2);
+  }
+  mA = fmaxf(mA, __shfl_xor_sync(kFull, mA, 1));
+  mB = fmaxf(mB, __shfl_xor_sync(kFull, mB, 1));
+  mA = fmaxf(mA, __shfl_xor_sync(kFull, mA, 2));
+  mB = fmaxf(mB, __shfl_xor_sync(kFull, mB, 2));
+  const float inf = __int_as_float(0x7f800000);
+#pragma unroll
+  for (int g = 0; g < GM; ++g) {
+    if (g < G && (g & 3) == p) {
+      const float qn = qn1[mh * G + g];
+      float2* out = a.bounds + static_cast<long long>(mh * G + g) * a.n + b0;
+      if (liveA) {
+        const float e = __fadd_ru(__fmul_ru(__fmul_ru(qn, mA), kErrFactor), 0x1p-118f);
+        float2 iv = make_float2(__fsub_rd(sA[g], e), __fadd_ru(sA[g], e));
+        if (!(iv.x <= iv.y)) iv = make_float2(-inf, inf);
+        out[bA] = iv;
+      }
+      if (liveB) {
+        const float e = __fadd_ru(__fmul_ru(__fmul_ru(qn, mB), kErrFactor), 0x1p-118f);
+        float2 iv = make_float2(__fsub_rd(sB[g], e), __fadd_ru(sB[g], e));
+        if (!(iv.x <= iv.y)) iv = make_float2(-inf, inf);
+        out[bB] = iv;
+      }
+    }
   }
 }
 
@@ -158,7 +222,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
   constexpr int D = kStepD;
   constexpr int DPH = kStepDPH;
   constexpr int NS = kStepStages;
-  constexpr float kErrFactor = 2.f * (D / 4 + 2) * 0x1p-24f;  // the interval scorer's radius (select.cu)
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ uint64_t full_bar[NS], empty_bar[NS];
   __shared__ int item_ok[NS];
@@ -168,7 +231,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
   __shared__ unsigned s_pmask[kStepMaxBlocks / 32], s_amask[kStepMaxBlocks / 32];
   __shared__ float s_wm[kStepWarps], s_wl[kStepWarps];
   __shared__ __align__(16) float s_wu[kStepWarps][D];
-  __shared__ float s_sink[1];
+  __shared__ uint64_t fold_bar;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int hq = a.hq, hkv = a.hkv, n = a.n, K = a.topk;
@@ -181,8 +244,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
   const int S = serial ? K : a.sp;
   const int ipH = (n + kMetaItemBlocks - 1) / kMetaItemBlocks;  // metadata items per KV head
   const int n_meta = hkv * ipH;
-  // Work CTA c: metadata items c, c + W, ... and jobs [j0, j1) of the hq * S (row, slot) jobs.
-  const int my_meta = row_cta ? 0 : (static_cast<int>(blockIdx.x) < n_meta ? (n_meta - 1 - static_cast<int>(blockIdx.x)) / W + 1 : 0);
+  // Every CTA c scores metadata items c, c + grid, ...; work CTA c then takes
+  // jobs [j0, j1) of the hq * S (row, slot) block states.
+  const int my_meta = static_cast<int>(blockIdx.x) < n_meta ? (n_meta - 1 - static_cast<int>(blockIdx.x)) / grid + 1 : 0;
   const long long J = static_cast<long long>(hq) * S;
   const int j0 = row_cta ? 0 : static_cast<int>(J * blockIdx.x / W);
   const int j1 = row_cta ? 0 : static_cast<int>(J * (blockIdx.x + 1) / W);
@@ -207,6 +271,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
       mbar_init(&full_bar[i], 1);
       mbar_init(&empty_bar[i], 1);
     }
+    mbar_init(&fold_bar, 1);
     fence_barrier_init();
     s_abort = 0;
   }
@@ -240,7 +305,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
     }
   };
   auto meta_item = [&](int it, int& mh, int& b0) {
-    const int m = static_cast<int>(blockIdx.x) + it * W;
+    const int m = static_cast<int>(blockIdx.x) + it * grid;
     mh = m / ipH;
     b0 = (m % ipH) * kMetaItemBlocks;
   };
@@ -248,8 +313,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
   // The small loads are issued first and consumed after the bulk copies are
   // queued: q (16 bytes per thread), the predicted IDs of this CTA's first
   // jobs (producer lanes) or of its row (row CTA).
-  const int qvals = row_cta ? D : hq * D;
-  const long long q0 = row_cta ? static_cast<long long>(row) * D : 0;
+  const int qvals = hq * D;
   const int qper = a.q_dtype == kF32 ? 4 : 8;  // values per 16-byte load
   float qv[2][8];
 #pragma unroll
@@ -259,7 +323,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
     for (int e = 0; e < 8; ++e) qv[c][e] = 0.f;
     if (i < qvals) {
       const uint4 x = __ldg(reinterpret_cast<const uint4*>(static_cast<const unsigned char*>(a.q) +
-                                                           (q0 + i) * (a.q_dtype == kF32 ? 4 : 2)));
+                                                           static_cast<long long>(i) * (a.q_dtype == kF32 ? 4 : 2)));
       if (a.q_dtype == kF32) {
         qv[c][0] = __uint_as_float(x.x); qv[c][1] = __uint_as_float(x.y);
         qv[c][2] = __uint_as_float(x.z); qv[c][3] = __uint_as_float(x.w);
@@ -297,11 +361,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
   for (int c = 0; c < 2; ++c) {
     const int i = (c * kStepThreads + tid) * qper;
     if (i < qvals)
-      for (int e = 0; e < qper; ++e) qs[q0 + i + e] = qv[c][e];
+      for (int e = 0; e < qper; ++e) qs[i + e] = qv[c][e];
   }
   __syncthreads();
-  for (int t = row_cta ? row : warp; t < (row_cta ? row + 1 : hq); t += kStepWarps) {
-    if (row_cta && warp != 0) break;
+  for (int t = warp; t < hq; t += kStepWarps) {
     float sum = 0.f;
     for (int dd = lane; dd < D; dd += 32) sum = __fadd_ru(sum, fabsf(qs[t * D + dd]));
 #pragma unroll
@@ -311,164 +374,132 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
   __syncthreads();
   if (tid == 0) SPT(1);
 
-  if (!row_cta) {
-    // ------------------------------------------------------------ work CTA
-    if (warp == kStepProducer) {
-      int ready_row = -1;  // serial: rows whose selection this warp has seen published
-      long long sid = -1;  // serial: selected ID of job sb + lane
-      int sb = -1;
-      for (int it = n_first; it < n_items; ++it) {
-        if (it < my_meta) {
-          if (lane == 0) {
-            int mh, b0;
-            meta_item(it, mh, b0);
-            produce(it, 0, mh, b0, 0);
-          }
-        } else {
-          const int jl = it - my_meta;  // this CTA's job index
-          const int job = j0 + jl;
-          const int r = job / S;
-          long long id = -1;
-          if (!serial) {
-            if (jl - jb == 32) {
-              jb += 32;
-              lid = jb + lane < my_jobs ? load_id(a.pred, a.pred64, j0 + jb + lane) : -1;
-            }
-            id = __shfl_sync(kFull, lid, jl - jb);
-          } else {
-            if (r > ready_row) {
-              if (lane == 0 && !s_abort && !wait_count(&row_ready[r], 1)) {
-                report(a.status, kStatusWaitTimeout);
-                s_abort = 1;
-              }
-              __syncwarp();
-              ready_row = r;
-              sb = -1;
-            }
-            if (sb < 0 || job - sb >= 32) {
-              // The selected IDs of the next 32 jobs of row r (job = r * K + slot).
-              sb = job;
-              const int jj = job + lane;
-              sid = (!s_abort && jj < j1 && jj / S == r) ? __ldcg(a.selected + jj) : -1;
-            }
-            id = __shfl_sync(kFull, sid, job - sb);
-          }
-          if (lane == 0) produce(it, 1, r / G, 0, id);
-        }
-        if (lane == 0 && it == my_meta) SPT(3);
-        __syncwarp();
-      }
-      if (lane == 0) SPT(4);
-    } else if (warp < NS) {
-      // Consumers: item it belongs to warp it % NS (one consumer per stage).
-      if (lane == 0 && warp == 0) SPT(12);
-      for (int it = warp; it < n_items; it += NS) {
-        const int st = it % NS;
-        const bool landed = mbar_wait(&full_bar[st], (it / NS) & 1u, a.status);
-        if (lane == 0 && it == 0) SPT(13);
-        if (!landed) s_abort = 1;
-        const bool ok = landed && item_ok[st] != 0;
-        const unsigned char* stage = pool + static_cast<size_t>(st) * kStageBytes;
-        if (it < my_meta) {
-          // Score intervals of up to 16 blocks of KV head mh for its G query
-          // heads, 8 blocks per pass; lane = block * 4 + quarter of D, with
-          // the lane mapping, error bound and rounding of bound_interval_kernel.
+  // ---------------------------------------------------------------- ring: metadata, then block states
+  if (warp == kStepProducer) {
+    int ready_row = -1;  // serial: rows whose selection this warp has seen published
+    long long sid = -1;  // serial: selected ID of job sb + lane
+    int sb = -1;
+    for (int it = n_first; it < n_items; ++it) {
+      if (it < my_meta) {
+        if (lane == 0) {
           int mh, b0;
           meta_item(it, mh, b0);
-          const int nb = min(kMetaItemBlocks, n - b0);
-          const float* slo = reinterpret_cast<const float*>(stage);
-          const float* shi = reinterpret_cast<const float*>(stage + kStageBytes / 2);
-          const float* qrow = qs + mh * G * D;
-          const int p = lane & 3;
-          if (ok) {
-#pragma unroll 1
-            for (int pass = 0; pass < kMetaItemBlocks / 8; ++pass) {
-              const int b = pass * 8 + (lane >> 2);
-              const bool live = b < nb;
-              const float4* L4 = reinterpret_cast<const float4*>(slo + (live ? b : 0) * D);
-              const float4* H4 = reinterpret_cast<const float4*>(shi + (live ? b : 0) * D);
-              float s[GM];
-#pragma unroll
-              for (int g = 0; g < GM; ++g) s[g] = 0.f;
-              float mabs = 0.f;
-#pragma unroll
-              for (int i = 0; i < D / 16; ++i) {
-                const float4 l = live ? L4[p + 4 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
-                const float4 h = live ? H4[p + 4 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
-                mabs = fmaxf(mabs, fmaxf(fmaxf(fabsf(l.x), fabsf(h.x)), fmaxf(fabsf(l.y), fabsf(h.y))));
-                mabs = fmaxf(mabs, fmaxf(fmaxf(fabsf(l.z), fabsf(h.z)), fmaxf(fabsf(l.w), fabsf(h.w))));
-                const int off = 4 * (p + 4 * i);
-#pragma unroll
-                for (int g = 0; g < GM; ++g) {
-                  if (g < G) {
-                    const float4 qq = *reinterpret_cast<const float4*>(qrow + g * D + off);
-                    s[g] = fmaf(qq.x, qq.x >= 0.f ? h.x : l.x, s[g]);
-                    s[g] = fmaf(qq.y, qq.y >= 0.f ? h.y : l.y, s[g]);
-                    s[g] = fmaf(qq.z, qq.z >= 0.f ? h.z : l.z, s[g]);
-                    s[g] = fmaf(qq.w, qq.w >= 0.f ? h.w : l.w, s[g]);
-                  }
-                }
-              }
-#pragma unroll
-              for (int g = 0; g < GM; ++g) {
-                s[g] += __shfl_xor_sync(kFull, s[g], 1);
-                s[g] += __shfl_xor_sync(kFull, s[g], 2);
-              }
-              mabs = fmaxf(mabs, __shfl_xor_sync(kFull, mabs, 1));
-              mabs = fmaxf(mabs, __shfl_xor_sync(kFull, mabs, 2));
-              if (live) {
-                const float inf = __int_as_float(0x7f800000);
-#pragma unroll
-                for (int g = 0; g < GM; ++g) {
-                  if (g < G && (g & 3) == p) {
-                    const float e = __fadd_ru(__fmul_ru(__fmul_ru(qn1[mh * G + g], mabs), kErrFactor), 0x1p-118f);
-                    float2 iv = make_float2(__fsub_rd(s[g], e), __fadd_ru(s[g], e));
-                    if (!(iv.x <= iv.y)) iv = make_float2(-inf, inf);
-                    a.bounds[static_cast<long long>(mh * G + g) * n + b0 + b] = iv;
-                  }
-                }
-              }
-            }
+          produce(it, 0, mh, b0, 0);
+        }
+      } else {
+        const int jl = it - my_meta;  // this CTA's job index
+        const int job = j0 + jl;
+        const int r = job / S;
+        long long id = -1;
+        if (!serial) {
+          if (jl - jb == 32) {
+            jb += 32;
+            lid = jb + lane < my_jobs ? load_id(a.pred, a.pred64, j0 + jb + lane) : -1;
           }
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&empty_bar[st]);
-            publish(&head_done[mh]);
-          }
+          id = __shfl_sync(kFull, lid, jl - jb);
         } else {
-          // One block's softmax state for (row r, slot).
-          const int job = j0 + (it - my_meta);
-          const int r = job / S, slot = job - r * S;
-          float m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
-#pragma unroll
-          for (int j = 0; j < DPH; ++j) { u[j] = 0.f; ua[j] = 0.f; }
-          if (ok) {
-            float qf[DPH];
-#pragma unroll
-            for (int j = 0; j < DPH; ++j) qf[j] = qs[r * D + (lane & 15) * DPH + j];
-            const T* ks = reinterpret_cast<const T*>(stage);
-            warp_block_state<T, DPH, kModeFull, true>(ks, ks + kStepB * D, kStepB, qf, a.scale, 0.f, m, l, u, ua,
-                                                      lane);
+          if (r > ready_row) {
+            if (lane == 0 && !s_abort && !wait_count(&row_ready[r], 1)) {
+              report(a.status, kStatusWaitTimeout);
+              s_abort = 1;
+            }
+            __syncwarp();
+            ready_row = r;
+            sb = -1;
           }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty_bar[st]);
-          const long long o = static_cast<long long>(r) * S + slot;
-          if (lane == 0) {
-            a.sm[o] = m;
-            a.sl[o] = l;
+          if (sb < 0 || job - sb >= 32) {
+            // The selected IDs of the next 32 jobs of row r (job = r * K + slot).
+            sb = job;
+            const int jj = job + lane;
+            sid = (!s_abort && jj < j1 && jj / S == r) ? __ldcg(a.selected + jj) : -1;
           }
-          if (lane < 16) store_vec<DPH>(a.su + o * D + lane * DPH, u);
-          __syncwarp();
-          if (lane == 0) publish(&row_states[r]);
+          id = __shfl_sync(kFull, sid, job - sb);
+        }
+        if (lane == 0) produce(it, 1, r / G, 0, id);
+      }
+      if (lane == 0 && it == my_meta) SPT(3);
+      if (lane == 0 && it == NS) SPT(30);
+      if (lane == 0 && it == 2 * NS) SPT(31);
+      __syncwarp();
+    }
+    if (lane == 0) SPT(4);
+  } else if (warp < NS) {
+    // Consumers: item it belongs to warp it % NS (one consumer per stage).
+    // Block-state completions are published per row in batches (one fence
+    // per row change and one at the end), metadata items one by one: the
+    // selections wait on them.
+    int pend_row = -1, pend = 0;
+    if (lane == 0 && warp == 0) SPT(12);
+    for (int it = warp; it < n_items; it += NS) {
+      const int st = it % NS;
+      const bool landed = mbar_wait(&full_bar[st], (it / NS) & 1u, a.status);
+      if (lane == 0 && it == 0) SPT(13);
+      if (lane == 0 && warp == 0 && it / NS < 3) SPT(24 + it / NS);
+      if (!landed) s_abort = 1;
+      const bool ok = landed && item_ok[st] != 0;
+      const unsigned char* stage = pool + static_cast<size_t>(st) * kStageBytes;
+      if (it < my_meta) {
+        int mh, b0;
+        meta_item(it, mh, b0);
+        if (ok)
+          score_item<GM>(a, reinterpret_cast<const float*>(stage),
+                         reinterpret_cast<const float*>(stage + kStageBytes / 2), qs, qn1, mh, b0,
+                         min(kMetaItemBlocks, n - b0), G, lane);
+        __syncwarp();
+        if (lane == 0 && warp == 0 && it == 0) SPT(22);
+        if (lane == 0) {
+          mbar_arrive(&empty_bar[st]);
+          publish(&head_done[mh]);
+        }
+      } else {
+        // One block's softmax state for (row r, slot).
+        const int job = j0 + (it - my_meta);
+        const int r = job / S, slot = job - r * S;
+        float m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
+#pragma unroll
+        for (int j = 0; j < DPH; ++j) { u[j] = 0.f; ua[j] = 0.f; }
+        if (ok) {
+          float qf[DPH];
+#pragma unroll
+          for (int j = 0; j < DPH; ++j) qf[j] = qs[r * D + (lane & 15) * DPH + j];
+          const T* ks = reinterpret_cast<const T*>(stage);
+          warp_block_state<T, DPH, kModeFull, true>(ks, ks + kStepB * D, kStepB, qf, a.scale, 0.f, m, l, u, ua,
+                                                    lane);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[st]);
+        const long long o = static_cast<long long>(r) * S + slot;
+        if (lane == 0) {
+          a.sm[o] = m;
+          a.sl[o] = l;
+        }
+        if (lane < 16) store_vec<DPH>(a.su + o * D + lane * DPH, u);
+        __syncwarp();
+        if (lane == 0 && warp == 0 && it == NS) SPT(23);
+        if (lane == 0) {
+          if (r != pend_row && pend > 0) {
+            __threadfence();
+            atomicAdd(&row_states[pend_row], static_cast<unsigned>(pend));
+            pend = 0;
+          }
+          pend_row = r;
+          ++pend;
         }
       }
-      if (lane == 0 && warp == 0) SPT(14);
+      if (lane == 0 && warp == 0 && it / NS < 3) SPT(27 + it / NS);
     }
-  } else {
-    // ------------------------------------------------------------ row CTA
+    if (lane == 0 && pend > 0) {
+      __threadfence();
+      atomicAdd(&row_states[pend_row], static_cast<unsigned>(pend));
+    }
+    if (lane == 0 && warp == 0) SPT(14);
+  }
+
+  // ---------------------------------------------------------------- row CTAs
+  __syncthreads();
+  if (row_cta) {
     const float* qrow = qs + row * D;
     const int mh = row / G;
-    warm_row_cta<T, E>(a, row, qrow, pool, warp, lane, s_sink);
     if (tid == 0) SPT(5);
     if (tid == 0 && !s_abort && !wait_count(&head_done[mh], static_cast<unsigned>(ipH))) {
       report(a.status, kStatusWaitTimeout);
@@ -482,7 +513,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
       sa.id_base = 0; sa.ids_out = a.selected; sa.keys_out = nullptr; sa.status = a.status;
       sa.bounds = a.bounds; sa.q = a.q; sa.q_dtype = a.q_dtype; sa.lo = a.lo; sa.hi = a.hi;
       sa.hq = hq; sa.hmeta = hkv; sa.d = D; sa.group_select = 0;
-      bounded_select_core<E>(sa, row, qrow, true);
+      bounded_select_core<E, kStepThreads>(sa, row, qrow, true);
+#ifdef STK_TOPK_TWICE
+      __syncthreads();
+      if (tid == 0) SPT(21);
+      bounded_select_core<E, kStepThreads>(sa, row, qrow, true);
+#endif
     }
     __syncthreads();
     if (tid == 0) SPT(7);
@@ -530,17 +566,19 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
       }
       __syncthreads();
       const int nmiss = s_abort ? 0 : s_nmiss;
-      // Misses through the ring (items 0 .. nmiss - 1 of this CTA).
+      // Misses through the ring, continuing after this CTA's metadata items.
       if (warp == kStepProducer) {
-        if (lane < min(nmiss, NS)) produce(lane, 1, mh, 0, s_miss[lane]);
-        for (int i = NS; i < nmiss; ++i) {
-          if (lane == 0) produce(i, 1, mh, 0, s_miss[i]);
+        for (int i = 0; i < nmiss; ++i) {
+          if (lane == 0) produce(n_items + i, 1, mh, 0, s_miss[i]);
           __syncwarp();
         }
       } else if (warp < NS) {
-        for (int it = warp; it < nmiss; it += NS) {
+        // Item n_items + i belongs to warp (n_items + i) % NS, like every item of the ring.
+        for (int i = (warp - n_items % NS + NS) % NS; i < nmiss; i += NS) {
+          const int it = n_items + i;
           const int st = it % NS;
           const bool landed = mbar_wait(&full_bar[st], (it / NS) & 1u, a.status);
+          if (lane == 0 && i < NS) SPT(15);
           if (!landed) s_abort = 1;
           if (landed && item_ok[st]) {
             float qf[DPH], m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
@@ -560,21 +598,18 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
     }
     if (tid == 0) SPT(8);
     // The row's S block states are complete: bring their numerators into
-    // shared memory with one bulk copy (S x D FP32, after the misses' stages
+    // shared memory with one bulk copy (S x D FP32, once the ring's stages
     // are drained), and their (m, l) with plain loads through L2.
     __syncthreads();
     float* st_u = reinterpret_cast<float*>(pool);
     float* st_m = reinterpret_cast<float*>(pool + static_cast<size_t>(S) * D * 4);
     float* st_l = st_m + S;
-    __shared__ uint64_t fold_bar;
     if (tid == 0) {
       if (!s_abort && !wait_count(&row_states[row], static_cast<unsigned>(S))) {
         report(a.status, kStatusWaitTimeout);
         s_abort = 1;
       }
       SPT(9);
-      mbar_init(&fold_bar, 1);
-      fence_barrier_init();
       if (!s_abort) {
         // The numerators were written by other CTAs (generic proxy) and are
         // read here by the bulk-copy (async) proxy.

@@ -10,6 +10,11 @@
 
 #include "internal.cuh"
 
+// Phase probes of bounded_select_core (profiling builds of a caller define it).
+#ifndef STK_TOPK_PROBE
+#define STK_TOPK_PROBE(ev) ((void)0)
+#endif
+
 namespace stk {
 
 // ------------------------------------------------------------------ Top-K
@@ -292,10 +297,14 @@ __device__ __forceinline__ int hist_bin(float x, float mn, float scale) {
   return min(kHistBins - 1, max(0, b));
 }
 
-// Block-wide exclusive scan of one unsigned per thread (blockDim <= 512);
-// returns the exclusive prefix and writes the block total to *total.
+// Block-wide exclusive scan of one unsigned per thread over NT (<= 1024)
+// threads; returns the exclusive prefix and writes the block total to
+// *total. One barrier: each warp scans the per-warp totals itself with
+// shuffles.
+template <int NT>
 __device__ __forceinline__ unsigned block_exclusive_scan(unsigned v, unsigned* wsum, unsigned* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  constexpr int NW = NT / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   unsigned inc = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -304,26 +313,29 @@ __device__ __forceinline__ unsigned block_exclusive_scan(unsigned v, unsigned* w
   }
   if (lane == 31) wsum[warp] = inc;
   __syncthreads();
-  unsigned before = 0, all = 0;
-  for (int w = 0; w < nw; ++w) {
-    const unsigned x = wsum[w];
-    before += w < warp ? x : 0u;
-    all += x;
+  const unsigned x = lane < NW ? wsum[lane] : 0u;
+  unsigned sc = x;
+#pragma unroll
+  for (int o = 1; o < NW; o <<= 1) {
+    const unsigned y = __shfl_up_sync(kFull, sc, o);
+    if (lane >= o) sc += y;
   }
-  *total = all;
-  return before + inc - v;
+  *total = __shfl_sync(kFull, sc, NW - 1);
+  return __shfl_sync(kFull, sc - x, warp) + inc - v;
 }
 
 // The second stage of the two-stage selection, for selection row `row` of
-// `a`, run by every thread of the calling CTA (blockDim.x <= 512 and
-// E * blockDim.x >= the row's blocks, checked by the caller). `qsm` holds
+// `a`, run by every thread of the calling CTA (NT threads, NT <= 512 and
+// E * NT >= the row's blocks, checked by the caller). `qsm` holds
 // the row's query heads as FP32 ([G][D] for a group row, [D] otherwise) when
 // `q_staged`; otherwise exact rescoring reads q from global memory. The
 // interval bounds are read through L2 (ld.global.cg), so they may come from
 // other CTAs of the calling kernel. Writes the row's IDs ascending (and,
 // with a.keys_out, their exact order keys).
-template <int E>
+template <int E, int NT>
 __device__ void bounded_select_core(const SelectArgs& a, int row, const float* qsm, bool q_staged) {
+  static_assert(NT % 32 == 0 && NT <= 512 && kHistBins % NT == 0, "selection block shape");
+  constexpr int NW = NT / 32;
   __shared__ unsigned hist[kHistBins];  // low 16 bits: lower ends; high 16 bits: upper ends
   __shared__ unsigned wsum[2][kSelMaxWarps];
   __shared__ float wmn[kSelMaxWarps], wmx[kSelMaxWarps];
@@ -333,7 +345,7 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
   __shared__ unsigned char unc_sel[kUncMax];
   __shared__ unsigned char cls_s[512 * E];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nw = blockDim.x >> 5;
+  constexpr int nw = NW;
   const int r = row / a.hsel, hs = row - r * a.hsel;
   const int off = a.block_offsets ? a.block_offsets[r] : 0;
   const int n = a.block_offsets ? a.block_offsets[r + 1] - off : a.n;
@@ -347,7 +359,8 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
   };
 
   {
-    for (int i = tid; i < kHistBins; i += blockDim.x) hist[i] = 0u;
+#pragma unroll
+    for (int i = tid; i < kHistBins; i += NT) hist[i] = 0u;
     if (tid == 0) { s_bt = 0; s_bu = 0; }
     float lo_[E], up_[E];
     float mn = inf, mx = -inf;
@@ -370,16 +383,21 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
     }
     if (lane == 0) { wmn[warp] = mn; wmx[warp] = mx; }
     __syncthreads();
-    mn = wmn[0];
-    mx = wmx[0];
-    for (int w = 1; w < nw; ++w) { mn = fminf(mn, wmn[w]); mx = fmaxf(mx, wmx[w]); }
+    STK_TOPK_PROBE(0);
+    mn = lane < NW ? wmn[lane] : inf;
+    mx = lane < NW ? wmx[lane] : -inf;
+#pragma unroll
+    for (int o = NW / 2; o > 0; o >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(kFull, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+    }
     float scale = 0.f;
     if (mx > mn) scale = fminf(static_cast<float>(kHistBins) / (mx - mn), 0x1p100f);
     if (!(mn < inf)) mn = 0.f;
 
     if (n == K) {
       // Everything is selected.
-      for (int i = tid; i < n; i += blockDim.x) out[i] = a.id_base + i;
+      for (int i = tid; i < n; i += NT) out[i] = a.id_base + i;
     } else {
 #pragma unroll
       for (int j = 0; j < E; ++j) {
@@ -389,21 +407,28 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
         }
       }
       __syncthreads();
+      STK_TOPK_PROBE(1);
       // Suffix counts: thread t owns bins [kHistBins - (t+1)*per, kHistBins - t*per), scanned downward.
-      const int per = kHistBins / blockDim.x;
+      constexpr int per = kHistBins / NT;
       const int top = kHistBins - 1 - tid * per;
-      unsigned loc = 0;
-      for (int i = 0; i < per; ++i) loc += hist[top - i];
-      unsigned tot;
-      unsigned c = block_exclusive_scan(loc, wsum[0], &tot);
+      unsigned hv[per], loc = 0;
+#pragma unroll
       for (int i = 0; i < per; ++i) {
-        const unsigned h = hist[top - i];
+        hv[i] = hist[top - i];
+        loc += hv[i];
+      }
+      unsigned tot;
+      unsigned c = block_exclusive_scan<NT>(loc, wsum[0], &tot);
+#pragma unroll
+      for (int i = 0; i < per; ++i) {
+        const unsigned h = hv[i];
         const unsigned lo_before = c & 0xffffu, up_before = c >> 16;
         c += h;
         if (lo_before < static_cast<unsigned>(K) && (c & 0xffffu) >= static_cast<unsigned>(K)) s_bt = top - i;
         if (up_before < static_cast<unsigned>(K + 1) && (c >> 16) >= static_cast<unsigned>(K + 1)) s_bu = top - i;
       }
       __syncthreads();
+      STK_TOPK_PROBE(2);
       const int bt = s_bt, bu = s_bu;
       // Classify: in (lower-end bin above U's bin), out (upper-end bin below T's bin), straddling.
       unsigned char cls[E];
@@ -419,8 +444,9 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
         }
       }
       const unsigned packed = (n_in << 16) | n_unc;
-      const unsigned ex = block_exclusive_scan(packed, wsum[1], &tot);
+      const unsigned ex = block_exclusive_scan<NT>(packed, wsum[1], &tot);
       const int total_in = static_cast<int>(tot >> 16), total_unc = static_cast<int>(tot & 0xffffu);
+      STK_TOPK_PROBE(3);
       int need = K - total_in;
       if (need < 0 || need > total_unc) {  // cannot happen for valid intervals
         if (tid == 0) report(a.status, kStatusShapeOverflow);
@@ -461,7 +487,7 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
             if (lane == 0) unc_key[t] = k;
           }
           __syncthreads();
-          for (int t = tid; t < total_unc; t += blockDim.x) {
+          for (int t = tid; t < total_unc; t += NT) {
             const unsigned long long kt = unc_key[t];
             int rank = 0;
             for (int j = 0; j < total_unc; ++j) {
@@ -472,6 +498,7 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
           }
           __syncthreads();
         }
+        STK_TOPK_PROBE(4);
         // Final flags and ascending output positions.
         idx = ex & 0xffffu;
         unsigned mine = 0;
@@ -486,7 +513,7 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
           mine += sel[j] ? 1u : 0u;
         }
         unsigned all;
-        unsigned pos = block_exclusive_scan(mine, wsum[0], &all);
+        unsigned pos = block_exclusive_scan<NT>(mine, wsum[0], &all);
 #pragma unroll
         for (int j = 0; j < E; ++j)
           if (sel[j]) out[pos++] = a.id_base + beg + j;
