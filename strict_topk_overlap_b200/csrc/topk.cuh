@@ -387,7 +387,7 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
     mn = lane < NW ? wmn[lane] : inf;
     mx = lane < NW ? wmx[lane] : -inf;
 #pragma unroll
-    for (int o = NW / 2; o > 0; o >>= 1) {
+    for (int o = 16; o > 0; o >>= 1) {  // every lane ends with the block's extremes
       mn = fminf(mn, __shfl_xor_sync(kFull, mn, o));
       mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
     }
