@@ -49,18 +49,25 @@
 // A writer publishes after its global writes with a fence and an atomic add;
 // a reader waits with acquire loads and reads the data through L2.
 
+#include <type_traits>
+
 #include "block_state.cuh"
 #include "common.cuh"
 
 #ifdef STK_TRACE
 namespace stk {
-// [cta][32] timeline of the fused step (profiling builds only).
-static __device__ unsigned long long g_step_trace[256 * 32];
-static __device__ long long g_step_clk[256 * 8];
+// Timeline of the fused step (profiling builds only): [cta][128] global
+// timer stamps. Probes record into shared memory (a global store could wait
+// behind this SM's bulk copies and delay the release that follows it); each
+// CTA copies its record out at exit.
+static __device__ unsigned long long g_step_trace[256 * 128];
+static __shared__ unsigned long long s_trc[128];
+// [launch % 64][first CTA start, last CTA exit] over consecutive launches.
+static __device__ unsigned long long g_step_span[2 * 64];
+static __device__ unsigned g_step_launch;
 }  // namespace stk
-// Phases of the selection inside the fused step: events 16 + ev, thread 0
-// (global timer), and the SM cycle counter beside it.
-#define STK_TOPK_PROBE(ev) do { if (threadIdx.x == 0 && blockIdx.x < 256) { STK_TRACE_AT(stk::g_step_trace, blockIdx.x * 32 + 16 + (ev)); stk::g_step_clk[blockIdx.x * 8 + (ev)] = clock64(); } } while (0)
+// Phases of the selection inside the fused step: events 16 + ev.
+#define STK_TOPK_PROBE(ev) do { if (threadIdx.x == 0) stk::s_trc[16 + (ev)] = stk::global_ns(); } while (0)
 #endif
 #include "topk.cuh"
 
@@ -70,6 +77,7 @@ constexpr int kStepThreads = 512;
 constexpr int kStepWarps = kStepThreads / 32;
 constexpr int kStepStages = 11;               // ring stages = consumer warps 0..10
 constexpr int kStepProducer = kStepStages;     // warp 11 issues the bulk copies
+constexpr int kStepHelper0 = kStepProducer + 1;  // warps 12..15 (selection, repair folds)
 constexpr int kStepD = 128;
 constexpr int kStepB = 32;
 constexpr int kStepDPH = kStepD / 16;
@@ -77,22 +85,43 @@ constexpr int kStageBytes = 2 * kStepB * kStepD * 2;            // one 16-bit K+
 constexpr int kMetaItemBlocks = kStageBytes / (2 * kStepD * 4);  // 16 blocks of FP32 lo + hi
 constexpr int kStepMaxList = 256;                                // topk and predicted-list limit
 constexpr int kStepMaxBlocks = 4096;                             // blocks per request limit
+constexpr int kItemEnd = -1;                                     // stage descriptor: no more items
+constexpr int kItemLocal = 1 << 30;                              // descriptor of row-local block i: kItemLocal + i
+// Serial step: the share of each row's selected blocks that its own row CTA
+// reduces (times 4 / (hq * topk / grid)); the rest go to the work CTAs.
+#ifndef STK_STEP_LOCAL_SHARE4
+#define STK_STEP_LOCAL_SHARE4 5
+#endif
 
 #ifdef STK_TRACE
-extern "C" __attribute__((visibility("default"))) int stk_trace_step_clk(void* host) {
-  return static_cast<int>(cudaMemcpyFromSymbol(host, g_step_clk, sizeof(g_step_clk)));
-}
 extern "C" __attribute__((visibility("default"))) int stk_trace_step_read(void* host, size_t bytes, int clear) {
   int rc = static_cast<int>(cudaMemcpyFromSymbol(host, g_step_trace, bytes));
   if (!rc && clear) {
-    static unsigned long long zeros[256 * 32];
+    static unsigned long long zeros[256 * 128];
     rc = static_cast<int>(cudaMemcpyToSymbol(g_step_trace, zeros, sizeof(zeros)));
   }
   return rc;
 }
-#define SPT(ev) do { if (blockIdx.x < 256) STK_TRACE_AT(g_step_trace, blockIdx.x * 32 + (ev)); } while (0)
+extern "C" __attribute__((visibility("default"))) int stk_trace_step_spans(void* host, int reset) {
+  int rc = static_cast<int>(cudaMemcpyFromSymbol(host, g_step_span, sizeof(g_step_span)));
+  if (!rc && reset) {
+    static unsigned long long init[2 * 64];
+    for (int i = 0; i < 2 * 64; ++i) init[i] = (i & 1) ? 0ull : ~0ull;
+    unsigned zero = 0;
+    rc = static_cast<int>(cudaMemcpyToSymbol(g_step_span, init, sizeof(init)));
+    if (!rc) rc = static_cast<int>(cudaMemcpyToSymbol(g_step_launch, &zero, sizeof(zero)));
+  }
+  return rc;
+}
+#define SPT(ev) (s_trc[(ev)] = global_ns())
+#define SPT_RAW(slot, val) (s_trc[(slot)] = (val))
+#define SPAN_START() do { if (threadIdx.x == 0) atomicMin(&g_step_span[2 * (g_step_launch & 63)], global_ns()); } while (0)
+#define SPAN_END() do { g_step_span[2 * (g_step_launch & 63) + 1] = global_ns(); ++g_step_launch; } while (0)
 #else
 #define SPT(ev) ((void)0)
+#define SPT_RAW(slot, val) ((void)0)
+#define SPAN_START() ((void)0)
+#define SPAN_END() ((void)0)
 #endif
 
 
@@ -115,9 +144,33 @@ __device__ bool wait_count(const unsigned* p, unsigned target) {
 
 // One thread, after the writes it publishes are ordered before it (warp or
 // CTA barrier): make them visible GPU-wide, then count.
-__device__ __forceinline__ void publish(unsigned* p) {
+__device__ __forceinline__ void publish(unsigned* p, unsigned count = 1u) {
   __threadfence();
-  atomicAdd(p, 1u);
+  atomicAdd(p, count);
+}
+
+// Non-blocking probe of an mbarrier phase (acquire, CTA scope).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Named barrier over the warps other than the producer (480 threads).
+__device__ __forceinline__ void sync_non_producer() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kStepThreads - 32) : "memory");
+}
+// Barrier 2: the producer arrives once its barriers are initialised, the
+// other warps wait there before their first barrier access.
+__device__ __forceinline__ void barriers_ready_arrive() {
+  asm volatile("bar.arrive 2, %0;" ::"n"(kStepThreads) : "memory");
+}
+__device__ __forceinline__ void barriers_ready_wait() {
+  asm volatile("bar.sync 2, %0;" ::"n"(kStepThreads) : "memory");
 }
 
 // Fold a block state (m, l, u) into a running LSE state (wm, wl, wu).
@@ -134,88 +187,106 @@ __device__ __forceinline__ void fold_state(float& wm, float& wl, float (&wu)[kSt
 }
 
 // Score intervals of one metadata item: up to 16 blocks of KV head mh for
-// its G query heads, staged as lo rows [16][D] then hi rows [16][D]. Lane =
-// block-in-half * 4 + quarter of D, and every lane takes one block of each
-// half (bA and bA + 8), so the query chunks it loads serve two blocks and it
-// keeps 2 G independent sums. Per block and head the sum, its radius and the
-// rounding are those of bound_interval_kernel (select.cu): each lane sums its
-// D / 4 dims in order with FP32 FMA, two shuffle levels finish the sum, and
-// the interval is widened by 2 (D/4 + 2) u ||q||_1 max|lo, hi| + 2^-118 and
-// rounded outward.
+// its G query heads, staged as lo rows [16][D] then hi rows [16][D].
+//
+// Lane l owns dims [4l, 4l + 4): every warp-wide 128-bit load reads one whole
+// 512-byte row (conflict-free), and q of four heads stays in registers. Per
+// group of 4 blocks and 4 heads each lane forms 16 partial sums (its 4 dims,
+// sequential FP32 FMA on the sign-selected bound); a transposed butterfly
+// (xor 8, 4, 2, 1) and one xor-16 add leave the total of (block j, head g) in
+// lanes 4 j + g and 16 + 4 j + g. Every term passes through at most 4 + 5
+// roundings, fewer than the D / 4 + 2 that the interval radius
+// 2 (D/4 + 2) u ||q||_1 max|lo, hi| + 2^-118 of bound_interval_kernel
+// (select.cu) covers, so the interval, rounded outward, contains the block's
+// FP64 score.
 template <int GM>
 __device__ __forceinline__ void score_item(const StepArgs& a, const float* slo, const float* shi, const float* qs,
                                            const float* qn1, int mh, int b0, int nb, int G, int lane) {
   constexpr int D = kStepD;
   constexpr float kErrFactor = 2.f * (D / 4 + 2) * 0x1p-24f;
-  const int p = lane & 3;
-  const int bA = lane >> 2, bB = bA + 8;
-  const bool liveA = bA < nb, liveB = bB < nb;
-  const float4* LA = reinterpret_cast<const float4*>(slo + (liveA ? bA : 0) * D);
-  const float4* HA = reinterpret_cast<const float4*>(shi + (liveA ? bA : 0) * D);
-  const float4* LB = reinterpret_cast<const float4*>(slo + (liveB ? bB : 0) * D);
-  const float4* HB = reinterpret_cast<const float4*>(shi + (liveB ? bB : 0) * D);
-  const float* qrow = qs + mh * G * D;
-  float sA[GM], sB[GM];
-#pragma unroll
-  for (int g = 0; g < GM; ++g) { sA[g] = 0.f; sB[g] = 0.f; }
-  float mA = 0.f, mB = 0.f;
-  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-  for (int i = 0; i < D / 16; ++i) {
-    const int c = p + 4 * i;
-    const float4 la = liveA ? LA[c] : z, ha = liveA ? HA[c] : z;
-    const float4 lb = liveB ? LB[c] : z, hb = liveB ? HB[c] : z;
-    mA = fmaxf(mA, fmaxf(fmaxf(fabsf(la.x), fabsf(ha.x)), fmaxf(fabsf(la.y), fabsf(ha.y))));
-    mA = fmaxf(mA, fmaxf(fmaxf(fabsf(la.z), fabsf(ha.z)), fmaxf(fabsf(la.w), fabsf(ha.w))));
-    mB = fmaxf(mB, fmaxf(fmaxf(fabsf(lb.x), fabsf(hb.x)), fmaxf(fabsf(lb.y), fabsf(hb.y))));
-    mB = fmaxf(mB, fmaxf(fmaxf(fabsf(lb.z), fabsf(hb.z)), fmaxf(fabsf(lb.w), fabsf(hb.w))));
-#pragma unroll
-    for (int g = 0; g < GM; ++g) {
-      if (g < G) {
-        const float4 qq = *reinterpret_cast<const float4*>(qrow + g * D + 4 * c);
-        sA[g] = fmaf(qq.x, qq.x >= 0.f ? ha.x : la.x, sA[g]);
-        sB[g] = fmaf(qq.x, qq.x >= 0.f ? hb.x : lb.x, sB[g]);
-        sA[g] = fmaf(qq.y, qq.y >= 0.f ? ha.y : la.y, sA[g]);
-        sB[g] = fmaf(qq.y, qq.y >= 0.f ? hb.y : lb.y, sB[g]);
-        sA[g] = fmaf(qq.z, qq.z >= 0.f ? ha.z : la.z, sA[g]);
-        sB[g] = fmaf(qq.z, qq.z >= 0.f ? hb.z : lb.z, sB[g]);
-        sA[g] = fmaf(qq.w, qq.w >= 0.f ? ha.w : la.w, sA[g]);
-        sB[g] = fmaf(qq.w, qq.w >= 0.f ? hb.w : lb.w, sB[g]);
-      }
-    }
-  }
-#pragma unroll
-  for (int g = 0; g < GM; ++g) {
-    sA[g] += __shfl_xor_sync(kFull, sA[g], 1);
-    sB[g] += __shfl_xor_sync(kFull, sB[g], 1);
-    sA[g] += __shfl_xor_sync(kFull, sA[g], 2);
-    sB[g] += __shfl_xor_sync(kFull, sB[g], 2);
-  }
-  mA = fmaxf(mA, __shfl_xor_sync(kFull, mA, 1));
-  mB = fmaxf(mB, __shfl_xor_sync(kFull, mB, 1));
-  mA = fmaxf(mA, __shfl_xor_sync(kFull, mA, 2));
-  mB = fmaxf(mB, __shfl_xor_sync(kFull, mB, 2));
   const float inf = __int_as_float(0x7f800000);
+#pragma unroll 1
+  for (int g0 = 0; g0 < G; g0 += 4) {
+    float4 q4[4];
 #pragma unroll
-  for (int g = 0; g < GM; ++g) {
-    if (g < G && (g & 3) == p) {
-      const float qn = qn1[mh * G + g];
-      float2* out = a.bounds + static_cast<long long>(mh * G + g) * a.n + b0;
-      if (liveA) {
-        const float e = __fadd_ru(__fmul_ru(__fmul_ru(qn, mA), kErrFactor), 0x1p-118f);
-        float2 iv = make_float2(__fsub_rd(sA[g], e), __fadd_ru(sA[g], e));
-        if (!(iv.x <= iv.y)) iv = make_float2(-inf, inf);
-        out[bA] = iv;
+    for (int g = 0; g < 4; ++g)
+      q4[g] = (g0 + g < G) ? *reinterpret_cast<const float4*>(qs + (mh * G + g0 + g) * D + 4 * lane)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+    for (int bq = 0; bq < kMetaItemBlocks && bq < nb; bq += 4) {
+      float part[16];
+      float mx[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int b = bq + j;
+        float4 l4 = make_float4(0.f, 0.f, 0.f, 0.f), h4 = l4;
+        if (b < nb) {
+          l4 = *reinterpret_cast<const float4*>(slo + b * D + 4 * lane);
+          h4 = *reinterpret_cast<const float4*>(shi + b * D + 4 * lane);
+        }
+        mx[j] = fmaxf(fmaxf(fmaxf(fabsf(l4.x), fabsf(h4.x)), fmaxf(fabsf(l4.y), fabsf(h4.y))),
+                      fmaxf(fmaxf(fabsf(l4.z), fabsf(h4.z)), fmaxf(fabsf(l4.w), fabsf(h4.w))));
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          float acc = q4[g].x * (q4[g].x >= 0.f ? h4.x : l4.x);
+          acc = fmaf(q4[g].y, q4[g].y >= 0.f ? h4.y : l4.y, acc);
+          acc = fmaf(q4[g].z, q4[g].z >= 0.f ? h4.z : l4.z, acc);
+          acc = fmaf(q4[g].w, q4[g].w >= 0.f ? h4.w : l4.w, acc);
+          part[4 * j + g] = acc;
+        }
       }
-      if (liveB) {
-        const float e = __fadd_ru(__fmul_ru(__fmul_ru(qn, mB), kErrFactor), 0x1p-118f);
-        float2 iv = make_float2(__fsub_rd(sB[g], e), __fadd_ru(sB[g], e));
+      // Sums: transposed over lane bits 3..0, then the two lane halves.
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < off; ++i) {
+          const float send = upper ? part[i] : part[i + off];
+          const float keep = upper ? part[i + off] : part[i];
+          part[i] = keep + __shfl_xor_sync(kFull, send, off);
+        }
+      }
+      const float sum = part[0] + __shfl_xor_sync(kFull, part[0], 16);
+      // Block maxima: transposed over lane bits 3, 2, then the rest.
+#pragma unroll
+      for (int off = 8, cnt = 2; off >= 4; off >>= 1, cnt >>= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < cnt; ++i) {
+          const float send = upper ? mx[i] : mx[i + cnt];
+          const float keep = upper ? mx[i + cnt] : mx[i];
+          mx[i] = fmaxf(keep, __shfl_xor_sync(kFull, send, off));
+        }
+      }
+      float bm = mx[0];
+      bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 16));
+      bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 2));
+      bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 1));
+      const int j = (lane >> 2) & 3, g = lane & 3, b = bq + j, head = g0 + g;
+      if (lane < 16 && b < nb && head < G) {
+        const float e = __fadd_ru(__fmul_ru(__fmul_ru(qn1[mh * G + head], bm), kErrFactor), 0x1p-118f);
+        float2 iv = make_float2(__fsub_rd(sum, e), __fadd_ru(sum, e));
         if (!(iv.x <= iv.y)) iv = make_float2(-inf, inf);
-        out[bB] = iv;
+        a.bounds[static_cast<long long>(mh * G + head) * a.n + b0 + b] = iv;
       }
     }
   }
 }
+
+// Shared-memory counter add with release semantics at CTA scope: the warp's
+// global writes before it (ordered by __syncwarp) are visible to a thread of
+// the CTA that reads the counter with ld_acquire_cta.
+__device__ __forceinline__ void red_release_cta(unsigned* p, unsigned v) {
+  asm volatile("red.release.cta.shared::cta.add.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_cta(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+
+constexpr int kStepPublisher = kStepHelper0;  // warp 12 forwards the CTA's completions GPU-wide
+constexpr int kStepMaxHeads = 32;             // hq (and so hkv) limit: hq * D <= 4096
 
 template <typename T, int E, int GM>
 __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a) {
@@ -223,15 +294,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
   constexpr int DPH = kStepDPH;
   constexpr int NS = kStepStages;
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ uint64_t full_bar[NS], empty_bar[NS];
-  __shared__ int item_ok[NS];
+  __shared__ uint64_t full_bar[NS], empty_bar[NS], q_bar;
+  __shared__ int s_desc[NS], item_ok[NS];
   __shared__ volatile int s_abort;
-  __shared__ int s_sel[kStepMaxList], s_pid[kStepMaxList], s_miss[kStepMaxList], s_hit[kStepMaxList];
-  __shared__ int s_nmiss, s_nhit;
+  __shared__ int s_sel[kStepMaxList], s_pid[kStepMaxList], s_loc[kStepMaxList], s_glb[kStepMaxList];
+  __shared__ int s_nloc, s_nglb;
   __shared__ unsigned s_pmask[kStepMaxBlocks / 32], s_amask[kStepMaxBlocks / 32];
+  __shared__ unsigned s_head_cnt[kStepMaxHeads], s_row_cnt[kStepMaxHeads];
   __shared__ float s_wm[kStepWarps], s_wl[kStepWarps];
   __shared__ __align__(16) float s_wu[kStepWarps][D];
-  __shared__ uint64_t fold_bar;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int hq = a.hq, hkv = a.hkv, n = a.n, K = a.topk;
@@ -242,16 +313,19 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
   const int row = row_cta ? static_cast<int>(blockIdx.x) - W : -1;
   const bool serial = a.sp == 0;
   const int S = serial ? K : a.sp;
+  // Serial step: row r's CTA reduces the first xl of its selected blocks
+  // itself; the other K - xl go to the work CTAs through the states buffer.
+  const int xl = serial ? min(K, (hq * K * STK_STEP_LOCAL_SHARE4 + 4 * grid - 1) / (4 * grid)) : 0;
+  const int SJ = S - xl;  // per-row block states computed by work CTAs
   const int ipH = (n + kMetaItemBlocks - 1) / kMetaItemBlocks;  // metadata items per KV head
   const int n_meta = hkv * ipH;
   // Every CTA c scores metadata items c, c + grid, ...; work CTA c then takes
-  // jobs [j0, j1) of the hq * S (row, slot) block states.
+  // jobs [j0, j1) of the hq * SJ (row, slot) block states.
   const int my_meta = static_cast<int>(blockIdx.x) < n_meta ? (n_meta - 1 - static_cast<int>(blockIdx.x)) / grid + 1 : 0;
-  const long long J = static_cast<long long>(hq) * S;
+  const long long J = static_cast<long long>(hq) * SJ;
   const int j0 = row_cta ? 0 : static_cast<int>(J * blockIdx.x / W);
   const int j1 = row_cta ? 0 : static_cast<int>(J * (blockIdx.x + 1) / W);
   const int my_jobs = j1 - j0;
-  const int n_items = my_meta + my_jobs;
   unsigned* head_done = a.ctrl;
   unsigned* row_states = a.ctrl + hkv;
   unsigned* row_ready = a.ctrl + hkv + hq;
@@ -264,27 +338,38 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
   const T* Vp = static_cast<const T*>(a.v);
   constexpr unsigned kBlockBytes = kStepB * D * sizeof(T);
 
-  // ---------------------------------------------------------------- set-up
-  if (tid == 0) SPT(0);
-  if (tid == 0) {
-    for (int i = 0; i < NS; ++i) {
-      mbar_init(&full_bar[i], 1);
-      mbar_init(&empty_bar[i], 1);
-    }
-    mbar_init(&fold_bar, 1);
-    fence_barrier_init();
-    s_abort = 0;
-  }
-  __syncthreads();
+  auto meta_item = [&](int it, int& mh, int& b0) {
+    const int m = static_cast<int>(blockIdx.x) + it * grid;
+    mh = m / ipH;
+    b0 = (m % ipH) * kMetaItemBlocks;
+  };
+  // Block ID of this CTA's job jl (slot xl + ... of its row): the predicted
+  // list (speculative step) or the published selection (serial step).
+  auto job_id = [&](int jl) -> long long {
+    if (jl < 0 || jl >= my_jobs) return -1;
+    const int jj = j0 + jl, r = jj / SJ;
+    const long long o = static_cast<long long>(r) * (serial ? K : S) + xl + (jj - r * SJ);
+    return serial ? static_cast<long long>(__ldcg(a.selected + o)) : load_id(a.pred, a.pred64, o);
+  };
 
-  // Issues item `it` into stage it % NS once the consumer of item it - NS has
-  // released it. An item it cannot fill (a bad ID, or after an abort) is
-  // completed without a copy and flagged, so that its consumer skips it.
-  auto produce = [&](int it, int kind, int mh, long long first, long long id) {
-    const int st = it % NS;
-    if (it >= NS && !mbar_wait(&empty_bar[st], ((it / NS) - 1) & 1u, a.status)) s_abort = 1;
+  // ---------------------------------------------------------------- producer (warp 11)
+  // Lane c < NS of the producer warp serves stage c. Each pass, every lane
+  // whose stage has been released takes the next unissued item, so one pass
+  // issues into all free stages at once and a slow item holds only its own
+  // stage. An item that cannot be filled (bad ID, abort) is completed
+  // without a copy and flagged, so that its consumer skips it.
+  unsigned my_uses = 0;  // producer lane c < NS: items issued into stage c
+  int npass = 0;         // profiling builds: passes that issued
+  auto lane_free = [&]() {
+    return lane < NS && (my_uses == 0 || mbar_test_wait(&empty_bar[lane], (my_uses - 1u) & 1u));
+  };
+  // kind 0 = metadata rows [first, first + 16) of KV head mh, 1 = K and V of
+  // block id of KV head mh, 2 = end (no copy).
+  auto fill_lane = [&](int code, int kind, int mh, long long first, long long id) {
+    const int st = lane;
     unsigned char* stage = pool + static_cast<size_t>(st) * kStageBytes;
-    if (kind == 0) {  // metadata: rows [first, first + nb) of KV head mh
+    s_desc[st] = code;
+    if (kind == 0) {
       const int nb = min(kMetaItemBlocks, n - static_cast<int>(first));
       const unsigned bytes = static_cast<unsigned>(nb) * D * 4;
       const long long off = (static_cast<long long>(mh) * n + first) * D;
@@ -292,169 +377,201 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
       mbar_arrive_expect_tx(&full_bar[st], 2 * bytes);
       bulk_g2s(stage, a.lo + off, bytes, &full_bar[st]);
       bulk_g2s(stage + kStageBytes / 2, a.hi + off, bytes, &full_bar[st]);
-    } else if (id >= 0 && id < n && !s_abort) {  // one block of KV head mh
+    } else if (kind == 1 && id >= 0 && id < n && !s_abort) {
       const long long off = (static_cast<long long>(mh) * n + id) * kStepB * D;
       item_ok[st] = 1;
       mbar_arrive_expect_tx(&full_bar[st], 2 * kBlockBytes);
       bulk_g2s(stage, Kp + off, kBlockBytes, &full_bar[st]);
       bulk_g2s(stage + kBlockBytes, Vp + off, kBlockBytes, &full_bar[st]);
     } else {
-      if (id >= n) report(a.status, kStatusBadBlockId);
+      if (kind == 1 && id >= n) report(a.status, kStatusBadBlockId);
       item_ok[st] = 0;
       mbar_arrive(&full_bar[st]);
     }
+    ++my_uses;
   };
-  auto meta_item = [&](int it, int& mh, int& b0) {
-    const int m = static_cast<int>(blockIdx.x) + it * grid;
-    mh = m / ipH;
-    b0 = (m % ipH) * kMetaItemBlocks;
-  };
-
-  // The small loads are issued first and consumed after the bulk copies are
-  // queued: q (16 bytes per thread), the predicted IDs of this CTA's first
-  // jobs (producer lanes) or of its row (row CTA).
-  const int qvals = hq * D;
-  const int qper = a.q_dtype == kF32 ? 4 : 8;  // values per 16-byte load
-  float qv[2][8];
-#pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    const int i = (c * kStepThreads + tid) * qper;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) qv[c][e] = 0.f;
-    if (i < qvals) {
-      const uint4 x = __ldg(reinterpret_cast<const uint4*>(static_cast<const unsigned char*>(a.q) +
-                                                           static_cast<long long>(i) * (a.q_dtype == kF32 ? 4 : 2)));
-      if (a.q_dtype == kF32) {
-        qv[c][0] = __uint_as_float(x.x); qv[c][1] = __uint_as_float(x.y);
-        qv[c][2] = __uint_as_float(x.z); qv[c][3] = __uint_as_float(x.w);
-      } else {
-        const unsigned w4[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          if (a.q_dtype == kBF16) {
-            qv[c][2 * e] = __uint_as_float(w4[e] << 16);
-            qv[c][2 * e + 1] = __uint_as_float(w4[e] & 0xffff0000u);
-          } else {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[e]));
-            qv[c][2 * e] = f.x;
-            qv[c][2 * e + 1] = f.y;
-          }
+  // Issue items [0, count): prepare(next) runs on every lane before a pass;
+  // item_of(i, ...) runs on every lane (i < 0: none) and describes item i.
+  auto produce = [&](int count, auto&& prepare, auto&& item_of) {
+    int next = 0;
+    unsigned long long t0 = 0;
+    bool waiting = false;
+    while (next < count && !s_abort) {
+      const bool fr = lane_free();
+      const unsigned fm = __ballot_sync(kFull, fr);
+      if (fm == 0) {
+        if (!waiting) {
+          t0 = global_ns();
+          waiting = true;
+        } else if (global_ns() - t0 > c_wait_ns) {
+          if (lane == 0) report(a.status, kStatusWaitTimeout);
+          s_abort = 1;
         }
+        continue;
       }
-    }
-  }
-  long long lid = -1;  // producer lane: predicted ID of job j0 + jb + lane
-  int jb = 0;
-  if (warp == kStepProducer && !serial && lane < my_jobs) lid = load_id(a.pred, a.pred64, j0 + lane);
-  if (row_cta && !serial)
-    for (int i = tid; i < a.sp; i += kStepThreads)
-      s_pid[i] = static_cast<int>(load_id(a.pred, a.pred64, static_cast<long long>(row) * a.sp + i));
-  // Metadata items into the free stages at once, one producer lane each.
-  const int n_first = min(my_meta, NS);
-  if (warp == kStepProducer && lane < n_first) {
-    int mh, b0;
-    meta_item(lane, mh, b0);
-    produce(lane, 0, mh, b0, 0);
-  }
-  if (tid == 0) SPT(2);
-#pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    const int i = (c * kStepThreads + tid) * qper;
-    if (i < qvals)
-      for (int e = 0; e < qper; ++e) qs[i + e] = qv[c][e];
-  }
-  __syncthreads();
-  for (int t = warp; t < hq; t += kStepWarps) {
-    float sum = 0.f;
-    for (int dd = lane; dd < D; dd += 32) sum = __fadd_ru(sum, fabsf(qs[t * D + dd]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum = __fadd_ru(sum, __shfl_xor_sync(kFull, sum, o));
-    if (lane == 0) qn1[t] = sum;
-  }
-  __syncthreads();
-  if (tid == 0) SPT(1);
-
-  // ---------------------------------------------------------------- ring: metadata, then block states
-  if (warp == kStepProducer) {
-    int ready_row = -1;  // serial: rows whose selection this warp has seen published
-    long long sid = -1;  // serial: selected ID of job sb + lane
-    int sb = -1;
-    for (int it = n_first; it < n_items; ++it) {
-      if (it < my_meta) {
-        if (lane == 0) {
-          int mh, b0;
-          meta_item(it, mh, b0);
-          produce(it, 0, mh, b0, 0);
-        }
-      } else {
-        const int jl = it - my_meta;  // this CTA's job index
-        const int job = j0 + jl;
-        const int r = job / S;
-        long long id = -1;
-        if (!serial) {
-          if (jl - jb == 32) {
-            jb += 32;
-            lid = jb + lane < my_jobs ? load_id(a.pred, a.pred64, j0 + jb + lane) : -1;
-          }
-          id = __shfl_sync(kFull, lid, jl - jb);
-        } else {
-          if (r > ready_row) {
-            if (lane == 0 && !s_abort && !wait_count(&row_ready[r], 1)) {
-              report(a.status, kStatusWaitTimeout);
-              s_abort = 1;
-            }
-            __syncwarp();
-            ready_row = r;
-            sb = -1;
-          }
-          if (sb < 0 || job - sb >= 32) {
-            // The selected IDs of the next 32 jobs of row r (job = r * K + slot).
-            sb = job;
-            const int jj = job + lane;
-            sid = (!s_abort && jj < j1 && jj / S == r) ? __ldcg(a.selected + jj) : -1;
-          }
-          id = __shfl_sync(kFull, sid, job - sb);
-        }
-        if (lane == 0) produce(it, 1, r / G, 0, id);
+      waiting = false;
+      prepare(next);
+      const int rank = __popc(fm & ((1u << lane) - 1u));
+      const int take = min(__popc(fm), count - next);
+      const bool mine = fr && rank < take;
+      int code = kItemEnd, kind = 2, mh = 0;
+      long long first = 0, id = -1;
+      item_of(mine ? next + rank : -1, code, kind, mh, first, id);
+      if (mine) fill_lane(code, kind, mh, first, id);
+      if (lane == 0 && npass < 32) {
+        SPT_RAW(64 + npass, global_ns());
+        SPT_RAW(96 + npass, static_cast<unsigned long long>(take) | (static_cast<unsigned long long>(next) << 16));
       }
-      if (lane == 0 && it == my_meta) SPT(3);
-      if (lane == 0 && it == NS) SPT(30);
-      if (lane == 0 && it == 2 * NS) SPT(31);
+      ++npass;
+      next += take;
       __syncwarp();
     }
-    if (lane == 0) SPT(4);
-  } else if (warp < NS) {
-    // Consumers: item it belongs to warp it % NS (one consumer per stage).
-    // Block-state completions are published per row in batches (one fence
-    // per row change and one at the end), metadata items one by one: the
-    // selections wait on them.
-    int pend_row = -1, pend = 0;
-    if (lane == 0 && warp == 0) SPT(12);
-    for (int it = warp; it < n_items; it += NS) {
-      const int st = it % NS;
-      const bool landed = mbar_wait(&full_bar[st], (it / NS) & 1u, a.status);
-      if (lane == 0 && it == 0) SPT(13);
-      if (lane == 0 && warp == 0 && it / NS < 3) SPT(24 + it / NS);
-      if (!landed) s_abort = 1;
-      const bool ok = landed && item_ok[st] != 0;
-      const unsigned char* stage = pool + static_cast<size_t>(st) * kStageBytes;
-      if (it < my_meta) {
+  };
+  auto produce_ends = [&]() {
+    bool ended = lane >= NS;
+    unsigned long long t0 = global_ns();
+    while (!__all_sync(kFull, ended) && !s_abort) {
+      if (!ended && lane_free()) {
+        fill_lane(kItemEnd, 2, 0, 0, 0);
+        ended = true;
+      }
+      if (global_ns() - t0 > c_wait_ns) {
+        if (lane == 0) report(a.status, kStatusWaitTimeout);
+        s_abort = 1;
+      }
+    }
+  };
+
+  // ---------------------------------------------------------------- set-up
+#ifdef STK_TRACE
+  const unsigned long long t_start = global_ns();
+  if (warp == kStepProducer)
+    for (int i = lane; i < 128; i += 32) s_trc[i] = 0ull;
+#endif
+  SPAN_START();
+  const int n_first = min(my_meta, NS);
+  // q arrives by one bulk copy queued ahead of the metadata (a load queued
+  // behind this SM's bulk copies would wait for all of them): FP32 q straight
+  // into qs, 16-bit q into s_wu (free until the row's final merge) and then
+  // widened.
+  const int qbytes = hq * D * (a.q_dtype == kF32 ? 4 : 2);
+  void* q_dst = a.q_dtype == kF32 ? static_cast<void*>(qs) : static_cast<void*>(&s_wu[0][0]);
+  long long lid_a = -1, lid_b = -1;  // producer lane: IDs of jobs jb + lane and jb + 32 + lane
+  int jb = 0;
+  if (warp == kStepProducer) {
+    if (!serial) {
+      lid_a = job_id(lane);
+      lid_b = job_id(32 + lane);
+    }
+    // Barriers and counters, q, then the first metadata items at once (one
+    // lane each), before anything else of the CTA.
+    if (lane == 0) {
+      for (int i = 0; i < NS; ++i) {
+        mbar_init(&full_bar[i], 1);
+        mbar_init(&empty_bar[i], 1);
+      }
+      mbar_init(&q_bar, 1);
+      fence_barrier_init();
+      s_abort = 0;
+      mbar_arrive_expect_tx(&q_bar, static_cast<unsigned>(qbytes));
+      bulk_g2s(q_dst, a.q, static_cast<unsigned>(qbytes), &q_bar);
+    }
+    s_head_cnt[lane] = 0u;
+    s_row_cnt[lane] = 0u;
+    __syncwarp();
+    barriers_ready_arrive();
+    if (lane < n_first) {
+      int mh, b0;
+      meta_item(lane, mh, b0);
+      fill_lane(lane, 0, mh, b0, 0);
+    }
+    __syncwarp();
+    if (lane == 0) SPT(2);
+  } else {
+    // q as FP32 in shared memory and its per-head ||q||_1 rounded up; the
+    // producer does not take part.
+    const int t = tid < kStepProducer * 32 ? tid : tid - 32;
+    if (row_cta && !serial)
+      for (int i = t; i < a.sp; i += kStepThreads - 32)
+        s_pid[i] = static_cast<int>(load_id(a.pred, a.pred64, static_cast<long long>(row) * a.sp + i));
+    barriers_ready_wait();
+#ifdef STK_TRACE
+    if (tid == 0) s_trc[0] = t_start;
+#endif
+    if (!mbar_wait(&q_bar, 0, a.status)) s_abort = 1;
+    if (a.q_dtype != kF32) {
+      const unsigned* raw = reinterpret_cast<const unsigned*>(&s_wu[0][0]);
+      sync_non_producer();
+      for (int i = t; i < hq * D / 2; i += kStepThreads - 32) {
+        const unsigned w = raw[i];
+        float lo, hi;
+        if (a.q_dtype == kBF16) {
+          lo = __uint_as_float(w << 16);
+          hi = __uint_as_float(w & 0xffff0000u);
+        } else {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+          lo = f.x;
+          hi = f.y;
+        }
+        qs[2 * i] = lo;
+        qs[2 * i + 1] = hi;
+      }
+    }
+    sync_non_producer();
+    const int wv = warp < kStepProducer ? warp : warp - 1;
+    for (int h = wv; h < hq; h += kStepWarps - 1) {
+      float sum = 0.f;
+      for (int dd = lane; dd < D; dd += 32) sum = __fadd_ru(sum, fabsf(qs[h * D + dd]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum = __fadd_ru(sum, __shfl_xor_sync(kFull, sum, o));
+      if (lane == 0) qn1[h] = sum;
+    }
+    sync_non_producer();
+    if (tid == 0) SPT(1);
+  }
+
+  // ---------------------------------------------------------------- the ring
+  // Consumer warp c (c < NS) owns stage c: it takes the stage's items one
+  // phase after another until an end descriptor. A scored metadata item
+  // counts for its KV head, a job's block state (written to the states
+  // buffer) for its row, in shared-memory counters that the publisher warp
+  // forwards to the control block; row-local blocks (misses, or the serial
+  // row's own share) fold into the warp's running state (wm, wl, wu).
+  unsigned kph = 0;  // phases this consumer has taken from its stage
+  auto consume = [&](auto local_tag, const float* qrow_local, float& wm, float& wl, float (&wu)[DPH]) {
+    constexpr bool kLocal = decltype(local_tag)::value;
+    const int st = warp;
+    const unsigned char* stage = pool + static_cast<size_t>(st) * kStageBytes;
+    while (true) {
+      const bool landed = mbar_wait(&full_bar[st], kph & 1u, a.status);
+      if (!landed) {
+        s_abort = 1;
+        break;
+      }
+      if (lane == 0 && warp == 0 && kph < 16) SPT(32 + 2 * kph);
+      ++kph;
+      const int code = s_desc[st];
+      const bool ok = item_ok[st] != 0;
+      if (code == kItemEnd) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[st]);
+        break;
+      }
+      if (code < my_meta) {
         int mh, b0;
-        meta_item(it, mh, b0);
+        meta_item(code, mh, b0);
         if (ok)
           score_item<GM>(a, reinterpret_cast<const float*>(stage),
                          reinterpret_cast<const float*>(stage + kStageBytes / 2), qs, qn1, mh, b0,
                          min(kMetaItemBlocks, n - b0), G, lane);
         __syncwarp();
-        if (lane == 0 && warp == 0 && it == 0) SPT(22);
         if (lane == 0) {
           mbar_arrive(&empty_bar[st]);
-          publish(&head_done[mh]);
+          red_release_cta(&s_head_cnt[mh], 1u);
         }
-      } else {
-        // One block's softmax state for (row r, slot).
-        const int job = j0 + (it - my_meta);
-        const int r = job / S, slot = job - r * S;
+      } else if (code < kItemLocal) {
+        const int job = j0 + (code - my_meta);
+        const int r = job / SJ, slot = xl + (job - r * SJ);
         float m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
 #pragma unroll
         for (int j = 0; j < DPH; ++j) { u[j] = 0.f; ua[j] = 0.f; }
@@ -475,24 +592,111 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
         }
         if (lane < 16) store_vec<DPH>(a.su + o * D + lane * DPH, u);
         __syncwarp();
-        if (lane == 0 && warp == 0 && it == NS) SPT(23);
-        if (lane == 0) {
-          if (r != pend_row && pend > 0) {
-            __threadfence();
-            atomicAdd(&row_states[pend_row], static_cast<unsigned>(pend));
-            pend = 0;
-          }
-          pend_row = r;
-          ++pend;
+        if (lane == 0) red_release_cta(&s_row_cnt[r], 1u);
+      } else if constexpr (kLocal) {
+        if (ok) {
+          float qf[DPH], m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
+#pragma unroll
+          for (int j = 0; j < DPH; ++j) { qf[j] = qrow_local[(lane & 15) * DPH + j]; u[j] = 0.f; ua[j] = 0.f; }
+          const T* ks = reinterpret_cast<const T*>(stage);
+          warp_block_state<T, DPH, kModeFull, true>(ks, ks + kStepB * D, kStepB, qf, a.scale, 0.f, m, l, u, ua,
+                                                    lane);
+          fold_state(wm, wl, wu, m, l, u);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[st]);
+        if (lane == 0 && warp == 0) SPT(15);
+      }
+      if (lane == 0 && warp == 0 && kph <= 16) SPT(33 + 2 * (kph - 1));
+    }
+  };
+
+  if (warp == kStepProducer) {
+    // First phase: the remaining metadata items, the CTA's jobs, then one
+    // end descriptor per stage.
+    produce(my_meta - n_first, [&](int) {},
+            [&](int i, int& code, int& kind, int& mh, long long& first, long long&) {
+              if (i < 0) return;
+              int b0;
+              code = n_first + i;
+              kind = 0;
+              meta_item(code, mh, b0);
+              first = b0;
+            });
+    if (my_jobs > 0) {
+      if (serial) {
+        // The rows of [j0, j1) must have published their selections.
+        if (lane == 0)
+          for (int r = j0 / SJ; r <= (j1 - 1) / SJ && !s_abort; ++r)
+            if (!wait_count(&row_ready[r], 1)) {
+              report(a.status, kStatusWaitTimeout);
+              s_abort = 1;
+            }
+        __syncwarp();
+        if (!s_abort) {
+          lid_a = job_id(lane);
+          lid_b = job_id(32 + lane);
         }
       }
-      if (lane == 0 && warp == 0 && it / NS < 3) SPT(27 + it / NS);
+      if (lane == 0) SPT(3);
+      produce(my_jobs,
+              [&](int next) {
+                if (next >= jb + 32) {  // slide the ID window
+                  jb += 32;
+                  lid_a = lid_b;
+                  lid_b = job_id(jb + 32 + lane);
+                }
+              },
+              [&](int i, int& code, int& kind, int& mh, long long&, long long& id) {
+                const int off = i < 0 ? 0 : i - jb;
+                const long long va = __shfl_sync(kFull, lid_a, off & 31);
+                long long vb = -1;  // read only when needed: it may still be loading
+                if (__any_sync(kFull, off >= 32)) vb = __shfl_sync(kFull, lid_b, off & 31);
+                if (i < 0) return;
+                code = my_meta + i;
+                kind = 1;
+                mh = ((j0 + i) / SJ) / G;
+                id = off < 32 ? va : vb;
+              });
     }
-    if (lane == 0 && pend > 0) {
-      __threadfence();
-      atomicAdd(&row_states[pend_row], static_cast<unsigned>(pend));
-    }
+    produce_ends();
+    if (lane == 0) SPT(4);
+  } else if (warp < NS) {
+    if (lane == 0 && warp == 0) SPT(12);
+    float dm = 0.f, dl = 0.f, du[DPH];
+    consume(std::false_type{}, nullptr, dm, dl, du);
     if (lane == 0 && warp == 0) SPT(14);
+  } else if (warp == kStepPublisher) {
+    // Forward the CTA's completions GPU-wide: one fence per batch (a GPU-
+    // scope fence waits behind this SM's bulk copies, so it is kept off the
+    // consumers). Lane h < hkv: KV head h's scored metadata items; lane r <
+    // hq: row r's block states.
+    unsigned pub_h = 0, pub_r = 0;
+    const unsigned want = static_cast<unsigned>(my_meta + my_jobs);
+    unsigned long long t0 = global_ns();
+    while (true) {
+      const unsigned ch = lane < hkv ? ld_acquire_cta(&s_head_cnt[lane]) : 0u;
+      const unsigned cr = lane < hq ? ld_acquire_cta(&s_row_cnt[lane]) : 0u;
+      const bool fresh = ch != pub_h || cr != pub_r;
+      if (__any_sync(kFull, fresh)) {
+        if (fresh) {
+          __threadfence();
+          if (ch != pub_h) atomicAdd(&head_done[lane], ch - pub_h);
+          if (cr != pub_r) atomicAdd(&row_states[lane], cr - pub_r);
+        }
+        pub_h = ch;
+        pub_r = cr;
+        t0 = global_ns();
+      }
+      if (static_cast<unsigned>(warp_sum_int(static_cast<int>(pub_h + pub_r))) >= want || s_abort) break;
+      if (global_ns() - t0 > c_wait_ns) {
+        if (lane == 0) report(a.status, kStatusWaitTimeout);
+        s_abort = 1;
+        break;
+      }
+      __nanosleep(64);
+    }
+    if (lane == 0) SPT(13);
   }
 
   // ---------------------------------------------------------------- row CTAs
@@ -514,11 +718,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
       sa.bounds = a.bounds; sa.q = a.q; sa.q_dtype = a.q_dtype; sa.lo = a.lo; sa.hi = a.hi;
       sa.hq = hq; sa.hmeta = hkv; sa.d = D; sa.group_select = 0;
       bounded_select_core<E, kStepThreads>(sa, row, qrow, true);
-#ifdef STK_TOPK_TWICE
-      __syncthreads();
-      if (tid == 0) SPT(21);
-      bounded_select_core<E, kStepThreads>(sa, row, qrow, true);
-#endif
     }
     __syncthreads();
     if (tid == 0) SPT(7);
@@ -526,14 +725,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
     if (serial && tid == 0 && !s_abort) publish(&row_ready[row]);
     __syncthreads();
 
-    float wm = neg_inf(), wl = 0.f, wu[DPH];
-#pragma unroll
-    for (int j = 0; j < DPH; ++j) wu[j] = 0.f;
-    int n_fold = K;  // retained states to fold
-    const int* fold_slot = nullptr;
+    // Row-local blocks: the misses (A not in P) of the saved repair, or the
+    // serial row's first xl selected blocks; the block states to fold from
+    // the states buffer: the hits (P slots in A), or the serial row's other
+    // K - xl slots.
     if (!serial) {
-      // Saved repair: misses (A not in P) computed here, hits (P slots in A)
-      // taken from the block states the work CTAs wrote.
       for (int i = tid; i < (n + 31) / 32; i += kStepThreads) { s_pmask[i] = 0u; s_amask[i] = 0u; }
       __syncthreads();
       for (int i = tid; i < a.sp; i += kStepThreads) {
@@ -551,7 +747,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
           const int id = b + lane < K ? s_sel[b + lane] : -1;
           const bool miss = id >= 0 && !((s_pmask[id >> 5] >> (id & 31)) & 1u);
           const unsigned bal = __ballot_sync(kFull, miss);
-          if (miss) s_miss[nm + __popc(bal & ((1u << lane) - 1u))] = id;
+          if (miss) s_loc[nm + __popc(bal & ((1u << lane) - 1u))] = id;
           nm += __popc(bal);
         }
         int nh = 0;
@@ -559,84 +755,77 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
           const int id = b + lane < a.sp ? s_pid[b + lane] : -1;
           const bool hit = id >= 0 && id < n && ((s_amask[id >> 5] >> (id & 31)) & 1u);
           const unsigned bal = __ballot_sync(kFull, hit);
-          if (hit) s_hit[nh + __popc(bal & ((1u << lane) - 1u))] = b + lane;
+          if (hit) s_glb[nh + __popc(bal & ((1u << lane) - 1u))] = b + lane;
           nh += __popc(bal);
         }
-        if (lane == 0) { s_nmiss = nm; s_nhit = nh; }
+        if (lane == 0) { s_nloc = nm; s_nglb = nh; }
       }
-      __syncthreads();
-      const int nmiss = s_abort ? 0 : s_nmiss;
-      // Misses through the ring, continuing after this CTA's metadata items.
-      if (warp == kStepProducer) {
-        for (int i = 0; i < nmiss; ++i) {
-          if (lane == 0) produce(n_items + i, 1, mh, 0, s_miss[i]);
-          __syncwarp();
-        }
-      } else if (warp < NS) {
-        // Item n_items + i belongs to warp (n_items + i) % NS, like every item of the ring.
-        for (int i = (warp - n_items % NS + NS) % NS; i < nmiss; i += NS) {
-          const int it = n_items + i;
-          const int st = it % NS;
-          const bool landed = mbar_wait(&full_bar[st], (it / NS) & 1u, a.status);
-          if (lane == 0 && i < NS) SPT(15);
-          if (!landed) s_abort = 1;
-          if (landed && item_ok[st]) {
-            float qf[DPH], m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
-#pragma unroll
-            for (int j = 0; j < DPH; ++j) { qf[j] = qrow[(lane & 15) * DPH + j]; u[j] = 0.f; ua[j] = 0.f; }
-            const T* ks = reinterpret_cast<const T*>(pool + static_cast<size_t>(st) * kStageBytes);
-            warp_block_state<T, DPH, kModeFull, true>(ks, ks + kStepB * D, kStepB, qf, a.scale, 0.f, m, l, u, ua,
-                                                      lane);
-            fold_state(wm, wl, wu, m, l, u);
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty_bar[st]);
-        }
+    } else {
+      for (int i = tid; i < K; i += kStepThreads) {
+        if (i < xl) s_loc[i] = s_sel[i];
+        else s_glb[i - xl] = i;
       }
-      n_fold = s_nhit;
-      fold_slot = s_hit;
+      if (tid == 0) { s_nloc = xl; s_nglb = K - xl; }
     }
-    if (tid == 0) SPT(8);
-    // The row's S block states are complete: bring their numerators into
-    // shared memory with one bulk copy (S x D FP32, once the ring's stages
-    // are drained), and their (m, l) with plain loads through L2.
     __syncthreads();
-    float* st_u = reinterpret_cast<float*>(pool);
-    float* st_m = reinterpret_cast<float*>(pool + static_cast<size_t>(S) * D * 4);
-    float* st_l = st_m + S;
-    if (tid == 0) {
-      if (!s_abort && !wait_count(&row_states[row], static_cast<unsigned>(S))) {
+    const int nloc = s_abort ? 0 : s_nloc;
+    const int nglb = s_abort ? 0 : s_nglb;
+    float wm = neg_inf(), wl = 0.f, wu[DPH];
+#pragma unroll
+    for (int j = 0; j < DPH; ++j) wu[j] = 0.f;
+    if (warp == kStepProducer) {
+      produce(nloc, [&](int) {},
+              [&](int i, int& code, int& kind, int& mh_, long long&, long long& id) {
+                if (i < 0) return;
+                code = kItemLocal + i;
+                kind = 1;
+                mh_ = mh;
+                id = s_loc[i];
+              });
+      produce_ends();
+      if (lane == 0) SPT(8);
+    } else if (warp < NS) {
+      consume(std::true_type{}, qrow, wm, wl, wu);
+      if (lane == 0 && warp == 0) SPT(24);
+    }
+    if (warp >= kStepProducer) {
+      // Warps 11..15: the states from the buffer, once every work CTA has
+      // written this row's (with plain loads through L2; a warp folds four
+      // states per round trip).
+      const int fw = warp - kStepProducer, nfw = kStepWarps - kStepProducer;
+      if (lane == 0 && nglb > 0 && !s_abort && !wait_count(&row_states[row], static_cast<unsigned>(SJ))) {
         report(a.status, kStatusWaitTimeout);
         s_abort = 1;
       }
-      SPT(9);
+      __syncwarp();
+      if (tid == kStepProducer * 32) SPT(9);
       if (!s_abort) {
-        // The numerators were written by other CTAs (generic proxy) and are
-        // read here by the bulk-copy (async) proxy.
-        asm volatile("fence.proxy.async.global;" ::: "memory");
-        const unsigned bytes = static_cast<unsigned>(S) * D * 4;
-        mbar_arrive_expect_tx(&fold_bar, bytes);
-        bulk_g2s(st_u, a.su + static_cast<long long>(row) * S * D, bytes, &fold_bar);
-      }
-    }
-    __syncthreads();
-    if (!s_abort) {
-      for (int i = tid; i < S; i += kStepThreads) {
-        st_m[i] = __ldcg(a.sm + static_cast<long long>(row) * S + i);
-        st_l[i] = __ldcg(a.sl + static_cast<long long>(row) * S + i);
-      }
-    }
-    const bool have_u = !s_abort && mbar_wait(&fold_bar, 0, a.status);
-    if (!have_u) s_abort = 1;
-    __syncthreads();
-    if (!s_abort) {
-      for (int i = warp; i < n_fold; i += kStepWarps) {
-        const int slot = fold_slot ? fold_slot[i] : i;
-        float u[DPH];
+        const long long rb = static_cast<long long>(row) * S;
+        for (int i0 = fw; i0 < nglb; i0 += 4 * nfw) {
+          float mm[4], ll[4], uu[4][DPH];
 #pragma unroll
-        for (int j = 0; j < DPH; ++j) u[j] = st_u[slot * D + (lane & 15) * DPH + j];
-        fold_state(wm, wl, wu, st_m[slot], st_l[slot], u);
+          for (int c = 0; c < 4; ++c) {
+            const int i = i0 + c * nfw;
+            mm[c] = neg_inf();
+            ll[c] = 0.f;
+            if (i < nglb) {
+              const long long o = rb + s_glb[i];
+              mm[c] = __ldcg(a.sm + o);
+              ll[c] = __ldcg(a.sl + o);
+              const float4* up = reinterpret_cast<const float4*>(a.su + o * D + (lane & 15) * DPH);
+              const float4 x0 = __ldcg(up), x1 = __ldcg(up + 1);
+              uu[c][0] = x0.x; uu[c][1] = x0.y; uu[c][2] = x0.z; uu[c][3] = x0.w;
+              uu[c][4] = x1.x; uu[c][5] = x1.y; uu[c][6] = x1.z; uu[c][7] = x1.w;
+            } else {
+#pragma unroll
+              for (int j = 0; j < DPH; ++j) uu[c][j] = 0.f;
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c) fold_state(wm, wl, wu, mm[c], ll[c], uu[c]);
+        }
       }
+      if (tid == kStepProducer * 32) SPT(23);
     }
     if (lane == 0) { s_wm[warp] = wm; s_wl[warp] = wl; }
     if (lane < 16) store_vec<DPH>(&s_wu[warp][lane * DPH], wu);
@@ -662,11 +851,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
   // control block for the next call.
   __syncthreads();
   if (tid == 0) SPT(11);
+#ifdef STK_TRACE
+  __syncthreads();
+  if (blockIdx.x < 256)
+    for (int i = tid; i < 128; i += kStepThreads) g_step_trace[blockIdx.x * 128 + i] = s_trc[i];
+#endif
   if (tid == 0) {
     __threadfence();
     if (atomicAdd(ctas_done, 1u) == static_cast<unsigned>(grid) - 1) {
       for (int i = 0; i < hkv + 2 * hq; ++i) atomicExch(a.ctrl + i, 0u);
       atomicExch(ctas_done, 0u);
+      SPAN_END();
       __threadfence();
     }
   }
@@ -687,9 +882,6 @@ const char* decode_step_unsupported(int hq, int hkv, int n, int b, int d, int kv
   if (static_cast<size_t>(hq) * kStepD > 4096) return "the fused step stages at most 4096 query values";
   if (n > kStepMaxBlocks || n < topk) return "the fused step takes topk <= blocks <= 4096";
   if (topk > kStepMaxList || sp > kStepMaxList) return "the fused step takes lists of at most 256 blocks";
-  const int slots = sp > 0 ? sp : topk;
-  if (static_cast<size_t>(slots) * (kStepD + 2) * 4 > static_cast<size_t>(kStepStages) * kStageBytes)
-    return "the fused step folds at most 336 block states per row";
   if (2 * hq >= num_sms) return "the fused step needs more than two SMs per query head";
   return nullptr;
 }
