@@ -49,7 +49,9 @@ sys.path.insert(0, str(ROOT))
 
 HQ, HKV, D, BLOCKS, B, TOPK = 32, 8, 128, 2048, 32, 64
 METRIC = "decode-step µs (score+topk+spec attn+repair) vs serial; HBM GB/s % of peak"
-LAUNCHES_PER_STEP = {"saved": 4, "light": 4, "compact": 8, "repair_fused": 5, "signed_fused": 5}
+# Kernel launches per step: the fused step (saved / light, one persistent
+# launch) and the launch chains of the other methods.
+LAUNCHES_PER_STEP = {"saved": 1, "light": 1, "compact": 8, "repair_fused": 5, "signed_fused": 5}
 MIN_TIMED_MS = 200.0
 
 
@@ -625,24 +627,36 @@ def main():
     dec = [SpeculativeDecoder(s["q"], s["k"], s["v"], s["lo"], s["hi"], s["p"], spec, graph=graph) for s in sets]
     ser = [SpeculativeDecoder(s["q"], s["k"], s["v"], s["lo"], s["hi"], s["p"], spec, serial=True, graph=graph)
            for s in sets]
+    # The same steps as launch chains (scorer -> Top-K -> states / exact ->
+    # repair): the serial baseline is the faster of the two serial forms.
+    ser_chain = [SpeculativeDecoder(s["q"], s["k"], s["v"], s["lo"], s["hi"], s["p"], spec, serial=True, graph=graph,
+                                    fused=False) for s in sets]
+    dec_chain = [SpeculativeDecoder(s["q"], s["k"], s["v"], s["lo"], s["hi"], s["p"], spec, graph=graph, fused=False)
+                 for s in sets]
     # Correctness gate before timing: speculative == serial within bf16 tolerance, IDs identical.
-    for d_, s_ in zip(dec, ser):
+    for d_, s_, c_, e_ in zip(dec, ser, ser_chain, dec_chain):
         o1 = d_.step().clone()
         o2 = s_.step().clone()
+        o3 = c_.step().clone()
+        o4 = e_.step().clone()
         torch.cuda.synchronize()
-        assert torch.equal(d_.selected.cpu(), s_.selected.cpu())
-        assert (o1 - o2).abs().max().item() <= 2e-3, "speculative and serial outputs differ"
+        for x in (s_, c_, e_):
+            assert torch.equal(d_.selected.cpu(), x.selected.cpu())
+        for o in (o2, o3, o4):
+            assert (o1 - o).abs().max().item() <= 2e-3, "speculative and serial outputs differ"
 
     # Exactly K steps per timed region: K // gsteps graphs of `gsteps`
     # consecutive decode steps (one per input set), then K % gsteps
     # single-step graphs, continuing the rotation.
     gsteps = max(1, min(args.graph_steps, nsets)) if graph else 1
     K = max(1, args.steps)
+    def graphs_of(decs):
+        return [capture_steps([decs[(j + i) % nsets] for i in range(gsteps)])[0] for j in range(0, nsets, gsteps)]
+
     if gsteps > 1:
-        gspec = [capture_steps([dec[(j + i) % nsets] for i in range(gsteps)])[0] for j in range(0, nsets, gsteps)]
-        gser = [capture_steps([ser[(j + i) % nsets] for i in range(gsteps)])[0] for j in range(0, nsets, gsteps)]
+        gspec, gser, gser_chain, gspec_chain = graphs_of(dec), graphs_of(ser), graphs_of(ser_chain), graphs_of(dec_chain)
     else:
-        gspec = gser = None
+        gspec = gser = gser_chain = gspec_chain = None
 
     def run_steps(decs, graphs, count):
         full, rest = divmod(count, gsteps) if graphs else (0, count)
@@ -665,16 +679,24 @@ def main():
     value = world * K / (ms / 1e3)
     clocks = clk.summary()
 
-    # Serial baseline with the same kernels (same rotation and repeats).
-    run_steps(ser, gser, 3 * gsteps)
-    reps_ser = timed_repeats(lambda: run_steps(ser, gser, K), world, device, quick=args.quick)
-    us_ser = statistics.median(reps_ser) * 1e3 / K
+    # Serial baselines with the same kernels (same rotation and repeats):
+    # the fused serial step and the serial launch chain; the faster one is
+    # the baseline. The speculative launch chain is reported beside them.
+    variants = {}
+    for name, decs, gr in (("serial_fused", ser, gser), ("serial_chained", ser_chain, gser_chain),
+                           ("speculative_chained", dec_chain, gspec_chain)):
+        run_steps(decs, gr, 3 * gsteps)
+        rp = timed_repeats(lambda: run_steps(decs, gr, K), world, device, quick=args.quick)
+        variants[name] = statistics.median(rp) * 1e3 / K
+    variants["speculative_fused"] = us_step
+    us_ser = min(variants["serial_fused"], variants["serial_chained"])
     # Context: one CUDA graph per step (graph-launch cost paid every step).
     single = {}
     if graph and gsteps > 1 and not args.quick:
         n1 = min(K * 10, 2000)
         single = {"spec_us": time_loop(lambda i: dec[i % nsets].step(), n1, device) * 1e3 / n1,
-                  "serial_us": time_loop(lambda i: ser[i % nsets].step(), n1, device) * 1e3 / n1}
+                  "serial_us": min(time_loop(lambda i: ser[i % nsets].step(), n1, device),
+                                   time_loop(lambda i: ser_chain[i % nsets].step(), n1, device)) * 1e3 / n1}
 
     # Roofline of the dominant kernel: predicted-block attention (block states over P).
     g = HQ // HKV
@@ -819,14 +841,27 @@ def main():
                        "graph": (f"{gsteps} decode steps per CUDA graph (one per input set, replayed; each step one "
                                  "launch chain)") if gsteps > 1 else "one CUDA graph per step"},
             "serial_us_per_step": us_ser, "speedup_vs_serial": us_ser / us_step,
+            "us_per_step_variants": variants,
             "one_graph_per_step_us": single or None,
             "step_algorithmic_bytes": step_bytes, "serial_algorithmic_bytes": serial_bytes,
             "step_hbm_frac": step_bytes / (us_step * 1e-6) / 1e9 / hbm_peak,
             "serial_hbm_frac": serial_bytes / (us_ser * 1e-6) / 1e9 / hbm_peak,
-            "roofline": {"bound": "hbm", "kernel": "jobs_fast_kernel (predicted-block attention, gqa.partials)",
-                         "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-                         "peak_kind": peak_kind, "us_per_launch": us_part, "bytes_per_launch": part_bytes,
-                         "traffic": traffic_of("jobs_fast_kernel")},
+            # The step is one launch of the fused kernel: its algorithmic bytes
+            # (metadata, predicted and missed K/V, q, IDs, output) over the
+            # step time (graph-replayed, launch gaps included).
+            "roofline": {"bound": "hbm", "kernel": "decode_step_kernel (fused speculative step: scoring, Top-K, "
+                                                   "predicted-block states, saved repair)",
+                         "achieved": step_bytes / (us_step * 1e-6) / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": step_bytes / (us_step * 1e-6) / 1e9 / hbm_peak, "peak_kind": peak_kind,
+                         "us_per_launch": us_step, "bytes_per_launch": step_bytes,
+                         "traffic": traffic_of("decode_step_kernel")},
+            # The predicted-block attention kernel of the launch-chain path
+            # (gqa.partials) timed alone.
+            "roofline_attention": {"bound": "hbm", "kernel": "jobs_fast_kernel (predicted-block attention, "
+                                                             "gqa.partials)",
+                                   "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                                   "peak_kind": peak_kind, "us_per_launch": us_part, "bytes_per_launch": part_bytes,
+                                   "traffic": traffic_of("jobs_fast_kernel")},
             "clocks": clocks,
             "e2e": {"value": e2e_value, "unit": "decode-steps/s", "h2d_bytes_per_step": HQ * D * 2 + HQ * TOPK * 4,
                     "d2h_bytes_per_step": HQ * D * 4,
@@ -844,7 +879,7 @@ def main():
         if sweep:
             line["sweep"] = sweep
         print(json.dumps(line), flush=True)
-    for d_ in dec + ser:
+    for d_ in dec + ser + ser_chain + dec_chain:
         d_.close()
     if world > 1:
         import torch.distributed as dist

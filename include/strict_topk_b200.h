@@ -273,8 +273,9 @@ STK_API int stk_speculative_step(const stk_kv* kv, const void* q, int q_dtype, c
 
 /* Workspace (bytes) for stk_decode_step: a control block of
  * (hkv + 2 hq + 1) 32-bit counters, then one 8-byte score slot per (query
- * head, block) and the block states of `slots` blocks per query head
- * (slots = sp for a speculative step, topk for a serial one). */
+ * head, block), the block states of `slots` blocks per query head
+ * (slots = sp for a speculative step, topk for a serial one) and one 32-bit
+ * tag per (query head, slot). */
 STK_API size_t stk_decode_step_workspace_bytes(int hq, int hkv, int n, int slots, int d);
 
 /* The whole decode step in one persistent, cooperative launch (one CTA per
@@ -295,8 +296,10 @@ STK_API size_t stk_decode_step_workspace_bytes(int hq, int hkv, int n, int slots
  * topk and sp <= 256, fewer than half as many query heads as SMs; other
  * shapes return STK_ESMEM and take stk_speculative_step / stk_select_topk +
  * stk_repair. The workspace must be zero before its first use (e.g. one
- * cudaMemset after allocation); every call leaves its control block zero
- * again. Calls sharing a workspace must be ordered on one stream. */
+ * cudaMemset after allocation); every call leaves its control block, score
+ * slots and tags zero again (a call whose status word reports
+ * STK_STATUS_WAIT_TIMEOUT may not: zero the workspace before reusing it).
+ * Calls sharing a workspace must be ordered on one stream. */
 STK_API int stk_decode_step(const stk_kv* kv, const void* q, int q_dtype, const float* lo, const float* hi, int hq,
                             int topk, const void* pred, int pred64, int sp, int32_t* selected, float* out,
                             void* workspace, size_t workspace_bytes, int32_t* status, void* stream);

@@ -447,7 +447,7 @@ size_t stk_decode_step_workspace_bytes(int hq, int hkv, int n, int slots, int d)
   if (hq <= 0 || hkv <= 0 || n <= 0 || slots <= 0 || d <= 0) return 0;
   const size_t s = static_cast<size_t>(hq) * slots;
   return decode_step_ctrl_bytes(hq, hkv) + align256(stk_select_workspace_bytes(hq, n)) +
-         2 * align256(s * sizeof(float)) + align256(s * d * sizeof(float));
+         2 * align256(s * sizeof(float)) + align256(s * d * sizeof(float)) + align256(s * sizeof(int32_t));
 }
 
 int stk_decode_step(const stk_kv* kv, const void* q, int q_dtype, const float* lo, const float* hi, int hq, int topk,
@@ -487,6 +487,8 @@ int stk_decode_step(const stk_kv* kv, const void* q, int q_dtype, const float* l
   a.sl = reinterpret_cast<float*>(w);
   w += align256(s * sizeof(float));
   a.su = reinterpret_cast<float*>(w);
+  w += align256(s * d * sizeof(float));
+  a.sel_tag = reinterpret_cast<int*>(w);
   a.status = status;
   a.scale = attn_scale(d);
   rc = launch_decode_step(a, kv->kv_dtype, nsm, static_cast<cudaStream_t>(stream));

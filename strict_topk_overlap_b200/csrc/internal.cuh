@@ -164,6 +164,7 @@ struct StepArgs {
   float* sl;
   float* su;       // [hq, S, D]
   unsigned* ctrl;  // [hkv + 2 hq + 1]
+  int* sel_tag;    // [hq, topk] serial step: selected ID + 1 (0 = not yet published)
   int* status;
   float scale;
 };

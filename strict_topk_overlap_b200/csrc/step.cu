@@ -62,6 +62,7 @@ namespace stk {
 // CTA copies its record out at exit.
 static __device__ unsigned long long g_step_trace[256 * 128];
 static __shared__ unsigned long long s_trc[128];
+static __shared__ unsigned s_trc_meta;  // scored metadata items of this CTA
 // [launch % 64][first CTA start, last CTA exit] over consecutive launches.
 static __device__ unsigned long long g_step_span[2 * 64];
 static __device__ unsigned g_step_launch;
@@ -190,15 +191,19 @@ __device__ __forceinline__ void fold_state(float& wm, float& wl, float (&wu)[kSt
 // its G query heads, staged as lo rows [16][D] then hi rows [16][D].
 //
 // Lane l owns dims [4l, 4l + 4): every warp-wide 128-bit load reads one whole
-// 512-byte row (conflict-free), and q of four heads stays in registers. Per
-// group of 4 blocks and 4 heads each lane forms 16 partial sums (its 4 dims,
-// sequential FP32 FMA on the sign-selected bound); a transposed butterfly
-// (xor 8, 4, 2, 1) and one xor-16 add leave the total of (block j, head g) in
-// lanes 4 j + g and 16 + 4 j + g. Every term passes through at most 4 + 5
-// roundings, fewer than the D / 4 + 2 that the interval radius
+// 512-byte row (conflict-free), and q of four heads stays in registers split
+// by sign, q+ = max(q, 0) and q- = min(q, 0), so that the sign-selected bound
+// term q (q >= 0 ? hi : lo) is q+ hi + q- lo: two FMAs, one of them adding an
+// exact zero. Per group of 4 blocks and 4 heads each lane forms 16 partial
+// sums (its 4 dims in order); a transposed butterfly (xor 8, 4, 2, 1) and one
+// xor-16 add leave the total of (block j, head g) in lanes 4 j + g and
+// 16 + 4 j + g. Every nonzero term passes through at most 4 + 5 roundings,
+// fewer than the D / 4 + 2 that the interval radius
 // 2 (D/4 + 2) u ||q||_1 max|lo, hi| + 2^-118 of bound_interval_kernel
 // (select.cu) covers, so the interval, rounded outward, contains the block's
-// FP64 score.
+// FP64 score (an infinite bound makes a NaN sum, and the interval then spans
+// everything). The interval is written as one 8-byte store into a slot that
+// reads zero until then.
 template <int GM>
 __device__ __forceinline__ void score_item(const StepArgs& a, const float* slo, const float* shi, const float* qs,
                                            const float* qn1, int mh, int b0, int nb, int G, int lane) {
@@ -207,11 +212,16 @@ __device__ __forceinline__ void score_item(const StepArgs& a, const float* slo, 
   const float inf = __int_as_float(0x7f800000);
 #pragma unroll 1
   for (int g0 = 0; g0 < G; g0 += 4) {
-    float4 q4[4];
+    float4 qp[4], qn[4];
 #pragma unroll
-    for (int g = 0; g < 4; ++g)
-      q4[g] = (g0 + g < G) ? *reinterpret_cast<const float4*>(qs + (mh * G + g0 + g) * D + 4 * lane)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int g = 0; g < 4; ++g) {
+      const float4 q = (g0 + g < G) ? *reinterpret_cast<const float4*>(qs + (mh * G + g0 + g) * D + 4 * lane)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      qp[g] = make_float4(q.x >= 0.f ? q.x : 0.f, q.y >= 0.f ? q.y : 0.f, q.z >= 0.f ? q.z : 0.f,
+                          q.w >= 0.f ? q.w : 0.f);
+      qn[g] = make_float4(q.x >= 0.f ? 0.f : q.x, q.y >= 0.f ? 0.f : q.y, q.z >= 0.f ? 0.f : q.z,
+                          q.w >= 0.f ? 0.f : q.w);
+    }
 #pragma unroll 1
     for (int bq = 0; bq < kMetaItemBlocks && bq < nb; bq += 4) {
       float part[16];
@@ -228,10 +238,14 @@ __device__ __forceinline__ void score_item(const StepArgs& a, const float* slo, 
                       fmaxf(fmaxf(fabsf(l4.z), fabsf(h4.z)), fmaxf(fabsf(l4.w), fabsf(h4.w))));
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          float acc = q4[g].x * (q4[g].x >= 0.f ? h4.x : l4.x);
-          acc = fmaf(q4[g].y, q4[g].y >= 0.f ? h4.y : l4.y, acc);
-          acc = fmaf(q4[g].z, q4[g].z >= 0.f ? h4.z : l4.z, acc);
-          acc = fmaf(q4[g].w, q4[g].w >= 0.f ? h4.w : l4.w, acc);
+          float acc = qp[g].x * h4.x;
+          acc = fmaf(qn[g].x, l4.x, acc);
+          acc = fmaf(qp[g].y, h4.y, acc);
+          acc = fmaf(qn[g].y, l4.y, acc);
+          acc = fmaf(qp[g].z, h4.z, acc);
+          acc = fmaf(qn[g].z, l4.z, acc);
+          acc = fmaf(qp[g].w, h4.w, acc);
+          acc = fmaf(qn[g].w, l4.w, acc);
           part[4 * j + g] = acc;
         }
       }
@@ -265,12 +279,25 @@ __device__ __forceinline__ void score_item(const StepArgs& a, const float* slo, 
       const int j = (lane >> 2) & 3, g = lane & 3, b = bq + j, head = g0 + g;
       if (lane < 16 && b < nb && head < G) {
         const float e = __fadd_ru(__fmul_ru(__fmul_ru(qn1[mh * G + head], bm), kErrFactor), 0x1p-118f);
-        float2 iv = make_float2(__fsub_rd(sum, e), __fadd_ru(sum, e));
-        if (!(iv.x <= iv.y)) iv = make_float2(-inf, inf);
-        a.bounds[static_cast<long long>(mh * G + head) * a.n + b0 + b] = iv;
+        float lo = __fsub_rd(sum, e), up = __fadd_ru(sum, e);
+        if (!(lo <= up)) { lo = -inf; up = inf; }
+        *reinterpret_cast<unsigned long long*>(a.bounds + static_cast<long long>(mh * G + head) * a.n + b0 + b) =
+            static_cast<unsigned long long>(__float_as_uint(lo)) |
+            (static_cast<unsigned long long>(__float_as_uint(up)) << 32);
       }
     }
   }
+}
+
+// Relaxed GPU-scope add (no ordering: readers of what it counts check the
+// data itself).
+__device__ __forceinline__ void red_relaxed_gpu(unsigned* p, unsigned v) {
+  asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_relaxed_gpu_s32(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // Shared-memory counter add with release semantics at CTA scope: the warp's
@@ -297,10 +324,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
   __shared__ uint64_t full_bar[NS], empty_bar[NS], q_bar;
   __shared__ int s_desc[NS], item_ok[NS];
   __shared__ volatile int s_abort;
+  __shared__ bool s_last;
   __shared__ int s_sel[kStepMaxList], s_pid[kStepMaxList], s_loc[kStepMaxList], s_glb[kStepMaxList];
   __shared__ int s_nloc, s_nglb;
   __shared__ unsigned s_pmask[kStepMaxBlocks / 32], s_amask[kStepMaxBlocks / 32];
-  __shared__ unsigned s_head_cnt[kStepMaxHeads], s_row_cnt[kStepMaxHeads];
+  __shared__ unsigned s_row_cnt[kStepMaxHeads];
   __shared__ float s_wm[kStepWarps], s_wl[kStepWarps];
   __shared__ __align__(16) float s_wu[kStepWarps][D];
 
@@ -349,7 +377,21 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
     if (jl < 0 || jl >= my_jobs) return -1;
     const int jj = j0 + jl, r = jj / SJ;
     const long long o = static_cast<long long>(r) * (serial ? K : S) + xl + (jj - r * SJ);
-    return serial ? static_cast<long long>(__ldcg(a.selected + o)) : load_id(a.pred, a.pred64, o);
+    if (!serial) return load_id(a.pred, a.pred64, o);
+    // Serial step: the row CTA publishes ID + 1 into the zeroed tags.
+    int t = ld_relaxed_gpu_s32(a.sel_tag + o);
+    if (t == 0) {
+      const unsigned long long t0 = global_ns();
+      while ((t = ld_relaxed_gpu_s32(a.sel_tag + o)) == 0) {
+        __nanosleep(100);
+        if (global_ns() - t0 > c_wait_ns) {
+          report(a.status, kStatusWaitTimeout);
+          s_abort = 1;
+          return -1;
+        }
+      }
+    }
+    return static_cast<long long>(t) - 1;
   };
 
   // ---------------------------------------------------------------- producer (warp 11)
@@ -445,8 +487,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
   // ---------------------------------------------------------------- set-up
 #ifdef STK_TRACE
   const unsigned long long t_start = global_ns();
-  if (warp == kStepProducer)
+  if (warp == kStepProducer) {
     for (int i = lane; i < 128; i += 32) s_trc[i] = 0ull;
+    s_trc_meta = 0u;
+  }
 #endif
   SPAN_START();
   const int n_first = min(my_meta, NS);
@@ -459,10 +503,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
   long long lid_a = -1, lid_b = -1;  // producer lane: IDs of jobs jb + lane and jb + 32 + lane
   int jb = 0;
   if (warp == kStepProducer) {
-    if (!serial) {
-      lid_a = job_id(lane);
-      lid_b = job_id(32 + lane);
-    }
     // Barriers and counters, q, then the first metadata items at once (one
     // lane each), before anything else of the CTA.
     if (lane == 0) {
@@ -476,7 +516,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
       mbar_arrive_expect_tx(&q_bar, static_cast<unsigned>(qbytes));
       bulk_g2s(q_dst, a.q, static_cast<unsigned>(qbytes), &q_bar);
     }
-    s_head_cnt[lane] = 0u;
     s_row_cnt[lane] = 0u;
     __syncwarp();
     barriers_ready_arrive();
@@ -487,6 +526,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
     }
     __syncwarp();
     if (lane == 0) SPT(2);
+    if (!serial) {
+      lid_a = job_id(lane);
+      lid_b = job_id(32 + lane);
+    }
   } else {
     // q as FP32 in shared memory and its per-head ||q||_1 rounded up; the
     // producer does not take part.
@@ -560,14 +603,30 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
       if (code < my_meta) {
         int mh, b0;
         meta_item(code, mh, b0);
+#ifdef STK_SCORE_TWICE
+        if (ok && warp == 0 && kph == 1) {
+          if (lane == 0) SPT(25);
+          score_item<GM>(a, reinterpret_cast<const float*>(stage),
+                         reinterpret_cast<const float*>(stage + kStageBytes / 2), qs, qn1, mh, b0,
+                         min(kMetaItemBlocks, n - b0), G, lane);
+          __syncwarp();
+          if (lane == 0) SPT(26);
+        }
+#endif
         if (ok)
           score_item<GM>(a, reinterpret_cast<const float*>(stage),
                          reinterpret_cast<const float*>(stage + kStageBytes / 2), qs, qn1, mh, b0,
                          min(kMetaItemBlocks, n - b0), G, lane);
         __syncwarp();
+#ifdef STK_SCORE_TWICE
+        if (warp == 0 && kph == 1 && lane == 0) SPT(27);
+#endif
         if (lane == 0) {
           mbar_arrive(&empty_bar[st]);
-          red_release_cta(&s_head_cnt[mh], 1u);
+          red_relaxed_gpu(&head_done[mh], 1u);
+#ifdef STK_TRACE
+          if (atomicAdd(&s_trc_meta, 1u) == static_cast<unsigned>(my_meta) - 1u) SPT(21);
+#endif
         }
       } else if (code < kItemLocal) {
         const int job = j0 + (code - my_meta);
@@ -580,6 +639,22 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
 #pragma unroll
           for (int j = 0; j < DPH; ++j) qf[j] = qs[r * D + (lane & 15) * DPH + j];
           const T* ks = reinterpret_cast<const T*>(stage);
+#ifdef STK_SCORE_TWICE
+          if (warp == 0 && (code - my_meta) < 64 && s_trc[28] == 0) {
+            if (lane == 0) SPT(28);
+            float m2 = neg_inf(), l2 = 0.f, u2[DPH], ua2[DPH];
+#pragma unroll
+            for (int j = 0; j < DPH; ++j) { u2[j] = 0.f; ua2[j] = 0.f; }
+            warp_block_state<T, DPH, kModeFull, true>(ks, ks + kStepB * D, kStepB, qf, a.scale, 0.f, m2, l2, u2, ua2,
+                                                      lane);
+            __syncwarp();
+            if (lane == 0) SPT(29);
+            warp_block_state<T, DPH, kModeFull, true>(ks, ks + kStepB * D, kStepB, qf, a.scale, 0.f, m, l, u, ua,
+                                                      lane);
+            __syncwarp();
+            if (lane == 0) SPT(30);
+          } else
+#endif
           warp_block_state<T, DPH, kModeFull, true>(ks, ks + kStepB * D, kStepB, qf, a.scale, 0.f, m, l, u, ua,
                                                     lane);
         }
@@ -625,7 +700,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
             });
     if (my_jobs > 0) {
       if (serial) {
-        // The rows of [j0, j1) must have published their selections.
+        // The rows of [j0, j1) publish their selections as tags; their
+        // row_ready counts tell when to start reading them.
         if (lane == 0)
           for (int r = j0 / SJ; r <= (j1 - 1) / SJ && !s_abort; ++r)
             if (!wait_count(&row_ready[r], 1)) {
@@ -633,10 +709,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
               s_abort = 1;
             }
         __syncwarp();
-        if (!s_abort) {
-          lid_a = job_id(lane);
-          lid_b = job_id(32 + lane);
-        }
+        if (!s_abort) lid_a = job_id(lane);
+        if (!s_abort) lid_b = job_id(32 + lane);
       }
       if (lane == 0) SPT(3);
       produce(my_jobs,
@@ -667,28 +741,24 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
     consume(std::false_type{}, nullptr, dm, dl, du);
     if (lane == 0 && warp == 0) SPT(14);
   } else if (warp == kStepPublisher) {
-    // Forward the CTA's completions GPU-wide: one fence per batch (a GPU-
-    // scope fence waits behind this SM's bulk copies, so it is kept off the
-    // consumers). Lane h < hkv: KV head h's scored metadata items; lane r <
-    // hq: row r's block states.
-    unsigned pub_h = 0, pub_r = 0;
-    const unsigned want = static_cast<unsigned>(my_meta + my_jobs);
+    // Forward the CTA's block-state completions GPU-wide: one fence per
+    // batch (a GPU-scope fence waits behind this SM's bulk copies, so it is
+    // kept off the consumers). Lane r < hq: row r's block states.
+    unsigned pub_r = 0;
+    const unsigned want = static_cast<unsigned>(my_jobs);
     unsigned long long t0 = global_ns();
-    while (true) {
-      const unsigned ch = lane < hkv ? ld_acquire_cta(&s_head_cnt[lane]) : 0u;
+    while (want > 0) {
       const unsigned cr = lane < hq ? ld_acquire_cta(&s_row_cnt[lane]) : 0u;
-      const bool fresh = ch != pub_h || cr != pub_r;
+      const bool fresh = cr != pub_r;
       if (__any_sync(kFull, fresh)) {
         if (fresh) {
           __threadfence();
-          if (ch != pub_h) atomicAdd(&head_done[lane], ch - pub_h);
-          if (cr != pub_r) atomicAdd(&row_states[lane], cr - pub_r);
+          atomicAdd(&row_states[lane], cr - pub_r);
         }
-        pub_h = ch;
         pub_r = cr;
         t0 = global_ns();
       }
-      if (static_cast<unsigned>(warp_sum_int(static_cast<int>(pub_h + pub_r))) >= want || s_abort) break;
+      if (static_cast<unsigned>(warp_sum_int(static_cast<int>(pub_r))) >= want || s_abort) break;
       if (global_ns() - t0 > c_wait_ns) {
         if (lane == 0) report(a.status, kStatusWaitTimeout);
         s_abort = 1;
@@ -705,127 +775,188 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
     const float* qrow = qs + row * D;
     const int mh = row / G;
     if (tid == 0) SPT(5);
+    // Membership of the predicted list (speculative step), the selection's
+    // mask and the row-local list start empty; the predicted IDs arrived at
+    // kernel start.
+    for (int i = tid; i < (n + 31) / 32; i += kStepThreads) { s_pmask[i] = 0u; s_amask[i] = 0u; }
+    __syncthreads();
+    if (!serial)
+      for (int i = tid; i < a.sp; i += kStepThreads) {
+        const int id = s_pid[i];
+        if (id >= 0 && id < n) atomicOr(&s_pmask[id >> 5], 1u << (id & 31));
+      }
     if (tid == 0 && !s_abort && !wait_count(&head_done[mh], static_cast<unsigned>(ipH))) {
       report(a.status, kStatusWaitTimeout);
       s_abort = 1;
     }
     __syncthreads();
     if (tid == 0) SPT(6);
+    // Row-local blocks: the misses (A not in P) of the saved repair, or the
+    // serial row's first xl selected blocks. While the selection runs, the
+    // blocks its intervals already classify as selected and that P lacks are
+    // asked into L2 (their copies, issued once the list is final, then hit
+    // L2); each selected block sets its bit in the selection's mask and
+    // flags its output position when it is a miss.
+    struct RowHook {
+      const StepArgs* a;
+      int* s_mflag;
+      unsigned* s_pmask;
+      unsigned* s_amask;
+      int mh, n;
+      bool serial;
+      __device__ void sure_in(int id) const {
+        if (serial || ((s_pmask[id >> 5] >> (id & 31)) & 1u)) return;
+        const long long off = (static_cast<long long>(mh) * n + id) * kStepB * kStepD;
+        constexpr unsigned kBytes = kStepB * kStepD * sizeof(T);
+        bulk_prefetch_l2(static_cast<const T*>(a->k) + off, kBytes);
+        bulk_prefetch_l2(static_cast<const T*>(a->v) + off, kBytes);
+      }
+      __device__ void selected(int pos, int id, bool) const {
+        atomicOr(&s_amask[id >> 5], 1u << (id & 31));
+        s_mflag[pos] = serial ? 0 : !((s_pmask[id >> 5] >> (id & 31)) & 1u);
+      }
+    };
+    const RowHook hook{&a, s_loc, s_pmask, s_amask, mh, n, serial};
     if (!s_abort) {
       SelectArgs sa{};
       sa.R = 1; sa.hsel = hq; sa.topk = K; sa.n = n; sa.block_offsets = nullptr; sa.total_blocks = n;
       sa.id_base = 0; sa.ids_out = a.selected; sa.keys_out = nullptr; sa.status = a.status;
       sa.bounds = a.bounds; sa.q = a.q; sa.q_dtype = a.q_dtype; sa.lo = a.lo; sa.hi = a.hi;
       sa.hq = hq; sa.hmeta = hkv; sa.d = D; sa.group_select = 0;
-      bounded_select_core<E, kStepThreads>(sa, row, qrow, true);
+      bounded_select_core<E, kStepThreads, true, RowHook>(sa, row, qrow, true, s_sel, hook);
     }
     __syncthreads();
     if (tid == 0) SPT(7);
-    for (int i = tid; i < K; i += kStepThreads) s_sel[i] = a.selected[static_cast<long long>(row) * K + i];
-    if (serial && tid == 0 && !s_abort) publish(&row_ready[row]);
-    __syncthreads();
-
-    // Row-local blocks: the misses (A not in P) of the saved repair, or the
-    // serial row's first xl selected blocks; the block states to fold from
-    // the states buffer: the hits (P slots in A), or the serial row's other
-    // K - xl slots.
-    if (!serial) {
-      for (int i = tid; i < (n + 31) / 32; i += kStepThreads) { s_pmask[i] = 0u; s_amask[i] = 0u; }
-      __syncthreads();
-      for (int i = tid; i < a.sp; i += kStepThreads) {
-        const int id = s_pid[i];
-        if (id >= 0 && id < n) atomicOr(&s_pmask[id >> 5], 1u << (id & 31));
+    // The ascending list of row-local blocks (warp 0; s_loc held the miss
+    // flags of the output positions).
+    if (warp == 0) {
+      int nm = 0;
+      for (int b = 0; b < K; b += 32) {
+        const int pos = b + lane;
+        const bool take = pos < K && (serial ? pos < xl : s_loc[pos] != 0);
+        const int id = pos < K ? s_sel[pos] : -1;
+        const unsigned bal = __ballot_sync(kFull, take);
+        __syncwarp();
+        if (take) s_glb[nm + __popc(bal & ((1u << lane) - 1u))] = id;
+        nm += __popc(bal);
       }
-      for (int i = tid; i < K; i += kStepThreads) {
-        const int id = s_sel[i];
-        if (id >= 0 && id < n) atomicOr(&s_amask[id >> 5], 1u << (id & 31));
-      }
-      __syncthreads();
-      if (warp == 0) {
-        int nm = 0;
-        for (int b = 0; b < K; b += 32) {
-          const int id = b + lane < K ? s_sel[b + lane] : -1;
-          const bool miss = id >= 0 && !((s_pmask[id >> 5] >> (id & 31)) & 1u);
-          const unsigned bal = __ballot_sync(kFull, miss);
-          if (miss) s_loc[nm + __popc(bal & ((1u << lane) - 1u))] = id;
-          nm += __popc(bal);
-        }
-        int nh = 0;
-        for (int b = 0; b < a.sp; b += 32) {
-          const int id = b + lane < a.sp ? s_pid[b + lane] : -1;
-          const bool hit = id >= 0 && id < n && ((s_amask[id >> 5] >> (id & 31)) & 1u);
-          const unsigned bal = __ballot_sync(kFull, hit);
-          if (hit) s_glb[nh + __popc(bal & ((1u << lane) - 1u))] = b + lane;
-          nh += __popc(bal);
-        }
-        if (lane == 0) { s_nloc = nm; s_nglb = nh; }
-      }
-    } else {
-      for (int i = tid; i < K; i += kStepThreads) {
-        if (i < xl) s_loc[i] = s_sel[i];
-        else s_glb[i - xl] = i;
-      }
-      if (tid == 0) { s_nloc = xl; s_nglb = K - xl; }
+      __syncwarp();
+      for (int i = lane; i < nm; i += 32) s_loc[i] = s_glb[i];
+      if (lane == 0) s_nloc = nm;
+    }
+    if (serial)
+      for (int i = xl + tid; i < K; i += kStepThreads) a.sel_tag[static_cast<long long>(row) * K + i] = s_sel[i] + 1;
+    // The row's score slots go back to zero for the next call.
+    {
+      unsigned long long* slots = reinterpret_cast<unsigned long long*>(a.bounds + static_cast<long long>(row) * n);
+      for (int i = tid; i < n; i += kStepThreads) slots[i] = 0ull;
     }
     __syncthreads();
+    if (serial && tid == 0 && !s_abort) red_relaxed_gpu(&row_ready[row], 1u);
     const int nloc = s_abort ? 0 : s_nloc;
-    const int nglb = s_abort ? 0 : s_nglb;
+    // Block states to fold from the buffer: the hits (P slots whose block is
+    // in A), or the serial row's slots xl .. K - 1.
+    const int nglb = s_abort ? 0 : (serial ? K - xl : a.sp);
     float wm = neg_inf(), wl = 0.f, wu[DPH];
 #pragma unroll
     for (int j = 0; j < DPH; ++j) wu[j] = 0.f;
-    if (warp == kStepProducer) {
-      produce(nloc, [&](int) {},
-              [&](int i, int& code, int& kind, int& mh_, long long&, long long& id) {
-                if (i < 0) return;
-                code = kItemLocal + i;
-                kind = 1;
-                mh_ = mh;
-                id = s_loc[i];
-              });
-      produce_ends();
-      if (lane == 0) SPT(8);
-    } else if (warp < NS) {
-      consume(std::true_type{}, qrow, wm, wl, wu);
-      if (lane == 0 && warp == 0) SPT(24);
-    }
-    if (warp >= kStepProducer) {
-      // Warps 11..15: the states from the buffer, once every work CTA has
-      // written this row's (with plain loads through L2; a warp folds four
-      // states per round trip).
-      const int fw = warp - kStepProducer, nfw = kStepWarps - kStepProducer;
+    // The buffered states, once every work CTA has written this row's: every
+    // warp but the producer folds its share of the slots, up to four per
+    // round trip, while the row-local blocks' copies are in flight.
+    constexpr int nfw = kStepWarps - 1;
+    const int fw = warp < kStepProducer ? warp : warp - 1;
+    const long long rb = static_cast<long long>(row) * S;
+    // Buffer slot of this warp's fold i (serial: xl + i; speculative: P slot
+    // i when its block is in A), or -1.
+    auto fold_slot = [&](int i) {
+      if (i >= nglb) return -1;
+      if (serial) return xl + i;
+      const int id = s_pid[i];
+      return (id >= 0 && id < n && ((s_amask[id >> 5] >> (id & 31)) & 1u)) ? i : -1;
+    };
+    auto wait_buffered = [&]() {
       if (lane == 0 && nglb > 0 && !s_abort && !wait_count(&row_states[row], static_cast<unsigned>(SJ))) {
         report(a.status, kStatusWaitTimeout);
         s_abort = 1;
       }
       __syncwarp();
-      if (tid == kStepProducer * 32) SPT(9);
-      if (!s_abort) {
-        const long long rb = static_cast<long long>(row) * S;
-        for (int i0 = fw; i0 < nglb; i0 += 4 * nfw) {
-          float mm[4], ll[4], uu[4][DPH];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int i = i0 + c * nfw;
-            mm[c] = neg_inf();
-            ll[c] = 0.f;
-            if (i < nglb) {
-              const long long o = rb + s_glb[i];
-              mm[c] = __ldcg(a.sm + o);
-              ll[c] = __ldcg(a.sl + o);
-              const float4* up = reinterpret_cast<const float4*>(a.su + o * D + (lane & 15) * DPH);
-              const float4 x0 = __ldcg(up), x1 = __ldcg(up + 1);
-              uu[c][0] = x0.x; uu[c][1] = x0.y; uu[c][2] = x0.z; uu[c][3] = x0.w;
-              uu[c][4] = x1.x; uu[c][5] = x1.y; uu[c][6] = x1.z; uu[c][7] = x1.w;
-            } else {
-#pragma unroll
-              for (int j = 0; j < DPH; ++j) uu[c][j] = 0.f;
-            }
-          }
-#pragma unroll
-          for (int c = 0; c < 4; ++c) fold_state(wm, wl, wu, mm[c], ll[c], uu[c]);
+    };
+    // Ask L1 for this warp's buffered states (lane l: 128-byte line l % 5 of
+    // fold l / 5), to be folded once its row-local blocks are done.
+    auto prefetch_buffered = [&]() {
+      if (s_abort) return;
+      for (int i0 = fw; i0 < nglb; i0 += 6 * nfw) {
+        const int f = lane / 5, line = lane % 5;
+        const int slot = f < 6 ? fold_slot(i0 + f * nfw) : -1;
+        if (slot >= 0) {
+          const float* p = line < 4 ? a.su + (rb + slot) * D + line * 32 : a.sm + rb + slot;
+          asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+          if (line == 4) asm volatile("prefetch.global.L1 [%0];" ::"l"(a.sl + rb + slot));
         }
       }
-      if (tid == kStepProducer * 32) SPT(23);
+    };
+    auto fold_buffered = [&]() {
+      if (s_abort) return;
+      for (int i0 = fw; i0 < nglb; i0 += 4 * nfw) {
+        float mm[4], ll[4], uu[4][DPH];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int slot = fold_slot(i0 + c * nfw);
+          mm[c] = neg_inf();
+          ll[c] = 0.f;
+          if (slot >= 0) {
+            const long long o = rb + slot;
+            // Through L1 (where prefetch_buffered put them): this SM reads
+            // these lines only after the row_states acquire of this call.
+            mm[c] = __ldca(a.sm + o);
+            ll[c] = __ldca(a.sl + o);
+            const float4* up = reinterpret_cast<const float4*>(a.su + o * D + (lane & 15) * DPH);
+            const float4 x0 = __ldca(up), x1 = __ldca(up + 1);
+            uu[c][0] = x0.x; uu[c][1] = x0.y; uu[c][2] = x0.z; uu[c][3] = x0.w;
+            uu[c][4] = x1.x; uu[c][5] = x1.y; uu[c][6] = x1.z; uu[c][7] = x1.w;
+          } else {
+#pragma unroll
+            for (int j = 0; j < DPH; ++j) uu[c][j] = 0.f;
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) fold_state(wm, wl, wu, mm[c], ll[c], uu[c]);
+      }
+    };
+    if (warp == kStepProducer) {
+      if (lane == 0) SPT(123);
+      // Row-local block i goes to stage i % NS, so that each consumer folds
+      // a fixed subsequence of the list in order: the result does not depend
+      // on timing.
+      for (int base = 0; base < nloc && !s_abort; base += NS) {
+        bool done = lane >= NS || base + lane >= nloc;
+        const unsigned long long t0 = global_ns();
+        while (!__all_sync(kFull, done) && !s_abort) {
+          if (!done && lane_free()) {
+            fill_lane(kItemLocal + base + lane, 1, mh, 0, s_loc[base + lane]);
+            done = true;
+          }
+          if (global_ns() - t0 > c_wait_ns) {
+            if (lane == 0) report(a.status, kStatusWaitTimeout);
+            s_abort = 1;
+          }
+        }
+      }
+      if (lane == 0) SPT(8);
+      produce_ends();
+      if (lane == 0) SPT(23);
+    } else if (warp < NS) {
+      // Consumers: the row-local blocks first (the critical path), then
+      // their share of the buffered states, prefetched into L1 meanwhile.
+      wait_buffered();
+      prefetch_buffered();
+      consume(std::true_type{}, qrow, wm, wl, wu);
+      if (lane == 0 && warp == 0) SPT(24);
+      fold_buffered();
+      if (lane == 0 && warp == 0) SPT(9);
+    } else {
+      wait_buffered();
+      fold_buffered();
     }
     if (lane == 0) { s_wm[warp] = wm; s_wl[warp] = wl; }
     if (lane < 16) store_vec<DPH>(&s_wu[warp][lane * DPH], wu);
@@ -858,12 +989,19 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
 #endif
   if (tid == 0) {
     __threadfence();
-    if (atomicAdd(ctas_done, 1u) == static_cast<unsigned>(grid) - 1) {
+    s_last = atomicAdd(ctas_done, 1u) == static_cast<unsigned>(grid) - 1;
+  }
+  __syncthreads();
+  if (s_last) {
+    // Every other CTA is done: zero the serial tags and the control block.
+    if (serial)
+      for (int i = tid; i < hq * K; i += kStepThreads) a.sel_tag[i] = 0;
+    if (tid == 0) {
       for (int i = 0; i < hkv + 2 * hq; ++i) atomicExch(a.ctrl + i, 0u);
       atomicExch(ctas_done, 0u);
       SPAN_END();
-      __threadfence();
     }
+    __threadfence();
   }
 }
 

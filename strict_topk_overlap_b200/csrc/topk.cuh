@@ -17,6 +17,12 @@
 
 namespace stk {
 
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const void* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // ------------------------------------------------------------------ Top-K
 
 __device__ __forceinline__ unsigned long long order_key(double x) {
@@ -332,8 +338,23 @@ __device__ __forceinline__ unsigned block_exclusive_scan(unsigned v, unsigned* w
 // interval bounds are read through L2 (ld.global.cg), so they may come from
 // other CTAs of the calling kernel. Writes the row's IDs ascending (and,
 // with a.keys_out, their exact order keys).
-template <int E, int NT>
-__device__ void bounded_select_core(const SelectArgs& a, int row, const float* qsm, bool q_staged) {
+// With kPoll, the row's intervals are still being written by other CTAs of
+// the calling kernel, each as one 8-byte store into a slot that was zero:
+// a slot reads zero until its interval lands (no valid interval is all-zero
+// bits: its lower end, rounded down, is never +0), so each thread re-reads
+// its zero slots until they fill (bounded by the wait limit).
+// ids_smem (optional): the IDs are also written there, in output order.
+// hook (optional): hook.sure_in(id) runs once per block known to be selected
+// as soon as the intervals classify it (before any exact rescoring), and
+// hook.selected(pos, id, was_sure_in) once per selected block as its output
+// position is written; both on the thread that owns the block.
+struct NoSelectHook {
+  __device__ void sure_in(int) const {}
+  __device__ void selected(int, int, bool) const {}
+};
+template <int E, int NT, bool kPoll = false, typename Hook = NoSelectHook>
+__device__ void bounded_select_core(const SelectArgs& a, int row, const float* qsm, bool q_staged,
+                                    int* ids_smem = nullptr, const Hook& hook = Hook()) {
   static_assert(NT % 32 == 0 && NT <= 512 && kHistBins % NT == 0, "selection block shape");
   constexpr int NW = NT / 32;
   __shared__ unsigned hist[kHistBins];  // low 16 bits: lower ends; high 16 bits: upper ends
@@ -364,16 +385,53 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
     if (tid == 0) { s_bt = 0; s_bu = 0; }
     float lo_[E], up_[E];
     float mn = inf, mx = -inf;
+    if constexpr (kPoll) {
+      unsigned long long raw[E];
 #pragma unroll
-    for (int j = 0; j < E; ++j) {
-      lo_[j] = inf;
-      up_[j] = -inf;
-      if (beg + j < n) {
-        const float2 v = __ldcg(src + beg + j);
-        lo_[j] = v.x;
-        up_[j] = v.y;
-        if (v.x > -inf) mn = fminf(mn, v.x);
-        if (v.y < inf) mx = fmaxf(mx, v.y);
+      for (int j = 0; j < E; ++j) raw[j] = beg + j < n ? ld_relaxed_gpu_u64(src + beg + j) : 1ull;
+      bool missing = false;
+#pragma unroll
+      for (int j = 0; j < E; ++j) missing |= raw[j] == 0ull;
+      if (missing) {
+        const unsigned long long t0 = global_ns();
+        while (missing) {
+          __nanosleep(100);
+          missing = false;
+#pragma unroll
+          for (int j = 0; j < E; ++j) {
+            if (raw[j] == 0ull) raw[j] = ld_relaxed_gpu_u64(src + beg + j);
+            missing |= raw[j] == 0ull;
+          }
+          if (missing && global_ns() - t0 > c_wait_ns) {
+            report(a.status, kStatusWaitTimeout);
+            break;
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        lo_[j] = inf;
+        up_[j] = -inf;
+        if (beg + j < n) {
+          lo_[j] = __uint_as_float(static_cast<unsigned>(raw[j]));
+          up_[j] = __uint_as_float(static_cast<unsigned>(raw[j] >> 32));
+          if (raw[j] == 0ull) { lo_[j] = -inf; up_[j] = inf; }
+          if (lo_[j] > -inf) mn = fminf(mn, lo_[j]);
+          if (up_[j] < inf) mx = fmaxf(mx, up_[j]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        lo_[j] = inf;
+        up_[j] = -inf;
+        if (beg + j < n) {
+          const float2 v = __ldcg(src + beg + j);
+          lo_[j] = v.x;
+          up_[j] = v.y;
+          if (v.x > -inf) mn = fminf(mn, v.x);
+          if (v.y < inf) mx = fmaxf(mx, v.y);
+        }
       }
     }
 #pragma unroll
@@ -397,7 +455,11 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
 
     if (n == K) {
       // Everything is selected.
-      for (int i = tid; i < n; i += NT) out[i] = a.id_base + i;
+      for (int i = tid; i < n; i += NT) {
+        out[i] = a.id_base + i;
+        if (ids_smem) ids_smem[i] = a.id_base + i;
+        hook.selected(i, a.id_base + i, false);
+      }
     } else {
 #pragma unroll
       for (int j = 0; j < E; ++j) {
@@ -443,6 +505,9 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
           n_unc += cls[j] == kClsUnc;
         }
       }
+#pragma unroll
+      for (int j = 0; j < E; ++j)
+        if (cls[j] == kClsIn) hook.sure_in(a.id_base + beg + j);
       const unsigned packed = (n_in << 16) | n_unc;
       const unsigned ex = block_exclusive_scan<NT>(packed, wsum[1], &tot);
       const int total_in = static_cast<int>(tot >> 16), total_unc = static_cast<int>(tot & 0xffffu);
@@ -474,6 +539,11 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
           key[j] = cls[j] == kClsIn ? ~0ull : (cls[j] == kClsUnc ? __ldcg(scratch + beg + j) : 0ull);
         const int base = a.id_base;
         select_registers<E>(key, n, K, [base](int i) { return base + i; }, out, nullptr);
+        __syncthreads();  // this CTA's ID writes are visible to the whole CTA
+        for (int i = tid; i < K; i += NT) {
+          if (ids_smem) ids_smem[i] = out[i];
+          hook.selected(i, out[i], cls_s[out[i] - a.id_base] == kClsIn);
+        }
       } else {
         unsigned idx = ex & 0xffffu;
         if (need < total_unc) {
@@ -515,8 +585,13 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
         unsigned all;
         unsigned pos = block_exclusive_scan<NT>(mine, wsum[0], &all);
 #pragma unroll
-        for (int j = 0; j < E; ++j)
-          if (sel[j]) out[pos++] = a.id_base + beg + j;
+        for (int j = 0; j < E; ++j) {
+          if (sel[j]) {
+            if (ids_smem) ids_smem[pos] = a.id_base + beg + j;
+            hook.selected(static_cast<int>(pos), a.id_base + beg + j, cls[j] == kClsIn);
+            out[pos++] = a.id_base + beg + j;
+          }
+        }
       }
     }
   }

@@ -126,8 +126,8 @@ STK_ESMEM = -2
 
 
 def decode_step_workspace(q, k, topk, predicted=None):
-    """A zeroed workspace for ``decode_step`` (its control block must start at
-    zero; every call leaves it zero again)."""
+    """A zeroed workspace for ``decode_step`` (its control block, score slots
+    and tags must start at zero; every call leaves them zero again)."""
     slots = predicted.shape[1] if predicted is not None else topk
     need = L.load().stk_decode_step_workspace_bytes(q.shape[0], k.shape[0], k.shape[1], slots, q.shape[1])
     return torch.zeros((max(need, 1),), device=q.device, dtype=torch.uint8)
