@@ -355,7 +355,6 @@ def measure_batched(args, rank, world, device, quick=False):
     Returns the object for the JSON line (rank 0) with times as max over ranks."""
     import torch
     from strict_topk_overlap_b200 import paged
-    from strict_topk_overlap_b200.decode import overlap_run
     HQB, PAGE = 16, 16
     gen = torch.Generator().manual_seed(args.seed + 3)
     lengths = [int(x) // 32 * 32 for x in (8192 + torch.rand(args.requests, generator=gen) * (32768 - 8192)).tolist()]
@@ -379,19 +378,18 @@ def measure_batched(args, rank, world, device, quick=False):
     a = paged.select_blocks(q, cache, TOPK).cpu()
     p = swap_rows(a, 0, lambda i: round((1 - overlaps[mine[i // HQB]]) * TOPK), args.seed + 17,
                   blocks_of_row=lambda i: lengths[mine[i // HQB]] // B).to(device)
-    s_sel = torch.cuda.Stream(device, priority=-1)
-    s_pred = torch.cuda.Stream(device)
     eps = 0.01
+    # Both speculative steps run as one launch chain over the whole batch
+    # (paged.speculative_step: selection -> predicted states -> repair).
+    ws_saved = paged.speculative_step_workspace(q, cache, p, "saved")
+    ws_hybrid = paged.speculative_step_workspace(q, cache, p, "repair_fused")
 
     def spec():
-        return overlap_run(lambda: paged.select_blocks(q, cache, TOPK), lambda: paged.partials(q, cache, p),
-                           lambda sel, st: paged.repair_saved(q, cache, sel, p, st), s_sel, s_pred)
+        return paged.speculative_step(q, cache, p, TOPK, workspace=ws_saved)[0]
 
     def relaxed():
-        return overlap_run(lambda: paged.select_blocks(q, cache, TOPK),
-                           lambda: paged.speculate(q, cache, p, mode="hybrid", mass_threshold=0.1, keep_mass=True),
-                           lambda sel, pr: paged.repair_fused(q, cache, sel, p, pr, max_extra_mass=eps).output,
-                           s_sel, s_pred)
+        return paged.speculative_step(q, cache, p, TOPK, variant="repair_fused", max_extra_mass=eps,
+                                      workspace=ws_hybrid)[0]
 
     def serial():
         return paged.exact(q, cache, paged.select_blocks(q, cache, TOPK))
@@ -625,8 +623,8 @@ def main():
     spec = StepSpec(topk=TOPK, method=args.method, max_extra_mass=0.0)
     graph = not args.eager
     dec = [SpeculativeDecoder(s["q"], s["k"], s["v"], s["lo"], s["hi"], s["p"], spec, graph=graph) for s in sets]
-    ser = [SpeculativeDecoder(s["q"], s["k"], s["v"], s["lo"], s["hi"], s["p"], spec, serial=True, graph=graph)
-           for s in sets]
+    ser = [SpeculativeDecoder(s["q"], s["k"], s["v"], s["lo"], s["hi"], s["p"], spec, serial=True, graph=graph,
+                              fused=True) for s in sets]
     # The same steps as launch chains (scorer -> Top-K -> states / exact ->
     # repair): the serial baseline is the faster of the two serial forms.
     ser_chain = [SpeculativeDecoder(s["q"], s["k"], s["v"], s["lo"], s["hi"], s["p"], spec, serial=True, graph=graph,

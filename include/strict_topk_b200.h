@@ -304,6 +304,31 @@ STK_API int stk_decode_step(const stk_kv* kv, const void* q, int q_dtype, const 
                             int topk, const void* pred, int pred64, int sp, int32_t* selected, float* out,
                             void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
+/* Workspace (bytes) for stk_speculative_step_batched: selection scratch for
+ * total_blocks blocks of hq query heads, the predicted blocks' states of the
+ * R * hq rows and, with hybrid != 0, the hybrid grouping's mask and low
+ * aggregate. */
+STK_API size_t stk_speculative_step_batched_workspace_bytes(int R, int hq, int total_blocks, int sp, int d, int hybrid);
+
+/* The chained speculative step (stk_speculative_step, stk_speculative_step_hybrid)
+ * for a batch of R requests of hq query heads each, dense (R == 1) or paged /
+ * batched (kv->block_offsets [R + 1], total_blocks, max_blocks as in
+ * stk_select_topk); rows = R * hq, request-local block IDs. One stream, one
+ * chain of dependent launches: bound scores -> strict Top-K (selected
+ * [rows, topk]) -> predicted blocks' states -> variant STK_VAR_SAVED: saved
+ * repair (out->out only); STK_VAR_FUSED / STK_VAR_SIGNED_FUSED: hybrid
+ * grouping with mass_threshold, then the guarded repair relaxed by
+ * max_extra_mass (every field of out as in stk_repair). Replaces, per
+ * request, the reference's overlapped step (benchmarks/run_benchmark.py:99-118
+ * with gqa.py:128-137,186-188, or kernels.py:450-501 + fused.py:174-220 /
+ * signed_fused.py:144-193) run over a batch. */
+STK_API int stk_speculative_step_batched(const stk_kv* kv, const void* q, int q_dtype, const float* lo,
+                                         const float* hi, int R, int hq, int total_blocks, int max_blocks, int topk,
+                                         const void* pred, int pred64, int sp, float mass_threshold, int variant,
+                                         float min_remaining, float cancellation_tol, float max_extra_mass,
+                                         int32_t* selected, const stk_repair_out* out, void* workspace,
+                                         size_t workspace_bytes, int32_t* status, void* stream);
+
 /* Workspace (bytes) for stk_speculative_step_hybrid: the saved step's
  * workspace plus the hybrid grouping's high mask and low aggregate. */
 STK_API size_t stk_speculative_step_hybrid_workspace_bytes(int hq, int n, int sp, int d);

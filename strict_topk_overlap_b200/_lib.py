@@ -31,7 +31,8 @@ SYMBOLS = (
     "stk_select_workspace_bytes", "stk_select_topk", "stk_select_topk_static", "stk_merge_candidates", "stk_block_states",
     "stk_merge_states", "stk_reduce_states", "stk_speculate_workspace_bytes", "stk_speculate", "stk_repair",
     "stk_speculative_step_workspace_bytes", "stk_speculative_step", "stk_speculative_step_hybrid_workspace_bytes",
-    "stk_speculative_step_hybrid", "stk_decode_step_workspace_bytes", "stk_decode_step", "stk_build_metadata", "stk_append_token",
+    "stk_speculative_step_hybrid", "stk_speculative_step_batched_workspace_bytes", "stk_speculative_step_batched",
+    "stk_decode_step_workspace_bytes", "stk_decode_step", "stk_build_metadata", "stk_append_token",
     "stk_predict", "stk_group_attention_workspace_bytes", "stk_group_attention", "stk_touch_kv",
 )
 
@@ -83,6 +84,9 @@ _SIGS = {
     "stk_speculative_step_hybrid_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "stk_speculative_step_hybrid": (_I, [C.POINTER(StkKV), _P, _I, _P, _P, _I, _I, _P, _I, _I, _F, _I, _F, _F, _F, _P,
                                          C.POINTER(StkRepairOut), _P, _SZ, _P, _P]),
+    "stk_speculative_step_batched_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
+    "stk_speculative_step_batched": (_I, [C.POINTER(StkKV), _P, _I, _P, _P, _I, _I, _I, _I, _I, _P, _I, _I, _F, _I, _F,
+                                          _F, _F, _P, C.POINTER(StkRepairOut), _P, _SZ, _P, _P]),
     "stk_decode_step_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
     "stk_decode_step": (_I, [C.POINTER(StkKV), _P, _I, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _SZ, _P, _P]),
     "stk_build_metadata": (_I, [C.POINTER(StkKV), _I, _I, _P, _P, _P, _P]),

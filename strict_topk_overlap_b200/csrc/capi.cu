@@ -376,11 +376,143 @@ int stk_repair(const stk_kv* kv, const void* q, int q_dtype, int rows, int hq, c
 
 static size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
+// ------------------------------------------------------------------ chained steps
+// One speculative step as one chain of dependent launches on one stream, for
+// R requests of hq query heads each (rows = R hq): bound scores -> strict
+// Top-K -> states of the predicted blocks (the Top-K kernel's programmatic
+// dependent: it streams the predicted K/V while the selection finishes) ->
+// [hybrid grouping ->] repair. Dense single requests (R = 1, no block
+// offsets) and batched or paged layouts take the same path.
+struct ChainShape {
+  int R, hq, rows, total, max_n;
+  const int32_t* block_offsets;
+};
+
+static int chain_shape(const stk_kv* kv, int R, int hq, const int32_t* block_offsets, int total_blocks,
+                       int max_blocks, ChainShape* c) {
+  if (R <= 0 || hq <= 0) return fail(STK_EINVAL, "R and hq must be positive");
+  if (kv->page_table && !block_offsets) return fail(STK_EINVAL, "a paged layout needs block offsets");
+  c->R = R; c->hq = hq; c->rows = R * hq; c->block_offsets = block_offsets;
+  if (block_offsets) {
+    if (total_blocks <= 0 || max_blocks <= 0) return fail(STK_EINVAL, "total_blocks and max_blocks required");
+    c->total = total_blocks; c->max_n = max_blocks;
+  } else {
+    if (R != 1) return fail(STK_EINVAL, "batched dense requests need block offsets");
+    c->total = kv->n; c->max_n = kv->n;
+  }
+  return 0;
+}
+
+static size_t chain_ws_saved(int rows_sel_hq, int total, int rows, int sp, int d) {
+  const size_t slots = static_cast<size_t>(rows) * sp;
+  return align256(stk_select_workspace_bytes(rows_sel_hq, total)) + 2 * align256(slots * sizeof(float)) +
+         align256(slots * d * sizeof(float));
+}
+static size_t chain_ws_hybrid(int rows_sel_hq, int total, int rows, int sp, int d) {
+  const size_t slots = static_cast<size_t>(rows) * sp;
+  return chain_ws_saved(rows_sel_hq, total, rows, sp, d) + align256(slots) + 2 * align256(rows * sizeof(float)) +
+         2 * align256(static_cast<size_t>(rows) * d * sizeof(float));
+}
+
+// variant STK_VAR_SAVED: saved speculation + saved repair (gqa.py:128-137,
+// 186-188); STK_VAR_FUSED / STK_VAR_SIGNED_FUSED: hybrid speculation with
+// threshold mass_threshold, then the guarded repair (fused.py:176-220,
+// signed_fused.py:144-193) relaxed by max_extra_mass.
+static int chain_step(const stk_kv* kv, const void* q, int q_dtype, const float* lo, const float* hi,
+                      const ChainShape& c, int topk, const void* pred, int pred64, int sp, float mass_threshold,
+                      int variant, float min_remaining, float cancellation_tol, float max_extra_mass,
+                      int32_t* selected, const stk_repair_out* out, void* workspace, size_t workspace_bytes,
+                      int32_t* status, void* stream) {
+  int rc = check_kv(kv, c.hq);
+  if (rc) return rc;
+  if (!q || !lo || !hi || !pred || !selected || !out || !out->out || !workspace || !valid_dtype(q_dtype))
+    return fail(STK_EINVAL, "null pointer or unsupported q dtype");
+  if (sp <= 0) return fail(STK_EINVAL, "empty prediction");
+  const bool hybrid = variant != STK_VAR_SAVED;
+  if (hybrid && variant != STK_VAR_FUSED && variant != STK_VAR_SIGNED_FUSED)
+    return fail(STK_EINVAL, "the hybrid chained step repairs with STK_VAR_FUSED or STK_VAR_SIGNED_FUSED");
+  if (!(mass_threshold >= 0.f && mass_threshold <= 1.f)) return fail(STK_EINVAL, "mass_threshold must be in [0,1]");
+  if (!(max_extra_mass >= 0.f && max_extra_mass <= 1.f)) return fail(STK_EINVAL, "max_extra_mass must be in [0, 1]");
+  if (hybrid && !hybrid_group_fits(sp))
+    return fail(STK_ESMEM, "hybrid grouping of %d predicted blocks per row exceeds the shared-memory plan", sp);
+  const int d = kv->d, rows = c.rows;
+  const size_t need = hybrid ? chain_ws_hybrid(c.hq, c.total, rows, sp, d) : chain_ws_saved(c.hq, c.total, rows, sp, d);
+  if (workspace_bytes < need) return fail(STK_EWS, "chained step workspace too small");
+  unsigned char* w = static_cast<unsigned char*>(workspace);
+  const size_t sel_bytes = stk_select_workspace_bytes(c.hq, c.total);
+  const size_t slots = static_cast<size_t>(rows) * sp;
+  float* pm = reinterpret_cast<float*>(w + align256(sel_bytes));
+  float* pl = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(pm) + align256(slots * sizeof(float)));
+  float* pu = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(pl) + align256(slots * sizeof(float)));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // 1. Bound scores and strict Top-K (the scorer, then the Top-K kernel as its dependent).
+  rc = stk_select_topk(q, q_dtype, lo, hi, c.R, c.hq, kv->hkv, c.block_offsets ? 0 : kv->n, c.block_offsets, c.total,
+                       c.max_n, d, topk, 0, 0, selected, nullptr, w, sel_bytes, status, stream);
+  if (rc) return rc;
+  // 2. States of the predicted blocks, launched as the Top-K kernel's
+  //    dependent: it starts as soon as every Top-K CTA is running and streams
+  //    the predicted K/V while the selection finishes, then holds its own
+  //    completion until the Top-K grid's. With few rows it leaves one SM per
+  //    Top-K CTA and skips the L2 prefetch window (the Top-K kernel beside it
+  //    is latency-bound); with many rows the Top-K grid runs in waves and the
+  //    states kernel takes every SM with its window.
+  const int nsm = sm_count_current();
+  JobArgs a{};
+  a.L = make_layout(kv);
+  a.q = q; a.q_dtype = q_dtype;
+  a.rows = rows; a.hq = c.hq; a.g = c.hq / kv->hkv; a.d = d; a.scale = attn_scale(d);
+  a.ids = pred; a.ids64 = pred64; a.s = sp;
+  a.mode = STK_MODE_FULL; a.m = pm; a.l = pl; a.u = pu; a.status = status;
+  a.chain = 1;
+  const bool few = rows <= nsm / 2;
+  a.sm_skip = few ? rows : 0;
+  a.l2_lean = few ? 1 : 0;
+  rc = launch_jobs(a, kv->kv_dtype, nsm, st);
+  if (rc) return cuda_status(rc, "block_states (chained)");
+  if (!hybrid) {
+    // 3. Saved repair (reuse predicted hits, compute selected misses, merge),
+    //    the states' dependent: its wait covers both the states and Top-K.
+    RepairArgs r{};
+    r.L = a.L;
+    r.q = q; r.q_dtype = q_dtype;
+    r.rows = rows; r.hq = c.hq; r.g = a.g; r.d = d; r.scale = a.scale;
+    r.sel = selected; r.sel64 = 0; r.sa = topk;
+    r.pred = pred; r.pred64 = pred64; r.sp = sp;
+    r.pmode = STK_PRED_SAVED; r.sc = sp;
+    r.pm = pm; r.pl = pl; r.pu = pu;
+    r.variant = STK_VAR_SAVED;
+    r.max_n = c.max_n;
+    r.out = out->out;
+    r.status = status;
+    r.chain = 1;
+    return cuda_status(launch_repair(r, kv->kv_dtype, st), "repair (chained)");
+  }
+  uint8_t* high = reinterpret_cast<uint8_t*>(w + chain_ws_saved(c.hq, c.total, rows, sp, d));
+  float* low_m = reinterpret_cast<float*>(high + align256(slots));
+  float* low_l = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(low_m) + align256(rows * sizeof(float)));
+  float* low_u = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(low_l) + align256(rows * sizeof(float)));
+  float* low_abs = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(low_u) +
+                                            align256(static_cast<size_t>(rows) * d * sizeof(float)));
+  // 3. Hybrid grouping (kernels.py:94-117) as the states' programmatic
+  //    dependent: it waits for their grid, whose completion follows Top-K's.
+  rc = launch_hybrid_group(pm, pl, pu, rows, sp, d, mass_threshold, high, low_m, low_l, low_u, low_abs, st, true);
+  if (rc) return cuda_status(rc, "hybrid_group");
+  // 4. Fused or signed-fused repair, the grouping's programmatic dependent
+  //    (it also reads A, written before the states completed). keep_mass
+  //    aliases the states' (m, l) (kernels.py:450-477), which the extra-mass
+  //    budget reads.
+  stk_prediction ps{};
+  ps.mode = STK_PRED_HYBRID; ps.sc = sp;
+  ps.m = pm; ps.l = pl; ps.u = pu; ps.high = high;
+  ps.low_m = low_m; ps.low_l = low_l; ps.low_u = low_u; ps.low_abs = low_abs;
+  ps.mass_m = pm; ps.mass_l = pl;
+  return repair_entry(kv, q, q_dtype, rows, c.hq, selected, 0, topk, pred, pred64, sp, &ps, variant, min_remaining,
+                      cancellation_tol, max_extra_mass, c.max_n, out, status, stream, 1);
+}
+
 size_t stk_speculative_step_workspace_bytes(int hq, int n, int sp, int d) {
   if (hq <= 0 || n <= 0 || sp <= 0 || d <= 0) return 0;
-  const size_t slots = static_cast<size_t>(hq) * sp;
-  return align256(stk_select_workspace_bytes(hq, n)) + 2 * align256(slots * sizeof(float)) +
-         align256(slots * d * sizeof(float));
+  return chain_ws_saved(hq, n, hq, sp, d);
 }
 
 int stk_speculative_step(const stk_kv* kv, const void* q, int q_dtype, const float* lo, const float* hi, int hq,
@@ -389,54 +521,33 @@ int stk_speculative_step(const stk_kv* kv, const void* q, int q_dtype, const flo
   int rc = check_kv(kv, hq);
   if (rc) return rc;
   if (kv->page_table || kv->block_offsets) return fail(STK_EINVAL, "speculative_step takes one dense request");
-  if (!q || !lo || !hi || !pred || !selected || !out || !workspace || !valid_dtype(q_dtype))
-    return fail(STK_EINVAL, "null pointer or unsupported q dtype");
-  if (sp <= 0) return fail(STK_EINVAL, "empty prediction");
-  const int n = kv->n, d = kv->d;
-  if (workspace_bytes < stk_speculative_step_workspace_bytes(hq, n, sp, d))
-    return fail(STK_EWS, "speculative_step workspace too small");
-  unsigned char* w = static_cast<unsigned char*>(workspace);
-  const size_t sel_bytes = stk_select_workspace_bytes(hq, n);
-  const size_t slots = static_cast<size_t>(hq) * sp;
-  float* pm = reinterpret_cast<float*>(w + align256(sel_bytes));
-  float* pl = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(pm) + align256(slots * sizeof(float)));
-  float* pu = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(pl) + align256(slots * sizeof(float)));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // 1. Bound scores and strict Top-K (the scorer, then the Top-K kernel as its dependent).
-  rc = stk_select_topk(q, q_dtype, lo, hi, 1, hq, kv->hkv, n, nullptr, n, n, d, topk, 0, 0, selected, nullptr, w,
-                       sel_bytes, status, stream);
+  ChainShape c{};
+  rc = chain_shape(kv, 1, hq, nullptr, 0, 0, &c);
   if (rc) return rc;
-  // 2. States of the predicted blocks, launched as the Top-K kernel's
-  //    dependent: it starts as soon as every Top-K CTA is running and streams
-  //    the predicted K/V while the selection finishes, then holds its own
-  //    completion until the Top-K grid's.
-  JobArgs a{};
-  a.L = make_layout(kv);
-  a.q = q; a.q_dtype = q_dtype;
-  a.rows = hq; a.hq = hq; a.g = hq / kv->hkv; a.d = d; a.scale = attn_scale(d);
-  a.ids = pred; a.ids64 = pred64; a.s = sp;
-  a.mode = STK_MODE_FULL; a.m = pm; a.l = pl; a.u = pu; a.status = status;
-  a.chain = 1;
-  a.sm_skip = hq;  // one Top-K CTA per selection row
-  a.l2_lean = 1;   // no L2 window: the Top-K kernel beside it is latency-bound
-  rc = launch_jobs(a, kv->kv_dtype, sm_count_current(), st);
-  if (rc) return cuda_status(rc, "block_states (chained)");
-  // 3. Saved repair (reuse predicted hits, compute selected misses, merge),
-  //    the states' dependent: its wait covers both the states and Top-K.
-  RepairArgs r{};
-  r.L = a.L;
-  r.q = q; r.q_dtype = q_dtype;
-  r.rows = hq; r.hq = hq; r.g = a.g; r.d = d; r.scale = a.scale;
-  r.sel = selected; r.sel64 = 0; r.sa = topk;
-  r.pred = pred; r.pred64 = pred64; r.sp = sp;
-  r.pmode = STK_PRED_SAVED; r.sc = sp;
-  r.pm = pm; r.pl = pl; r.pu = pu;
-  r.variant = STK_VAR_SAVED;
-  r.max_n = n;
-  r.out = out;
-  r.status = status;
-  r.chain = 1;
-  return cuda_status(launch_repair(r, kv->kv_dtype, st), "repair (chained)");
+  stk_repair_out ro{};
+  ro.out = out;
+  return chain_step(kv, q, q_dtype, lo, hi, c, topk, pred, pred64, sp, 0.f, STK_VAR_SAVED, 0.f, 0.f, 0.f, selected,
+                    &ro, workspace, workspace_bytes, status, stream);
+}
+
+size_t stk_speculative_step_batched_workspace_bytes(int R, int hq, int total_blocks, int sp, int d, int hybrid) {
+  if (R <= 0 || hq <= 0 || total_blocks <= 0 || sp <= 0 || d <= 0) return 0;
+  return hybrid ? chain_ws_hybrid(hq, total_blocks, R * hq, sp, d) : chain_ws_saved(hq, total_blocks, R * hq, sp, d);
+}
+
+int stk_speculative_step_batched(const stk_kv* kv, const void* q, int q_dtype, const float* lo, const float* hi, int R,
+                                 int hq, int total_blocks, int max_blocks, int topk, const void* pred, int pred64,
+                                 int sp, float mass_threshold, int variant, float min_remaining,
+                                 float cancellation_tol, float max_extra_mass, int32_t* selected,
+                                 const stk_repair_out* out, void* workspace, size_t workspace_bytes, int32_t* status,
+                                 void* stream) {
+  int rc = check_kv(kv, hq);
+  if (rc) return rc;
+  ChainShape c{};
+  rc = chain_shape(kv, R, hq, kv->block_offsets, total_blocks, max_blocks, &c);
+  if (rc) return rc;
+  return chain_step(kv, q, q_dtype, lo, hi, c, topk, pred, pred64, sp, mass_threshold, variant, min_remaining,
+                    cancellation_tol, max_extra_mass, selected, out, workspace, workspace_bytes, status, stream);
 }
 
 static size_t decode_step_ctrl_bytes(int hq, int hkv) {
@@ -498,9 +609,7 @@ int stk_decode_step(const stk_kv* kv, const void* q, int q_dtype, const float* l
 
 size_t stk_speculative_step_hybrid_workspace_bytes(int hq, int n, int sp, int d) {
   if (hq <= 0 || n <= 0 || sp <= 0 || d <= 0) return 0;
-  const size_t slots = static_cast<size_t>(hq) * sp;
-  return stk_speculative_step_workspace_bytes(hq, n, sp, d) + align256(slots) + 2 * align256(hq * sizeof(float)) +
-         2 * align256(static_cast<size_t>(hq) * d * sizeof(float));
+  return chain_ws_hybrid(hq, n, hq, sp, d);
 }
 
 int stk_speculative_step_hybrid(const stk_kv* kv, const void* q, int q_dtype, const float* lo, const float* hi, int hq,
@@ -511,62 +620,13 @@ int stk_speculative_step_hybrid(const stk_kv* kv, const void* q, int q_dtype, co
   int rc = check_kv(kv, hq);
   if (rc) return rc;
   if (kv->page_table || kv->block_offsets) return fail(STK_EINVAL, "speculative_step_hybrid takes one dense request");
-  if (!q || !lo || !hi || !pred || !selected || !out || !out->out || !workspace || !valid_dtype(q_dtype))
-    return fail(STK_EINVAL, "null pointer or unsupported q dtype");
-  if (sp <= 0) return fail(STK_EINVAL, "empty prediction");
   if (variant != STK_VAR_FUSED && variant != STK_VAR_SIGNED_FUSED)
     return fail(STK_EINVAL, "speculative_step_hybrid repairs with STK_VAR_FUSED or STK_VAR_SIGNED_FUSED");
-  if (!(mass_threshold >= 0.f && mass_threshold <= 1.f)) return fail(STK_EINVAL, "mass_threshold must be in [0,1]");
-  if (!(max_extra_mass >= 0.f && max_extra_mass <= 1.f)) return fail(STK_EINVAL, "max_extra_mass must be in [0, 1]");
-  if (!hybrid_group_fits(sp))
-    return fail(STK_ESMEM, "hybrid grouping of %d predicted blocks per row exceeds the shared-memory plan", sp);
-  const int n = kv->n, d = kv->d;
-  if (workspace_bytes < stk_speculative_step_hybrid_workspace_bytes(hq, n, sp, d))
-    return fail(STK_EWS, "speculative_step_hybrid workspace too small");
-  unsigned char* w = static_cast<unsigned char*>(workspace);
-  const size_t sel_bytes = stk_select_workspace_bytes(hq, n);
-  const size_t slots = static_cast<size_t>(hq) * sp;
-  float* pm = reinterpret_cast<float*>(w + align256(sel_bytes));
-  float* pl = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(pm) + align256(slots * sizeof(float)));
-  float* pu = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(pl) + align256(slots * sizeof(float)));
-  uint8_t* high = reinterpret_cast<uint8_t*>(w + stk_speculative_step_workspace_bytes(hq, n, sp, d));
-  float* low_m = reinterpret_cast<float*>(high + align256(slots));
-  float* low_l = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(low_m) + align256(hq * sizeof(float)));
-  float* low_u = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(low_l) + align256(hq * sizeof(float)));
-  float* low_abs = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(low_u) +
-                                            align256(static_cast<size_t>(hq) * d * sizeof(float)));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // 1. Bound scores and strict Top-K.
-  rc = stk_select_topk(q, q_dtype, lo, hi, 1, hq, kv->hkv, n, nullptr, n, n, d, topk, 0, 0, selected, nullptr, w,
-                       sel_bytes, status, stream);
+  ChainShape c{};
+  rc = chain_shape(kv, 1, hq, nullptr, 0, 0, &c);
   if (rc) return rc;
-  // 2. Predicted blocks' full states as the Top-K kernel's dependent, as in
-  //    stk_speculative_step.
-  JobArgs a{};
-  a.L = make_layout(kv);
-  a.q = q; a.q_dtype = q_dtype;
-  a.rows = hq; a.hq = hq; a.g = hq / kv->hkv; a.d = d; a.scale = attn_scale(d);
-  a.ids = pred; a.ids64 = pred64; a.s = sp;
-  a.mode = STK_MODE_FULL; a.m = pm; a.l = pl; a.u = pu; a.status = status;
-  a.chain = 1;
-  a.sm_skip = hq;
-  a.l2_lean = 1;
-  rc = launch_jobs(a, kv->kv_dtype, sm_count_current(), st);
-  if (rc) return cuda_status(rc, "block_states (chained)");
-  // 3. Hybrid grouping (kernels.py:94-117) as the states' programmatic
-  //    dependent: it waits for their grid, whose completion follows Top-K's.
-  rc = launch_hybrid_group(pm, pl, pu, hq, sp, d, mass_threshold, high, low_m, low_l, low_u, low_abs, st, true);
-  if (rc) return cuda_status(rc, "hybrid_group");
-  // 4. Fused or signed-fused repair, the grouping's programmatic dependent
-  //    (it also reads A, written before the states completed). keep_mass aliases the states' (m, l)
-  //    (kernels.py:450-477), which the extra-mass budget reads.
-  stk_prediction ps{};
-  ps.mode = STK_PRED_HYBRID; ps.sc = sp;
-  ps.m = pm; ps.l = pl; ps.u = pu; ps.high = high;
-  ps.low_m = low_m; ps.low_l = low_l; ps.low_u = low_u; ps.low_abs = low_abs;
-  ps.mass_m = pm; ps.mass_l = pl;
-  return repair_entry(kv, q, q_dtype, hq, hq, selected, 0, topk, pred, pred64, sp, &ps, variant, min_remaining,
-                      cancellation_tol, max_extra_mass, n, out, status, stream, 1);
+  return chain_step(kv, q, q_dtype, lo, hi, c, topk, pred, pred64, sp, mass_threshold, variant, min_remaining,
+                    cancellation_tol, max_extra_mass, selected, out, workspace, workspace_bytes, status, stream);
 }
 
 static int metadata_rows(const stk_kv* kv, int R, int total) {

@@ -207,12 +207,16 @@ class SpeculativeDecoder:
     repair) is captured once and replayed as one CUDA-graph launch."""
 
     def __init__(self, q, k, v, lo, hi, predicted, spec: StepSpec, *, graph: bool = True, serial: bool = False,
-                 chained: bool = True, fused: bool = True):
+                 chained: bool = True, fused: bool | None = None):
         self.q, self.k, self.v, self.lo, self.hi, self.predicted = q, k, v, lo, hi, predicted
         self.spec = spec
         self.serial = serial
-        # The saved method and the serial step run as one persistent launch
-        # (decode_step) where the shape fits its plan.
+        # The saved method runs as one persistent launch (decode_step) where
+        # the shape fits its plan. The serial step takes the launch chain by
+        # default (selection, then exact attention: measured faster than the
+        # fused serial launch at config 1); fused=True asks for the fused one.
+        if fused is None:
+            fused = not serial
         self.fused = fused and (serial or spec.method in ("saved", "light"))
         self._fws = decode_step_workspace(q, k, spec.topk, None if serial else predicted) if self.fused else None
         # The saved and hybrid (repair_fused, signed_fused) methods run as one

@@ -294,3 +294,55 @@ def shard_requests(lengths, world):
         shards[r].append(i)
         load[r] += int(lengths[i])
     return [sorted(s) for s in shards]
+
+_STEP_VARIANTS = {"saved": L.VAR_SAVED, "repair_fused": L.VAR_FUSED, "signed_fused": L.VAR_SIGNED_FUSED}
+
+
+def speculative_step_workspace(q, cache: PagedKVCache, predicted, variant="saved"):
+    """Workspace for ``speculative_step`` (selection scratch, the predicted
+    blocks' states and, for the hybrid variants, the grouping's mask and low
+    aggregate)."""
+    hq = _check_q(q, cache)
+    need = L.load().stk_speculative_step_batched_workspace_bytes(
+        cache.requests, hq, cache.total_blocks, predicted.shape[1], cache.dim, int(variant != "saved"))
+    return torch.empty((max(need, 1),), device=q.device, dtype=torch.uint8)
+
+
+def speculative_step(q, cache: PagedKVCache, predicted, topk, *, variant="saved", mass_threshold=0.1,
+                     min_remaining=1.e-3, cancellation_tol=1.e-5, max_extra_mass=0., workspace=None):
+    """One speculative decode step of the whole batch as one chain of
+    dependent launches on the current stream (stk_speculative_step_batched):
+    strict Top-K selection, the predicted blocks' states while the selection
+    finishes, then the saved repair (``variant="saved"``: equal to
+    select_blocks, partials and repair_saved in sequence) or the hybrid
+    grouping and the guarded repair (``"repair_fused"`` / ``"signed_fused"``:
+    equal to select_blocks, speculate(mode="hybrid", keep_mass=True) and
+    repair_fused / the signed fused repair, relaxed by ``max_extra_mass``).
+    Returns (output FP32 [rows, D], selected int32 [rows, topk])."""
+    hq = _check_q(q, cache)
+    _check_ids(predicted, q)
+    if variant not in _STEP_VARIANTS:
+        raise ValueError(f"variant must be one of {sorted(_STEP_VARIANTS)}")
+    if not 0 <= max_extra_mass <= 1:
+        raise ValueError("max_extra_mass must be in [0, 1]")
+    rows, d = q.shape
+    dev = q.device
+    if workspace is None:
+        workspace = speculative_step_workspace(q, cache, predicted, variant)
+    selected = torch.empty((rows, topk), device=dev, dtype=torch.int32)
+    out = torch.empty((rows, d), device=dev, dtype=torch.float32)
+    flags = torch.empty((rows,), device=dev, dtype=torch.bool)
+    remaining = torch.empty((rows,), device=dev, dtype=torch.float32)
+    approx = torch.empty_like(flags)
+    extra = torch.empty_like(remaining)
+    ro = L.StkRepairOut(out.data_ptr(), flags.data_ptr(), remaining.data_ptr(), approx.data_ptr(), extra.data_ptr(),
+                        None, None)
+    kv = cache.kv()
+    rc = L.load().stk_speculative_step_batched(
+        C.byref(kv), q.data_ptr(), L.dtype_code(q), cache.lo.data_ptr(), cache.hi.data_ptr(), cache.requests, hq,
+        cache.total_blocks, cache.max_blocks, topk, predicted.data_ptr(), L.id_is64(predicted), predicted.shape[1],
+        float(mass_threshold), _STEP_VARIANTS[variant], float(min_remaining), float(cancellation_tol),
+        float(max_extra_mass), selected.data_ptr(), C.byref(ro), workspace.data_ptr(), workspace.numel(),
+        L.status_ptr(), L.stream_of(q))
+    L.check(rc, "speculative_step (batched)")
+    return out, selected

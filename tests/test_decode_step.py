@@ -149,18 +149,22 @@ def test_fused_step_rejects_shapes_outside_its_plan():
 
 
 def test_decoder_uses_fused_step():
-    """SpeculativeDecoder runs the saved method and the serial step through
-    the fused kernel where the shape fits, with the same results."""
+    """SpeculativeDecoder runs the saved method through the fused kernel
+    where the shape fits, and the serial step through it on request (its
+    default is the launch chain), with the same results."""
     from strict_topk_overlap_b200.decode import SpeculativeDecoder, StepSpec
     q, k, v, lo, hi, ids, p = _case(32, 8, 2048, 64, 0.75, seed=21)
     qd, kd, vd, lod, hid, pd = (t.to(DEV) for t in (q, k, v, lo, hi, p))
     spec = SpeculativeDecoder(qd, kd, vd, lod, hid, pd, StepSpec(topk=64))
-    ser = SpeculativeDecoder(qd, kd, vd, lod, hid, pd, StepSpec(topk=64), serial=True)
-    assert spec.fused and ser.fused
-    o1, o2 = spec.step().clone(), ser.step().clone()
+    ser = SpeculativeDecoder(qd, kd, vd, lod, hid, pd, StepSpec(topk=64), serial=True, fused=True)
+    chain = SpeculativeDecoder(qd, kd, vd, lod, hid, pd, StepSpec(topk=64), serial=True)
+    assert spec.fused and ser.fused and not chain.fused
+    o1, o2, o3 = spec.step().clone(), ser.step().clone(), chain.step().clone()
     torch.cuda.synchronize()
-    assert np.array_equal(spec.selected.cpu().numpy(), ids)
-    assert np.array_equal(ser.selected.cpu().numpy(), ids)
+    for d in (spec, ser, chain):
+        assert np.array_equal(d.selected.cpu().numpy(), ids)
     assert (o1 - o2).abs().max().item() <= 1e-5
+    assert (o1 - o3).abs().max().item() <= 1e-5
     spec.close()
     ser.close()
+    chain.close()

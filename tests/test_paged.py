@@ -153,3 +153,30 @@ def test_paged_equals_dense_per_request(batch):
         assert torch.equal(ar, a[r * HQ:(r + 1) * HQ])
         o = gqa.exact(qr, kd, vd, ar)
         assert (o - out[r * HQ:(r + 1) * HQ]).abs().max().item() <= 1e-5
+
+
+@pytest.mark.parametrize("variant", ["saved", "repair_fused", "signed_fused"])
+def test_batched_chained_step_equals_separate_calls(variant):
+    """paged.speculative_step (one launch chain for the whole batch) against
+    the separate batched calls it replaces, and its IDs against the oracle;
+    the strict variants' outputs within the bf16 bar of FP64."""
+    from strict_topk_overlap_b200 import paged
+    q, ks, vs, cache = _batch(seed=7)
+    qd = q.to(DEV)
+    ids = _oracle_ids(q, ks)
+    lengths = [k.shape[1] for k in ks]
+    p = _predicted(ids, lengths, 0.75, seed=3).to(DEV).contiguous()
+    out, sel = paged.speculative_step(qd, cache, p, TOPK, variant=variant)
+    a = paged.select_blocks(qd, cache, TOPK)
+    if variant == "saved":
+        ref = paged.repair_saved(qd, cache, a, p, paged.partials(qd, cache, p))
+    else:
+        pr = paged.speculate(qd, cache, p, mode="hybrid", mass_threshold=0.1, keep_mass=True)
+        if variant == "repair_fused":
+            ref = paged.repair_fused(qd, cache, a, p, pr).output
+        else:
+            ref = paged._repair(qd, cache, a, p, pr, 3)[0]
+    torch.cuda.synchronize()
+    assert np.array_equal(sel.cpu().numpy(), ids)
+    assert (out - ref).abs().max().item() <= 1e-5
+    assert _close(out, _oracle_out(q, ks, vs, ids))
