@@ -737,40 +737,41 @@ def main():
     step_bytes = score_bytes + 2 * blk * upred + 2 * blk * miss + HQ * D * 4
     serial_bytes = score_bytes + 2 * blk * ua + HQ * D * 4
 
-    # End to end through the public API with host buffers: each step's graph
-    # copies q and P in from pinned host memory, runs the step and copies the
-    # output back to pinned host memory; the host reads every step's output
-    # (double-buffered: it waits for step i - 1's copy while step i runs).
+    # End to end through the public API with host buffers: every step copies
+    # its q and P in from pinned host memory and its output back to pinned
+    # host memory (decode.capture_host_steps: the graphs hold `gsteps` such
+    # steps, one per input set); the host reads every step's output, double-
+    # buffered (it reads one graph's outputs while the next graph runs).
     e2e_value = None
     if graph and not args.quick:
+        from strict_topk_overlap_b200.decode import capture_host_steps
         hq_pin = [s["q"].cpu().pin_memory() for s in sets]
         hp_pin = [s["p"].cpu().pin_memory() for s in sets]
-        hout = [torch.empty(HQ, D, dtype=torch.float32).pin_memory() for _ in range(nsets)]
-        for j in range(nsets):
-            dec[j].bind_host(hq_pin[j], hp_pin[j], hout[j])
-        evs = [torch.cuda.Event() for _ in range(nsets)]
+        houts = [[torch.empty(HQ, D, dtype=torch.float32).pin_memory() for _ in range(gsteps)] for _ in range(2)]
+        hgraphs = [capture_host_steps([dec[j % nsets] for j in range(gsteps)], hq_pin[:gsteps], hp_pin[:gsteps],
+                                      houts[b]) for b in range(2)]
+        evs = [torch.cuda.Event() for _ in range(2)]
 
         def e2e_steps(count):
             sink = 0.0
-            for i in range(count):
-                j = i % nsets
-                dec[j].step_host()
-                evs[j].record()
-                jp = (i - 1) % nsets
+            for i in range(count // gsteps):
+                b = i % 2
+                hgraphs[b].replay()
+                evs[b].record()
                 if i > 0:
-                    evs[jp].synchronize()
-                    sink += float(hout[jp][0, 0])
+                    evs[1 - b].synchronize()
+                    sink += sum(float(h[0, 0]) for h in houts[1 - b])
             torch.cuda.current_stream().synchronize()
             return sink
 
-        e2e_steps(20)
-        n_e2e = max(200, min(K, 5000))
+        e2e_steps(4 * gsteps)
+        n_e2e = max(200, min(K, 5000)) // gsteps * gsteps
         barrier(world)
         t0 = time.perf_counter()
         e2e_steps(n_e2e)
         e2e_s = max_over_ranks(time.perf_counter() - t0, world, device)
         e2e_value = world * n_e2e / e2e_s
-        # The single-step graphs must be replayed again below: re-prime them.
+        del hgraphs
         torch.cuda.synchronize()
 
     sweep = {}
@@ -863,8 +864,8 @@ def main():
             "clocks": clocks,
             "e2e": {"value": e2e_value, "unit": "decode-steps/s", "h2d_bytes_per_step": HQ * D * 2 + HQ * TOPK * 4,
                     "d2h_bytes_per_step": HQ * D * 4,
-                    "path": "SpeculativeDecoder.bind_host/step_host: pinned H2D of q and P, the step and the D2H of "
-                            "the output in one graph per step; the host reads every step's output"},
+                    "path": "decode.capture_host_steps: per step the pinned H2D of q and P, the step and the D2H of "
+                            "its output, graphs of consecutive steps; the host reads every step's output"},
             "gpu_launches": LAUNCHES_PER_STEP.get(args.method, 4) * K * len(reps),
             "cpu_baseline": cpu,
         }

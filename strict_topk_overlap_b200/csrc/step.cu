@@ -846,11 +846,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
     }
     if (serial)
       for (int i = xl + tid; i < K; i += kStepThreads) a.sel_tag[static_cast<long long>(row) * K + i] = s_sel[i] + 1;
-    // The row's score slots go back to zero for the next call.
-    {
-      unsigned long long* slots = reinterpret_cast<unsigned long long*>(a.bounds + static_cast<long long>(row) * n);
-      for (int i = tid; i < n; i += kStepThreads) slots[i] = 0ull;
-    }
     __syncthreads();
     if (serial && tid == 0 && !s_abort) red_relaxed_gpu(&row_ready[row], 1u);
     const int nloc = s_abort ? 0 : s_nloc;
@@ -863,55 +858,41 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
     // The buffered states, once every work CTA has written this row's: every
     // warp but the producer folds its share of the slots, up to four per
     // round trip, while the row-local blocks' copies are in flight.
-    constexpr int nfw = kStepWarps - 1;
-    const int fw = warp < kStepProducer ? warp : warp - 1;
+    // The buffered states are folded by the helper warps 12..15, eight per
+    // memory round trip, in a fixed slot order, while the consumers take the
+    // row-local blocks.
+    constexpr int nfw = kStepWarps - kStepHelper0;
+    const int fw = warp - kStepHelper0;
     const long long rb = static_cast<long long>(row) * S;
-    // Buffer slot of this warp's fold i (serial: xl + i; speculative: P slot
-    // i when its block is in A), or -1.
+    // Buffer slot of fold i (serial: xl + i; speculative: P slot i when its
+    // block is in A), or -1.
     auto fold_slot = [&](int i) {
       if (i >= nglb) return -1;
       if (serial) return xl + i;
       const int id = s_pid[i];
       return (id >= 0 && id < n && ((s_amask[id >> 5] >> (id & 31)) & 1u)) ? i : -1;
     };
-    auto wait_buffered = [&]() {
+    auto fold_buffered = [&]() {
       if (lane == 0 && nglb > 0 && !s_abort && !wait_count(&row_states[row], static_cast<unsigned>(SJ))) {
         report(a.status, kStatusWaitTimeout);
         s_abort = 1;
       }
       __syncwarp();
-    };
-    // Ask L1 for this warp's buffered states (lane l: 128-byte line l % 5 of
-    // fold l / 5), to be folded once its row-local blocks are done.
-    auto prefetch_buffered = [&]() {
       if (s_abort) return;
-      for (int i0 = fw; i0 < nglb; i0 += 6 * nfw) {
-        const int f = lane / 5, line = lane % 5;
-        const int slot = f < 6 ? fold_slot(i0 + f * nfw) : -1;
-        if (slot >= 0) {
-          const float* p = line < 4 ? a.su + (rb + slot) * D + line * 32 : a.sm + rb + slot;
-          asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
-          if (line == 4) asm volatile("prefetch.global.L1 [%0];" ::"l"(a.sl + rb + slot));
-        }
-      }
-    };
-    auto fold_buffered = [&]() {
-      if (s_abort) return;
-      for (int i0 = fw; i0 < nglb; i0 += 4 * nfw) {
-        float mm[4], ll[4], uu[4][DPH];
+      constexpr int kBatch = 8;
+      for (int i0 = fw; i0 < nglb; i0 += kBatch * nfw) {
+        float mm[kBatch], ll[kBatch], uu[kBatch][DPH];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < kBatch; ++c) {
           const int slot = fold_slot(i0 + c * nfw);
           mm[c] = neg_inf();
           ll[c] = 0.f;
           if (slot >= 0) {
             const long long o = rb + slot;
-            // Through L1 (where prefetch_buffered put them): this SM reads
-            // these lines only after the row_states acquire of this call.
-            mm[c] = __ldca(a.sm + o);
-            ll[c] = __ldca(a.sl + o);
+            mm[c] = __ldcg(a.sm + o);
+            ll[c] = __ldcg(a.sl + o);
             const float4* up = reinterpret_cast<const float4*>(a.su + o * D + (lane & 15) * DPH);
-            const float4 x0 = __ldca(up), x1 = __ldca(up + 1);
+            const float4 x0 = __ldcg(up), x1 = __ldcg(up + 1);
             uu[c][0] = x0.x; uu[c][1] = x0.y; uu[c][2] = x0.z; uu[c][3] = x0.w;
             uu[c][4] = x1.x; uu[c][5] = x1.y; uu[c][6] = x1.z; uu[c][7] = x1.w;
           } else {
@@ -920,7 +901,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
           }
         }
 #pragma unroll
-        for (int c = 0; c < 4; ++c) fold_state(wm, wl, wu, mm[c], ll[c], uu[c]);
+        for (int c = 0; c < kBatch; ++c) fold_state(wm, wl, wu, mm[c], ll[c], uu[c]);
       }
     };
     if (warp == kStepProducer) {
@@ -946,17 +927,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
       produce_ends();
       if (lane == 0) SPT(23);
     } else if (warp < NS) {
-      // Consumers: the row-local blocks first (the critical path), then
-      // their share of the buffered states, prefetched into L1 meanwhile.
-      wait_buffered();
-      prefetch_buffered();
       consume(std::true_type{}, qrow, wm, wl, wu);
       if (lane == 0 && warp == 0) SPT(24);
-      fold_buffered();
-      if (lane == 0 && warp == 0) SPT(9);
     } else {
-      wait_buffered();
       fold_buffered();
+      if (warp == kStepHelper0 && lane == 0) SPT(9);
+      // The row's score slots go back to zero for the next call.
+      unsigned long long* slots = reinterpret_cast<unsigned long long*>(a.bounds + static_cast<long long>(row) * n);
+      for (int i = tid - kStepHelper0 * 32; i < n; i += nfw * 32) slots[i] = 0ull;
     }
     if (lane == 0) { s_wm[warp] = wm; s_wl[warp] = wl; }
     if (lane < 16) store_vec<DPH>(&s_wu[warp][lane * DPH], wu);

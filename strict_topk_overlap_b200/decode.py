@@ -353,3 +353,36 @@ def capture_steps(decoders):
             sels.append(sel)
     return graph, outs, sels
 
+def capture_host_steps(decoders, q_hosts, predicted_hosts, out_hosts):
+    """One CUDA graph that runs, for every decoder in turn, the copy of its
+    pinned host inputs (``q_hosts[i]``, ``predicted_hosts[i]``, shaped like
+    its ``q`` and ``predicted``) into its device inputs, its decode step and
+    the copy of the step's output into the pinned ``out_hosts[i]`` (FP32
+    [Hq, D]): the host-facing form of ``capture_steps``. The host reads
+    ``out_hosts`` after synchronising with the stream (or an event recorded
+    after the replay)."""
+    for d, qh, ph, oh in zip(decoders, q_hosts, predicted_hosts, out_hosts):
+        for t, want in ((qh, d.q), (ph, d.predicted)):
+            if t.shape != want.shape or t.dtype != want.dtype or t.is_cuda or not t.is_pinned():
+                raise ValueError("host inputs must be pinned CPU tensors shaped like the device inputs")
+        if oh.is_cuda or not oh.is_pinned() or oh.dtype != torch.float32 or oh.shape != (d.q.shape[0], d.q.shape[1]):
+            raise ValueError("out_hosts must be pinned FP32 CPU tensors [Hq, D]")
+
+    def run():
+        for d, qh, ph, oh in zip(decoders, q_hosts, predicted_hosts, out_hosts):
+            d.q.copy_(qh, non_blocking=True)
+            d.predicted.copy_(ph, non_blocking=True)
+            out, _ = d._run()
+            oh.copy_(out, non_blocking=True)
+    dev = decoders[0].q.device
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        run()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        run()
+    return graph
+

@@ -168,3 +168,29 @@ def test_decoder_uses_fused_step():
     spec.close()
     ser.close()
     chain.close()
+
+
+def test_capture_host_steps_copies_inputs_and_outputs():
+    """capture_host_steps: one graph of several steps, each with its pinned
+    host inputs copied in and its output copied out; new host inputs are
+    picked up on replay and every step's output reaches its host buffer."""
+    from strict_topk_overlap_b200.decode import SpeculativeDecoder, StepSpec, capture_host_steps
+    decs, hq_pin, hp_pin, refs = [], [], [], []
+    for seed in (31, 32):
+        q, k, v, lo, hi, ids, p = _case(16, 4, 512, 32, 0.75, seed=seed)
+        qd, kd, vd, lod, hid, pd = (t.to(DEV) for t in (q, k, v, lo, hi, p))
+        decs.append(SpeculativeDecoder(torch.zeros_like(qd), kd, vd, lod, hid, torch.zeros_like(pd),
+                                       StepSpec(topk=32), graph=False))
+        hq_pin.append(q.pin_memory())
+        hp_pin.append(p.pin_memory())
+        refs.append(OA.attention_fp64(C.as_np(q), C.as_np(k), C.as_np(v), ids))
+    outs = [torch.empty(16, 128, dtype=torch.float32).pin_memory() for _ in decs]
+    g = capture_host_steps(decs, hq_pin, hp_pin, outs)
+    for o in outs:
+        o.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    for o, ref in zip(outs, refs):
+        ok, err = _bar(o, ref)
+        assert ok, err
+    del g
