@@ -76,9 +76,10 @@ def parse():
     ap.add_argument("--graph-steps", type=int, default=8,
                     help="decode steps per CUDA graph in the timed loops (one per input set, like the attention "
                          "calls of consecutive layers of one token step); 1 = one graph per step")
-    ap.add_argument("--workload", choices=("c1", "c2", "batched", "cp"), default="c1",
+    ap.add_argument("--workload", choices=("c1", "c2", "batched", "cp", "kernels"), default="c1",
                     help="c1: BASELINE config 1 (default, the headline, with the config-2, -3 and -4 objects); "
-                         "c2 / batched / cp: only the config-2 / -3 / -4 measurement, as its own line")
+                         "c2 / batched / cp: only the config-2 / -3 / -4 measurement, as its own line; "
+                         "kernels: one untimed eager pass over every kernel family (for profiler captures)")
     ap.add_argument("--requests", type=int, default=64, help="config 3: requests in the whole batch")
     ap.add_argument("--eager", action="store_true",
                     help="launch each step's kernels directly instead of replaying a CUDA graph (for per-kernel "
@@ -583,12 +584,91 @@ def measure_c2(args, device, quick=False):
     return out
 
 
+def run_kernels(args, device):
+    """One eager pass over every kernel family of the library, on config-1
+    inputs (and small config-2 / -3 / -4 shapes), for profiler launch lists
+    and captures: the fused step, the saved, hybrid (fused and signed fused)
+    and compact speculation with their repairs, the split repair, the
+    hierarchical (config 2) calls with the tensor-core group attention, the
+    batched paged chain, metadata building and token append, and the
+    context-parallel candidate and state merges. Nothing is timed."""
+    import torch
+    from strict_topk import gqa, gqa_hierarchical as GH, kernels
+    from strict_topk_overlap_b200 import context_parallel, decode, metadata, paged
+    ran = []
+    s = make_set(args.seed, 0.9, device)
+    q, k, v, lo, hi, p = s["q"], s["k"], s["v"], s["lo"], s["hi"], s["p"]
+    decode.decode_step(q, k, v, lo, hi, TOPK, p)
+    decode.decode_step(q, k, v, lo, hi, TOPK, None)
+    ran += ["decode_step (speculative, serial)"]
+    decode.speculative_step(q, k, v, lo, hi, p, TOPK)
+    for variant in ("repair_fused", "signed_fused"):
+        decode.speculative_step_hybrid(q, k, v, lo, hi, p, TOPK, variant=variant, max_extra_mass=0.01)
+    ran += ["speculative_step", "speculative_step_hybrid (repair_fused, signed_fused)"]
+    a = gqa.select_blocks(q, lo, hi, TOPK)
+    pc = kernels.speculate(q, k, v, p, mode="compact", mass_threshold=0.1)
+    kernels.repair(q, k, v, a, p, pc)
+    gqa.exact(q, k, v, a)
+    ran += ["compact speculation + split repair", "exact"]
+    lo2, hi2 = metadata.build_metadata(k)
+    metadata.append_token(k.clone(), v.clone(), lo2, hi2, k[:, 0, 0].contiguous(), v[:, 0, 0].contiguous(), 5)
+    ran += ["build_metadata", "append_token"]
+    del s, q, k, v, lo, hi, p, a, pc, lo2, hi2
+    torch.cuda.empty_cache()  # a profiler saves and restores what stays allocated
+    # Config 2 (one input set): the hierarchical API and the tensor-core group attention.
+    hq2, hkv2, n2, b2, d2, k2 = 96, 8, 8192, 4, 128, 512
+    gen = torch.Generator(device=device).manual_seed(args.seed + 200)
+    q2 = torch.randn(hq2, d2, device=device, generator=gen).to(torch.bfloat16)
+    kk = (torch.randn(hkv2, n2, b2, d2, device=device, generator=gen)
+          + torch.randn(hkv2, n2, 1, d2, device=device, generator=gen) * 0.5).to(torch.bfloat16)
+    vv = torch.randn(hkv2, n2, b2, d2, device=device, generator=gen).to(torch.bfloat16)
+    lo2, hi2 = kk.amin(dim=2).float(), kk.amax(dim=2).float()
+    a2 = GH.select_blocks_shared(q2, lo2, hi2, k2)
+    g2 = hq2 // hkv2
+    p2 = swap_rows(a2[::g2].cpu(), n2, round(0.2 * k2), args.seed + 300).repeat_interleave(g2, 0).contiguous().to(device)
+    st2 = GH.partials(q2, kk, vv, p2)
+    GH.repair_saved_shared(q2, kk, vv, a2, p2, st2)
+    GH.exact(q2, kk, vv, a2)
+    GH.exact_shared(q2, kk, vv, a2[::g2].contiguous())
+    ran += ["config 2: select_blocks_shared, partials, repair_saved_shared, exact, exact_shared"]
+    del q2, kk, vv, lo2, hi2, a2, p2, st2
+    torch.cuda.empty_cache()
+    # Config 3 shape, 8 requests: the batched paged chain, strict and relaxed.
+    gen = torch.Generator().manual_seed(args.seed + 3)
+    lengths = [int(x) // 32 * 32 for x in (8192 + torch.rand(8, generator=gen) * (32768 - 8192)).tolist()]
+    ks, vs, qs = [], [], []
+    for r, ln in enumerate(lengths):
+        gd = torch.Generator(device=device).manual_seed(r)
+        kt = torch.randn(HKV, ln // B, B, D, device=device, generator=gd)
+        kt += torch.randn(HKV, ln // B, 1, D, device=device, generator=gd) * 0.5
+        ks.append(kt.to(torch.bfloat16))
+        vs.append(torch.randn(HKV, ln // B, B, D, device=device, generator=gd).to(torch.bfloat16))
+        qs.append(torch.randn(16, D, device=device, generator=gd).to(torch.bfloat16))
+    cache = paged.build_paged_cache(ks, vs, 16, generator=torch.Generator().manual_seed(11), device=device)
+    q3 = torch.cat(qs, 0).contiguous()
+    a3 = paged.select_blocks(q3, cache, TOPK).cpu()
+    p3 = swap_rows(a3, 0, 8, args.seed + 17, blocks_of_row=lambda i: lengths[i // 16] // B).to(device)
+    paged.speculative_step(q3, cache, p3, TOPK)
+    paged.speculative_step(q3, cache, p3, TOPK, variant="repair_fused", max_extra_mass=0.01)
+    paged.exact(q3, cache, paged.select_blocks(q3, cache, TOPK))
+    ran += ["config 3 (8 requests): paged speculative_step saved / repair_fused, exact"]
+    del ks, vs, qs, cache, q3
+    torch.cuda.empty_cache()
+    # Config 4 shape on one rank: shard candidates, candidate merge, state reduce and merge.
+    cp = measure_cp(args, 0, 1, device, quick=True)
+    ran += [f"config 4 (one rank): {cp['workload']}"]
+    torch.cuda.synchronize(device)
+    return {"ran": ran}
+
+
 def run_single_workload(args):
     import torch
     rank, world, local = dist_setup("nccl")
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    if args.workload == "c2":
+    if args.workload == "kernels":
+        obj = run_kernels(args, device)
+    elif args.workload == "c2":
         obj = measure_c2(args, device, quick=args.quick)
     else:
         fn = measure_batched if args.workload == "batched" else measure_cp

@@ -73,7 +73,7 @@ struct JobArgs {
   const void* ids;  // [rows, s] block ids (per request)
   int ids64, s;
   const unsigned char* active;  // optional mask
-  int active_mode;              // 0 none, 1 per row [rows], 2 per slot [rows, s]
+  int active_mode;              // 0 none, 1 per row [rows], 2 per slot [rows, s], 3 per slot: int [rows, s] < 0
   int active_invert;            // 1: a set mask entry means "skip"
   const void* pred;             // optional: search ids in pred[row, :sp]; hits are skipped
   int pred64, sp;

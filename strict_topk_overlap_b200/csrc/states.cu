@@ -12,6 +12,8 @@
 // block_state.cuh); misaligned or odd shapes take a plain-load generic kernel
 // with the same math.
 
+#include <algorithm>
+
 #include "block_state.cuh"
 
 namespace stk {
@@ -162,6 +164,7 @@ __global__ void __launch_bounds__(kFastMaxWarps * 32, 1) jobs_fast_kernel(JobArg
       bool act = bid >= 0;
       if (a.active_mode == 1) act = act && ((a.active[row] != 0) != (a.active_invert != 0));
       else if (a.active_mode == 2) act = act && ((a.active[job] != 0) != (a.active_invert != 0));
+      else if (a.active_mode == 3) act = act && reinterpret_cast<const int*>(a.active)[job] < 0;
       else if (a.active_invert) act = false;
       if (act && bid >= request_blocks(a.L, row / a.hq)) {
         report(a.status, kStatusBadBlockId);
@@ -462,13 +465,15 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* m, const float*
 __global__ void __launch_bounds__(256) reduce_states_kernel(const float* m, const float* l, const float* u,
                                                             const unsigned char* include, int s, int d, float* m_out,
                                                             float* l_out, float* u_out) {
-  extern __shared__ __align__(16) float rsm[];  // w[s]
-  __shared__ float sM;
+  // rsm: w[s] (slot weights), then part[8][d] (each warp's numerators).
+  extern __shared__ __align__(16) float rsm[];
   const int row = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int kWarps = 8;
   float* w = rsm;
+  float* part = rsm + ((s + 3) & ~3);
   const long long base = static_cast<long long>(row) * s;
-  if (tid < 32) {
+  if (warp == 0) {
     float M = neg_inf();
     for (int i = lane; i < s; i += 32)
       if (include == nullptr || include[base + i]) M = fmaxf(M, m[base + i]);
@@ -482,24 +487,51 @@ __global__ void __launch_bounds__(256) reduce_states_kernel(const float* m, cons
     }
     z = warp_sum(z);
     if (lane == 0) {
-      sM = M;
       m_out[row] = M;
       l_out[row] = z;
     }
   }
   __syncthreads();
+  // Warp k folds slots k, k + 8, ... (lane: 4 consecutive dims per 128),
+  // four slots' loads in flight at a time; the warps' parts are then added
+  // in warp order, so the result does not depend on timing.
+  for (int d0 = 0; d0 < d; d0 += 128) {
+    const int dd = d0 + 4 * lane;
+    const bool live = dd < d;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i0 = warp; i0 < s; i0 += 4 * kWarps) {
+      float4 x[4];
+      float wi[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int i = i0 + c * kWarps;
+        wi[c] = i < s ? w[i] : 0.f;
+        x[c] = (wi[c] != 0.f && live) ? *reinterpret_cast<const float4*>(u + (base + i) * d + dd)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        acc.x = fmaf(wi[c], x[c].x, acc.x);
+        acc.y = fmaf(wi[c], x[c].y, acc.y);
+        acc.z = fmaf(wi[c], x[c].z, acc.z);
+        acc.w = fmaf(wi[c], x[c].w, acc.w);
+      }
+    }
+    if (live) *reinterpret_cast<float4*>(part + warp * d + dd) = acc;
+  }
+  __syncthreads();
   for (int dd = tid; dd < d; dd += blockDim.x) {
-    const float* ur = u + base * d + dd;
     float acc = 0.f;
-    for (int i = 0; i < s; ++i)
-      if (w[i] != 0.f) acc = fmaf(w[i], ur[static_cast<long long>(i) * d], acc);
+#pragma unroll
+    for (int k = 0; k < kWarps; ++k) acc += part[k * d + dd];
     u_out[static_cast<long long>(row) * d + dd] = acc;
   }
 }
 
 int launch_reduce_states(const float* m, const float* l, const float* u, const unsigned char* include, int rows,
                          int s, int d, float* m_out, float* l_out, float* u_out, cudaStream_t stream) {
-  const size_t smem = static_cast<size_t>(s) * 4;
+  if (d % 4) return -1;  // 16-byte numerator rows
+  const size_t smem = (static_cast<size_t>((s + 3) & ~3) + 8 * static_cast<size_t>(d)) * 4;
   if (smem > 200 * 1024) return -1;
   cudaFuncSetAttribute(reduce_states_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   reduce_states_kernel<<<rows, 256, smem, stream>>>(m, l, u, include, s, d, m_out, l_out, u_out);
@@ -731,8 +763,50 @@ static int launch_fast_d(const JobArgs& a, int num_sms, cudaStream_t stream) {
   }
 }
 
+// The predicted-slot search of a job list whose hits are skipped (the
+// context-parallel shard states): slot_out[job] = the highest pred slot of
+// the row holding the job's block, -1 when none (one warp per job).
+__global__ void __launch_bounds__(256) slot_search_kernel(JobArgs a) {
+  const int lane = threadIdx.x & 31;
+  const long long njobs = static_cast<long long>(a.rows) * a.s;
+  const long long nw = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  for (long long job = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; job < njobs;
+       job += nw) {
+    const int row = static_cast<int>(job / a.s);
+    const long long bid = load_id(a.ids, a.ids64, job);
+    int found = -1;
+    if (bid >= 0)
+      for (int p = lane; p < a.sp; p += 32)
+        if (load_id(a.pred, a.pred64, static_cast<long long>(row) * a.sp + p) == bid) found = max(found, p);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) found = max(found, __shfl_xor_sync(kFull, found, o));
+    if (lane == 0) a.slot_out[job] = found;
+  }
+}
+
 template <typename T>
 static int launch_jobs_t(const JobArgs& a, int num_sms, cudaStream_t stream) {
+  if (a.pred != nullptr && a.slot_out != nullptr && !a.chain && a.active_mode == 0 && !a.active_invert) {
+    // Hits skipped: the slot search first, then the fast kernel over the
+    // misses (active iff slot_out < 0; hits keep no state, as a.pred is set).
+    JobArgs b = a;
+    b.pred = nullptr;
+    if (fast_eligible(b, sizeof(T))) {
+      const long long njobs = static_cast<long long>(a.rows) * a.s;
+      const long long ctas = std::min<long long>((njobs + 7) / 8, static_cast<long long>(num_sms) * 8);
+      slot_search_kernel<<<static_cast<unsigned>(ctas), 256, 0, stream>>>(a);
+      const cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return static_cast<int>(e);
+      b.pred = a.pred;
+      b.active = reinterpret_cast<const unsigned char*>(a.slot_out);
+      b.active_mode = 3;
+      switch (b.mode) {
+        case kModeFull: return launch_fast_d<T, kModeFull>(b, num_sms, stream);
+        case kModeMass: return launch_fast_d<T, kModeMass>(b, num_sms, stream);
+        default: return launch_fast_d<T, kModeFixed>(b, num_sms, stream);
+      }
+    }
+  }
   if (fast_eligible(a, sizeof(T))) {
     switch (a.mode) {
       case kModeFull: return launch_fast_d<T, kModeFull>(a, num_sms, stream);
