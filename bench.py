@@ -577,8 +577,11 @@ def measure_c2(args, device, quick=False):
            "hbm_frac": {"select_shared": meta / (res["select_shared"] * 1e-6) / 1e9 / hbm_peak,
                         "exact": kv_sel / (res["exact"] * 1e-6) / 1e9 / hbm_peak,
                         "exact_shared": kv_sel / (res["exact_shared"] * 1e-6) / 1e9 / hbm_peak},
+           # The serial step's attention over the shared lists is the tensor-core group tile
+           # (exact_shared); the per-head exact is reported beside it.
            "step_us": {"speculative": res["select_shared"] + max(0.0, res["partials"]) + res["repair_saved_shared"],
-                       "serial": res["select_shared"] + res["exact"]},
+                       "serial": res["select_shared"] + res["exact_shared"],
+                       "serial_per_head": res["select_shared"] + res["exact"]},
            "timing": f"each call alone, CUDA graph of {nset} calls on rotating inputs (> L2), CUDA events"}
     del sets
     return out

@@ -386,6 +386,23 @@ STK_API int stk_predict(int policy, const int32_t* step_ids, const unsigned long
                         const int32_t* layer_ids, const unsigned long long* layer_keys, int kl, int rows,
                         int n_blocks, int budget, int32_t* out, int32_t* status, void* stream);
 
+/* Workspace (bytes) for stk_group_repair_saved. */
+STK_API size_t stk_group_repair_saved_workspace_bytes(int hq, int hkv, int sa, int sp, int b, int d);
+
+/* The saved repair for shared lists on the tensor cores: every query head of
+ * a KV group has the same selected IDs (selected [hq, sa] int32, ascending)
+ * and the same predicted IDs (pred [hq, sp] int32), so the misses (A not in
+ * P, from each group's first row) are attended on the group's MMA tile (each
+ * missed block read once per group) and each head folds its own saved
+ * states (pm, pl [hq, sp], pu [hq, sp, d]) of the hits (P slots in A); out
+ * [hq, d] FP32. One dense request, q and K/V both bf16 or both f16, d 64 or
+ * 128, b dividing 256, hq / hkv <= 16. Replaces gqa_hierarchical.py:137-144
+ * repair_saved_shared (its _match_ids, _packed_partials and _groups passes). */
+STK_API int stk_group_repair_saved(const stk_kv* kv, const void* q, int q_dtype, int hq, const int32_t* selected,
+                                   int sa, const int32_t* pred, int sp, const float* pm, const float* pl,
+                                   const float* pu, float* out, void* workspace, size_t workspace_bytes,
+                                   int32_t* status, void* stream);
+
 /* Workspace (bytes) for stk_group_attention. */
 STK_API size_t stk_group_attention_workspace_bytes(int hq, int sa, int b, int d);
 

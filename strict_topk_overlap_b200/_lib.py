@@ -33,7 +33,8 @@ SYMBOLS = (
     "stk_speculative_step_workspace_bytes", "stk_speculative_step", "stk_speculative_step_hybrid_workspace_bytes",
     "stk_speculative_step_hybrid", "stk_speculative_step_batched_workspace_bytes", "stk_speculative_step_batched",
     "stk_decode_step_workspace_bytes", "stk_decode_step", "stk_build_metadata", "stk_append_token",
-    "stk_predict", "stk_group_attention_workspace_bytes", "stk_group_attention", "stk_touch_kv",
+    "stk_predict", "stk_group_repair_saved_workspace_bytes", "stk_group_repair_saved",
+    "stk_group_attention_workspace_bytes", "stk_group_attention", "stk_touch_kv",
 )
 
 
@@ -92,6 +93,8 @@ _SIGS = {
     "stk_build_metadata": (_I, [C.POINTER(StkKV), _I, _I, _P, _P, _P, _P]),
     "stk_append_token": (_I, [C.POINTER(StkKV), _I, _I, _P, _P, _P, _P, _P, _P, _P]),
     "stk_predict": (_I, [_I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P, _P, _P]),
+    "stk_group_repair_saved_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
+    "stk_group_repair_saved": (_I, [C.POINTER(StkKV), _P, _I, _I, _P, _I, _P, _I, _P, _P, _P, _P, _P, _SZ, _P, _P]),
     "stk_group_attention_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "stk_group_attention": (_I, [C.POINTER(StkKV), _P, _I, _I, _P, _I, _P, _P, _SZ, _P, _P]),
     "stk_touch_kv": (_I, [C.POINTER(StkKV), _I, _I, _P, _I, _I, _P, _P]),

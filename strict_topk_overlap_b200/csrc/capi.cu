@@ -710,6 +710,51 @@ int stk_group_attention(const stk_kv* kv, const void* q, int q_dtype, int hq, co
   return cuda_status(launch_merge(m, l, u, nullptr, hq, splits, kv->d, out, st), "group attention merge");
 }
 
+size_t stk_group_repair_saved_workspace_bytes(int hq, int hkv, int sa, int sp, int b, int d) {
+  if (hq <= 0 || hkv <= 0 || sa <= 0 || sp <= 0 || b <= 0 || d <= 0) return 0;
+  const size_t slots = static_cast<size_t>(hq) * group_mma_splits(sa, b);
+  return align256(static_cast<size_t>(hkv) * sa * 4) + align256(static_cast<size_t>(hkv) * 4) +
+         align256(static_cast<size_t>(hkv) * sp) + 2 * align256(slots * sizeof(float)) +
+         align256(slots * d * sizeof(float));
+}
+
+int stk_group_repair_saved(const stk_kv* kv, const void* q, int q_dtype, int hq, const int32_t* selected, int sa,
+                           const int32_t* pred, int sp, const float* pm, const float* pl, const float* pu, float* out,
+                           void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  int rc = check_kv(kv, hq);
+  if (rc) return rc;
+  if (!q || !selected || !pred || !pm || !pl || !pu || !out || !workspace) return fail(STK_EINVAL, "null pointer");
+  if (kv->page_table || kv->block_offsets) return fail(STK_EINVAL, "group repair takes one dense request");
+  if (q_dtype != kv->kv_dtype || (q_dtype != STK_BF16 && q_dtype != STK_F16))
+    return fail(STK_EINVAL, "group repair needs q and K/V in the same 16-bit type (bf16 or f16)");
+  if (kv->d != 64 && kv->d != 128) return fail(STK_EDIM, "group repair supports head dim 64 or 128, not %d", kv->d);
+  const int G = hq / kv->hkv;
+  if (G > 16) return fail(STK_EINVAL, "group repair tiles at most 16 query heads per KV head, not %d", G);
+  if (256 % kv->b) return fail(STK_EINVAL, "block size %d must divide 256", kv->b);
+  if (sa <= 0 || sp <= 0) return fail(STK_EINVAL, "empty block list");
+  if ((reinterpret_cast<uintptr_t>(kv->k) | reinterpret_cast<uintptr_t>(kv->v)) & 15)
+    return fail(STK_EINVAL, "K/V must be 16-byte aligned");
+  if (workspace_bytes < stk_group_repair_saved_workspace_bytes(hq, kv->hkv, sa, sp, kv->b, kv->d))
+    return fail(STK_EWS, "group repair workspace too small");
+  const int splits = group_mma_splits(sa, kv->b);
+  const size_t slots = static_cast<size_t>(hq) * splits;
+  unsigned char* w = static_cast<unsigned char*>(workspace);
+  int* miss = reinterpret_cast<int*>(w);
+  w += align256(static_cast<size_t>(kv->hkv) * sa * 4);
+  int* count = reinterpret_cast<int*>(w);
+  w += align256(static_cast<size_t>(kv->hkv) * 4);
+  unsigned char* hit = w;
+  w += align256(static_cast<size_t>(kv->hkv) * sp);
+  float* sm = reinterpret_cast<float*>(w);
+  w += align256(slots * sizeof(float));
+  float* sl = reinterpret_cast<float*>(w);
+  w += align256(slots * sizeof(float));
+  float* su = reinterpret_cast<float*>(w);
+  return cuda_status(launch_group_repair(make_layout(kv), kv->kv_dtype, q, G, attn_scale(kv->d), selected, sa, pred, sp, pm, pl, pu, miss,
+                                         count, hit, sm, sl, su, out, status, static_cast<cudaStream_t>(stream)),
+                     "group repair");
+}
+
 int stk_touch_kv(const stk_kv* kv, int rows, int hq, const void* ids, int ids64, int s, float* out, void* stream) {
   int rc = check_kv(kv, hq);
   if (rc) return rc;

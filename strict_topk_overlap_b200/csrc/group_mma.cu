@@ -36,6 +36,7 @@ struct GroupArgs {
   int G;             // query heads per KV head (<= 16)
   const int* ids;    // [hkv, sa] shared block list per KV head
   int sa;
+  const int* counts; // optional [hkv]: list length per KV head (the rest of its row is unused)
   float scale;
   int splits;
   float* m;          // [hkv * G, splits]
@@ -97,7 +98,8 @@ __global__ void __launch_bounds__(kGroupWarps * 32) group_mma_kernel(GroupArgs a
   const int B = a.L.b;
   const int bpc = kTokensPerCta / B;                 // blocks per CTA
   const int j0 = split * bpc;
-  const int nb = max(0, min(bpc, a.sa - j0));        // blocks of this CTA
+  const int len = a.counts ? min(a.sa, a.counts[h]) : a.sa;
+  const int nb = max(0, min(bpc, len - j0));         // blocks of this CTA
   const int ntok = nb * B;
   const T* K = static_cast<const T*>(a.L.k);
   const T* V = static_cast<const T*>(a.L.v);
@@ -290,6 +292,171 @@ int launch_group_mma(const KVLayout& L, int kv_dtype, const void* q, int G, cons
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   prefer_shared(kern);
   kern<<<grid, kGroupWarps * 32, smem, stream>>>(a);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ shared saved repair
+// gqa_hierarchical.repair_saved_shared (gqa_hierarchical.py:137-144) for
+// groups whose query heads share one selected list A and one predicted
+// list P: the misses (A not in P) are then the same for every head of a
+// group, so they run on the tensor-core group tile above (each missed block
+// read once per group), and each head folds its own saved states of the hits
+// (P slots whose block is in A). Membership comes from the group's first row.
+
+// Per KV head h (one CTA): the misses of row h * G in A order, their count,
+// and the hit flag of every P slot.
+__global__ void __launch_bounds__(256) group_miss_kernel(const int* sel, int sa, const int* pred, int sp, int G, int n,
+                                                         int* miss, int* count, unsigned char* hit, int* status) {
+  extern __shared__ unsigned gmask[];  // P bits [nw], then A bits [nw]
+  __shared__ int wtot[8];
+  const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nw = (n + 31) / 32;
+  unsigned* pb = gmask;
+  unsigned* ab = gmask + nw;
+  const int* arow = sel + static_cast<long long>(h) * G * sa;
+  const int* prow = pred + static_cast<long long>(h) * G * sp;
+  for (int i = tid; i < 2 * nw; i += blockDim.x) gmask[i] = 0u;
+  __syncthreads();
+  for (int i = tid; i < sp; i += blockDim.x) {
+    const int id = prow[i];
+    if (id >= 0 && id < n) atomicOr(&pb[id >> 5], 1u << (id & 31));
+  }
+  for (int i = tid; i < sa; i += blockDim.x) {
+    const int id = arow[i];
+    if (id >= 0 && id < n) atomicOr(&ab[id >> 5], 1u << (id & 31));
+    else report(status, kStatusBadBlockId);
+  }
+  __syncthreads();
+  for (int i = tid; i < sp; i += blockDim.x) {
+    const int id = prow[i];
+    hit[static_cast<long long>(h) * sp + i] = (id >= 0 && id < n && ((ab[id >> 5] >> (id & 31)) & 1u)) ? 1 : 0;
+  }
+  // Misses in A order: chunks of 256 entries, one ballot per warp.
+  int base = 0;
+  for (int c0 = 0; c0 < sa; c0 += blockDim.x) {
+    const int i = c0 + tid;
+    const int id = i < sa ? arow[i] : -1;
+    const bool m = id >= 0 && id < n && !((pb[id >> 5] >> (id & 31)) & 1u);
+    const unsigned bal = __ballot_sync(kFull, m);
+    if (lane == 0) wtot[warp] = __popc(bal);
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int w = 0; w < (blockDim.x >> 5); ++w) {
+      before += w < warp ? wtot[w] : 0;
+      total += wtot[w];
+    }
+    if (m) miss[static_cast<long long>(h) * sa + base + before + __popc(bal & ((1u << lane) - 1u))] = id;
+    base += total;
+    __syncthreads();
+  }
+  if (tid == 0) count[h] = base;
+}
+
+// Per row r (query head; one CTA of 16 warps): M over the row's hits and
+// the group tile's split states, then every source's weight; warp k folds
+// sources k, k + 16, ... (hits in P-slot order, then splits) with 4
+// consecutive dims per lane, eight sources' loads in flight; the warps'
+// parts add in warp order, so the result does not depend on timing.
+__global__ void __launch_bounds__(512) group_repair_merge_kernel(const float* pm, const float* pl, const float* pu,
+                                                                 const unsigned char* hit, int sp, const float* sm,
+                                                                 const float* sl, const float* su, int splits, int G,
+                                                                 int d, float* out) {
+  extern __shared__ __align__(16) float gms[];  // w[sp + splits], part[16][d]
+  __shared__ float red[16];
+  constexpr int kWarps = 16;
+  constexpr int kBatch = 8;
+  const int r = blockIdx.x, h = r / G;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ns = sp + splits;
+  float* w = gms;
+  float* part = gms + ((ns + 3) & ~3);
+  const unsigned char* hr = hit + static_cast<long long>(h) * sp;
+  const long long pr = static_cast<long long>(r) * sp, srow = static_cast<long long>(r) * splits;
+  auto src_m = [&](int i) { return i < sp ? (hr[i] ? pm[pr + i] : neg_inf()) : sm[srow + i - sp]; };
+  float mx = neg_inf();
+  for (int i = tid; i < ns; i += blockDim.x) mx = fmaxf(mx, src_m(i));
+  mx = warp_max(mx);
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  float M = neg_inf();
+#pragma unroll
+  for (int k = 0; k < kWarps; ++k) M = fmaxf(M, red[k]);
+  __syncthreads();
+  float z = 0.f;
+  for (int i = tid; i < ns; i += blockDim.x) {
+    const float mi = src_m(i);
+    const float wi = (M != neg_inf() && mi != neg_inf()) ? expf(mi - M) : 0.f;
+    w[i] = wi;
+    z += wi * (i < sp ? pl[pr + i] : sl[srow + i - sp]);
+  }
+  z = warp_sum(z);
+  if (lane == 0) red[warp] = z;
+  __syncthreads();
+  float Z = 0.f;
+#pragma unroll
+  for (int k = 0; k < kWarps; ++k) Z += red[k];
+  for (int d0 = 0; d0 < d; d0 += 128) {
+    const int dd = d0 + 4 * lane;
+    const bool live = dd < d;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i0 = warp; i0 < ns; i0 += kBatch * kWarps) {
+      float4 x[kBatch];
+      float wi[kBatch];
+#pragma unroll
+      for (int c = 0; c < kBatch; ++c) {
+        const int i = i0 + c * kWarps;
+        wi[c] = i < ns ? w[i] : 0.f;
+        const float* src = i < sp ? pu + (pr + i) * d : su + (srow + i - sp) * d;
+        x[c] = (wi[c] != 0.f && live) ? *reinterpret_cast<const float4*>(src + dd) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int c = 0; c < kBatch; ++c) {
+        acc.x = fmaf(wi[c], x[c].x, acc.x);
+        acc.y = fmaf(wi[c], x[c].y, acc.y);
+        acc.z = fmaf(wi[c], x[c].z, acc.z);
+        acc.w = fmaf(wi[c], x[c].w, acc.w);
+      }
+    }
+    if (live) *reinterpret_cast<float4*>(part + warp * d + dd) = acc;
+  }
+  __syncthreads();
+  for (int dd = tid; dd < d; dd += blockDim.x) {
+    float U = 0.f;
+#pragma unroll
+    for (int k = 0; k < kWarps; ++k) U += part[k * d + dd];
+    out[static_cast<long long>(r) * d + dd] = U / fmaxf(Z, 1e-30f);
+  }
+}
+
+int launch_group_repair(const KVLayout& L, int kv_dtype, const void* q, int G, float scale, const int* sel, int sa,
+                        const int* pred, int sp, const float* pm, const float* pl, const float* pu, int* miss, int* count,
+                        unsigned char* hit, float* sm, float* sl, float* su, float* out, int* status,
+                        cudaStream_t stream) {
+  const int hkv = L.hkv;
+  const size_t msmem = static_cast<size_t>(2 * ((L.n + 31) / 32)) * 4;
+  if (msmem > 48 * 1024)
+    cudaFuncSetAttribute(group_miss_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(msmem));
+  group_miss_kernel<<<hkv, 256, msmem, stream>>>(sel, sa, pred, sp, G, L.n, miss, count, hit, status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return static_cast<int>(e);
+  GroupArgs a{};
+  a.L = L; a.q = q; a.G = G; a.ids = miss; a.sa = sa; a.counts = count; a.scale = scale;
+  a.splits = group_mma_splits(sa, L.b);
+  a.m = sm; a.l = sl; a.u = su; a.status = status;
+  const size_t smem = group_mma_smem(L.d, 2);
+  const dim3 grid(static_cast<unsigned>(a.splits), static_cast<unsigned>(hkv));
+  void (*kern)(GroupArgs);
+  if (kv_dtype == kBF16) kern = L.d == 64 ? group_mma_kernel<__nv_bfloat16, 64> : group_mma_kernel<__nv_bfloat16, 128>;
+  else kern = L.d == 64 ? group_mma_kernel<__half, 64> : group_mma_kernel<__half, 128>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  prefer_shared(kern);
+  kern<<<grid, kGroupWarps * 32, smem, stream>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return static_cast<int>(e);
+  const size_t gsm = (static_cast<size_t>((sp + a.splits + 3) & ~3) + 16 * static_cast<size_t>(L.d)) * 4;
+  if (gsm > 48 * 1024)
+    cudaFuncSetAttribute(group_repair_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(gsm));
+  group_repair_merge_kernel<<<hkv * G, 512, gsm, stream>>>(pm, pl, pu, hit, sp, sm, sl, su, a.splits, G, L.d, out);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -225,6 +225,10 @@ int launch_select_bounded(const SelectArgs& a, int max_n, cudaStream_t stream);
 int launch_merge_candidates(const MergeArgs& a, cudaStream_t stream);
 size_t group_mma_smem(int d, int esize);
 int group_mma_splits(int sa, int b);
+int launch_group_repair(const KVLayout& L, int kv_dtype, const void* q, int G, float scale, const int* sel, int sa,
+                        const int* pred, int sp, const float* pm, const float* pl, const float* pu, int* miss, int* count,
+                        unsigned char* hit, float* sm, float* sl, float* su, float* out, int* status,
+                        cudaStream_t stream);
 int launch_group_mma(const KVLayout& L, int kv_dtype, const void* q, int G, const int* ids, int sa, float scale,
                      float* m, float* l, float* u, int* status, cudaStream_t stream);
 int launch_build_metadata(const KVLayout& L, int R, int total, int kv_dtype, float* lo, float* hi, cudaStream_t stream);

@@ -46,11 +46,46 @@ def repair_saved(q, k, v, selected, predicted, state):
     return _repair(q, k, v, selected, predicted, state, False)
 
 
+def _group_tile_ok(q, k, selected, predicted):
+    """Shapes the tensor-core group repair takes: q and K/V in one 16-bit
+    dtype, D 64 or 128, blocks dividing 256 tokens, a dense tile of 8..16
+    query heads per KV head, int32 contiguous lists."""
+    hq, d = q.shape
+    hkv, n, b, _ = k.shape
+    g = hq // hkv
+    return (q.dtype == k.dtype and q.dtype in (torch.bfloat16, torch.float16) and d in (64, 128)
+            and 256 % b == 0 and 8 <= g <= 16 and hq % hkv == 0
+            and selected.dtype == torch.int32 and predicted.dtype == torch.int32
+            and selected.is_contiguous() and predicted.is_contiguous())
+
+
 def repair_saved_shared(q, k, v, selected, predicted, state):
-    """Shared selection: every head has identical ordered IDs (caller-validated
-    contract). Membership is resolved per row on chip, so the result equals
-    repair_saved; attention states stay independent for every query head."""
-    return _repair(q, k, v, selected, predicted, state, True)
+    """Shared selection: every head of a KV group has identical ordered IDs
+    (caller-validated contract, as in the reference; membership is taken from
+    each group's first row). Where the group forms a dense tensor-core tile
+    (8..16 query heads per KV head, 16-bit q and K/V, D 64 or 128), the
+    misses are attended on the group's MMA tile, each missed block read once
+    per group, and every head folds its own saved states of the hits
+    (stk_group_repair_saved); other shapes resolve membership per row on
+    chip. Attention states stay independent for every query head."""
+    h, n, b, d, group, sa = gqa._shape(q, k, v, selected)
+    gqa._validate_ids(q, predicted)
+    sp = predicted.shape[1]
+    if state.u.shape != (h, sp, d) or state.m.shape != (h, sp) or state.l.shape != (h, sp):
+        raise ValueError('prediction state shape does not match predicted blocks')
+    if not _group_tile_ok(q, k, selected, predicted):
+        return _repair(q, k, v, selected, predicted, state, True)
+    lib = L.load()
+    out = torch.empty((h, d), device=q.device, dtype=torch.float32)
+    ws_bytes = lib.stk_group_repair_saved_workspace_bytes(h, k.shape[0], sa, sp, b, d)
+    ws = torch.empty((ws_bytes,), device=q.device, dtype=torch.uint8)
+    kv = L.kv_struct(k, v)
+    rc = lib.stk_group_repair_saved(C.byref(kv), q.data_ptr(), L.dtype_code(q), h, selected.data_ptr(), sa,
+                                    predicted.data_ptr(), sp, state.m.contiguous().data_ptr(),
+                                    state.l.contiguous().data_ptr(), state.u.contiguous().data_ptr(), out.data_ptr(),
+                                    ws.data_ptr(), ws_bytes, L.status_ptr(), L.stream_of(q))
+    L.check(rc, "group_repair_saved")
+    return out
 
 
 select_blocks_shared = gqa.select_blocks_shared

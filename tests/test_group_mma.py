@@ -47,3 +47,30 @@ def test_group_attention_matches_per_head_and_oracle(hq, hkv, n, b, d, k, dtype)
     assert (out - per_head).abs().max().item() <= 1e-4
     ref = OA.attention_fp64(q.float().numpy(), kk.float().numpy(), vv.float().numpy(), ids)
     assert (np.abs(out.cpu().numpy() - ref) <= 2e-3 + 1e-2 * np.abs(ref)).all()
+
+
+@pytest.mark.parametrize("hq,hkv,n,b,d,k,sp,nswap,dtype", [
+    (96, 8, 2048, 4, 128, 256, 256, 51, torch.bfloat16),   # config-2 shape, reduced context, 80 % overlap
+    (64, 8, 700, 4, 64, 100, 90, 30, torch.float16),        # 8 heads per group, shorter predicted list
+    (32, 2, 400, 8, 128, 50, 50, 0, torch.bfloat16),        # full overlap: no misses
+])
+def test_group_repair_saved_shared_matches_per_row_and_oracle(hq, hkv, n, b, d, k, sp, nswap, dtype):
+    """repair_saved_shared on the tensor-core group tile (misses once per
+    group, hits per head) against the per-row saved repair on the same
+    inputs and the FP64 oracle over the strict set."""
+    from strict_topk import gqa_hierarchical as gh
+    q, kk, vv, lo, hi = C.synthetic_kv(hq, hkv, n, b, d, dtype, seed=hq + n + 1)
+    ids = OS.select_blocks(C.as_np(q), lo.numpy(), hi.numpy(), k, shared=True)
+    g = hq // hkv
+    pg = C.swap_prediction(torch.from_numpy(np.ascontiguousarray(ids[::g])), n, nswap, seed=hq + 2)[:, :sp]
+    p = pg.repeat_interleave(g, 0).to(torch.int32).contiguous().to(DEV)
+    a = torch.from_numpy(ids).to(torch.int32).contiguous().to(DEV)
+    qd, kd, vd = q.to(DEV), kk.to(DEV), vv.to(DEV)
+    st = gh.partials(qd, kd, vd, p)
+    assert gh._group_tile_ok(qd, kd, a, p)
+    out = gh.repair_saved_shared(qd, kd, vd, a, p, st)
+    per_row = gh.repair_saved(qd, kd, vd, a, p, st)
+    torch.cuda.synchronize()
+    assert (out - per_row).abs().max().item() <= 1e-4
+    ref = OA.attention_fp64(q.float().numpy(), kk.float().numpy(), vv.float().numpy(), ids)
+    assert (np.abs(out.cpu().numpy() - ref) <= 2e-3 + 1e-2 * np.abs(ref)).all()
