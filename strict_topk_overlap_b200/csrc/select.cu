@@ -569,6 +569,109 @@ __global__ void __launch_bounds__(kBWarps * 32) bound_interval_kernel(ScoreArgs 
   if (!mbar_wait(&meta_bar, 0, a.status)) return;  // bounded; the status records a wait that gave up
 
   const int rr = (live && a.block_offsets) ? find_request(a.block_offsets, a.R, static_cast<int>(gb)) - r0 : 0;
+  if constexpr (C == 4) {
+    // D = 128: lane l owns dims [4l, 4l + 4), so every warp-wide 128-bit
+    // load reads one whole 512-byte metadata (or q) row, conflict-free. Per
+    // group of 4 blocks and 4 heads each lane forms 16 partial sums (its 4
+    // dims in order, FP32 FMA on the sign-selected bound); a transposed
+    // butterfly (xor 8, 4, 2, 1) and one xor-16 add leave the total of
+    // (block j, head g) in lanes 4 j + g and 16 + 4 j + g. Every term passes
+    // through at most 4 + 5 roundings, within the D/4 + 2 the radius covers.
+    // Lane b * 4 + p of the lane layout below held block b of the warp; its
+    // request index rr is read from lane 4 b.
+    if (__all_sync(kFull, !live || rr < kQReq)) {
+      const float4* slo4 = reinterpret_cast<const float4*>(slo);
+      const float4* shi4 = reinterpret_cast<const float4*>(shi);
+      const float4* qs4 = reinterpret_cast<const float4*>(qs);
+      const float inf = __int_as_float(0x7f800000);
+#pragma unroll 1
+      for (int grp = 0; grp < 2; ++grp) {
+        const int bb = warp * 8 + grp * 4;  // tile-local first block of the group
+        float gl = 0.f, gu = 0.f;           // group selection: lanes 4 j accumulate block j
+#pragma unroll 1
+        for (int g0 = 0; g0 < G; g0 += 4) {
+          float part[16];
+          float mx[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int rl2 = bb + j;
+            const bool lj = rl2 < nrows;
+            const int rrj = __shfl_sync(kFull, rr, 4 * (grp * 4 + j));
+            const float4 l4 = lj ? slo4[rl2 * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 h4 = lj ? shi4[rl2 * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+            mx[j] = fmaxf(fmaxf(fmaxf(fabsf(l4.x), fabsf(h4.x)), fmaxf(fabsf(l4.y), fabsf(h4.y))),
+                          fmaxf(fmaxf(fabsf(l4.z), fabsf(h4.z)), fmaxf(fabsf(l4.w), fabsf(h4.w))));
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              const float4 q = (lj && g0 + g < G) ? qs4[(rrj * G + g0 + g) * 32 + lane]
+                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+              float acc = q.x * (q.x >= 0.f ? h4.x : l4.x);
+              acc = fmaf(q.y, q.y >= 0.f ? h4.y : l4.y, acc);
+              acc = fmaf(q.z, q.z >= 0.f ? h4.z : l4.z, acc);
+              acc = fmaf(q.w, q.w >= 0.f ? h4.w : l4.w, acc);
+              part[4 * j + g] = acc;
+            }
+          }
+#pragma unroll
+          for (int off = 8; off > 0; off >>= 1) {
+            const bool upper = (lane & off) != 0;
+#pragma unroll
+            for (int i = 0; i < off; ++i) {
+              const float send = upper ? part[i] : part[i + off];
+              const float keep = upper ? part[i + off] : part[i];
+              part[i] = keep + __shfl_xor_sync(kFull, send, off);
+            }
+          }
+          const float sum = part[0] + __shfl_xor_sync(kFull, part[0], 16);
+#pragma unroll
+          for (int off = 8, cnt = 2; off >= 4; off >>= 1, cnt >>= 1) {
+            const bool upper = (lane & off) != 0;
+#pragma unroll
+            for (int i = 0; i < cnt; ++i) {
+              const float send = upper ? mx[i] : mx[i + cnt];
+              const float keep = upper ? mx[i + cnt] : mx[i];
+              mx[i] = fmaxf(keep, __shfl_xor_sync(kFull, send, off));
+            }
+          }
+          float bm = mx[0];
+          bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 16));
+          bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 2));
+          bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 1));
+          const int j = (lane >> 2) & 3, g = lane & 3, head = g0 + g;
+          const int rl2 = bb + j;
+          const bool lj = rl2 < nrows && head < G;
+          const int rrj = __shfl_sync(kFull, rr, 4 * (grp * 4 + j));
+          float lo = 0.f, up = 0.f;
+          if (lj) {
+            const float e = __fadd_ru(__fmul_ru(__fmul_ru(qn1[rrj * G + head], bm), kErrFactor), 0x1p-118f);
+            lo = __fsub_rd(sum, e);
+            up = __fadd_ru(sum, e);
+            if (!(lo <= up)) { lo = -inf; up = inf; }
+          }
+          if (!a.group_select) {
+            if (lane < 16 && lj)
+              out[static_cast<long long>(mh * G + head) * a.total_blocks + row0 + rl2] = make_float2(lo, up);
+          } else {
+            // The group's sum: heads of the chunk (lanes 4 j .. 4 j + 3), then
+            // chunk after chunk, rounded outward at every step.
+            lo = __fadd_rd(lo, __shfl_xor_sync(kFull, lo, 1));
+            up = __fadd_ru(up, __shfl_xor_sync(kFull, up, 1));
+            lo = __fadd_rd(lo, __shfl_xor_sync(kFull, lo, 2));
+            up = __fadd_ru(up, __shfl_xor_sync(kFull, up, 2));
+            gl = __fadd_rd(gl, lo);
+            gu = __fadd_ru(gu, up);
+          }
+        }
+        if (a.group_select && lane < 16 && (lane & 3) == 0 && bb + (lane >> 2) < nrows) {
+          float2 iv = make_float2(gl, gu);
+          if (!(iv.x <= iv.y)) iv = make_float2(-inf, inf);
+          out[static_cast<long long>(mh) * a.total_blocks + row0 + bb + (lane >> 2)] = iv;
+        }
+      }
+      ST(3);
+      return;
+    }
+  }
   float s[GM];
 #pragma unroll
   for (int g = 0; g < GM; ++g) s[g] = 0.f;
