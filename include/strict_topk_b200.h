@@ -396,7 +396,7 @@ STK_API size_t stk_group_repair_saved_workspace_bytes(int hq, int hkv, int sa, i
  * missed block read once per group) and each head folds its own saved
  * states (pm, pl [hq, sp], pu [hq, sp, d]) of the hits (P slots in A); out
  * [hq, d] FP32. One dense request, q and K/V both bf16 or both f16, d 64 or
- * 128, b dividing 256, hq / hkv <= 16. Replaces gqa_hierarchical.py:137-144
+ * 128, b dividing 64, hq / hkv <= 16. Replaces gqa_hierarchical.py:137-144
  * repair_saved_shared (its _match_ids, _packed_partials and _groups passes). */
 STK_API int stk_group_repair_saved(const stk_kv* kv, const void* q, int q_dtype, int hq, const int32_t* selected,
                                    int sa, const int32_t* pred, int sp, const float* pm, const float* pl,
@@ -409,7 +409,7 @@ STK_API size_t stk_group_attention_workspace_bytes(int hq, int sa, int b, int d)
 /* Attention of every query head over its KV group's shared block list, on
  * the tensor cores: the hq / hkv (<= 16) query heads of a KV head form one
  * MMA tile, so each listed K/V block is read once per group. One dense
- * request, q and K/V both bf16 or both f16, d 64 or 128, b dividing 256;
+ * request, q and K/V both bf16 or both f16, d 64 or 128, b dividing 64;
  * group_ids [hkv, sa] int32; out [hq, d] FP32 (normalised). Replaces, for
  * shared lists (select_blocks_shared), the per-head partials and merge of
  * gqa_hierarchical.py:55-112 and gqa.py:140-142. */

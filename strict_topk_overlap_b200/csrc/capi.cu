@@ -693,7 +693,7 @@ int stk_group_attention(const stk_kv* kv, const void* q, int q_dtype, int hq, co
   if (kv->d != 64 && kv->d != 128) return fail(STK_EDIM, "group attention supports head dim 64 or 128, not %d", kv->d);
   const int G = hq / kv->hkv;
   if (G > 16) return fail(STK_EINVAL, "group attention tiles at most 16 query heads per KV head, not %d", G);
-  if (256 % kv->b) return fail(STK_EINVAL, "block size %d must divide 256", kv->b);
+  if (64 % kv->b) return fail(STK_EINVAL, "block size %d must divide 64", kv->b);
   if (sa <= 0) return fail(STK_EINVAL, "empty block list");
   if ((reinterpret_cast<uintptr_t>(kv->k) | reinterpret_cast<uintptr_t>(kv->v)) & 15)
     return fail(STK_EINVAL, "K/V must be 16-byte aligned");
@@ -730,7 +730,7 @@ int stk_group_repair_saved(const stk_kv* kv, const void* q, int q_dtype, int hq,
   if (kv->d != 64 && kv->d != 128) return fail(STK_EDIM, "group repair supports head dim 64 or 128, not %d", kv->d);
   const int G = hq / kv->hkv;
   if (G > 16) return fail(STK_EINVAL, "group repair tiles at most 16 query heads per KV head, not %d", G);
-  if (256 % kv->b) return fail(STK_EINVAL, "block size %d must divide 256", kv->b);
+  if (64 % kv->b) return fail(STK_EINVAL, "block size %d must divide 64", kv->b);
   if (sa <= 0 || sp <= 0) return fail(STK_EINVAL, "empty block list");
   if ((reinterpret_cast<uintptr_t>(kv->k) | reinterpret_cast<uintptr_t>(kv->v)) & 15)
     return fail(STK_EINVAL, "K/V must be 16-byte aligned");

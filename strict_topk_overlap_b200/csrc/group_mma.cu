@@ -10,9 +10,10 @@
 //
 // Grid: (splits, hkv). A CTA of four warps takes kTokensPerCta consecutive
 // tokens of its KV head's list (whole blocks, gathered into shared memory
-// with one bulk copy per block), each warp 64 of them:
-//   S = Q K^T (8 n-tiles of 8 tokens x 8 k-steps of 16 dims), scaled by
-//   D^-1/2 in FP32; a row-wise softmax over the warp's 64 tokens; O = P V
+// with one bulk copy per block, issued by the lanes of warp 0), each warp 16
+// of them (64 per CTA: config 2's 2,048 tokens per group give 256 CTAs):
+//   S = Q K^T (2 n-tiles of 8 tokens x 8 k-steps of 16 dims), scaled by
+//   D^-1/2 in FP32; a row-wise softmax over the warp's 16 tokens; O = P V
 //   with P split into a bf16 (or f16) high part and the residual's low part,
 //   two MMAs per tile, so the weights keep ~16 bits instead of 8.
 // The four warps' (m, l, O) merge in shared memory; the CTA writes one
@@ -27,7 +28,9 @@
 namespace stk {
 
 constexpr int kGroupWarps = 4;
-constexpr int kTokensPerWarp = 64;
+constexpr int kTokensPerWarp = 16;
+constexpr int kSTiles = kTokensPerWarp / 8;   // QK n-tiles of 8 tokens
+constexpr int kPSteps = kTokensPerWarp / 16;  // PV k-steps of 16 tokens
 constexpr int kTokensPerCta = kGroupWarps * kTokensPerWarp;
 
 struct GroupArgs {
@@ -110,9 +113,10 @@ __global__ void __launch_bounds__(kGroupWarps * 32) group_mma_kernel(GroupArgs a
     fence_barrier_init();
   }
   __syncthreads();
-  if (tid == 0 && nb > 0) {
-    mbar_arrive_expect_tx(&bar, 2u * blk_bytes * static_cast<unsigned>(nb));
-    for (int j = 0; j < nb; ++j) {
+  if (warp == 0 && nb > 0) {
+    if (lane == 0) mbar_arrive_expect_tx(&bar, 2u * blk_bytes * static_cast<unsigned>(nb));
+    __syncwarp();
+    for (int j = lane; j < nb; j += 32) {
       int bid = a.ids[static_cast<long long>(h) * a.sa + j0 + j];
       if (bid < 0 || bid >= a.L.n) {
         report(a.status, kStatusBadBlockId);
@@ -146,10 +150,10 @@ __global__ void __launch_bounds__(kGroupWarps * 32) group_mma_kernel(GroupArgs a
   for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
 
   if (ok && tw0 < ntok) {
-    // ---- S = Q K^T over the warp's 64 tokens.
-    float s[8][4];
+    // ---- S = Q K^T over the warp's tokens.
+    float s[kSTiles][4];
 #pragma unroll
-    for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+    for (int n = 0; n < kSTiles; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
 #pragma unroll
     for (int ks = 0; ks < KS; ++ks) {
       unsigned af[4];
@@ -159,7 +163,7 @@ __global__ void __launch_bounds__(kGroupWarps * 32) group_mma_kernel(GroupArgs a
       af[2] = *reinterpret_cast<const unsigned*>(Qs + g * D + c + 8);
       af[3] = *reinterpret_cast<const unsigned*>(Qs + (g + 8) * D + c + 8);
 #pragma unroll
-      for (int n = 0; n < 8; ++n) {
+      for (int n = 0; n < kSTiles; ++n) {
         const T* kr = Ks + (tw0 + n * 8 + g) * D + c;  // token n*8+g, dims c, c+1 (and +8)
         const unsigned b0 = *reinterpret_cast<const unsigned*>(kr);
         const unsigned b1 = *reinterpret_cast<const unsigned*>(kr + 8);
@@ -168,7 +172,7 @@ __global__ void __launch_bounds__(kGroupWarps * 32) group_mma_kernel(GroupArgs a
     }
     // ---- row-wise softmax over the warp's tokens (rows g and g + 8).
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
+    for (int n = 0; n < kSTiles; ++n) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int tok = tw0 + n * 8 + t4 * 2 + (e & 1);
@@ -179,13 +183,13 @@ __global__ void __launch_bounds__(kGroupWarps * 32) group_mma_kernel(GroupArgs a
     for (int hr = 0; hr < 2; ++hr) {
       float mx = neg_inf();
 #pragma unroll
-      for (int n = 0; n < 8; ++n) mx = fmaxf(mx, fmaxf(s[n][2 * hr], s[n][2 * hr + 1]));
+      for (int n = 0; n < kSTiles; ++n) mx = fmaxf(mx, fmaxf(s[n][2 * hr], s[n][2 * hr + 1]));
       mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
       mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
       mrow[hr] = mx;
       float sum = 0.f;
 #pragma unroll
-      for (int n = 0; n < 8; ++n) {
+      for (int n = 0; n < kSTiles; ++n) {
 #pragma unroll
         for (int e = 2 * hr; e < 2 * hr + 2; ++e) {
           const float p = s[n][e] == neg_inf() ? 0.f : expf(s[n][e] - mx);
@@ -199,7 +203,7 @@ __global__ void __launch_bounds__(kGroupWarps * 32) group_mma_kernel(GroupArgs a
     }
     // ---- O = P V: P as A fragments (hi and lo halves), V as column-major B.
 #pragma unroll
-    for (int kt = 0; kt < 4; ++kt) {  // 16-token k-steps
+    for (int kt = 0; kt < kPSteps; ++kt) {  // 16-token k-steps
       unsigned ph[4], pl[4];
       const float* s0 = s[2 * kt];
       const float* s1 = s[2 * kt + 1];

@@ -505,9 +505,13 @@ __global__ void __launch_bounds__(kBWarps * 32) bound_interval_kernel(ScoreArgs 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nq = kQReq * G * D;
   float* qn1 = qs + nq;
+  // Group selection: per staged request the group's Q+ and Q- rows
+  // ([kQReq][2][D]) and its ||q||_1 (4 floats reserved).
+  float* qsum = qs + ((nq + kQReq * G + 3) & ~3);
+  float* qng = qsum + kQReq * 2 * D;
   // The tile's metadata rows, [kBTile][D] lo then hi: two contiguous ranges
   // of the metadata, each brought in by one bulk copy.
-  float* slo = qs + ((nq + kQReq * G + 3) & ~3);
+  float* slo = qng + 4;
   float* shi = slo + kBTile * D;
   __shared__ uint64_t meta_bar;
   ST(0);
@@ -565,6 +569,33 @@ __global__ void __launch_bounds__(kBWarps * 32) bound_interval_kernel(ScoreArgs 
     if (lane == 0) qn1[t] = sum;
   }
   __syncthreads();
+  if (C == 4 && a.group_select) {
+    // q . (q >= 0 ? hi : lo) = max(q, 0) hi + min(q, 0) lo, so the group's
+    // score is one dot product of the metadata row with Q+ = sum_g max(q_g, 0)
+    // and Q- = sum_g min(q_g, 0) (heads ascending, FP32). Its interval
+    // radius is the per-head radii's sum: kErrFactor * sum_g ||q_g||_1 *
+    // max|lo, hi|. Same-sign sums give |Q^ - Q| <= gamma_11 |Q| (G <= 12;
+    // gamma_15 for G = 16), and each term of the dot passes 8 + 5 roundings,
+    // so the FP32 score is within (gamma_13 (1 + gamma_15) + gamma_15) of
+    // that bound's base: 28 u against the 2 (D/4 + 2) u = 68 u it takes.
+    for (int i = tid; i < kQReq * D; i += blockDim.x) {
+      const int rq = i / D, dd = i - rq * D;
+      float qp = 0.f, qm = 0.f;
+      for (int g = 0; g < G; ++g) {
+        const float x = qs[(rq * G + g) * D + dd];
+        qp += x > 0.f ? x : 0.f;
+        qm += x < 0.f ? x : (x == x ? 0.f : x);  // a NaN q stays visible
+      }
+      qsum[(rq * 2) * D + dd] = qp;
+      qsum[(rq * 2 + 1) * D + dd] = qm;
+    }
+    if (tid < kQReq) {
+      float nsum = 0.f;
+      for (int g = 0; g < G; ++g) nsum = __fadd_ru(nsum, qn1[tid * G + g]);
+      qng[tid] = nsum;
+    }
+    __syncthreads();
+  }
   ST(1);
   if (!mbar_wait(&meta_bar, 0, a.status)) return;  // bounded; the status records a wait that gave up
 
@@ -584,6 +615,63 @@ __global__ void __launch_bounds__(kBWarps * 32) bound_interval_kernel(ScoreArgs 
       const float4* shi4 = reinterpret_cast<const float4*>(shi);
       const float4* qs4 = reinterpret_cast<const float4*>(qs);
       const float inf = __int_as_float(0x7f800000);
+      if (a.group_select) {
+        // The warp's 8 blocks at once: 8 partial dots per lane, a transposed
+        // butterfly (xor 16, 8, 4) and xor 2, 1 leave block j's score in
+        // lanes 4 j .. 4 j + 3; the largest |lo|, |hi| likewise.
+        const float4* qs4g = reinterpret_cast<const float4*>(qsum);
+        float part[8], mx[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int rl2 = warp * 8 + j;
+          const bool lj = rl2 < nrows;
+          const int rrj = __shfl_sync(kFull, rr, 4 * j);
+          const float4 l4 = lj ? slo4[rl2 * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 h4 = lj ? shi4[rl2 * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 qp = qs4g[(rrj * 2) * 32 + lane];
+          const float4 qm = qs4g[(rrj * 2 + 1) * 32 + lane];
+          float acc = qp.x * h4.x;
+          acc = fmaf(qp.y, h4.y, acc);
+          acc = fmaf(qp.z, h4.z, acc);
+          acc = fmaf(qp.w, h4.w, acc);
+          acc = fmaf(qm.x, l4.x, acc);
+          acc = fmaf(qm.y, l4.y, acc);
+          acc = fmaf(qm.z, l4.z, acc);
+          acc = fmaf(qm.w, l4.w, acc);
+          part[j] = acc;
+          mx[j] = fmaxf(fmaxf(fmaxf(fabsf(l4.x), fabsf(h4.x)), fmaxf(fabsf(l4.y), fabsf(h4.y))),
+                        fmaxf(fmaxf(fabsf(l4.z), fabsf(h4.z)), fmaxf(fabsf(l4.w), fabsf(h4.w))));
+        }
+#pragma unroll
+        for (int off = 16, cnt = 4; off >= 4; off >>= 1, cnt >>= 1) {
+          const bool upper = (lane & off) != 0;
+#pragma unroll
+          for (int i = 0; i < cnt; ++i) {
+            const float send = upper ? part[i] : part[i + cnt];
+            const float keep = upper ? part[i + cnt] : part[i];
+            part[i] = keep + __shfl_xor_sync(kFull, send, off);
+            const float msend = upper ? mx[i] : mx[i + cnt];
+            const float mkeep = upper ? mx[i + cnt] : mx[i];
+            mx[i] = fmaxf(mkeep, __shfl_xor_sync(kFull, msend, off));
+          }
+        }
+        float sum = part[0], bm = mx[0];
+        sum += __shfl_xor_sync(kFull, sum, 2);
+        sum += __shfl_xor_sync(kFull, sum, 1);
+        bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 2));
+        bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 1));
+        const int j = lane >> 2;
+        const int rl2 = warp * 8 + j;
+        const int rrj = __shfl_sync(kFull, rr, 4 * j);
+        if ((lane & 3) == 0 && rl2 < nrows) {
+          const float e = __fadd_ru(__fmul_ru(__fmul_ru(qng[rrj], bm), kErrFactor), 0x1p-118f);
+          float2 iv = make_float2(__fsub_rd(sum, e), __fadd_ru(sum, e));
+          if (!(iv.x <= iv.y)) iv = make_float2(-inf, inf);
+          out[static_cast<long long>(mh) * a.total_blocks + row0 + rl2] = iv;
+        }
+        ST(3);
+        return;
+      }
 #pragma unroll 1
       for (int grp = 0; grp < 2; ++grp) {
         const int bb = warp * 8 + grp * 4;  // tile-local first block of the group
@@ -837,7 +925,7 @@ int launch_bounds(const ScoreArgs& a, float2* bounds, cudaStream_t stream) {
   if (!aligned || G > 16 || (a.d != 64 && a.d != 128 && a.d != 256)) return 1;
   // q rows and their norms (rounded up to 16 bytes), then the tile's lo and hi rows.
   const size_t smem = (((static_cast<size_t>(kQReq) * G * a.d + kQReq * G) + 3) & ~static_cast<size_t>(3)) * 4 +
-                      static_cast<size_t>(2) * kBTile * a.d * 4;
+                      (static_cast<size_t>(kQReq) * 2 * a.d + 4) * 4 + static_cast<size_t>(2) * kBTile * a.d * 4;
   const dim3 grid((a.total_blocks + kBTile - 1) / kBTile, a.hmeta);
   void (*kern)(ScoreArgs, float2*);
   if (a.d == 64) kern = G <= 4 ? bound_interval_kernel<2, 4> : bound_interval_kernel<2, 16>;

@@ -314,6 +314,222 @@ __global__ void __launch_bounds__(kFastMaxWarps * 32, 1) jobs_fast_kernel(JobArg
   if (a.chain) pdl_wait();  // this grid completes only after its predecessor
 }
 
+// ------------------------------------------------------------------ tiny blocks, wide groups
+// Per-block states for blocks of NB <= 8 tokens when several query heads
+// share a KV head (12 heads per KV head, 4-token blocks,
+// one list per group). One warp takes one (request, KV head, slot): it reads
+// the block of the group's first head once and computes the state of every
+// head of the group whose ID at that slot is the same; a head with another
+// ID then reads its own block (asked into L2 at the start of the slot). Lane
+// l owns dims [DPL l, DPL l + DPL) of every token, so a token row is one
+// coalesced warp load, and the group's q rows are staged per warp with
+// cp.async while the IDs and the block load. The per-(row, block) jobs
+// above would read each 2 KiB block once per query head and spend a 32-token
+// chunk on 4 tokens. States as everywhere: s = (k . q) * scale, m = max s,
+// l = sum exp(s - m), u = sum exp(s - m) v; (-inf, 0, 0) for a negative or
+// out-of-range ID (the latter also reported in the status word).
+constexpr int kGroupJobWarps = 8;
+constexpr int kGroupJobMaxG = 16;
+
+template <int BYTES>
+__device__ __forceinline__ void cp_async_ca(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(smem_u32(smem)), "l"(gmem), "n"(BYTES) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Transposed butterfly over NB values: on exit every lane of the group of
+// 32 / NB lanes holding token t = lane / (32 / NB) has the warp's sum of v[t].
+template <int NB>
+__device__ __forceinline__ float transpose_sum(float (&v)[NB], int lane) {
+#pragma unroll
+  for (int cnt = NB, off = 16; cnt > 1; cnt >>= 1, off >>= 1) {
+    const bool upper = (lane & off) != 0;
+    const int half = cnt >> 1;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const float send = upper ? v[i] : v[i + half];
+      const float keep = upper ? v[i + half] : v[i];
+      v[i] = keep + __shfl_xor_sync(kFull, send, off);
+    }
+  }
+  float x = v[0];
+#pragma unroll
+  for (int off = 16 / NB; off > 0; off >>= 1) x += __shfl_xor_sync(kFull, x, off);
+  return x;
+}
+
+template <typename T, int DPL, int NB>
+__device__ __forceinline__ void load_tiny_block(const T* base, int lane, float (&x)[NB][DPL]) {
+  constexpr int D = 32 * DPL;
+#pragma unroll
+  for (int t = 0; t < NB; ++t) load_vec<T, DPL>(base + static_cast<size_t>(t) * D + lane * DPL, x[t]);
+}
+
+template <int DPL, int NB>
+__device__ __forceinline__ void tiny_block_state(const float (&qf)[DPL], const float (&kf)[NB][DPL],
+                                                 const float (&vf)[NB][DPL], float scale, int lane, float& m,
+                                                 float& l, float (&u)[DPL]) {
+  constexpr int kLanesPerTok = 32 / NB;
+  float p[NB];
+#pragma unroll
+  for (int t = 0; t < NB; ++t) {
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) acc = fmaf(kf[t][j], qf[j], acc);
+    p[t] = acc;
+  }
+  const float s = transpose_sum<NB>(p, lane) * scale;  // logit of token lane / kLanesPerTok
+  float mx = s;
+#pragma unroll
+  for (int off = 16; off >= kLanesPerTok; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, off));
+  const float e = expf(s - mx);
+  float sum = e;
+#pragma unroll
+  for (int off = 16; off >= kLanesPerTok; off >>= 1) sum += __shfl_xor_sync(kFull, sum, off);
+  m = mx;
+  l = sum;
+#pragma unroll
+  for (int j = 0; j < DPL; ++j) u[j] = 0.f;
+#pragma unroll
+  for (int t = 0; t < NB; ++t) {
+    const float w = __shfl_sync(kFull, e, t * kLanesPerTok);
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) u[j] = fmaf(w, vf[t][j], u[j]);
+  }
+}
+
+// CTAs per SM the register budget is set for (no spills at 4 x 4 and 8 x 4 values per lane).
+template <int DPL, int NB>
+constexpr int group_ctas_per_sm() { return NB * DPL > 16 ? 2 : (NB * DPL == 16 ? 3 : 4); }
+
+template <typename T, int DPL, int NB>
+__global__ void __launch_bounds__(kGroupJobWarps * 32, group_ctas_per_sm<DPL, NB>()) jobs_group_kernel(JobArgs a) {
+  constexpr int D = 32 * DPL;
+  extern __shared__ __align__(16) unsigned char gq_raw[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  T* wq = reinterpret_cast<T*>(gq_raw) + static_cast<size_t>(warp) * kGroupJobMaxG * D + lane * DPL;
+  const T* Q = static_cast<const T*>(a.q);
+  const T* K = static_cast<const T*>(a.L.k);
+  const T* V = static_cast<const T*>(a.L.v);
+  const int hkv = a.hq / a.g;
+  const long long tasks = static_cast<long long>(a.rows / a.hq) * hkv * a.s;
+  const long long stride = static_cast<long long>(gridDim.x) * kGroupJobWarps;
+  constexpr unsigned kBlockBytes = static_cast<unsigned>(NB * D * sizeof(T));
+#pragma unroll 1
+  for (long long t = static_cast<long long>(blockIdx.x) * kGroupJobWarps + warp; t < tasks; t += stride) {
+    const int j = static_cast<int>(t % a.s);
+    const long long rk = t / a.s;
+    const int kv = static_cast<int>(rk % hkv);
+    const int r = static_cast<int>(rk / hkv);
+    const int row0 = r * a.hq + kv * a.g;
+    const int nblk = request_blocks(a.L, r);
+    // The group's q rows (each lane copies, and later reads, its own dims).
+    for (int h = 0; h < a.g; ++h)
+      cp_async_ca<DPL * sizeof(T)>(wq + h * D, Q + static_cast<long long>(row0 + h) * D + lane * DPL);
+    cp_async_commit();
+    // Lane h < g: head h's ID at this slot.
+    long long my = -1;
+    if (lane < a.g) my = load_id(a.ids, a.ids64, static_cast<long long>(row0 + lane) * a.s + j);
+    const long long lead = __shfl_sync(kFull, my, 0);
+    const bool valid = my >= 0 && my < nblk;
+    if (lane < a.g && my >= nblk) report(a.status, kStatusBadBlockId);
+    if (lane < a.g && valid && my != lead) {
+      const long long off = block_seg(a.L, r, kv, my, 0).elem_off;
+      bulk_prefetch_l2(K + off, kBlockBytes);
+      bulk_prefetch_l2(V + off, kBlockBytes);
+    }
+    const unsigned shared_heads = __ballot_sync(kFull, lane < a.g && valid && my == lead);
+    const unsigned own_heads = __ballot_sync(kFull, lane < a.g && valid && my != lead);
+    const unsigned void_heads = __ballot_sync(kFull, lane < a.g && !valid);
+    float kf[NB][DPL], vf[NB][DPL];
+    if (shared_heads) {
+      const long long off = block_seg(a.L, r, kv, lead, 0).elem_off;
+      load_tiny_block<T, DPL, NB>(K + off, lane, kf);
+      load_tiny_block<T, DPL, NB>(V + off, lane, vf);
+    }
+    cp_async_wait_all();
+    auto finish = [&](int h, float m, float l, const float (&u)[DPL]) {
+      const long long job = static_cast<long long>(row0 + h) * a.s + j;
+      if (lane == 0) {
+        a.m[job] = m;
+        a.l[job] = l;
+      }
+      store_vec<DPL>(a.u + job * D + lane * DPL, u);
+    };
+    auto one_head = [&](int h) {
+      float qf[DPL], u[DPL], m, l;
+      load_vec<T, DPL>(wq + h * D, qf);
+      tiny_block_state<DPL, NB>(qf, kf, vf, a.scale, lane, m, l, u);
+      finish(h, m, l, u);
+    };
+#pragma unroll 1
+    for (unsigned w = shared_heads; w; w &= w - 1) one_head(__ffs(w) - 1);
+    // Heads whose ID differs from the first head's: each reads its own block.
+#pragma unroll 1
+    for (unsigned w = own_heads; w; w &= w - 1) {
+      const int h = __ffs(w) - 1;
+      const long long off = block_seg(a.L, r, kv, __shfl_sync(kFull, my, h), 0).elem_off;
+      load_tiny_block<T, DPL, NB>(K + off, lane, kf);
+      load_tiny_block<T, DPL, NB>(V + off, lane, vf);
+      one_head(h);
+    }
+#pragma unroll 1
+    for (unsigned w = void_heads; w; w &= w - 1) {
+      float z[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) z[i] = 0.f;
+      finish(__ffs(w) - 1, neg_inf(), 0.f, z);
+    }
+  }
+}
+
+// Dense K/V, full states, no masks or slot search, whole requests, tiny
+// blocks, 2..16 query heads per KV head, q in the K/V dtype.
+static bool group_eligible(const JobArgs& a, int elem, int dtype) {
+  if (a.mode != kModeFull || a.pred != nullptr || a.active_mode != 0 || a.active_invert || a.chain) return false;
+  if (a.L.page_table != nullptr || a.q_dtype != dtype) return false;
+  if (a.g < 2 || a.g > kGroupJobMaxG || a.hq % a.g || a.rows % a.hq) return false;
+  if (a.d != 64 && a.d != 128) return false;
+  if (a.L.b != 2 && a.L.b != 4 && a.L.b != 8) return false;
+  if ((a.L.b * a.d * elem) % 16) return false;  // L2 prefetch granularity
+  const uintptr_t pk = reinterpret_cast<uintptr_t>(a.L.k), pv = reinterpret_cast<uintptr_t>(a.L.v);
+  const uintptr_t pq = reinterpret_cast<uintptr_t>(a.q);
+  if ((pk | pv | pq) & 15) return false;
+  if (a.L.kv_request_stride % 8) return false;
+  return true;
+}
+
+template <typename T, int DPL, int NB>
+static int launch_group_nb(const JobArgs& a, int num_sms, cudaStream_t stream) {
+  const long long tasks = static_cast<long long>(a.rows / a.hq) * (a.hq / a.g) * a.s;
+  constexpr int kPerSm = group_ctas_per_sm<DPL, NB>();
+  long long ctas = (tasks + kGroupJobWarps - 1) / kGroupJobWarps;
+  const long long cap = static_cast<long long>(num_sms) * kPerSm;
+  if (ctas > cap) ctas = cap;
+  if (ctas < 1) ctas = 1;
+  const size_t smem = static_cast<size_t>(kGroupJobWarps) * kGroupJobMaxG * 32 * DPL * sizeof(T);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(jobs_group_kernel<T, DPL, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+  jobs_group_kernel<T, DPL, NB><<<static_cast<unsigned>(ctas), kGroupJobWarps * 32, smem, stream>>>(a);
+  return static_cast<int>(cudaGetLastError());
+}
+
+template <typename T, int DPL>
+static int launch_group_d(const JobArgs& a, int num_sms, cudaStream_t stream) {
+  switch (a.L.b) {
+    case 2: return launch_group_nb<T, DPL, 2>(a, num_sms, stream);
+    case 4: return launch_group_nb<T, DPL, 4>(a, num_sms, stream);
+    default: return launch_group_nb<T, DPL, 8>(a, num_sms, stream);
+  }
+}
+
+template <typename T>
+static int launch_group(const JobArgs& a, int num_sms, cudaStream_t stream) {
+  return a.d == 64 ? launch_group_d<T, 2>(a, num_sms, stream) : launch_group_d<T, 4>(a, num_sms, stream);
+}
+
 // ------------------------------------------------------------------ generic path
 // Any D <= 1024, any B, any alignment. Lane = token for QK, lane = dim for PV.
 template <typename T>
@@ -807,6 +1023,8 @@ static int launch_jobs_t(const JobArgs& a, int num_sms, cudaStream_t stream) {
       }
     }
   }
+  constexpr int kCode = sizeof(T) == 4 ? kF32 : (std::is_same<T, __half>::value ? kF16 : kBF16);
+  if (group_eligible(a, sizeof(T), kCode)) return launch_group<T>(a, num_sms, stream);
   if (fast_eligible(a, sizeof(T))) {
     switch (a.mode) {
       case kModeFull: return launch_fast_d<T, kModeFull>(a, num_sms, stream);

@@ -48,13 +48,13 @@ def repair_saved(q, k, v, selected, predicted, state):
 
 def _group_tile_ok(q, k, selected, predicted):
     """Shapes the tensor-core group repair takes: q and K/V in one 16-bit
-    dtype, D 64 or 128, blocks dividing 256 tokens, a dense tile of 8..16
+    dtype, D 64 or 128, blocks dividing 64 tokens, a dense tile of 8..16
     query heads per KV head, int32 contiguous lists."""
     hq, d = q.shape
     hkv, n, b, _ = k.shape
     g = hq // hkv
     return (q.dtype == k.dtype and q.dtype in (torch.bfloat16, torch.float16) and d in (64, 128)
-            and 256 % b == 0 and 8 <= g <= 16 and hq % hkv == 0
+            and 64 % b == 0 and 8 <= g <= 16 and hq % hkv == 0
             and selected.dtype == torch.int32 and predicted.dtype == torch.int32
             and selected.is_contiguous() and predicted.is_contiguous())
 

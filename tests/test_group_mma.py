@@ -74,3 +74,42 @@ def test_group_repair_saved_shared_matches_per_row_and_oracle(hq, hkv, n, b, d, 
     assert (out - per_row).abs().max().item() <= 1e-4
     ref = OA.attention_fp64(q.float().numpy(), kk.float().numpy(), vv.float().numpy(), ids)
     assert (np.abs(out.cpu().numpy() - ref) <= 2e-3 + 1e-2 * np.abs(ref)).all()
+
+
+@pytest.mark.parametrize("hq,hkv,n,b,d,dtype", [
+    (24, 2, 300, 4, 128, torch.bfloat16),   # config-2 group (12 heads) and block size
+    (32, 2, 150, 4, 128, torch.bfloat16),   # 16 heads per group
+    (16, 2, 200, 8, 64, torch.float16),
+    (6, 3, 100, 2, 128, torch.float32),     # 2 heads per group
+])
+def test_tiny_block_group_states(hq, hkv, n, b, d, dtype):
+    """Per-block states of tiny blocks (the group kernel: a block shared by a
+    KV group is read once, a head with its own ID reads its own block, -1
+    gives (-inf, 0, 0)) against the oracle's per-block state, on lists that
+    are shared per group with some heads' slots replaced or emptied."""
+    from strict_topk import kernels
+    from oracle import speculative as OP
+    q, kk, vv, _, _ = C.synthetic_kv(hq, hkv, n, b, d, dtype, seed=hq + b)
+    g, s = hq // hkv, 40
+    gen = torch.Generator().manual_seed(hq + d)
+    ids = torch.stack([torch.randperm(n, generator=gen)[:s] for _ in range(hkv)]).repeat_interleave(g, 0)
+    own = torch.rand(hq, s, generator=gen) < 0.2
+    ids[own] = torch.randint(0, n, (int(own.sum()),), generator=gen)
+    ids[torch.rand(hq, s, generator=gen) < 0.05] = -1
+    ids[0::g, 3] = -1  # the group's first head has no block at slot 3: the others still do
+    ids[1::g, 5] = -1
+    ids = ids.to(torch.int32).contiguous()
+    st = kernels.block_partials(q.to(DEV), kk.to(DEV), vv.to(DEV), ids.to(DEV))
+    torch.cuda.synchronize()
+    m, l, u = st.m.cpu().numpy(), st.l.cpu().numpy(), st.u.cpu().numpy()
+    X = OP.Inputs(C.as_np(q), C.as_np(kk), C.as_np(vv))
+    for h in range(hq):
+        for j in range(s):
+            bid = int(ids[h, j])
+            if bid < 0:
+                assert np.isneginf(m[h, j]) and l[h, j] == 0 and not u[h, j].any(), (h, j)
+                continue
+            mm, ll, uu = OP.block_state(X, h, bid)
+            assert np.isclose(m[h, j], mm, rtol=1e-5, atol=1e-5), (h, j)
+            assert np.isclose(l[h, j], ll, rtol=1e-5), (h, j)
+            assert np.allclose(u[h, j], uu, rtol=1e-4, atol=1e-4), (h, j)

@@ -77,6 +77,18 @@ def test_near_ties_bit_exact(d):
         assert np.array_equal(_select(q, lo, hi, k, shared=True)[0], _want(q, lo, hi, k, shared=True)), k
 
 
+@pytest.mark.parametrize("hq", [24, 32])
+def test_near_ties_wide_group_selection(hq):
+    """Group selection with 12 and 16 query heads per KV head (the group
+    scorer's one dot product with the summed positive and negative q parts)
+    on near-tie metadata: IDs bit-exact."""
+    hkv, n, d = 2, 512, 128
+    lo, hi = _near_tie_metadata(hkv, n, d, seed=hq)
+    q = torch.randn(hq, d, generator=torch.Generator().manual_seed(hq + 1)).to(torch.bfloat16)
+    for k in (1, 7, 64, 255, 511):
+        assert np.array_equal(_select(q, lo, hi, k, shared=True)[0], _want(q, lo, hi, k, shared=True)), k
+
+
 def test_duplicated_blocks_take_the_lower_index():
     """Every block repeats one of 7: whole classes tie exactly and straddle
     the boundary (more than the ranked list holds)."""
