@@ -26,13 +26,20 @@
 // skipped, two barriers per digit), then one packed block scan that places
 // every selected ID at its ascending-order position.
 
+#ifdef STK_TRACE
+// [cta][8] timeline of the Top-K kernels (profiling builds only): 0 start,
+// 1..5 the bounded core's phase probes, 6 after the dependency wait, 7 end.
+namespace stk {
+static __device__ unsigned long long g_topk_trace[4096 * 8];
+}
+#define STK_TOPK_PROBE(ev) \
+  do { if (blockIdx.x < 4096 && threadIdx.x == 0) stk::g_topk_trace[blockIdx.x * 8 + 1 + (ev)] = stk::global_ns(); } while (0)
+#endif
 #include "topk.cuh"
 
 namespace stk {
 
 #ifdef STK_TRACE
-// [cta][8] timeline of the Top-K kernel (profiling builds only).
-static __device__ unsigned long long g_topk_trace[4096 * 8];
 extern "C" __attribute__((visibility("default"))) void* stk_trace_topk() {
   void* p = nullptr;
   cudaGetSymbolAddress(&p, g_topk_trace);
@@ -526,17 +533,47 @@ __global__ void __launch_bounds__(kBWarps * 32) bound_interval_kernel(ScoreArgs 
     bulk_g2s(shi, a.hi + moff, bytes, &meta_bar);
   }
 
-  // q first: loads issued behind the metadata stream would wait for it.
+  // q first: loads issued behind the metadata stream would wait for it. The
+  // staged requests' rows of this meta head are G * D consecutive elements
+  // each; they are read in 8-element chunks (16-byte loads for 16-bit q),
+  // two chunks in flight per thread, and rows of absent requests are zero.
   const int r0 = find_request(a.block_offsets, a.R, row0);
-  constexpr int kQPer = 8;
-  float qv[kQPer];
+  {
+    const int nreq = max(0, min(kQReq, a.R - r0));
+    const int chunks = G * D / 8;
+    const bool vec = (reinterpret_cast<uintptr_t>(a.q) & 15) == 0;
+    for (int i = nreq * G * D + tid; i < nq; i += blockDim.x) qs[i] = 0.f;
+    for (int c0 = 0; c0 < nreq * chunks; c0 += 2 * blockDim.x) {
+      float x[2][8];
+      int dst[2];
 #pragma unroll
-  for (int e = 0; e < kQPer; ++e) {
-    const int i = e * blockDim.x + tid;
-    qv[e] = 0.f;
-    if (i < nq) {
-      const int rr = i / (G * D), rem = i - rr * G * D;
-      if (r0 + rr < a.R) qv[e] = load_any(a.q, a.q_dtype, (static_cast<long long>(r0 + rr) * a.hq + mh * G) * D + rem);
+      for (int u = 0; u < 2; ++u) {
+        const int c = c0 + u * blockDim.x + tid;
+        dst[u] = -1;
+        if (c < nreq * chunks) {
+          const int rr = c / chunks, cc = c - rr * chunks;
+          const long long src = (static_cast<long long>(r0 + rr) * a.hq + mh * G) * D + cc * 8;
+          dst[u] = rr * G * D + cc * 8;
+          if (vec && a.q_dtype == kF32) {
+            load_vec<float, 8>(static_cast<const float*>(a.q) + src, x[u]);
+          } else if (vec && a.q_dtype == kBF16) {
+            load_vec<__nv_bfloat16, 8>(static_cast<const __nv_bfloat16*>(a.q) + src, x[u]);
+          } else if (vec && a.q_dtype == kF16) {
+            load_vec<__half, 8>(static_cast<const __half*>(a.q) + src, x[u]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[u][e] = load_any(a.q, a.q_dtype, src + e);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (dst[u] >= 0) {
+          float4* d4 = reinterpret_cast<float4*>(qs + dst[u]);
+          d4[0] = make_float4(x[u][0], x[u][1], x[u][2], x[u][3]);
+          d4[1] = make_float4(x[u][4], x[u][5], x[u][6], x[u][7]);
+        }
+      }
     }
   }
 #ifdef STK_QFIRST
@@ -550,15 +587,6 @@ __global__ void __launch_bounds__(kBWarps * 32) bound_interval_kernel(ScoreArgs 
   const float4* L4 = reinterpret_cast<const float4*>(slo + (live ? rl : 0) * D);
   const float4* H4 = reinterpret_cast<const float4*>(shi + (live ? rl : 0) * D);
   float4 lv[NBAT], hv[NBAT];
-#pragma unroll
-  for (int e = 0; e < kQPer; ++e) {
-    const int i = e * blockDim.x + tid;
-    if (i < nq) qs[i] = qv[e];
-  }
-  for (int i = kQPer * blockDim.x + tid; i < nq; i += blockDim.x) {  // large groups only
-    const int rr = i / (G * D), rem = i - rr * G * D;
-    qs[i] = r0 + rr < a.R ? load_any(a.q, a.q_dtype, (static_cast<long long>(r0 + rr) * a.hq + mh * G) * D + rem) : 0.f;
-  }
   __syncthreads();
   // ||q||_1 per staged row, rounded up at every step.
   for (int t = warp; t < kQReq * G; t += kBWarps) {
@@ -844,6 +872,7 @@ __global__ void __launch_bounds__(kBWarps * 32) bound_interval_kernel(ScoreArgs 
 template <int E, int NT>
 __global__ void __launch_bounds__(NT, 1) select_bounded_kernel(SelectArgs a) {
   __shared__ __align__(16) float qsm[kQStage];  // the row's query heads, FP32, for exact rescoring
+  extern __shared__ float2 sel_stage[];          // the row's intervals (n + n / 16 slots)
   KT(0);
   pdl_release();
   const int tid = threadIdx.x;
@@ -865,8 +894,9 @@ __global__ void __launch_bounds__(NT, 1) select_bounded_kernel(SelectArgs a) {
     for (int i = tid; i < q_heads * a.d; i += NT) qsm[i] = load_any(a.q, a.q_dtype, q0 + i);
   }
   pdl_wait();  // bounds come from the preceding interval scorer
-  bounded_select_core<E, NT>(a, row, qsm, q_staged);
-  KT(3);
+  KT(6);
+  bounded_select_core<E, NT>(a, row, qsm, q_staged, nullptr, NoSelectHook(), sel_stage);
+  KT(7);
 }
 
 // ------------------------------------------------------------------ host side
@@ -939,8 +969,11 @@ int launch_bounds(const ScoreArgs& a, float2* bounds, cudaStream_t stream) {
 
 template <int E, int NT>
 static int launch_bounded_e(const SelectArgs& a, cudaStream_t stream) {
+  constexpr size_t smem = static_cast<size_t>(E * NT + (E * NT) / 16) * sizeof(float2);
+  cudaFuncSetAttribute(select_bounded_kernel<E, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(smem));
   prefer_shared(select_bounded_kernel<E, NT>);
-  return launch_pdl(select_bounded_kernel<E, NT>, dim3(a.R * a.hsel), dim3(NT), 0, stream, 0, a);
+  return launch_pdl(select_bounded_kernel<E, NT>, dim3(a.R * a.hsel), dim3(NT), smem, stream, 0, a);
 }
 
 int launch_select_bounded(const SelectArgs& a, int max_n, cudaStream_t stream) {

@@ -348,13 +348,18 @@ __device__ __forceinline__ unsigned block_exclusive_scan(unsigned v, unsigned* w
 // as soon as the intervals classify it (before any exact rescoring), and
 // hook.selected(pos, id, was_sure_in) once per selected block as its output
 // position is written; both on the thread that owns the block.
+// stage (optional, without kPoll): shared memory for n + n / 16 intervals.
+// The row's intervals are then read with coalesced loads (thread t takes
+// t, t + NT, ...) into it, one 8-byte slot of padding after every 16, so
+// that each thread's E contiguous intervals read back without bank
+// conflicts; read directly, each warp load of them touches 32 lines.
 struct NoSelectHook {
   __device__ void sure_in(int) const {}
   __device__ void selected(int, int, bool) const {}
 };
 template <int E, int NT, bool kPoll = false, typename Hook = NoSelectHook>
 __device__ void bounded_select_core(const SelectArgs& a, int row, const float* qsm, bool q_staged,
-                                    int* ids_smem = nullptr, const Hook& hook = Hook()) {
+                                    int* ids_smem = nullptr, const Hook& hook = Hook(), float2* stage = nullptr) {
   static_assert(NT % 32 == 0 && NT <= 512 && kHistBins % NT == 0, "selection block shape");
   constexpr int NW = NT / 32;
   __shared__ unsigned hist[kHistBins];  // low 16 bits: lower ends; high 16 bits: upper ends
@@ -421,12 +426,27 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
         }
       }
     } else {
+      if (stage != nullptr) {
+        float2 t[E];
+#pragma unroll
+        for (int k = 0; k < E; ++k) {
+          const int i = k * NT + tid;
+          if (i < n) t[k] = __ldcg(src + i);
+        }
+#pragma unroll
+        for (int k = 0; k < E; ++k) {
+          const int i = k * NT + tid;
+          if (i < n) stage[i + (i >> 4)] = t[k];
+        }
+        __syncthreads();
+      }
 #pragma unroll
       for (int j = 0; j < E; ++j) {
         lo_[j] = inf;
         up_[j] = -inf;
         if (beg + j < n) {
-          const float2 v = __ldcg(src + beg + j);
+          const int i = beg + j;
+          const float2 v = stage != nullptr ? stage[i + (i >> 4)] : __ldcg(src + i);
           lo_[j] = v.x;
           up_[j] = v.y;
           if (v.x > -inf) mn = fminf(mn, v.x);
