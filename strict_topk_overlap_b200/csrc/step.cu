@@ -823,7 +823,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
       sa.id_base = 0; sa.ids_out = a.selected; sa.keys_out = nullptr; sa.status = a.status;
       sa.bounds = a.bounds; sa.q = a.q; sa.q_dtype = a.q_dtype; sa.lo = a.lo; sa.hi = a.hi;
       sa.hq = hq; sa.hmeta = hkv; sa.d = D; sa.group_select = 0;
-      bounded_select_core<E, kStepThreads, true, RowHook>(sa, row, qrow, true, s_sel, hook);
+      // The ring's first three stages hold no copy from the end of the scoring
+      // phase until the first miss is issued: they stage the row's intervals.
+      static_assert(3 * kStageBytes >= (kStepMaxBlocks + kStepMaxBlocks / 16) * 8 && kStepStages >= 3, "interval stage");
+      bounded_select_core<E, kStepThreads, true, RowHook>(sa, row, qrow, true, s_sel, hook,
+                                                          reinterpret_cast<float2*>(pool));
     }
     __syncthreads();
     if (tid == 0) SPT(7);

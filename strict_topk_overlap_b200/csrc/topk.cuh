@@ -348,11 +348,11 @@ __device__ __forceinline__ unsigned block_exclusive_scan(unsigned v, unsigned* w
 // as soon as the intervals classify it (before any exact rescoring), and
 // hook.selected(pos, id, was_sure_in) once per selected block as its output
 // position is written; both on the thread that owns the block.
-// stage (optional, without kPoll): shared memory for n + n / 16 intervals.
-// The row's intervals are then read with coalesced loads (thread t takes
-// t, t + NT, ...) into it, one 8-byte slot of padding after every 16, so
-// that each thread's E contiguous intervals read back without bank
-// conflicts; read directly, each warp load of them touches 32 lines.
+// stage (optional): shared memory for n + n / 16 intervals. The row's
+// intervals are then read (or, with kPoll, polled) with coalesced loads
+// (thread t takes t, t + NT, ...) into it, one 8-byte slot of padding after
+// every 16, so that each thread's E contiguous intervals read back without
+// bank conflicts; read directly, each warp load of them spans E * 32 slots.
 struct NoSelectHook {
   __device__ void sure_in(int) const {}
   __device__ void selected(int, int, bool) const {}
@@ -391,9 +391,13 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
     float lo_[E], up_[E];
     float mn = inf, mx = -inf;
     if constexpr (kPoll) {
+      // With a stage, thread t polls slots t, t + NT, ... (coalesced) and the
+      // slots are then exchanged through shared memory as in the plain path.
+      const int pb = stage != nullptr ? tid : beg;
+      const int ps = stage != nullptr ? NT : 1;
       unsigned long long raw[E];
 #pragma unroll
-      for (int j = 0; j < E; ++j) raw[j] = beg + j < n ? ld_relaxed_gpu_u64(src + beg + j) : 1ull;
+      for (int j = 0; j < E; ++j) raw[j] = pb + j * ps < n ? ld_relaxed_gpu_u64(src + pb + j * ps) : 1ull;
       bool missing = false;
 #pragma unroll
       for (int j = 0; j < E; ++j) missing |= raw[j] == 0ull;
@@ -404,13 +408,27 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
           missing = false;
 #pragma unroll
           for (int j = 0; j < E; ++j) {
-            if (raw[j] == 0ull) raw[j] = ld_relaxed_gpu_u64(src + beg + j);
+            if (raw[j] == 0ull) raw[j] = ld_relaxed_gpu_u64(src + pb + j * ps);
             missing |= raw[j] == 0ull;
           }
           if (missing && global_ns() - t0 > c_wait_ns) {
             report(a.status, kStatusWaitTimeout);
             break;
           }
+        }
+      }
+      if (stage != nullptr) {
+        unsigned long long* st64 = reinterpret_cast<unsigned long long*>(stage);
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+          const int i = tid + j * NT;
+          if (i < n) st64[i + (i >> 4)] = raw[j];
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+          const int i = beg + j;
+          raw[j] = i < n ? st64[i + (i >> 4)] : 1ull;
         }
       }
 #pragma unroll
