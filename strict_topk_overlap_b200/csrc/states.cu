@@ -627,10 +627,85 @@ __global__ void __launch_bounds__(128) jobs_generic_kernel(JobArgs a) {
 
 // ------------------------------------------------------------------ epilogues
 
-// merge_partials (kernels.py:74-91): one CTA per row. Warp 0 forms the
-// weights exp(m - M) (M = max included m, or 0 if none); threads then reduce
-// the numerators over slots with coalesced loads, eight slots in flight.
-__global__ void __launch_bounds__(256) merge_kernel(const float* m, const float* l, const float* u,
+// merge_partials (kernels.py:74-91): one CTA of 16 warps per row. Every
+// thread takes a stripe of slots for M (max included m, or 0 if none) and
+// the weights exp(m - M); warp k then folds slots k, k + 16, ... with 4
+// consecutive dims per lane and eight slots' loads in flight, and the warps'
+// parts add in warp order (the result does not depend on timing).
+__global__ void __launch_bounds__(512) merge_kernel(const float* m, const float* l, const float* u,
+                                                   const unsigned char* include, int s, int d, float* out) {
+  extern __shared__ __align__(16) float msm[];  // w[s], then part[16][d]
+  __shared__ float red[16];
+  constexpr int kWarps = 16;
+  constexpr int kBatch = 8;
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* w = msm;
+  float* part = msm + ((s + 3) & ~3);
+  const long long base = static_cast<long long>(row) * s;
+  float mx = neg_inf();
+  for (int i = tid; i < s; i += blockDim.x)
+    if (include == nullptr || include[base + i]) mx = fmaxf(mx, m[base + i]);
+  mx = warp_max(mx);
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  float M = neg_inf();
+#pragma unroll
+  for (int k = 0; k < kWarps; ++k) M = fmaxf(M, red[k]);
+  if (M == neg_inf()) M = 0.f;
+  __syncthreads();
+  float z = 0.f;
+  for (int i = tid; i < s; i += blockDim.x) {
+    const bool inc = include == nullptr || include[base + i];
+    const float wi = inc ? expf(m[base + i] - M) : 0.f;
+    w[i] = wi;
+    if (inc) z += wi * l[base + i];
+  }
+  z = warp_sum(z);
+  if (lane == 0) red[warp] = z;
+  __syncthreads();
+  float Z = 0.f;
+#pragma unroll
+  for (int k = 0; k < kWarps; ++k) Z += red[k];
+  Z = fmaxf(Z, 1e-30f);
+  for (int d0 = 0; d0 < d; d0 += 128) {
+    const int dd = d0 + 4 * lane;
+    const bool live = dd < d;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i0 = warp; i0 < s; i0 += kBatch * kWarps) {
+      float4 x[kBatch];
+      float wi[kBatch];
+#pragma unroll
+      for (int c = 0; c < kBatch; ++c) {
+        const int i = i0 + c * kWarps;
+        wi[c] = i < s ? w[i] : 0.f;
+        x[c] = (wi[c] != 0.f && live) ? *reinterpret_cast<const float4*>(u + (base + i) * d + dd)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int c = 0; c < kBatch; ++c) {
+        acc.x = fmaf(wi[c], x[c].x, acc.x);
+        acc.y = fmaf(wi[c], x[c].y, acc.y);
+        acc.z = fmaf(wi[c], x[c].z, acc.z);
+        acc.w = fmaf(wi[c], x[c].w, acc.w);
+      }
+    }
+    if (live) *reinterpret_cast<float4*>(part + warp * d + dd) = acc;
+  }
+  __syncthreads();
+  for (int dd = tid; dd < d; dd += blockDim.x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < kWarps; ++k) acc += part[k * d + dd];
+    out[static_cast<long long>(row) * d + dd] = acc / Z;
+  }
+}
+
+// merge_partials (kernels.py:74-91) for head dims that are not a multiple
+// of 4: one CTA per row. Warp 0 forms the weights exp(m - M) (M = max
+// included m, or 0 if none); threads then reduce the numerators over slots
+// with coalesced loads, eight slots in flight.
+__global__ void __launch_bounds__(256) merge_scalar_kernel(const float* m, const float* l, const float* u,
                                                    const unsigned char* include, int s, int d, float* out) {
   extern __shared__ __align__(16) float msm[];  // w[s]
   __shared__ float sZ;
@@ -678,55 +753,66 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* m, const float*
 // included slots of m (-inf when none), Z = sum exp(m - M) l, U = sum exp(m - M) u.
 // The context-parallel path reduces each shard's per-block states to one
 // state per row this way before the shards' states are exchanged.
-__global__ void __launch_bounds__(256) reduce_states_kernel(const float* m, const float* l, const float* u,
+__global__ void __launch_bounds__(512) reduce_states_kernel(const float* m, const float* l, const float* u,
                                                             const unsigned char* include, int s, int d, float* m_out,
                                                             float* l_out, float* u_out) {
-  // rsm: w[s] (slot weights), then part[8][d] (each warp's numerators).
+  // rsm: w[s] (slot weights), then part[16][d] (each warp's numerators).
   extern __shared__ __align__(16) float rsm[];
+  __shared__ float red[16];
+  constexpr int kWarps = 16;
+  constexpr int kBatch = 8;
   const int row = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  constexpr int kWarps = 8;
   float* w = rsm;
   float* part = rsm + ((s + 3) & ~3);
   const long long base = static_cast<long long>(row) * s;
-  if (warp == 0) {
-    float M = neg_inf();
-    for (int i = lane; i < s; i += 32)
-      if (include == nullptr || include[base + i]) M = fmaxf(M, m[base + i]);
-    M = warp_max(M);
-    float z = 0.f;
-    for (int i = lane; i < s; i += 32) {
-      const bool inc = (include == nullptr || include[base + i]) && m[base + i] != neg_inf();
-      const float wi = inc ? expf(m[base + i] - M) : 0.f;
-      w[i] = wi;
-      z += wi * (inc ? l[base + i] : 0.f);
-    }
-    z = warp_sum(z);
-    if (lane == 0) {
-      m_out[row] = M;
-      l_out[row] = z;
-    }
-  }
+  auto included = [&](int i) { return (include == nullptr || include[base + i]) && m[base + i] != neg_inf(); };
+  // M and Z over every thread's stripe of slots, then the warps in order.
+  float mx = neg_inf();
+  for (int i = tid; i < s; i += blockDim.x)
+    if (included(i)) mx = fmaxf(mx, m[base + i]);
+  mx = warp_max(mx);
+  if (lane == 0) red[warp] = mx;
   __syncthreads();
-  // Warp k folds slots k, k + 8, ... (lane: 4 consecutive dims per 128),
-  // four slots' loads in flight at a time; the warps' parts are then added
+  float M = neg_inf();
+#pragma unroll
+  for (int k = 0; k < kWarps; ++k) M = fmaxf(M, red[k]);
+  __syncthreads();
+  float z = 0.f;
+  for (int i = tid; i < s; i += blockDim.x) {
+    const bool inc = included(i);
+    const float wi = inc ? expf(m[base + i] - M) : 0.f;
+    w[i] = wi;
+    z += inc ? wi * l[base + i] : 0.f;
+  }
+  z = warp_sum(z);
+  if (lane == 0) red[warp] = z;
+  __syncthreads();
+  if (tid == 0) {
+    float Z = 0.f;
+    for (int k = 0; k < kWarps; ++k) Z += red[k];
+    m_out[row] = M;
+    l_out[row] = Z;
+  }
+  // Warp k folds slots k, k + 16, ... (lane: 4 consecutive dims per 128),
+  // eight slots' loads in flight at a time; the warps' parts are then added
   // in warp order, so the result does not depend on timing.
   for (int d0 = 0; d0 < d; d0 += 128) {
     const int dd = d0 + 4 * lane;
     const bool live = dd < d;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int i0 = warp; i0 < s; i0 += 4 * kWarps) {
-      float4 x[4];
-      float wi[4];
+    for (int i0 = warp; i0 < s; i0 += kBatch * kWarps) {
+      float4 x[kBatch];
+      float wi[kBatch];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < kBatch; ++c) {
         const int i = i0 + c * kWarps;
         wi[c] = i < s ? w[i] : 0.f;
         x[c] = (wi[c] != 0.f && live) ? *reinterpret_cast<const float4*>(u + (base + i) * d + dd)
                                       : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < kBatch; ++c) {
         acc.x = fmaf(wi[c], x[c].x, acc.x);
         acc.y = fmaf(wi[c], x[c].y, acc.y);
         acc.z = fmaf(wi[c], x[c].z, acc.z);
@@ -747,10 +833,10 @@ __global__ void __launch_bounds__(256) reduce_states_kernel(const float* m, cons
 int launch_reduce_states(const float* m, const float* l, const float* u, const unsigned char* include, int rows,
                          int s, int d, float* m_out, float* l_out, float* u_out, cudaStream_t stream) {
   if (d % 4) return -1;  // 16-byte numerator rows
-  const size_t smem = (static_cast<size_t>((s + 3) & ~3) + 8 * static_cast<size_t>(d)) * 4;
+  const size_t smem = (static_cast<size_t>((s + 3) & ~3) + 16 * static_cast<size_t>(d)) * 4;
   if (smem > 200 * 1024) return -1;
   cudaFuncSetAttribute(reduce_states_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  reduce_states_kernel<<<rows, 256, smem, stream>>>(m, l, u, include, s, d, m_out, l_out, u_out);
+  reduce_states_kernel<<<rows, 512, smem, stream>>>(m, l, u, include, s, d, m_out, l_out, u_out);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -1055,10 +1141,17 @@ int launch_jobs(const JobArgs& a, int kv_dtype, int num_sms, cudaStream_t stream
 
 int launch_merge(const float* m, const float* l, const float* u, const unsigned char* include, int rows, int s, int d,
                  float* out, cudaStream_t stream) {
+  const size_t wide_smem = (static_cast<size_t>((s + 3) & ~3) + 16 * static_cast<size_t>(d)) * 4;
+  if (d % 4 == 0 && wide_smem <= 200 * 1024) {
+    const size_t smem = wide_smem;
+    cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    merge_kernel<<<rows, 512, smem, stream>>>(m, l, u, include, s, d, out);
+    return static_cast<int>(cudaGetLastError());
+  }
   const size_t smem = static_cast<size_t>(s) * 4;
   if (smem > 200 * 1024) return -1;
-  cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  merge_kernel<<<rows, 256, smem, stream>>>(m, l, u, include, s, d, out);
+  cudaFuncSetAttribute(merge_scalar_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  merge_scalar_kernel<<<rows, 256, smem, stream>>>(m, l, u, include, s, d, out);
   return static_cast<int>(cudaGetLastError());
 }
 

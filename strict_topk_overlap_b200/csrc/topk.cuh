@@ -293,6 +293,51 @@ __device__ __forceinline__ unsigned long long exact_row_key_staged(const SelectA
   return order_key(grp);
 }
 
+// Exact order keys of NK metadata rows gb[] (live[] false: skipped, key 0)
+// with the rows' metadata loads all in flight before any arithmetic; each
+// key is exact_row_key_staged's, computed in the same order.
+template <int NK>
+__device__ __forceinline__ void exact_row_keys_staged(const SelectArgs& a, int hs, const long long (&gb)[NK],
+                                                      const bool (&live)[NK], int lane, const float* qsm,
+                                                      unsigned long long (&key)[NK]) {
+  const int D = a.d, c = (D + 31) / 32;
+  const int G = a.hq / a.hmeta;
+  const int heads = a.group_select ? G : 1;
+  const int mh = a.group_select ? hs : hs / G;
+  float lo_r[NK][8], hi_r[NK][8];
+#pragma unroll
+  for (int k = 0; k < NK; ++k) {
+    const long long moff = (static_cast<long long>(mh) * a.total_blocks + gb[k]) * D;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int dd = lane * c + e;
+      const bool ok = live[k] && e < c && dd < D;
+      lo_r[k][e] = ok ? a.lo[moff + dd] : 0.f;
+      hi_r[k][e] = ok ? a.hi[moff + dd] : 0.f;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NK; ++k) {
+    double grp = 0.0, one = 0.0;
+    for (int g = 0; g < heads; ++g) {
+      double acc = 0.0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int dd = lane * c + e;
+        if (e < c && dd < D) {
+          const double qv = static_cast<double>(qsm[g * D + dd]);
+          acc = __fma_rn(qv, static_cast<double>(qv >= 0.0 ? hi_r[k][e] : lo_r[k][e]), acc);
+        }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(kFull, acc, off));
+      if (!a.group_select) { one = acc; break; }
+      grp = __dadd_rn(grp, acc);
+    }
+    key[k] = live[k] ? order_key(a.group_select ? grp : one) : 0ull;
+  }
+}
+
 constexpr int kHistBins = 2048;
 constexpr int kUncMax = 256;  // straddling blocks resolved by ranking; more take the radix path
 constexpr int kQStage = 2048;  // staged query floats per Top-K CTA (heads x D)
@@ -635,10 +680,32 @@ __device__ void bounded_select_core(const SelectArgs& a, int row, const float* q
   }
   if (a.keys_out) {
     __syncthreads();  // this CTA's ID writes are visible to the whole CTA
-    for (int t = warp; t < K; t += nw) {
-      const int pos = out[t] - a.id_base;
-      const unsigned long long k = row_key(static_cast<long long>(off) + pos);
-      if (lane == 0) a.keys_out[static_cast<long long>(row) * K + t] = k;
+    if (q_staged) {
+      // Four keys per warp at a time: their metadata loads overlap.
+      constexpr int NK = 4;
+      for (int t0 = warp; t0 < K; t0 += NK * nw) {
+        long long gbk[NK];
+        bool lk[NK];
+        unsigned long long kk[NK];
+#pragma unroll
+        for (int k = 0; k < NK; ++k) {
+          const int t = t0 + k * nw;
+          lk[k] = t < K;
+          gbk[k] = lk[k] ? static_cast<long long>(off) + (out[t] - a.id_base) : 0;
+        }
+        exact_row_keys_staged<NK>(a, hs, gbk, lk, lane, qsm, kk);
+        if (lane == 0) {
+#pragma unroll
+          for (int k = 0; k < NK; ++k)
+            if (lk[k]) a.keys_out[static_cast<long long>(row) * K + t0 + k * nw] = kk[k];
+        }
+      }
+    } else {
+      for (int t = warp; t < K; t += nw) {
+        const int pos = out[t] - a.id_base;
+        const unsigned long long k = row_key(static_cast<long long>(off) + pos);
+        if (lane == 0) a.keys_out[static_cast<long long>(row) * K + t] = k;
+      }
     }
   }
 }
