@@ -42,7 +42,9 @@
 // Cross-CTA progress goes through counters in the workspace's control
 // block, which must be zero before the first call on a workspace; the last
 // CTA to finish a call zeroes it again:
-//   ctrl[mh]                metadata items done for KV head mh,
+//   ctrl[mh]                metadata items done for KV head mh (counted; the
+//                           row CTAs poll their score slots instead of
+//                           waiting for it),
 //   ctrl[hkv + r]           block states done for row r,
 //   ctrl[hkv + hq + r]      row r's selection published (serial step),
 //   ctrl[hkv + 2 hq]        CTAs finished.
@@ -162,6 +164,12 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, unsigned parity) {
 }
 
 // Named barrier over the warps other than the producer (480 threads).
+// Warps 0..11 (consumers and producer): the miss list of the speculative
+// row phase is published to them alone, so that the helper warps can start
+// folding the buffered hits as soon as the selection ends.
+__device__ __forceinline__ void sync_list_warps() {
+  asm volatile("bar.sync 3, %0;" ::"n"((kStepStages + 1) * 32) : "memory");
+}
 __device__ __forceinline__ void sync_non_producer() {
   asm volatile("bar.sync 1, %0;" ::"n"(kStepThreads - 32) : "memory");
 }
@@ -785,10 +793,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
         const int id = s_pid[i];
         if (id >= 0 && id < n) atomicOr(&s_pmask[id >> 5], 1u << (id & 31));
       }
-    if (tid == 0 && !s_abort && !wait_count(&head_done[mh], static_cast<unsigned>(ipH))) {
-      report(a.status, kStatusWaitTimeout);
-      s_abort = 1;
-    }
+    // No wait for the head's metadata count: the selection polls the row's
+    // score slots (each fills with one 8-byte store) and starts as soon as
+    // the last one lands, with a bounded wait of its own.
     __syncthreads();
     if (tid == 0) SPT(6);
     // Row-local blocks: the misses (A not in P) of the saved repair, or the
@@ -848,11 +855,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
       for (int i = lane; i < nm; i += 32) s_loc[i] = s_glb[i];
       if (lane == 0) s_nloc = nm;
     }
-    if (serial)
+    if (serial) {
       for (int i = xl + tid; i < K; i += kStepThreads) a.sel_tag[static_cast<long long>(row) * K + i] = s_sel[i] + 1;
-    __syncthreads();
+      __syncthreads();
+    } else if (warp < kStepHelper0) {
+      sync_list_warps();  // the helpers need only the selection's mask, complete above
+    }
     if (serial && tid == 0 && !s_abort) red_relaxed_gpu(&row_ready[row], 1u);
-    const int nloc = s_abort ? 0 : s_nloc;
+    const int nloc = (s_abort || (!serial && warp >= kStepHelper0)) ? 0 : s_nloc;
     // Block states to fold from the buffer: the hits (P slots whose block is
     // in A), or the serial row's slots xl .. K - 1.
     const int nglb = s_abort ? 0 : (serial ? K - xl : a.sp);
