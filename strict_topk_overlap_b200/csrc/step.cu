@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
   constexpr int DPH = kStepDPH;
   constexpr int NS = kStepStages;
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ uint64_t full_bar[NS], empty_bar[NS], q_bar;
+  __shared__ uint64_t full_bar[NS], empty_bar[NS], q_bar, hit_bar;
   __shared__ int s_desc[NS], item_ok[NS];
   __shared__ volatile int s_abort;
   __shared__ bool s_last;
@@ -477,8 +477,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
       __syncwarp();
     }
   };
-  auto produce_ends = [&]() {
-    bool ended = lane >= NS;
+  auto produce_ends = [&](int nstages) {
+    bool ended = lane >= nstages;
     unsigned long long t0 = global_ns();
     while (!__all_sync(kFull, ended) && !s_abort) {
       if (!ended && lane_free()) {
@@ -519,6 +519,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
         mbar_init(&empty_bar[i], 1);
       }
       mbar_init(&q_bar, 1);
+      mbar_init(&hit_bar, 1);
       fence_barrier_init();
       s_abort = 0;
       mbar_arrive_expect_tx(&q_bar, static_cast<unsigned>(qbytes));
@@ -741,7 +742,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
                 id = off < 32 ? va : vb;
               });
     }
-    produce_ends();
+    produce_ends(NS);
     if (lane == 0) SPT(4);
   } else if (warp < NS) {
     if (lane == 0 && warp == 0) SPT(12);
@@ -878,6 +879,20 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
     constexpr int nfw = kStepWarps - kStepHelper0;
     const int fw = warp - kStepHelper0;
     const long long rb = static_cast<long long>(row) * S;
+    // Speculative step with a predicted list whose states fit three stages:
+    // the misses use stages 0 .. NS - 4 only, the row's predicted states
+    // (u, then m, then l) arrive in the last three stages with bulk copies
+    // as soon as every work CTA has written them, and seven warps (the
+    // helpers and the three consumers without a stage) fold the hits from
+    // shared memory.
+    constexpr int kHitStages = 3;
+    const bool smem_hits = !serial && a.sp % 4 == 0 && a.sp * (D + 2) * 4 <= kHitStages * kStageBytes;
+    const int NR = smem_hits ? NS - kHitStages : NS;  // stages of the row-local blocks
+    constexpr int nhw = kHitStages + nfw;              // hit-folding warps in that case
+    const int hw = warp >= kStepHelper0 ? kHitStages + (warp - kStepHelper0) : warp - (NS - kHitStages);
+    float* hit_u = reinterpret_cast<float*>(pool + static_cast<size_t>(NS - kHitStages) * kStageBytes);
+    float* hit_m = hit_u + a.sp * D;
+    float* hit_l = hit_m + a.sp;
     // Buffer slot of fold i (serial: xl + i; speculative: P slot i when its
     // block is in A), or -1.
     auto fold_slot = [&](int i) {
@@ -892,6 +907,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
         s_abort = 1;
       }
       __syncwarp();
+      if (fw == 0 && lane == 0) SPT(110);
       if (s_abort) return;
       constexpr int kBatch = 8;
       for (int i0 = fw; i0 < nglb; i0 += kBatch * nfw) {
@@ -914,17 +930,54 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
             for (int j = 0; j < DPH; ++j) uu[c][j] = 0.f;
           }
         }
+        if (fw == 0 && lane == 0 && i0 == fw) SPT(111);
 #pragma unroll
         for (int c = 0; c < kBatch; ++c) fold_state(wm, wl, wu, mm[c], ll[c], uu[c]);
       }
     };
+    // Shared-memory hits: the first helper lane waits for the row's states
+    // and issues their copy; every hit-folding warp then folds P slots
+    // hw, hw + nhw, ... in order.
+    auto fold_smem = [&]() {
+      if (warp == kStepHelper0 && lane == 0) {
+        bool ok = !s_abort && wait_count(&row_states[row], static_cast<unsigned>(SJ));
+        if (ok) {
+          // The states were written by other CTAs through the generic proxy
+          // and acquired above; the bulk copy reads them through the async
+          // proxy.
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          const unsigned ub = static_cast<unsigned>(a.sp) * D * 4, mb = static_cast<unsigned>(a.sp) * 4;
+          mbar_arrive_expect_tx(&hit_bar, ub + 2 * mb);
+          bulk_g2s(hit_u, a.su + rb * D, ub, &hit_bar);
+          bulk_g2s(hit_m, a.sm + rb, mb, &hit_bar);
+          bulk_g2s(hit_l, a.sl + rb, mb, &hit_bar);
+        } else {
+          report(a.status, kStatusWaitTimeout);
+          s_abort = 1;
+          mbar_arrive(&hit_bar);  // complete the phase without data
+        }
+      }
+      if (!mbar_wait(&hit_bar, 0u, a.status)) s_abort = 1;
+      __syncwarp();
+      if (warp == kStepHelper0 && lane == 0) SPT(110);
+      if (s_abort) return;
+      for (int i = hw; i < a.sp; i += nhw) {
+        if (fold_slot(i) < 0) continue;
+        float uu[DPH];
+        const float4* up = reinterpret_cast<const float4*>(hit_u + static_cast<size_t>(i) * D + (lane & 15) * DPH);
+        const float4 x0 = up[0], x1 = up[1];
+        uu[0] = x0.x; uu[1] = x0.y; uu[2] = x0.z; uu[3] = x0.w;
+        uu[4] = x1.x; uu[5] = x1.y; uu[6] = x1.z; uu[7] = x1.w;
+        fold_state(wm, wl, wu, hit_m[i], hit_l[i], uu);
+      }
+    };
     if (warp == kStepProducer) {
       if (lane == 0) SPT(123);
-      // Row-local block i goes to stage i % NS, so that each consumer folds
+      // Row-local block i goes to stage i % NR, so that each consumer folds
       // a fixed subsequence of the list in order: the result does not depend
       // on timing.
-      for (int base = 0; base < nloc && !s_abort; base += NS) {
-        bool done = lane >= NS || base + lane >= nloc;
+      for (int base = 0; base < nloc && !s_abort; base += NR) {
+        bool done = lane >= NR || base + lane >= nloc;
         const unsigned long long t0 = global_ns();
         while (!__all_sync(kFull, done) && !s_abort) {
           if (!done && lane_free()) {
@@ -938,13 +991,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
         }
       }
       if (lane == 0) SPT(8);
-      produce_ends();
+      produce_ends(NR);
       if (lane == 0) SPT(23);
-    } else if (warp < NS) {
+    } else if (warp < NR) {
       consume(std::true_type{}, qrow, wm, wl, wu);
       if (lane == 0 && warp == 0) SPT(24);
+    } else if (warp < NS) {
+      fold_smem();  // smem_hits: the consumers of the hit stages
     } else {
-      fold_buffered();
+      if (smem_hits) fold_smem(); else fold_buffered();
       if (warp == kStepHelper0 && lane == 0) SPT(9);
       // The row's score slots go back to zero for the next call.
       unsigned long long* slots = reinterpret_cast<unsigned long long*>(a.bounds + static_cast<long long>(row) * n);
