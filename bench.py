@@ -948,7 +948,8 @@ def main():
             "e2e": {"value": e2e_value, "unit": "decode-steps/s", "h2d_bytes_per_step": HQ * D * 2 + HQ * TOPK * 4,
                     "d2h_bytes_per_step": HQ * D * 4,
                     "path": "decode.capture_host_steps: per step the pinned H2D of q and P, the step and the D2H of "
-                            "its output, graphs of consecutive steps; the host reads every step's output"},
+                            "its output, graphs of consecutive steps with the copies on side streams (step i's copies "
+                            "overlap the other steps); the host reads every step's output"},
             "gpu_launches": LAUNCHES_PER_STEP.get(args.method, 4) * K * len(reps),
             "cpu_baseline": cpu,
         }

@@ -360,29 +360,61 @@ def capture_host_steps(decoders, q_hosts, predicted_hosts, out_hosts):
     the copy of the step's output into the pinned ``out_hosts[i]`` (FP32
     [Hq, D]): the host-facing form of ``capture_steps``. The host reads
     ``out_hosts`` after synchronising with the stream (or an event recorded
-    after the replay)."""
+    after the replay).
+
+    The copies run on two side streams inside the graph: step i's inputs
+    only have to land before step i starts and its output copy only waits
+    for step i, so the copies of the other steps overlap the decode steps.
+    A decoder listed twice gets the extra orderings its shared buffers need
+    (its next input copy waits for its previous step, its next step for its
+    previous output copy)."""
     for d, qh, ph, oh in zip(decoders, q_hosts, predicted_hosts, out_hosts):
         for t, want in ((qh, d.q), (ph, d.predicted)):
             if t.shape != want.shape or t.dtype != want.dtype or t.is_cuda or not t.is_pinned():
                 raise ValueError("host inputs must be pinned CPU tensors shaped like the device inputs")
         if oh.is_cuda or not oh.is_pinned() or oh.dtype != torch.float32 or oh.shape != (d.q.shape[0], d.q.shape[1]):
             raise ValueError("out_hosts must be pinned FP32 CPU tensors [Hq, D]")
+    dev = decoders[0].q.device
+    copy_in = torch.cuda.Stream(dev)
+    copy_out = torch.cuda.Stream(dev)
 
     def run():
+        main = torch.cuda.current_stream(dev)
+        copy_in.wait_stream(main)
+        copy_out.wait_stream(main)
+        last_step, last_out = {}, {}  # per decoder: events of its latest step / output copy
         for d, qh, ph, oh in zip(decoders, q_hosts, predicted_hosts, out_hosts):
-            d.q.copy_(qh, non_blocking=True)
-            d.predicted.copy_(ph, non_blocking=True)
+            key = id(d)
+            landed = torch.cuda.Event()
+            with torch.cuda.stream(copy_in):
+                if key in last_step:
+                    copy_in.wait_event(last_step[key])
+                d.q.copy_(qh, non_blocking=True)
+                d.predicted.copy_(ph, non_blocking=True)
+                landed.record(copy_in)
+            main.wait_event(landed)
+            if key in last_out:
+                main.wait_event(last_out[key])
             out, _ = d._run()
-            oh.copy_(out, non_blocking=True)
-    dev = decoders[0].q.device
+            stepped = torch.cuda.Event()
+            stepped.record(main)
+            last_step[key] = stepped
+            copied = torch.cuda.Event()
+            with torch.cuda.stream(copy_out):
+                copy_out.wait_event(stepped)
+                oh.copy_(out, non_blocking=True)
+                copied.record(copy_out)
+            last_out[key] = copied
+        main.wait_stream(copy_in)
+        main.wait_stream(copy_out)
+
     side = torch.cuda.Stream(dev)
-    side.wait_stream(torch.cuda.current_stream())
+    side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):
         run()
-    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.current_stream(dev).wait_stream(side)
     torch.cuda.synchronize(dev)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         run()
     return graph
-

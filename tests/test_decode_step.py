@@ -184,13 +184,23 @@ def test_capture_host_steps_copies_inputs_and_outputs():
         hq_pin.append(q.pin_memory())
         hp_pin.append(p.pin_memory())
         refs.append(OA.attention_fp64(C.as_np(q), C.as_np(k), C.as_np(v), ids))
+    # The first decoder again, with another query: its second step's input
+    # copy must wait for its first step, and that step for its output copy.
+    q0, k0, v0, lo0, hi0, _, p0 = _case(16, 4, 512, 32, 0.75, seed=31)
+    q2 = torch.randn(16, 128, generator=torch.Generator().manual_seed(77)).to(q0.dtype)
+    ids2 = OS.select_blocks(C.as_np(q2), lo0.numpy(), hi0.numpy(), 32)
+    decs.append(decs[0])
+    hq_pin.append(q2.pin_memory())
+    hp_pin.append(p0.pin_memory())
+    refs.append(OA.attention_fp64(C.as_np(q2), C.as_np(k0), C.as_np(v0), ids2))
     outs = [torch.empty(16, 128, dtype=torch.float32).pin_memory() for _ in decs]
     g = capture_host_steps(decs, hq_pin, hp_pin, outs)
-    for o in outs:
-        o.zero_()
-    g.replay()
-    torch.cuda.synchronize()
-    for o, ref in zip(outs, refs):
-        ok, err = _bar(o, ref)
-        assert ok, err
+    for _ in range(2):
+        for o in outs:
+            o.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        for o, ref in zip(outs, refs):
+            ok, err = _bar(o, ref)
+            assert ok, err
     del g
