@@ -39,6 +39,13 @@
 // issued before any bulk copy: a load queued behind the bulk stream waits
 // for all of it.
 //
+// A row CTA's phase: it polls the row's score slots (coalesced, exchanged
+// through the ring's first stages) and selects; in the speculative step
+// the misses then go to stages 0..7, the row's predicted states arrive in
+// stages 8..10 with bulk copies once every work CTA has written them, and
+// the helpers with consumers 8..10 fold the hits from there while
+// consumers 0..7 reduce the misses; the warps' states merge in warp order.
+//
 // Cross-CTA progress goes through counters in the workspace's control
 // block, which must be zero before the first call on a workspace; the last
 // CTA to finish a call zeroes it again:
@@ -870,12 +877,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(StepArgs a
     float wm = neg_inf(), wl = 0.f, wu[DPH];
 #pragma unroll
     for (int j = 0; j < DPH; ++j) wu[j] = 0.f;
-    // The buffered states, once every work CTA has written this row's: every
-    // warp but the producer folds its share of the slots, up to four per
-    // round trip, while the row-local blocks' copies are in flight.
-    // The buffered states are folded by the helper warps 12..15, eight per
-    // memory round trip, in a fixed slot order, while the consumers take the
-    // row-local blocks.
+    // Without the shared-memory hits below (serial step, or a predicted list
+    // too large for three stages), the buffered states are folded from L2 by
+    // the helper warps 12..15, eight per memory round trip, in a fixed slot
+    // order, while the consumers take the row-local blocks.
     constexpr int nfw = kStepWarps - kStepHelper0;
     const int fw = warp - kStepHelper0;
     const long long rb = static_cast<long long>(row) * S;
