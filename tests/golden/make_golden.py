@@ -1,9 +1,9 @@
 """Generate golden fixtures by running the REFERENCE implementation on the CPU.
 
-Run once, in a container that has the reference checkout (read-only) at
-``$STK_REFERENCE`` (default ``/root/reference``)::
+Run once, in a container that has the reference checkout (read-only), with
+``STK_REFERENCE`` naming its directory::
 
-    python tests/golden/make_golden.py
+    STK_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 The reference is pure Python + Triton. Its kernels execute on the CPU under
 Triton's interpreter (``TRITON_INTERPRET=1``); only its CUDA-device shape
@@ -27,7 +27,9 @@ import time
 from pathlib import Path
 
 os.environ["TRITON_INTERPRET"] = "1"
-REF = os.environ.get("STK_REFERENCE", "/root/reference")
+REF = os.environ.get("STK_REFERENCE")
+if not REF:
+    raise SystemExit("set STK_REFERENCE to the reference checkout's directory")
 sys.path.insert(0, REF)
 sys.path.insert(0, str(Path(__file__).resolve().parent))
 
