@@ -385,14 +385,14 @@ __global__ void __launch_bounds__(kAW * 32) attend_kernel(RepairArgs a) {
 // order writes the row's output.
 constexpr int kLW = 8;
 
-template <typename T, int DPH, bool FULL32>
-__global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
+template <typename T, int DPH, bool FULL32, int LW>
+__global__ void __launch_bounds__(LW * 32) light_kernel(RepairArgs a) {
   constexpr int D = 16 * DPH;
   constexpr int kChunk = 32 * D;
   constexpr int kDL = D / 32;  // dims per lane in the retained fold
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ uint64_t bar[kLW];
-  __shared__ float sh_w[kLW + 1][2];
+  __shared__ uint64_t bar[LW];
+  __shared__ float sh_w[LW + 1][2];
   __shared__ int sh_total;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = blockIdx.x;
@@ -403,9 +403,9 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
   AT(0);
   pdl_release();
 
-  // Shared memory: stages [kLW][2][32][D] T, then the row's bookkeeping.
+  // Shared memory: stages [LW][2][32][D] T, then the row's bookkeeping.
   T* stage = reinterpret_cast<T*>(smem) + static_cast<size_t>(warp) * 2 * kChunk;
-  size_t off = static_cast<size_t>(kLW) * 2 * kChunk * sizeof(T);
+  size_t off = static_cast<size_t>(LW) * 2 * kChunk * sizeof(T);
   auto carve = [&](size_t bytes) {
     off = (off + 15) & ~size_t(15);
     unsigned char* p = smem + off;
@@ -420,8 +420,8 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
   unsigned* bitP = reinterpret_cast<unsigned*>(carve(static_cast<size_t>(nwords) * 4));
   int* list = reinterpret_cast<int*>(carve(static_cast<size_t>(a.sa) * 4));
   float* qv = reinterpret_cast<float*>(carve(static_cast<size_t>(D) * 4));
-  float* wU = reinterpret_cast<float*>(carve(static_cast<size_t>(kLW) * D * 4));  // miss numerators per warp
-  float* wR = reinterpret_cast<float*>(carve(static_cast<size_t>(kLW) * D * 4));  // retained numerators per warp
+  float* wU = reinterpret_cast<float*>(carve(static_cast<size_t>(LW) * D * 4));  // miss numerators per warp
+  float* wR = reinterpret_cast<float*>(carve(static_cast<size_t>(LW) * D * 4));  // retained numerators per warp
 
   if (lane == 0) {
     mbar_init(&bar[warp], 1);
@@ -523,10 +523,10 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
   if (warp < ngroups && lane == 0) issue(warp, 0);
   AT(3);
   // Later misses (beyond one stage per warp) are prefetched into L2 now.
-  for (int k = kLW * mp + tid; k < count; k += blockDim.x) prefetch_block<T>(a.L, r, kv, a_ids[list[k]], true);
+  for (int k = LW * mp + tid; k < count; k += blockDim.x) prefetch_block<T>(a.L, r, kv, a_ids[list[k]], true);
 
   // Retained slots while the copies land: every warp finds their max Mr;
-  // warp w folds slots w, w + kLW, ... with weights exp(m - Mr); the last
+  // warp w folds slots w, w + LW, ... with weights exp(m - Mr); the last
   // warp also records (Mr, Zr).
   float Mr = neg_inf();
   auto kept = [&](int c) {
@@ -536,12 +536,12 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
   for (int c = lane; c < a.sp; c += 32)
     if (kept(c)) Mr = fmaxf(Mr, pm_s[c]);
   Mr = warp_max(Mr);
-  if (warp == kLW - 1) {
+  if (warp == LW - 1) {
     float Zr = 0.f;
     for (int c = lane; c < a.sp; c += 32)
       if (kept(c) && pm_s[c] != neg_inf()) Zr += expf(pm_s[c] - Mr) * pl_s[c];
     Zr = warp_sum(Zr);
-    if (lane == 0) { sh_w[kLW][0] = Mr; sh_w[kLW][1] = Zr; }
+    if (lane == 0) { sh_w[LW][0] = Mr; sh_w[LW][1] = Zr; }
   }
   {
     // Eight slots' numerators are loaded before any is used (one memory
@@ -550,11 +550,11 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
     float R[kDL];
 #pragma unroll
     for (int j = 0; j < kDL; ++j) R[j] = 0.f;
-    for (int c0 = warp; c0 < a.sp; c0 += kLW * kBatch) {
+    for (int c0 = warp; c0 < a.sp; c0 += LW * kBatch) {
       float v[kBatch][kDL], w[kBatch];
 #pragma unroll
       for (int t = 0; t < kBatch; ++t) {
-        const int c = c0 + t * kLW;
+        const int c = c0 + t * LW;
         w[t] = 0.f;
         if (c < a.sp) {
           const float* pu = a.pu + (sr + c) * D;
@@ -585,7 +585,7 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
   unsigned phase = 0;
   bool ok = true;
 #pragma unroll 1
-  for (int k = warp; k < ngroups && ok; k += kLW) {
+  for (int k = warp; k < ngroups && ok; k += LW) {
     float m = neg_inf(), l = 0.f, u[DPH], ua[DPH];
 #pragma unroll
     for (int j = 0; j < DPH; ++j) { u[j] = 0.f; ua[j] = 0.f; }
@@ -599,7 +599,7 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
       __syncwarp();
       if (lane == 0) {
         if (c + 1 < nchunks) issue(k, c + 1);
-        else if (k + kLW < ngroups) issue(k + kLW, 0);
+        else if (k + LW < ngroups) issue(k + LW, 0);
       }
     }
     if (ok) fold_state<DPH>(wm, wl, myU, m, l, u, lane);
@@ -608,19 +608,19 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
   __syncthreads();
   AT(4);
   // Final merge: warps in order, then the retained slots.
-  float M = sh_w[kLW][0];
-  for (int w = 0; w < kLW; ++w) M = fmaxf(M, sh_w[w][0]);
-  float Z = sh_w[kLW][0] != neg_inf() ? expf(sh_w[kLW][0] - M) * sh_w[kLW][1] : 0.f;
-  for (int w = 0; w < kLW; ++w)
+  float M = sh_w[LW][0];
+  for (int w = 0; w < LW; ++w) M = fmaxf(M, sh_w[w][0]);
+  float Z = sh_w[LW][0] != neg_inf() ? expf(sh_w[LW][0] - M) * sh_w[LW][1] : 0.f;
+  for (int w = 0; w < LW; ++w)
     if (sh_w[w][0] != neg_inf()) Z += expf(sh_w[w][0] - M) * sh_w[w][1];
-  const float kscale = sh_w[kLW][0] != neg_inf() ? expf(sh_w[kLW][0] - M) : 0.f;
+  const float kscale = sh_w[LW][0] != neg_inf() ? expf(sh_w[LW][0] - M) : 0.f;
   for (int dd = tid; dd < D; dd += blockDim.x) {
     float U = 0.f;
-    for (int w = 0; w < kLW; ++w)
+    for (int w = 0; w < LW; ++w)
       if (sh_w[w][0] != neg_inf()) U += expf(sh_w[w][0] - M) * wU[w * D + dd];
     if (kscale != 0.f) {
       float R = 0.f;
-      for (int w = 0; w < kLW; ++w) R += wR[w * D + dd];
+      for (int w = 0; w < LW; ++w) R += wR[w * D + dd];
       U += kscale * R;
     }
     a.out[static_cast<long long>(row) * D + dd] = U / fmaxf(Z, 1e-30f);
@@ -636,21 +636,37 @@ __global__ void __launch_bounds__(kLW * 32) light_kernel(RepairArgs a) {
   AT(7);
 }
 
-template <typename T, int DPH>
-static int launch_light_t(const RepairArgs& a, cudaStream_t stream) {
+template <typename T, int DPH, int LW>
+static int launch_light_lw(const RepairArgs& a, cudaStream_t stream) {
   const int nwords = (a.max_n + 31) / 32;
   const int D = a.d;
-  size_t smem = static_cast<size_t>(kLW) * 2 * 32 * D * sizeof(T);
+  size_t smem = static_cast<size_t>(LW) * 2 * 32 * D * sizeof(T);
   auto add = [&](size_t b) { smem = ((smem + 15) & ~size_t(15)) + b; };
   add(static_cast<size_t>(a.sp) * 4); add(static_cast<size_t>(a.sp) * 4);
   add(static_cast<size_t>(a.sp) * 8); add(static_cast<size_t>(a.sa) * 8); add(static_cast<size_t>(nwords) * 4);
   add(static_cast<size_t>(nwords) * 4); add(static_cast<size_t>(a.sa) * 4); add(static_cast<size_t>(D) * 4);
-  add(static_cast<size_t>(kLW) * D * 4); add(static_cast<size_t>(kLW) * D * 4);
+  add(static_cast<size_t>(LW) * D * 4); add(static_cast<size_t>(LW) * D * 4);
   if (smem > 225 * 1024) return 1;
-  auto kern = a.L.b % 32 == 0 ? light_kernel<T, DPH, true> : light_kernel<T, DPH, false>;
+  auto kern = a.L.b % 32 == 0 ? light_kernel<T, DPH, true, LW> : light_kernel<T, DPH, false, LW>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   prefer_shared(kern);
-  return launch_pdl(kern, dim3(static_cast<unsigned>(a.rows)), dim3(kLW * 32), smem, stream, 0, a);
+  return launch_pdl(kern, dim3(static_cast<unsigned>(a.rows)), dim3(LW * 32), smem, stream, 0, a);
+}
+
+// A row's CTA takes kLW warps and kLW stages; a batch of rows at least
+// twice the SM count (batched requests) takes half as many per row, so that
+// three rows' CTAs share an SM and their latencies overlap.
+static int current_sm_count() {
+  int dev = 0, v = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    v = 0;
+  return v > 0 ? v : 148;
+}
+
+template <typename T, int DPH>
+static int launch_light_t(const RepairArgs& a, cudaStream_t stream) {
+  if (a.rows >= 2 * current_sm_count()) return launch_light_lw<T, DPH, kLW / 2>(a, stream);
+  return launch_light_lw<T, DPH, kLW>(a, stream);
 }
 
 // ------------------------------------------------------------------ host side
